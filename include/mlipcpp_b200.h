@@ -1,0 +1,82 @@
+/*
+ * Extensions of the mlipcpp C API provided by the B200 backend.
+ *
+ * The reference exposes batched prediction only through C++
+ * (PETModel::predict_batch, src/models/pet/pet.h:140-143); it is made
+ * available to C callers here.  The remaining entry points serve
+ * benchmarking and MD drivers that keep positions on the GPU.
+ */
+#ifndef MLIPCPP_B200_H
+#define MLIPCPP_B200_H
+
+#include "mlipcpp.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Predict a batch of independent structures in one call
+ * (PETModel::predict_batch, src/models/pet/pet.cpp:125-694).  Non-periodic
+ * structures are evaluated together; periodic ones one after another.
+ * results[k] receives a handle that owns its data (valid until freed with
+ * mlipcpp_result_free). */
+mlipcpp_error_t mlipcpp_predict_batch(mlipcpp_model_t model, int32_t n_systems,
+                                      const mlipcpp_system_t *systems,
+                                      const mlipcpp_predict_options_t *options,
+                                      mlipcpp_result_t *results);
+
+/* Predict one structure whose positions are already in device memory
+ * (d_positions: device pointer to [3n] float).  atomic_numbers, cell and pbc
+ * are host pointers.  Forces are copied back only when copy_forces is true.
+ * Same result-handle semantics as mlipcpp_predict. */
+mlipcpp_error_t mlipcpp_b200_predict_device(mlipcpp_model_t model, int32_t n_atoms,
+                                            const float *d_positions,
+                                            const int32_t *atomic_numbers, const float *cell,
+                                            const bool *pbc,
+                                            const mlipcpp_predict_options_t *options,
+                                            bool copy_forces, mlipcpp_result_t *result);
+
+/* Enable per-phase CUDA-event timing of later predictions. */
+mlipcpp_error_t mlipcpp_b200_set_timing(mlipcpp_model_t model, bool enable);
+
+/* Phase times (ms) of the last prediction: h2d, neighbour list, graph prep,
+ * forward, backward, reductions, d2h, total. */
+mlipcpp_error_t mlipcpp_b200_last_timings(mlipcpp_model_t model, float times_ms[8]);
+
+/* Size of the last prediction: atoms, edges, max neighbours, device bytes
+ * held by the model (MiB). */
+mlipcpp_error_t mlipcpp_b200_last_shape(mlipcpp_model_t model, int64_t shape[4]);
+
+/* Full neighbour list (no self pairs) of one structure computed on the GPU,
+ * bit-identical to the reference's NeighborListBuilder
+ * (src/core/neighbor_list.cpp:118-297), in its enumeration order.  Host
+ * pointers in and out; writes at most `cap` pairs into the (optional)
+ * arrays and returns the total pair count, or -(error code) on failure, so
+ * a call with cap = 0 sizes the buffers.  shifts: [3 * pairs] int32,
+ * vectors: [3 * pairs] float, distances: [pairs] float. */
+int64_t mlipcpp_b200_neighbor_list(int32_t n_atoms, const float *positions, const float *cell,
+                                   const bool *pbc, float cutoff, int64_t cap, int32_t *centers,
+                                   int32_t *neighbors, int32_t *shifts, float *vectors,
+                                   float *distances);
+
+/* Number of CUDA kernels this library has launched in this process. */
+int64_t mlipcpp_b200_kernel_launches(void);
+
+/* CUDA device ordinal used by models created afterwards (default: the
+ * calling thread's current device). */
+mlipcpp_error_t mlipcpp_b200_set_device(int32_t device);
+
+/* Time every GEMM and attention launch with CUDA events on the model's
+ * stream (also resets the statistics). */
+mlipcpp_error_t mlipcpp_b200_set_kernel_profiling(mlipcpp_model_t model, bool enable);
+
+/* Cumulative per-class statistics since profiling was enabled: for classes
+ * GEMM, attention, neighbour list, other: {launches, total ms, algorithmic
+ * FLOPs, algorithmic HBM bytes} -> stats[4 * class + 0..3]. */
+mlipcpp_error_t mlipcpp_b200_kernel_stats(mlipcpp_model_t model, double stats[16]);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLIPCPP_B200_H */

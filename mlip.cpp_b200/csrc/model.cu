@@ -1,0 +1,661 @@
+// PET forward pass and hand-written backward pass to the edge vectors, on
+// ragged per-atom token blocks.  Replaces mlip.cpp's ggml graph
+// (src/models/pet/pet.cpp, pet_layers.cpp) and ggml autograd
+// (pet.cpp:292-320) with explicit kernels.
+//
+// Data layout in HBM (T = N + E token rows, row-major [T, d] fp32):
+//   atom i owns rows [off_i + i, off_i + i + 1 + n_i): its node token then
+//   its n_i edge tokens in neighbour-list slot order.  All dense layers run
+//   on all T rows at once; attention runs per atom on its own rows.
+// Stored for the backward pass (per transformer block): QKV [T,3d],
+// LN-normalised inputs and 1/sigma of both layer norms, the FFN
+// pre-activation [T,f]; per GNN layer the compress pre-activation [E,H] and
+// the readout pre-activations.  Nothing else: no dW is needed, so GEMM
+// inputs of linear layers are never kept.
+#include "model.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+#include "gguf.h"
+#include "kernels.cuh"
+#include "ops.cuh"
+
+namespace pet {
+
+namespace {
+
+// Bump allocator run twice: once to size (base == nullptr), once to assign.
+struct Plan {
+  char *base = nullptr;
+  size_t off = 0;
+  template <class T> T *take(size_t n) {
+    const size_t b = (n * sizeof(T) + 255) / 256 * 256;
+    T *p = base ? reinterpret_cast<T *>(base + off) : nullptr;
+    off += b;
+    return p;
+  }
+};
+
+struct BlockW {
+  const float *Win, *bin, *Wout, *bout, *ga, *ba, *gm, *bm, *W0, *b0, *W3, *b3;
+  const float *WinT, *WoutT, *W0T, *W3T;
+};
+struct HeadW {
+  const float *H0, *h0, *H2, *h2, *HL, *hl, *H0T, *H2T;
+};
+struct LayerW {
+  const float *We, *be, *node_emb, *nbr_emb, *C0, *c0, *C2, *c2, *C0T, *C2T;
+  BlockW blk[2];
+  HeadW node, edge;
+};
+
+struct Acts {
+  // graph
+  float *r, *fc, *dfc_dr, *key_mask;
+  int *edge_row, *node_row, *nbr_species, *rev;
+  // kept for backward
+  float *qkv[4], *xa[4], *ra[4], *zf[4], *xm[4], *rm[4];
+  float *zc[2], *zn1[2], *zn2[2], *ze1[2], *ze2[2];
+  float *gfc, *e_atom;
+  // forward scratch
+  float *cat, *hc, *xin, *xmid, *xl[2], *o, *u, *x1, *hf, *u2, *yn1, *yn2, *ye1, *ye2, *node_pred,
+      *edge_pred;
+  // backward scratch
+  float *dx, *dx2, *du, *dout, *dqkv, *dx1, *dhf, *dz1, *dz2, *dzc, *demb, *dmsg, *g4, *g, *F;
+};
+
+
+GemmArgs make_gemm(const float *A, int lda, const int *a_rows, const float *B, int ldb, float *C, int ldc,
+                   const int *c_rows, int M, int N, int K, const float *bias, int epi,
+                   float *Z = nullptr, int ldz = 0, const float *R = nullptr, int ldr = 0) {
+  GemmArgs g;
+  g.A = A; g.lda = lda; g.a_rows = a_rows;
+  g.B = B; g.ldb = ldb;
+  g.C = C; g.ldc = ldc; g.c_rows = c_rows;
+  g.M = M; g.N = N; g.K = K;
+  g.bias = bias; g.epi = epi; g.Z = Z; g.ldz = ldz; g.R = R; g.ldr = ldr;
+  return g;
+}
+
+// Algorithmic HBM bytes of one GEMM: A and C once, B once, plus epilogue
+// side streams (Z written or read, residual read).
+double gemm_bytes(const GemmArgs &g) {
+  double b = 4.0 * (static_cast<double>(g.M) * g.K + static_cast<double>(g.N) * g.K +
+                    static_cast<double>(g.M) * g.N);
+  if (g.epi == EPI_SILU || g.epi == EPI_DSILU || g.epi == EPI_RESID || g.epi == EPI_ACCUM)
+    b += 4.0 * static_cast<double>(g.M) * g.N;
+  return b;
+}
+
+}  // namespace
+
+struct PETModel::Internals {
+  Acts a;
+  LayerW lw[2];
+};
+
+int g_default_device = -1;  // set by mlipcpp_b200_set_device
+
+PETModel::PETModel() : in_(new Internals()) {
+  if (g_default_device >= 0) CUDA_CHECK(cudaSetDevice(g_default_device));
+  CUDA_CHECK(cudaGetDevice(&device_));
+  CUDA_CHECK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+  for (auto &e : ev_) CUDA_CHECK(cudaEventCreate(&e));
+}
+
+PETModel::~PETModel() {
+  for (auto &e : ev_)
+    if (e) cudaEventDestroy(e);
+  for (auto &e : ev_pool_) cudaEventDestroy(e);
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+void PETModel::mark_begin(cudaEvent_t &a) {
+  if (ev_used_ + 2 > ev_pool_.size()) {
+    for (int k = 0; k < 64; ++k) {
+      cudaEvent_t e;
+      CUDA_CHECK(cudaEventCreate(&e));
+      ev_pool_.push_back(e);
+    }
+  }
+  a = ev_pool_[ev_used_++];
+  CUDA_CHECK(cudaEventRecord(a, stream_));
+}
+
+void PETModel::mark_end(int cls, cudaEvent_t a, double flops, double bytes) {
+  cudaEvent_t b = ev_pool_[ev_used_++];
+  CUDA_CHECK(cudaEventRecord(b, stream_));
+  marks_.push_back({cls, a, b, flops, bytes});
+}
+
+void PETModel::collect_marks() {
+  for (const Mark &m : marks_) {
+    float ms = 0.f;
+    CUDA_CHECK(cudaEventElapsedTime(&ms, m.a, m.b));
+    KernelStat &k = kstats_[m.cls];
+    k.launches += 1;
+    k.ms += ms;
+    k.flops += m.flops;
+    k.bytes += m.bytes;
+  }
+  marks_.clear();
+  ev_used_ = 0;
+}
+
+const float *PETModel::w(const std::string &name) const {
+  auto it = wptr_.find(name);
+  if (it == wptr_.end()) throw Error(kErrIO, "Required tensor '" + name + "' not found");
+  return it->second;
+}
+
+size_t PETModel::device_bytes() const {
+  return wbuf_.cap + persist_.cap + scratch_.cap + nl_.center.cap * 10;
+}
+
+// ---------------------------------------------------------------------------
+// Weights (PETModel::load_from_gguf, pet.cpp:1100-1312)
+// ---------------------------------------------------------------------------
+void PETModel::load(const std::string &path, float cutoff_override) {
+  GGUFFile f(path);
+  const auto *emb = f.tensor("model.embedding.weight");
+  if (!emb) throw Error(kErrIO, "Required tensor 'model.embedding.weight' not found");
+  Hypers h;
+  // pet.cpp:1178-1187; like the reference, a cutoff override set before the
+  // load only survives when the file carries no pet.cutoff key.
+  h.cutoff = f.get_f32("pet.cutoff", cutoff_override > 0.0f ? cutoff_override : 4.5f);
+  h.heads = f.get_i32("pet.num_heads", 8);
+  h.gnn_layers = f.get_i32("pet.num_gnn_layers", 2);
+  h.ff = f.get_i32("pet.d_feedforward", 512);
+  h.dh = f.get_i32("pet.d_head", 128);
+  h.width = f.get_f32("pet.cutoff_width", 0.5f);
+  h.d = static_cast<int>(emb->ne[0]);
+  if (h.gnn_layers != 2) throw Error(kErrUnsupported, "pet layout supports exactly 2 GNN layers");
+  if (h.d % h.heads != 0) throw Error(kErrIO, "d_pet not divisible by num_heads");
+  const auto *c0 = f.tensor("model.gnn.0.compress.0.weight");
+  if (!c0) throw Error(kErrIO, "Required tensor 'model.gnn.0.compress.0.weight' not found");
+  h.hid = static_cast<int>(c0->ne[1]);
+  const auto *w0 = f.tensor("model.gnn.0.tl.0.mlp.0.weight");
+  if (w0) h.ff = static_cast<int>(w0->ne[1]);
+  const auto *hd = f.tensor("model.node_heads.energy.0.0.weight");
+  if (hd) h.dh = static_cast<int>(hd->ne[1]);
+
+  // Device copies: every f32 tensor, plus [in, out] transposes of the
+  // linears the backward pass multiplies by (dX = dY W).
+  std::vector<std::pair<std::string, std::vector<float>>> host;
+  for (const auto &kv : f.tensors()) {
+    const GGUFTensor &t = kv.second;
+    if (t.type != 0) continue;
+    std::vector<float> v(t.numel());
+    std::memcpy(v.data(), t.data.data(), v.size() * 4);
+    host.emplace_back(kv.first, std::move(v));
+  }
+  auto transpose_of = [&](const std::string &name) {
+    const GGUFTensor *t = f.tensor(name);
+    if (!t || t->ne.size() != 2) throw Error(kErrIO, "Required tensor '" + name + "' not found");
+    const int64_t in = t->ne[0], out = t->ne[1];
+    const float *src = reinterpret_cast<const float *>(t->data.data());
+    std::vector<float> v(in * out);
+    for (int64_t o = 0; o < out; ++o)
+      for (int64_t i = 0; i < in; ++i) v[i * out + o] = src[o * in + i];
+    host.emplace_back(name + ".T", std::move(v));
+  };
+  for (int l = 0; l < 2; ++l) {
+    const std::string p = "model.gnn." + std::to_string(l) + ".";
+    transpose_of(p + "compress.0.weight");
+    transpose_of(p + "compress.2.weight");
+    for (int t = 0; t < 2; ++t) {
+      const std::string q = p + "tl." + std::to_string(t) + ".";
+      transpose_of(q + "attn.in.weight");
+      transpose_of(q + "attn.out.weight");
+      transpose_of(q + "mlp.0.weight");
+      transpose_of(q + "mlp.3.weight");
+    }
+    for (const char *kind : {"node", "edge"}) {
+      const std::string hp = std::string("model.") + kind + "_heads.energy." + std::to_string(l) + ".";
+      transpose_of(hp + "0.weight");
+      transpose_of(hp + "2.weight");
+    }
+  }
+  size_t total = 0;
+  for (auto &kv : host) total += (kv.second.size() * 4 + 255) / 256 * 256;
+  wbuf_.ensure(total);
+  wptr_.clear();
+  std::vector<char> staging(total);
+  size_t off = 0;
+  for (auto &kv : host) {
+    std::memcpy(staging.data() + off, kv.second.data(), kv.second.size() * 4);
+    wptr_[kv.first] = reinterpret_cast<const float *>(wbuf_.as<char>() + off);
+    off += (kv.second.size() * 4 + 255) / 256 * 256;
+  }
+  CUDA_CHECK(cudaMemcpy(wbuf_.ptr, staging.data(), total, cudaMemcpyHostToDevice));
+
+  // composition map and species index (pet.cpp:1280-1303)
+  species_index_.clear();
+  composition_.clear();
+  const auto *zt = f.tensor("composition.atomic_numbers");
+  const auto *et = f.tensor("composition.energies");
+  if (zt && et) {
+    const int ns = static_cast<int>(zt->ne[0]);
+    const int32_t *z = reinterpret_cast<const int32_t *>(zt->data.data());
+    const float *e = reinterpret_cast<const float *>(et->data.data());
+    for (int i = 0; i < ns; ++i) {
+      composition_[z[i]] = e[i];
+      species_index_[z[i]] = i;
+    }
+    h.n_species = ns;
+  }
+  h_ = h;
+
+  // resolve pointers once
+  for (int l = 0; l < 2; ++l) {
+    const std::string p = "model.gnn." + std::to_string(l) + ".";
+    LayerW &L = in_->lw[l];
+    L.We = w(p + "edge_embedder.weight");
+    L.be = w(p + "edge_embedder.bias");
+    L.node_emb = w(p + "node_embedder.weight");
+    L.nbr_emb = l > 0 ? w(p + "neighbor_embedder.weight") : nullptr;
+    L.C0 = w(p + "compress.0.weight");
+    L.c0 = w(p + "compress.0.bias");
+    L.C2 = w(p + "compress.2.weight");
+    L.c2 = w(p + "compress.2.bias");
+    L.C0T = w(p + "compress.0.weight.T");
+    L.C2T = w(p + "compress.2.weight.T");
+    for (int t = 0; t < 2; ++t) {
+      const std::string q = p + "tl." + std::to_string(t) + ".";
+      BlockW &B = L.blk[t];
+      B.Win = w(q + "attn.in.weight"); B.bin = w(q + "attn.in.bias");
+      B.Wout = w(q + "attn.out.weight"); B.bout = w(q + "attn.out.bias");
+      B.ga = w(q + "norm_a.weight"); B.ba = w(q + "norm_a.bias");
+      B.gm = w(q + "norm_m.weight"); B.bm = w(q + "norm_m.bias");
+      B.W0 = w(q + "mlp.0.weight"); B.b0 = w(q + "mlp.0.bias");
+      B.W3 = w(q + "mlp.3.weight"); B.b3 = w(q + "mlp.3.bias");
+      B.WinT = w(q + "attn.in.weight.T"); B.WoutT = w(q + "attn.out.weight.T");
+      B.W0T = w(q + "mlp.0.weight.T"); B.W3T = w(q + "mlp.3.weight.T");
+    }
+    for (int k = 0; k < 2; ++k) {
+      const std::string kind = k == 0 ? "node" : "edge";
+      const std::string hp = "model." + kind + "_heads.energy." + std::to_string(l) + ".";
+      const std::string lp = "model." + kind + "_last_layers.energy." + std::to_string(l) + ".energy___0.";
+      HeadW &H = k == 0 ? L.node : L.edge;
+      H.H0 = w(hp + "0.weight"); H.h0 = w(hp + "0.bias");
+      H.H2 = w(hp + "2.weight"); H.h2 = w(hp + "2.bias");
+      H.HL = w(lp + "weight"); H.hl = w(lp + "bias");
+      H.H0T = w(hp + "0.weight.T"); H.H2T = w(hp + "2.weight.T");
+    }
+  }
+  (void)w("model.embedding.weight");
+}
+
+// ---------------------------------------------------------------------------
+// Memory plan
+// ---------------------------------------------------------------------------
+static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, int N, int E, bool grad) {
+  const size_t T = static_cast<size_t>(N) + E, d = h.d, f = h.ff, r = h.dh, H = h.hid;
+  const size_t En = E > 0 ? E : 1, Nn = N > 0 ? N : 1;
+  // persistent (graph + activations kept for backward)
+  a.r = P.take<float>(En); a.fc = P.take<float>(En); a.dfc_dr = P.take<float>(En);
+  a.key_mask = P.take<float>(En);
+  a.edge_row = P.take<int>(En); a.node_row = P.take<int>(Nn); a.nbr_species = P.take<int>(En);
+  a.rev = P.take<int>(En);
+  for (int b = 0; b < 4; ++b) {
+    a.qkv[b] = P.take<float>(T * 3 * d);
+    a.xa[b] = P.take<float>(T * d); a.ra[b] = P.take<float>(T);
+    a.zf[b] = P.take<float>(T * f);
+    a.xm[b] = P.take<float>(T * d); a.rm[b] = P.take<float>(T);
+  }
+  for (int l = 0; l < 2; ++l) {
+    a.zc[l] = P.take<float>(En * H);
+    a.zn1[l] = P.take<float>(Nn * r); a.zn2[l] = P.take<float>(Nn * r);
+    a.ze1[l] = P.take<float>(En * r); a.ze2[l] = P.take<float>(En * r);
+  }
+  a.gfc = P.take<float>(En);
+  a.e_atom = P.take<float>(Nn);
+  a.F = P.take<float>(3 * Nn);
+  a.g = P.take<float>(3 * En);
+  a.g4 = P.take<float>(4 * En);
+  // forward scratch
+  Plan fs = S;
+  a.cat = fs.take<float>(En * 3 * d); a.hc = fs.take<float>(En * H);
+  a.xin = fs.take<float>(T * d); a.xmid = fs.take<float>(T * d);
+  a.xl[0] = fs.take<float>(T * d); a.xl[1] = fs.take<float>(T * d);
+  a.o = fs.take<float>(T * d); a.u = fs.take<float>(T * d); a.x1 = fs.take<float>(T * d);
+  a.hf = fs.take<float>(T * f); a.u2 = fs.take<float>(T * d);
+  a.yn1 = fs.take<float>(Nn * r); a.yn2 = fs.take<float>(Nn * r);
+  a.ye1 = fs.take<float>(En * r); a.ye2 = fs.take<float>(En * r);
+  a.node_pred = fs.take<float>(Nn); a.edge_pred = fs.take<float>(En);
+  size_t fwd_end = fs.off;
+  // backward scratch (aliases the forward scratch)
+  Plan bs = S;
+  if (grad) {
+    a.dx = bs.take<float>(T * d); a.dx2 = bs.take<float>(T * d); a.du = bs.take<float>(T * d);
+    a.dout = bs.take<float>(T * d); a.dqkv = bs.take<float>(T * 3 * d); a.dx1 = bs.take<float>(T * d);
+    a.dhf = bs.take<float>(T * f);
+    const size_t rows = std::max(Nn, En);
+    a.dz1 = bs.take<float>(rows * r); a.dz2 = bs.take<float>(rows * r);
+    a.dzc = bs.take<float>(En * H); a.demb = bs.take<float>(En * d); a.dmsg = bs.take<float>(En * d);
+  }
+  S.off = std::max(fwd_end, bs.off);
+}
+
+// ---------------------------------------------------------------------------
+// Forward + backward
+// ---------------------------------------------------------------------------
+void PETModel::forward_backward(bool grad) {
+  const Acts &a = in_->a;
+  const LayerW *g_lw = in_->lw;
+  const Hypers &h = h_;
+  const int N = N_, E = E_, T = T_;
+  const int d = h.d, f = h.ff, r = h.dh, H = h.hid;
+  cudaStream_t s = stream_;
+  const int *offset = nl_.offset.as<int>();
+  const int *species = d_species_.as<int>();
+  const float *emb0 = w("model.embedding.weight");
+
+  auto gemm = [&](const float *A, int lda, const int *a_rows, const float *B, int ldb, float *C, int ldc,
+                  const int *c_rows, int M, int N, int K, const float *bias, int epi, cudaStream_t st,
+                  float *Z = nullptr, int ldz = 0, const float *R = nullptr, int ldr = 0) {
+    GemmArgs g = make_gemm(A, lda, a_rows, B, ldb, C, ldc, c_rows, M, N, K, bias, epi, Z, ldz, R, ldr);
+    cudaEvent_t e0 = nullptr;
+    if (kprof_) mark_begin(e0);
+    gemm_f32(g, st);
+    if (kprof_) mark_end(KC_GEMM, e0, 2.0 * M * N * static_cast<double>(K), gemm_bytes(g));
+  };
+  auto attn = [&](bool backward, const AttnArgs &x) {
+    cudaEvent_t e0 = nullptr;
+    if (kprof_) mark_begin(e0);
+    if (backward) attention_bwd(x, s); else attention_fwd(x, s);
+    if (kprof_) mark_end(KC_ATTENTION, e0, 0.0, 4.0 * T * (backward ? 7.0 : 4.0) * d);
+  };
+  AttnArgs at{};
+  at.key_mask = a.key_mask;
+  at.offset = offset;
+  at.n_atoms = N;
+  at.d = d;
+  at.heads = h.heads;
+  at.max_tokens = max_tok_;
+
+  auto block_fwd = [&](int b, const float *x, float *out) {
+    const BlockW &B = g_lw[b / 2].blk[b % 2];
+    gemm(x, d, nullptr, B.Win, d, a.qkv[b], 3 * d, nullptr, T, 3 * d, d, B.bin, EPI_STORE, s);
+    at.qkv = a.qkv[b];
+    at.out = a.o;
+    attn(false, at);
+    gemm(a.o, d, nullptr, B.Wout, d, a.u, d, nullptr, T, d, d, B.bout, EPI_RESID, s, nullptr, 0, x, d);
+    layer_norm_fwd(a.u, B.ga, B.ba, a.x1, a.xa[b], a.ra[b], T, d, s);
+    gemm(a.x1, d, nullptr, B.W0, d, a.hf, f, nullptr, T, f, d, B.b0, EPI_SILU, s, a.zf[b], f);
+    gemm(a.hf, f, nullptr, B.W3, f, a.u2, d, nullptr, T, d, f, B.b3, EPI_RESID, s, nullptr, 0, a.x1, d);
+    layer_norm_fwd(a.u2, B.gm, B.bm, out, a.xm[b], a.rm[b], T, d, s);
+  };
+
+  for (int l = 0; l < 2; ++l) {
+    const LayerW &L = g_lw[l];
+    const int K = (l == 0 ? 2 : 3) * d;
+    if (E > 0) {
+      FeaturizeArgs fa{};
+      fa.n_edges = E; fa.d = d; fa.layer = l;
+      fa.vec = nl_.vec.as<float>(); fa.r = a.r;
+      fa.nbr_species = a.nbr_species; fa.rev = a.rev; fa.edge_row = a.edge_row;
+      fa.We = L.We; fa.be = L.be; fa.emb0 = emb0; fa.nbr_emb = L.nbr_emb; fa.x_prev = a.xl[0];
+      fa.cat = a.cat;
+      featurize(fa, s);
+      gemm(a.cat, K, nullptr, L.C0, K, a.hc, H, nullptr, E, H, K, L.c0, EPI_SILU, s, a.zc[l], H);
+      gemm(a.hc, H, nullptr, L.C2, H, a.xin, d, a.edge_row, E, d, H, L.c2, EPI_STORE, s);
+    }
+    node_tokens(L.node_emb, species, a.node_row, a.xin, N, d, s);
+    block_fwd(2 * l, a.xin, a.xmid);
+    block_fwd(2 * l + 1, a.xmid, a.xl[l]);
+    // readout (pet_layers.cpp:920-1015)
+    gemm(a.xl[l], d, a.node_row, L.node.H0, d, a.yn1, r, nullptr, N, r, d, L.node.h0, EPI_SILU, s, a.zn1[l], r);
+    gemm(a.yn1, r, nullptr, L.node.H2, r, a.yn2, r, nullptr, N, r, r, L.node.h2, EPI_SILU, s, a.zn2[l], r);
+    head_last(a.yn2, L.node.HL, L.node.hl, a.node_pred, N, r, s);
+    if (E > 0) {
+      gemm(a.xl[l], d, a.edge_row, L.edge.H0, d, a.ye1, r, nullptr, E, r, d, L.edge.h0, EPI_SILU, s, a.ze1[l], r);
+      gemm(a.ye1, r, nullptr, L.edge.H2, r, a.ye2, r, nullptr, E, r, r, L.edge.h2, EPI_SILU, s, a.ze2[l], r);
+      head_last(a.ye2, L.edge.HL, L.edge.hl, a.edge_pred, E, r, s);
+      add_vec(a.edge_pred, a.gfc, E, l > 0, s);
+    }
+    atom_energy(a.node_pred, a.edge_pred, a.fc, offset, a.e_atom, N, l > 0, s);
+  }
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[4], s));
+  if (!grad) return;
+
+  // ---- backward ----------------------------------------------------------
+  auto readout_bwd = [&](int l, float *dst) {
+    const LayerW &L = g_lw[l];
+    head_last_bwd(a.zn2[l], L.node.HL, nullptr, a.dz2, N, r, s);
+    gemm(a.dz2, r, nullptr, L.node.H2T, r, a.dz1, r, nullptr, N, r, r, nullptr, EPI_DSILU, s, a.zn1[l], r);
+    gemm(a.dz1, r, nullptr, L.node.H0T, r, dst, d, a.node_row, N, d, r, nullptr, EPI_STORE, s);
+    if (E > 0) {
+      head_last_bwd(a.ze2[l], L.edge.HL, a.fc, a.dz2, E, r, s);
+      gemm(a.dz2, r, nullptr, L.edge.H2T, r, a.dz1, r, nullptr, E, r, r, nullptr, EPI_DSILU, s, a.ze1[l], r);
+      gemm(a.dz1, r, nullptr, L.edge.H0T, r, dst, d, a.edge_row, E, d, r, nullptr, EPI_STORE, s);
+    }
+  };
+  auto block_bwd = [&](int b, const float *dy, float *dxin) {
+    const BlockW &B = g_lw[b / 2].blk[b % 2];
+    layer_norm_bwd(dy, a.xm[b], a.rm[b], B.gm, a.du, T, d, s);
+    gemm(a.du, d, nullptr, B.W3T, d, a.dhf, f, nullptr, T, f, d, nullptr, EPI_DSILU, s, a.zf[b], f);
+    gemm(a.dhf, f, nullptr, B.W0T, f, a.dx1, d, nullptr, T, d, f, nullptr, EPI_RESID, s, nullptr, 0, a.du, d);
+    layer_norm_bwd(a.dx1, a.xa[b], a.ra[b], B.ga, a.du, T, d, s);
+    gemm(a.du, d, nullptr, B.WoutT, d, a.dout, d, nullptr, T, d, d, nullptr, EPI_STORE, s);
+    at.qkv = a.qkv[b];
+    at.d_out = a.dout;
+    at.d_qkv = a.dqkv;
+    attn(true, at);
+    gemm(a.dqkv, 3 * d, nullptr, B.WinT, 3 * d, dxin, d, nullptr, T, d, 3 * d, nullptr, EPI_RESID, s, nullptr,
+         0, a.du, d);
+  };
+  auto compress_bwd = [&](int l, const float *dtok, bool accumulate) {
+    const LayerW &L = g_lw[l];
+    gemm(dtok, d, a.edge_row, L.C2T, d, a.dzc, H, nullptr, E, H, d, nullptr, EPI_DSILU, s, a.zc[l], H);
+    gemm(a.dzc, H, nullptr, L.C0T, H, a.demb, d, nullptr, E, d, H, nullptr, EPI_STORE, s);
+    if (l == 1)
+      gemm(a.dzc, H, nullptr, L.C0T + static_cast<size_t>(2) * d * H, H, a.dmsg, d, nullptr, E, d, H, nullptr,
+           EPI_STORE, s);
+    edge_embed_bwd(a.demb, d, L.We, a.g4, E, d, accumulate, s);
+  };
+
+  readout_bwd(1, a.dx);
+  block_bwd(3, a.dx, a.dx2);
+  block_bwd(2, a.dx2, a.dx);
+  if (E > 0) compress_bwd(1, a.dx, false);
+  readout_bwd(0, a.dx);
+  if (E > 0) message_bwd(a.dmsg, d, a.rev, a.edge_row, a.dx, E, d, s);
+  block_bwd(1, a.dx, a.dx2);
+  block_bwd(0, a.dx2, a.dx);
+  if (E > 0) {
+    compress_bwd(0, a.dx, true);
+    edge_grad(a.g4, a.gfc, a.dfc_dr, nl_.vec.as<float>(), a.r, a.g, E, s);
+  }
+  forces(a.g, offset, nl_.nbr.as<int>(), a.rev, a.F, N, E, s);
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[5], s));
+}
+
+// ---------------------------------------------------------------------------
+// Prediction
+// ---------------------------------------------------------------------------
+void PETModel::run_group(const float *d_pos, int n_atoms, const std::vector<const SystemView *> &systems,
+                         const std::vector<int> &atom_begin, bool grad, std::vector<Result *> &results,
+                         bool copy_forces) {
+  cudaStream_t s = stream_;
+  const int n_sys = static_cast<int>(systems.size());
+  N_ = n_atoms;
+  n_sys_ = n_sys;
+  // species indices (pet_batch.cpp:146-167): unknown Z is an error
+  int *hsp = static_cast<int *>(h_species_.ensure(sizeof(int) * (n_atoms + 1) + sizeof(int) * (n_sys + 1)));
+  for (int k = 0; k < n_sys; ++k) {
+    const SystemView &sv = *systems[k];
+    for (int i = 0; i < sv.n_atoms; ++i) {
+      auto it = species_index_.find(sv.numbers[i]);
+      if (it == species_index_.end())
+        throw Error(kErrComputation, "Unknown atomic number " + std::to_string(sv.numbers[i]) +
+                                         " not found in species_to_index mapping");
+      hsp[atom_begin[k] + i] = it->second;
+    }
+  }
+  int *hsb = hsp + n_atoms + 1;
+  for (int k = 0; k <= n_sys; ++k) hsb[k] = atom_begin[k];
+  int *dsp = static_cast<int *>(d_species_.ensure(sizeof(int) * (n_atoms + 1)));
+  int *dsb = static_cast<int *>(d_sys_atoms_.ensure(sizeof(int) * (n_sys + 1)));
+  CUDA_CHECK(cudaMemcpyAsync(dsp, hsp, sizeof(int) * n_atoms, cudaMemcpyHostToDevice, s));
+  CUDA_CHECK(cudaMemcpyAsync(dsb, hsb, sizeof(int) * (n_sys + 1), cudaMemcpyHostToDevice, s));
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[1], s));
+
+  // neighbour list
+  const bool periodic = systems[0]->cell != nullptr;
+  if (periodic) {
+    if (n_sys != 1) throw Error(kErrInternal, "periodic systems run one per group");
+    GridParams g;
+    make_grid_params(systems[0]->cell, systems[0]->pbc, h_.cutoff, &g);
+    build_periodic_nl(d_pos, n_atoms, g, nl_, nls_, s);
+  } else {
+    std::vector<int> b(n_atoms), e(n_atoms);
+    for (int k = 0; k < n_sys; ++k)
+      for (int i = atom_begin[k]; i < atom_begin[k + 1]; ++i) {
+        b[i] = atom_begin[k];
+        e[i] = atom_begin[k + 1];
+      }
+    int *db = static_cast<int *>(d_sys_begin_.ensure(sizeof(int) * (n_atoms + 1)));
+    int *de = static_cast<int *>(d_sys_end_.ensure(sizeof(int) * (n_atoms + 1)));
+    CUDA_CHECK(cudaMemcpyAsync(db, b.data(), sizeof(int) * n_atoms, cudaMemcpyHostToDevice, s));
+    CUDA_CHECK(cudaMemcpyAsync(de, e.data(), sizeof(int) * n_atoms, cudaMemcpyHostToDevice, s));
+    build_open_nl(d_pos, db, de, n_atoms, h_.cutoff, nl_, nls_, s);
+  }
+  E_ = nl_.n_edges;
+  T_ = N_ + E_;
+  max_tok_ = nl_.max_count + 1;
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[2], s));
+  if (max_tok_ > attention_max_tokens(h_.d / h_.heads))
+    throw Error(kErrUnsupported, "an atom has " + std::to_string(nl_.max_count) +
+                                     " neighbours, above the supported maximum of " +
+                                     std::to_string(attention_max_tokens(h_.d / h_.heads) - 1));
+
+  // memory plan: size, allocate, assign
+  Plan P, S;
+  plan_memory(P, S, in_->a, h_, N_, E_, grad);
+  persist_.ensure(P.off);
+  scratch_.ensure(S.off);
+  P = Plan{persist_.as<char>(), 0};
+  S = Plan{scratch_.as<char>(), 0};
+  plan_memory(P, S, in_->a, h_, N_, E_, grad);
+  const Acts &a = in_->a;
+
+  EdgePrepArgs ep{};
+  ep.n_atoms = N_; ep.n_edges = E_;
+  ep.offset = nl_.offset.as<int>(); ep.center = nl_.center.as<int>(); ep.nbr = nl_.nbr.as<int>();
+  ep.shift = nl_.shift.as<int>(); ep.species = dsp;
+  ep.vec = nl_.vec.as<float>(); ep.dist_nl = nl_.dist.as<float>();
+  ep.cutoff = h_.cutoff; ep.width = h_.width;
+  ep.r = a.r; ep.fc = a.fc; ep.dfc_dr = a.dfc_dr; ep.key_mask = a.key_mask;
+  ep.edge_row = a.edge_row; ep.node_row = a.node_row; ep.nbr_species = a.nbr_species; ep.rev = a.rev;
+  edge_prep(ep, s);
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[3], s));
+
+  forward_backward(grad);
+
+  // per-system energy and virial in f64 (pet.cpp:542-548, 1041-1077)
+  double *red = static_cast<double *>(d_red_.ensure(sizeof(double) * 7 * (n_sys + 1)));
+  reduce_systems(nl_.vec.as<float>(), a.g, a.e_atom, nl_.offset.as<int>(), dsb, n_sys, red + n_sys, red,
+                 grad && E_ > 0, s);
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[6], s));
+  const size_t fbytes = (grad && copy_forces) ? sizeof(float) * 3 * n_atoms : 0;
+  char *hout = static_cast<char *>(h_out_.ensure(sizeof(double) * 7 * n_sys + fbytes + 16));
+  CUDA_CHECK(cudaMemcpyAsync(hout, red, sizeof(double) * 7 * n_sys, cudaMemcpyDeviceToHost, s));
+  if (fbytes)
+    CUDA_CHECK(cudaMemcpyAsync(hout + sizeof(double) * 7 * n_sys, a.F, fbytes, cudaMemcpyDeviceToHost, s));
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[7], s));
+  CUDA_CHECK(cudaStreamSynchronize(s));
+  if (kprof_) collect_marks();
+
+  const double *he = reinterpret_cast<const double *>(hout);
+  const double *hv = he + n_sys;
+  const float *hF = reinterpret_cast<const float *>(hout + sizeof(double) * 7 * n_sys);
+  for (int k = 0; k < n_sys; ++k) {
+    const SystemView &sv = *systems[k];
+    Result &R = *results[k];
+    double tot = he[k];
+    for (int i = 0; i < sv.n_atoms; ++i) {
+      auto it = composition_.find(sv.numbers[i]);
+      if (it != composition_.end()) tot += it->second;
+    }
+    R.energy = static_cast<float>(tot);
+    R.has_forces = false;
+    R.has_stress = false;
+    R.forces.clear();
+    R.stress.clear();
+    if (grad) {
+      R.has_forces = true;
+      if (copy_forces) R.forces.assign(hF + 3 * atom_begin[k], hF + 3 * atom_begin[k + 1]);
+      R.stress.assign(6, 0.0f);
+      const float *m = sv.cell;
+      if (m && (sv.pbc[0] || sv.pbc[1] || sv.pbc[2])) {
+        // pet.cpp:1079-1097: f32 determinant, stress only when |V| > 1e-10
+        float vol = m[0] * (m[4] * m[8] - m[5] * m[7]) - m[1] * (m[3] * m[8] - m[5] * m[6]) +
+                    m[2] * (m[3] * m[7] - m[4] * m[6]);
+        vol = std::fabs(vol);
+        if (vol > 1e-10f) {
+          for (int c = 0; c < 6; ++c) R.stress[c] = static_cast<float>(hv[6 * k + c]) / vol;
+          R.has_stress = true;
+        }
+      }
+    }
+  }
+  if (timing_) {
+    float ms;
+    CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[0], ev_[1])); times_.h2d = ms;
+    CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[1], ev_[2])); times_.nl = ms;
+    CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[2], ev_[3])); times_.prep = ms;
+    CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[3], ev_[4])); times_.forward = ms;
+    if (grad) { CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[4], ev_[5])); times_.backward = ms; }
+    CUDA_CHECK(cudaEventElapsedTime(&ms, grad ? ev_[5] : ev_[4], ev_[6])); times_.reduce = ms;
+    CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[6], ev_[7])); times_.d2h = ms;
+    CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[0], ev_[7])); times_.total = ms;
+  }
+}
+
+std::vector<Result> PETModel::predict(const std::vector<SystemView> &systems, bool grad) {
+  std::vector<Result> out(systems.size());
+  if (systems.empty()) return out;
+  if (wptr_.empty()) throw Error(3, "Model weights not loaded");
+  CUDA_CHECK(cudaSetDevice(device_));
+  auto run = [&](const std::vector<int> &idx) {
+    std::vector<const SystemView *> sv;
+    std::vector<Result *> rs;
+    std::vector<int> begin{0};
+    for (int k : idx) {
+      sv.push_back(&systems[k]);
+      rs.push_back(&out[k]);
+      begin.push_back(begin.back() + systems[k].n_atoms);
+    }
+    const int n = begin.back();
+    float *hp = static_cast<float *>(h_pos_.ensure(sizeof(float) * 3 * (n + 1)));
+    for (size_t k = 0; k < sv.size(); ++k)
+      std::memcpy(hp + 3 * begin[k], sv[k]->positions, sizeof(float) * 3 * sv[k]->n_atoms);
+    float *dp = static_cast<float *>(d_pos_.ensure(sizeof(float) * 3 * (n + 1)));
+    if (timing_) CUDA_CHECK(cudaEventRecord(ev_[0], stream_));
+    CUDA_CHECK(cudaMemcpyAsync(dp, hp, sizeof(float) * 3 * n, cudaMemcpyHostToDevice, stream_));
+    run_group(dp, n, sv, begin, grad, rs, true);
+  };
+  std::vector<int> open;
+  for (size_t k = 0; k < systems.size(); ++k) {
+    if (systems[k].n_atoms <= 0) continue;
+    if (systems[k].cell) run({static_cast<int>(k)});
+    else open.push_back(static_cast<int>(k));
+  }
+  if (!open.empty()) run(open);
+  return out;
+}
+
+void PETModel::predict_device(const float *d_pos, const SystemView &sys, bool grad, Result &out,
+                              bool copy_forces) {
+  if (wptr_.empty()) throw Error(3, "Model weights not loaded");
+  std::vector<const SystemView *> sv{&sys};
+  std::vector<Result *> rs{&out};
+  std::vector<int> begin{0, sys.n_atoms};
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[0], stream_));
+  run_group(d_pos, sys.n_atoms, sv, begin, grad, rs, copy_forces);
+}
+
+}  // namespace pet

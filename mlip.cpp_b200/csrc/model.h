@@ -1,0 +1,127 @@
+// PET energy / force / stress model on one B200: the replacement for
+// mlip.cpp's PETModel (src/models/pet/pet.{h,cpp}) behind the mlipcpp C API.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "neighbor.cuh"
+
+namespace pet {
+
+struct Hypers {
+  int d = 256, heads = 8, ff = 512, dh = 128, hid = 256;  // hid: compress hidden width
+  int gnn_layers = 2, attn_layers = 2, n_species = 0;
+  float cutoff = 4.5f, width = 0.5f;
+};
+
+// One structure as the C API receives it (host pointers, not owned).
+struct SystemView {
+  int n_atoms = 0;
+  const float *positions = nullptr;    // [n, 3]
+  const int32_t *numbers = nullptr;    // [n]
+  const float *cell = nullptr;         // [9] row-major or null
+  bool pbc[3] = {true, true, true};
+};
+
+struct Result {
+  float energy = 0.0f;
+  std::vector<float> forces;  // [n, 3]
+  std::vector<float> stress;  // [6] Voigt xx yy zz yz xz xy
+  bool has_forces = false;
+  bool has_stress = false;
+};
+
+// Kernel classes timed individually when kernel profiling is on.
+enum KernelClass { KC_GEMM = 0, KC_ATTENTION = 1, KC_NEIGHBOR = 2, KC_OTHER = 3, KC_COUNT = 4 };
+
+struct KernelStat {
+  long long launches = 0;
+  double ms = 0.0, flops = 0.0, bytes = 0.0;
+};
+
+// Per-phase CUDA-event timings of the last predict (milliseconds).
+struct PhaseTimes {
+  float h2d = 0, nl = 0, prep = 0, forward = 0, backward = 0, reduce = 0, d2h = 0, total = 0;
+};
+
+class PETModel {
+ public:
+  PETModel();
+  ~PETModel();
+  PETModel(const PETModel &) = delete;
+  PETModel &operator=(const PETModel &) = delete;
+
+  // PETModel::load_from_gguf (pet.cpp:1100-1312)
+  void load(const std::string &path, float cutoff_override = 0.0f);
+  float cutoff() const { return h_.cutoff; }
+  const Hypers &hypers() const { return h_; }
+
+  // predict_batch (pet.cpp:125-694).  With compute_grad the result carries
+  // forces, and stress for periodic systems.
+  std::vector<Result> predict(const std::vector<SystemView> &systems, bool compute_grad);
+
+  // Device-resident entry for benchmarks: positions already on the device.
+  void predict_device(const float *d_pos, const SystemView &sys, bool compute_grad, Result &out,
+                      bool copy_forces);
+
+  const PhaseTimes &last_times() const { return times_; }
+  // Per-launch CUDA events around GEMM and attention launches, accumulated
+  // into kernel_stats() after each predict (cumulative until reset).
+  void set_kernel_profiling(bool on) { kprof_ = on; }
+  const KernelStat *kernel_stats() const { return kstats_; }
+  void reset_kernel_stats() { for (auto &k : kstats_) k = KernelStat{}; }
+  int last_atoms() const { return N_; }
+  int last_edges() const { return E_; }
+  int last_max_neighbors() const { return max_tok_ - 1; }
+  void set_timing(bool on) { timing_ = on; }
+  cudaStream_t stream() const { return stream_; }
+  size_t device_bytes() const;
+
+ private:
+  struct Group;  // systems that share one neighbour-list launch
+  void run_group(const float *d_pos, int n_atoms, const std::vector<const SystemView *> &systems,
+                 const std::vector<int> &atom_begin, bool compute_grad,
+                 std::vector<Result *> &results, bool copy_forces);
+  void forward_backward(bool compute_grad);
+  const float *w(const std::string &name) const;
+
+  struct Internals;  // device pointers of weights and activations (model.cu)
+  std::unique_ptr<Internals> in_;
+  Hypers h_;
+  cudaStream_t stream_ = nullptr;
+  int device_ = 0;
+  DevBuf wbuf_;
+  std::map<std::string, const float *> wptr_;
+  std::map<int, int> species_index_;
+  std::map<int, float> composition_;
+
+  // per-call device state
+  DevBuf d_pos_, d_species_, d_sys_begin_, d_sys_end_, d_sys_atoms_;
+  EdgeList nl_;
+  NLScratch nls_;
+  DevBuf persist_, scratch_;
+  DevBuf d_red_;  // per-system energy (f64) + virial (f64 x 6)
+  HostBuf h_pos_, h_species_, h_out_;
+  int N_ = 0, E_ = 0, T_ = 0, max_tok_ = 0, n_sys_ = 0;
+  bool timing_ = false;
+  bool kprof_ = false;
+  KernelStat kstats_[KC_COUNT];
+  struct Mark { int cls; cudaEvent_t a, b; double flops, bytes; };
+  std::vector<Mark> marks_;
+  std::vector<cudaEvent_t> ev_pool_;
+  size_t ev_used_ = 0;
+  void mark_begin(cudaEvent_t &a);
+  void mark_end(int cls, cudaEvent_t a, double flops, double bytes);
+  void collect_marks();
+  PhaseTimes times_;
+  cudaEvent_t ev_[8] = {};
+};
+
+}  // namespace pet

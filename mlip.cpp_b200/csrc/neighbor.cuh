@@ -1,0 +1,57 @@
+// GPU cell-list neighbour search, bit-exact with mlip.cpp's
+// NeighborListBuilder (src/core/neighbor_list.cpp:126-297).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace pet {
+
+// Bin grid of one periodic cell, computed on the host in fp64 with the
+// reference's operation order (CellGrid ctor, neighbor_list.cpp:38-66).
+struct GridParams {
+  double inv[9];     // f32 cofactor inverse widened to f64 (system.cpp:19-48)
+  double bv[9];      // bin vectors: bv[3*a + xyz] = cell[a] * (1.0 / nb[a])
+  int nb[3];         // bins per axis
+  int ns[3];         // search half-width per axis
+  int pbc[3];
+  double cutoff_sq;  // (double)cutoff squared in f64 (periodic path)
+};
+
+void make_grid_params(const float cell[9], const bool pbc[3], float cutoff, GridParams *g);
+void cell_inverse_f32(const float m[9], float inv[9]);
+
+// Edges of a neighbour list in centre-major order (the reference's slot
+// order inside each centre), SoA, sized by `ensure`.
+struct EdgeList {
+  int n_atoms = 0;
+  int n_edges = 0;
+  int max_count = 0;
+  DevBuf count, offset;        // [N], [N+1]
+  DevBuf center, nbr, shift;   // [E], [E], [3E]
+  DevBuf vec, dist;            // [3E] f32, [E] f32
+};
+
+struct NLScratch {
+  DevBuf braw, bin_of, bin_count, bin_start, bin_cursor, bin_atoms, scan_aux;
+};
+
+// Build the full list (no self pairs) for one periodic system.  `pos` is a
+// device [N,3] f32 array.  Synchronises once on `stream` to size the edge
+// arrays.  Raises Error on failure.
+void build_periodic_nl(const float *pos, int n, const GridParams &g, EdgeList &out,
+                       NLScratch &s, cudaStream_t stream);
+
+// Open-boundary O(n^2) search, batched: atom a belongs to the system whose
+// atoms are [sys_begin[a], sys_end[a]).  `cutoff_sq_f32` is the f32 product
+// cutoff*cutoff the reference compares against (neighbor_list.cpp:131).
+void build_open_nl(const float *pos, const int *sys_begin, const int *sys_end, int n,
+                   float cutoff, EdgeList &out, NLScratch &s, cudaStream_t stream);
+
+// Exclusive scan of n int32 counts into out[0..n] (out[n] = total) and the
+// maximum count into *max_out (device scalars); single CTA.
+void scan_counts(const int *in, int *out, int *max_out, int n, cudaStream_t stream);
+
+}  // namespace pet

@@ -1,0 +1,372 @@
+// Per-edge / per-atom kernels of the PET pass.  All are HBM- or
+// latency-bound elementwise work; grids are grid-stride over edges or atoms.
+#include <cuda_fp16.h>
+
+#include <cfloat>
+#include <cmath>
+
+#include "common.cuh"
+#include "ops.cuh"
+
+namespace pet {
+namespace {
+
+constexpr float kPi = 3.14159265358979323846f;
+
+int grid_for(int64_t n, int block) {
+  int64_t g = (n + block - 1) / block;
+  if (g < 1) g = 1;
+  if (g > 148 * 64) g = 148 * 64;
+  return static_cast<int>(g);
+}
+
+__global__ void k_edge_prep(EdgePrepArgs a) {
+  const float inv_delta = 1.0f / a.width;
+  const float off = (a.width - a.cutoff) * inv_delta;
+  const int total = a.n_edges > a.n_atoms ? a.n_edges : a.n_atoms;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
+    if (e < a.n_atoms) a.node_row[e] = a.offset[e] + e;
+    if (e >= a.n_edges) continue;
+    const int i = a.center[e], j = a.nbr[e];
+    const float x = a.vec[3 * e], y = a.vec[3 * e + 1], z = a.vec[3 * e + 2];
+    // in-graph distance and cutoff (pet.cpp:208-256)
+    const float r = sqrtf(x * x + y * y + z * z);
+    const float xx = r * inv_delta + off;
+    const float xc = fminf(fmaxf(xx, 0.0f), 1.0f);
+    a.r[e] = r;
+    a.fc[e] = cosf(xc * kPi) * 0.5f + 0.5f;
+    a.dfc_dr[e] = (xx > 0.0f && xx < 1.0f) ? -0.5f * sinf(xc * kPi) * kPi * inv_delta : 0.0f;
+    // attention key mask: fp16(log(smooth_cutoff(d_nl))) (pet_batch.cpp:37-47, 628-638);
+    // cos/log evaluated in f64 and rounded once, i.e. correctly rounded f32.
+    const float dn = a.dist_nl[e];
+    float fcm;
+    if (dn >= a.cutoff) fcm = 0.0f;
+    else if (dn <= a.cutoff - a.width) fcm = 1.0f;
+    else {
+      const float xm = (dn - a.cutoff + a.width) / a.width;
+      fcm = 0.5f + 0.5f * static_cast<float>(cos(static_cast<double>(kPi * xm)));
+    }
+    a.key_mask[e] = fcm > 0.0f
+        ? __half2float(__float2half_rn(static_cast<float>(log(static_cast<double>(fcm)))))
+        : -INFINITY;
+    a.edge_row[e] = e + i + 1;
+    a.nbr_species[e] = a.species[j];
+    // reverse edge (j -> i, -S); the reference's hash map keeps the last edge
+    // inserted under a key, so the last match wins (pet_batch.cpp:416-436)
+    const int s0 = a.shift[3 * e], s1 = a.shift[3 * e + 1], s2 = a.shift[3 * e + 2];
+    int rv = -1;
+    for (int k = a.offset[j], ke = a.offset[j + 1]; k < ke; ++k) {
+      if (a.nbr[k] == i && a.shift[3 * k] == -s0 && a.shift[3 * k + 1] == -s1 &&
+          a.shift[3 * k + 2] == -s2)
+        rv = k;
+    }
+    a.rev[e] = rv;
+  }
+}
+
+__global__ void k_featurize(FeaturizeArgs a) {
+  const int d = a.d;
+  const int K = (a.layer == 0 ? 2 : 3) * d;
+  const int64_t total = static_cast<int64_t>(a.n_edges) * K;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int e = static_cast<int>(t / K), c = static_cast<int>(t % K);
+    float v;
+    if (c < d) {
+      const float *w = a.We + 4 * c;
+      const float x = a.vec[3 * e], y = a.vec[3 * e + 1], z = a.vec[3 * e + 2];
+      v = fmaf(w[2], z, fmaf(w[1], y, w[0] * x)) + w[3] * a.r[e] + a.be[c];
+    } else if (c < 2 * d) {
+      const float *tab = a.layer == 0 ? a.emb0 : a.nbr_emb;
+      v = tab[static_cast<size_t>(a.nbr_species[e]) * d + (c - d)];
+    } else {
+      const int cc = c - 2 * d;
+      const int rv = a.rev[e];
+      const float m0 = a.emb0[static_cast<size_t>(a.nbr_species[e]) * d + cc];
+      const float mr = rv >= 0 ? a.x_prev[static_cast<size_t>(a.edge_row[rv]) * d + cc] : 0.0f;
+      v = 0.5f * (m0 + mr);
+    }
+    a.cat[t] = v;
+  }
+}
+
+__global__ void k_node_tokens(const float *__restrict__ tab, const int *__restrict__ sp,
+                              const int *__restrict__ node_row, float *__restrict__ x, int n, int d) {
+  const int64_t total = static_cast<int64_t>(n) * d;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(t / d), c = static_cast<int>(t % d);
+    x[static_cast<size_t>(node_row[i]) * d + c] = tab[static_cast<size_t>(sp[i]) * d + c];
+  }
+}
+
+__global__ void k_head_last(const float *__restrict__ y, const float *__restrict__ w,
+                            const float *__restrict__ b, float *__restrict__ pred, int rows, int r) {
+  const int lane = threadIdx.x & 31;
+  for (int m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; m < rows;
+       m += (gridDim.x * blockDim.x) >> 5) {
+    const float *yr = y + static_cast<size_t>(m) * r;
+    float s = 0.f;
+    for (int c = lane; c < r; c += 32) s = fmaf(yr[c], w[c], s);
+    s = warp_sum(s);
+    if (lane == 0) pred[m] = s + b[0];
+  }
+}
+
+__global__ void k_head_last_bwd(const float *__restrict__ z, const float *__restrict__ w,
+                                const float *__restrict__ scale, float *__restrict__ dz, int rows, int r) {
+  const int64_t total = static_cast<int64_t>(rows) * r;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int m = static_cast<int>(t / r), c = static_cast<int>(t % r);
+    const float sc = scale ? scale[m] : 1.0f;
+    dz[t] = w[c] * dsilu_f(z[t]) * sc;
+  }
+}
+
+__global__ void k_atom_energy(const float *__restrict__ np, const float *__restrict__ ep,
+                              const float *__restrict__ fc, const int *__restrict__ offset,
+                              float *__restrict__ e_atom, int n, int accumulate) {
+  const int lane = threadIdx.x & 31;
+  for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < n;
+       i += (gridDim.x * blockDim.x) >> 5) {
+    float s = 0.f;
+    for (int e = offset[i] + lane; e < offset[i + 1]; e += 32) s = fmaf(ep[e], fc[e], s);
+    s = warp_sum(s);
+    if (lane == 0) e_atom[i] = (accumulate ? e_atom[i] : 0.0f) + np[i] + s;
+  }
+}
+
+__global__ void k_add_vec(const float *__restrict__ x, float *__restrict__ y, int n, int accumulate) {
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n; t += gridDim.x * blockDim.x)
+    y[t] = accumulate ? y[t] + x[t] : x[t];
+}
+
+__global__ void k_edge_embed_bwd(const float *__restrict__ demb, int ld, const float *__restrict__ We,
+                                 float *__restrict__ g4, int n_edges, int d, int accumulate) {
+  const int lane = threadIdx.x & 31;
+  for (int e = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; e < n_edges;
+       e += (gridDim.x * blockDim.x) >> 5) {
+    const float *gr = demb + static_cast<size_t>(e) * ld;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    for (int o = lane; o < d; o += 32) {
+      const float g = gr[o];
+      const float4 w = *reinterpret_cast<const float4 *>(We + 4 * o);
+      s0 = fmaf(g, w.x, s0);
+      s1 = fmaf(g, w.y, s1);
+      s2 = fmaf(g, w.z, s2);
+      s3 = fmaf(g, w.w, s3);
+    }
+    s0 = warp_sum(s0);
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    s3 = warp_sum(s3);
+    if (lane == 0) {
+      float4 *o = reinterpret_cast<float4 *>(g4) + e;
+      float4 v = make_float4(s0, s1, s2, s3);
+      if (accumulate) {
+        const float4 p = *o;
+        v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
+      }
+      *o = v;
+    }
+  }
+}
+
+__global__ void k_message_bwd(const float *__restrict__ dmsg, int ld, const int *__restrict__ rev,
+                              const int *__restrict__ edge_row, float *__restrict__ dx, int n_edges, int d) {
+  const int64_t total = static_cast<int64_t>(n_edges) * d;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int x = static_cast<int>(t / d), c = static_cast<int>(t % d);
+    const int rv = rev[x];
+    if (rv >= 0) dx[static_cast<size_t>(edge_row[x]) * d + c] += 0.5f * dmsg[static_cast<size_t>(rv) * ld + c];
+  }
+}
+
+__global__ void k_edge_grad(const float *__restrict__ g4, const float *__restrict__ gfc,
+                            const float *__restrict__ dfc_dr, const float *__restrict__ vec,
+                            const float *__restrict__ r, float *__restrict__ g, int n_edges) {
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n_edges; e += gridDim.x * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4 *>(g4)[e];
+    const float gr = (a.w + gfc[e] * dfc_dr[e]) / r[e];
+    g[3 * e] = a.x + gr * vec[3 * e];
+    g[3 * e + 1] = a.y + gr * vec[3 * e + 1];
+    g[3 * e + 2] = a.z + gr * vec[3 * e + 2];
+  }
+}
+
+__global__ void k_forces(const float *__restrict__ g, const int *__restrict__ offset,
+                         const int *__restrict__ rev, float *__restrict__ F, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    float fx = 0.f, fy = 0.f, fz = 0.f;
+    for (int e = offset[i]; e < offset[i + 1]; ++e) {
+      fx += g[3 * e];
+      fy += g[3 * e + 1];
+      fz += g[3 * e + 2];
+      const int rv = rev[e];
+      if (rv >= 0) {
+        fx -= g[3 * rv];
+        fy -= g[3 * rv + 1];
+        fz -= g[3 * rv + 2];
+      }
+    }
+    F[3 * i] = fx;
+    F[3 * i + 1] = fy;
+    F[3 * i + 2] = fz;
+  }
+}
+
+// Edges whose reverse is missing (a pair that only one side sees at the
+// cutoff) still push -g onto their neighbour.
+__global__ void k_forces_unpaired(const float *__restrict__ g, const int *__restrict__ nbr,
+                                  const int *__restrict__ rev, float *__restrict__ F, int n_edges) {
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n_edges; e += gridDim.x * blockDim.x) {
+    if (rev[e] >= 0) continue;
+    const int j = nbr[e];
+    atomicAdd(F + 3 * j, -g[3 * e]);
+    atomicAdd(F + 3 * j + 1, -g[3 * e + 1]);
+    atomicAdd(F + 3 * j + 2, -g[3 * e + 2]);
+  }
+}
+
+template <int NV>
+__device__ void block_sum(double (&v)[NV], double *sm) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) v[k] = warp_sum_d(v[k]);
+  if (lane == 0)
+    for (int k = 0; k < NV; ++k) sm[w * NV + k] = v[k];
+  __syncthreads();
+  if (w == 0) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      double t = lane < nw ? sm[lane * NV + k] : 0.0;
+      v[k] = warp_sum_d(t);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(512) k_reduce_systems(
+    const float *__restrict__ vec, const float *__restrict__ g, const float *__restrict__ e_atom,
+    const int *__restrict__ offset, const int *__restrict__ sys_begin, double *__restrict__ virial,
+    double *__restrict__ energy, int with_virial) {
+  __shared__ double sm[16 * 7];
+  const int k = blockIdx.x;
+  const int a0 = sys_begin[k], a1 = sys_begin[k + 1];
+  double v[7] = {0, 0, 0, 0, 0, 0, 0};
+  for (int i = a0 + threadIdx.x; i < a1; i += blockDim.x) v[6] += static_cast<double>(e_atom[i]);
+  if (with_virial) {
+    for (int e = offset[a0] + threadIdx.x; e < offset[a1]; e += blockDim.x) {
+      const double ex = vec[3 * e], ey = vec[3 * e + 1], ez = vec[3 * e + 2];
+      const double gx = g[3 * e], gy = g[3 * e + 1], gz = g[3 * e + 2];
+      v[0] += ex * gx;
+      v[1] += ey * gy;
+      v[2] += ez * gz;
+      v[3] += 0.5 * (ey * gz + ez * gy);
+      v[4] += 0.5 * (ex * gz + ez * gx);
+      v[5] += 0.5 * (ex * gy + ey * gx);
+    }
+  }
+  block_sum<7>(v, sm);
+  if (threadIdx.x == 0) {
+    for (int c = 0; c < 6; ++c) virial[6 * k + c] = v[c];
+    energy[k] = v[6];
+  }
+}
+
+}  // namespace
+
+void edge_prep(const EdgePrepArgs &a, cudaStream_t s) {
+  const int total = a.n_edges > a.n_atoms ? a.n_edges : a.n_atoms;
+  if (total <= 0) return;
+  k_edge_prep<<<grid_for(total, 256), 256, 0, s>>>(a);
+  CUDA_LAUNCH_CHECK();
+}
+
+void featurize(const FeaturizeArgs &a, cudaStream_t s) {
+  const int64_t total = static_cast<int64_t>(a.n_edges) * (a.layer == 0 ? 2 : 3) * a.d;
+  if (total <= 0) return;
+  k_featurize<<<grid_for(total, 256), 256, 0, s>>>(a);
+  CUDA_LAUNCH_CHECK();
+}
+
+void node_tokens(const float *table, const int *species, const int *node_row, float *x, int n,
+                 int d, cudaStream_t s) {
+  if (n <= 0) return;
+  k_node_tokens<<<grid_for(static_cast<int64_t>(n) * d, 256), 256, 0, s>>>(table, species, node_row, x, n, d);
+  CUDA_LAUNCH_CHECK();
+}
+
+void head_last(const float *y, const float *w, const float *b, float *pred, int rows, int r,
+               cudaStream_t s) {
+  if (rows <= 0) return;
+  k_head_last<<<grid_for(static_cast<int64_t>(rows) * 32, 256), 256, 0, s>>>(y, w, b, pred, rows, r);
+  CUDA_LAUNCH_CHECK();
+}
+
+void head_last_bwd(const float *z, const float *w, const float *scale, float *dz, int rows, int r,
+                   cudaStream_t s) {
+  if (rows <= 0) return;
+  k_head_last_bwd<<<grid_for(static_cast<int64_t>(rows) * r, 256), 256, 0, s>>>(z, w, scale, dz, rows, r);
+  CUDA_LAUNCH_CHECK();
+}
+
+void atom_energy(const float *node_pred, const float *edge_pred, const float *fc, const int *offset,
+                 float *e_atom, int n, bool accumulate, cudaStream_t s) {
+  if (n <= 0) return;
+  k_atom_energy<<<grid_for(static_cast<int64_t>(n) * 32, 256), 256, 0, s>>>(node_pred, edge_pred, fc, offset,
+                                                                            e_atom, n, accumulate);
+  CUDA_LAUNCH_CHECK();
+}
+
+void add_vec(const float *x, float *y, int n, bool accumulate, cudaStream_t s) {
+  if (n <= 0) return;
+  k_add_vec<<<grid_for(n, 256), 256, 0, s>>>(x, y, n, accumulate);
+  CUDA_LAUNCH_CHECK();
+}
+
+void edge_embed_bwd(const float *demb, int ld, const float *We, float *g4, int n_edges, int d,
+                    bool accumulate, cudaStream_t s) {
+  if (n_edges <= 0) return;
+  k_edge_embed_bwd<<<grid_for(static_cast<int64_t>(n_edges) * 32, 256), 256, 0, s>>>(demb, ld, We, g4, n_edges,
+                                                                                     d, accumulate);
+  CUDA_LAUNCH_CHECK();
+}
+
+void message_bwd(const float *dmsg, int ld, const int *rev, const int *edge_row, float *dx,
+                 int n_edges, int d, cudaStream_t s) {
+  if (n_edges <= 0) return;
+  k_message_bwd<<<grid_for(static_cast<int64_t>(n_edges) * d, 256), 256, 0, s>>>(dmsg, ld, rev, edge_row, dx,
+                                                                                 n_edges, d);
+  CUDA_LAUNCH_CHECK();
+}
+
+void edge_grad(const float *g4, const float *gfc, const float *dfc_dr, const float *vec,
+               const float *r, float *g, int n_edges, cudaStream_t s) {
+  if (n_edges <= 0) return;
+  k_edge_grad<<<grid_for(n_edges, 256), 256, 0, s>>>(g4, gfc, dfc_dr, vec, r, g, n_edges);
+  CUDA_LAUNCH_CHECK();
+}
+
+void forces(const float *g, const int *offset, const int *nbr, const int *rev, float *F, int n,
+            int n_edges, cudaStream_t s) {
+  if (n <= 0) return;
+  k_forces<<<grid_for(n, 128), 128, 0, s>>>(g, offset, rev, F, n);
+  CUDA_LAUNCH_CHECK();
+  if (n_edges > 0) {
+    k_forces_unpaired<<<grid_for(n_edges, 256), 256, 0, s>>>(g, nbr, rev, F, n_edges);
+    CUDA_LAUNCH_CHECK();
+  }
+}
+
+void reduce_systems(const float *vec, const float *g, const float *e_atom, const int *offset,
+                    const int *sys_atom_begin, int n_sys, double *virial, double *energy,
+                    bool with_virial, cudaStream_t s) {
+  if (n_sys <= 0) return;
+  k_reduce_systems<<<n_sys, 512, 0, s>>>(vec, g, e_atom, offset, sys_atom_begin, virial, energy,
+                                         with_virial ? 1 : 0);
+  CUDA_LAUNCH_CHECK();
+}
+
+}  // namespace pet

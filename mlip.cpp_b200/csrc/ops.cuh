@@ -1,0 +1,70 @@
+// Per-edge and per-atom kernels of the PET pass (graph preparation,
+// featuriser, message passing, readout, gradients, forces, virial).
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace pet {
+
+struct EdgePrepArgs {
+  int n_atoms, n_edges;
+  const int *offset, *center, *nbr, *shift, *species;
+  const float *vec, *dist_nl;
+  float cutoff, width;
+  // outputs
+  float *r, *fc, *dfc_dr, *key_mask;
+  int *edge_row, *node_row, *nbr_species, *rev;
+};
+// r, f_c and df_c/dr in-graph (pet.cpp:208-256); the fp16 log-cutoff key
+// mask from the neighbour-list distance (pet_batch.cpp:37-47,603-653); token
+// rows; neighbour species; reverse edge (pet_batch.cpp:399-495).
+void edge_prep(const EdgePrepArgs &a, cudaStream_t s);
+
+// cat[e, 0:d] = W_e [x y z r] + b_e  (pet_layers.cpp:151-217)
+// layer 0: cat[e, d:2d] = embedding[nbr species]               (pet.cpp:789-832)
+// layer 1: cat[e, d:2d] = neighbor_embedder[nbr species],
+//          cat[e, 2d:3d] = 0.5 (embedding[nbr species] + X0[row(rev e)])  (pet_layers.cpp:608-679)
+struct FeaturizeArgs {
+  int n_edges, d, layer;
+  const float *vec, *r;
+  const int *nbr_species, *rev, *edge_row;
+  const float *We, *be, *emb0, *nbr_emb, *x_prev;
+  float *cat;
+};
+void featurize(const FeaturizeArgs &a, cudaStream_t s);
+
+// X[node_row[i], :] = table[species[i], :]
+void node_tokens(const float *table, const int *species, const int *node_row, float *x, int n,
+                 int d, cudaStream_t s);
+
+// pred[m] = dot(y[m, :], w) + b
+void head_last(const float *y, const float *w, const float *b, float *pred, int rows, int r,
+               cudaStream_t s);
+// dz[m, c] = w[c] silu'(z[m, c]) scale[m]   (scale null -> 1)
+void head_last_bwd(const float *z, const float *w, const float *scale, float *dz, int rows, int r,
+                   cudaStream_t s);
+// e_atom[i] (+)= node_pred[i] + sum_{e in i} edge_pred[e] fc[e]
+void atom_energy(const float *node_pred, const float *edge_pred, const float *fc, const int *offset,
+                 float *e_atom, int n, bool accumulate, cudaStream_t s);
+// gfc[e] (+)= edge_pred[e]
+void add_vec(const float *x, float *y, int n, bool accumulate, cudaStream_t s);
+
+// g4[e, 0:3] (+)= W_e[:, 0:3]^T demb[e],  g4[e, 3] (+)= W_e[:, 3]^T demb[e]
+void edge_embed_bwd(const float *demb, int ld, const float *We, float *g4, int n_edges, int d,
+                    bool accumulate, cudaStream_t s);
+// dX[edge_row[x], :] += 0.5 dmsg[rev[x], :]   for rev[x] >= 0
+void message_bwd(const float *dmsg, int ld, const int *rev, const int *edge_row, float *dx,
+                 int n_edges, int d, cudaStream_t s);
+// g[e] = g4[e, 0:3] + (g4[e, 3] + gfc[e] dfc_dr[e]) vec[e] / r[e]
+void edge_grad(const float *g4, const float *gfc, const float *dfc_dr, const float *vec,
+               const float *r, float *g, int n_edges, cudaStream_t s);
+// F[i] = sum_{e in i} g[e] - sum_{e : nbr[e] = i} g[e]   (pet.cpp:965-998)
+void forces(const float *g, const int *offset, const int *nbr, const int *rev, float *F, int n,
+            int n_edges, cudaStream_t s);
+// Per system k: virial[k][6] = sum over its edges of sym(vec (x) g) (Voigt),
+// energy[k] = sum of its atomic energies (both in f64).
+void reduce_systems(const float *vec, const float *g, const float *e_atom, const int *offset,
+                    const int *sys_atom_begin, int n_sys, double *virial, double *energy,
+                    bool with_virial, cudaStream_t s);
+
+}  // namespace pet

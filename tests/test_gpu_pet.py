@@ -1,0 +1,145 @@
+"""GPU PET energy / forces / stress through the C ABI against the oracle.
+
+fp32 tolerances of the parity bar: |dE|/N <= 1e-5 eV, |dF| <= 1e-4 eV/A,
+|dsigma| <= 1e-4 eV/A^3 (against the float64 restatement)."""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+import mlipcpp_b200 as mb
+from mlipcpp_b200 import workloads as wl
+from oracle import pet_oracle as po
+
+pytestmark = pytest.mark.gpu
+TOL_E, TOL_F, TOL_S = 1e-5, 1e-4, 1e-4
+FIXTURES = sorted(glob.glob(os.path.join(GOLDEN, "pet_*.npz")))
+
+
+def assert_close(res, e_ref, f_ref, s_ref, n):
+    assert abs(res.energy - e_ref) / n <= TOL_E, (res.energy, e_ref)
+    if f_ref is not None:
+        assert res.has_forces()
+        assert np.abs(res.forces - f_ref).max() <= TOL_F, np.abs(res.forces - f_ref).max()
+    if s_ref is not None and len(s_ref):
+        assert res.has_stress()
+        assert np.abs(res.stress - s_ref).max() <= TOL_S, np.abs(res.stress - s_ref).max()
+
+
+@pytest.mark.parametrize("path", FIXTURES, ids=lambda p: os.path.basename(p)[4:-4])
+def test_gpu_matches_golden(path, model_file):
+    f = np.load(path)
+    pred = mb.Predictor(model_file(str(f["hypers"]), int(f["seed"])))
+    n_sys = int(f["n_systems"])
+    systems = []
+    for k in range(n_sys):
+        cell = f[f"cell_{k}"]
+        systems.append(wl.Structure(f[f"positions_{k}"], f[f"numbers_{k}"],
+                                    cell if cell.size else None, (True,) * 3 if cell.size else None))
+    if n_sys == 1:
+        s = systems[0]
+        res = [pred.predict(s.positions, s.numbers, s.cell, s.pbc, compute_stress=s.cell is not None)]
+    else:
+        res = pred.predict_batch(systems)
+    for k, r in enumerate(res):
+        assert_close(r, float(f[f"energy_{k}"]), f[f"forces_{k}"], f[f"stress_{k}"],
+                     systems[k].n_atoms)
+
+
+@pytest.mark.parametrize("case", ["si216_mads", "water384_mads", "fcc512_oaml", "si_partial_pbc"])
+def test_gpu_matches_oracle(case, model_file):
+    hname, s = {
+        "si216_mads": lambda: ("pet-mad-s", wl.si_diamond(3, seed=31)),
+        "water384_mads": lambda: ("pet-mad-s", wl.water_box(384, seed=32)),
+        "fcc512_oaml": lambda: ("pet-oam-l", wl.fcc_alloy(8, seed=33)),
+        "si_partial_pbc": lambda: ("tiny", wl.Structure(*(lambda t: (t.positions, t.numbers, t.cell))(
+            wl.si_diamond(2, seed=34)), (True, True, False))),
+    }[case]()
+    path = model_file(hname, 3)
+    orc = po.load_oracle(path, torch.float64)
+    ref = orc.predict([s])[0]
+    res = mb.Predictor(path).predict(s.positions, s.numbers, s.cell, s.pbc, compute_stress=True)
+    assert_close(res, ref["energy_f64"], ref["forces"], ref.get("stress"), s.n_atoms)
+
+
+def test_gpu_molecule_batch_matches_single(model_file):
+    """Batch == individual within 1e-5 (tests/test_pet.cpp:147-184)."""
+    pred = mb.Predictor(model_file("tiny", 4))
+    mols = wl.molecules(6, seed=41, n_min=3, n_max=40)
+    batch = pred.predict_batch(mols)
+    orc = po.load_oracle(model_file("tiny", 4), torch.float64)
+    ref = orc.predict(mols)
+    for k, m in enumerate(mols):
+        single = pred.predict(m.positions, m.numbers)
+        assert abs(batch[k].energy - single.energy) <= 1e-5 * max(1.0, abs(single.energy))
+        np.testing.assert_allclose(batch[k].forces, single.forces, atol=1e-5)
+        assert_close(batch[k], ref[k]["energy_f64"], ref[k]["forces"], None, m.n_atoms)
+
+
+def test_gpu_edge_cases(model_file):
+    path = model_file("tiny", 5)
+    pred = mb.Predictor(path)
+    orc = po.load_oracle(path, torch.float64)
+    # isolated atom (test_pet.cpp:226-273)
+    one = wl.Structure(np.zeros((1, 3), np.float32), np.array([6], np.int32))
+    r = pred.predict(one.positions, one.numbers)
+    assert_close(r, orc.predict([one])[0]["energy_f64"], np.zeros((1, 3)), None, 1)
+    # a dimer and an isolated atom mixed in one batch
+    dim = wl.Structure(np.array([[0, 0, 0], [1.1, 0.2, -0.1]], np.float32), np.array([1, 8], np.int32))
+    out = pred.predict_batch([dim, one])
+    ref = orc.predict([dim, one])
+    assert_close(out[0], ref[0]["energy_f64"], ref[0]["forces"], None, 2)
+    assert_close(out[1], ref[1]["energy_f64"], ref[1]["forces"], None, 1)
+    # momentum conservation (test_pet_gradients.cpp:203-234)
+    s = wl.water_box(96, seed=6)
+    F = pred.predict(s.positions, s.numbers, s.cell).forces
+    assert np.abs(F.sum(0)).max() < 1e-3
+    # unknown species -> MLIPCPP_ERROR_COMPUTATION (pet_batch.cpp:156-163)
+    with pytest.raises(mb.MLIPError) as ei:
+        pred.predict(one.positions, np.array([150], np.int32))
+    assert ei.value.code == mb.COMPUTATION
+
+
+def test_gpu_options_semantics(model_file):
+    """predict_with_options: gradient only when forces or stress are asked
+    for; unrequested outputs are cleared (mlipcpp_api.cpp:569-593)."""
+    pred = mb.Predictor(model_file("tiny", 6))
+    s = wl.si_diamond(1, seed=7)
+    full = pred.predict_with_options(s.positions, s.numbers, s.cell, None,
+                                     mb.PredictOptions(True, True))
+    assert full.has_forces() and full.has_stress()
+    e_only = pred.predict_with_options(s.positions, s.numbers, s.cell, None,
+                                       mb.PredictOptions(False, False))
+    assert not e_only.has_forces() and not e_only.has_stress()
+    assert abs(e_only.energy - full.energy) < 1e-4
+    f_only = pred.predict_with_options(s.positions, s.numbers, s.cell, None, mb.PredictOptions(True, False))
+    assert f_only.has_forces() and not f_only.has_stress()
+    s_only = pred.predict_with_options(s.positions, s.numbers, s.cell, None, mb.PredictOptions(False, True))
+    assert s_only.has_stress() and not s_only.has_forces()
+    np.testing.assert_allclose(s_only.stress, full.stress, atol=1e-6)
+    m = wl.molecules(1, seed=3)[0]
+    r = pred.predict(m.positions, m.numbers, compute_stress=True)
+    assert r.has_forces() and not r.has_stress()   # stress only for periodic cells
+    assert pred.cutoff == pytest.approx(4.5)
+
+
+def test_gpu_fd_stress_option(model_file):
+    """fd_stress (mlipcpp_cpp.cpp:221-259) agrees with the virial within the
+    reference's own FD tolerance (scripts/test_stress_fd.py:176)."""
+    pred = mb.Predictor(model_file("tiny", 2, cutoff=4.0, cutoff_width=0.5))
+    s = wl.si_diamond(1, seed=3, jitter=0.03)
+    an = pred.predict(s.positions, s.numbers, s.cell, compute_stress=True).stress
+    fd = pred.predict(s.positions, s.numbers, s.cell, compute_stress=True, fd_stress=True).stress
+    diff = np.abs(an - fd).max()
+    assert diff < 5e-3 or diff / np.abs(fd).max() < 5e-2
+
+
+def test_gpu_kernel_launches_counted(model_file):
+    pred = mb.Predictor(model_file("tiny", 0))
+    before = mb.kernel_launches()
+    s = wl.si_diamond(1)
+    pred.predict(s.positions, s.numbers, s.cell)
+    assert mb.kernel_launches() > before
