@@ -16,8 +16,10 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
+#include "gemm_tc.cuh"
 #include "gguf.h"
 #include "kernels.cuh"
 #include "ops.cuh"
@@ -218,18 +220,33 @@ void PETModel::load(const std::string &path, float cutoff_override) {
       transpose_of(hp + "2.weight");
     }
   }
+  // One arena holding three copies with identical layout: fp32, its tf32
+  // truncation (hi) and the remainder (lo), so the split operands of any
+  // weight pointer (sub-blocks included) sit at fixed offsets from it.
   size_t total = 0;
   for (auto &kv : host) total += (kv.second.size() * 4 + 255) / 256 * 256;
-  wbuf_.ensure(total);
+  wbuf_.ensure(3 * total);
+  wspan_ = total / 4;
   wptr_.clear();
-  std::vector<char> staging(total);
+  std::vector<char> staging(3 * total, 0);
   size_t off = 0;
   for (auto &kv : host) {
     std::memcpy(staging.data() + off, kv.second.data(), kv.second.size() * 4);
+    float *hi = reinterpret_cast<float *>(staging.data() + total + off);
+    float *lo = reinterpret_cast<float *>(staging.data() + 2 * total + off);
+    for (size_t k = 0; k < kv.second.size(); ++k) {
+      uint32_t u;
+      std::memcpy(&u, &kv.second[k], 4);
+      u &= 0xFFFFE000u;
+      std::memcpy(&hi[k], &u, 4);
+      lo[k] = kv.second[k] - hi[k];
+    }
     wptr_[kv.first] = reinterpret_cast<const float *>(wbuf_.as<char>() + off);
     off += (kv.second.size() * 4 + 255) / 256 * 256;
   }
-  CUDA_CHECK(cudaMemcpy(wbuf_.ptr, staging.data(), total, cudaMemcpyHostToDevice));
+  CUDA_CHECK(cudaMemcpy(wbuf_.ptr, staging.data(), 3 * total, cudaMemcpyHostToDevice));
+  const char *g = std::getenv("MLIPCPP_B200_GEMM");
+  use_tc_ = !(g && std::string(g) == "simt");
 
   // composition map and species index (pet.cpp:1280-1303)
   species_index_.clear();
@@ -357,10 +374,14 @@ void PETModel::forward_backward(bool grad) {
                   const int *c_rows, int M, int N, int K, const float *bias, int epi, cudaStream_t st,
                   float *Z = nullptr, int ldz = 0, const float *R = nullptr, int ldr = 0) {
     GemmArgs g = make_gemm(A, lda, a_rows, B, ldb, C, ldc, c_rows, M, N, K, bias, epi, Z, ldz, R, ldr);
+    const float *wb = wbuf_.as<float>();
+    const bool in_arena = B >= wb && B < wb + wspan_;
+    const bool tc = use_tc_ && in_arena && gemm_tc_supported(g);
     cudaEvent_t e0 = nullptr;
     if (kprof_) mark_begin(e0);
-    gemm_f32(g, st);
-    if (kprof_) mark_end(KC_GEMM, e0, 2.0 * M * N * static_cast<double>(K), gemm_bytes(g));
+    if (tc) gemm_3xtf32(g, TCWeights{B + wspan_, B + 2 * wspan_}, d_err_.as<int>(), st);
+    else gemm_f32(g, st);
+    if (kprof_) mark_end(tc ? KC_GEMM_TC : KC_GEMM_SIMT, e0, 2.0 * M * N * static_cast<double>(K), gemm_bytes(g));
   };
   auto attn = [&](bool backward, const AttnArgs &x) {
     cudaEvent_t e0 = nullptr;
@@ -483,6 +504,8 @@ void PETModel::run_group(const float *d_pos, int n_atoms, const std::vector<cons
   const int n_sys = static_cast<int>(systems.size());
   N_ = n_atoms;
   n_sys_ = n_sys;
+  int *derr = static_cast<int *>(d_err_.ensure(sizeof(int) * 4));
+  CUDA_CHECK(cudaMemsetAsync(derr, 0, sizeof(int), s));
   // species indices (pet_batch.cpp:146-167): unknown Z is an error
   int *hsp = static_cast<int *>(h_species_.ensure(sizeof(int) * (n_atoms + 1) + sizeof(int) * (n_sys + 1)));
   for (int k = 0; k < n_sys; ++k) {
@@ -562,12 +585,17 @@ void PETModel::run_group(const float *d_pos, int n_atoms, const std::vector<cons
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[6], s));
   const size_t fbytes = (grad && copy_forces) ? sizeof(float) * 3 * n_atoms : 0;
   char *hout = static_cast<char *>(h_out_.ensure(sizeof(double) * 7 * n_sys + fbytes + 16));
+  int *herr = reinterpret_cast<int *>(hout + sizeof(double) * 7 * n_sys + fbytes);
+  CUDA_CHECK(cudaMemcpyAsync(herr, d_err_.ptr, sizeof(int), cudaMemcpyDeviceToHost, s));
   CUDA_CHECK(cudaMemcpyAsync(hout, red, sizeof(double) * 7 * n_sys, cudaMemcpyDeviceToHost, s));
   if (fbytes)
     CUDA_CHECK(cudaMemcpyAsync(hout + sizeof(double) * 7 * n_sys, a.F, fbytes, cudaMemcpyDeviceToHost, s));
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[7], s));
   CUDA_CHECK(cudaStreamSynchronize(s));
   if (kprof_) collect_marks();
+  if (*herr != 0)
+    throw Error(kErrComputation, "a tensor-core pipeline wait timed out (device error " +
+                                     std::to_string(*herr) + ")");
 
   const double *he = reinterpret_cast<const double *>(hout);
   const double *hv = he + n_sys;

@@ -39,7 +39,7 @@ struct Result {
 };
 
 // Kernel classes timed individually when kernel profiling is on.
-enum KernelClass { KC_GEMM = 0, KC_ATTENTION = 1, KC_NEIGHBOR = 2, KC_OTHER = 3, KC_COUNT = 4 };
+enum KernelClass { KC_GEMM_TC = 0, KC_GEMM_SIMT = 1, KC_ATTENTION = 2, KC_NEIGHBOR = 3, KC_OTHER = 4, KC_COUNT = 5 };
 
 struct KernelStat {
   long long launches = 0;
@@ -97,7 +97,10 @@ class PETModel {
   Hypers h_;
   cudaStream_t stream_ = nullptr;
   int device_ = 0;
-  DevBuf wbuf_;
+  DevBuf wbuf_;          // [fp32 | tf32 hi | lo] copies of every weight
+  size_t wspan_ = 0;     // floats between the three copies
+  bool use_tc_ = true;   // tensor-core GEMMs (MLIPCPP_B200_GEMM=simt disables)
+  DevBuf d_err_;         // device error word written by bounded waits
   std::map<std::string, const float *> wptr_;
   std::map<int, int> species_index_;
   std::map<int, float> composition_;
