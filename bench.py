@@ -229,11 +229,11 @@ def main():
 
     if rank == 0:
         hbm, bf16, bf16_sus, src = _peaks()
-        g = kstats["gemm"]
+        g = kstats["gemm_tc"]
+        gs = kstats["gemm_simt"]
         achieved = g["flops"] / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else 0.0
-        # exact-fp32 SIMT path: FFMA peak (148 SMs x 128 lanes x 2 flops x
-        # clock) is not in MEASURED_PEAKS; the measured bf16 tensor peak is the
-        # denominator the judge compares against.
+        # 3xTF32 runs three tf32 MMAs per fp32 product at half the bf16 rate:
+        # its ceiling is the measured bf16 peak / 6 (achieved counts 2MNK).
         shape = pred.last_shape()
         line = {
             "metric": METRIC, "value": value, "unit": "atom-steps/s", "n_gpus": world,
@@ -247,10 +247,13 @@ def main():
                     "h2d_bytes_per_step": int(s.positions.nbytes + s.numbers.nbytes),
                     "d2h_bytes_per_step": int(r.forces.nbytes + r.stress.nbytes + 4)},
             "gpu_launches": int(launches),
-            "roofline": {"bound": "tensor", "kernel": "gemm_f32 (all dense layers)",
-                         "achieved": achieved, "peak": bf16_sus, "unit": "TFLOP/s",
-                         "frac": achieved / bf16_sus, "peak_source": f"{src} bf16 sustained",
-                         "traffic": None, "gemm_share_of_step": g["ms"] / (t_dev * 1e3) if t_dev else None},
+            "roofline": {"bound": "tensor", "kernel": "k_gemm_3xtf32 (tcgen05, all dense layers)",
+                         "achieved": achieved, "peak": bf16_sus / 6.0, "unit": "TFLOP/s",
+                         "frac": achieved / (bf16_sus / 6.0),
+                         "peak_source": f"{src} bf16 sustained / 6 (3 tf32 MMAs at half bf16 rate)",
+                         "tensor_pipe_frac_of_bf16": 6.0 * achieved / bf16_sus,
+                         "traffic": None,
+                         "gemm_share_of_step": (g["ms"] + gs["ms"]) / (t_dev * 1e3) if t_dev else None},
             "kernel_stats": kstats,
             "phase_ms": pred.last_timings(),
             "clocks": clk.summary(),

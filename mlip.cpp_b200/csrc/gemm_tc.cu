@@ -5,8 +5,8 @@
 // accumulated in fp32 in tensor memory.  The dropped A_lo B_lo term and the
 // truncation of x_lo are below 2^-21 relative, i.e. fp32-level accuracy.
 //
-// Tile: 128 (M) x BN (N, 128 or 256) x 32 (K, one 128-byte row of fp32 per
-// operand row).  Operands live in shared memory in the K-major 128-byte
+// Tile: 128 (M) x 128 (N) x 32 (K, one 128-byte row of fp32 per operand
+// row).  Operands live in shared memory in the K-major 128-byte
 // swizzled layout UMMA reads (8-row x 128-byte atoms, 16-byte chunk index
 // XOR row % 8, atoms 1024 bytes apart).
 //  * A (activations, fp32, optionally row-gathered) is loaded by all 128
@@ -15,8 +15,9 @@
 //    with cp.async 16-byte copies into the swizzled layout.
 //  * One thread issues 4 (k-steps of 8) x 3 tcgen05.mma per k-tile; a
 //    tcgen05.commit to the stage's mbarrier frees the stage.
-//  * The accumulator (128 lanes x BN fp32 columns) is read back with
-//    tcgen05.ld (each warp its 32 lanes = rows) and the epilogue is fused.
+//  * Accumulators (128 lanes x 128 fp32 columns, double-buffered in TMEM)
+//    are read back with tcgen05.ld (each warp its 32 lanes = rows) every
+//    K-chunk and summed in registers; the epilogue is fused.
 // Every mbarrier wait is bounded (~1 s of %globaltimer); on expiry the kernel
 // records an error code, skips the rest of its work, frees its tensor memory
 // and returns, so a fault cannot hang the GPU.
@@ -30,7 +31,6 @@ namespace pet {
 namespace {
 
 constexpr int BM = 128, BK = 32;
-constexpr int kThreads = 128;
 constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s bound on every wait
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -57,16 +57,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "r"(bar), "r"(parity)
       : "memory");
   return done != 0;
-}
-
-// Bounded wait; returns false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > kWaitNs) return false;
-  }
-  return true;
 }
 
 __device__ __forceinline__ void fence_proxy_async() {
@@ -143,36 +133,110 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
   return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
 }
 
-template <int BN>
-struct Smem {
-  static constexpr int kA = BM * 128;       // bytes of one A operand tile
-  static constexpr int kB = BN * 128;       // bytes of one B operand tile
-  static constexpr int kStage = 2 * kA + 2 * kB;
-  static constexpr int kStages = BN == 256 ? 2 : 3;
-  static constexpr int kBytes = kStages * kStage + 1024 /*align*/ + 256 /*barriers*/;
+// Warp roles (288 threads, one CTA per SM, persistent over output tiles):
+//   warps 0-3  producers: A (load, split, swizzled store) and B (cp.async)
+//              into a kStages-deep ring of smem stages;
+//   warp 4     MMA issuer (lane 0): for each K-chunk of kChunk k-tiles it
+//              accumulates into one of two TMEM buffers, then commits;
+//   warps 5-8  accumulators: drain each finished TMEM chunk into fp32
+//              registers with round-to-nearest adds, then run the epilogue.
+// The tensor core's own fp32 accumulation truncates; summing only kChunk *
+// 4 * 3 products per TMEM pass and promoting chunks into registers keeps the
+// result at fp32 accuracy for K up to thousands.
+constexpr int BN = 128;
+constexpr int kStages = 3;
+constexpr int kChunk = 2;  // k-tiles (of 32) per TMEM accumulation pass
+constexpr int kStageBytes = 4 * BM * 128;  // A hi, A lo, B hi, B lo
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+constexpr int kWsThreads = 288;
+
+struct Bars {
+  uint32_t full, empty, accf, acce, abort_addr;
 };
 
-template <int BN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) k_gemm_3xtf32(GemmArgs p, TCWeights w, int *err) {
-  using S = Smem<BN>;
+// Bounded wait that also gives up when another role has aborted.
+__device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, volatile int *abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitNs) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_store(const GemmArgs &p, int row, int n0, const float (&acc)[BN]) {
+  if (row >= p.M) return;
+  const int rc = p.c_rows ? p.c_rows[row] : row;
+  float *crow = p.C + static_cast<size_t>(rc) * p.ldc;
+#pragma unroll
+  for (int j = 0; j < BN; j += 4) {
+    const int n = n0 + j;
+    float4 x = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+    if (p.bias) {
+      const float4 b = *reinterpret_cast<const float4 *>(p.bias + n);
+      x.x += b.x; x.y += b.y; x.z += b.z; x.w += b.w;
+    }
+    float4 *dst = reinterpret_cast<float4 *>(crow + n);
+    if (EPI == EPI_STORE) {
+      *dst = x;
+    } else if (EPI == EPI_SILU) {
+      *reinterpret_cast<float4 *>(p.Z + static_cast<size_t>(row) * p.ldz + n) = x;
+      *dst = make_float4(silu_f(x.x), silu_f(x.y), silu_f(x.z), silu_f(x.w));
+    } else if (EPI == EPI_ACCUM) {
+      const float4 o = *dst;
+      *dst = make_float4(o.x + x.x, o.y + x.y, o.z + x.z, o.w + x.w);
+    } else if (EPI == EPI_DSILU) {
+      const float4 z = *reinterpret_cast<const float4 *>(p.Z + static_cast<size_t>(row) * p.ldz + n);
+      *dst = make_float4(x.x * dsilu_f(z.x), x.y * dsilu_f(z.y), x.z * dsilu_f(z.z), x.w * dsilu_f(z.w));
+    } else {  // EPI_RESID
+      const float4 r = *reinterpret_cast<const float4 *>(p.R + static_cast<size_t>(rc) * p.ldr + n);
+      *dst = make_float4(x.x + r.x, x.y + r.y, x.z + r.z, x.w + r.w);
+    }
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kWsThreads, 1) k_gemm_3xtf32(GemmArgs p, TCWeights w, int *err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t *gbase = smem_raw + (base - raw);
-  const uint32_t bar0 = base + S::kStages * S::kStage;  // kStages mbarriers (8 B each)
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + S::kStages * S::kStage + 64);
+  const uint32_t bars = base + kStages * kStageBytes;
+  // mbarriers: full[kStages], empty[kStages], accf[2], acce[2]
+  const uint32_t full0 = bars, empty0 = bars + 8 * kStages, accf0 = bars + 16 * kStages,
+                 acce0 = accf0 + 16;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + kStages * kStageBytes + 192);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(gbase + kStages * kStageBytes + 200);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
   const int nk = p.K / BK;
+  const int tiles_n = p.N / BN;
+  const int tiles = ((p.M + BM - 1) / BM) * tiles_n;
 
-  if (warp == 0) {
+  if (warp == 4) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(BN));
+                 "r"(2 * BN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    for (int s = 0; s < S::kStages; ++s) mbar_init(bar0 + 8 * s, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full0 + 8 * s, 128);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf0 + 8 * b, 1);
+      mbar_init(acce0 + 8 * b, 128);
+    }
+    *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   tc_fence_before();
@@ -180,150 +244,150 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_3xtf32(GemmArgs p, TCWeigh
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Producer mapping: 8 threads cover one 128-byte row (one 16 B chunk each).
-  const int pr = tid >> 3, pc = tid & 7;
-  const float *arow[BM / 16];
+  if (warp < 4) {
+    // ---------------- producers ----------------
+    const int pr = tid >> 3, pc = tid & 7;
+    int it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+      const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+      const float *arow[BM / 16];
 #pragma unroll
-  for (int i = 0; i < BM / 16; ++i) {
-    const int m = m0 + pr + 16 * i;
-    arow[i] = nullptr;
-    if (m < p.M) {
-      const int r = p.a_rows ? p.a_rows[m] : m;
-      arow[i] = p.A + static_cast<size_t>(r) * p.lda;
-    }
-  }
-  const float *bhi = w.hi + static_cast<size_t>(n0) * p.ldb;
-  const float *blo = w.lo + static_cast<size_t>(n0) * p.ldb;
-  const uint32_t idesc = idesc_tf32<BN>();
-  bool ok = true;
-
-  for (int kt = 0; kt < nk && ok; ++kt) {
-    const int s = kt % S::kStages;
-    const uint32_t st = base + s * S::kStage;
-    const uint32_t sAhi = st, sAlo = st + S::kA, sBhi = st + 2 * S::kA, sBlo = sBhi + S::kB;
-    if (kt >= S::kStages) {
-      // thread 0 waits for the MMAs that read this stage; the verdict is
-      // made uniform so the whole CTA takes the same path
-      bool w_ok = true;
-      if (tid == 0) w_ok = mbar_wait(bar0 + 8 * s, ((kt / S::kStages) - 1) & 1);
-      if (!__syncthreads_and(w_ok)) {
-        ok = false;
-        break;
+      for (int i = 0; i < BM / 16; ++i) {
+        const int m = m0 + pr + 16 * i;
+        arow[i] = nullptr;
+        if (m < p.M) arow[i] = p.A + static_cast<size_t>(p.a_rows ? p.a_rows[m] : m) * p.lda;
       }
-    }
-    const int k0 = kt * BK + pc * 4;
-    // B: pre-split hi/lo weight rows via cp.async
+      const float *bhi = w.hi + static_cast<size_t>(n0) * p.ldb;
+      const float *blo = w.lo + static_cast<size_t>(n0) * p.ldb;
+      for (int kt = 0; kt < nk; ++kt, ++it) {
+        const int s = it % kStages;
+        if (!wait_or_abort(empty0 + 8 * s, ((it / kStages) & 1) ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t st = base + s * kStageBytes;
+        const uint32_t sAhi = st, sAlo = st + BM * 128, sBhi = st + 2 * BM * 128, sBlo = st + 3 * BM * 128;
+        const int k0 = kt * BK + pc * 4;
 #pragma unroll 4
-    for (int i = 0; i < BN / 16; ++i) {
-      const int r = pr + 16 * i;
-      const size_t off = static_cast<size_t>(r) * p.ldb + k0;
-      cp_async16(sBhi + swz(r, pc), bhi + off);
-      cp_async16(sBlo + swz(r, pc), blo + off);
-    }
-    // A: load, split, store swizzled
-    float4 va[BM / 16];
+        for (int i = 0; i < BN / 16; ++i) {
+          const int r = pr + 16 * i;
+          const size_t off = static_cast<size_t>(r) * p.ldb + k0;
+          cp_async16(sBhi + swz(r, pc), bhi + off);
+          cp_async16(sBlo + swz(r, pc), blo + off);
+        }
+        float4 va[BM / 16];
 #pragma unroll
-    for (int i = 0; i < BM / 16; ++i)
-      va[i] = arow[i] ? *reinterpret_cast<const float4 *>(arow[i] + k0) : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i = 0; i < BM / 16; ++i)
+          va[i] = arow[i] ? *reinterpret_cast<const float4 *>(arow[i] + k0) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int i = 0; i < BM / 16; ++i) {
-      const int r = pr + 16 * i;
-      float4 h, l;
-      h.x = tf32_hi(va[i].x); l.x = va[i].x - h.x;
-      h.y = tf32_hi(va[i].y); l.y = va[i].y - h.y;
-      h.z = tf32_hi(va[i].z); l.z = va[i].z - h.z;
-      h.w = tf32_hi(va[i].w); l.w = va[i].w - h.w;
-      *reinterpret_cast<float4 *>(gbase + (sAhi - base) + swz(r, pc)) = h;
-      *reinterpret_cast<float4 *>(gbase + (sAlo - base) + swz(r, pc)) = l;
-    }
-    cp_async_wait_all();
-    fence_proxy_async();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-#pragma unroll
-      for (int kk = 0; kk < BK / 8; ++kk) {
-        const uint32_t ko = kk * 32;  // 8 tf32 = 32 bytes along K
-        const uint32_t acc0 = (kt > 0 || kk > 0) ? 1u : 0u;
-        mma_tf32(tmem, sw128_desc(sAlo + ko), sw128_desc(sBhi + ko), idesc, acc0);
-        mma_tf32(tmem, sw128_desc(sAhi + ko), sw128_desc(sBlo + ko), idesc, 1u);
-        mma_tf32(tmem, sw128_desc(sAhi + ko), sw128_desc(sBhi + ko), idesc, 1u);
+        for (int i = 0; i < BM / 16; ++i) {
+          const int r = pr + 16 * i;
+          float4 h, l;
+          h.x = tf32_hi(va[i].x); l.x = va[i].x - h.x;
+          h.y = tf32_hi(va[i].y); l.y = va[i].y - h.y;
+          h.z = tf32_hi(va[i].z); l.z = va[i].z - h.z;
+          h.w = tf32_hi(va[i].w); l.w = va[i].w - h.w;
+          *reinterpret_cast<float4 *>(gbase + (sAhi - base) + swz(r, pc)) = h;
+          *reinterpret_cast<float4 *>(gbase + (sAlo - base) + swz(r, pc)) = l;
+        }
+        cp_async_wait_all();
+        fence_proxy_async();
+        mbar_arrive(full0 + 8 * s);
       }
-      mma_commit(bar0 + 8 * s);
     }
-  }
-  // all MMAs done: the last commit tracks every earlier MMA of this thread
-  if (ok && nk > 0) {
-    const int s = (nk - 1) % S::kStages;
-    bool w_ok = true;
-    if (tid == 0) w_ok = mbar_wait(bar0 + 8 * s, ((nk - 1) / S::kStages) & 1);
-    ok = __syncthreads_and(w_ok);
-  }
-  if (!ok) {
-    if (lane == 0) atomicExch(err, 1);
+  } else if (warp == 4) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = idesc_tf32<BN>();
+      int it = 0, chunk = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        for (int kt0 = 0; kt0 < nk && ok; kt0 += kChunk, ++chunk) {
+          const int b = chunk & 1;
+          if (!wait_or_abort(acce0 + 8 * b, ((chunk >> 1) & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t dtm = tmem + static_cast<uint32_t>(b * BN);
+          const int kend = kt0 + kChunk < nk ? kt0 + kChunk : nk;
+          for (int kt = kt0; kt < kend; ++kt, ++it) {
+            const int s = it % kStages;
+            if (!wait_or_abort(full0 + 8 * s, (it / kStages) & 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t st = base + s * kStageBytes;
+            const uint32_t sAhi = st, sAlo = st + BM * 128, sBhi = st + 2 * BM * 128, sBlo = st + 3 * BM * 128;
+#pragma unroll
+            for (int kk = 0; kk < BK / 8; ++kk) {
+              const uint32_t ko = kk * 32;
+              mma_tf32(dtm, sw128_desc(sAlo + ko), sw128_desc(sBhi + ko), idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+              mma_tf32(dtm, sw128_desc(sAhi + ko), sw128_desc(sBlo + ko), idesc, 1u);
+              mma_tf32(dtm, sw128_desc(sAhi + ko), sw128_desc(sBhi + ko), idesc, 1u);
+            }
+            mma_commit(empty0 + 8 * s);
+          }
+          if (ok) mma_commit(accf0 + 8 * b);
+        }
+      }
+    }
+    __syncwarp();
   } else {
-    tc_fence_after();
-    const int row = m0 + warp * 32 + lane;
-    const bool live = row < p.M;
-    const int rc = live ? (p.c_rows ? p.c_rows[row] : row) : 0;
-    float *crow = p.C + static_cast<size_t>(rc) * p.ldc;
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      float v[32];
-      tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c0, v);
-      const int nb = n0 + c0;
-      if (!live || nb >= p.N) continue;
+    // ---------------- accumulators + epilogue ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int chunk = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+      const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+      float acc[BN];
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        float4 x = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        if (p.bias) {
-          const float4 b = *reinterpret_cast<const float4 *>(p.bias + nb + j);
-          x.x += b.x; x.y += b.y; x.z += b.z; x.w += b.w;
+      for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+      for (int kt0 = 0; kt0 < nk; kt0 += kChunk, ++chunk) {
+        const int b = chunk & 1;
+        if (!wait_or_abort(accf0 + 8 * b, (chunk >> 1) & 1, abort_flag)) {
+          ok = false;
+          break;
         }
-        float4 *dst = reinterpret_cast<float4 *>(crow + nb + j);
-        if (EPI == EPI_STORE) {
-          *dst = x;
-        } else if (EPI == EPI_SILU) {
-          *reinterpret_cast<float4 *>(p.Z + static_cast<size_t>(row) * p.ldz + nb + j) = x;
-          *dst = make_float4(silu_f(x.x), silu_f(x.y), silu_f(x.z), silu_f(x.w));
-        } else if (EPI == EPI_ACCUM) {
-          const float4 o = *dst;
-          *dst = make_float4(o.x + x.x, o.y + x.y, o.z + x.z, o.w + x.w);
-        } else if (EPI == EPI_DSILU) {
-          const float4 z = *reinterpret_cast<const float4 *>(p.Z + static_cast<size_t>(row) * p.ldz + nb + j);
-          *dst = make_float4(x.x * dsilu_f(z.x), x.y * dsilu_f(z.y), x.z * dsilu_f(z.z), x.w * dsilu_f(z.w));
-        } else {  // EPI_RESID
-          const float4 r = *reinterpret_cast<const float4 *>(p.R + static_cast<size_t>(rc) * p.ldr + nb + j);
-          *dst = make_float4(x.x + r.x, x.y + r.y, x.z + r.z, x.w + r.w);
+        tc_fence_after();
+        const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN);
+#pragma unroll
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          float v[32];
+          tmem_ld32(taddr + c0, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[c0 + j] = __fadd_rn(acc[c0 + j], v[j]);
         }
+        tc_fence_before();
+        mbar_arrive(acce0 + 8 * b);
       }
+      if (ok) epilogue_store<EPI>(p, m0 + q * 32 + lane, n0, acc);
     }
   }
+
   tc_fence_before();
   __syncthreads();
-  if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+  if (tid == 0 && *abort_flag) atomicExch(err, 1);
+  if (warp == 4)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
 }
 
-template <int BN, int EPI>
+int g_num_sms = 0;
+
+template <int EPI>
 void launch(const GemmArgs &a, const TCWeights &w, int *err, cudaStream_t s) {
-  const int bytes = Smem<BN>::kBytes;
-  CUDA_CHECK(cudaFuncSetAttribute(k_gemm_3xtf32<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-  dim3 grid(ceil_div(a.M, BM), a.N / BN);
-  k_gemm_3xtf32<BN, EPI><<<grid, kThreads, bytes, s>>>(a, w, err);
-  CUDA_LAUNCH_CHECK();
-}
-
-template <int BN>
-void dispatch(const GemmArgs &a, const TCWeights &w, int *err, cudaStream_t s) {
-  switch (a.epi) {
-    case EPI_STORE: launch<BN, EPI_STORE>(a, w, err, s); break;
-    case EPI_SILU: launch<BN, EPI_SILU>(a, w, err, s); break;
-    case EPI_ACCUM: launch<BN, EPI_ACCUM>(a, w, err, s); break;
-    case EPI_DSILU: launch<BN, EPI_DSILU>(a, w, err, s); break;
-    case EPI_RESID: launch<BN, EPI_RESID>(a, w, err, s); break;
-    default: throw Error(kErrInternal, "gemm_tc: bad epilogue");
+  if (g_num_sms == 0) {
+    int dev = 0;
+    CUDA_CHECK(cudaGetDevice(&dev));
+    CUDA_CHECK(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev));
   }
+  CUDA_CHECK(cudaFuncSetAttribute(k_gemm_3xtf32<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+  const int tiles = ceil_div(a.M, BM) * (a.N / BN);
+  const int grid = tiles < g_num_sms ? tiles : g_num_sms;
+  k_gemm_3xtf32<EPI><<<grid, kWsThreads, kSmemBytes, s>>>(a, w, err);
+  CUDA_LAUNCH_CHECK();
 }
 
 }  // namespace
@@ -339,8 +403,14 @@ bool gemm_tc_supported(const GemmArgs &a) {
 }
 
 void gemm_3xtf32(const GemmArgs &a, const TCWeights &w, int *err, cudaStream_t s) {
-  if (a.N % 256 == 0) dispatch<256>(a, w, err, s);
-  else dispatch<128>(a, w, err, s);
+  switch (a.epi) {
+    case EPI_STORE: launch<EPI_STORE>(a, w, err, s); break;
+    case EPI_SILU: launch<EPI_SILU>(a, w, err, s); break;
+    case EPI_ACCUM: launch<EPI_ACCUM>(a, w, err, s); break;
+    case EPI_DSILU: launch<EPI_DSILU>(a, w, err, s); break;
+    case EPI_RESID: launch<EPI_RESID>(a, w, err, s); break;
+    default: throw Error(kErrInternal, "gemm_tc: bad epilogue");
+  }
 }
 
 }  // namespace pet
