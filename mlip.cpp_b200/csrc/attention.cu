@@ -9,9 +9,6 @@
 // zero weight, so processing each atom's real S_i = n_i + 1 tokens only is
 // the same computation without the padding.
 //
-// One CTA per (atom, head): K and V (and for backward Q, dO, P, dS) of that
-// head live in shared memory with a +1 pad so lane-per-key and
-// lane-per-channel accesses are bank-conflict free.
 #include <cfloat>
 
 #include "common.cuh"
@@ -20,213 +17,252 @@
 namespace pet {
 namespace {
 
-constexpr int kFwdWarps = 2;
-constexpr int kBwdWarps = 4;
+// One thread owns one (query token, head) row: its q (forward) or q and dO
+// (backward) stay in registers, and the head's K and V rows are read from
+// shared memory with 16-byte loads that every thread of a warp shares
+// (broadcast), so each load feeds 4-8 FMAs.  A CTA covers one atom and a
+// group of HG heads (threads = HG * S).  The forward keeps an online softmax
+// and stores each row's log-sum-exp; the backward recomputes P from it.
+constexpr size_t kSmemLimit = 227 * 1024;
 
-size_t fwd_smem(int S, int hd) {
-  return sizeof(float) * (2ull * S * (hd + 1) + S + kFwdWarps * hd + kFwdWarps * S);
+// Floats between consecutive heads' [S][HD] blocks in shared memory: padded
+// to 16 mod 32 so the two heads a warp can straddle read disjoint banks.
+__host__ __device__ __forceinline__ int head_stride(int S, int hd) {
+  const int n = S * hd;
+  return n + ((16 - n % 32) + 32) % 32;
 }
-size_t bwd_smem(int S, int hd) {
-  return sizeof(float) * (4ull * S * (hd + 1) + S + 2ull * S * (S + 1));
+size_t fwd_smem(int S, int hd, int hg) {
+  return sizeof(float) * (2ull * hg * head_stride(S, hd) + S);
+}
+size_t bwd_smem(int S, int hd, int hg) {
+  const int ps = S | 1;
+  return sizeof(float) * (4ull * hg * head_stride(S, hd) + 2ull * hg * S * ps + S + static_cast<size_t>(hg) * S);
 }
 
 template <int HD>
-__global__ void __launch_bounds__(32 * kFwdWarps) k_attn_fwd(AttnArgs a) {
-  extern __shared__ float sm[];
-  const int atom = blockIdx.x, h = blockIdx.y;
+__device__ __forceinline__ float dot_row(const float (&q)[HD], const float *__restrict__ krow) {
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+  for (int c = 0; c < HD; c += 4) {
+    const float4 k = *reinterpret_cast<const float4 *>(krow + c);
+    a0 = fmaf(q[c], k.x, a0);
+    a1 = fmaf(q[c + 1], k.y, a1);
+    a2 = fmaf(q[c + 2], k.z, a2);
+    a3 = fmaf(q[c + 3], k.w, a3);
+  }
+  return (a0 + a1) + (a2 + a3);
+}
+
+template <int HD>
+__device__ __forceinline__ void axpy_row(float (&o)[HD], float p, const float *__restrict__ vrow) {
+#pragma unroll
+  for (int c = 0; c < HD; c += 4) {
+    const float4 v = *reinterpret_cast<const float4 *>(vrow + c);
+    o[c] = fmaf(p, v.x, o[c]);
+    o[c + 1] = fmaf(p, v.y, o[c + 1]);
+    o[c + 2] = fmaf(p, v.z, o[c + 2]);
+    o[c + 3] = fmaf(p, v.w, o[c + 3]);
+  }
+}
+
+// Cooperative float4 copy of the (token, head-group) block of one of q/k/v
+// (column offset `col`) or of a [T, d] array into smem laid out [HG][S][HD].
+template <int HD>
+__device__ __forceinline__ void load_block(float *dst, const float *src, int ld, int col, int t0, int S,
+                                           int hg) {
+  const int per_row = HD / 4, per_head = S * per_row, n = hg * per_head, hs = head_stride(S, HD);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int hh = i / per_head, rem = i - hh * per_head, k = rem / per_row, c = (rem - k * per_row) * 4;
+    *reinterpret_cast<float4 *>(dst + hh * hs + k * HD + c) =
+        *reinterpret_cast<const float4 *>(src + static_cast<size_t>(t0 + k) * ld + col + hh * HD + c);
+  }
+}
+
+template <int HD>
+__global__ void k_attn_fwd(AttnArgs a, int hg) {
+  extern __shared__ __align__(16) float sm[];
+  const int atom = blockIdx.x, h0 = blockIdx.y * hg;
   const int e0 = a.offset[atom];
   const int S = a.offset[atom + 1] - e0 + 1;
   const int t0 = e0 + atom;
   const int d = a.d, ld = 3 * d;
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  float *sK = sm;
-  float *sV = sK + S * (HD + 1);
-  float *sM = sV + S * (HD + 1);
-  float *sQ = sM + S + w * HD;
-  float *sP = sM + S + kFwdWarps * HD + w * S;
-  for (int idx = threadIdx.x; idx < S * HD; idx += blockDim.x) {
-    const int s = idx / HD, c = idx % HD;
-    const float *row = a.qkv + static_cast<size_t>(t0 + s) * ld + h * HD + c;
-    sK[s * (HD + 1) + c] = row[d];
-    sV[s * (HD + 1) + c] = row[2 * d];
-  }
-  for (int s = threadIdx.x; s < S; s += blockDim.x) sM[s] = s == 0 ? 0.f : a.key_mask[e0 + s - 1];
+  const int hs = head_stride(S, HD);
+  float *sK = sm, *sV = sK + hg * hs, *sM = sV + hg * hs;
+  load_block<HD>(sK, a.qkv, ld, d + h0 * HD, t0, S, hg);
+  load_block<HD>(sV, a.qkv, ld, 2 * d + h0 * HD, t0, S, hg);
+  for (int k = threadIdx.x; k < S; k += blockDim.x) sM[k] = k == 0 ? 0.f : a.key_mask[e0 + k - 1];
   __syncthreads();
-  const float scale = 1.0f / sqrtf(static_cast<float>(HD));
-  for (int q = w; q < S; q += kFwdWarps) {
-    const float *qrow = a.qkv + static_cast<size_t>(t0 + q) * ld + h * HD;
-    for (int c = lane; c < HD; c += 32) sQ[c] = qrow[c];
-    __syncwarp();
-    float mx = -FLT_MAX;
-    for (int k = lane; k < S; k += 32) {
-      float s = 0.f;
+  const int t = threadIdx.x;
+  if (t >= hg * S) return;
+  const int hh = t / S, q = t - hh * S, h = h0 + hh;
+  float qr[HD], o[HD];
+  const float *qsrc = a.qkv + static_cast<size_t>(t0 + q) * ld + h * HD;
 #pragma unroll
-      for (int c = 0; c < HD; ++c) s = fmaf(sQ[c], sK[k * (HD + 1) + c], s);
-      s = s * scale + sM[k];
-      sP[k] = s;
-      mx = fmaxf(mx, s);
-    }
-    mx = warp_max(mx);
-    float sum = 0.f;
-    for (int k = lane; k < S; k += 32) {
-      const float p = expf(sP[k] - mx);
-      sP[k] = p;
-      sum += p;
-    }
-    sum = warp_sum(sum);
-    __syncwarp();
-    const float inv = 1.0f / sum;
-    float *orow = a.out + static_cast<size_t>(t0 + q) * d + h * HD;
-    for (int c = lane; c < HD; c += 32) {
-      float o = 0.f;
-      for (int k = 0; k < S; ++k) o = fmaf(sP[k], sV[k * (HD + 1) + c], o);
-      orow[c] = o * inv;
-    }
-    __syncwarp();
+  for (int c = 0; c < HD; c += 4) {
+    const float4 v = *reinterpret_cast<const float4 *>(qsrc + c);
+    qr[c] = v.x; qr[c + 1] = v.y; qr[c + 2] = v.z; qr[c + 3] = v.w;
+    o[c] = o[c + 1] = o[c + 2] = o[c + 3] = 0.f;
   }
+  const float scale = 1.0f / sqrtf(static_cast<float>(HD));
+  const float *K = sK + hh * hs, *V = sV + hh * hs;
+  float m = -FLT_MAX, l = 0.f;
+  for (int k = 0; k < S; ++k) {
+    const float s = dot_row<HD>(qr, K + k * HD) * scale + sM[k];
+    if (s > m) {
+      const float corr = expf(m - s);
+      l *= corr;
+#pragma unroll
+      for (int c = 0; c < HD; ++c) o[c] *= corr;
+      m = s;
+    }
+    const float p = expf(s - m);
+    l += p;
+    axpy_row<HD>(o, p, V + k * HD);
+  }
+  const float inv = 1.0f / l;
+  float *dst = a.out + static_cast<size_t>(t0 + q) * d + h * HD;
+#pragma unroll
+  for (int c = 0; c < HD; c += 4)
+    *reinterpret_cast<float4 *>(dst + c) = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+  a.lse[static_cast<size_t>(t0 + q) * a.heads + h] = m + logf(l);
 }
 
-// dV = P^T dO, dP = dO V^T, dS = P (dP - rowsum(P dP)), dQ = s dS K, dK = s dS^T Q.
+// dS = P (dP - rowsum(P dP)), dQ = s dS K, dK = s dS^T Q, dV = P^T dO.
 // The mask is a constant input in the reference (pet.cpp:274-275): no grad.
 template <int HD>
-__global__ void __launch_bounds__(32 * kBwdWarps) k_attn_bwd(AttnArgs a) {
-  extern __shared__ float sm[];
-  const int atom = blockIdx.x, h = blockIdx.y;
+__global__ void k_attn_bwd(AttnArgs a, int hg) {
+  extern __shared__ __align__(16) float sm[];
+  const int atom = blockIdx.x, h0 = blockIdx.y * hg;
   const int e0 = a.offset[atom];
   const int S = a.offset[atom + 1] - e0 + 1;
   const int t0 = e0 + atom;
   const int d = a.d, ld = 3 * d;
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const int P1 = HD + 1, PS = S + 1;
-  float *sQ = sm;
-  float *sK = sQ + S * P1;
-  float *sV = sK + S * P1;
-  float *sG = sV + S * P1;  // dO
-  float *sM = sG + S * P1;
-  float *sP = sM + S;       // [S][S+1]
-  float *sD = sP + S * PS;  // dS [S][S+1]
-  for (int idx = threadIdx.x; idx < S * HD; idx += blockDim.x) {
-    const int s = idx / HD, c = idx % HD;
-    const float *row = a.qkv + static_cast<size_t>(t0 + s) * ld + h * HD + c;
-    sQ[s * P1 + c] = row[0];
-    sK[s * P1 + c] = row[d];
-    sV[s * P1 + c] = row[2 * d];
-    sG[s * P1 + c] = a.d_out[static_cast<size_t>(t0 + s) * d + h * HD + c];
+  const int PS = S | 1;
+  const int hs = head_stride(S, HD);
+  float *sQ = sm, *sK = sQ + hg * hs, *sV = sK + hg * hs, *sG = sV + hg * hs;
+  float *sP = sG + hg * hs, *sD = sP + hg * S * PS, *sM = sD + hg * S * PS, *sL = sM + S;
+  load_block<HD>(sQ, a.qkv, ld, h0 * HD, t0, S, hg);
+  load_block<HD>(sK, a.qkv, ld, d + h0 * HD, t0, S, hg);
+  load_block<HD>(sV, a.qkv, ld, 2 * d + h0 * HD, t0, S, hg);
+  load_block<HD>(sG, a.d_out, d, h0 * HD, t0, S, hg);
+  for (int k = threadIdx.x; k < S; k += blockDim.x) sM[k] = k == 0 ? 0.f : a.key_mask[e0 + k - 1];
+  for (int i = threadIdx.x; i < hg * S; i += blockDim.x) {
+    const int hh = i / S, q = i - hh * S;
+    sL[i] = a.lse[static_cast<size_t>(t0 + q) * a.heads + h0 + hh];
   }
-  for (int s = threadIdx.x; s < S; s += blockDim.x) sM[s] = s == 0 ? 0.f : a.key_mask[e0 + s - 1];
   __syncthreads();
+  const int t = threadIdx.x;
+  const bool live = t < hg * S;
+  const int hh = live ? t / S : 0, r = live ? t - hh * S : 0, h = h0 + hh;
   const float scale = 1.0f / sqrtf(static_cast<float>(HD));
-  for (int q = w; q < S; q += kBwdWarps) {
-    float *prow = sP + q * PS;
-    float *drow = sD + q * PS;
-    float mx = -FLT_MAX;
-    for (int k = lane; k < S; k += 32) {
-      float s = 0.f;
+  const float *Q = sQ + hh * hs, *K = sK + hh * hs, *V = sV + hh * hs, *G = sG + hh * hs;
+  float *P = sP + hh * S * PS, *Dm = sD + hh * S * PS;
+  if (live) {
+    // phase A: thread = query row r
+    float qr[HD], g[HD], acc[HD];
 #pragma unroll
-      for (int c = 0; c < HD; ++c) s = fmaf(sQ[q * P1 + c], sK[k * P1 + c], s);
-      s = s * scale + sM[k];
-      prow[k] = s;
-      mx = fmaxf(mx, s);
+    for (int c = 0; c < HD; c += 4) {
+      const float4 v = *reinterpret_cast<const float4 *>(Q + r * HD + c);
+      const float4 w = *reinterpret_cast<const float4 *>(G + r * HD + c);
+      qr[c] = v.x; qr[c + 1] = v.y; qr[c + 2] = v.z; qr[c + 3] = v.w;
+      g[c] = w.x; g[c + 1] = w.y; g[c + 2] = w.z; g[c + 3] = w.w;
+      acc[c] = acc[c + 1] = acc[c + 2] = acc[c + 3] = 0.f;
     }
-    mx = warp_max(mx);
-    float sum = 0.f;
-    for (int k = lane; k < S; k += 32) {
-      const float p = expf(prow[k] - mx);
-      prow[k] = p;
-      sum += p;
+    const float lse = sL[hh * S + r];
+    float D = 0.f;
+    for (int k = 0; k < S; ++k) {
+      const float p = expf(dot_row<HD>(qr, K + k * HD) * scale + sM[k] - lse);
+      const float dp = dot_row<HD>(g, V + k * HD);
+      P[r * PS + k] = p;
+      Dm[r * PS + k] = dp;
+      D = fmaf(p, dp, D);
     }
-    sum = warp_sum(sum);
-    const float inv = 1.0f / sum;
-    float dsum = 0.f;
-    for (int k = lane; k < S; k += 32) {
-      const float p = prow[k] * inv;
-      prow[k] = p;
-      float dp = 0.f;
+    for (int k = 0; k < S; ++k) {
+      const float ds = P[r * PS + k] * (Dm[r * PS + k] - D);
+      Dm[r * PS + k] = ds;
+      axpy_row<HD>(acc, ds, K + k * HD);
+    }
+    float *dq = a.d_qkv + static_cast<size_t>(t0 + r) * ld + h * HD;
 #pragma unroll
-      for (int c = 0; c < HD; ++c) dp = fmaf(sG[q * P1 + c], sV[k * P1 + c], dp);
-      drow[k] = dp;
-      dsum = fmaf(p, dp, dsum);
-    }
-    dsum = warp_sum(dsum);
-    for (int k = lane; k < S; k += 32) drow[k] = prow[k] * (drow[k] - dsum);
-    __syncwarp();
-    float *dq = a.d_qkv + static_cast<size_t>(t0 + q) * ld + h * HD;
-    for (int c = lane; c < HD; c += 32) {
-      float acc = 0.f;
-      for (int k = 0; k < S; ++k) acc = fmaf(drow[k], sK[k * P1 + c], acc);
-      dq[c] = acc * scale;
-    }
+    for (int c = 0; c < HD; c += 4)
+      *reinterpret_cast<float4 *>(dq + c) =
+          make_float4(acc[c] * scale, acc[c + 1] * scale, acc[c + 2] * scale, acc[c + 3] * scale);
   }
   __syncthreads();
-  for (int k = w; k < S; k += kBwdWarps) {
-    float *dk = a.d_qkv + static_cast<size_t>(t0 + k) * ld + h * HD;
-    for (int c = lane; c < HD; c += 32) {
-      float gk = 0.f, gv = 0.f;
-      for (int q = 0; q < S; ++q) {
-        gk = fmaf(sD[q * PS + k], sQ[q * P1 + c], gk);
-        gv = fmaf(sP[q * PS + k], sG[q * P1 + c], gv);
-      }
-      dk[d + c] = gk * scale;
-      dk[2 * d + c] = gv;
+  if (live) {
+    // phase B: thread = key row r
+    float dk[HD], dv[HD];
+#pragma unroll
+    for (int c = 0; c < HD; ++c) dk[c] = dv[c] = 0.f;
+    for (int q = 0; q < S; ++q) {
+      axpy_row<HD>(dk, Dm[q * PS + r], Q + q * HD);
+      axpy_row<HD>(dv, P[q * PS + r], G + q * HD);
+    }
+    float *dst = a.d_qkv + static_cast<size_t>(t0 + r) * ld + h * HD;
+#pragma unroll
+    for (int c = 0; c < HD; c += 4) {
+      *reinterpret_cast<float4 *>(dst + d + c) =
+          make_float4(dk[c] * scale, dk[c + 1] * scale, dk[c + 2] * scale, dk[c + 3] * scale);
+      *reinterpret_cast<float4 *>(dst + 2 * d + c) = make_float4(dv[c], dv[c + 1], dv[c + 2], dv[c + 3]);
     }
   }
 }
 
-template <int HD>
-void run_fwd(const AttnArgs &a, cudaStream_t s) {
-  const size_t sm = fwd_smem(a.max_tokens, HD);
-  CUDA_CHECK(cudaFuncSetAttribute(k_attn_fwd<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(sm)));
-  k_attn_fwd<HD><<<dim3(a.n_atoms, a.heads), 32 * kFwdWarps, sm, s>>>(a);
-  CUDA_LAUNCH_CHECK();
+// Heads per CTA: the largest of 4, 2, 1 that divides the head count, keeps
+// HG * S threads <= 1024 and fits the shared-memory budget `limit`.
+int pick_group(int heads, int S, int hd, bool bwd, size_t limit) {
+  for (int hg = 4; hg >= 1; hg >>= 1) {
+    if (heads % hg) continue;
+    if (hg * S > 1024) continue;
+    if ((bwd ? bwd_smem(S, hd, hg) : fwd_smem(S, hd, hg)) <= limit) return hg;
+  }
+  return 0;
 }
 
 template <int HD>
-void run_bwd(const AttnArgs &a, cudaStream_t s) {
-  const size_t sm = bwd_smem(a.max_tokens, HD);
-  CUDA_CHECK(cudaFuncSetAttribute(k_attn_bwd<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(sm)));
-  k_attn_bwd<HD><<<dim3(a.n_atoms, a.heads), 32 * kBwdWarps, sm, s>>>(a);
+void run(const AttnArgs &a, bool bwd, cudaStream_t s) {
+  const int S = a.max_tokens;
+  // prefer two CTAs per SM for the backward's large footprint
+  int hg = pick_group(a.heads, S, HD, bwd, bwd ? kSmemLimit / 2 : kSmemLimit / 4);
+  if (!hg) hg = pick_group(a.heads, S, HD, bwd, kSmemLimit);
+  if (!hg) throw Error(kErrUnsupported, "attention: too many neighbours for one CTA");
+  const size_t smem = bwd ? bwd_smem(S, HD, hg) : fwd_smem(S, HD, hg);
+  const int threads = (hg * S + 31) / 32 * 32;
+  dim3 grid(a.n_atoms, a.heads / hg);
+  if (bwd) {
+    CUDA_CHECK(cudaFuncSetAttribute(k_attn_bwd<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    k_attn_bwd<HD><<<grid, threads, smem, s>>>(a, hg);
+  } else {
+    CUDA_CHECK(cudaFuncSetAttribute(k_attn_fwd<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    k_attn_fwd<HD><<<grid, threads, smem, s>>>(a, hg);
+  }
   CUDA_LAUNCH_CHECK();
 }
 
-constexpr size_t kSmemLimit = 227 * 1024;
+void dispatch(const AttnArgs &a, bool bwd, cudaStream_t s) {
+  if (a.n_atoms <= 0) return;
+  const int hd = a.d / a.heads;
+  if (a.max_tokens > attention_max_tokens(hd))
+    throw Error(kErrUnsupported, "attention: " + std::to_string(a.max_tokens - 1) +
+                                     " neighbours exceed the per-atom limit");
+  switch (hd) {
+    case 16: run<16>(a, bwd, s); break;
+    case 32: run<32>(a, bwd, s); break;
+    case 64: run<64>(a, bwd, s); break;
+    default: throw Error(kErrUnsupported, "attention: head size " + std::to_string(hd));
+  }
+}
 
 }  // namespace
 
 int attention_max_tokens(int hd) {
   int S = 1;
-  while (bwd_smem(S + 1, hd) <= kSmemLimit && fwd_smem(S + 1, hd) <= kSmemLimit) ++S;
+  while (pick_group(1, S + 1, hd, true, kSmemLimit) && pick_group(1, S + 1, hd, false, kSmemLimit)) ++S;
   return S;
 }
 
-void attention_fwd(const AttnArgs &a, cudaStream_t s) {
-  if (a.n_atoms <= 0) return;
-  const int hd = a.d / a.heads;
-  if (a.max_tokens > attention_max_tokens(hd))
-    throw Error(kErrUnsupported, "attention: " + std::to_string(a.max_tokens - 1) +
-                                     " neighbours exceed the per-atom limit");
-  switch (hd) {
-    case 16: run_fwd<16>(a, s); break;
-    case 32: run_fwd<32>(a, s); break;
-    case 64: run_fwd<64>(a, s); break;
-    default: throw Error(kErrUnsupported, "attention: head size " + std::to_string(hd));
-  }
-}
-
-void attention_bwd(const AttnArgs &a, cudaStream_t s) {
-  if (a.n_atoms <= 0) return;
-  const int hd = a.d / a.heads;
-  if (a.max_tokens > attention_max_tokens(hd))
-    throw Error(kErrUnsupported, "attention: " + std::to_string(a.max_tokens - 1) +
-                                     " neighbours exceed the per-atom limit");
-  switch (hd) {
-    case 16: run_bwd<16>(a, s); break;
-    case 32: run_bwd<32>(a, s); break;
-    case 64: run_bwd<64>(a, s); break;
-    default: throw Error(kErrUnsupported, "attention: head size " + std::to_string(hd));
-  }
-}
+void attention_fwd(const AttnArgs &a, cudaStream_t s) { dispatch(a, false, s); }
+void attention_bwd(const AttnArgs &a, cudaStream_t s) { dispatch(a, true, s); }
 
 // ---------------------------------------------------------------------------
 // Layer norm (warp per row)

@@ -46,6 +46,7 @@ struct AttnArgs {
   float *out;             // [T, d]   forward output
   const float *d_out;     // [T, d]   backward: upstream grad
   float *d_qkv;           // [T, 3d]  backward: result
+  float *lse;             // [T, heads] row log-sum-exp (forward writes, backward reads)
   const float *key_mask;  // [E] additive mask of each edge key (node key: 0)
   const int *offset;      // [N+1] edge offsets (CSR)
   int n_atoms, d, heads, max_tokens;

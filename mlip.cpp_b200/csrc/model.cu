@@ -58,7 +58,7 @@ struct Acts {
   float *r, *fc, *dfc_dr, *key_mask;
   int *edge_row, *node_row, *nbr_species, *rev;
   // kept for backward
-  float *qkv[4], *xa[4], *ra[4], *zf[4], *xm[4], *rm[4];
+  float *qkv[4], *xa[4], *ra[4], *zf[4], *xm[4], *rm[4], *lse[4];
   float *zc[2], *zn1[2], *zn2[2], *ze1[2], *ze2[2];
   float *gfc, *e_atom;
   // forward scratch
@@ -318,6 +318,7 @@ static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, int N, int E
   a.rev = P.take<int>(En);
   for (int b = 0; b < 4; ++b) {
     a.qkv[b] = P.take<float>(T * 3 * d);
+    a.lse[b] = P.take<float>(T * h.heads);
     a.xa[b] = P.take<float>(T * d); a.ra[b] = P.take<float>(T);
     a.zf[b] = P.take<float>(T * f);
     a.xm[b] = P.take<float>(T * d); a.rm[b] = P.take<float>(T);
@@ -401,6 +402,7 @@ void PETModel::forward_backward(bool grad) {
     const BlockW &B = g_lw[b / 2].blk[b % 2];
     gemm(x, d, nullptr, B.Win, d, a.qkv[b], 3 * d, nullptr, T, 3 * d, d, B.bin, EPI_STORE, s);
     at.qkv = a.qkv[b];
+    at.lse = a.lse[b];
     at.out = a.o;
     attn(false, at);
     gemm(a.o, d, nullptr, B.Wout, d, a.u, d, nullptr, T, d, d, B.bout, EPI_RESID, s, nullptr, 0, x, d);
@@ -462,6 +464,7 @@ void PETModel::forward_backward(bool grad) {
     layer_norm_bwd(a.dx1, a.xa[b], a.ra[b], B.ga, a.du, T, d, s);
     gemm(a.du, d, nullptr, B.WoutT, d, a.dout, d, nullptr, T, d, d, nullptr, EPI_STORE, s);
     at.qkv = a.qkv[b];
+    at.lse = a.lse[b];
     at.d_out = a.dout;
     at.d_qkv = a.dqkv;
     attn(true, at);
