@@ -20,7 +20,8 @@ from dataclasses import dataclass, field
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libmlipcpp_b200.so")
+# MLIPCPP_B200_LIB selects another build of the library (e.g. a variant).
+LIB_PATH = os.environ.get("MLIPCPP_B200_LIB") or os.path.join(HERE, "libmlipcpp_b200.so")
 
 # mlipcpp_error_t (include/mlipcpp.h)
 OK, INVALID_HANDLE, NULL_POINTER, MODEL_NOT_LOADED, OUT_OF_MEMORY, IO_ERROR, COMPUTATION, \
@@ -116,6 +117,42 @@ def _check(code: int):
     if code != OK:
         msg = lib().mlipcpp_get_last_error() or lib().mlipcpp_error_string(code)
         raise MLIPError(code, msg.decode())
+
+
+class LogLevel:
+    """mlipcpp.LogLevel (logging is a no-op in this backend)."""
+    Trace, Debug, Info, Warn, Error, Off = range(6)
+
+
+def set_log_level(level) -> None:
+    """Accepted for compatibility; the library does not log."""
+    lib().mlipcpp_suppress_logging()
+
+
+def enable_logging() -> None:
+    """Accepted for compatibility; the library does not log."""
+
+
+def set_backend(backend: int) -> None:
+    """Global backend for Predictors created afterwards (CUDA / Auto only)."""
+    lib().mlipcpp_set_backend(int(backend))
+
+
+def get_backend_name() -> str:
+    return lib().mlipcpp_get_backend_name().decode()
+
+
+def backend_is_gpu() -> bool:
+    return bool(lib().mlipcpp_backend_is_gpu())
+
+
+def is_backend_available(backend: int) -> bool:
+    return bool(lib().mlipcpp_is_backend_available(int(backend)))
+
+
+def load_model(path: str, **kwargs) -> "Predictor":
+    """mlipcpp.load_model: a Predictor with ModelOptions(**kwargs)."""
+    return Predictor(path, ModelOptions(**kwargs))
 
 
 def set_device(device: int):
@@ -394,3 +431,9 @@ def neighbor_list(positions, cell=None, pbc=None, cutoff: float = 4.5) -> dict:
         _check(int(-m2))
     out["n_atoms"] = pos.shape[0]
     return out
+
+
+def __getattr__(name):
+    if name == "__version__":
+        return version()
+    raise AttributeError(name)

@@ -10,8 +10,8 @@
 #include <string>
 #include <vector>
 
-#include "../../include/mlipcpp.h"
-#include "../../include/mlipcpp_b200.h"
+#include "mlipcpp.h"
+#include "mlipcpp_b200.h"
 #include "gguf.h"
 #include "model.h"
 

@@ -145,7 +145,10 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
 // result at fp32 accuracy for K up to thousands.
 constexpr int BN = 128;
 constexpr int kStages = 3;
-constexpr int kChunk = 2;  // k-tiles (of 32) per TMEM accumulation pass
+#ifndef PET_GEMM_CHUNK
+#define PET_GEMM_CHUNK 4
+#endif
+constexpr int kChunk = PET_GEMM_CHUNK;  // k-tiles (of 32) per TMEM accumulation pass
 constexpr int kStageBytes = 4 * BM * 128;  // A hi, A lo, B hi, B lo
 constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
 constexpr int kWsThreads = 288;
