@@ -252,7 +252,12 @@ def main():
                          "frac": achieved / (bf16_sus / 6.0),
                          "peak_source": f"{src} bf16 sustained / 6 (3 tf32 MMAs at half bf16 rate)",
                          "tensor_pipe_frac_of_bf16": 6.0 * achieved / bf16_sus,
-                         "traffic": None,
+                         # DRAM bytes per average GEMM launch: ncu dram__bytes_read.sum +
+                         # dram__bytes_write.sum over all 57 GEMM launches of one step of the
+                         # 1,728-atom cell of this alloy (354 MB/launch at 65,202 tokens,
+                         # 5,429 B per token), scaled by this step's token count
+                         "traffic": 5429.0 * (shape["atoms"] + shape["edges"]) if world == 1 else None,
+                         "traffic_unit": "bytes per GEMM launch (scaled from the 1,728-atom capture)",
                          "gemm_share_of_step": (g["ms"] + gs["ms"]) / (t_dev * 1e3) if t_dev else None},
             "kernel_stats": kstats,
             "phase_ms": pred.last_timings(),

@@ -36,6 +36,25 @@ mlipcpp_error_t mlipcpp_b200_predict_device(mlipcpp_model_t model, int32_t n_ato
                                             const mlipcpp_predict_options_t *options,
                                             bool copy_forces, mlipcpp_result_t *result);
 
+/* One spatial domain of a large periodic cell (multi-GPU domain
+ * decomposition).  d_positions: device pointer to [3 * n_local] double, the
+ * owned atoms first, then the ghost atoms within one cutoff of the owned
+ * region, then the other ghosts (periodic images already placed);
+ * atomic_numbers is a host array.  Layer 0 runs on the first n_layer0
+ * atoms, layer 1 and the readout on the first n_owned.  bbox: row-major
+ * cell that encloses the local positions (searched without periodicity).
+ * Outputs: energy of the owned atoms (host, eV, f64, composition included),
+ * gradient forces on every local atom (d_forces: device [3 * n_local] float,
+ * may be NULL), and the local virial sum_e e (x) dE/de in Voigt order (host,
+ * f64, not divided by a volume).  Summing energies, virials and the forces
+ * of each atom over all domains gives the whole cell's results. */
+mlipcpp_error_t mlipcpp_b200_predict_local(mlipcpp_model_t model, int32_t n_local,
+                                           const double *d_positions,
+                                           const int32_t *atomic_numbers, int32_t n_layer0,
+                                           int32_t n_owned, const float bbox[9],
+                                           bool compute_forces, float *d_forces, double *energy,
+                                           double virial[6]);
+
 /* Enable per-phase CUDA-event timing of later predictions. */
 mlipcpp_error_t mlipcpp_b200_set_timing(mlipcpp_model_t model, bool enable);
 

@@ -532,6 +532,29 @@ mlipcpp_error_t mlipcpp_b200_predict_device(mlipcpp_model_t model, int32_t n_ato
   }
 }
 
+mlipcpp_error_t mlipcpp_b200_predict_local(mlipcpp_model_t model, int32_t n_local, const double *d_positions,
+                                           const int32_t *atomic_numbers, int32_t n_layer0, int32_t n_owned,
+                                           const float bbox[9], bool compute_forces, float *d_forces,
+                                           double *energy, double virial[6]) {
+  if (auto e = check_model(model)) return e;
+  if (!d_positions || !atomic_numbers || !bbox || !energy || !virial) {
+    set_error("NULL pointer argument");
+    return MLIPCPP_ERROR_NULL_POINTER;
+  }
+  if (n_local <= 0 || n_owned < 0 || n_layer0 < n_owned || n_local < n_layer0) {
+    set_error("local system needs 0 <= n_owned <= n_layer0 <= n_local, n_local > 0");
+    return MLIPCPP_ERROR_INVALID_PARAMETER;
+  }
+  try {
+    model->model->predict_local(d_positions, n_local, atomic_numbers, n_layer0, n_owned, bbox, compute_forces,
+                                d_forces, energy, virial);
+    clear_error();
+    return MLIPCPP_OK;
+  } catch (const std::exception &e) {
+    return map_exception(e, "Prediction failed: ", MLIPCPP_ERROR_COMPUTATION);
+  }
+}
+
 mlipcpp_error_t mlipcpp_b200_set_timing(mlipcpp_model_t model, bool enable) {
   if (auto e = check_model(model)) return e;
   model->model->set_timing(enable);

@@ -308,15 +308,25 @@ void PETModel::load(const std::string &path, float cutoff_override) {
 // ---------------------------------------------------------------------------
 // Memory plan
 // ---------------------------------------------------------------------------
-static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, int N, int E, bool grad) {
-  const size_t T = static_cast<size_t>(N) + E, d = h.d, f = h.ff, r = h.dh, H = h.hid;
-  const size_t En = E > 0 ? E : 1, Nn = N > 0 ? N : 1;
+// Sizes: n_local atoms in the system, layer 0 runs on the first N0 atoms
+// (E0 edges, T0 = N0 + E0 tokens), layer 1 and the readout on the first N1
+// (E1, T1).  A whole structure has n_local = N0 = N1.
+struct Counts {
+  int n_local, N0, E0, N1, E1;
+};
+
+static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, const Counts &c, bool grad) {
+  const size_t d = h.d, f = h.ff, r = h.dh, H = h.hid;
+  const size_t E0 = std::max(c.E0, 1), N0 = std::max(c.N0, 1), E1 = std::max(c.E1, 1),
+               N1 = std::max(c.N1, 1), NL = std::max(c.n_local, 1);
+  const size_t T0 = N0 + E0, T1 = N1 + E1;
   // persistent (graph + activations kept for backward)
-  a.r = P.take<float>(En); a.fc = P.take<float>(En); a.dfc_dr = P.take<float>(En);
-  a.key_mask = P.take<float>(En);
-  a.edge_row = P.take<int>(En); a.node_row = P.take<int>(Nn); a.nbr_species = P.take<int>(En);
-  a.rev = P.take<int>(En);
+  a.r = P.take<float>(E0); a.fc = P.take<float>(E0); a.dfc_dr = P.take<float>(E0);
+  a.key_mask = P.take<float>(E0);
+  a.edge_row = P.take<int>(E0); a.node_row = P.take<int>(N0); a.nbr_species = P.take<int>(E0);
+  a.rev = P.take<int>(E0);
   for (int b = 0; b < 4; ++b) {
+    const size_t T = b < 2 ? T0 : T1;
     a.qkv[b] = P.take<float>(T * 3 * d);
     a.lse[b] = P.take<float>(T * h.heads);
     a.xa[b] = P.take<float>(T * d); a.ra[b] = P.take<float>(T);
@@ -324,35 +334,35 @@ static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, int N, int E
     a.xm[b] = P.take<float>(T * d); a.rm[b] = P.take<float>(T);
   }
   for (int l = 0; l < 2; ++l) {
-    a.zc[l] = P.take<float>(En * H);
-    a.zn1[l] = P.take<float>(Nn * r); a.zn2[l] = P.take<float>(Nn * r);
-    a.ze1[l] = P.take<float>(En * r); a.ze2[l] = P.take<float>(En * r);
+    a.zc[l] = P.take<float>((l == 0 ? E0 : E1) * H);
+    a.zn1[l] = P.take<float>(N1 * r); a.zn2[l] = P.take<float>(N1 * r);
+    a.ze1[l] = P.take<float>(E1 * r); a.ze2[l] = P.take<float>(E1 * r);
   }
-  a.gfc = P.take<float>(En);
-  a.e_atom = P.take<float>(Nn);
-  a.F = P.take<float>(3 * Nn);
-  a.g = P.take<float>(3 * En);
-  a.g4 = P.take<float>(4 * En);
+  a.gfc = P.take<float>(E0);
+  a.e_atom = P.take<float>(N1);
+  a.F = P.take<float>(3 * NL);
+  a.g = P.take<float>(3 * E0);
+  a.g4 = P.take<float>(4 * E0);
   // forward scratch
   Plan fs = S;
-  a.cat = fs.take<float>(En * 3 * d); a.hc = fs.take<float>(En * H);
-  a.xin = fs.take<float>(T * d); a.xmid = fs.take<float>(T * d);
-  a.xl[0] = fs.take<float>(T * d); a.xl[1] = fs.take<float>(T * d);
-  a.o = fs.take<float>(T * d); a.u = fs.take<float>(T * d); a.x1 = fs.take<float>(T * d);
-  a.hf = fs.take<float>(T * f); a.u2 = fs.take<float>(T * d);
-  a.yn1 = fs.take<float>(Nn * r); a.yn2 = fs.take<float>(Nn * r);
-  a.ye1 = fs.take<float>(En * r); a.ye2 = fs.take<float>(En * r);
-  a.node_pred = fs.take<float>(Nn); a.edge_pred = fs.take<float>(En);
+  a.cat = fs.take<float>(E0 * 3 * d); a.hc = fs.take<float>(E0 * H);
+  a.xin = fs.take<float>(T0 * d); a.xmid = fs.take<float>(T0 * d);
+  a.xl[0] = fs.take<float>(T0 * d); a.xl[1] = fs.take<float>(T1 * d);
+  a.o = fs.take<float>(T0 * d); a.u = fs.take<float>(T0 * d); a.x1 = fs.take<float>(T0 * d);
+  a.hf = fs.take<float>(T0 * f); a.u2 = fs.take<float>(T0 * d);
+  a.yn1 = fs.take<float>(N1 * r); a.yn2 = fs.take<float>(N1 * r);
+  a.ye1 = fs.take<float>(E1 * r); a.ye2 = fs.take<float>(E1 * r);
+  a.node_pred = fs.take<float>(N1); a.edge_pred = fs.take<float>(E1);
   size_t fwd_end = fs.off;
   // backward scratch (aliases the forward scratch)
   Plan bs = S;
   if (grad) {
-    a.dx = bs.take<float>(T * d); a.dx2 = bs.take<float>(T * d); a.du = bs.take<float>(T * d);
-    a.dout = bs.take<float>(T * d); a.dqkv = bs.take<float>(T * 3 * d); a.dx1 = bs.take<float>(T * d);
-    a.dhf = bs.take<float>(T * f);
-    const size_t rows = std::max(Nn, En);
+    a.dx = bs.take<float>(T0 * d); a.dx2 = bs.take<float>(T0 * d); a.du = bs.take<float>(T0 * d);
+    a.dout = bs.take<float>(T0 * d); a.dqkv = bs.take<float>(T0 * 3 * d); a.dx1 = bs.take<float>(T0 * d);
+    a.dhf = bs.take<float>(T0 * f);
+    const size_t rows = std::max(N1, E1);
     a.dz1 = bs.take<float>(rows * r); a.dz2 = bs.take<float>(rows * r);
-    a.dzc = bs.take<float>(En * H); a.demb = bs.take<float>(En * d); a.dmsg = bs.take<float>(En * d);
+    a.dzc = bs.take<float>(E0 * H); a.demb = bs.take<float>(E0 * d); a.dmsg = bs.take<float>(E1 * d);
   }
   S.off = std::max(fwd_end, bs.off);
 }
@@ -364,8 +374,9 @@ void PETModel::forward_backward(bool grad) {
   const Acts &a = in_->a;
   const LayerW *g_lw = in_->lw;
   const Hypers &h = h_;
-  const int N = N_, E = E_, T = T_;
   const int d = h.d, f = h.ff, r = h.dh, H = h.hid;
+  const int N1 = Nl_[1], E1 = El_[1], E0 = El_[0], T0 = Tl_[0];
+  int N = Nl_[0], E = El_[0], T = Tl_[0];  // the layer being processed
   cudaStream_t s = stream_;
   const int *offset = nl_.offset.as<int>();
   const int *species = d_species_.as<int>();
@@ -389,6 +400,7 @@ void PETModel::forward_backward(bool grad) {
     if (kprof_) mark_begin(e0);
     if (backward) attention_bwd(x, s); else attention_fwd(x, s);
     if (kprof_) mark_end(KC_ATTENTION, e0, 0.0, 4.0 * T * (backward ? 7.0 : 4.0) * d);
+    (void)x;
   };
   AttnArgs at{};
   at.key_mask = a.key_mask;
@@ -412,9 +424,14 @@ void PETModel::forward_backward(bool grad) {
     layer_norm_fwd(a.u2, B.gm, B.bm, out, a.xm[b], a.rm[b], T, d, s);
   };
 
+  if (E0 > E1) CUDA_CHECK(cudaMemsetAsync(a.gfc, 0, sizeof(float) * E0, s));
   for (int l = 0; l < 2; ++l) {
     const LayerW &L = g_lw[l];
     const int K = (l == 0 ? 2 : 3) * d;
+    N = Nl_[l];
+    E = El_[l];
+    T = Tl_[l];
+    at.n_atoms = N;
     if (E > 0) {
       FeaturizeArgs fa{};
       fa.n_edges = E; fa.d = d; fa.layer = l;
@@ -429,17 +446,17 @@ void PETModel::forward_backward(bool grad) {
     node_tokens(L.node_emb, species, a.node_row, a.xin, N, d, s);
     block_fwd(2 * l, a.xin, a.xmid);
     block_fwd(2 * l + 1, a.xmid, a.xl[l]);
-    // readout (pet_layers.cpp:920-1015)
-    gemm(a.xl[l], d, a.node_row, L.node.H0, d, a.yn1, r, nullptr, N, r, d, L.node.h0, EPI_SILU, s, a.zn1[l], r);
-    gemm(a.yn1, r, nullptr, L.node.H2, r, a.yn2, r, nullptr, N, r, r, L.node.h2, EPI_SILU, s, a.zn2[l], r);
-    head_last(a.yn2, L.node.HL, L.node.hl, a.node_pred, N, r, s);
-    if (E > 0) {
-      gemm(a.xl[l], d, a.edge_row, L.edge.H0, d, a.ye1, r, nullptr, E, r, d, L.edge.h0, EPI_SILU, s, a.ze1[l], r);
-      gemm(a.ye1, r, nullptr, L.edge.H2, r, a.ye2, r, nullptr, E, r, r, L.edge.h2, EPI_SILU, s, a.ze2[l], r);
-      head_last(a.ye2, L.edge.HL, L.edge.hl, a.edge_pred, E, r, s);
-      add_vec(a.edge_pred, a.gfc, E, l > 0, s);
+    // readout (pet_layers.cpp:920-1015) of the N1 atoms whose energy counts
+    gemm(a.xl[l], d, a.node_row, L.node.H0, d, a.yn1, r, nullptr, N1, r, d, L.node.h0, EPI_SILU, s, a.zn1[l], r);
+    gemm(a.yn1, r, nullptr, L.node.H2, r, a.yn2, r, nullptr, N1, r, r, L.node.h2, EPI_SILU, s, a.zn2[l], r);
+    head_last(a.yn2, L.node.HL, L.node.hl, a.node_pred, N1, r, s);
+    if (E1 > 0) {
+      gemm(a.xl[l], d, a.edge_row, L.edge.H0, d, a.ye1, r, nullptr, E1, r, d, L.edge.h0, EPI_SILU, s, a.ze1[l], r);
+      gemm(a.ye1, r, nullptr, L.edge.H2, r, a.ye2, r, nullptr, E1, r, r, L.edge.h2, EPI_SILU, s, a.ze2[l], r);
+      head_last(a.ye2, L.edge.HL, L.edge.hl, a.edge_pred, E1, r, s);
+      add_vec(a.edge_pred, a.gfc, E1, l > 0, s);
     }
-    atom_energy(a.node_pred, a.edge_pred, a.fc, offset, a.e_atom, N, l > 0, s);
+    atom_energy(a.node_pred, a.edge_pred, a.fc, offset, a.e_atom, N1, l > 0, s);
   }
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[4], s));
   if (!grad) return;
@@ -447,13 +464,13 @@ void PETModel::forward_backward(bool grad) {
   // ---- backward ----------------------------------------------------------
   auto readout_bwd = [&](int l, float *dst) {
     const LayerW &L = g_lw[l];
-    head_last_bwd(a.zn2[l], L.node.HL, nullptr, a.dz2, N, r, s);
-    gemm(a.dz2, r, nullptr, L.node.H2T, r, a.dz1, r, nullptr, N, r, r, nullptr, EPI_DSILU, s, a.zn1[l], r);
-    gemm(a.dz1, r, nullptr, L.node.H0T, r, dst, d, a.node_row, N, d, r, nullptr, EPI_STORE, s);
-    if (E > 0) {
-      head_last_bwd(a.ze2[l], L.edge.HL, a.fc, a.dz2, E, r, s);
-      gemm(a.dz2, r, nullptr, L.edge.H2T, r, a.dz1, r, nullptr, E, r, r, nullptr, EPI_DSILU, s, a.ze1[l], r);
-      gemm(a.dz1, r, nullptr, L.edge.H0T, r, dst, d, a.edge_row, E, d, r, nullptr, EPI_STORE, s);
+    head_last_bwd(a.zn2[l], L.node.HL, nullptr, a.dz2, N1, r, s);
+    gemm(a.dz2, r, nullptr, L.node.H2T, r, a.dz1, r, nullptr, N1, r, r, nullptr, EPI_DSILU, s, a.zn1[l], r);
+    gemm(a.dz1, r, nullptr, L.node.H0T, r, dst, d, a.node_row, N1, d, r, nullptr, EPI_STORE, s);
+    if (E1 > 0) {
+      head_last_bwd(a.ze2[l], L.edge.HL, a.fc, a.dz2, E1, r, s);
+      gemm(a.dz2, r, nullptr, L.edge.H2T, r, a.dz1, r, nullptr, E1, r, r, nullptr, EPI_DSILU, s, a.ze1[l], r);
+      gemm(a.dz1, r, nullptr, L.edge.H0T, r, dst, d, a.edge_row, E1, d, r, nullptr, EPI_STORE, s);
     }
   };
   auto block_bwd = [&](int b, const float *dy, float *dxin) {
@@ -481,31 +498,142 @@ void PETModel::forward_backward(bool grad) {
     edge_embed_bwd(a.demb, d, L.We, a.g4, E, d, accumulate, s);
   };
 
+  // layer 1 (its N1 atoms), then layer 0 (N0 atoms); layer-0 tokens of
+  // atoms beyond N1 receive gradient only through the reversed messages.
+  N = N1; E = E1; T = Tl_[1];
+  at.n_atoms = N;
+  if (E0 > 0) CUDA_CHECK(cudaMemsetAsync(a.g4, 0, sizeof(float) * 4 * E0, s));
   readout_bwd(1, a.dx);
   block_bwd(3, a.dx, a.dx2);
   block_bwd(2, a.dx2, a.dx);
-  if (E > 0) compress_bwd(1, a.dx, false);
+  if (E > 0) compress_bwd(1, a.dx, true);
+  N = Nl_[0]; E = E0; T = T0;
+  at.n_atoms = N;
+  if (T0 > Tl_[1]) CUDA_CHECK(cudaMemsetAsync(a.dx, 0, sizeof(float) * static_cast<size_t>(T0) * d, s));
   readout_bwd(0, a.dx);
-  if (E > 0) message_bwd(a.dmsg, d, a.rev, a.edge_row, a.dx, E, d, s);
+  if (E1 > 0) message_bwd(a.dmsg, d, a.rev, a.edge_row, a.dx, E0, E1, d, s);
   block_bwd(1, a.dx, a.dx2);
   block_bwd(0, a.dx2, a.dx);
-  if (E > 0) {
+  if (E0 > 0) {
     compress_bwd(0, a.dx, true);
-    edge_grad(a.g4, a.gfc, a.dfc_dr, nl_.vec.as<float>(), a.r, a.g, E, s);
+    edge_grad(a.g4, a.gfc, a.dfc_dr, nl_.vec.as<float>(), a.r, a.g, E0, s);
   }
-  forces(a.g, offset, nl_.nbr.as<int>(), a.rev, a.F, N, E, s);
+  if (n_local_ > Nl_[0]) CUDA_CHECK(cudaMemsetAsync(a.F, 0, sizeof(float) * 3 * n_local_, s));
+  forces(a.g, offset, nl_.nbr.as<int>(), a.rev, a.F, Nl_[0], E0, s);
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[5], s));
 }
 
 // ---------------------------------------------------------------------------
 // Prediction
 // ---------------------------------------------------------------------------
+void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const int *d_species, bool grad) {
+  n_local_ = n_local;
+  Nl_[0] = N0; El_[0] = E0; Tl_[0] = N0 + E0;
+  Nl_[1] = N1; El_[1] = E1; Tl_[1] = N1 + E1;
+  max_tok_ = nl_.max_count + 1;
+  if (max_tok_ > attention_max_tokens(h_.d / h_.heads))
+    throw Error(kErrUnsupported, "an atom has " + std::to_string(nl_.max_count) +
+                                     " neighbours, above the supported maximum of " +
+                                     std::to_string(attention_max_tokens(h_.d / h_.heads) - 1));
+  // memory plan: size, allocate, assign
+  const Counts c{n_local, N0, E0, N1, E1};
+  Plan P, S;
+  plan_memory(P, S, in_->a, h_, c, grad);
+  persist_.ensure(P.off);
+  scratch_.ensure(S.off);
+  P = Plan{persist_.as<char>(), 0};
+  S = Plan{scratch_.as<char>(), 0};
+  plan_memory(P, S, in_->a, h_, c, grad);
+  const Acts &a = in_->a;
+  EdgePrepArgs ep{};
+  ep.n_atoms = N0; ep.n_edges = E0;
+  ep.offset = nl_.offset.as<int>(); ep.center = nl_.center.as<int>(); ep.nbr = nl_.nbr.as<int>();
+  ep.shift = nl_.shift.as<int>(); ep.species = d_species;
+  ep.vec = nl_.vec.as<float>(); ep.dist_nl = nl_.dist.as<float>();
+  ep.cutoff = h_.cutoff; ep.width = h_.width;
+  ep.r = a.r; ep.fc = a.fc; ep.dfc_dr = a.dfc_dr; ep.key_mask = a.key_mask;
+  ep.edge_row = a.edge_row; ep.node_row = a.node_row; ep.nbr_species = a.nbr_species; ep.rev = a.rev;
+  edge_prep(ep, stream_);
+}
+
+void PETModel::predict_local(const double *d_pos, int n_local, const int32_t *numbers, int n_layer0, int n_owned,
+                             const float bbox[9], bool grad, float *d_forces, double *energy, double virial[6]) {
+  if (wptr_.empty()) throw Error(3, "Model weights not loaded");
+  if (n_owned < 0 || n_layer0 < n_owned || n_local < n_layer0)
+    throw Error(kErrInvalidParameter, "local system needs 0 <= n_owned <= n_layer0 <= n_local");
+  CUDA_CHECK(cudaSetDevice(device_));
+  cudaStream_t s = stream_;
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[0], s));
+  int *derr = static_cast<int *>(d_err_.ensure(sizeof(int) * 4));
+  CUDA_CHECK(cudaMemsetAsync(derr, 0, sizeof(int), s));
+  int *hsp = static_cast<int *>(h_species_.ensure(sizeof(int) * (n_local + 1)));
+  double comp = 0.0;
+  for (int i = 0; i < n_local; ++i) {
+    auto it = species_index_.find(numbers[i]);
+    if (it == species_index_.end())
+      throw Error(kErrComputation, "Unknown atomic number " + std::to_string(numbers[i]) +
+                                       " not found in species_to_index mapping");
+    hsp[i] = it->second;
+    if (i < n_owned) {
+      auto ct = composition_.find(numbers[i]);
+      if (ct != composition_.end()) comp += ct->second;
+    }
+  }
+  int *dsp = static_cast<int *>(d_species_.ensure(sizeof(int) * (n_local + 1)));
+  CUDA_CHECK(cudaMemcpyAsync(dsp, hsp, sizeof(int) * n_local, cudaMemcpyHostToDevice, s));
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[1], s));
+  // non-periodic grid over the bounding cell; only the first n_layer0 atoms
+  // are centres, every local atom is a candidate neighbour
+  GridParams g;
+  const bool open3[3] = {false, false, false};
+  make_grid_params(bbox, open3, h_.cutoff, &g);
+  build_local_nl(d_pos, n_local, n_layer0, g, nl_, nls_, s);
+  int e1 = 0;
+  CUDA_CHECK(cudaMemcpyAsync(&e1, nl_.offset.as<int>() + n_owned, sizeof(int), cudaMemcpyDeviceToHost, s));
+  CUDA_CHECK(cudaStreamSynchronize(s));
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[2], s));
+  setup_graph(n_local, n_layer0, nl_.n_edges, n_owned, e1, dsp, grad);
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[3], s));
+  forward_backward(grad);
+  const Acts &a = in_->a;
+  double *red = static_cast<double *>(d_red_.ensure(sizeof(double) * 16));
+  reduce_local(nl_.vec.as<float>(), a.g, a.e_atom, n_owned, grad ? El_[0] : 0, red, s);
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[6], s));
+  if (grad && d_forces)
+    CUDA_CHECK(cudaMemcpyAsync(d_forces, a.F, sizeof(float) * 3 * n_local, cudaMemcpyDeviceToDevice, s));
+  double *hout = static_cast<double *>(h_out_.ensure(sizeof(double) * 16));
+  int *herr = reinterpret_cast<int *>(hout + 8);
+  CUDA_CHECK(cudaMemcpyAsync(hout, red, sizeof(double) * 7, cudaMemcpyDeviceToHost, s));
+  CUDA_CHECK(cudaMemcpyAsync(herr, d_err_.ptr, sizeof(int), cudaMemcpyDeviceToHost, s));
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[7], s));
+  CUDA_CHECK(cudaStreamSynchronize(s));
+  if (kprof_) collect_marks();
+  if (*herr != 0)
+    throw Error(kErrComputation, "a tensor-core pipeline wait timed out (device error " +
+                                     std::to_string(*herr) + ")");
+  *energy = hout[0] + comp;
+  for (int c = 0; c < 6; ++c) virial[c] = grad ? hout[1 + c] : 0.0;
+  if (timing_) read_times(grad);
+}
+
+void PETModel::read_times(bool grad) {
+  float ms;
+  CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[0], ev_[1])); times_.h2d = ms;
+  CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[1], ev_[2])); times_.nl = ms;
+  CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[2], ev_[3])); times_.prep = ms;
+  CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[3], ev_[4])); times_.forward = ms;
+  times_.backward = 0.f;
+  if (grad) { CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[4], ev_[5])); times_.backward = ms; }
+  CUDA_CHECK(cudaEventElapsedTime(&ms, grad ? ev_[5] : ev_[4], ev_[6])); times_.reduce = ms;
+  CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[6], ev_[7])); times_.d2h = ms;
+  CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[0], ev_[7])); times_.total = ms;
+}
+
 void PETModel::run_group(const float *d_pos, int n_atoms, const std::vector<const SystemView *> &systems,
                          const std::vector<int> &atom_begin, bool grad, std::vector<Result *> &results,
                          bool copy_forces) {
   cudaStream_t s = stream_;
   const int n_sys = static_cast<int>(systems.size());
-  N_ = n_atoms;
   n_sys_ = n_sys;
   int *derr = static_cast<int *>(d_err_.ensure(sizeof(int) * 4));
   CUDA_CHECK(cudaMemsetAsync(derr, 0, sizeof(int), s));
@@ -549,34 +677,9 @@ void PETModel::run_group(const float *d_pos, int n_atoms, const std::vector<cons
     CUDA_CHECK(cudaMemcpyAsync(de, e.data(), sizeof(int) * n_atoms, cudaMemcpyHostToDevice, s));
     build_open_nl(d_pos, db, de, n_atoms, h_.cutoff, nl_, nls_, s);
   }
-  E_ = nl_.n_edges;
-  T_ = N_ + E_;
-  max_tok_ = nl_.max_count + 1;
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[2], s));
-  if (max_tok_ > attention_max_tokens(h_.d / h_.heads))
-    throw Error(kErrUnsupported, "an atom has " + std::to_string(nl_.max_count) +
-                                     " neighbours, above the supported maximum of " +
-                                     std::to_string(attention_max_tokens(h_.d / h_.heads) - 1));
-
-  // memory plan: size, allocate, assign
-  Plan P, S;
-  plan_memory(P, S, in_->a, h_, N_, E_, grad);
-  persist_.ensure(P.off);
-  scratch_.ensure(S.off);
-  P = Plan{persist_.as<char>(), 0};
-  S = Plan{scratch_.as<char>(), 0};
-  plan_memory(P, S, in_->a, h_, N_, E_, grad);
+  setup_graph(n_atoms, n_atoms, nl_.n_edges, n_atoms, nl_.n_edges, dsp, grad);
   const Acts &a = in_->a;
-
-  EdgePrepArgs ep{};
-  ep.n_atoms = N_; ep.n_edges = E_;
-  ep.offset = nl_.offset.as<int>(); ep.center = nl_.center.as<int>(); ep.nbr = nl_.nbr.as<int>();
-  ep.shift = nl_.shift.as<int>(); ep.species = dsp;
-  ep.vec = nl_.vec.as<float>(); ep.dist_nl = nl_.dist.as<float>();
-  ep.cutoff = h_.cutoff; ep.width = h_.width;
-  ep.r = a.r; ep.fc = a.fc; ep.dfc_dr = a.dfc_dr; ep.key_mask = a.key_mask;
-  ep.edge_row = a.edge_row; ep.node_row = a.node_row; ep.nbr_species = a.nbr_species; ep.rev = a.rev;
-  edge_prep(ep, s);
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[3], s));
 
   forward_backward(grad);
@@ -584,7 +687,7 @@ void PETModel::run_group(const float *d_pos, int n_atoms, const std::vector<cons
   // per-system energy and virial in f64 (pet.cpp:542-548, 1041-1077)
   double *red = static_cast<double *>(d_red_.ensure(sizeof(double) * 7 * (n_sys + 1)));
   reduce_systems(nl_.vec.as<float>(), a.g, a.e_atom, nl_.offset.as<int>(), dsb, n_sys, red + n_sys, red,
-                 grad && E_ > 0, s);
+                 grad && El_[0] > 0, s);
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[6], s));
   const size_t fbytes = (grad && copy_forces) ? sizeof(float) * 3 * n_atoms : 0;
   char *hout = static_cast<char *>(h_out_.ensure(sizeof(double) * 7 * n_sys + fbytes + 16));
@@ -633,17 +736,7 @@ void PETModel::run_group(const float *d_pos, int n_atoms, const std::vector<cons
       }
     }
   }
-  if (timing_) {
-    float ms;
-    CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[0], ev_[1])); times_.h2d = ms;
-    CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[1], ev_[2])); times_.nl = ms;
-    CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[2], ev_[3])); times_.prep = ms;
-    CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[3], ev_[4])); times_.forward = ms;
-    if (grad) { CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[4], ev_[5])); times_.backward = ms; }
-    CUDA_CHECK(cudaEventElapsedTime(&ms, grad ? ev_[5] : ev_[4], ev_[6])); times_.reduce = ms;
-    CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[6], ev_[7])); times_.d2h = ms;
-    CUDA_CHECK(cudaEventElapsedTime(&ms, ev_[0], ev_[7])); times_.total = ms;
-  }
+  if (timing_) read_times(grad);
 }
 
 std::vector<Result> PETModel::predict(const std::vector<SystemView> &systems, bool grad) {

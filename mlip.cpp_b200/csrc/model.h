@@ -67,6 +67,18 @@ class PETModel {
   // forces, and stress for periodic systems.
   std::vector<Result> predict(const std::vector<SystemView> &systems, bool compute_grad);
 
+  // One spatial domain of a larger cell: n_local atoms with f64 device
+  // positions (owned atoms first, then the ghost atoms within one cutoff of
+  // the owned region, then the remaining ghosts, periodic images already
+  // placed).  Layer 0 runs on the first n_layer0 atoms, layer 1 and the
+  // readout on the first n_owned.  Returns the owned atoms' energy (with
+  // composition), the gradient forces on all n_local atoms (device, may be
+  // null) and the virial sum_e e (x) dE/de over the local edges (not divided
+  // by a volume).  `bbox` is a cell enclosing the local positions, searched
+  // without periodicity.
+  void predict_local(const double *d_pos, int n_local, const int32_t *numbers, int n_layer0, int n_owned,
+                     const float bbox[9], bool grad, float *d_forces, double *energy, double virial[6]);
+
   // Device-resident entry for benchmarks: positions already on the device.
   void predict_device(const float *d_pos, const SystemView &sys, bool compute_grad, Result &out,
                       bool copy_forces);
@@ -77,8 +89,8 @@ class PETModel {
   void set_kernel_profiling(bool on) { kprof_ = on; }
   const KernelStat *kernel_stats() const { return kstats_; }
   void reset_kernel_stats() { for (auto &k : kstats_) k = KernelStat{}; }
-  int last_atoms() const { return N_; }
-  int last_edges() const { return E_; }
+  int last_atoms() const { return n_local_; }
+  int last_edges() const { return El_[0]; }
   int last_max_neighbors() const { return max_tok_ - 1; }
   void set_timing(bool on) { timing_ = on; }
   cudaStream_t stream() const { return stream_; }
@@ -90,6 +102,8 @@ class PETModel {
                  const std::vector<int> &atom_begin, bool compute_grad,
                  std::vector<Result *> &results, bool copy_forces);
   void forward_backward(bool compute_grad);
+  void setup_graph(int n_local, int N0, int E0, int N1, int E1, const int *d_species, bool grad);
+  void read_times(bool grad);
   const float *w(const std::string &name) const;
 
   struct Internals;  // device pointers of weights and activations (model.cu)
@@ -112,7 +126,7 @@ class PETModel {
   DevBuf persist_, scratch_;
   DevBuf d_red_;  // per-system energy (f64) + virial (f64 x 6)
   HostBuf h_pos_, h_species_, h_out_;
-  int N_ = 0, E_ = 0, T_ = 0, max_tok_ = 0, n_sys_ = 0;
+  int n_local_ = 0, Nl_[2] = {0, 0}, El_[2] = {0, 0}, Tl_[2] = {0, 0}, max_tok_ = 0, n_sys_ = 0;
   bool timing_ = false;
   bool kprof_ = false;
   KernelStat kstats_[KC_COUNT];

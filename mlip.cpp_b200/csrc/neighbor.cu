@@ -112,7 +112,8 @@ __device__ __forceinline__ void rel_pos(const GridParams &g, double x, double y,
   }
 }
 
-__global__ void k_bin_atoms(const float *__restrict__ pos, int n, GridParams g,
+template <typename P>
+__global__ void k_bin_atoms(const P *__restrict__ pos, int n, GridParams g,
                             int *__restrict__ braw, int *__restrict__ bin_of,
                             int *__restrict__ bin_count) {
   int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -159,9 +160,9 @@ constexpr int kNLWarps = 4;  // warps (centres) per CTA
 
 // Periodic search (build_periodic, neighbor_list.cpp:163-297).
 // kFill = false: count edges per centre; true: write them at offset[i].
-template <bool kFill>
+template <bool kFill, typename P>
 __global__ void __launch_bounds__(32 * kNLWarps)
-k_periodic(const float *__restrict__ pos, int n, GridParams g, const int *__restrict__ braw,
+k_periodic(const P *__restrict__ pos, int n, GridParams g, const int *__restrict__ braw,
            const int *__restrict__ bin_start, const int *__restrict__ bin_atoms,
            int *__restrict__ count, const int *__restrict__ offset, int *__restrict__ e_center,
            int *__restrict__ e_nbr, int *__restrict__ e_shift, float *__restrict__ e_vec,
@@ -398,9 +399,10 @@ void size_edges(EdgeList &out, int n, cudaStream_t stream) {
 }
 }  // namespace
 
-void build_periodic_nl(const float *pos, int n, const GridParams &g, EdgeList &out, NLScratch &s,
-                       cudaStream_t stream) {
-  out.n_atoms = n;
+template <typename P>
+void build_grid_nl(const P *pos, int n, int n_centers, const GridParams &g, EdgeList &out, NLScratch &s,
+                   cudaStream_t stream) {
+  out.n_atoms = n_centers;
   const int nbins = g.nb[0] * g.nb[1] * g.nb[2];
   int *braw = static_cast<int *>(s.braw.ensure(sizeof(int) * 3 * (n + 1)));
   int *bin_of = static_cast<int *>(s.bin_of.ensure(sizeof(int) * (n + 1)));
@@ -408,12 +410,12 @@ void build_periodic_nl(const float *pos, int n, const GridParams &g, EdgeList &o
   int *bin_start = static_cast<int *>(s.bin_start.ensure(sizeof(int) * (nbins + 2)));
   int *cursor = static_cast<int *>(s.bin_cursor.ensure(sizeof(int) * (nbins + 1)));
   int *bin_atoms = static_cast<int *>(s.bin_atoms.ensure(sizeof(int) * (n + 1)));
-  int *count = static_cast<int *>(out.count.ensure(sizeof(int) * (n + 1)));
-  int *offset = static_cast<int *>(out.offset.ensure(sizeof(int) * (n + 2)));
+  int *count = static_cast<int *>(out.count.ensure(sizeof(int) * (n_centers + 1)));
+  int *offset = static_cast<int *>(out.offset.ensure(sizeof(int) * (n_centers + 2)));
   CUDA_CHECK(cudaMemsetAsync(bin_count, 0, sizeof(int) * nbins, stream));
   CUDA_CHECK(cudaMemsetAsync(cursor, 0, sizeof(int) * nbins, stream));
   if (n > 0) {
-    k_bin_atoms<<<ceil_div(n, 256), 256, 0, stream>>>(pos, n, g, braw, bin_of, bin_count);
+    k_bin_atoms<P><<<ceil_div(n, 256), 256, 0, stream>>>(pos, n, g, braw, bin_of, bin_count);
     CUDA_LAUNCH_CHECK();
   }
   scan_counts(bin_count, bin_start, nullptr, nbins, stream);
@@ -422,19 +424,31 @@ void build_periodic_nl(const float *pos, int n, const GridParams &g, EdgeList &o
     CUDA_LAUNCH_CHECK();
     k_sort_bins<<<ceil_div(nbins, 128), 128, 0, stream>>>(bin_start, nbins, bin_atoms);
     CUDA_LAUNCH_CHECK();
-    k_periodic<false><<<ceil_div(n, kNLWarps), 32 * kNLWarps, 0, stream>>>(
-        pos, n, g, braw, bin_start, bin_atoms, count, nullptr, nullptr, nullptr, nullptr, nullptr,
+  }
+  if (n_centers > 0) {
+    k_periodic<false, P><<<ceil_div(n_centers, kNLWarps), 32 * kNLWarps, 0, stream>>>(
+        pos, n_centers, g, braw, bin_start, bin_atoms, count, nullptr, nullptr, nullptr, nullptr, nullptr,
         nullptr);
     CUDA_LAUNCH_CHECK();
   }
-  scan_counts(count, offset, offset + n + 1, n, stream);
-  size_edges(out, n, stream);
-  if (n > 0 && out.n_edges > 0) {
-    k_periodic<true><<<ceil_div(n, kNLWarps), 32 * kNLWarps, 0, stream>>>(
-        pos, n, g, braw, bin_start, bin_atoms, nullptr, offset, out.center.as<int>(),
+  scan_counts(count, offset, offset + n_centers + 1, n_centers, stream);
+  size_edges(out, n_centers, stream);
+  if (n_centers > 0 && out.n_edges > 0) {
+    k_periodic<true, P><<<ceil_div(n_centers, kNLWarps), 32 * kNLWarps, 0, stream>>>(
+        pos, n_centers, g, braw, bin_start, bin_atoms, nullptr, offset, out.center.as<int>(),
         out.nbr.as<int>(), out.shift.as<int>(), out.vec.as<float>(), out.dist.as<float>());
     CUDA_LAUNCH_CHECK();
   }
+}
+
+void build_periodic_nl(const float *pos, int n, const GridParams &g, EdgeList &out, NLScratch &s,
+                       cudaStream_t stream) {
+  build_grid_nl<float>(pos, n, n, g, out, s, stream);
+}
+
+void build_local_nl(const double *pos, int n, int n_centers, const GridParams &g, EdgeList &out,
+                    NLScratch &s, cudaStream_t stream) {
+  build_grid_nl<double>(pos, n, n_centers, g, out, s, stream);
 }
 
 void build_open_nl(const float *pos, const int *sys_begin, const int *sys_end, int n, float cutoff,

@@ -44,6 +44,13 @@ struct NLScratch {
 void build_periodic_nl(const float *pos, int n, const GridParams &g, EdgeList &out,
                        NLScratch &s, cudaStream_t stream);
 
+// Local system of a spatial domain: n atoms with f64 positions (owned
+// atoms, then ghost shells, images already placed), pairs found with the
+// grid search of a non-periodic bounding cell (g.pbc all 0), only for the
+// first n_centers atoms (all n atoms are candidate neighbours).
+void build_local_nl(const double *pos, int n, int n_centers, const GridParams &g, EdgeList &out,
+                    NLScratch &s, cudaStream_t stream);
+
 // Open-boundary O(n^2) search, batched: atom a belongs to the system whose
 // atoms are [sys_begin[a], sys_end[a]).  `cutoff_sq_f32` is the f32 product
 // cutoff*cutoff the reference compares against (neighbor_list.cpp:131).

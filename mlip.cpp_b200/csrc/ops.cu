@@ -55,7 +55,8 @@ __global__ void k_edge_prep(EdgePrepArgs a) {
     // inserted under a key, so the last match wins (pet_batch.cpp:416-436)
     const int s0 = a.shift[3 * e], s1 = a.shift[3 * e + 1], s2 = a.shift[3 * e + 2];
     int rv = -1;
-    for (int k = a.offset[j], ke = a.offset[j + 1]; k < ke; ++k) {
+    const int kb = j < a.n_atoms ? a.offset[j] : 0, kend = j < a.n_atoms ? a.offset[j + 1] : 0;
+    for (int k = kb, ke = kend; k < ke; ++k) {
       if (a.nbr[k] == i && a.shift[3 * k] == -s0 && a.shift[3 * k + 1] == -s1 &&
           a.shift[3 * k + 2] == -s2)
         rv = k;
@@ -174,13 +175,14 @@ __global__ void k_edge_embed_bwd(const float *__restrict__ demb, int ld, const f
 }
 
 __global__ void k_message_bwd(const float *__restrict__ dmsg, int ld, const int *__restrict__ rev,
-                              const int *__restrict__ edge_row, float *__restrict__ dx, int n_edges, int d) {
+                              const int *__restrict__ edge_row, float *__restrict__ dx, int n_edges,
+                              int n_msg, int d) {
   const int64_t total = static_cast<int64_t>(n_edges) * d;
   for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
        t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int x = static_cast<int>(t / d), c = static_cast<int>(t % d);
     const int rv = rev[x];
-    if (rv >= 0) dx[static_cast<size_t>(edge_row[x]) * d + c] += 0.5f * dmsg[static_cast<size_t>(rv) * ld + c];
+    if (rv >= 0 && rv < n_msg) dx[static_cast<size_t>(edge_row[x]) * d + c] += 0.5f * dmsg[static_cast<size_t>(rv) * ld + c];
   }
 }
 
@@ -275,7 +277,34 @@ __global__ void __launch_bounds__(512) k_reduce_systems(
   }
 }
 
+__global__ void __launch_bounds__(1024) k_reduce_local(const float *__restrict__ vec, const float *__restrict__ g,
+                                                     const float *__restrict__ e_atom, int n_energy, int n_edges,
+                                                     double *__restrict__ out) {
+  __shared__ double sm[32 * 7];
+  double v[7] = {0, 0, 0, 0, 0, 0, 0};
+  for (int i = threadIdx.x; i < n_energy; i += blockDim.x) v[0] += static_cast<double>(e_atom[i]);
+  for (int e = threadIdx.x; e < n_edges; e += blockDim.x) {
+    const double ex = vec[3 * e], ey = vec[3 * e + 1], ez = vec[3 * e + 2];
+    const double gx = g[3 * e], gy = g[3 * e + 1], gz = g[3 * e + 2];
+    v[1] += ex * gx;
+    v[2] += ey * gy;
+    v[3] += ez * gz;
+    v[4] += 0.5 * (ey * gz + ez * gy);
+    v[5] += 0.5 * (ex * gz + ez * gx);
+    v[6] += 0.5 * (ex * gy + ey * gx);
+  }
+  block_sum<7>(v, sm);
+  if (threadIdx.x == 0)
+    for (int c = 0; c < 7; ++c) out[c] = v[c];
+}
+
 }  // namespace
+
+void reduce_local(const float *vec, const float *g, const float *e_atom, int n_energy, int n_edges,
+                  double *out, cudaStream_t s) {
+  k_reduce_local<<<1, 1024, 0, s>>>(vec, g, e_atom, n_energy, n_edges, out);
+  CUDA_LAUNCH_CHECK();
+}
 
 void edge_prep(const EdgePrepArgs &a, cudaStream_t s) {
   const int total = a.n_edges > a.n_atoms ? a.n_edges : a.n_atoms;
@@ -335,10 +364,10 @@ void edge_embed_bwd(const float *demb, int ld, const float *We, float *g4, int n
 }
 
 void message_bwd(const float *dmsg, int ld, const int *rev, const int *edge_row, float *dx,
-                 int n_edges, int d, cudaStream_t s) {
+                 int n_edges, int n_msg, int d, cudaStream_t s) {
   if (n_edges <= 0) return;
   k_message_bwd<<<grid_for(static_cast<int64_t>(n_edges) * d, 256), 256, 0, s>>>(dmsg, ld, rev, edge_row, dx,
-                                                                                 n_edges, d);
+                                                                                 n_edges, n_msg, d);
   CUDA_LAUNCH_CHECK();
 }
 

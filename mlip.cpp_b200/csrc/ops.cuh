@@ -52,9 +52,9 @@ void add_vec(const float *x, float *y, int n, bool accumulate, cudaStream_t s);
 // g4[e, 0:3] (+)= W_e[:, 0:3]^T demb[e],  g4[e, 3] (+)= W_e[:, 3]^T demb[e]
 void edge_embed_bwd(const float *demb, int ld, const float *We, float *g4, int n_edges, int d,
                     bool accumulate, cudaStream_t s);
-// dX[edge_row[x], :] += 0.5 dmsg[rev[x], :]   for rev[x] >= 0
+// dX[edge_row[x], :] += 0.5 dmsg[rev[x], :]   for 0 <= rev[x] < n_msg
 void message_bwd(const float *dmsg, int ld, const int *rev, const int *edge_row, float *dx,
-                 int n_edges, int d, cudaStream_t s);
+                 int n_edges, int n_msg, int d, cudaStream_t s);
 // g[e] = g4[e, 0:3] + (g4[e, 3] + gfc[e] dfc_dr[e]) vec[e] / r[e]
 void edge_grad(const float *g4, const float *gfc, const float *dfc_dr, const float *vec,
                const float *r, float *g, int n_edges, cudaStream_t s);
@@ -66,5 +66,10 @@ void forces(const float *g, const int *offset, const int *nbr, const int *rev, f
 void reduce_systems(const float *vec, const float *g, const float *e_atom, const int *offset,
                     const int *sys_atom_begin, int n_sys, double *virial, double *energy,
                     bool with_virial, cudaStream_t s);
+
+// out[0] = sum of e_atom[0..n_energy), out[1..6] = Voigt sum over edges
+// [0, n_edges) of sym(vec (x) g) (f64, one CTA).
+void reduce_local(const float *vec, const float *g, const float *e_atom, int n_energy, int n_edges,
+                  double *out, cudaStream_t s);
 
 }  // namespace pet
