@@ -10,9 +10,14 @@ GNN layers, readout and the full backward pass.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Multi-GPU (launched with torch.distributed.run): every rank evaluates its own
-replica of the cell with no data-path collective (weak scaling); the timed
-region is bracketed by barriers and the reported time is the max over ranks.
+Multi-GPU (launched with torch.distributed.run), weak scaling at 32,768 atoms
+per GPU: N ranks evaluate one cell of N x 32,768 atoms (32x32x64 primitive
+cells for 2 GPUs, 32x64x64 for 4, 64^3 = 262,144 for 8) split into N spatial
+domains (owned atoms plus two ghost shells of one cutoff each); the only
+exchange is an NCCL all-reduce of the forces and of (energy, virial) per
+step.  `--parallel replicas` instead runs an independent copy of the 32k cell
+per rank.  The timed region is bracketed by barriers and the reported time is
+the max over ranks.
 
 `--impl reference` times the CPU implementation of the path on the host
 cores: the reference's model cannot be built here (its ggml dependency is
@@ -129,6 +134,8 @@ def main():
     ap.add_argument("--reps", type=int, default=32, help="primitive fcc cells per axis")
     ap.add_argument("--cpu-reps", type=int, default=6, help="CPU-baseline sample cells per axis")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--parallel", default="domains", choices=["domains", "replicas"],
+                    help="multi-GPU mode: one cell split into spatial domains, or a replica per rank")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -137,7 +144,7 @@ def main():
     mb = _package()
     from mlipcpp_b200 import workloads as wl
     h = wl.HYPERS[args.hypers]
-    workload = (f"fcc alloy {args.reps}^3 primitive cells ({args.reps ** 3} atoms, triclinic, a=3.6, "
+    workload = (f"fcc alloy {args.reps}^3 primitive cells ({args.reps ** 3} atoms per GPU, triclinic, a=3.6, "
                 f"20 elements, jitter 0.08), {args.hypers}-shaped random-init weights "
                 f"(d={h.d_pet}, heads={h.num_heads}, ff={h.d_feedforward}, d_head={h.d_head}, "
                 f"rc={h.cutoff}), E+F+stress")
@@ -174,21 +181,46 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
 
-    s = wl.fcc_alloy(args.reps, seed=0)
+    domains = world > 1 and args.parallel == "domains"
+    reps = (args.reps,) * 3
+    if domains:
+        # N x 32k atoms: double the cell along z, then y, then x
+        r = list(reps)
+        k, w = 2, world
+        while w > 1:
+            r[k] *= 2
+            w //= 2
+            k = (k - 1) % 3
+        reps = tuple(r)
+    s = wl.fcc_alloy(reps, seed=0)
     pred = mb.Predictor(gguf)
     pred.set_timing(True)
     d_pos = torch.from_numpy(s.positions).cuda()
     torch.cuda.synchronize()
-
-    def step_device():
-        return pred.predict_device(d_pos.data_ptr(), s.n_atoms, s.numbers, s.cell, s.pbc,
-                                   compute_forces=True, compute_stress=True, copy_forces=False)
 
     def barrier():
         torch.cuda.synchronize()
         if dist:
             dist.barrier()
         torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if dist:
+            t = torch.tensor([x], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            x = float(t.item())
+        return x
+
+    from mlipcpp_b200 import domain as dd
+    if domains:
+        runner = dd.DomainRunner(dd.predictor_eval(pred), s.numbers, s.cell, h.cutoff, world=world, rank=rank)
+
+        def step_device():
+            return runner.step(d_pos)
+    else:
+        def step_device():
+            return pred.predict_device(d_pos.data_ptr(), s.n_atoms, s.numbers, s.cell, s.pbc,
+                                       compute_forces=True, compute_stress=True, copy_forces=False)
 
     for _ in range(max(args.warmup, 3)):
         step_device()
@@ -197,35 +229,48 @@ def main():
     launches0 = mb.kernel_launches()
     barrier()
     with ClockSampler(local) as clk:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         dev_ms = []
+        ev0.record()
         for _ in range(args.steps):
             step_device()
-            dev_ms.append(pred.last_timings()["total"])
+            if not domains:
+                dev_ms.append(pred.last_timings()["total"])
+        ev1.record()
         barrier()
     launches = mb.kernel_launches() - launches0
     kstats = pred.kernel_stats()
     pred.set_kernel_profiling(False)
-    t_dev = float(np.sum(dev_ms)) / 1e3
-    if dist:
-        t = torch.tensor([t_dev], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_dev = float(t.item())
-    value = world * s.n_atoms * args.steps / t_dev
+    # single cell: the library's own events on its stream; domains: torch
+    # events around whole steps (the library synchronises its stream before
+    # returning, so they span its work, the partition and the all-reduces)
+    t_dev = float(np.sum(dev_ms)) / 1e3 if not domains else ev0.elapsed_time(ev1) / 1e3
+    t_dev = max_over_ranks(t_dev)
+    n_job = s.n_atoms if domains else world * s.n_atoms
+    value = n_job * args.steps / t_dev
 
     # ---- end-to-end through the public API with host buffers --------------
     pos_host = torch.from_numpy(s.positions).pin_memory()
-    e2e_ms = []
     barrier()
-    for _ in range(args.steps):
-        r = pred.predict(pos_host.numpy(), s.numbers, s.cell, s.pbc, compute_stress=True)
-        e2e_ms.append(pred.last_timings()["total"])
-    barrier()
-    t_e2e = float(np.sum(e2e_ms)) / 1e3
-    if dist:
-        t = torch.tensor([t_e2e], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_e2e = float(t.item())
-    e2e = world * s.n_atoms * args.steps / t_e2e
+    if domains:
+        ev0.record()
+        for _ in range(args.steps):
+            e, F, vir = runner.step(pos_host.to("cuda", non_blocking=True))
+            F_host = F.cpu()
+        ev1.record()
+        barrier()
+        t_e2e = ev0.elapsed_time(ev1) / 1e3
+        d2h = int(F_host.numel() * 4 + 8 * 7)
+    else:
+        e2e_ms = []
+        for _ in range(args.steps):
+            r = pred.predict(pos_host.numpy(), s.numbers, s.cell, s.pbc, compute_stress=True)
+            e2e_ms.append(pred.last_timings()["total"])
+        barrier()
+        t_e2e = float(np.sum(e2e_ms)) / 1e3
+        d2h = int(r.forces.nbytes + r.stress.nbytes + 4)
+    t_e2e = max_over_ranks(t_e2e)
+    e2e = n_job * args.steps / t_e2e
 
     if rank == 0:
         hbm, bf16, bf16_sus, src = _peaks()
@@ -240,12 +285,15 @@ def main():
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": t_dev / args.steps * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
-            "config": {"workload": workload, "atoms_per_gpu": s.n_atoms, "edges": shape["edges"],
-                       "max_neighbors": shape["max_neighbors"], "parallelism": f"replicas x{world}",
+            "config": {"workload": workload, "atoms_per_gpu": n_job // world, "atoms_total": n_job,
+                       "edges_rank0": shape["edges"], "max_neighbors": shape["max_neighbors"],
+                       "parallelism": (f"spatial domains {'x'.join(map(str, dd.grid_for(world)))} "
+                                       "(owned + 2 ghost shells), NCCL all-reduce of F and (E, virial)"
+                                       if domains else f"replicas x{world}"),
                        "l2": "inputs larger than L2 (multi-GB working set per step)"},
             "e2e": {"value": e2e, "unit": "atom-steps/s",
-                    "h2d_bytes_per_step": int(s.positions.nbytes + s.numbers.nbytes),
-                    "d2h_bytes_per_step": int(r.forces.nbytes + r.stress.nbytes + 4)},
+                    "h2d_bytes_per_step": int(s.positions.nbytes + (0 if domains else s.numbers.nbytes)),
+                    "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches),
             "roofline": {"bound": "tensor", "kernel": "k_gemm_3xtf32 (tcgen05, all dense layers)",
                          "achieved": achieved, "peak": bf16_sus / 6.0, "unit": "TFLOP/s",
@@ -256,7 +304,7 @@ def main():
                          # dram__bytes_write.sum over all 57 GEMM launches of one step of the
                          # 1,728-atom cell of this alloy (354 MB/launch at 65,202 tokens,
                          # 5,429 B per token), scaled by this step's token count
-                         "traffic": 5429.0 * (shape["atoms"] + shape["edges"]) if world == 1 else None,
+                         "traffic": 5429.0 * (shape["atoms"] + shape["edges"]) if not domains else None,
                          "traffic_unit": "bytes per GEMM launch (scaled from the 1,728-atom capture)",
                          "gemm_share_of_step": (g["ms"] + gs["ms"]) / (t_dev * 1e3) if t_dev else None},
             "kernel_stats": kstats,

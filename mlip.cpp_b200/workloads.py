@@ -215,18 +215,20 @@ def si_diamond(reps: int = 3, a: float = 5.431, jitter: float = 0.05, seed: int 
                      cell.astype(np.float32), (True, True, True))
 
 
-def fcc_alloy(reps: int = 32, a: float = 3.6, n_elements: int = 20, jitter: float = 0.08,
+def fcc_alloy(reps=32, a: float = 3.6, n_elements: int = 20, jitter: float = 0.08,
               seed: int = 0) -> Structure:
-    """reps^3 primitive fcc cells (one atom each; a triclinic supercell),
-    species drawn uniformly from `n_elements` random elements among Z=1..89."""
+    """reps^3 (or reps = (nx, ny, nz)) primitive fcc cells (one atom each; a
+    triclinic supercell), species drawn uniformly from `n_elements` random
+    elements among Z=1..89."""
+    r = (reps,) * 3 if np.isscalar(reps) else tuple(int(x) for x in reps)
     prim = 0.5 * a * np.array([[0, 1, 1], [1, 0, 1], [1, 1, 0]], dtype=np.float64)
-    g = np.stack(np.meshgrid(*(np.arange(reps),) * 3, indexing="ij"), -1).reshape(-1, 3)
+    g = np.stack(np.meshgrid(*(np.arange(k) for k in r), indexing="ij"), -1).reshape(-1, 3)
     pos = g @ prim
     rng = np.random.default_rng(seed)
     pos = pos + rng.normal(0.0, jitter, pos.shape)
     elements = rng.choice(np.arange(1, 90), size=n_elements, replace=False)
     z = rng.choice(elements, size=len(pos)).astype(np.int32)
-    return Structure(pos.astype(np.float32), z, (prim * reps).astype(np.float32),
+    return Structure(pos.astype(np.float32), z, (prim * np.array(r)[:, None]).astype(np.float32),
                      (True, True, True))
 
 
