@@ -78,6 +78,31 @@ int64_t mlipcpp_b200_neighbor_list(int32_t n_atoms, const float *positions, cons
                                    int32_t *neighbors, int32_t *shifts, float *vectors,
                                    float *distances);
 
+/* No counterpart in the reference.  The periodic (or partially periodic)
+ * neighbour list of mlipcpp_b200_neighbor_list, same pairs in the same
+ * order, for callers that cannot let a library allocate GPU memory: an MD
+ * engine or host framework that hands out every device buffer from its own
+ * pool, and code running where a cudaMalloc would stall other streams or is
+ * not permitted.  It allocates nothing.  `d_positions` ([3 n_atoms] float)
+ * and the five pair arrays are the caller's device buffers on the calling
+ * thread's current device; `cell` and `pbc` are host arrays as in
+ * mlipcpp_b200_neighbor_list (cell is required).  The working memory is a
+ * fixed static device array of 2.6 MB inside this library, which limits a
+ * call to at most 65536 atoms and 65536 cutoff-sized bins; larger requests
+ * return -MLIPCPP_ERROR_INVALID_PARAMETER with a message naming the limit,
+ * before any device work.  The first call on each device looks up that
+ * array's address (cudaGetSymbolAddress), so make it before any stream
+ * capture.  All calls on one device share the array: calls that overlap in
+ * time (from several host threads) race, so serialise them.
+ * Work runs on `stream` (NULL: the legacy default stream); the call returns
+ * after that work has finished.  Returns the total pair count; the arrays
+ * are written only when it is at most `cap` (else call again with larger
+ * arrays), or -(error code) on failure. */
+int64_t mlipcpp_b200_neighbor_list_noalloc(int32_t n_atoms, const float *d_positions, const float *cell,
+                                           const bool *pbc, float cutoff, int64_t cap, int32_t *d_centers,
+                                           int32_t *d_neighbors, int32_t *d_shifts, float *d_vectors,
+                                           float *d_distances, void *stream);
+
 /* Number of CUDA kernels this library has launched in this process. */
 int64_t mlipcpp_b200_kernel_launches(void);
 

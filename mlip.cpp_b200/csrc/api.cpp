@@ -653,6 +653,54 @@ int64_t mlipcpp_b200_neighbor_list(int32_t n_atoms, const float *positions, cons
   }
 }
 
+int64_t mlipcpp_b200_neighbor_list_noalloc(int32_t n_atoms, const float *d_positions, const float *cell,
+                                           const bool *pbc, float cutoff, int64_t cap, int32_t *d_centers,
+                                           int32_t *d_neighbors, int32_t *d_shifts, float *d_vectors,
+                                           float *d_distances, void *stream) {
+  if (n_atoms < 0 || cap < 0) {
+    set_error("Invalid number of atoms or pair capacity");
+    return -MLIPCPP_ERROR_INVALID_PARAMETER;
+  }
+  if (!cell) {
+    set_error("The no-allocation neighbour list needs a cell (open boundaries: mlipcpp_b200_neighbor_list)");
+    return -MLIPCPP_ERROR_INVALID_PARAMETER;
+  }
+  bool p[3] = {true, true, true};
+  if (pbc) { p[0] = pbc[0]; p[1] = pbc[1]; p[2] = pbc[2]; }
+  pet::GridParams g;
+  pet::make_grid_params(cell, p, cutoff, &g);
+  // size limits before any device work, so an oversized call touches nothing
+  const int64_t nbins = static_cast<int64_t>(g.nb[0]) * g.nb[1] * g.nb[2];
+  if (n_atoms > pet::kNoAllocMaxAtoms || nbins > pet::kNoAllocMaxBins) {
+    set_error("The no-allocation neighbour list takes at most " + std::to_string(pet::kNoAllocMaxAtoms) +
+              " atoms and " + std::to_string(pet::kNoAllocMaxBins) + " cutoff-sized bins (got " +
+              std::to_string(n_atoms) + " atoms, " + std::to_string(nbins) + " bins)");
+    return -MLIPCPP_ERROR_INVALID_PARAMETER;
+  }
+  if ((n_atoms > 0 && !d_positions) ||
+      (cap > 0 && (!d_centers || !d_neighbors || !d_shifts || !d_vectors || !d_distances))) {
+    set_error("NULL device pointer");
+    return -MLIPCPP_ERROR_NULL_POINTER;
+  }
+  if (!have_cuda_device()) {
+    set_error("No CUDA device available (this backend has no CPU fallback)");
+    return -MLIPCPP_ERROR_BACKEND;
+  }
+  try {
+    const int64_t m = pet::build_periodic_nl_noalloc(d_positions, n_atoms, g, cap, d_centers, d_neighbors,
+                                                     d_shifts, d_vectors, d_distances,
+                                                     static_cast<cudaStream_t>(stream));
+    clear_error();
+    return m;
+  } catch (const pet::Error &e) {
+    set_error(std::string("Neighbour list failed: ") + e.what());
+    return -static_cast<int64_t>(e.code);
+  } catch (const std::exception &e) {
+    set_error(std::string("Neighbour list failed: ") + e.what());
+    return -MLIPCPP_ERROR_COMPUTATION;
+  }
+}
+
 int64_t mlipcpp_b200_kernel_launches(void) { return pet::g_kernel_launches.load(); }
 
 mlipcpp_error_t mlipcpp_b200_set_device(int32_t device) {

@@ -17,6 +17,7 @@
 #include "neighbor.cuh"
 
 #include <cmath>
+#include <mutex>
 
 namespace pet {
 
@@ -472,6 +473,100 @@ void build_open_nl(const float *pos, const int *sys_begin, const int *sys_end, i
         out.shift.as<int>(), out.vec.as<float>(), out.dist.as<float>());
     CUDA_LAUNCH_CHECK();
   }
+}
+
+// ---------------------------------------------------------------------------
+// Search without allocation (build_periodic_nl_noalloc)
+// ---------------------------------------------------------------------------
+// Working memory: one static array per device, as ints
+//   braw [3 (A+1)] | bin_of [A+1] | bin_atoms [A+1] | count [A+1] |
+//   offset [A+2] | bin_count [B+1] | bin_start [B+2] | cursor [B+1]
+// with A = kNoAllocMaxAtoms, B = kNoAllocMaxBins.  bin_count and cursor must
+// start at zero and are cleared by every call; every other part is fully
+// written before it is read.
+namespace {
+constexpr size_t kNAAtomSlot = static_cast<size_t>(kNoAllocMaxAtoms) + 1;
+constexpr size_t kNABinSlot = static_cast<size_t>(kNoAllocMaxBins) + 1;
+constexpr size_t kNAOffBinOf = 3 * kNAAtomSlot;
+constexpr size_t kNAOffBinAtoms = kNAOffBinOf + kNAAtomSlot;
+constexpr size_t kNAOffCount = kNAOffBinAtoms + kNAAtomSlot;
+constexpr size_t kNAOffOffset = kNAOffCount + kNAAtomSlot;
+constexpr size_t kNAOffBinCount = kNAOffOffset + kNAAtomSlot + 1;
+constexpr size_t kNAOffBinStart = kNAOffBinCount + kNABinSlot;
+constexpr size_t kNAOffCursor = kNAOffBinStart + kNABinSlot + 1;
+constexpr size_t kNAInts = kNAOffCursor + kNABinSlot;
+static_assert(kNAInts == 7 * kNAAtomSlot + 3 * kNABinSlot + 2, "scratch layout");
+__device__ __align__(256) int g_nl_noalloc_scratch[kNAInts];
+
+constexpr int kNAMaxDevices = 64;
+std::mutex g_nl_noalloc_mu;
+int *g_nl_noalloc_ptr[kNAMaxDevices] = {};
+
+// Device address of g_nl_noalloc_scratch on the current device.  The first
+// call on a device looks it up (cudaGetSymbolAddress, with that device
+// current) and keeps it; later calls only read the table.
+int *noalloc_scratch() {
+  int dev = 0;
+  CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNAMaxDevices) throw Error(kErrUnsupported, "device ordinal above 63");
+  std::lock_guard<std::mutex> lock(g_nl_noalloc_mu);
+  if (!g_nl_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    const cudaError_t rc = cudaGetSymbolAddress(&p, g_nl_noalloc_scratch);
+    if (rc != cudaSuccess || !p)
+      throw Error(kErrBackend, std::string("cudaGetSymbolAddress of the neighbour-list scratch failed: ") +
+                                   cudaGetErrorString(rc));
+    g_nl_noalloc_ptr[dev] = static_cast<int *>(p);
+  }
+  return g_nl_noalloc_ptr[dev];
+}
+}  // namespace
+
+int64_t build_periodic_nl_noalloc(const float *pos, int n, const GridParams &g, int64_t cap,
+                                  int *e_center, int *e_nbr, int *e_shift, float *e_vec, float *e_dist,
+                                  cudaStream_t stream) {
+  const int64_t nbins = static_cast<int64_t>(g.nb[0]) * g.nb[1] * g.nb[2];
+  if (n < 0 || n > kNoAllocMaxAtoms)
+    throw Error(kErrInvalidParameter, "the no-allocation neighbour list takes at most " +
+                                          std::to_string(kNoAllocMaxAtoms) + " atoms (got " +
+                                          std::to_string(n) + ")");
+  if (nbins > kNoAllocMaxBins)
+    throw Error(kErrInvalidParameter, "the no-allocation neighbour list takes at most " +
+                                          std::to_string(kNoAllocMaxBins) + " cutoff-sized bins (this cell needs " +
+                                          std::to_string(nbins) + ")");
+  if (n == 0) return 0;
+  int *braw = noalloc_scratch();
+  int *bin_of = braw + kNAOffBinOf;
+  int *bin_atoms = braw + kNAOffBinAtoms;
+  int *count = braw + kNAOffCount;
+  int *offset = braw + kNAOffOffset;        // A + 2 entries
+  int *bin_count = braw + kNAOffBinCount;
+  int *bin_start = braw + kNAOffBinStart;   // B + 2 entries
+  int *cursor = braw + kNAOffCursor;
+  const int nb = static_cast<int>(nbins);
+  CUDA_CHECK(cudaMemsetAsync(bin_count, 0, sizeof(int) * nb, stream));
+  CUDA_CHECK(cudaMemsetAsync(cursor, 0, sizeof(int) * nb, stream));
+  k_bin_atoms<float><<<ceil_div(n, 256), 256, 0, stream>>>(pos, n, g, braw, bin_of, bin_count);
+  CUDA_LAUNCH_CHECK();
+  scan_counts(bin_count, bin_start, nullptr, nb, stream);
+  k_fill_bins<<<ceil_div(n, 256), 256, 0, stream>>>(bin_of, n, bin_start, cursor, bin_atoms);
+  CUDA_LAUNCH_CHECK();
+  k_sort_bins<<<ceil_div(nb, 128), 128, 0, stream>>>(bin_start, nb, bin_atoms);
+  CUDA_LAUNCH_CHECK();
+  k_periodic<false, float><<<ceil_div(n, kNLWarps), 32 * kNLWarps, 0, stream>>>(
+      pos, n, g, braw, bin_start, bin_atoms, count, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr);
+  CUDA_LAUNCH_CHECK();
+  scan_counts(count, offset, offset + n + 1, n, stream);
+  int total = 0;
+  CUDA_CHECK(cudaMemcpyAsync(&total, offset + n, sizeof(int), cudaMemcpyDeviceToHost, stream));
+  CUDA_CHECK(cudaStreamSynchronize(stream));
+  if (total > 0 && total <= cap) {
+    k_periodic<true, float><<<ceil_div(n, kNLWarps), 32 * kNLWarps, 0, stream>>>(
+        pos, n, g, braw, bin_start, bin_atoms, nullptr, offset, e_center, e_nbr, e_shift, e_vec, e_dist);
+    CUDA_LAUNCH_CHECK();
+    CUDA_CHECK(cudaStreamSynchronize(stream));
+  }
+  return total;
 }
 
 }  // namespace pet

@@ -57,6 +57,22 @@ void build_local_nl(const double *pos, int n, int n_centers, const GridParams &g
 void build_open_nl(const float *pos, const int *sys_begin, const int *sys_end, int n,
                    float cutoff, EdgeList &out, NLScratch &s, cudaStream_t stream);
 
+// Periodic (or partially periodic) search that allocates nothing, for
+// callers that own all device memory.  Positions and the five pair arrays
+// are the caller's device buffers on the current device; the working memory
+// is one fixed static device array per device (7 kNoAllocMaxAtoms +
+// 3 kNoAllocMaxBins ints, 2.6 MB), whose address the first call on a
+// device looks up.  Throws Error(kErrInvalidParameter) above either limit.
+// Returns the total pair count; the arrays are written only when it is at
+// most `cap`.  Synchronises `stream`, and all of its work has finished when
+// it returns.  Calls on one device share the array: calls that overlap in
+// time (other host threads) race.
+constexpr int kNoAllocMaxAtoms = 65536;
+constexpr int kNoAllocMaxBins = 65536;
+int64_t build_periodic_nl_noalloc(const float *pos, int n, const GridParams &g, int64_t cap,
+                                  int *e_center, int *e_nbr, int *e_shift, float *e_vec, float *e_dist,
+                                  cudaStream_t stream);
+
 // Exclusive scan of n int32 counts into out[0..n] (out[n] = total) and the
 // maximum count into *max_out (device scalars); single CTA.
 void scan_counts(const int *in, int *out, int *max_out, int n, cudaStream_t stream);
