@@ -41,8 +41,11 @@ mlipcpp_error_t mlipcpp_b200_predict_device(mlipcpp_model_t model, int32_t n_ato
  * owned atoms first, then the ghost atoms within one cutoff of the owned
  * region, then the other ghosts (periodic images already placed);
  * atomic_numbers is a host array.  Layer 0 runs on the first n_layer0
- * atoms, layer 1 and the readout on the first n_owned.  bbox: row-major
- * cell that encloses the local positions (searched without periodicity).
+ * atoms, layer 1 and the readout on the first n_owned.  cell: row-major
+ * cell of the search grid; pbc: per axis, whether the local system is
+ * periodic along it (an axis the decomposition does not split) or open
+ * (NULL: open along all three).  Along open axes the local positions should
+ * lie inside the cell, for an even spread over the bins.
  * Outputs: energy of the owned atoms (host, eV, f64, composition included),
  * gradient forces on every local atom (d_forces: device [3 * n_local] float,
  * may be NULL), and the local virial sum_e e (x) dE/de in Voigt order (host,
@@ -51,8 +54,8 @@ mlipcpp_error_t mlipcpp_b200_predict_device(mlipcpp_model_t model, int32_t n_ato
 mlipcpp_error_t mlipcpp_b200_predict_local(mlipcpp_model_t model, int32_t n_local,
                                            const double *d_positions,
                                            const int32_t *atomic_numbers, int32_t n_layer0,
-                                           int32_t n_owned, const float bbox[9],
-                                           bool compute_forces, float *d_forces, double *energy,
+                                           int32_t n_owned, const float cell[9],
+                                           const bool *pbc, bool compute_forces, float *d_forces, double *energy,
                                            double virial[6]);
 
 /* Enable per-phase CUDA-event timing of later predictions. */

@@ -534,10 +534,10 @@ mlipcpp_error_t mlipcpp_b200_predict_device(mlipcpp_model_t model, int32_t n_ato
 
 mlipcpp_error_t mlipcpp_b200_predict_local(mlipcpp_model_t model, int32_t n_local, const double *d_positions,
                                            const int32_t *atomic_numbers, int32_t n_layer0, int32_t n_owned,
-                                           const float bbox[9], bool compute_forces, float *d_forces,
-                                           double *energy, double virial[6]) {
+                                           const float cell[9], const bool *pbc, bool compute_forces,
+                                           float *d_forces, double *energy, double virial[6]) {
   if (auto e = check_model(model)) return e;
-  if (!d_positions || !atomic_numbers || !bbox || !energy || !virial) {
+  if (!d_positions || !atomic_numbers || !cell || !energy || !virial) {
     set_error("NULL pointer argument");
     return MLIPCPP_ERROR_NULL_POINTER;
   }
@@ -546,8 +546,9 @@ mlipcpp_error_t mlipcpp_b200_predict_local(mlipcpp_model_t model, int32_t n_loca
     return MLIPCPP_ERROR_INVALID_PARAMETER;
   }
   try {
-    model->model->predict_local(d_positions, n_local, atomic_numbers, n_layer0, n_owned, bbox, compute_forces,
-                                d_forces, energy, virial);
+    const bool open3[3] = {false, false, false};
+    model->model->predict_local(d_positions, n_local, atomic_numbers, n_layer0, n_owned, cell,
+                                pbc ? pbc : open3, compute_forces, d_forces, energy, virial);
     clear_error();
     return MLIPCPP_OK;
   } catch (const std::exception &e) {

@@ -557,7 +557,7 @@ void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const in
 }
 
 void PETModel::predict_local(const double *d_pos, int n_local, const int32_t *numbers, int n_layer0, int n_owned,
-                             const float bbox[9], bool grad, float *d_forces, double *energy, double virial[6]) {
+                             const float cell[9], const bool pbc[3], bool grad, float *d_forces, double *energy, double virial[6]) {
   if (wptr_.empty()) throw Error(3, "Model weights not loaded");
   if (n_owned < 0 || n_layer0 < n_owned || n_local < n_layer0)
     throw Error(kErrInvalidParameter, "local system needs 0 <= n_owned <= n_layer0 <= n_local");
@@ -582,11 +582,10 @@ void PETModel::predict_local(const double *d_pos, int n_local, const int32_t *nu
   int *dsp = static_cast<int *>(d_species_.ensure(sizeof(int) * (n_local + 1)));
   CUDA_CHECK(cudaMemcpyAsync(dsp, hsp, sizeof(int) * n_local, cudaMemcpyHostToDevice, s));
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[1], s));
-  // non-periodic grid over the bounding cell; only the first n_layer0 atoms
-  // are centres, every local atom is a candidate neighbour
+  // grid over the cell, periodic only along unsplit axes; only the first
+  // n_layer0 atoms are centres, every local atom is a candidate neighbour
   GridParams g;
-  const bool open3[3] = {false, false, false};
-  make_grid_params(bbox, open3, h_.cutoff, &g);
+  make_grid_params(cell, pbc, h_.cutoff, &g);
   build_local_nl(d_pos, n_local, n_layer0, g, nl_, nls_, s);
   int e1 = 0;
   CUDA_CHECK(cudaMemcpyAsync(&e1, nl_.offset.as<int>() + n_owned, sizeof(int), cudaMemcpyDeviceToHost, s));

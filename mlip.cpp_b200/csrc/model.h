@@ -74,10 +74,10 @@ class PETModel {
   // readout on the first n_owned.  Returns the owned atoms' energy (with
   // composition), the gradient forces on all n_local atoms (device, may be
   // null) and the virial sum_e e (x) dE/de over the local edges (not divided
-  // by a volume).  `bbox` is a cell enclosing the local positions, searched
-  // without periodicity.
+  // by a volume).  `cell` and `pbc` define the search grid: periodic along
+  // the axes the decomposition leaves whole, open along the split ones.
   void predict_local(const double *d_pos, int n_local, const int32_t *numbers, int n_layer0, int n_owned,
-                     const float bbox[9], bool grad, float *d_forces, double *energy, double virial[6]);
+                     const float cell[9], const bool pbc[3], bool grad, float *d_forces, double *energy, double virial[6]);
 
   // Device-resident entry for benchmarks: positions already on the device.
   void predict_device(const float *d_pos, const SystemView &sys, bool compute_grad, Result &out,

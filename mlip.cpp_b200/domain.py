@@ -10,7 +10,9 @@ Atom i's energy depends on every atom within num_gnn_layers x cutoff of i:
 * those outputs depend on the neighbours' own neighbours;
 * attention is per atom.
 
-So each rank builds a local system of three groups:
+So each rank builds a local system of three groups (ghosts only across the
+faces the grid splits; along an unsplit axis the local system stays
+periodic):
 
     owned atoms                           layer 0, layer 1 and the readout
     ghosts within 1 cutoff of the slab    layer 0 only (their outputs feed
@@ -23,9 +25,8 @@ edges. Summing the three over ranks gives the whole cell's energy, forces and
 virial. That sum is the only exchange step: one NCCL all-reduce of the force
 array and one of (energy, virial). Every rank holds the whole position array;
 each step it partitions on the device (fractional coordinates, 27 image
-shifts, three host synchronisations for the counts), gathers its local
-system with exact f64 image shifts and translates it into a non-negative
-bounding box for the local grid search.
+shifts, two host synchronisations for the counts) and gathers its local
+system with exact f64 image shifts.
 """
 from __future__ import annotations
 
@@ -40,7 +41,8 @@ class LocalDomain:
     shift: np.ndarray       # [n_local, 3] integer image shift (in cell vectors)
     n_layer0: int           # owned + first ghost shell
     n_owned: int
-    bbox: np.ndarray        # (3, 3) float32 cell enclosing the local positions
+    cell: np.ndarray        # (3, 3) float32 search-grid cell (the global cell)
+    pbc: tuple              # periodic along the axes the grid does not split
     grid: tuple
     rank: int
 
@@ -80,8 +82,8 @@ def partition(positions, cell, cutoff: float, grid: tuple, rank: int, layers: in
     import torch
     d = partition_device(torch.from_numpy(np.asarray(positions, np.float64).reshape(-1, 3)),
                          torch.from_numpy(np.asarray(cell, np.float64).reshape(3, 3)), cutoff, grid, rank, layers)
-    return LocalDomain(d["index"].numpy(), d["shift"].numpy(), d["n_layer0"], d["n_owned"], d["bbox"],
-                       tuple(int(x) for x in grid), rank)
+    return LocalDomain(d["index"].numpy(), d["shift"].numpy(), d["n_layer0"], d["n_owned"], d["cell"],
+                       d["pbc"], tuple(int(x) for x in grid), rank)
 
 
 _SHIFTS = np.array(np.meshgrid(*([(-1, 0, 1)] * 3), indexing="ij")).reshape(3, -1).T  # [27, 3]
@@ -89,10 +91,11 @@ _SHIFTS = np.array(np.meshgrid(*([(-1, 0, 1)] * 3), indexing="ij")).reshape(3, -
 
 def partition_device(positions, cell, cutoff: float, grid: tuple, rank: int, layers: int = 2) -> dict:
     """partition() with torch tensors on any device (positions [N, 3],
-    cell [3, 3]).  Returns index and shift tensors on that device, the
-    local positions translated to a non-negative bounding box (f64), the
-    counts and the bounding cell.  Three host synchronisations (counts and
-    the box extent)."""
+    cell [3, 3]).  An axis the grid does not split stays periodic and gets
+    no ghosts.  Returns index and shift tensors on that device, the local
+    positions (f64; translated along split axes so that their fractional
+    coordinates start at 0), the counts, the search cell and its pbc flags.
+    Two host synchronisations (the counts)."""
     import torch
 
     dev = positions.device
@@ -101,8 +104,9 @@ def partition_device(positions, cell, cutoff: float, grid: tuple, rank: int, lay
     p = torch.tensor(grid, dtype=torch.float64, device=dev)
     pi = torch.tensor(grid, dtype=torch.int64, device=dev)
     face = torch.from_numpy(face_distances(c.cpu().numpy())).to(dev)
-    d1 = cutoff / face
-    dn = layers * cutoff / face
+    split = p > 1
+    d1 = torch.where(split, cutoff / face, torch.zeros_like(face))
+    dn = torch.where(split, layers * cutoff / face, torch.zeros_like(face))
     if bool(torch.any(dn >= 1.0 / p)):
         # one image (+-1) per axis suffices only if a ghost shell is thinner than a slab
         raise ValueError("cell too small for this many domains (ghost shell thicker than a slab)")
@@ -129,16 +133,11 @@ def partition_device(positions, cell, cutoff: float, grid: tuple, rank: int, lay
     shift = shift + base[index].to(torch.int64)
     n_owned = int(owned.shape[0])
     n_layer0 = n_owned + int(i1.shape[0])
-    local = pos[index] + shift.to(torch.float64) @ c
-    if local.shape[0]:
-        lo_xyz = local.min(0).values
-        local = local - lo_xyz
-        ext = local.max(0).values.cpu().numpy()
-    else:
-        ext = np.zeros(3)
-    bbox = np.diag(np.maximum(ext + 1.0, cutoff)).astype(np.float32)
+    origin = torch.where(split, lo - dn, torch.zeros_like(lo))
+    local = pos[index] + (shift.to(torch.float64) - origin) @ c
+    pbc = tuple(bool(x) for x in (np.asarray(grid) == 1))
     return {"index": index, "shift": shift, "local": local, "n_owned": n_owned, "n_layer0": n_layer0,
-            "bbox": bbox}
+            "cell": c.cpu().numpy().astype(np.float32), "pbc": pbc}
 
 
 def predictor_eval(predictor):
@@ -148,8 +147,8 @@ def predictor_eval(predictor):
 
     def run(d: LocalDomain, local_pos, numbers, forces_out):
         torch.cuda.synchronize()  # the library runs on its own stream
-        return predictor.predict_local(local_pos.data_ptr(), numbers, d.n_layer0, d.n_owned, d.bbox, True,
-                                       forces_out.data_ptr())
+        return predictor.predict_local(local_pos.data_ptr(), numbers, d.n_layer0, d.n_owned, d.cell, d.pbc,
+                                       True, forces_out.data_ptr())
     return run
 
 
@@ -188,7 +187,7 @@ class DomainRunner:
         for r in self.my_domains:
             d = partition_device(positions, self.cell_t, self.cutoff, self.grid, r)
             idx = d["index"]
-            dom = LocalDomain(idx, d["shift"], d["n_layer0"], d["n_owned"], d["bbox"], self.grid, r)
+            dom = LocalDomain(idx, d["shift"], d["n_layer0"], d["n_owned"], d["cell"], d["pbc"], self.grid, r)
             z = self.numbers[idx.cpu().numpy()]
             local = d["local"].contiguous()
             forces = torch.empty((idx.shape[0], 3), dtype=torch.float32, device=self.device)

@@ -31,8 +31,13 @@ def test_partition_owns_once_and_ghosts_complete(grid):
     for r in range(n_dom):
         d = dd.partition(s.positions, cell, rc, grid, r)
         owners[d.index[:d.n_owned]] += 1
+        assert d.pbc == tuple(g == 1 for g in grid)
+        split = np.array([g > 1 for g in grid])
         local = s.positions[d.index].astype(np.float64) + d.shift @ cell
-        keys = {(int(i), *map(int, sh)) for i, sh in zip(d.index, d.shift)}
+        # images are told apart only along split axes (the local system is
+        # periodic along the others)
+        key = lambda i, sh: (int(i), *(int(x) if sp else 0 for x, sp in zip(sh, split)))  # noqa: E731
+        keys = {key(i, sh) for i, sh in zip(d.index, d.shift)}
         assert len(keys) == d.n_local  # no duplicate images
         own = local[:d.n_owned]
         # every image of every atom within 2 rc of an owned atom is local, and
@@ -40,15 +45,15 @@ def test_partition_owns_once_and_ghosts_complete(grid):
         shifts = np.array(np.meshgrid(*([(-2, -1, 0, 1, 2)] * 3), indexing="ij")).reshape(3, -1).T
         frac = s.positions.astype(np.float64) @ np.linalg.inv(cell)
         base = -np.floor(frac)
-        lay0 = {(int(i), *map(int, sh)) for i, sh in zip(d.index[:d.n_layer0], d.shift[:d.n_layer0])}
+        lay0 = {key(i, sh) for i, sh in zip(d.index[:d.n_layer0], d.shift[:d.n_layer0])}
         for sh in shifts:
             img_shift = base + sh
             pos_img = s.positions.astype(np.float64) + img_shift @ cell
             dmin = np.min(np.linalg.norm(pos_img[:, None, :] - own[None, :, :], axis=2), axis=1)
             for i in np.nonzero(dmin < 2 * rc)[0]:
-                assert (int(i), *map(int, img_shift[i])) in keys
+                assert key(i, img_shift[i]) in keys
             for i in np.nonzero(dmin < rc)[0]:
-                assert (int(i), *map(int, img_shift[i])) in lay0
+                assert key(i, img_shift[i]) in lay0
     assert np.all(owners == 1)
 
 
@@ -58,7 +63,7 @@ def oracle_local_eval(orc):
     h = orc.h
 
     def run(d, local_pos, numbers, forces_out):
-        st = wl.Structure(local_pos.numpy().astype(np.float32), np.asarray(numbers, np.int32))
+        st = wl.Structure(local_pos.numpy().astype(np.float32), np.asarray(numbers, np.int32), d.cell, d.pbc)
         b = po.prepare_batch([st], h.cutoff, h.cutoff_width, orc.species_to_index)
         vec = torch.tensor(b.vec, dtype=torch.float64, requires_grad=True)
         e = orc.atomic_energies(b, vec)[:d.n_owned].sum()
