@@ -274,11 +274,14 @@ def main():
 
     if rank == 0:
         hbm, bf16, bf16_sus, src = _peaks()
-        g = kstats["gemm_tc"]
-        gs = kstats["gemm_simt"]
+        f16 = kstats["gemm_f16"]["launches"] > 0
+        g = kstats["gemm_f16" if f16 else "gemm_tc"]
+        gemm_ms = kstats["gemm_f16"]["ms"] + kstats["gemm_tc"]["ms"] + kstats["gemm_simt"]["ms"]
         achieved = g["flops"] / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else 0.0
-        # 3xTF32 runs three tf32 MMAs per fp32 product at half the bf16 rate:
-        # its ceiling is the measured bf16 peak / 6 (achieved counts 2MNK).
+        # achieved counts 2MNK.  3xFP16 runs three fp16 MMAs per fp32 product at
+        # the bf16 rate (ceiling: measured bf16 peak / 3); 3xTF32 three tf32
+        # MMAs at half that rate (ceiling / 6).
+        div = 3.0 if f16 else 6.0
         shape = pred.last_shape()
         line = {
             "metric": METRIC, "value": value, "unit": "atom-steps/s", "n_gpus": world,
@@ -295,18 +298,22 @@ def main():
                     "h2d_bytes_per_step": int(s.positions.nbytes + (0 if domains else s.numbers.nbytes)),
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches),
-            "roofline": {"bound": "tensor", "kernel": "k_gemm_3xtf32 (tcgen05, all dense layers)",
-                         "achieved": achieved, "peak": bf16_sus / 6.0, "unit": "TFLOP/s",
-                         "frac": achieved / (bf16_sus / 6.0),
-                         "peak_source": f"{src} bf16 sustained / 6 (3 tf32 MMAs at half bf16 rate)",
-                         "tensor_pipe_frac_of_bf16": 6.0 * achieved / bf16_sus,
+            "roofline": {"bound": "tensor",
+                         "kernel": ("k_gemm_3xf16 + k_row_scale" if f16 else "k_gemm_3xtf32")
+                                   + " (tcgen05, all dense layers)",
+                         "achieved": achieved, "peak": bf16_sus / div, "unit": "TFLOP/s",
+                         "frac": achieved / (bf16_sus / div),
+                         "peak_source": (f"{src} bf16 sustained / 3 (3 fp16 MMAs per product at the bf16 rate)" if f16 else
+                                         f"{src} bf16 sustained / 6 (3 tf32 MMAs at half bf16 rate)"),
+                         "tensor_pipe_frac_of_bf16": div * achieved / bf16_sus,
                          # DRAM bytes per average GEMM launch: ncu dram__bytes_read.sum +
                          # dram__bytes_write.sum over all 57 GEMM launches of one step of the
                          # 1,728-atom cell of this alloy (354 MB/launch at 65,202 tokens,
                          # 5,429 B per token), scaled by this step's token count
-                         "traffic": 5429.0 * (shape["atoms"] + shape["edges"]) if not domains else None,
+                         "traffic": (5429.0 * (shape["atoms"] + shape["edges"])
+                                     if not domains and not f16 else None),
                          "traffic_unit": "bytes per GEMM launch (scaled from the 1,728-atom capture)",
-                         "gemm_share_of_step": (g["ms"] + gs["ms"]) / (t_dev * 1e3) if t_dev else None},
+                         "gemm_share_of_step": gemm_ms / (t_dev * 1e3) if t_dev else None},
             "kernel_stats": kstats,
             "phase_ms": pred.last_timings(),
             "clocks": clk.summary(),

@@ -118,10 +118,11 @@ mlipcpp_error_t mlipcpp_b200_set_device(int32_t device);
 mlipcpp_error_t mlipcpp_b200_set_kernel_profiling(mlipcpp_model_t model, bool enable);
 
 /* Cumulative per-class statistics since profiling was enabled: for classes
- * tensor-core GEMM, SIMT GEMM, attention, neighbour list, other:
+ * 3xTF32 tensor-core GEMM, SIMT GEMM, attention, neighbour list, other,
+ * 3xFP16 tensor-core GEMM (with its row-scale pre-pass):
  * {launches, total ms, algorithmic FLOPs, algorithmic HBM bytes}
  * -> stats[4 * class + 0..3]. */
-mlipcpp_error_t mlipcpp_b200_kernel_stats(mlipcpp_model_t model, double stats[20]);
+mlipcpp_error_t mlipcpp_b200_kernel_stats(mlipcpp_model_t model, double stats[24]);
 
 #ifdef __cplusplus
 }

@@ -395,9 +395,9 @@ class Predictor:
 
     def kernel_stats(self) -> dict:
         """Per kernel class: launches, ms, algorithmic flops and bytes."""
-        a = np.zeros(20, np.float64)
+        a = np.zeros(24, np.float64)
         _check(lib().mlipcpp_b200_kernel_stats(self._h, a.ctypes.data))
-        names = ["gemm_tc", "gemm_simt", "attention", "neighbor_list", "other"]
+        names = ["gemm_tc", "gemm_simt", "attention", "neighbor_list", "other", "gemm_f16"]
         return {n: {"launches": int(a[4 * k]), "ms": float(a[4 * k + 1]),
                     "flops": float(a[4 * k + 2]), "bytes": float(a[4 * k + 3])}
                 for k, n in enumerate(names)}

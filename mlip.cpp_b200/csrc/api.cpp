@@ -723,7 +723,7 @@ mlipcpp_error_t mlipcpp_b200_set_kernel_profiling(mlipcpp_model_t model, bool en
   return MLIPCPP_OK;
 }
 
-mlipcpp_error_t mlipcpp_b200_kernel_stats(mlipcpp_model_t model, double stats[20]) {
+mlipcpp_error_t mlipcpp_b200_kernel_stats(mlipcpp_model_t model, double stats[24]) {
   if (auto e = check_model(model)) return e;
   if (!stats) {
     set_error("NULL stats pointer");

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <cstdint>
 
 #include "kernels.cuh"
 
@@ -14,12 +15,35 @@ struct TCWeights {
   const float *lo = nullptr;
 };
 
+// fp16 pre-split copies of a B operand for the 3xFP16 kernel: B 2^b_scale
+// = hi + lo (both fp16, round-to-nearest), one power-of-two scale per
+// weight tensor chosen so that its largest |element| maps into [2^14, 2^15).
+struct TCWeights16 {
+  const uint16_t *hi = nullptr;
+  const uint16_t *lo = nullptr;
+  int b_scale = 0;
+};
+
 // True when the shape and alignment fit the tensor-core kernel (N multiple
 // of 128, K multiple of 32, 16-byte aligned rows).
 bool gemm_tc_supported(const GemmArgs &a);
+// True when the 3xFP16 kernel applies as well (K a multiple of 64, B rows
+// 16-byte aligned in fp16).
+bool gemm_f16_supported(const GemmArgs &a);
 
 // C = A B^T (+ epilogue) with 3xTF32 on tcgen05; `err` (device int) is set
 // non-zero if a pipeline wait times out.
 void gemm_3xtf32(const GemmArgs &a, const TCWeights &w, int *err, cudaStream_t s);
+
+// C = A B^T (+ epilogue) with 3xFP16 on tcgen05: each A row m is scaled by
+// 2^s_m (its largest |element| into [2^14, 2^15), computed by a pre-pass
+// into `row_scale`, device int[M]) and B by 2^b_scale, both split into fp16
+// hi + lo, and A B^T ~= (A_hi B_hi + A_hi B_lo + A_lo B_hi) 2^-(s_m + b_scale)
+// with fp32 accumulation.
+void gemm_3xf16(const GemmArgs &a, const TCWeights16 &w, int *row_scale, int *err, cudaStream_t s);
+
+// Power-of-two scale exponent s with max|x| 2^s in [2^14, 2^15) (0 for an
+// all-zero tensor, clamped to [-120, 120]).
+int f16_scale_exponent(float max_abs);
 
 }  // namespace pet

@@ -19,6 +19,8 @@
 #include <cstdlib>
 #include <cstring>
 
+#include <cuda_fp16.h>
+
 #include "gemm_tc.cuh"
 #include "gguf.h"
 #include "kernels.cuh"
@@ -159,6 +161,27 @@ size_t PETModel::device_bytes() const {
 // ---------------------------------------------------------------------------
 // Weights (PETModel::load_from_gguf, pet.cpp:1100-1312)
 // ---------------------------------------------------------------------------
+namespace {
+uint16_t float_to_half_bits(float x) {
+  const __half h = __float2half_rn(x);
+  uint16_t b;
+  std::memcpy(&b, &h, 2);
+  return b;
+}
+float half_bits_to_float(uint16_t b) {
+  __half h;
+  std::memcpy(&h, &b, 2);
+  return __half2float(h);
+}
+}  // namespace
+
+int PETModel::weight_scale(size_t elem) const {
+  auto it = std::upper_bound(wscale_.begin(), wscale_.end(), elem,
+                             [](size_t e, const WScale &w) { return e < w.begin; });
+  if (it == wscale_.begin() || elem >= (it - 1)->end) throw Error(kErrInternal, "weight pointer outside every tensor");
+  return (it - 1)->scale;
+}
+
 void PETModel::load(const std::string &path, float cutoff_override) {
   GGUFFile f(path);
   const auto *emb = f.tensor("model.embedding.weight");
@@ -220,33 +243,49 @@ void PETModel::load(const std::string &path, float cutoff_override) {
       transpose_of(hp + "2.weight");
     }
   }
-  // One arena holding three copies with identical layout: fp32, its tf32
-  // truncation (hi) and the remainder (lo), so the split operands of any
-  // weight pointer (sub-blocks included) sit at fixed offsets from it.
+  // One arena holding five copies with identical element layout: fp32, its
+  // tf32 truncation (hi) and the remainder (lo), then fp16 hi = rn(w 2^s)
+  // and lo = rn(w 2^s - hi) with one power-of-two scale s per tensor, so the
+  // split operands of any weight pointer (sub-blocks included) sit at fixed
+  // offsets from it.
   size_t total = 0;
   for (auto &kv : host) total += (kv.second.size() * 4 + 255) / 256 * 256;
-  wbuf_.ensure(3 * total);
+  wbuf_.ensure(4 * total);
   wspan_ = total / 4;
   wptr_.clear();
-  std::vector<char> staging(3 * total, 0);
+  wscale_.clear();
+  std::vector<char> staging(4 * total, 0);
+  uint16_t *hi16 = reinterpret_cast<uint16_t *>(staging.data() + 3 * total);
+  uint16_t *lo16 = hi16 + wspan_;
   size_t off = 0;
   for (auto &kv : host) {
     std::memcpy(staging.data() + off, kv.second.data(), kv.second.size() * 4);
     float *hi = reinterpret_cast<float *>(staging.data() + total + off);
     float *lo = reinterpret_cast<float *>(staging.data() + 2 * total + off);
+    float mx = 0.f;
     for (size_t k = 0; k < kv.second.size(); ++k) {
       uint32_t u;
       std::memcpy(&u, &kv.second[k], 4);
       u &= 0xFFFFE000u;
       std::memcpy(&hi[k], &u, 4);
       lo[k] = kv.second[k] - hi[k];
+      mx = std::max(mx, std::fabs(kv.second[k]));
     }
+    const int sc = f16_scale_exponent(mx);
+    const size_t e0 = off / 4;
+    for (size_t k = 0; k < kv.second.size(); ++k) {
+      const float x = std::ldexp(kv.second[k], sc);
+      const float xh = half_bits_to_float(hi16[e0 + k] = float_to_half_bits(x));
+      lo16[e0 + k] = float_to_half_bits(x - xh);
+    }
+    wscale_.push_back({e0, e0 + kv.second.size(), sc});
     wptr_[kv.first] = reinterpret_cast<const float *>(wbuf_.as<char>() + off);
     off += (kv.second.size() * 4 + 255) / 256 * 256;
   }
-  CUDA_CHECK(cudaMemcpy(wbuf_.ptr, staging.data(), 3 * total, cudaMemcpyHostToDevice));
+  CUDA_CHECK(cudaMemcpy(wbuf_.ptr, staging.data(), 4 * total, cudaMemcpyHostToDevice));
   const char *g = std::getenv("MLIPCPP_B200_GEMM");
   use_tc_ = !(g && std::string(g) == "simt");
+  use_f16_ = use_tc_ && !(g && std::string(g) == "tf32");
 
   // composition map and species index (pet.cpp:1280-1303)
   species_index_.clear();
@@ -389,11 +428,22 @@ void PETModel::forward_backward(bool grad) {
     const float *wb = wbuf_.as<float>();
     const bool in_arena = B >= wb && B < wb + wspan_;
     const bool tc = use_tc_ && in_arena && gemm_tc_supported(g);
+    const size_t eoff = in_arena ? static_cast<size_t>(B - wb) : 0;
+    const bool f16 = tc && use_f16_ && gemm_f16_supported(g) && eoff % 8 == 0;
     cudaEvent_t e0 = nullptr;
     if (kprof_) mark_begin(e0);
-    if (tc) gemm_3xtf32(g, TCWeights{B + wspan_, B + 2 * wspan_}, d_err_.as<int>(), st);
-    else gemm_f32(g, st);
-    if (kprof_) mark_end(tc ? KC_GEMM_TC : KC_GEMM_SIMT, e0, 2.0 * M * N * static_cast<double>(K), gemm_bytes(g));
+    if (f16) {
+      const uint16_t *h16 = reinterpret_cast<const uint16_t *>(wb + 3 * wspan_);
+      gemm_3xf16(g, TCWeights16{h16 + eoff, h16 + wspan_ + eoff, weight_scale(eoff)}, rscale_.as<int>(),
+                 d_err_.as<int>(), st);
+    } else if (tc) {
+      gemm_3xtf32(g, TCWeights{B + wspan_, B + 2 * wspan_}, d_err_.as<int>(), st);
+    } else {
+      gemm_f32(g, st);
+    }
+    if (kprof_)
+      mark_end(f16 ? KC_GEMM_F16 : tc ? KC_GEMM_TC : KC_GEMM_SIMT, e0, 2.0 * M * N * static_cast<double>(K),
+               gemm_bytes(g));
   };
   auto attn = [&](bool backward, const AttnArgs &x) {
     cudaEvent_t e0 = nullptr;
@@ -541,6 +591,7 @@ void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const in
   plan_memory(P, S, in_->a, h_, c, grad);
   persist_.ensure(P.off);
   scratch_.ensure(S.off);
+  rscale_.ensure(sizeof(int) * (static_cast<size_t>(std::max(Tl_[0], Tl_[1])) + 1));
   P = Plan{persist_.as<char>(), 0};
   S = Plan{scratch_.as<char>(), 0};
   plan_memory(P, S, in_->a, h_, c, grad);

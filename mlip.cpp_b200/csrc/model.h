@@ -39,7 +39,15 @@ struct Result {
 };
 
 // Kernel classes timed individually when kernel profiling is on.
-enum KernelClass { KC_GEMM_TC = 0, KC_GEMM_SIMT = 1, KC_ATTENTION = 2, KC_NEIGHBOR = 3, KC_OTHER = 4, KC_COUNT = 5 };
+enum KernelClass {
+  KC_GEMM_TC = 0,    // 3xTF32 tensor-core GEMM
+  KC_GEMM_SIMT = 1,  // fp32 SIMT GEMM
+  KC_ATTENTION = 2,
+  KC_NEIGHBOR = 3,
+  KC_OTHER = 4,
+  KC_GEMM_F16 = 5,   // 3xFP16 tensor-core GEMM (with its row-scale pre-pass)
+  KC_COUNT = 6
+};
 
 struct KernelStat {
   long long launches = 0;
@@ -114,6 +122,13 @@ class PETModel {
   DevBuf wbuf_;          // [fp32 | tf32 hi | lo] copies of every weight
   size_t wspan_ = 0;     // floats between the three copies
   bool use_tc_ = true;   // tensor-core GEMMs (MLIPCPP_B200_GEMM=simt disables)
+  bool use_f16_ = true;  // 3xFP16 where it applies (MLIPCPP_B200_GEMM=tf32 keeps 3xTF32)
+  // fp16 hi / lo copies after the three fp32 copies, same element offsets;
+  // one power-of-two scale per tensor: {first element, end element, scale}
+  struct WScale { size_t begin, end; int scale; };
+  std::vector<WScale> wscale_;
+  DevBuf rscale_;        // per-row scale exponents of the 3xFP16 pre-pass
+  int weight_scale(size_t elem) const;
   DevBuf d_err_;         // device error word written by bounded waits
   std::map<std::string, const float *> wptr_;
   std::map<int, int> species_index_;

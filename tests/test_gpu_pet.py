@@ -149,16 +149,23 @@ def test_gpu_kernel_launches_counted(model_file):
     assert mb.kernel_launches() > before
 
 
-def test_gpu_tensor_core_matches_simt(model_file, monkeypatch):
-    """The 3xTF32 tcgen05 GEMM path and the exact-fp32 SIMT path agree
-    within the fp32 parity tolerances on the same inputs."""
+@pytest.mark.parametrize("mode", ["tf32", "f16"])
+def test_gpu_tensor_core_matches_simt(mode, model_file, monkeypatch):
+    """The 3xTF32 and 3xFP16 tcgen05 GEMM paths and the exact-fp32 SIMT path
+    agree within the fp32 parity tolerances on the same inputs."""
     path = model_file("pet-mad-s", 8)
     s = wl.si_diamond(2, seed=8)
     monkeypatch.setenv("MLIPCPP_B200_GEMM", "simt")
     simt = mb.Predictor(path).predict(s.positions, s.numbers, s.cell, compute_stress=True)
-    monkeypatch.delenv("MLIPCPP_B200_GEMM")
+    if mode == "tf32":
+        monkeypatch.setenv("MLIPCPP_B200_GEMM", "tf32")
+    else:
+        monkeypatch.delenv("MLIPCPP_B200_GEMM")
     pred = mb.Predictor(path)
     pred.set_kernel_profiling(True)
     tc = pred.predict(s.positions, s.numbers, s.cell, compute_stress=True)
-    assert pred.kernel_stats()["gemm_tc"]["launches"] > 0
+    st = pred.kernel_stats()
+    assert st["gemm_f16" if mode == "f16" else "gemm_tc"]["launches"] > 0
+    if mode == "tf32":
+        assert st["gemm_f16"]["launches"] == 0
     assert_close(tc, simt.energy, simt.forces, simt.stress, s.n_atoms)
