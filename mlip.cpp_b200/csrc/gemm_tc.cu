@@ -32,9 +32,12 @@
 // Every mbarrier wait is bounded (~1 s of %globaltimer); on expiry the kernel
 // records an error code, skips the rest of its work, frees its tensor memory
 // and returns, so a fault cannot hang the GPU.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -415,17 +418,19 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_gemm_3xtf32(GemmArgs p, TCWei
 }
 
 // ---------------------------------------------------------------------------
-// 3xFP16: same roles and pipeline as k_gemm_3xtf32, k-tiles of 64 fp16
+// 3xFP16 with TMA-fed operands
 // ---------------------------------------------------------------------------
-constexpr int BK16 = 64;
-#ifndef PET_GEMM_CHUNK16
-#define PET_GEMM_CHUNK16 2
-#endif
-// k-tiles (of 64) per TMEM accumulation pass: 2 x 64 x 3 = 384 products, as
-// many as 4 tf32 k-tiles of 32
-constexpr int kChunk16 = PET_GEMM_CHUNK16;
+// A pre-pass (k_split_a) writes A, row-gathered if asked, as "split fp16":
+// hi = rn(a 2^s), lo = rn(a 2^s - hi) ([M, K] fp16 each) with one scale
+// exponent s per row and 128-element k block ([K/128, M] int8), chosen so
+// that the block's largest |element| maps into [2^14, 2^15).  The GEMM
+// streams A hi/lo and the pre-split weights B hi/lo with TMA (128-byte
+// swizzle, exactly the UMMA K-major layout), and one TMEM pass covers one
+// k block, so the accumulator warps promote each pass with its row's block
+// scale: acc += pass 2^-s.  The epilogue applies the weight tensor's scale.
+constexpr int kSBlock = 128;               // k per A scale block = one TMEM pass (384 products)
+constexpr int kMaxSBlocks = 16;            // K <= 2048
 
-// Row pre-pass: rs[m] = s with max_k |A[m, k]| 2^s in [2^14, 2^15).
 __device__ __forceinline__ int scale_exponent_dev(float mx) {
   if (!(mx > 0.f)) return 0;
   const int E = static_cast<int>((__float_as_uint(mx) >> 23) & 0xFFu);
@@ -433,70 +438,118 @@ __device__ __forceinline__ int scale_exponent_dev(float mx) {
   return s < -120 ? -120 : (s > 120 ? 120 : s);
 }
 
-__global__ void __launch_bounds__(256) k_row_scale(const float *__restrict__ A, int lda,
-                                                   const int *__restrict__ a_rows, int M, int K,
-                                                   int *__restrict__ rs) {
+// Warp per row: lane l holds elements 4l..4l+3 of every 128-element block.
+__global__ void __launch_bounds__(256) k_split_a(const float *__restrict__ A, int lda,
+                                                 const int *__restrict__ a_rows, int M, int K,
+                                                 uint16_t *__restrict__ hi, uint16_t *__restrict__ lo,
+                                                 int8_t *__restrict__ sc) {
   const int m = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (m >= M) return;
   const float *row = A + static_cast<size_t>(a_rows ? a_rows[m] : m) * lda;
-  float mx = 0.f;
-  for (int k = lane * 4; k < K; k += 128) {
-    const float4 v = *reinterpret_cast<const float4 *>(row + k);
-    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-  }
+  const int nb = K / kSBlock;
+  float4 v[kMaxSBlocks];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if (lane == 0) rs[m] = scale_exponent_dev(mx);
+  for (int b = 0; b < kMaxSBlocks; ++b)
+    if (b < nb) v[b] = *reinterpret_cast<const float4 *>(row + b * kSBlock + lane * 4);
+#pragma unroll
+  for (int b = 0; b < kMaxSBlocks; ++b) {
+    if (b >= nb) break;
+    float mx = fmaxf(fmaxf(fabsf(v[b].x), fabsf(v[b].y)), fmaxf(fabsf(v[b].z), fabsf(v[b].w)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int s = scale_exponent_dev(mx);
+    const float f = pow2f(s);
+    const float x0 = v[b].x * f, x1 = v[b].y * f, x2 = v[b].z * f, x3 = v[b].w * f;
+    const __half2 h01 = __floats2half2_rn(x0, x1), h23 = __floats2half2_rn(x2, x3);
+    const float2 r01 = __half22float2(h01), r23 = __half22float2(h23);
+    const __half2 l01 = __floats2half2_rn(x0 - r01.x, x1 - r01.y), l23 = __floats2half2_rn(x2 - r23.x, x3 - r23.y);
+    const size_t o = static_cast<size_t>(m) * K + b * kSBlock + lane * 4;
+    *reinterpret_cast<uint2 *>(hi + o) =
+        make_uint2(*reinterpret_cast<const uint32_t *>(&h01), *reinterpret_cast<const uint32_t *>(&h23));
+    *reinterpret_cast<uint2 *>(lo + o) =
+        make_uint2(*reinterpret_cast<const uint32_t *>(&l01), *reinterpret_cast<const uint32_t *>(&l23));
+    if (lane == 0) sc[static_cast<size_t>(b) * M + m] = static_cast<int8_t>(s);
+  }
 }
 
-// 8 scaled fp32 values -> 8 fp16 hi (rn) and 8 fp16 lo = rn(x - hi), packed
-// in element order (lower k at the lower address).
-__device__ __forceinline__ void split_f16x8(const float4 &a, const float4 &b, float sc, uint4 &hi, uint4 &lo) {
-  const float x[8] = {a.x * sc, a.y * sc, a.z * sc, a.w * sc, b.x * sc, b.y * sc, b.z * sc, b.w * sc};
-  uint32_t h[4], l[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const __half2 hh = __floats2half2_rn(x[2 * j], x[2 * j + 1]);
-    const float2 hf = __half22float2(hh);
-    const __half2 ll = __floats2half2_rn(x[2 * j] - hf.x, x[2 * j + 1] - hf.y);
-    h[j] = *reinterpret_cast<const uint32_t *>(&hh);
-    l[j] = *reinterpret_cast<const uint32_t *>(&ll);
-  }
-  hi = make_uint4(h[0], h[1], h[2], h[3]);
-  lo = make_uint4(l[0], l[1], l[2], l[3]);
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
-template <int EPI>
-__global__ void __launch_bounds__(kWsThreads, 1)
-    k_gemm_3xf16(GemmArgs p, TCWeights16 w, const int *__restrict__ rs, int *err) {
+// 2D tiled TMA load (box 64 x 128 fp16, 128-byte swizzle) completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Tile shapes of the 3xFP16 kernel.  BN = 128: k-tiles of 64 (128-byte rows,
+// 128-byte swizzle), 3 stages of 64 KB, 4 TMEM buffers, 4 accumulator
+// warps.  BN = 256: k-tiles of 32 (64-byte rows, 64-byte swizzle), 4 stages
+// of 48 KB (a quarter fewer operand bytes per product and one more stage in
+// flight), 2 TMEM buffers of 256 columns, 8 accumulator warps (two per TMEM
+// lane quarter, 128 columns each).
+template <int BN_>
+struct F16Cfg {
+  static constexpr int BK = BN_ == 256 ? 32 : 64;
+  static constexpr int RowBytes = BK * 2;
+  static constexpr int ATile = BM * RowBytes;
+  static constexpr int BTile = BN_ * RowBytes;
+  static constexpr int StageBytes = 2 * ATile + 2 * BTile;
+  static constexpr int Stages = (192 * 1024) / StageBytes;
+  static constexpr int Chunk = kSBlock / BK;          // k-tiles per TMEM pass (one A scale block)
+  static constexpr int TmemBufs = 512 / BN_;
+  static constexpr int AccWarps = BN_ / 32;
+  static constexpr int Threads = 64 + 32 * AccWarps;
+  // 10 warps put 3 on some SM sub-partitions: 168 registers at most
+  static constexpr int LaunchBound = BN_ == 256 ? 384 : 192;
+  static constexpr uint32_t Sbo = 8 * RowBytes;      // bytes between 8-row swizzle atoms
+  static constexpr uint64_t Layout = BN_ == 256 ? 4 : 2;  // SWIZZLE_64B : SWIZZLE_128B
+  static constexpr int Smem = Stages * StageBytes + 1024 + 256;
+};
+
+template <typename C>
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t start) {
+  return static_cast<uint64_t>((start >> 4) & 0x3FFFu) | (1ull << 16) |
+         (static_cast<uint64_t>(C::Sbo >> 4) << 32) | (1ull << 46) | (C::Layout << 61);
+}
+
+template <int EPI, int BNt>
+__global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
+    k_gemm_3xf16(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
+                 const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
+                 GemmArgs p, const int8_t *__restrict__ sc, int b_scale, int *err) {
+  using C = F16Cfg<BNt>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t *gbase = smem_raw + (base - raw);
-  const uint32_t bars = base + kStages * kStageBytes;
-  const uint32_t full0 = bars, empty0 = bars + 8 * kStages, accf0 = bars + 16 * kStages,
-                 acce0 = accf0 + 16;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + kStages * kStageBytes + 192);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(gbase + kStages * kStageBytes + 200);
+  const uint32_t bars = base + C::Stages * C::StageBytes;
+  // mbarriers: full[Stages], empty[Stages], accf[TmemBufs], acce[TmemBufs]
+  const uint32_t full0 = bars, empty0 = bars + 8 * C::Stages, accf0 = bars + 16 * C::Stages,
+                 acce0 = accf0 + 8 * C::TmemBufs;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + C::Stages * C::StageBytes + 192);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(gbase + C::Stages * C::StageBytes + 200);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nk = p.K / BK16;
-  const int tiles_n = p.N / BN;
+  const int nk = p.K / C::BK;
+  const int tiles_n = p.N / BNt;
   const int tiles = ((p.M + BM - 1) / BM) * tiles_n;
 
-  if (warp == 4) {
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(2 * BN));
+                 "r"(512));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(full0 + 8 * s, 128);
+    for (int s = 0; s < C::Stages; ++s) {
+      mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < C::TmemBufs; ++b) {
       mbar_init(accf0 + 8 * b, 1);
-      mbar_init(acce0 + 8 * b, 128);
+      mbar_init(acce0 + 8 * b, 32 * C::AccWarps);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -506,97 +559,62 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < 4) {
-    // ---------------- producers ----------------
-    const int pr = tid >> 3, pc = tid & 7;
-    int it = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-      const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
-      const float *arow[BM / 16];
-      float asc[BM / 16];
-#pragma unroll
-      for (int i = 0; i < BM / 16; ++i) {
-        const int m = m0 + pr + 16 * i;
-        arow[i] = nullptr;
-        asc[i] = 1.f;
-        if (m < p.M) {
-          arow[i] = p.A + static_cast<size_t>(p.a_rows ? p.a_rows[m] : m) * p.lda;
-          asc[i] = pow2f(rs[m]);
-        }
-      }
-      const uint16_t *bhi = w.hi + static_cast<size_t>(n0) * p.ldb;
-      const uint16_t *blo = w.lo + static_cast<size_t>(n0) * p.ldb;
-      for (int kt = 0; kt < nk; ++kt, ++it) {
-        const int s = it % kStages;
-        if (!wait_or_abort(empty0 + 8 * s, ((it / kStages) & 1) ^ 1, abort_flag)) {
-          ok = false;
-          break;
-        }
-        const uint32_t st = base + s * kStageBytes;
-        const uint32_t sAhi = st, sAlo = st + BM * 128, sBhi = st + 2 * BM * 128, sBlo = st + 3 * BM * 128;
-        const int k0 = kt * BK16 + pc * 8;
-#pragma unroll 4
-        for (int i = 0; i < BN / 16; ++i) {
-          const int r = pr + 16 * i;
-          const size_t off = static_cast<size_t>(r) * p.ldb + k0;
-          cp_async16(sBhi + swz(r, pc), bhi + off);
-          cp_async16(sBlo + swz(r, pc), blo + off);
-        }
-        float4 va[BM / 16][2];
-#pragma unroll
-        for (int i = 0; i < BM / 16; ++i) {
-          if (arow[i]) {
-            va[i][0] = *reinterpret_cast<const float4 *>(arow[i] + k0);
-            va[i][1] = *reinterpret_cast<const float4 *>(arow[i] + k0 + 4);
-          } else {
-            va[i][0] = va[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BNt;
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % C::Stages;
+          if (!wait_or_abort(empty0 + 8 * s, ((it / C::Stages) & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
           }
+          const uint32_t st = base + s * C::StageBytes;
+          const uint32_t fb = full0 + 8 * s;
+          mbar_expect_tx(fb, C::StageBytes);
+          tma_load_2d(st, &tAh, fb, kt * C::BK, m0);
+          tma_load_2d(st + C::ATile, &tAl, fb, kt * C::BK, m0);
+          tma_load_2d(st + 2 * C::ATile, &tBh, fb, kt * C::BK, n0);
+          tma_load_2d(st + 2 * C::ATile + C::BTile, &tBl, fb, kt * C::BK, n0);
         }
-#pragma unroll
-        for (int i = 0; i < BM / 16; ++i) {
-          const int r = pr + 16 * i;
-          uint4 h, l;
-          split_f16x8(va[i][0], va[i][1], asc[i], h, l);
-          *reinterpret_cast<uint4 *>(gbase + (sAhi - base) + swz(r, pc)) = h;
-          *reinterpret_cast<uint4 *>(gbase + (sAlo - base) + swz(r, pc)) = l;
-        }
-        cp_async_wait_all();
-        fence_proxy_async();
-        mbar_arrive(full0 + 8 * s);
       }
     }
-  } else if (warp == 4) {
+    __syncwarp();
+  } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16<BN>();
+      const uint32_t idesc = idesc_f16<BNt>();
       int it = 0, chunk = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-        for (int kt0 = 0; kt0 < nk && ok; kt0 += kChunk16, ++chunk) {
-          const int b = chunk & 1;
-          if (!wait_or_abort(acce0 + 8 * b, ((chunk >> 1) & 1) ^ 1, abort_flag)) {
+        for (int kt0 = 0; kt0 < nk && ok; kt0 += C::Chunk, ++chunk) {
+          const int b = chunk % C::TmemBufs;
+          if (!wait_or_abort(acce0 + 8 * b, ((chunk / C::TmemBufs) & 1) ^ 1, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t dtm = tmem + static_cast<uint32_t>(b * BN);
-          const int kend = kt0 + kChunk16 < nk ? kt0 + kChunk16 : nk;
-          for (int kt = kt0; kt < kend; ++kt, ++it) {
-            const int s = it % kStages;
-            if (!wait_or_abort(full0 + 8 * s, (it / kStages) & 1, abort_flag)) {
+          const uint32_t dtm = tmem + static_cast<uint32_t>(b * BNt);
+          for (int kt = kt0; kt < kt0 + C::Chunk; ++kt, ++it) {
+            const int s = it % C::Stages;
+            if (!wait_or_abort(full0 + 8 * s, (it / C::Stages) & 1, abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t st = base + s * kStageBytes;
-            const uint32_t sAhi = st, sAlo = st + BM * 128, sBhi = st + 2 * BM * 128, sBlo = st + 3 * BM * 128;
+            const uint32_t st = base + s * C::StageBytes;
+            const uint32_t sAhi = st, sAlo = st + C::ATile, sBhi = st + 2 * C::ATile,
+                           sBlo = st + 2 * C::ATile + C::BTile;
 #pragma unroll
-            for (int kk = 0; kk < BK16 / 16; ++kk) {
+            for (int kk = 0; kk < C::BK / 16; ++kk) {
               const uint32_t ko = kk * 32;  // 16 fp16 = 32 bytes per MMA k-step
-              mma_f16(dtm, sw128_desc(sAlo + ko), sw128_desc(sBhi + ko), idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
-              mma_f16(dtm, sw128_desc(sAhi + ko), sw128_desc(sBlo + ko), idesc, 1u);
-              mma_f16(dtm, sw128_desc(sAhi + ko), sw128_desc(sBhi + ko), idesc, 1u);
+              mma_f16(dtm, kmajor_desc<C>(sAlo + ko), kmajor_desc<C>(sBhi + ko), idesc,
+                      (kt > kt0 || kk > 0) ? 1u : 0u);
+              mma_f16(dtm, kmajor_desc<C>(sAhi + ko), kmajor_desc<C>(sBlo + ko), idesc, 1u);
+              mma_f16(dtm, kmajor_desc<C>(sAhi + ko), kmajor_desc<C>(sBhi + ko), idesc, 1u);
             }
             mma_commit(empty0 + 8 * s);
           }
@@ -606,44 +624,46 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- accumulators + epilogue ----------------
+    // ------- accumulators + epilogue: warp -> (TMEM lane quarter, 128-column half) -------
     const int q = warp & 3;
-    const float sb = pow2f(-w.b_scale);
+    const int h = (warp - 2) / 4;
+    const float sb = pow2f(-b_scale);
     int chunk = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-      const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
-      float acc[BN];
+      const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BNt + h * 128;
+      const int row = m0 + q * 32 + lane;
+      float acc[128];
 #pragma unroll
-      for (int j = 0; j < BN; ++j) acc[j] = 0.f;
-      for (int kt0 = 0; kt0 < nk; kt0 += kChunk16, ++chunk) {
-        const int b = chunk & 1;
-        if (!wait_or_abort(accf0 + 8 * b, (chunk >> 1) & 1, abort_flag)) {
+      for (int j = 0; j < 128; ++j) acc[j] = 0.f;
+      for (int kt0 = 0; kt0 < nk; kt0 += C::Chunk, ++chunk) {
+        const int b = chunk % C::TmemBufs;
+        const float sa = row < p.M ? pow2f(-static_cast<int>(sc[static_cast<size_t>(kt0 / C::Chunk) * p.M + row])) : 0.f;
+        if (!wait_or_abort(accf0 + 8 * b, (chunk / C::TmemBufs) & 1, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BN);
+        const uint32_t taddr =
+            tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BNt + h * 128);
 #pragma unroll
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        for (int c0 = 0; c0 < 128; c0 += 32) {
           float v[32];
           tmem_ld32(taddr + c0, v);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[c0 + j] = __fadd_rn(acc[c0 + j], v[j]);
+          for (int j = 0; j < 32; ++j) acc[c0 + j] = __fmaf_rn(v[j], sa, acc[c0 + j]);
         }
         tc_fence_before();
         mbar_arrive(acce0 + 8 * b);
       }
-      const int row = m0 + q * 32 + lane;
-      if (ok) epilogue_store<EPI, true>(p, row, n0, acc, row < p.M ? pow2f(-rs[row]) : 1.f, sb);
+      if (ok) epilogue_store<EPI, true>(p, row, n0, acc, 1.f, sb);
     }
   }
 
   tc_fence_before();
   __syncthreads();
   if (tid == 0 && *abort_flag) atomicExch(err, 1);
-  if (warp == 4)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
 }
 
 int g_num_sms = 0;
@@ -662,20 +682,61 @@ void launch(const GemmArgs &a, const TCWeights &w, int *err, cudaStream_t s) {
   CUDA_LAUNCH_CHECK();
 }
 
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+// MLIPCPP_B200_F16_TILE=128 keeps the 128-wide tile for every N
+const int g_f16_bn = [] {
+  const char *e = std::getenv("MLIPCPP_B200_F16_TILE");
+  return e ? std::atoi(e) : 256;
+}();
+
+// Row-major [rows, cols] fp16 matrix with leading dimension ld (elements):
+// boxes of box_k x box_rows, 128- or 64-byte swizzle, zero fill outside.
+CUtensorMap make_map_f16(const void *ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_k,
+                         uint32_t box_rows) {
+  if (!g_encode_tiled) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+    if (!fn || q != cudaDriverEntryPointSuccess) throw Error(kErrBackend, "cuTensorMapEncodeTiled unavailable");
+    g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld * 2};
+  const cuuint32_t box[2] = {box_k, box_rows};
+  const cuuint32_t es[2] = {1, 1};
+  const CUtensorMapSwizzle sw = box_k * 2 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const CUresult r = g_encode_tiled(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(ptr), dims, strides,
+                                    box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Error(kErrBackend, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return m;
+}
+
+template <int EPI, int BNt>
+void launch16_bn(const GemmArgs &a, const TCWeights16 &w, const Split16 &sp, int *err, cudaStream_t s) {
+  using C = F16Cfg<BNt>;
+  const CUtensorMap ah = make_map_f16(sp.hi, a.M, a.K, a.K, C::BK, BM), al = make_map_f16(sp.lo, a.M, a.K, a.K, C::BK, BM);
+  const CUtensorMap bh = make_map_f16(w.hi, a.N, a.K, a.ldb, C::BK, BNt),
+                    bl = make_map_f16(w.lo, a.N, a.K, a.ldb, C::BK, BNt);
+  CUDA_CHECK(cudaFuncSetAttribute(k_gemm_3xf16<EPI, BNt>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::Smem));
+  const int tiles = ceil_div(a.M, BM) * (a.N / BNt);
+  const int grid = tiles < g_num_sms ? tiles : g_num_sms;
+  k_gemm_3xf16<EPI, BNt><<<grid, C::Threads, C::Smem, s>>>(ah, al, bh, bl, a, sp.sc, w.b_scale, err);
+  CUDA_LAUNCH_CHECK();
+}
+
 template <int EPI>
-void launch16(const GemmArgs &a, const TCWeights16 &w, int *rs, int *err, cudaStream_t s) {
+void launch16(const GemmArgs &a, const TCWeights16 &w, const Split16 &sp, int *err, cudaStream_t s) {
   if (g_num_sms == 0) {
     int dev = 0;
     CUDA_CHECK(cudaGetDevice(&dev));
     CUDA_CHECK(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev));
   }
-  k_row_scale<<<ceil_div(a.M, 8), 256, 0, s>>>(a.A, a.lda, a.a_rows, a.M, a.K, rs);
+  k_split_a<<<ceil_div(a.M, 8), 256, 0, s>>>(a.A, a.lda, a.a_rows, a.M, a.K, sp.hi, sp.lo, sp.sc);
   CUDA_LAUNCH_CHECK();
-  CUDA_CHECK(cudaFuncSetAttribute(k_gemm_3xf16<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-  const int tiles = ceil_div(a.M, BM) * (a.N / BN);
-  const int grid = tiles < g_num_sms ? tiles : g_num_sms;
-  k_gemm_3xf16<EPI><<<grid, kWsThreads, kSmemBytes, s>>>(a, w, rs, err);
-  CUDA_LAUNCH_CHECK();
+  if (a.N % 256 == 0 && g_f16_bn != 128) launch16_bn<EPI, 256>(a, w, sp, err, s);
+  else launch16_bn<EPI, 128>(a, w, sp, err, s);
 }
 
 }  // namespace
@@ -690,18 +751,19 @@ int f16_scale_exponent(float mx) {
 }
 
 bool gemm_f16_supported(const GemmArgs &a) {
-  return gemm_tc_supported(a) && a.K % BK16 == 0 && a.ldb % 8 == 0;
+  return gemm_tc_supported(a) && a.K % kSBlock == 0 && a.K <= kSBlock * kMaxSBlocks && a.ldb % 8 == 0;
 }
 
-void gemm_3xf16(const GemmArgs &a, const TCWeights16 &w, int *rs, int *err, cudaStream_t s) {
-  if (reinterpret_cast<uintptr_t>(w.hi) % 16 || reinterpret_cast<uintptr_t>(w.lo) % 16)
-    throw Error(kErrInternal, "gemm_3xf16: fp16 weight copies not 16-byte aligned");
+void gemm_3xf16(const GemmArgs &a, const TCWeights16 &w, const Split16 &sp, int *err, cudaStream_t s) {
+  if (reinterpret_cast<uintptr_t>(w.hi) % 16 || reinterpret_cast<uintptr_t>(w.lo) % 16 ||
+      reinterpret_cast<uintptr_t>(sp.hi) % 16 || reinterpret_cast<uintptr_t>(sp.lo) % 16)
+    throw Error(kErrInternal, "gemm_3xf16: fp16 operands not 16-byte aligned");
   switch (a.epi) {
-    case EPI_STORE: launch16<EPI_STORE>(a, w, rs, err, s); break;
-    case EPI_SILU: launch16<EPI_SILU>(a, w, rs, err, s); break;
-    case EPI_ACCUM: launch16<EPI_ACCUM>(a, w, rs, err, s); break;
-    case EPI_DSILU: launch16<EPI_DSILU>(a, w, rs, err, s); break;
-    case EPI_RESID: launch16<EPI_RESID>(a, w, rs, err, s); break;
+    case EPI_STORE: launch16<EPI_STORE>(a, w, sp, err, s); break;
+    case EPI_SILU: launch16<EPI_SILU>(a, w, sp, err, s); break;
+    case EPI_ACCUM: launch16<EPI_ACCUM>(a, w, sp, err, s); break;
+    case EPI_DSILU: launch16<EPI_DSILU>(a, w, sp, err, s); break;
+    case EPI_RESID: launch16<EPI_RESID>(a, w, sp, err, s); break;
     default: throw Error(kErrInternal, "gemm_tc: bad epilogue");
   }
 }

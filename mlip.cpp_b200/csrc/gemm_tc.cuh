@@ -27,20 +27,28 @@ struct TCWeights16 {
 // True when the shape and alignment fit the tensor-core kernel (N multiple
 // of 128, K multiple of 32, 16-byte aligned rows).
 bool gemm_tc_supported(const GemmArgs &a);
-// True when the 3xFP16 kernel applies as well (K a multiple of 64, B rows
-// 16-byte aligned in fp16).
+// True when the 3xFP16 kernel applies as well (K a multiple of 128 and at
+// most 2048, B rows 16-byte aligned in fp16).
 bool gemm_f16_supported(const GemmArgs &a);
 
 // C = A B^T (+ epilogue) with 3xTF32 on tcgen05; `err` (device int) is set
 // non-zero if a pipeline wait times out.
 void gemm_3xtf32(const GemmArgs &a, const TCWeights &w, int *err, cudaStream_t s);
 
-// C = A B^T (+ epilogue) with 3xFP16 on tcgen05: each A row m is scaled by
-// 2^s_m (its largest |element| into [2^14, 2^15), computed by a pre-pass
-// into `row_scale`, device int[M]) and B by 2^b_scale, both split into fp16
-// hi + lo, and A B^T ~= (A_hi B_hi + A_hi B_lo + A_lo B_hi) 2^-(s_m + b_scale)
-// with fp32 accumulation.
-void gemm_3xf16(const GemmArgs &a, const TCWeights16 &w, int *row_scale, int *err, cudaStream_t s);
+// Scratch for the split-fp16 copy of A: hi and lo [M, K] fp16, sc
+// [K/128, M] int8 scale exponents (16-byte aligned).
+struct Split16 {
+  uint16_t *hi = nullptr;
+  uint16_t *lo = nullptr;
+  int8_t *sc = nullptr;
+};
+
+// C = A B^T (+ epilogue) with 3xFP16 on tcgen05: a pre-pass writes A
+// (row-gathered) as fp16 hi + lo scaled by 2^s per row and 128-element k
+// block (block max into [2^14, 2^15)); B is pre-split with one scale
+// 2^b_scale; A B^T ~= sum over blocks of (A_hi B_hi + A_hi B_lo + A_lo B_hi)
+// 2^-(s + b_scale), fp32 accumulation, operands streamed by TMA.
+void gemm_3xf16(const GemmArgs &a, const TCWeights16 &w, const Split16 &sp, int *err, cudaStream_t s);
 
 // Power-of-two scale exponent s with max|x| 2^s in [2^14, 2^15) (0 for an
 // all-zero tensor, clamped to [-120, 120]).

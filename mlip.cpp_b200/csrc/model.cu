@@ -155,7 +155,7 @@ const float *PETModel::w(const std::string &name) const {
 }
 
 size_t PETModel::device_bytes() const {
-  return wbuf_.cap + persist_.cap + scratch_.cap + nl_.center.cap * 10;
+  return wbuf_.cap + persist_.cap + scratch_.cap + split_.cap + nl_.center.cap * 10;
 }
 
 // ---------------------------------------------------------------------------
@@ -434,8 +434,11 @@ void PETModel::forward_backward(bool grad) {
     if (kprof_) mark_begin(e0);
     if (f16) {
       const uint16_t *h16 = reinterpret_cast<const uint16_t *>(wb + 3 * wspan_);
-      gemm_3xf16(g, TCWeights16{h16 + eoff, h16 + wspan_ + eoff, weight_scale(eoff)}, rscale_.as<int>(),
-                 d_err_.as<int>(), st);
+      const size_t mk = static_cast<size_t>(M) * K;
+      if (split_.cap < mk * 4 + mk / 128) throw Error(kErrInternal, "split-fp16 scratch too small");
+      uint16_t *sh = split_.as<uint16_t>();
+      const Split16 sp{sh, sh + mk, reinterpret_cast<int8_t *>(sh + 2 * mk)};
+      gemm_3xf16(g, TCWeights16{h16 + eoff, h16 + wspan_ + eoff, weight_scale(eoff)}, sp, d_err_.as<int>(), st);
     } else if (tc) {
       gemm_3xtf32(g, TCWeights{B + wspan_, B + 2 * wspan_}, d_err_.as<int>(), st);
     } else {
@@ -591,7 +594,11 @@ void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const in
   plan_memory(P, S, in_->a, h_, c, grad);
   persist_.ensure(P.off);
   scratch_.ensure(S.off);
-  rscale_.ensure(sizeof(int) * (static_cast<size_t>(std::max(Tl_[0], Tl_[1])) + 1));
+  if (use_f16_) {  // largest A operand of a 3xFP16 GEMM: [tokens, max(3d, ff, hid)]
+    const size_t kmax = static_cast<size_t>(std::max({3 * h_.d, h_.ff, h_.hid}));
+    const size_t mk = static_cast<size_t>(std::max(Tl_[0], Tl_[1])) * kmax;
+    split_.ensure(mk * 4 + mk / 128 + 256);
+  }
   P = Plan{persist_.as<char>(), 0};
   S = Plan{scratch_.as<char>(), 0};
   plan_memory(P, S, in_->a, h_, c, grad);

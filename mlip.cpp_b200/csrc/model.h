@@ -127,7 +127,7 @@ class PETModel {
   // one power-of-two scale per tensor: {first element, end element, scale}
   struct WScale { size_t begin, end; int scale; };
   std::vector<WScale> wscale_;
-  DevBuf rscale_;        // per-row scale exponents of the 3xFP16 pre-pass
+  DevBuf split_;         // split-fp16 copy of a 3xFP16 GEMM's A operand
   int weight_scale(size_t elem) const;
   DevBuf d_err_;         // device error word written by bounded waits
   std::map<std::string, const float *> wptr_;
