@@ -34,9 +34,14 @@ __host__ __device__ __forceinline__ int head_stride(int S, int hd) {
 size_t fwd_smem(int S, int hd, int hg) {
   return sizeof(float) * (2ull * hg * head_stride(S, hd) + S);
 }
+// Floats between consecutive heads' [S][S|1] P / dS matrices (16 mod 32).
+__host__ __device__ __forceinline__ int mat_stride(int S) {
+  const int n = S * (S | 1);
+  return n + ((16 - n % 32) + 32) % 32;
+}
 size_t bwd_smem(int S, int hd, int hg) {
-  const int ps = S | 1;
-  return sizeof(float) * (4ull * hg * head_stride(S, hd) + 2ull * hg * S * ps + S + static_cast<size_t>(hg) * S);
+  return sizeof(float) * (4ull * hg * head_stride(S, hd) + 2ull * hg * mat_stride(S) + S +
+                          static_cast<size_t>(hg) * S);
 }
 
 template <int HD>
@@ -65,17 +70,24 @@ __device__ __forceinline__ void axpy_row(float (&o)[HD], float p, const float *_
   }
 }
 
-// Cooperative float4 copy of the (token, head-group) block of one of q/k/v
-// (column offset `col`) or of a [T, d] array into smem laid out [HG][S][HD].
+// Cooperative asynchronous 16-byte copies (cp.async) of the (token,
+// head-group) block of one of q/k/v (column offset `col`) or of a [T, d]
+// array into smem laid out [HG][S][HD]; every copy of the block is in flight
+// at once.  The caller commits and waits (cp_async_wait_all) before use.
 template <int HD>
 __device__ __forceinline__ void load_block(float *dst, const float *src, int ld, int col, int t0, int S,
                                            int hg) {
   const int per_row = HD / 4, per_head = S * per_row, n = hg * per_head, hs = head_stride(S, HD);
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int hh = i / per_head, rem = i - hh * per_head, k = rem / per_row, c = (rem - k * per_row) * 4;
-    *reinterpret_cast<float4 *>(dst + hh * hs + k * HD + c) =
-        *reinterpret_cast<const float4 *>(src + static_cast<size_t>(t0 + k) * ld + col + hh * HD + c);
+    const uint32_t d32 = static_cast<uint32_t>(__cvta_generic_to_shared(dst + hh * hs + k * HD + c));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d32),
+                 "l"(src + static_cast<size_t>(t0 + k) * ld + col + hh * HD + c)
+                 : "memory");
   }
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
 template <int HD>
@@ -91,6 +103,7 @@ __global__ void k_attn_fwd(AttnArgs a, int hg) {
   load_block<HD>(sK, a.qkv, ld, d + h0 * HD, t0, S, hg);
   load_block<HD>(sV, a.qkv, ld, 2 * d + h0 * HD, t0, S, hg);
   for (int k = threadIdx.x; k < S; k += blockDim.x) sM[k] = k == 0 ? 0.f : a.key_mask[e0 + k - 1];
+  cp_async_wait_all();
   __syncthreads();
   const int t = threadIdx.x;
   if (t >= hg * S) return;
@@ -138,9 +151,9 @@ __global__ void k_attn_bwd(AttnArgs a, int hg) {
   const int t0 = e0 + atom;
   const int d = a.d, ld = 3 * d;
   const int PS = S | 1;
-  const int hs = head_stride(S, HD);
+  const int hs = head_stride(S, HD), ms = mat_stride(S);
   float *sQ = sm, *sK = sQ + hg * hs, *sV = sK + hg * hs, *sG = sV + hg * hs;
-  float *sP = sG + hg * hs, *sD = sP + hg * S * PS, *sM = sD + hg * S * PS, *sL = sM + S;
+  float *sP = sG + hg * hs, *sD = sP + hg * ms, *sM = sD + hg * ms, *sL = sM + S;
   load_block<HD>(sQ, a.qkv, ld, h0 * HD, t0, S, hg);
   load_block<HD>(sK, a.qkv, ld, d + h0 * HD, t0, S, hg);
   load_block<HD>(sV, a.qkv, ld, 2 * d + h0 * HD, t0, S, hg);
@@ -150,13 +163,14 @@ __global__ void k_attn_bwd(AttnArgs a, int hg) {
     const int hh = i / S, q = i - hh * S;
     sL[i] = a.lse[static_cast<size_t>(t0 + q) * a.heads + h0 + hh];
   }
+  cp_async_wait_all();
   __syncthreads();
   const int t = threadIdx.x;
   const bool live = t < hg * S;
   const int hh = live ? t / S : 0, r = live ? t - hh * S : 0, h = h0 + hh;
   const float scale = 1.0f / sqrtf(static_cast<float>(HD));
   const float *Q = sQ + hh * hs, *K = sK + hh * hs, *V = sV + hh * hs, *G = sG + hh * hs;
-  float *P = sP + hh * S * PS, *Dm = sD + hh * S * PS;
+  float *P = sP + hh * ms, *Dm = sD + hh * ms;
   if (live) {
     // phase A: thread = query row r
     float qr[HD], g[HD], acc[HD];
