@@ -40,7 +40,7 @@ __host__ __device__ __forceinline__ int mat_stride(int S) {
   return n + ((16 - n % 32) + 32) % 32;
 }
 size_t bwd_smem(int S, int hd, int hg) {
-  return sizeof(float) * (4ull * hg * head_stride(S, hd) + 2ull * hg * mat_stride(S) + S +
+  return sizeof(float) * (2ull * hg * head_stride(S, hd) + 2ull * hg * mat_stride(S) + S +
                           static_cast<size_t>(hg) * S);
 }
 
@@ -142,6 +142,10 @@ __global__ void k_attn_fwd(AttnArgs a, int hg) {
 
 // dS = P (dP - rowsum(P dP)), dQ = s dS K, dK = s dS^T Q, dV = P^T dO.
 // The mask is a constant input in the reference (pet.cpp:274-275): no grad.
+// Phase A (thread = query row) needs K and V in shared memory and its own q
+// and dO rows in registers; phase B (thread = key row) needs Q and dO.  The
+// two phases share one [2][HG][S][HD] region (K, V then Q, dO), so a CTA
+// holds two row blocks and the P / dS matrices.
 template <int HD>
 __global__ void k_attn_bwd(AttnArgs a, int hg) {
   extern __shared__ __align__(16) float sm[];
@@ -152,38 +156,43 @@ __global__ void k_attn_bwd(AttnArgs a, int hg) {
   const int d = a.d, ld = 3 * d;
   const int PS = S | 1;
   const int hs = head_stride(S, HD), ms = mat_stride(S);
-  float *sQ = sm, *sK = sQ + hg * hs, *sV = sK + hg * hs, *sG = sV + hg * hs;
-  float *sP = sG + hg * hs, *sD = sP + hg * ms, *sM = sD + hg * ms, *sL = sM + S;
-  load_block<HD>(sQ, a.qkv, ld, h0 * HD, t0, S, hg);
-  load_block<HD>(sK, a.qkv, ld, d + h0 * HD, t0, S, hg);
-  load_block<HD>(sV, a.qkv, ld, 2 * d + h0 * HD, t0, S, hg);
-  load_block<HD>(sG, a.d_out, d, h0 * HD, t0, S, hg);
+  float *sA = sm, *sB = sA + hg * hs;  // K, V (phase A) then Q, dO (phase B)
+  float *sP = sB + hg * hs, *sD = sP + hg * ms, *sM = sD + hg * ms, *sL = sM + S;
+  load_block<HD>(sA, a.qkv, ld, d + h0 * HD, t0, S, hg);
+  load_block<HD>(sB, a.qkv, ld, 2 * d + h0 * HD, t0, S, hg);
   for (int k = threadIdx.x; k < S; k += blockDim.x) sM[k] = k == 0 ? 0.f : a.key_mask[e0 + k - 1];
   for (int i = threadIdx.x; i < hg * S; i += blockDim.x) {
     const int hh = i / S, q = i - hh * S;
     sL[i] = a.lse[static_cast<size_t>(t0 + q) * a.heads + h0 + hh];
   }
-  cp_async_wait_all();
-  __syncthreads();
   const int t = threadIdx.x;
   const bool live = t < hg * S;
   const int hh = live ? t / S : 0, r = live ? t - hh * S : 0, h = h0 + hh;
   const float scale = 1.0f / sqrtf(static_cast<float>(HD));
-  const float *Q = sQ + hh * hs, *K = sK + hh * hs, *V = sV + hh * hs, *G = sG + hh * hs;
+  float qr[HD], g[HD];
+  if (live) {
+    const float *qs = a.qkv + static_cast<size_t>(t0 + r) * ld + h * HD;
+    const float *gs = a.d_out + static_cast<size_t>(t0 + r) * d + h * HD;
+#pragma unroll
+    for (int c = 0; c < HD; c += 4) {
+      const float4 v = *reinterpret_cast<const float4 *>(qs + c);
+      const float4 w = *reinterpret_cast<const float4 *>(gs + c);
+      qr[c] = v.x; qr[c + 1] = v.y; qr[c + 2] = v.z; qr[c + 3] = v.w;
+      g[c] = w.x; g[c + 1] = w.y; g[c + 2] = w.z; g[c + 3] = w.w;
+    }
+  }
+  cp_async_wait_all();
+  __syncthreads();
   float *P = sP + hh * ms, *Dm = sD + hh * ms;
   if (live) {
     // phase A: thread = query row r
-    float qr[HD], g[HD], acc[HD];
+    const float *K = sA + hh * hs, *V = sB + hh * hs;
+    float acc[HD];
 #pragma unroll
-    for (int c = 0; c < HD; c += 4) {
-      const float4 v = *reinterpret_cast<const float4 *>(Q + r * HD + c);
-      const float4 w = *reinterpret_cast<const float4 *>(G + r * HD + c);
-      qr[c] = v.x; qr[c + 1] = v.y; qr[c + 2] = v.z; qr[c + 3] = v.w;
-      g[c] = w.x; g[c + 1] = w.y; g[c + 2] = w.z; g[c + 3] = w.w;
-      acc[c] = acc[c + 1] = acc[c + 2] = acc[c + 3] = 0.f;
-    }
+    for (int c = 0; c < HD; ++c) acc[c] = 0.f;
     const float lse = sL[hh * S + r];
     float D = 0.f;
+#pragma unroll 2
     for (int k = 0; k < S; ++k) {
       const float p = expf(dot_row<HD>(qr, K + k * HD) * scale + sM[k] - lse);
       const float dp = dot_row<HD>(g, V + k * HD);
@@ -191,6 +200,7 @@ __global__ void k_attn_bwd(AttnArgs a, int hg) {
       Dm[r * PS + k] = dp;
       D = fmaf(p, dp, D);
     }
+#pragma unroll 2
     for (int k = 0; k < S; ++k) {
       const float ds = P[r * PS + k] * (Dm[r * PS + k] - D);
       Dm[r * PS + k] = ds;
@@ -202,12 +212,18 @@ __global__ void k_attn_bwd(AttnArgs a, int hg) {
       *reinterpret_cast<float4 *>(dq + c) =
           make_float4(acc[c] * scale, acc[c + 1] * scale, acc[c + 2] * scale, acc[c + 3] * scale);
   }
+  __syncthreads();  // K and V no longer read: bring in Q and dO
+  load_block<HD>(sA, a.qkv, ld, h0 * HD, t0, S, hg);
+  load_block<HD>(sB, a.d_out, d, h0 * HD, t0, S, hg);
+  cp_async_wait_all();
   __syncthreads();
   if (live) {
     // phase B: thread = key row r
+    const float *Q = sA + hh * hs, *G = sB + hh * hs;
     float dk[HD], dv[HD];
 #pragma unroll
     for (int c = 0; c < HD; ++c) dk[c] = dv[c] = 0.f;
+#pragma unroll 2
     for (int q = 0; q < S; ++q) {
       axpy_row<HD>(dk, Dm[q * PS + r], Q + q * HD);
       axpy_row<HD>(dv, P[q * PS + r], G + q * HD);
