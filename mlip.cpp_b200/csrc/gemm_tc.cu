@@ -666,6 +666,248 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
 }
 
+// ---------------------------------------------------------------------------
+// 3xFP16 on an SM pair (cta_group::2): cluster of 2 CTAs, tile 256 x 256.
+// Each CTA streams its own 128 rows of A and one 128-row half of B into its
+// shared memory (32 KB per k-tile of 32, 6 stages); the leader CTA (rank 0)
+// issues M = 256 MMAs that read both CTAs' operands and accumulate each
+// CTA's 128 rows in its own tensor memory.  Both CTAs' TMA loads complete on
+// the leader's stage barrier; MMA commits arrive on the barriers of both
+// CTAs; the peer's accumulator warps release a TMEM buffer by arriving on the
+// leader's barrier.  No load uses multicast.
+// ---------------------------------------------------------------------------
+struct PairCfg {
+  static constexpr int BK = 32;                       // fp16 k per tile (64-byte rows)
+  static constexpr int RowBytes = 64;
+  static constexpr int ATile = BM * RowBytes;         // this CTA's 128 A rows
+  static constexpr int BTile = 128 * RowBytes;        // this CTA's half of the 256 B rows
+  static constexpr int StageBytes = 2 * ATile + 2 * BTile;  // 32 KB
+  static constexpr int Stages = 6;
+  static constexpr int Chunk = kSBlock / BK;          // 4 k-tiles per TMEM pass
+  static constexpr int TmemBufs = 2;                  // 2 x 256 columns
+  static constexpr int AccWarps = 8;
+  static constexpr int Threads = 64 + 32 * AccWarps;  // 320
+  static constexpr uint32_t Sbo = 8 * RowBytes;
+  static constexpr uint64_t Layout = 4;               // SWIZZLE_64B
+  static constexpr int Smem = Stages * StageBytes + 1024 + 256;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t num_clusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared variable in CTA `rank`
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// TMA load into this CTA's shared memory that completes on a (possibly peer) barrier.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, uint32_t bar_cluster, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void mma_f16_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+// Commit of the leader's MMAs, arriving on the barrier at `bar` in both CTAs.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+      ::"r"(bar), "h"(mask)
+      : "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(384, 1)
+    k_gemm_3xf16_pair(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
+                      const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
+                      GemmArgs p, const int8_t *__restrict__ sc, int b_scale, int *err) {
+  using C = PairCfg;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t *gbase = smem_raw + (base - raw);
+  const uint32_t bars = base + C::Stages * C::StageBytes;
+  // mbarriers: full[Stages], empty[Stages], accf[2], acce[2] (same offsets in both CTAs)
+  const uint32_t full0 = bars, empty0 = bars + 8 * C::Stages, accf0 = bars + 16 * C::Stages,
+                 acce0 = accf0 + 8 * C::TmemBufs;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + C::Stages * C::StageBytes + 192);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(gbase + C::Stages * C::StageBytes + 200);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int nk = p.K / C::BK;
+  const int tiles_n = p.N / 256;
+  const int tiles = ((p.M + 255) / 256) * tiles_n;
+  const int pair = static_cast<int>(cluster_id_x()), npairs = static_cast<int>(num_clusters_x());
+
+  if (tid == 0) {
+    for (int s = 0; s < C::Stages; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < C::TmemBufs; ++b) {
+      mbar_init(accf0 + 8 * b, 1);
+      mbar_init(acce0 + 8 * b, 2 * 32 * C::AccWarps);  // both CTAs' accumulator threads
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers and tensor memory of both CTAs exist before any cross-CTA use
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < tiles && ok; tile += npairs) {
+        const int m0 = (tile / tiles_n) * 256 + static_cast<int>(rank) * BM;
+        const int n0 = (tile % tiles_n) * 256 + static_cast<int>(rank) * 128;
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % C::Stages;
+          if (!wait_or_abort(empty0 + 8 * s, ((it / C::Stages) & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t st = base + s * C::StageBytes;
+          const uint32_t fb = map_to_rank(full0 + 8 * s, 0);
+          if (leader) mbar_expect_tx(full0 + 8 * s, 2 * C::StageBytes);
+          tma_load_2d_pair(st, &tAh, fb, kt * C::BK, m0);
+          tma_load_2d_pair(st + C::ATile, &tAl, fb, kt * C::BK, m0);
+          tma_load_2d_pair(st + 2 * C::ATile, &tBh, fb, kt * C::BK, n0);
+          tma_load_2d_pair(st + 2 * C::ATile + C::BTile, &tBl, fb, kt * C::BK, n0);
+        }
+      }
+      // tail: wait for the commits that free the last stages, so that no
+      // MMA-commit arrival is still headed for this CTA when it exits
+      for (int i = it; ok && i < it + C::Stages; ++i) {
+        const int s = i % C::Stages;
+        ok = wait_or_abort(empty0 + 8 * s, ((i / C::Stages) & 1) ^ 1, abort_flag);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA only) ----------------
+    if (leader && lane == 0) {
+      const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(256 >> 3) << 17) | (static_cast<uint32_t>(256 >> 4) << 24);
+      int it = 0, chunk = 0;
+      bool ok = true;
+      for (int tile = pair; tile < tiles && ok; tile += npairs) {
+        for (int kt0 = 0; kt0 < nk && ok; kt0 += C::Chunk, ++chunk) {
+          const int b = chunk % C::TmemBufs;
+          if (!wait_or_abort(acce0 + 8 * b, ((chunk / C::TmemBufs) & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t dtm = tmem + static_cast<uint32_t>(b * 256);
+          for (int kt = kt0; kt < kt0 + C::Chunk; ++kt, ++it) {
+            const int s = it % C::Stages;
+            if (!wait_or_abort(full0 + 8 * s, (it / C::Stages) & 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t st = base + s * C::StageBytes;
+            const uint32_t sAhi = st, sAlo = st + C::ATile, sBhi = st + 2 * C::ATile,
+                           sBlo = st + 2 * C::ATile + C::BTile;
+#pragma unroll
+            for (int kk = 0; kk < C::BK / 16; ++kk) {
+              const uint32_t ko = kk * 32;
+              mma_f16_pair(dtm, kmajor_desc<C>(sAlo + ko), kmajor_desc<C>(sBhi + ko), idesc,
+                           (kt > kt0 || kk > 0) ? 1u : 0u);
+              mma_f16_pair(dtm, kmajor_desc<C>(sAhi + ko), kmajor_desc<C>(sBlo + ko), idesc, 1u);
+              mma_f16_pair(dtm, kmajor_desc<C>(sAhi + ko), kmajor_desc<C>(sBhi + ko), idesc, 1u);
+            }
+            mma_commit_pair(empty0 + 8 * s);
+          }
+          if (ok) mma_commit_pair(accf0 + 8 * b);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------- accumulators + epilogue (both CTAs): warp -> (lane quarter, column half) -------
+    const int q = warp & 3;
+    const int h = (warp - 2) / 4;
+    const float sb = pow2f(-b_scale);
+    int chunk = 0;
+    bool ok = true;
+    for (int tile = pair; tile < tiles && ok; tile += npairs) {
+      const int m0 = (tile / tiles_n) * 256 + static_cast<int>(rank) * BM;
+      const int n0 = (tile % tiles_n) * 256 + h * 128;
+      const int row = m0 + q * 32 + lane;
+      float acc[128];
+#pragma unroll
+      for (int j = 0; j < 128; ++j) acc[j] = 0.f;
+      for (int kt0 = 0; kt0 < nk; kt0 += C::Chunk, ++chunk) {
+        const int b = chunk % C::TmemBufs;
+        const float sa = row < p.M ? pow2f(-static_cast<int>(sc[static_cast<size_t>(kt0 / C::Chunk) * p.M + row])) : 0.f;
+        if (!wait_or_abort(accf0 + 8 * b, (chunk / C::TmemBufs) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t taddr =
+            tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * 256 + h * 128);
+#pragma unroll
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          float v[32];
+          tmem_ld32(taddr + c0, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[c0 + j] = __fmaf_rn(v[j], sa, acc[c0 + j]);
+        }
+        tc_fence_before();
+        mbar_arrive_cluster(map_to_rank(acce0 + 8 * b, 0));
+      }
+      if (ok) epilogue_store<EPI, true>(p, row, n0, acc, 1.f, sb);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && *abort_flag) atomicExch(err, 1);
+  cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+  tc_fence_after();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+}
+
 int g_num_sms = 0;
 
 template <int EPI>
@@ -683,7 +925,8 @@ void launch(const GemmArgs &a, const TCWeights &w, int *err, cudaStream_t s) {
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
-// MLIPCPP_B200_F16_TILE=128 keeps the 128-wide tile for every N
+// MLIPCPP_B200_F16_TILE: 128 keeps the 128-wide tile for every N, 256 the
+// one-SM 128 x 256 tile, 512 the SM-pair 256 x 256 tile
 const int g_f16_bn = [] {
   const char *e = std::getenv("MLIPCPP_B200_F16_TILE");
   return e ? std::atoi(e) : 256;
@@ -727,6 +970,33 @@ void launch16_bn(const GemmArgs &a, const TCWeights16 &w, const Split16 &sp, int
 }
 
 template <int EPI>
+void launch16_pair(const GemmArgs &a, const TCWeights16 &w, const Split16 &sp, int *err, cudaStream_t s) {
+  using C = PairCfg;
+  const CUtensorMap ah = make_map_f16(sp.hi, a.M, a.K, a.K, C::BK, BM), al = make_map_f16(sp.lo, a.M, a.K, a.K, C::BK, BM);
+  const CUtensorMap bh = make_map_f16(w.hi, a.N, a.K, a.ldb, C::BK, 128),
+                    bl = make_map_f16(w.lo, a.N, a.K, a.ldb, C::BK, 128);
+  CUDA_CHECK(cudaFuncSetAttribute(k_gemm_3xf16_pair<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::Smem));
+  const int tiles = ceil_div(a.M, 256) * (a.N / 256);
+  int pairs = g_num_sms / 2;
+  if (tiles < pairs) pairs = tiles;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(C::Threads);
+  cfg.dynamicSmemBytes = C::Smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_gemm_3xf16_pair<EPI>, ah, al, bh, bl, a,
+                                static_cast<const int8_t *>(sp.sc), w.b_scale, err));
+  ::pet::g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+template <int EPI>
 void launch16(const GemmArgs &a, const TCWeights16 &w, const Split16 &sp, int *err, cudaStream_t s) {
   if (g_num_sms == 0) {
     int dev = 0;
@@ -735,7 +1005,8 @@ void launch16(const GemmArgs &a, const TCWeights16 &w, const Split16 &sp, int *e
   }
   k_split_a<<<ceil_div(a.M, 8), 256, 0, s>>>(a.A, a.lda, a.a_rows, a.M, a.K, sp.hi, sp.lo, sp.sc);
   CUDA_LAUNCH_CHECK();
-  if (a.N % 256 == 0 && g_f16_bn != 128) launch16_bn<EPI, 256>(a, w, sp, err, s);
+  if (a.N % 256 == 0 && g_f16_bn == 512) launch16_pair<EPI>(a, w, sp, err, s);
+  else if (a.N % 256 == 0 && g_f16_bn != 128) launch16_bn<EPI, 256>(a, w, sp, err, s);
   else launch16_bn<EPI, 128>(a, w, sp, err, s);
 }
 
