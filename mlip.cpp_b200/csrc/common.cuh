@@ -102,6 +102,12 @@ __device__ __forceinline__ float dsilu_f(float z) {
   float s = 1.0f / (1.0f + expf(-z));
   return s * (1.0f + z * (1.0f - s));
 }
+// silu(z) and silu'(z) from one exponential and one reciprocal
+__device__ __forceinline__ void silu_pair(float z, float &y, float &dy) {
+  const float s = __frcp_rn(1.0f + expf(-z));
+  y = z * s;
+  dy = s * (1.0f + z * (1.0f - s));
+}
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

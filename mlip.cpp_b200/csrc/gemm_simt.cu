@@ -92,12 +92,14 @@ __global__ void __launch_bounds__(256) k_gemm_f32(GemmArgs p) {
         if (EPI == EPI_STORE) {
           crow[n] = v;
         } else if (EPI == EPI_SILU) {
-          p.Z[static_cast<size_t>(m) * p.ldz + n] = v;
-          crow[n] = silu_f(v);
+          float y, dy;
+          silu_pair(v, y, dy);
+          p.Z[static_cast<size_t>(m) * p.ldz + n] = dy;
+          crow[n] = y;
         } else if (EPI == EPI_ACCUM) {
           crow[n] += v;
         } else if (EPI == EPI_DSILU) {
-          crow[n] = v * dsilu_f(p.Z[static_cast<size_t>(m) * p.ldz + n]);
+          crow[n] = v * p.Z[static_cast<size_t>(m) * p.ldz + n];
         } else {  // EPI_RESID
           crow[n] = v + p.R[static_cast<size_t>(rc) * p.ldr + n];
         }

@@ -216,33 +216,53 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs &p, int row, int n
   if (row >= p.M) return;
   const int rc = p.c_rows ? p.c_rows[row] : row;
   float *crow = p.C + static_cast<size_t>(rc) * p.ldc;
+  const float *zrow = (EPI == EPI_SILU || EPI == EPI_DSILU) ? p.Z + static_cast<size_t>(row) * p.ldz : nullptr;
+  const float *rrow = EPI == EPI_RESID ? p.R + static_cast<size_t>(rc) * p.ldr : nullptr;
+  // 32 columns at a time: all loads of a group (bias, Z or R, C for ACCUM)
+  // are issued before its stores, so a thread waits on memory once per group
 #pragma unroll
-  for (int j = 0; j < BN; j += 4) {
-    const int n = n0 + j;
-    float4 x = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-    if (kScaled) {  // two exact power-of-two multiplies
-      x.x = (x.x * s_row) * s_b; x.y = (x.y * s_row) * s_b;
-      x.z = (x.z * s_row) * s_b; x.w = (x.w * s_row) * s_b;
+  for (int g = 0; g < BN; g += 32) {
+    float4 x[8], ld[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int j = g + 4 * k;
+      x[k] = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+      if (kScaled) {  // two exact power-of-two multiplies
+        x[k].x = (x[k].x * s_row) * s_b; x[k].y = (x[k].y * s_row) * s_b;
+        x[k].z = (x[k].z * s_row) * s_b; x[k].w = (x[k].w * s_row) * s_b;
+      }
     }
     if (p.bias) {
-      const float4 b = *reinterpret_cast<const float4 *>(p.bias + n);
-      x.x += b.x; x.y += b.y; x.z += b.z; x.w += b.w;
+      float4 b[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) b[k] = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + g + 4 * k));
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        x[k].x += b[k].x; x[k].y += b[k].y; x[k].z += b[k].z; x[k].w += b[k].w;
+      }
     }
-    float4 *dst = reinterpret_cast<float4 *>(crow + n);
-    if (EPI == EPI_STORE) {
-      *dst = x;
-    } else if (EPI == EPI_SILU) {
-      *reinterpret_cast<float4 *>(p.Z + static_cast<size_t>(row) * p.ldz + n) = x;
-      *dst = make_float4(silu_f(x.x), silu_f(x.y), silu_f(x.z), silu_f(x.w));
-    } else if (EPI == EPI_ACCUM) {
-      const float4 o = *dst;
-      *dst = make_float4(o.x + x.x, o.y + x.y, o.z + x.z, o.w + x.w);
-    } else if (EPI == EPI_DSILU) {
-      const float4 z = *reinterpret_cast<const float4 *>(p.Z + static_cast<size_t>(row) * p.ldz + n);
-      *dst = make_float4(x.x * dsilu_f(z.x), x.y * dsilu_f(z.y), x.z * dsilu_f(z.z), x.w * dsilu_f(z.w));
-    } else {  // EPI_RESID
-      const float4 r = *reinterpret_cast<const float4 *>(p.R + static_cast<size_t>(rc) * p.ldr + n);
-      *dst = make_float4(x.x + r.x, x.y + r.y, x.z + r.z, x.w + r.w);
+    if (EPI == EPI_DSILU || EPI == EPI_RESID || EPI == EPI_ACCUM) {
+      const float *src = EPI == EPI_DSILU ? zrow : EPI == EPI_RESID ? rrow : crow;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ld[k] = *reinterpret_cast<const float4 *>(src + n0 + g + 4 * k);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int n = n0 + g + 4 * k;
+      float4 *dst = reinterpret_cast<float4 *>(crow + n);
+      if (EPI == EPI_STORE) {
+        *dst = x[k];
+      } else if (EPI == EPI_SILU) {
+        float4 y, dy;
+        silu_pair(x[k].x, y.x, dy.x); silu_pair(x[k].y, y.y, dy.y);
+        silu_pair(x[k].z, y.z, dy.z); silu_pair(x[k].w, y.w, dy.w);
+        *reinterpret_cast<float4 *>(const_cast<float *>(zrow) + n) = dy;
+        *dst = y;
+      } else if (EPI == EPI_DSILU) {
+        *dst = make_float4(x[k].x * ld[k].x, x[k].y * ld[k].y, x[k].z * ld[k].z, x[k].w * ld[k].w);
+      } else {  // EPI_RESID, EPI_ACCUM: x + R or x + C
+        *dst = make_float4(x[k].x + ld[k].x, x[k].y + ld[k].y, x[k].z + ld[k].z, x[k].w + ld[k].w);
+      }
     }
   }
 }

@@ -121,7 +121,7 @@ __global__ void k_head_last_bwd(const float *__restrict__ z, const float *__rest
        t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int m = static_cast<int>(t / r), c = static_cast<int>(t % r);
     const float sc = scale ? scale[m] : 1.0f;
-    dz[t] = w[c] * dsilu_f(z[t]) * sc;
+    dz[t] = w[c] * z[t] * sc;  // z holds silu' from the forward
   }
 }
 

@@ -40,7 +40,8 @@ void node_tokens(const float *table, const int *species, const int *node_row, fl
 // pred[m] = dot(y[m, :], w) + b
 void head_last(const float *y, const float *w, const float *b, float *pred, int rows, int r,
                cudaStream_t s);
-// dz[m, c] = w[c] silu'(z[m, c]) scale[m]   (scale null -> 1)
+// dz[m, c] = w[c] z[m, c] scale[m], z = silu' of the forward pre-activation
+// (scale null -> 1)
 void head_last_bwd(const float *z, const float *w, const float *scale, float *dz, int rows, int r,
                    cudaStream_t s);
 // e_atom[i] (+)= node_pred[i] + sum_{e in i} edge_pred[e] fc[e]
