@@ -13,6 +13,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "split16.cuh"
 
 namespace pet {
 namespace {
@@ -32,16 +33,39 @@ __host__ __device__ __forceinline__ int head_stride(int S, int hd) {
   return n + ((16 - n % 32) + 32) % 32;
 }
 size_t fwd_smem(int S, int hd, int hg) {
-  return sizeof(float) * (2ull * hg * head_stride(S, hd) + S);
+  return sizeof(float) * (2ull * hg * head_stride(S, hd) + S + static_cast<size_t>(hg) * S);
 }
 // Floats between consecutive heads' [S][S|1] P / dS matrices (16 mod 32).
 __host__ __device__ __forceinline__ int mat_stride(int S) {
   const int n = S * (S | 1);
   return n + ((16 - n % 32) + 32) % 32;
 }
+// [2][HG] row blocks, P and dS, key mask [S], log-sum-exp [HG][S] and the
+// three [HG][S] arrays of the split outputs' block maxima
 size_t bwd_smem(int S, int hd, int hg) {
   return sizeof(float) * (2ull * hg * head_stride(S, hd) + 2ull * hg * mat_stride(S) + S +
-                          static_cast<size_t>(hg) * S);
+                          4ull * hg * S);
+}
+
+// Split-fp16 output of a (row, head-group) block: each of the HG threads of
+// `row` holds its head's HD values; `mx` (smem, [HG][S]) has been filled with
+// every thread's max |value| and synchronised.  Writes the block's split form.
+template <int HD>
+__device__ __forceinline__ void group_split_store(const Split16View &o, int row, int col, int blk, const float *mx,
+                                                  int hg, int S, int r, int hh, float (&v)[HD]) {
+  float m = 0.f;
+  for (int k = 0; k < hg; ++k) m = fmaxf(m, mx[k * S + r]);
+  const int s = split_scale_exponent(m);
+  thread_split_store<HD>(o, row, col, v, s);
+  if (hh == 0) o.sc[static_cast<size_t>(blk) * o.rows + row] = static_cast<int8_t>(s);
+}
+
+template <int HD>
+__device__ __forceinline__ float absmax(const float (&v)[HD]) {
+  float m = 0.f;
+#pragma unroll
+  for (int c = 0; c < HD; ++c) m = fmaxf(m, fabsf(v[c]));
+  return m;
 }
 
 template <int HD>
@@ -99,45 +123,56 @@ __global__ void k_attn_fwd(AttnArgs a, int hg) {
   const int t0 = e0 + atom;
   const int d = a.d, ld = 3 * d;
   const int hs = head_stride(S, HD);
-  float *sK = sm, *sV = sK + hg * hs, *sM = sV + hg * hs;
+  float *sK = sm, *sV = sK + hg * hs, *sM = sV + hg * hs, *sX = sM + S;
   load_block<HD>(sK, a.qkv, ld, d + h0 * HD, t0, S, hg);
   load_block<HD>(sV, a.qkv, ld, 2 * d + h0 * HD, t0, S, hg);
   for (int k = threadIdx.x; k < S; k += blockDim.x) sM[k] = k == 0 ? 0.f : a.key_mask[e0 + k - 1];
   cp_async_wait_all();
   __syncthreads();
   const int t = threadIdx.x;
-  if (t >= hg * S) return;
-  const int hh = t / S, q = t - hh * S, h = h0 + hh;
-  float qr[HD], o[HD];
-  const float *qsrc = a.qkv + static_cast<size_t>(t0 + q) * ld + h * HD;
+  const bool live = t < hg * S;
+  const int hh = live ? t / S : 0, q = live ? t - hh * S : 0, h = h0 + hh;
+  float o[HD];
+  if (live) {
+    float qr[HD];
+    const float *qsrc = a.qkv + static_cast<size_t>(t0 + q) * ld + h * HD;
 #pragma unroll
-  for (int c = 0; c < HD; c += 4) {
-    const float4 v = *reinterpret_cast<const float4 *>(qsrc + c);
-    qr[c] = v.x; qr[c + 1] = v.y; qr[c + 2] = v.z; qr[c + 3] = v.w;
-    o[c] = o[c + 1] = o[c + 2] = o[c + 3] = 0.f;
-  }
-  const float scale = 1.0f / sqrtf(static_cast<float>(HD));
-  const float *K = sK + hh * hs, *V = sV + hh * hs;
-  float m = -FLT_MAX, l = 0.f;
-  for (int k = 0; k < S; ++k) {
-    const float s = dot_row<HD>(qr, K + k * HD) * scale + sM[k];
-    if (s > m) {
-      const float corr = expf(m - s);
-      l *= corr;
-#pragma unroll
-      for (int c = 0; c < HD; ++c) o[c] *= corr;
-      m = s;
+    for (int c = 0; c < HD; c += 4) {
+      const float4 v = *reinterpret_cast<const float4 *>(qsrc + c);
+      qr[c] = v.x; qr[c + 1] = v.y; qr[c + 2] = v.z; qr[c + 3] = v.w;
+      o[c] = o[c + 1] = o[c + 2] = o[c + 3] = 0.f;
     }
-    const float p = expf(s - m);
-    l += p;
-    axpy_row<HD>(o, p, V + k * HD);
-  }
-  const float inv = 1.0f / l;
-  float *dst = a.out + static_cast<size_t>(t0 + q) * d + h * HD;
+    const float scale = 1.0f / sqrtf(static_cast<float>(HD));
+    const float *K = sK + hh * hs, *V = sV + hh * hs;
+    float m = -FLT_MAX, l = 0.f;
+    for (int k = 0; k < S; ++k) {
+      const float s = dot_row<HD>(qr, K + k * HD) * scale + sM[k];
+      if (s > m) {
+        const float corr = expf(m - s);
+        l *= corr;
 #pragma unroll
-  for (int c = 0; c < HD; c += 4)
-    *reinterpret_cast<float4 *>(dst + c) = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
-  a.lse[static_cast<size_t>(t0 + q) * a.heads + h] = m + logf(l);
+        for (int c = 0; c < HD; ++c) o[c] *= corr;
+        m = s;
+      }
+      const float p = expf(s - m);
+      l += p;
+      axpy_row<HD>(o, p, V + k * HD);
+    }
+    const float inv = 1.0f / l;
+#pragma unroll
+    for (int c = 0; c < HD; ++c) o[c] *= inv;
+    a.lse[static_cast<size_t>(t0 + q) * a.heads + h] = m + logf(l);
+    if (a.out) {
+      float *dst = a.out + static_cast<size_t>(t0 + q) * d + h * HD;
+#pragma unroll
+      for (int c = 0; c < HD; c += 4) *reinterpret_cast<float4 *>(dst + c) = make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]);
+    }
+    if (a.out_split.hi) sX[hh * S + q] = absmax<HD>(o);
+  }
+  if (a.out_split.hi) {
+    __syncthreads();
+    if (live) group_split_store<HD>(a.out_split, t0 + q, h * HD, blockIdx.y, sX, hg, S, q, hh, o);
+  }
 }
 
 // dS = P (dP - rowsum(P dP)), dQ = s dS K, dK = s dS^T Q, dV = P^T dO.
@@ -157,7 +192,7 @@ __global__ void k_attn_bwd(AttnArgs a, int hg) {
   const int PS = S | 1;
   const int hs = head_stride(S, HD), ms = mat_stride(S);
   float *sA = sm, *sB = sA + hg * hs;  // K, V (phase A) then Q, dO (phase B)
-  float *sP = sB + hg * hs, *sD = sP + hg * ms, *sM = sD + hg * ms, *sL = sM + S;
+  float *sP = sB + hg * hs, *sD = sP + hg * ms, *sM = sD + hg * ms, *sL = sM + S, *sX = sL + hg * S;
   load_block<HD>(sA, a.qkv, ld, d + h0 * HD, t0, S, hg);
   load_block<HD>(sB, a.qkv, ld, 2 * d + h0 * HD, t0, S, hg);
   for (int k = threadIdx.x; k < S; k += blockDim.x) sM[k] = k == 0 ? 0.f : a.key_mask[e0 + k - 1];
@@ -184,10 +219,11 @@ __global__ void k_attn_bwd(AttnArgs a, int hg) {
   cp_async_wait_all();
   __syncthreads();
   float *P = sP + hh * ms, *Dm = sD + hh * ms;
+  const bool split = a.dqkv_split.hi != nullptr;
+  float acc[HD];
   if (live) {
     // phase A: thread = query row r
     const float *K = sA + hh * hs, *V = sB + hh * hs;
-    float acc[HD];
 #pragma unroll
     for (int c = 0; c < HD; ++c) acc[c] = 0.f;
     const float lse = sL[hh * S + r];
@@ -206,21 +242,26 @@ __global__ void k_attn_bwd(AttnArgs a, int hg) {
       Dm[r * PS + k] = ds;
       axpy_row<HD>(acc, ds, K + k * HD);
     }
-    float *dq = a.d_qkv + static_cast<size_t>(t0 + r) * ld + h * HD;
 #pragma unroll
-    for (int c = 0; c < HD; c += 4)
-      *reinterpret_cast<float4 *>(dq + c) =
-          make_float4(acc[c] * scale, acc[c + 1] * scale, acc[c + 2] * scale, acc[c + 3] * scale);
+    for (int c = 0; c < HD; ++c) acc[c] *= scale;
+    if (a.d_qkv) {
+      float *dq = a.d_qkv + static_cast<size_t>(t0 + r) * ld + h * HD;
+#pragma unroll
+      for (int c = 0; c < HD; c += 4)
+        *reinterpret_cast<float4 *>(dq + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+    }
+    if (split) sX[hh * S + r] = absmax<HD>(acc);
   }
   __syncthreads();  // K and V no longer read: bring in Q and dO
+  if (split && live) group_split_store<HD>(a.dqkv_split, t0 + r, h * HD, blockIdx.y, sX, hg, S, r, hh, acc);
   load_block<HD>(sA, a.qkv, ld, h0 * HD, t0, S, hg);
   load_block<HD>(sB, a.d_out, d, h0 * HD, t0, S, hg);
   cp_async_wait_all();
   __syncthreads();
+  float dk[HD], dv[HD];
   if (live) {
     // phase B: thread = key row r
     const float *Q = sA + hh * hs, *G = sB + hh * hs;
-    float dk[HD], dv[HD];
 #pragma unroll
     for (int c = 0; c < HD; ++c) dk[c] = dv[c] = 0.f;
 #pragma unroll 2
@@ -228,12 +269,28 @@ __global__ void k_attn_bwd(AttnArgs a, int hg) {
       axpy_row<HD>(dk, Dm[q * PS + r], Q + q * HD);
       axpy_row<HD>(dv, P[q * PS + r], G + q * HD);
     }
-    float *dst = a.d_qkv + static_cast<size_t>(t0 + r) * ld + h * HD;
 #pragma unroll
-    for (int c = 0; c < HD; c += 4) {
-      *reinterpret_cast<float4 *>(dst + d + c) =
-          make_float4(dk[c] * scale, dk[c + 1] * scale, dk[c + 2] * scale, dk[c + 3] * scale);
-      *reinterpret_cast<float4 *>(dst + 2 * d + c) = make_float4(dv[c], dv[c + 1], dv[c + 2], dv[c + 3]);
+    for (int c = 0; c < HD; ++c) dk[c] *= scale;
+    if (a.d_qkv) {
+      float *dst = a.d_qkv + static_cast<size_t>(t0 + r) * ld + h * HD;
+#pragma unroll
+      for (int c = 0; c < HD; c += 4) {
+        *reinterpret_cast<float4 *>(dst + d + c) = make_float4(dk[c], dk[c + 1], dk[c + 2], dk[c + 3]);
+        *reinterpret_cast<float4 *>(dst + 2 * d + c) = make_float4(dv[c], dv[c + 1], dv[c + 2], dv[c + 3]);
+      }
+    }
+    if (split) {
+      sX[hg * S + hh * S + r] = absmax<HD>(dk);
+      sX[2 * hg * S + hh * S + r] = absmax<HD>(dv);
+    }
+  }
+  if (split) {
+    __syncthreads();
+    if (live) {
+      const int nbq = d / 128;
+      group_split_store<HD>(a.dqkv_split, t0 + r, d + h * HD, nbq + blockIdx.y, sX + hg * S, hg, S, r, hh, dk);
+      group_split_store<HD>(a.dqkv_split, t0 + r, 2 * d + h * HD, 2 * nbq + blockIdx.y, sX + 2 * hg * S, hg, S, r,
+                            hh, dv);
     }
   }
 }
@@ -252,10 +309,19 @@ int pick_group(int heads, int S, int hd, bool bwd, size_t limit) {
 template <int HD>
 void run(const AttnArgs &a, bool bwd, cudaStream_t s) {
   const int S = a.max_tokens;
-  // prefer two CTAs per SM for the backward's large footprint
-  int hg = pick_group(a.heads, S, HD, bwd, bwd ? kSmemLimit / 2 : kSmemLimit / 4);
-  if (!hg) hg = pick_group(a.heads, S, HD, bwd, kSmemLimit);
-  if (!hg) throw Error(kErrUnsupported, "attention: too many neighbours for one CTA");
+  int hg = 0;
+  if (bwd ? a.dqkv_split.hi != nullptr : a.out_split.hi != nullptr) {
+    // split output: the CTA's heads form one 128-column block
+    hg = 128 / HD;
+    if (128 % HD || a.heads % hg || hg * S > 1024 ||
+        (bwd ? bwd_smem(S, HD, hg) : fwd_smem(S, HD, hg)) > kSmemLimit)
+      throw Error(kErrInternal, "attention: split output needs 128 / head size heads per CTA");
+  } else {
+    // prefer two CTAs per SM for the backward's large footprint
+    hg = pick_group(a.heads, S, HD, bwd, bwd ? kSmemLimit / 2 : kSmemLimit / 4);
+    if (!hg) hg = pick_group(a.heads, S, HD, bwd, kSmemLimit);
+    if (!hg) throw Error(kErrUnsupported, "attention: too many neighbours for one CTA");
+  }
   const size_t smem = bwd ? bwd_smem(S, HD, hg) : fwd_smem(S, HD, hg);
   const int threads = (hg * S + 31) / 32 * 32;
   dim3 grid(a.n_atoms, a.heads / hg);
@@ -288,6 +354,14 @@ void dispatch(const AttnArgs &a, bool bwd, cudaStream_t s) {
 int attention_max_tokens(int hd) {
   int S = 1;
   while (pick_group(1, S + 1, hd, true, kSmemLimit) && pick_group(1, S + 1, hd, false, kSmemLimit)) ++S;
+  return S;
+}
+
+int attention_split_max_tokens(int hd) {
+  if (hd <= 0 || 128 % hd) return 0;
+  const int hg = 128 / hd;
+  int S = 0;
+  while (hg * (S + 1) <= 1024 && bwd_smem(S + 1, hd, hg) <= kSmemLimit && fwd_smem(S + 1, hd, hg) <= kSmemLimit) ++S;
   return S;
 }
 
@@ -351,19 +425,124 @@ __global__ void k_ln_bwd(const float *__restrict__ dy, const float *__restrict__
   for (int c = lane; c < d; c += 32) dxr[c] = r * (dyr[c] * g[c] - m1 - hr[c] * m2);
 }
 
+// Rows of d = 128 nb columns: lane l holds float4 columns 128 b + 4 l, so
+// each 128-column block of the output is one warp-wide split block.
+template <int NB>
+__global__ void k_ln_fwd4(const float *__restrict__ x, const float *__restrict__ g,
+                          const float *__restrict__ b, float *__restrict__ y,
+                          float *__restrict__ xhat, float *__restrict__ rstd, int rows, Split16View ys) {
+  constexpr int d = 128 * NB;
+  const int lane = threadIdx.x & 31;
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (row >= rows) return;
+  const float *xr = x + static_cast<size_t>(row) * d;
+  float4 v[NB];
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < NB; ++k) {
+    v[k] = *reinterpret_cast<const float4 *>(xr + 128 * k + 4 * lane);
+    s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+  }
+  const float inv_d = 1.0f / static_cast<float>(d);
+  const float mean = warp_sum(s) * inv_d;
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < NB; ++k) {
+    const float t0 = v[k].x - mean, t1 = v[k].y - mean, t2 = v[k].z - mean, t3 = v[k].w - mean;
+    q = fmaf(t0, t0, q); q = fmaf(t1, t1, q); q = fmaf(t2, t2, q); q = fmaf(t3, t3, q);
+  }
+  const float var = warp_sum(q) * inv_d;
+  const float sd = sqrtf(var * (1.0f + kLnEps));
+  float *yr = y + static_cast<size_t>(row) * d;
+  float *hr = xhat + static_cast<size_t>(row) * d;
+#pragma unroll
+  for (int k = 0; k < NB; ++k) {
+    const int c = 128 * k + 4 * lane;
+    const float4 gg = __ldg(reinterpret_cast<const float4 *>(g + c));
+    const float4 bb = __ldg(reinterpret_cast<const float4 *>(b + c));
+    const float4 h = make_float4((v[k].x - mean) / sd, (v[k].y - mean) / sd, (v[k].z - mean) / sd,
+                                 (v[k].w - mean) / sd);
+    const float4 o = make_float4(h.x * gg.x + bb.x, h.y * gg.y + bb.y, h.z * gg.z + bb.z, h.w * gg.w + bb.w);
+    *reinterpret_cast<float4 *>(hr + c) = h;
+    *reinterpret_cast<float4 *>(yr + c) = o;
+    if (ys.hi) warp_split_block(ys, row, k, o, lane);
+  }
+  if (lane == 0) rstd[row] = 1.0f / sd;
+}
+
+template <int NB>
+__global__ void k_ln_bwd4(const float *__restrict__ dy, const float *__restrict__ xhat,
+                          const float *__restrict__ rstd, const float *__restrict__ g,
+                          float *__restrict__ dx, int rows, Split16View dxs) {
+  constexpr int d = 128 * NB;
+  const int lane = threadIdx.x & 31;
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (row >= rows) return;
+  const float *dyr = dy + static_cast<size_t>(row) * d;
+  const float *hr = xhat + static_cast<size_t>(row) * d;
+  float4 gh[NB], hh[NB];
+  float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+  for (int k = 0; k < NB; ++k) {
+    const int c = 128 * k + 4 * lane;
+    const float4 a = *reinterpret_cast<const float4 *>(dyr + c);
+    const float4 gg = __ldg(reinterpret_cast<const float4 *>(g + c));
+    hh[k] = *reinterpret_cast<const float4 *>(hr + c);
+    gh[k] = make_float4(a.x * gg.x, a.y * gg.y, a.z * gg.z, a.w * gg.w);
+    s1 += (gh[k].x + gh[k].y) + (gh[k].z + gh[k].w);
+    s2 = fmaf(gh[k].x, hh[k].x, s2); s2 = fmaf(gh[k].y, hh[k].y, s2);
+    s2 = fmaf(gh[k].z, hh[k].z, s2); s2 = fmaf(gh[k].w, hh[k].w, s2);
+  }
+  const float inv_d = 1.0f / static_cast<float>(d);
+  const float m1 = warp_sum(s1) * inv_d;
+  const float m2 = warp_sum(s2) * inv_d * (1.0f + kLnEps);
+  const float r = rstd[row];
+  float *dxr = dx + static_cast<size_t>(row) * d;
+#pragma unroll
+  for (int k = 0; k < NB; ++k) {
+    const int c = 128 * k + 4 * lane;
+    const float4 o = make_float4(r * (gh[k].x - m1 - hh[k].x * m2), r * (gh[k].y - m1 - hh[k].y * m2),
+                                 r * (gh[k].z - m1 - hh[k].z * m2), r * (gh[k].w - m1 - hh[k].w * m2));
+    *reinterpret_cast<float4 *>(dxr + c) = o;
+    if (dxs.hi) warp_split_block(dxs, row, k, o, lane);
+  }
+}
+
 }  // namespace
 
 void layer_norm_fwd(const float *x, const float *g, const float *b, float *y, float *xhat,
-                    float *rstd, int rows, int d, cudaStream_t s) {
+                    float *rstd, int rows, int d, cudaStream_t s, const Split16View *ys) {
   if (rows <= 0) return;
-  k_ln_fwd<<<ceil_div(static_cast<int64_t>(rows) * 32, 256), 256, 0, s>>>(x, g, b, y, xhat, rstd, rows, d);
+  const int grid = ceil_div(static_cast<int64_t>(rows) * 32, 256);
+  const Split16View none{};
+  const Split16View &o = ys ? *ys : none;
+  switch (d % 128 == 0 ? d / 128 : 0) {
+    case 1: k_ln_fwd4<1><<<grid, 256, 0, s>>>(x, g, b, y, xhat, rstd, rows, o); break;
+    case 2: k_ln_fwd4<2><<<grid, 256, 0, s>>>(x, g, b, y, xhat, rstd, rows, o); break;
+    case 4: k_ln_fwd4<4><<<grid, 256, 0, s>>>(x, g, b, y, xhat, rstd, rows, o); break;
+    case 8: k_ln_fwd4<8><<<grid, 256, 0, s>>>(x, g, b, y, xhat, rstd, rows, o); break;
+    default:
+      if (ys) throw Error(kErrInternal, "layer_norm_fwd: split output needs d in {128, 256, 512, 1024}");
+      k_ln_fwd<<<grid, 256, 0, s>>>(x, g, b, y, xhat, rstd, rows, d);
+  }
   CUDA_LAUNCH_CHECK();
 }
 
 void layer_norm_bwd(const float *dy, const float *xhat, const float *rstd, const float *g,
-                    float *dx, int rows, int d, cudaStream_t s) {
+                    float *dx, int rows, int d, cudaStream_t s, const Split16View *dxs) {
   if (rows <= 0) return;
-  k_ln_bwd<<<ceil_div(static_cast<int64_t>(rows) * 32, 256), 256, 0, s>>>(dy, xhat, rstd, g, dx, rows, d);
+  const int grid = ceil_div(static_cast<int64_t>(rows) * 32, 256);
+  const Split16View none{};
+  const Split16View &o = dxs ? *dxs : none;
+  switch (d % 128 == 0 ? d / 128 : 0) {
+    case 1: k_ln_bwd4<1><<<grid, 256, 0, s>>>(dy, xhat, rstd, g, dx, rows, o); break;
+    case 2: k_ln_bwd4<2><<<grid, 256, 0, s>>>(dy, xhat, rstd, g, dx, rows, o); break;
+    case 4: k_ln_bwd4<4><<<grid, 256, 0, s>>>(dy, xhat, rstd, g, dx, rows, o); break;
+    case 8: k_ln_bwd4<8><<<grid, 256, 0, s>>>(dy, xhat, rstd, g, dx, rows, o); break;
+    default:
+      if (dxs) throw Error(kErrInternal, "layer_norm_bwd: split output needs d in {128, 256, 512, 1024}");
+      k_ln_bwd<<<grid, 256, 0, s>>>(dy, xhat, rstd, g, dx, rows, d);
+  }
   CUDA_LAUNCH_CHECK();
 }
 

@@ -43,6 +43,7 @@
 #include "common.cuh"
 #include "gemm_tc.cuh"
 #include "kernels.cuh"
+#include "split16.cuh"
 
 namespace pet {
 namespace {
@@ -207,15 +208,16 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-// 2^e for e in [-126, 127], built from its IEEE-754 bit pattern (exact).
-__device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
-
+// Epilogue of one thread's row segment [n0, n0 + 128): bias, activation,
+// fp32 store (if p.C), and for the 3xFP16 kernel (kScaled) optionally the
+// split-fp16 form of the result (p.c_split; the segment is one scale block).
 template <int EPI, bool kScaled = false>
-__device__ __forceinline__ void epilogue_store(const GemmArgs &p, int row, int n0, const float (&acc)[BN],
+__device__ __forceinline__ void epilogue_store(const GemmArgs &p, int row, int n0, float (&acc)[BN],
                                                float s_row = 1.f, float s_b = 1.f) {
   if (row >= p.M) return;
   const int rc = p.c_rows ? p.c_rows[row] : row;
-  float *crow = p.C + static_cast<size_t>(rc) * p.ldc;
+  float *crow = p.C ? p.C + static_cast<size_t>(rc) * p.ldc : nullptr;
+  const bool split = kScaled && p.c_split.hi != nullptr;
   const float *zrow = (EPI == EPI_SILU || EPI == EPI_DSILU) ? p.Z + static_cast<size_t>(row) * p.ldz : nullptr;
   const float *rrow = EPI == EPI_RESID ? p.R + static_cast<size_t>(rc) * p.ldr : nullptr;
   // 32 columns at a time: all loads of a group (bias, Z or R, C for ACCUM)
@@ -249,21 +251,33 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs &p, int row, int n
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int n = n0 + g + 4 * k;
-      float4 *dst = reinterpret_cast<float4 *>(crow + n);
+      float4 out;
       if (EPI == EPI_STORE) {
-        *dst = x[k];
+        out = x[k];
       } else if (EPI == EPI_SILU) {
-        float4 y, dy;
-        silu_pair(x[k].x, y.x, dy.x); silu_pair(x[k].y, y.y, dy.y);
-        silu_pair(x[k].z, y.z, dy.z); silu_pair(x[k].w, y.w, dy.w);
+        float4 dy;
+        silu_pair(x[k].x, out.x, dy.x); silu_pair(x[k].y, out.y, dy.y);
+        silu_pair(x[k].z, out.z, dy.z); silu_pair(x[k].w, out.w, dy.w);
         *reinterpret_cast<float4 *>(const_cast<float *>(zrow) + n) = dy;
-        *dst = y;
       } else if (EPI == EPI_DSILU) {
-        *dst = make_float4(x[k].x * ld[k].x, x[k].y * ld[k].y, x[k].z * ld[k].z, x[k].w * ld[k].w);
+        out = make_float4(x[k].x * ld[k].x, x[k].y * ld[k].y, x[k].z * ld[k].z, x[k].w * ld[k].w);
       } else {  // EPI_RESID, EPI_ACCUM: x + R or x + C
-        *dst = make_float4(x[k].x + ld[k].x, x[k].y + ld[k].y, x[k].z + ld[k].z, x[k].w + ld[k].w);
+        out = make_float4(x[k].x + ld[k].x, x[k].y + ld[k].y, x[k].z + ld[k].z, x[k].w + ld[k].w);
+      }
+      if (crow) *reinterpret_cast<float4 *>(crow + n) = out;
+      if (split) {
+        const int j = g + 4 * k;
+        acc[j] = out.x; acc[j + 1] = out.y; acc[j + 2] = out.z; acc[j + 3] = out.w;
       }
     }
+  }
+  if (split) {
+    float mx = 0.f;
+#pragma unroll
+    for (int j = 0; j < BN; ++j) mx = fmaxf(mx, fabsf(acc[j]));
+    const int s = split_scale_exponent(mx);
+    thread_split_store<BN>(p.c_split, rc, n0, acc, s);
+    p.c_split.sc[static_cast<size_t>(n0 / 128) * p.c_split.rows + rc] = static_cast<int8_t>(s);
   }
 }
 
@@ -451,18 +465,9 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_gemm_3xtf32(GemmArgs p, TCWei
 constexpr int kSBlock = 128;               // k per A scale block = one TMEM pass (384 products)
 constexpr int kMaxSBlocks = 16;            // K <= 2048
 
-__device__ __forceinline__ int scale_exponent_dev(float mx) {
-  if (!(mx > 0.f)) return 0;
-  const int E = static_cast<int>((__float_as_uint(mx) >> 23) & 0xFFu);
-  int s = 141 - (E > 0 ? E : 0);
-  return s < -120 ? -120 : (s > 120 ? 120 : s);
-}
-
 // Warp per row: lane l holds elements 4l..4l+3 of every 128-element block.
 __global__ void __launch_bounds__(256) k_split_a(const float *__restrict__ A, int lda,
-                                                 const int *__restrict__ a_rows, int M, int K,
-                                                 uint16_t *__restrict__ hi, uint16_t *__restrict__ lo,
-                                                 int8_t *__restrict__ sc) {
+                                                 const int *__restrict__ a_rows, int M, int K, Split16View o) {
   const int m = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (m >= M) return;
   const float *row = A + static_cast<size_t>(a_rows ? a_rows[m] : m) * lda;
@@ -474,21 +479,7 @@ __global__ void __launch_bounds__(256) k_split_a(const float *__restrict__ A, in
 #pragma unroll
   for (int b = 0; b < kMaxSBlocks; ++b) {
     if (b >= nb) break;
-    float mx = fmaxf(fmaxf(fabsf(v[b].x), fabsf(v[b].y)), fmaxf(fabsf(v[b].z), fabsf(v[b].w)));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const int s = scale_exponent_dev(mx);
-    const float f = pow2f(s);
-    const float x0 = v[b].x * f, x1 = v[b].y * f, x2 = v[b].z * f, x3 = v[b].w * f;
-    const __half2 h01 = __floats2half2_rn(x0, x1), h23 = __floats2half2_rn(x2, x3);
-    const float2 r01 = __half22float2(h01), r23 = __half22float2(h23);
-    const __half2 l01 = __floats2half2_rn(x0 - r01.x, x1 - r01.y), l23 = __floats2half2_rn(x2 - r23.x, x3 - r23.y);
-    const size_t o = static_cast<size_t>(m) * K + b * kSBlock + lane * 4;
-    *reinterpret_cast<uint2 *>(hi + o) =
-        make_uint2(*reinterpret_cast<const uint32_t *>(&h01), *reinterpret_cast<const uint32_t *>(&h23));
-    *reinterpret_cast<uint2 *>(lo + o) =
-        make_uint2(*reinterpret_cast<const uint32_t *>(&l01), *reinterpret_cast<const uint32_t *>(&l23));
-    if (lane == 0) sc[static_cast<size_t>(b) * M + m] = static_cast<int8_t>(s);
+    warp_split_block(o, m, b, v[b], lane);
   }
 }
 
@@ -977,7 +968,8 @@ CUtensorMap make_map_f16(const void *ptr, uint64_t rows, uint64_t cols, uint64_t
 }
 
 template <int EPI, int BNt>
-void launch16_bn(const GemmArgs &a, const TCWeights16 &w, const Split16 &sp, int *err, cudaStream_t s) {
+void launch16_bn(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t s) {
+  const Split16View &sp = a.a_split;
   using C = F16Cfg<BNt>;
   const CUtensorMap ah = make_map_f16(sp.hi, a.M, a.K, a.K, C::BK, BM), al = make_map_f16(sp.lo, a.M, a.K, a.K, C::BK, BM);
   const CUtensorMap bh = make_map_f16(w.hi, a.N, a.K, a.ldb, C::BK, BNt),
@@ -990,7 +982,8 @@ void launch16_bn(const GemmArgs &a, const TCWeights16 &w, const Split16 &sp, int
 }
 
 template <int EPI>
-void launch16_pair(const GemmArgs &a, const TCWeights16 &w, const Split16 &sp, int *err, cudaStream_t s) {
+void launch16_pair(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t s) {
+  const Split16View &sp = a.a_split;
   using C = PairCfg;
   const CUtensorMap ah = make_map_f16(sp.hi, a.M, a.K, a.K, C::BK, BM), al = make_map_f16(sp.lo, a.M, a.K, a.K, C::BK, BM);
   const CUtensorMap bh = make_map_f16(w.hi, a.N, a.K, a.ldb, C::BK, 128),
@@ -1017,17 +1010,19 @@ void launch16_pair(const GemmArgs &a, const TCWeights16 &w, const Split16 &sp, i
 }
 
 template <int EPI>
-void launch16(const GemmArgs &a, const TCWeights16 &w, const Split16 &sp, int *err, cudaStream_t s) {
+void launch16(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t s) {
   if (g_num_sms == 0) {
     int dev = 0;
     CUDA_CHECK(cudaGetDevice(&dev));
     CUDA_CHECK(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev));
   }
-  k_split_a<<<ceil_div(a.M, 8), 256, 0, s>>>(a.A, a.lda, a.a_rows, a.M, a.K, sp.hi, sp.lo, sp.sc);
-  CUDA_LAUNCH_CHECK();
-  if (a.N % 256 == 0 && g_f16_bn == 512) launch16_pair<EPI>(a, w, sp, err, s);
-  else if (a.N % 256 == 0 && g_f16_bn != 128) launch16_bn<EPI, 256>(a, w, sp, err, s);
-  else launch16_bn<EPI, 128>(a, w, sp, err, s);
+  if (!a.a_split_ready) {
+    k_split_a<<<ceil_div(a.M, 8), 256, 0, s>>>(a.A, a.lda, a.a_rows, a.M, a.K, a.a_split);
+    CUDA_LAUNCH_CHECK();
+  }
+  if (a.N % 256 == 0 && g_f16_bn == 512) launch16_pair<EPI>(a, w, err, s);
+  else if (a.N % 256 == 0 && g_f16_bn != 128) launch16_bn<EPI, 256>(a, w, err, s);
+  else launch16_bn<EPI, 128>(a, w, err, s);
 }
 
 }  // namespace
@@ -1045,16 +1040,22 @@ bool gemm_f16_supported(const GemmArgs &a) {
   return gemm_tc_supported(a) && a.K % kSBlock == 0 && a.K <= kSBlock * kMaxSBlocks && a.ldb % 8 == 0;
 }
 
-void gemm_3xf16(const GemmArgs &a, const TCWeights16 &w, const Split16 &sp, int *err, cudaStream_t s) {
+void gemm_3xf16(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t s) {
+  const Split16View &sp = a.a_split;
+  if (!sp.hi || sp.rows != a.M || sp.cols != a.K)
+    throw Error(kErrInternal, "gemm_3xf16: split A view does not match the GEMM shape");
+  if (a.c_split.hi && (a.c_split.cols != a.N || a.N % 128 != 0))
+    throw Error(kErrInternal, "gemm_3xf16: split output view does not match the GEMM shape");
   if (reinterpret_cast<uintptr_t>(w.hi) % 16 || reinterpret_cast<uintptr_t>(w.lo) % 16 ||
-      reinterpret_cast<uintptr_t>(sp.hi) % 16 || reinterpret_cast<uintptr_t>(sp.lo) % 16)
+      reinterpret_cast<uintptr_t>(sp.hi) % 16 || reinterpret_cast<uintptr_t>(sp.lo) % 16 ||
+      (a.c_split.hi && (reinterpret_cast<uintptr_t>(a.c_split.hi) % 16 || reinterpret_cast<uintptr_t>(a.c_split.lo) % 16)))
     throw Error(kErrInternal, "gemm_3xf16: fp16 operands not 16-byte aligned");
   switch (a.epi) {
-    case EPI_STORE: launch16<EPI_STORE>(a, w, sp, err, s); break;
-    case EPI_SILU: launch16<EPI_SILU>(a, w, sp, err, s); break;
-    case EPI_ACCUM: launch16<EPI_ACCUM>(a, w, sp, err, s); break;
-    case EPI_DSILU: launch16<EPI_DSILU>(a, w, sp, err, s); break;
-    case EPI_RESID: launch16<EPI_RESID>(a, w, sp, err, s); break;
+    case EPI_STORE: launch16<EPI_STORE>(a, w, err, s); break;
+    case EPI_SILU: launch16<EPI_SILU>(a, w, err, s); break;
+    case EPI_ACCUM: launch16<EPI_ACCUM>(a, w, err, s); break;
+    case EPI_DSILU: launch16<EPI_DSILU>(a, w, err, s); break;
+    case EPI_RESID: launch16<EPI_RESID>(a, w, err, s); break;
     default: throw Error(kErrInternal, "gemm_tc: bad epilogue");
   }
 }

@@ -35,20 +35,14 @@ bool gemm_f16_supported(const GemmArgs &a);
 // non-zero if a pipeline wait times out.
 void gemm_3xtf32(const GemmArgs &a, const TCWeights &w, int *err, cudaStream_t s);
 
-// Scratch for the split-fp16 copy of A: hi and lo [M, K] fp16, sc
-// [K/128, M] int8 scale exponents (16-byte aligned).
-struct Split16 {
-  uint16_t *hi = nullptr;
-  uint16_t *lo = nullptr;
-  int8_t *sc = nullptr;
-};
-
-// C = A B^T (+ epilogue) with 3xFP16 on tcgen05: a pre-pass writes A
-// (row-gathered) as fp16 hi + lo scaled by 2^s per row and 128-element k
-// block (block max into [2^14, 2^15)); B is pre-split with one scale
-// 2^b_scale; A B^T ~= sum over blocks of (A_hi B_hi + A_hi B_lo + A_lo B_hi)
-// 2^-(s + b_scale), fp32 accumulation, operands streamed by TMA.
-void gemm_3xf16(const GemmArgs &a, const TCWeights16 &w, const Split16 &sp, int *err, cudaStream_t s);
+// C = A B^T (+ epilogue) with 3xFP16 on tcgen05.  A comes in split-fp16
+// form (a.a_split; when not a.a_split_ready a pre-pass first writes it from
+// the fp32 A, row-gathered): fp16 hi + lo scaled by 2^s per row and
+// 128-element k block.  B is pre-split with one scale 2^b_scale.
+// A B^T ~= sum over blocks of (A_hi B_hi + A_hi B_lo + A_lo B_hi)
+// 2^-(s + b_scale) with fp32 accumulation, operands streamed by TMA.  With
+// a.c_split the epilogue also writes the result in split form.
+void gemm_3xf16(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t s);
 
 // Power-of-two scale exponent s with max|x| 2^s in [2^14, 2^15) (0 for an
 // all-zero tensor, clamped to [-120, 120]).

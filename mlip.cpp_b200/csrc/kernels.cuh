@@ -19,6 +19,15 @@ enum Epilogue : int {
   EPI_RESID = 4,    // C = acc + bias + R[row_c(m)]
 };
 
+// A matrix in split-fp16 form (split16.cuh): hi, lo [rows][cols] fp16 and
+// scale exponents sc [cols / 128][rows].  hi == nullptr: none.
+struct Split16View {
+  uint16_t *hi = nullptr;
+  uint16_t *lo = nullptr;
+  int8_t *sc = nullptr;
+  int rows = 0, cols = 0;
+};
+
 struct GemmArgs {
   const float *A = nullptr;
   int lda = 0;
@@ -35,6 +44,13 @@ struct GemmArgs {
   const float *R = nullptr;     // EPI_RESID residual, rows row_c(m)
   int ldr = 0;
   int epi = EPI_STORE;
+  // 3xFP16 only.  a_split: split form of A ([M, K]); a_split_ready = it
+  // already holds A (else the GEMM first writes A, row-gathered, into it).
+  // c_split: also write the result in split form (rows row_c(m)); C may
+  // then be null.
+  Split16View a_split;
+  bool a_split_ready = false;
+  Split16View c_split;
 };
 
 // Dense fp32 GEMM (exact fp32 FFMA accumulation).
@@ -50,18 +66,28 @@ struct AttnArgs {
   const float *key_mask;  // [E] additive mask of each edge key (node key: 0)
   const int *offset;      // [N+1] edge offsets (CSR)
   int n_atoms, d, heads, max_tokens;
+  // Optional split-fp16 outputs (then out / d_qkv may be null): the forward
+  // output [T, d] and the backward result [T, 3d].  Needs 128 / head size
+  // heads per CTA, one 128-column block.
+  Split16View out_split;
+  Split16View dqkv_split;
 };
 void attention_fwd(const AttnArgs &a, cudaStream_t stream);
 void attention_bwd(const AttnArgs &a, cudaStream_t stream);
 // Largest per-atom token count the attention kernels accept for head size hd.
 int attention_max_tokens(int hd);
+// Largest tokens per atom for which the attention kernels can write
+// split-fp16 outputs (128 / hd heads per CTA); 0 if hd does not divide 128.
+int attention_split_max_tokens(int hd);
 
 // ---- row-wise ops ---------------------------------------------------------
-// y = (x - mean) / sqrt(var * (1 + eps)) * g + b  (pet_layers.cpp:85-145)
+// y = (x - mean) / sqrt(var * (1 + eps)) * g + b  (pet_layers.cpp:85-145);
+// ys: also write y in split-fp16 form (d a multiple of 128, at most 1024)
 void layer_norm_fwd(const float *x, const float *g, const float *b, float *y, float *xhat,
-                    float *rstd, int rows, int d, cudaStream_t stream);
-// dx = rstd (dxhat - mean(dxhat) - (1 + eps) xhat mean(dxhat xhat)), dxhat = dy g
+                    float *rstd, int rows, int d, cudaStream_t stream, const Split16View *ys = nullptr);
+// dx = rstd (dxhat - mean(dxhat) - (1 + eps) xhat mean(dxhat xhat)), dxhat = dy g;
+// dxs: also write dx in split-fp16 form
 void layer_norm_bwd(const float *dy, const float *xhat, const float *rstd, const float *g,
-                    float *dx, int rows, int d, cudaStream_t stream);
+                    float *dx, int rows, int d, cudaStream_t stream, const Split16View *dxs = nullptr);
 
 }  // namespace pet

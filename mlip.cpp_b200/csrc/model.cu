@@ -155,7 +155,7 @@ const float *PETModel::w(const std::string &name) const {
 }
 
 size_t PETModel::device_bytes() const {
-  return wbuf_.cap + persist_.cap + scratch_.cap + split_.cap + nl_.center.cap * 10;
+  return wbuf_.cap + persist_.cap + scratch_.cap + sp_[0].cap + sp_[1].cap + nl_.center.cap * 10;
 }
 
 // ---------------------------------------------------------------------------
@@ -174,6 +174,18 @@ float half_bits_to_float(uint16_t b) {
   return __half2float(h);
 }
 }  // namespace
+
+Split16View PETModel::split_view(int i, int rows, int cols) {
+  const size_t n = static_cast<size_t>(rows) * cols;
+  if (sp_[i].cap < n * 4 + n / 128) throw Error(kErrInternal, "split-fp16 buffer too small");
+  Split16View v;
+  v.hi = sp_[i].as<uint16_t>();
+  v.lo = v.hi + n;
+  v.sc = reinterpret_cast<int8_t *>(v.lo + n);
+  v.rows = rows;
+  v.cols = cols;
+  return v;
+}
 
 int PETModel::weight_scale(size_t elem) const {
   auto it = std::upper_bound(wscale_.begin(), wscale_.end(), elem,
@@ -286,6 +298,16 @@ void PETModel::load(const std::string &path, float cutoff_override) {
   const char *g = std::getenv("MLIPCPP_B200_GEMM");
   use_tc_ = !(g && std::string(g) == "simt");
   use_f16_ = use_tc_ && !(g && std::string(g) == "tf32");
+  {
+    // chain mode: every dense layer's K and N a multiple of 128 (K <= 2048),
+    // 128 / head-size heads form one 128-column block, layer norms of <= 1024
+    const int hd = h.d / h.heads;
+    const bool m128 = h.d % 128 == 0 && h.ff % 128 == 0 && h.hid % 128 == 0 && h.dh % 128 == 0;
+    chain_ok_ = use_f16_ && m128 && 3 * h.d <= 2048 && h.ff <= 2048 && h.hid <= 2048 && h.d <= 1024 &&
+                hd > 0 && 128 % hd == 0 && h.heads % (128 / hd) == 0;
+    const char *c = std::getenv("MLIPCPP_B200_CHAIN");
+    if (c && std::string(c) == "0") chain_ok_ = false;
+  }
 
   // composition map and species index (pet.cpp:1280-1303)
   species_index_.clear();
@@ -354,7 +376,7 @@ struct Counts {
   int n_local, N0, E0, N1, E1;
 };
 
-static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, const Counts &c, bool grad) {
+static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, const Counts &c, bool grad, bool chain) {
   const size_t d = h.d, f = h.ff, r = h.dh, H = h.hid;
   const size_t E0 = std::max(c.E0, 1), N0 = std::max(c.N0, 1), E1 = std::max(c.E1, 1),
                N1 = std::max(c.N1, 1), NL = std::max(c.n_local, 1);
@@ -384,24 +406,27 @@ static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, const Counts
   a.g4 = P.take<float>(4 * E0);
   // forward scratch
   Plan fs = S;
-  a.cat = fs.take<float>(E0 * 3 * d); a.hc = fs.take<float>(E0 * H);
+  // chain mode keeps GEMM-only operands (cat, hc, o, hf, yn1, ye1; dqkv,
+  // dhf, dzc, dz1, dz2) in the split buffers alone
+  auto ftake = [&](Plan &pl, size_t n) -> float * { return chain ? nullptr : pl.take<float>(n); };
+  a.cat = ftake(fs, E0 * 3 * d); a.hc = ftake(fs, E0 * H);
   a.xin = fs.take<float>(T0 * d); a.xmid = fs.take<float>(T0 * d);
   a.xl[0] = fs.take<float>(T0 * d); a.xl[1] = fs.take<float>(T1 * d);
-  a.o = fs.take<float>(T0 * d); a.u = fs.take<float>(T0 * d); a.x1 = fs.take<float>(T0 * d);
-  a.hf = fs.take<float>(T0 * f); a.u2 = fs.take<float>(T0 * d);
-  a.yn1 = fs.take<float>(N1 * r); a.yn2 = fs.take<float>(N1 * r);
-  a.ye1 = fs.take<float>(E1 * r); a.ye2 = fs.take<float>(E1 * r);
+  a.o = ftake(fs, T0 * d); a.u = fs.take<float>(T0 * d); a.x1 = fs.take<float>(T0 * d);
+  a.hf = ftake(fs, T0 * f); a.u2 = fs.take<float>(T0 * d);
+  a.yn1 = ftake(fs, N1 * r); a.yn2 = fs.take<float>(N1 * r);
+  a.ye1 = ftake(fs, E1 * r); a.ye2 = fs.take<float>(E1 * r);
   a.node_pred = fs.take<float>(N1); a.edge_pred = fs.take<float>(E1);
   size_t fwd_end = fs.off;
   // backward scratch (aliases the forward scratch)
   Plan bs = S;
   if (grad) {
     a.dx = bs.take<float>(T0 * d); a.dx2 = bs.take<float>(T0 * d); a.du = bs.take<float>(T0 * d);
-    a.dout = bs.take<float>(T0 * d); a.dqkv = bs.take<float>(T0 * 3 * d); a.dx1 = bs.take<float>(T0 * d);
-    a.dhf = bs.take<float>(T0 * f);
+    a.dout = bs.take<float>(T0 * d); a.dqkv = ftake(bs, T0 * 3 * d); a.dx1 = bs.take<float>(T0 * d);
+    a.dhf = ftake(bs, T0 * f);
     const size_t rows = std::max(N1, E1);
-    a.dz1 = bs.take<float>(rows * r); a.dz2 = bs.take<float>(rows * r);
-    a.dzc = bs.take<float>(E0 * H); a.demb = bs.take<float>(E0 * d); a.dmsg = bs.take<float>(E1 * d);
+    a.dz1 = ftake(bs, rows * r); a.dz2 = ftake(bs, rows * r);
+    a.dzc = ftake(bs, E0 * H); a.demb = bs.take<float>(E0 * d); a.dmsg = bs.take<float>(E1 * d);
   }
   S.off = std::max(fwd_end, bs.off);
 }
@@ -420,10 +445,26 @@ void PETModel::forward_backward(bool grad) {
   const int *offset = nl_.offset.as<int>();
   const int *species = d_species_.as<int>();
   const float *emb0 = w("model.embedding.weight");
+  const bool ch = chain_;
+
+  // Split-fp16 operands of the chain mode: each producer takes the next
+  // buffer; the GEMM that consumes it runs before the buffer comes round
+  // again, and a GEMM that writes a split result writes the other buffer.
+  int next_sp = 0;
+  auto take_split = [&](int rows, int cols) {
+    const Split16View v = split_view(next_sp, rows, cols);
+    next_sp ^= 1;
+    return v;
+  };
+  struct SplitIO {
+    const Split16View *a = nullptr;  // A operand in split form
+    bool a_ready = true;             // ... already written (else: write it from fp32 A first)
+    const Split16View *c = nullptr;  // also write C in split form
+  };
 
   auto gemm = [&](const float *A, int lda, const int *a_rows, const float *B, int ldb, float *C, int ldc,
                   const int *c_rows, int M, int N, int K, const float *bias, int epi, cudaStream_t st,
-                  float *Z = nullptr, int ldz = 0, const float *R = nullptr, int ldr = 0) {
+                  float *Z = nullptr, int ldz = 0, const float *R = nullptr, int ldr = 0, SplitIO io = {}) {
     GemmArgs g = make_gemm(A, lda, a_rows, B, ldb, C, ldc, c_rows, M, N, K, bias, epi, Z, ldz, R, ldr);
     const float *wb = wbuf_.as<float>();
     const bool in_arena = B >= wb && B < wb + wspan_;
@@ -434,11 +475,17 @@ void PETModel::forward_backward(bool grad) {
     if (kprof_) mark_begin(e0);
     if (f16) {
       const uint16_t *h16 = reinterpret_cast<const uint16_t *>(wb + 3 * wspan_);
-      const size_t mk = static_cast<size_t>(M) * K;
-      if (split_.cap < mk * 4 + mk / 128) throw Error(kErrInternal, "split-fp16 scratch too small");
-      uint16_t *sh = split_.as<uint16_t>();
-      const Split16 sp{sh, sh + mk, reinterpret_cast<int8_t *>(sh + 2 * mk)};
-      gemm_3xf16(g, TCWeights16{h16 + eoff, h16 + wspan_ + eoff, weight_scale(eoff)}, sp, d_err_.as<int>(), st);
+      if (io.a) {
+        g.a_split = *io.a;
+        g.a_split_ready = io.a_ready;
+      } else {
+        g.a_split = split_view(0, M, K);
+        g.a_split_ready = false;
+      }
+      if (io.c) g.c_split = *io.c;
+      gemm_3xf16(g, TCWeights16{h16 + eoff, h16 + wspan_ + eoff, weight_scale(eoff)}, d_err_.as<int>(), st);
+    } else if (io.c || (io.a && io.a_ready)) {
+      throw Error(kErrInternal, "split-fp16 operands need the 3xFP16 GEMM");
     } else if (tc) {
       gemm_3xtf32(g, TCWeights{B + wspan_, B + 2 * wspan_}, d_err_.as<int>(), st);
     } else {
@@ -463,18 +510,46 @@ void PETModel::forward_backward(bool grad) {
   at.heads = h.heads;
   at.max_tokens = max_tok_;
 
-  auto block_fwd = [&](int b, const float *x, float *out) {
+  // Transformer block b on input x (its split form sx in chain mode); the
+  // output goes to `out`, and in chain mode also to *sout when non-null.
+  auto block_fwd = [&](int b, const float *x, const Split16View *sx, float *out, Split16View *sout) {
     const BlockW &B = g_lw[b / 2].blk[b % 2];
-    gemm(x, d, nullptr, B.Win, d, a.qkv[b], 3 * d, nullptr, T, 3 * d, d, B.bin, EPI_STORE, s);
+    gemm(x, d, nullptr, B.Win, d, a.qkv[b], 3 * d, nullptr, T, 3 * d, d, B.bin, EPI_STORE, s, nullptr, 0, nullptr,
+         0, SplitIO{sx});
     at.qkv = a.qkv[b];
     at.lse = a.lse[b];
     at.out = a.o;
+    Split16View so, sx1, shf;
+    if (ch) {
+      so = take_split(T, d);
+      at.out_split = so;
+    }
     attn(false, at);
-    gemm(a.o, d, nullptr, B.Wout, d, a.u, d, nullptr, T, d, d, B.bout, EPI_RESID, s, nullptr, 0, x, d);
-    layer_norm_fwd(a.u, B.ga, B.ba, a.x1, a.xa[b], a.ra[b], T, d, s);
-    gemm(a.x1, d, nullptr, B.W0, d, a.hf, f, nullptr, T, f, d, B.b0, EPI_SILU, s, a.zf[b], f);
-    gemm(a.hf, f, nullptr, B.W3, f, a.u2, d, nullptr, T, d, f, B.b3, EPI_RESID, s, nullptr, 0, a.x1, d);
-    layer_norm_fwd(a.u2, B.gm, B.bm, out, a.xm[b], a.rm[b], T, d, s);
+    at.out_split = Split16View{};
+    gemm(a.o, d, nullptr, B.Wout, d, a.u, d, nullptr, T, d, d, B.bout, EPI_RESID, s, nullptr, 0, x, d,
+         SplitIO{ch ? &so : nullptr});
+    if (ch) sx1 = take_split(T, d);
+    layer_norm_fwd(a.u, B.ga, B.ba, a.x1, a.xa[b], a.ra[b], T, d, s, ch ? &sx1 : nullptr);
+    if (ch) shf = take_split(T, f);
+    gemm(a.x1, d, nullptr, B.W0, d, a.hf, f, nullptr, T, f, d, B.b0, EPI_SILU, s, a.zf[b], f, nullptr, 0,
+         SplitIO{ch ? &sx1 : nullptr, true, ch ? &shf : nullptr});
+    gemm(a.hf, f, nullptr, B.W3, f, a.u2, d, nullptr, T, d, f, B.b3, EPI_RESID, s, nullptr, 0, a.x1, d,
+         SplitIO{ch ? &shf : nullptr});
+    if (ch && sout) *sout = take_split(T, d);
+    layer_norm_fwd(a.u2, B.gm, B.bm, out, a.xm[b], a.rm[b], T, d, s, ch ? sout : nullptr);
+  };
+  // Energy head (node or edge) on rows `rows` of the layer output.
+  auto head_fwd = [&](const float *x, const int *rows, int M, const HeadW &hw, float *y1, float *y2, float *z1,
+                      float *z2) {
+    Split16View sa, sy;
+    if (ch) {
+      sa = take_split(M, d);  // row-gathered copy of x
+      sy = take_split(M, r);
+    }
+    gemm(x, d, rows, hw.H0, d, y1, r, nullptr, M, r, d, hw.h0, EPI_SILU, s, z1, r, nullptr, 0,
+         SplitIO{ch ? &sa : nullptr, false, ch ? &sy : nullptr});
+    gemm(y1, r, nullptr, hw.H2, r, y2, r, nullptr, M, r, r, hw.h2, EPI_SILU, s, z2, r, nullptr, 0,
+         SplitIO{ch ? &sy : nullptr});
   };
 
   if (E0 > E1) CUDA_CHECK(cudaMemsetAsync(a.gfc, 0, sizeof(float) * E0, s));
@@ -485,6 +560,7 @@ void PETModel::forward_backward(bool grad) {
     E = El_[l];
     T = Tl_[l];
     at.n_atoms = N;
+    Split16View sx;
     if (E > 0) {
       FeaturizeArgs fa{};
       fa.n_edges = E; fa.d = d; fa.layer = l;
@@ -492,20 +568,30 @@ void PETModel::forward_backward(bool grad) {
       fa.nbr_species = a.nbr_species; fa.rev = a.rev; fa.edge_row = a.edge_row;
       fa.We = L.We; fa.be = L.be; fa.emb0 = emb0; fa.nbr_emb = L.nbr_emb; fa.x_prev = a.xl[0];
       fa.cat = a.cat;
+      Split16View scat, shc;
+      if (ch) {
+        scat = take_split(E, K);
+        fa.cat_split = scat;
+      }
       featurize(fa, s);
-      gemm(a.cat, K, nullptr, L.C0, K, a.hc, H, nullptr, E, H, K, L.c0, EPI_SILU, s, a.zc[l], H);
-      gemm(a.hc, H, nullptr, L.C2, H, a.xin, d, a.edge_row, E, d, H, L.c2, EPI_STORE, s);
+      if (ch) shc = take_split(E, H);
+      gemm(a.cat, K, nullptr, L.C0, K, a.hc, H, nullptr, E, H, K, L.c0, EPI_SILU, s, a.zc[l], H, nullptr, 0,
+           SplitIO{ch ? &scat : nullptr, true, ch ? &shc : nullptr});
+      if (ch) sx = take_split(T, d);
+      gemm(a.hc, H, nullptr, L.C2, H, a.xin, d, a.edge_row, E, d, H, L.c2, EPI_STORE, s, nullptr, 0, nullptr, 0,
+           SplitIO{ch ? &shc : nullptr, true, ch ? &sx : nullptr});
+    } else if (ch) {
+      sx = take_split(T, d);
     }
-    node_tokens(L.node_emb, species, a.node_row, a.xin, N, d, s);
-    block_fwd(2 * l, a.xin, a.xmid);
-    block_fwd(2 * l + 1, a.xmid, a.xl[l]);
+    node_tokens(L.node_emb, species, a.node_row, a.xin, N, d, s, ch ? &sx : nullptr);
+    Split16View smid;
+    block_fwd(2 * l, a.xin, ch ? &sx : nullptr, a.xmid, ch ? &smid : nullptr);
+    block_fwd(2 * l + 1, a.xmid, ch ? &smid : nullptr, a.xl[l], nullptr);
     // readout (pet_layers.cpp:920-1015) of the N1 atoms whose energy counts
-    gemm(a.xl[l], d, a.node_row, L.node.H0, d, a.yn1, r, nullptr, N1, r, d, L.node.h0, EPI_SILU, s, a.zn1[l], r);
-    gemm(a.yn1, r, nullptr, L.node.H2, r, a.yn2, r, nullptr, N1, r, r, L.node.h2, EPI_SILU, s, a.zn2[l], r);
+    head_fwd(a.xl[l], a.node_row, N1, L.node, a.yn1, a.yn2, a.zn1[l], a.zn2[l]);
     head_last(a.yn2, L.node.HL, L.node.hl, a.node_pred, N1, r, s);
     if (E1 > 0) {
-      gemm(a.xl[l], d, a.edge_row, L.edge.H0, d, a.ye1, r, nullptr, E1, r, d, L.edge.h0, EPI_SILU, s, a.ze1[l], r);
-      gemm(a.ye1, r, nullptr, L.edge.H2, r, a.ye2, r, nullptr, E1, r, r, L.edge.h2, EPI_SILU, s, a.ze2[l], r);
+      head_fwd(a.xl[l], a.edge_row, E1, L.edge, a.ye1, a.ye2, a.ze1[l], a.ze2[l]);
       head_last(a.ye2, L.edge.HL, L.edge.hl, a.edge_pred, E1, r, s);
       add_vec(a.edge_pred, a.gfc, E1, l > 0, s);
     }
@@ -515,39 +601,63 @@ void PETModel::forward_backward(bool grad) {
   if (!grad) return;
 
   // ---- backward ----------------------------------------------------------
+  auto head_bwd = [&](const HeadW &hw, const float *z1, const float *z2, const float *scale, const int *rows, int M,
+                      float *dst) {
+    Split16View s2, s1;
+    if (ch) s2 = take_split(M, r);
+    head_last_bwd(z2, hw.HL, scale, a.dz2, M, r, s, ch ? &s2 : nullptr);
+    if (ch) s1 = take_split(M, r);
+    gemm(a.dz2, r, nullptr, hw.H2T, r, a.dz1, r, nullptr, M, r, r, nullptr, EPI_DSILU, s, const_cast<float *>(z1), r,
+         nullptr, 0, SplitIO{ch ? &s2 : nullptr, true, ch ? &s1 : nullptr});
+    gemm(a.dz1, r, nullptr, hw.H0T, r, dst, d, rows, M, d, r, nullptr, EPI_STORE, s, nullptr, 0, nullptr, 0,
+         SplitIO{ch ? &s1 : nullptr});
+  };
   auto readout_bwd = [&](int l, float *dst) {
     const LayerW &L = g_lw[l];
-    head_last_bwd(a.zn2[l], L.node.HL, nullptr, a.dz2, N1, r, s);
-    gemm(a.dz2, r, nullptr, L.node.H2T, r, a.dz1, r, nullptr, N1, r, r, nullptr, EPI_DSILU, s, a.zn1[l], r);
-    gemm(a.dz1, r, nullptr, L.node.H0T, r, dst, d, a.node_row, N1, d, r, nullptr, EPI_STORE, s);
-    if (E1 > 0) {
-      head_last_bwd(a.ze2[l], L.edge.HL, a.fc, a.dz2, E1, r, s);
-      gemm(a.dz2, r, nullptr, L.edge.H2T, r, a.dz1, r, nullptr, E1, r, r, nullptr, EPI_DSILU, s, a.ze1[l], r);
-      gemm(a.dz1, r, nullptr, L.edge.H0T, r, dst, d, a.edge_row, E1, d, r, nullptr, EPI_STORE, s);
-    }
+    head_bwd(L.node, a.zn1[l], a.zn2[l], nullptr, a.node_row, N1, dst);
+    if (E1 > 0) head_bwd(L.edge, a.ze1[l], a.ze2[l], a.fc, a.edge_row, E1, dst);
   };
   auto block_bwd = [&](int b, const float *dy, float *dxin) {
     const BlockW &B = g_lw[b / 2].blk[b % 2];
-    layer_norm_bwd(dy, a.xm[b], a.rm[b], B.gm, a.du, T, d, s);
-    gemm(a.du, d, nullptr, B.W3T, d, a.dhf, f, nullptr, T, f, d, nullptr, EPI_DSILU, s, a.zf[b], f);
-    gemm(a.dhf, f, nullptr, B.W0T, f, a.dx1, d, nullptr, T, d, f, nullptr, EPI_RESID, s, nullptr, 0, a.du, d);
-    layer_norm_bwd(a.dx1, a.xa[b], a.ra[b], B.ga, a.du, T, d, s);
-    gemm(a.du, d, nullptr, B.WoutT, d, a.dout, d, nullptr, T, d, d, nullptr, EPI_STORE, s);
+    Split16View sdu, sdhf, sdu2, sdq;
+    if (ch) sdu = take_split(T, d);
+    layer_norm_bwd(dy, a.xm[b], a.rm[b], B.gm, a.du, T, d, s, ch ? &sdu : nullptr);
+    if (ch) sdhf = take_split(T, f);
+    gemm(a.du, d, nullptr, B.W3T, d, a.dhf, f, nullptr, T, f, d, nullptr, EPI_DSILU, s, a.zf[b], f, nullptr, 0,
+         SplitIO{ch ? &sdu : nullptr, true, ch ? &sdhf : nullptr});
+    gemm(a.dhf, f, nullptr, B.W0T, f, a.dx1, d, nullptr, T, d, f, nullptr, EPI_RESID, s, nullptr, 0, a.du, d,
+         SplitIO{ch ? &sdhf : nullptr});
+    if (ch) sdu2 = take_split(T, d);
+    layer_norm_bwd(a.dx1, a.xa[b], a.ra[b], B.ga, a.du, T, d, s, ch ? &sdu2 : nullptr);
+    gemm(a.du, d, nullptr, B.WoutT, d, a.dout, d, nullptr, T, d, d, nullptr, EPI_STORE, s, nullptr, 0, nullptr, 0,
+         SplitIO{ch ? &sdu2 : nullptr});
     at.qkv = a.qkv[b];
     at.lse = a.lse[b];
     at.d_out = a.dout;
     at.d_qkv = a.dqkv;
+    if (ch) {
+      sdq = take_split(T, 3 * d);
+      at.dqkv_split = sdq;
+    }
     attn(true, at);
+    at.dqkv_split = Split16View{};
     gemm(a.dqkv, 3 * d, nullptr, B.WinT, 3 * d, dxin, d, nullptr, T, d, 3 * d, nullptr, EPI_RESID, s, nullptr,
-         0, a.du, d);
+         0, a.du, d, SplitIO{ch ? &sdq : nullptr});
   };
   auto compress_bwd = [&](int l, const float *dtok, bool accumulate) {
     const LayerW &L = g_lw[l];
-    gemm(dtok, d, a.edge_row, L.C2T, d, a.dzc, H, nullptr, E, H, d, nullptr, EPI_DSILU, s, a.zc[l], H);
-    gemm(a.dzc, H, nullptr, L.C0T, H, a.demb, d, nullptr, E, d, H, nullptr, EPI_STORE, s);
+    Split16View sa, sz;
+    if (ch) {
+      sa = take_split(E, d);  // row-gathered copy of dtok
+      sz = take_split(E, H);
+    }
+    gemm(dtok, d, a.edge_row, L.C2T, d, a.dzc, H, nullptr, E, H, d, nullptr, EPI_DSILU, s, a.zc[l], H, nullptr, 0,
+         SplitIO{ch ? &sa : nullptr, false, ch ? &sz : nullptr});
+    gemm(a.dzc, H, nullptr, L.C0T, H, a.demb, d, nullptr, E, d, H, nullptr, EPI_STORE, s, nullptr, 0, nullptr, 0,
+         SplitIO{ch ? &sz : nullptr});
     if (l == 1)
       gemm(a.dzc, H, nullptr, L.C0T + static_cast<size_t>(2) * d * H, H, a.dmsg, d, nullptr, E, d, H, nullptr,
-           EPI_STORE, s);
+           EPI_STORE, s, nullptr, 0, nullptr, 0, SplitIO{ch ? &sz : nullptr});
     edge_embed_bwd(a.demb, d, L.We, a.g4, E, d, accumulate, s);
   };
 
@@ -588,20 +698,22 @@ void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const in
     throw Error(kErrUnsupported, "an atom has " + std::to_string(nl_.max_count) +
                                      " neighbours, above the supported maximum of " +
                                      std::to_string(attention_max_tokens(h_.d / h_.heads) - 1));
+  chain_ = chain_ok_ && max_tok_ <= attention_split_max_tokens(h_.d / h_.heads);
   // memory plan: size, allocate, assign
   const Counts c{n_local, N0, E0, N1, E1};
   Plan P, S;
-  plan_memory(P, S, in_->a, h_, c, grad);
+  plan_memory(P, S, in_->a, h_, c, grad, chain_);
   persist_.ensure(P.off);
   scratch_.ensure(S.off);
   if (use_f16_) {  // largest A operand of a 3xFP16 GEMM: [tokens, max(3d, ff, hid)]
     const size_t kmax = static_cast<size_t>(std::max({3 * h_.d, h_.ff, h_.hid}));
     const size_t mk = static_cast<size_t>(std::max(Tl_[0], Tl_[1])) * kmax;
-    split_.ensure(mk * 4 + mk / 128 + 256);
+    sp_[0].ensure(mk * 4 + mk / 128 + 256);
+    if (chain_) sp_[1].ensure(mk * 4 + mk / 128 + 256);
   }
   P = Plan{persist_.as<char>(), 0};
   S = Plan{scratch_.as<char>(), 0};
-  plan_memory(P, S, in_->a, h_, c, grad);
+  plan_memory(P, S, in_->a, h_, c, grad, chain_);
   const Acts &a = in_->a;
   EdgePrepArgs ep{};
   ep.n_atoms = N0; ep.n_edges = E0;

@@ -11,6 +11,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "kernels.cuh"
 #include "neighbor.cuh"
 
 namespace pet {
@@ -127,7 +128,14 @@ class PETModel {
   // one power-of-two scale per tensor: {first element, end element, scale}
   struct WScale { size_t begin, end; int scale; };
   std::vector<WScale> wscale_;
-  DevBuf split_;         // split-fp16 copy of a 3xFP16 GEMM's A operand
+  // Split-fp16 buffers.  sp_[0]: the A operand a 3xFP16 GEMM converts from
+  // fp32.  In chain mode (every dense layer on 3xFP16) the kernels that
+  // produce a GEMM's A operand write it in split form, alternating between
+  // sp_[0] and sp_[1]; each is consumed by the next GEMM.
+  DevBuf sp_[2];
+  bool chain_ok_ = false;  // the model's shapes allow chain mode (set at load)
+  bool chain_ = false;     // chain mode for the current prediction
+  Split16View split_view(int i, int rows, int cols);
   int weight_scale(size_t elem) const;
   DevBuf d_err_;         // device error word written by bounded waits
   std::map<std::string, const float *> wptr_;

@@ -7,6 +7,7 @@
 
 #include "common.cuh"
 #include "ops.cuh"
+#include "split16.cuh"
 
 namespace pet {
 namespace {
@@ -65,30 +66,45 @@ __global__ void k_edge_prep(EdgePrepArgs a) {
   }
 }
 
-__global__ void k_featurize(FeaturizeArgs a) {
+__device__ __forceinline__ float feat_value(const FeaturizeArgs &a, int e, int c) {
   const int d = a.d;
-  const int K = (a.layer == 0 ? 2 : 3) * d;
+  if (c < d) {
+    const float *w = a.We + 4 * c;
+    const float x = a.vec[3 * e], y = a.vec[3 * e + 1], z = a.vec[3 * e + 2];
+    return fmaf(w[2], z, fmaf(w[1], y, w[0] * x)) + w[3] * a.r[e] + a.be[c];
+  }
+  if (c < 2 * d) {
+    const float *tab = a.layer == 0 ? a.emb0 : a.nbr_emb;
+    return tab[static_cast<size_t>(a.nbr_species[e]) * d + (c - d)];
+  }
+  const int cc = c - 2 * d;
+  const int rv = a.rev[e];
+  const float m0 = a.emb0[static_cast<size_t>(a.nbr_species[e]) * d + cc];
+  const float mr = rv >= 0 ? a.x_prev[static_cast<size_t>(a.edge_row[rv]) * d + cc] : 0.0f;
+  return 0.5f * (m0 + mr);
+}
+
+__global__ void k_featurize(FeaturizeArgs a) {
+  const int K = (a.layer == 0 ? 2 : 3) * a.d;
   const int64_t total = static_cast<int64_t>(a.n_edges) * K;
   for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
        t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int e = static_cast<int>(t / K), c = static_cast<int>(t % K);
-    float v;
-    if (c < d) {
-      const float *w = a.We + 4 * c;
-      const float x = a.vec[3 * e], y = a.vec[3 * e + 1], z = a.vec[3 * e + 2];
-      v = fmaf(w[2], z, fmaf(w[1], y, w[0] * x)) + w[3] * a.r[e] + a.be[c];
-    } else if (c < 2 * d) {
-      const float *tab = a.layer == 0 ? a.emb0 : a.nbr_emb;
-      v = tab[static_cast<size_t>(a.nbr_species[e]) * d + (c - d)];
-    } else {
-      const int cc = c - 2 * d;
-      const int rv = a.rev[e];
-      const float m0 = a.emb0[static_cast<size_t>(a.nbr_species[e]) * d + cc];
-      const float mr = rv >= 0 ? a.x_prev[static_cast<size_t>(a.edge_row[rv]) * d + cc] : 0.0f;
-      v = 0.5f * (m0 + mr);
-    }
-    a.cat[t] = v;
+    a.cat[t] = feat_value(a, e, c);
   }
+}
+
+// Split-fp16 output: warp per (edge, 128-column block), 4 columns a lane.
+__global__ void k_featurize_split(FeaturizeArgs a) {
+  const int K = (a.layer == 0 ? 2 : 3) * a.d, nb = K / 128;
+  const int64_t w = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= static_cast<int64_t>(a.n_edges) * nb) return;
+  const int e = static_cast<int>(w / nb), blk = static_cast<int>(w % nb);
+  const int c = blk * 128 + lane * 4;
+  const float4 v = make_float4(feat_value(a, e, c), feat_value(a, e, c + 1), feat_value(a, e, c + 2),
+                               feat_value(a, e, c + 3));
+  warp_split_block(a.cat_split, e, blk, v, lane);
 }
 
 __global__ void k_node_tokens(const float *__restrict__ tab, const int *__restrict__ sp,
@@ -99,6 +115,21 @@ __global__ void k_node_tokens(const float *__restrict__ tab, const int *__restri
     const int i = static_cast<int>(t / d), c = static_cast<int>(t % d);
     x[static_cast<size_t>(node_row[i]) * d + c] = tab[static_cast<size_t>(sp[i]) * d + c];
   }
+}
+
+// Node tokens with the split-fp16 form of the same rows: warp per (atom, block).
+__global__ void k_node_tokens_split(const float *__restrict__ tab, const int *__restrict__ sp,
+                                    const int *__restrict__ node_row, float *__restrict__ x, int n, int d,
+                                    Split16View xs) {
+  const int nb = d / 128;
+  const int64_t w = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= static_cast<int64_t>(n) * nb) return;
+  const int i = static_cast<int>(w / nb), blk = static_cast<int>(w % nb);
+  const int c = blk * 128 + lane * 4, row = node_row[i];
+  const float4 v = *reinterpret_cast<const float4 *>(tab + static_cast<size_t>(sp[i]) * d + c);
+  *reinterpret_cast<float4 *>(x + static_cast<size_t>(row) * d + c) = v;
+  warp_split_block(xs, row, blk, v, lane);
 }
 
 __global__ void k_head_last(const float *__restrict__ y, const float *__restrict__ w,
@@ -123,6 +154,22 @@ __global__ void k_head_last_bwd(const float *__restrict__ z, const float *__rest
     const float sc = scale ? scale[m] : 1.0f;
     dz[t] = w[c] * z[t] * sc;  // z holds silu' from the forward
   }
+}
+
+// dz in split-fp16 form only: warp per (row, 128-column block).
+__global__ void k_head_last_bwd_split(const float *__restrict__ z, const float *__restrict__ w,
+                                      const float *__restrict__ scale, int rows, int r, Split16View dzs) {
+  const int nb = r / 128;
+  const int64_t wi = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wi >= static_cast<int64_t>(rows) * nb) return;
+  const int m = static_cast<int>(wi / nb), blk = static_cast<int>(wi % nb);
+  const int c = blk * 128 + lane * 4;
+  const float sc = scale ? scale[m] : 1.0f;
+  const float4 zz = *reinterpret_cast<const float4 *>(z + static_cast<size_t>(m) * r + c);
+  const float4 ww = *reinterpret_cast<const float4 *>(w + c);
+  warp_split_block(dzs, m, blk, make_float4(ww.x * zz.x * sc, ww.y * zz.y * sc, ww.z * zz.z * sc, ww.w * zz.w * sc),
+                   lane);
 }
 
 __global__ void k_atom_energy(const float *__restrict__ np, const float *__restrict__ ep,
@@ -314,16 +361,29 @@ void edge_prep(const EdgePrepArgs &a, cudaStream_t s) {
 }
 
 void featurize(const FeaturizeArgs &a, cudaStream_t s) {
-  const int64_t total = static_cast<int64_t>(a.n_edges) * (a.layer == 0 ? 2 : 3) * a.d;
+  const int K = (a.layer == 0 ? 2 : 3) * a.d;
+  const int64_t total = static_cast<int64_t>(a.n_edges) * K;
   if (total <= 0) return;
-  k_featurize<<<grid_for(total, 256), 256, 0, s>>>(a);
+  if (a.cat_split.hi) {
+    if (K % 128) throw Error(kErrInternal, "featurize: split output needs a multiple of 128 columns");
+    const int64_t threads = static_cast<int64_t>(a.n_edges) * (K / 128) * 32;
+    k_featurize_split<<<ceil_div(threads, 256), 256, 0, s>>>(a);
+  } else {
+    k_featurize<<<grid_for(total, 256), 256, 0, s>>>(a);
+  }
   CUDA_LAUNCH_CHECK();
 }
 
 void node_tokens(const float *table, const int *species, const int *node_row, float *x, int n,
-                 int d, cudaStream_t s) {
+                 int d, cudaStream_t s, const Split16View *xs) {
   if (n <= 0) return;
-  k_node_tokens<<<grid_for(static_cast<int64_t>(n) * d, 256), 256, 0, s>>>(table, species, node_row, x, n, d);
+  if (xs) {
+    if (d % 128) throw Error(kErrInternal, "node_tokens: split output needs a multiple of 128 columns");
+    k_node_tokens_split<<<ceil_div(static_cast<int64_t>(n) * (d / 128) * 32, 256), 256, 0, s>>>(
+        table, species, node_row, x, n, d, *xs);
+  } else {
+    k_node_tokens<<<grid_for(static_cast<int64_t>(n) * d, 256), 256, 0, s>>>(table, species, node_row, x, n, d);
+  }
   CUDA_LAUNCH_CHECK();
 }
 
@@ -335,9 +395,15 @@ void head_last(const float *y, const float *w, const float *b, float *pred, int 
 }
 
 void head_last_bwd(const float *z, const float *w, const float *scale, float *dz, int rows, int r,
-                   cudaStream_t s) {
+                   cudaStream_t s, const Split16View *dzs) {
   if (rows <= 0) return;
-  k_head_last_bwd<<<grid_for(static_cast<int64_t>(rows) * r, 256), 256, 0, s>>>(z, w, scale, dz, rows, r);
+  if (dzs) {
+    if (r % 128) throw Error(kErrInternal, "head_last_bwd: split output needs a multiple of 128 columns");
+    k_head_last_bwd_split<<<ceil_div(static_cast<int64_t>(rows) * (r / 128) * 32, 256), 256, 0, s>>>(
+        z, w, scale, rows, r, *dzs);
+  } else {
+    k_head_last_bwd<<<grid_for(static_cast<int64_t>(rows) * r, 256), 256, 0, s>>>(z, w, scale, dz, rows, r);
+  }
   CUDA_LAUNCH_CHECK();
 }
 

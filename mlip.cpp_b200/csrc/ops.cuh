@@ -4,6 +4,8 @@
 
 #include <cuda_runtime.h>
 
+#include "kernels.cuh"
+
 namespace pet {
 
 struct EdgePrepArgs {
@@ -30,20 +32,22 @@ struct FeaturizeArgs {
   const int *nbr_species, *rev, *edge_row;
   const float *We, *be, *emb0, *nbr_emb, *x_prev;
   float *cat;
+  Split16View cat_split;  // if set, cat is written in split-fp16 form only
 };
 void featurize(const FeaturizeArgs &a, cudaStream_t s);
 
-// X[node_row[i], :] = table[species[i], :]
+// X[node_row[i], :] = table[species[i], :]  (xs: the same rows in split form too)
 void node_tokens(const float *table, const int *species, const int *node_row, float *x, int n,
-                 int d, cudaStream_t s);
+                 int d, cudaStream_t s, const Split16View *xs = nullptr);
 
 // pred[m] = dot(y[m, :], w) + b
 void head_last(const float *y, const float *w, const float *b, float *pred, int rows, int r,
                cudaStream_t s);
 // dz[m, c] = w[c] z[m, c] scale[m], z = silu' of the forward pre-activation
 // (scale null -> 1)
+// (dzs: write dz in split form only; dz unused)
 void head_last_bwd(const float *z, const float *w, const float *scale, float *dz, int rows, int r,
-                   cudaStream_t s);
+                   cudaStream_t s, const Split16View *dzs = nullptr);
 // e_atom[i] (+)= node_pred[i] + sum_{e in i} edge_pred[e] fc[e]
 void atom_energy(const float *node_pred, const float *edge_pred, const float *fc, const int *offset,
                  float *e_atom, int n, bool accumulate, cudaStream_t s);
