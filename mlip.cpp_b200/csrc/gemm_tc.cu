@@ -936,11 +936,13 @@ void launch(const GemmArgs &a, const TCWeights &w, int *err, cudaStream_t s) {
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
-// MLIPCPP_B200_F16_TILE: 128 keeps the 128-wide tile for every N, 256 the
-// one-SM 128 x 256 tile, 512 the SM-pair 256 x 256 tile
+// Tile of the 3xFP16 GEMM.  By default 128 x 128 (3 stages, 4 TMEM
+// buffers: the MMA runs furthest ahead of the epilogue; fastest on the PET
+// layer shapes).  MLIPCPP_B200_F16_TILE selects 256 (one-SM 128 x 256) or
+// 512 (the SM-pair 256 x 256) where N allows.
 const int g_f16_bn = [] {
   const char *e = std::getenv("MLIPCPP_B200_F16_TILE");
-  return e ? std::atoi(e) : 256;
+  return e ? std::atoi(e) : 0;
 }();
 
 // Row-major [rows, cols] fp16 matrix with leading dimension ld (elements):
@@ -1020,8 +1022,9 @@ void launch16(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t s)
     k_split_a<<<ceil_div(a.M, 8), 256, 0, s>>>(a.A, a.lda, a.a_rows, a.M, a.K, a.a_split);
     CUDA_LAUNCH_CHECK();
   }
-  if (a.N % 256 == 0 && g_f16_bn == 512) launch16_pair<EPI>(a, w, err, s);
-  else if (a.N % 256 == 0 && g_f16_bn != 128) launch16_bn<EPI, 256>(a, w, err, s);
+  const int bn = g_f16_bn ? g_f16_bn : 128;
+  if (a.N % 256 == 0 && bn == 512) launch16_pair<EPI>(a, w, err, s);
+  else if (a.N % 256 == 0 && bn == 256) launch16_bn<EPI, 256>(a, w, err, s);
   else launch16_bn<EPI, 128>(a, w, err, s);
 }
 

@@ -94,17 +94,44 @@ __global__ void k_featurize(FeaturizeArgs a) {
   }
 }
 
-// Split-fp16 output: warp per (edge, 128-column block), 4 columns a lane.
+// Split-fp16 output: warp per edge, lane l holds columns 4l..4l+3 of each
+// 128-column block (d a multiple of 128, so a block lies in one section).
 __global__ void k_featurize_split(FeaturizeArgs a) {
-  const int K = (a.layer == 0 ? 2 : 3) * a.d, nb = K / 128;
-  const int64_t w = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int d = a.d, nbd = d / 128;
+  const int e = static_cast<int>((blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
-  if (w >= static_cast<int64_t>(a.n_edges) * nb) return;
-  const int e = static_cast<int>(w / nb), blk = static_cast<int>(w % nb);
-  const int c = blk * 128 + lane * 4;
-  const float4 v = make_float4(feat_value(a, e, c), feat_value(a, e, c + 1), feat_value(a, e, c + 2),
-                               feat_value(a, e, c + 3));
-  warp_split_block(a.cat_split, e, blk, v, lane);
+  if (e >= a.n_edges) return;
+  const float x = a.vec[3 * e], y = a.vec[3 * e + 1], z = a.vec[3 * e + 2], r = a.r[e];
+  const int sp = a.nbr_species[e];
+  // edge embedding W [x y z r] + b  (W rows of 4)
+  for (int k = 0; k < nbd; ++k) {
+    const int c = k * 128 + lane * 4;
+    float o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 w = __ldg(reinterpret_cast<const float4 *>(a.We + 4 * (c + j)));
+      o[j] = fmaf(w.z, z, fmaf(w.y, y, w.x * x)) + w.w * r + __ldg(a.be + c + j);
+    }
+    warp_split_block(a.cat_split, e, k, make_float4(o[0], o[1], o[2], o[3]), lane);
+  }
+  // neighbour-species embedding
+  const float *tab = (a.layer == 0 ? a.emb0 : a.nbr_emb) + static_cast<size_t>(sp) * d;
+  for (int k = 0; k < nbd; ++k) {
+    const float4 v = __ldg(reinterpret_cast<const float4 *>(tab + k * 128 + lane * 4));
+    warp_split_block(a.cat_split, e, nbd + k, v, lane);
+  }
+  if (a.layer == 0) return;
+  // message: 0.5 (embedding[nbr species] + X0[row(reverse edge)])
+  const int rv = a.rev[e];
+  const float *m0 = a.emb0 + static_cast<size_t>(sp) * d;
+  const float *mr = rv >= 0 ? a.x_prev + static_cast<size_t>(a.edge_row[rv]) * d : nullptr;
+  for (int k = 0; k < nbd; ++k) {
+    const int c = k * 128 + lane * 4;
+    const float4 p = __ldg(reinterpret_cast<const float4 *>(m0 + c));
+    const float4 q = mr ? *reinterpret_cast<const float4 *>(mr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    warp_split_block(a.cat_split, e, 2 * nbd + k,
+                     make_float4(0.5f * (p.x + q.x), 0.5f * (p.y + q.y), 0.5f * (p.z + q.z), 0.5f * (p.w + q.w)), lane);
+  }
 }
 
 __global__ void k_node_tokens(const float *__restrict__ tab, const int *__restrict__ sp,
@@ -365,9 +392,8 @@ void featurize(const FeaturizeArgs &a, cudaStream_t s) {
   const int64_t total = static_cast<int64_t>(a.n_edges) * K;
   if (total <= 0) return;
   if (a.cat_split.hi) {
-    if (K % 128) throw Error(kErrInternal, "featurize: split output needs a multiple of 128 columns");
-    const int64_t threads = static_cast<int64_t>(a.n_edges) * (K / 128) * 32;
-    k_featurize_split<<<ceil_div(threads, 256), 256, 0, s>>>(a);
+    if (a.d % 128) throw Error(kErrInternal, "featurize: split output needs d a multiple of 128");
+    k_featurize_split<<<ceil_div(static_cast<int64_t>(a.n_edges) * 32, 256), 256, 0, s>>>(a);
   } else {
     k_featurize<<<grid_for(total, 256), 256, 0, s>>>(a);
   }
