@@ -208,22 +208,37 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-// Epilogue of one thread's row segment [n0, n0 + 128): bias, activation,
+// The two warps that share a TMEM lane quarter, each with 64 columns of a
+// 128-column scale block, exchange their maxima through shared memory:
+// slot [2 (tile parity)][2 (column half)][32 (lane)], one mbarrier of 64.
+struct PairExchange {
+  float *slot;
+  uint32_t bar;
+  int parity, half;
+  volatile int *abort_flag;
+};
+
+// Epilogue of one thread's row segment [n0, n0 + NC): bias, activation,
 // fp32 store (if p.C), and for the 3xFP16 kernel (kScaled) optionally the
-// split-fp16 form of the result (p.c_split; the segment is one scale block).
-template <int EPI, bool kScaled = false>
-__device__ __forceinline__ void epilogue_store(const GemmArgs &p, int row, int n0, float (&acc)[BN],
-                                               float s_row = 1.f, float s_b = 1.f) {
-  if (row >= p.M) return;
-  const int rc = p.c_rows ? p.c_rows[row] : row;
-  float *crow = p.C ? p.C + static_cast<size_t>(rc) * p.ldc : nullptr;
+// split-fp16 form of the result (p.c_split).  NC = 128: the segment is one
+// scale block.  NC = 64: a block is shared with the partner warp (px).
+template <int EPI, bool kScaled = false, int NC = BN>
+__device__ __forceinline__ void epilogue_store(const GemmArgs &p, int row, int n0, float (&acc)[NC],
+                                               float s_row = 1.f, float s_b = 1.f,
+                                               const PairExchange *px = nullptr) {
   const bool split = kScaled && p.c_split.hi != nullptr;
+  const bool valid = row < p.M;
+  constexpr bool kShared = NC < 128;
+  if (!valid && !(split && kShared)) return;  // the block exchange needs every thread
+  const int rc = valid ? (p.c_rows ? p.c_rows[row] : row) : 0;
+  float *crow = (p.C && valid) ? p.C + static_cast<size_t>(rc) * p.ldc : nullptr;
   const float *zrow = (EPI == EPI_SILU || EPI == EPI_DSILU) ? p.Z + static_cast<size_t>(row) * p.ldz : nullptr;
   const float *rrow = EPI == EPI_RESID ? p.R + static_cast<size_t>(rc) * p.ldr : nullptr;
   // 32 columns at a time: all loads of a group (bias, Z or R, C for ACCUM)
   // are issued before its stores, so a thread waits on memory once per group
 #pragma unroll
-  for (int g = 0; g < BN; g += 32) {
+  for (int g = 0; g < NC; g += 32) {
+    if (!valid) break;
     float4 x[8], ld[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -273,11 +288,23 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs &p, int row, int n
   }
   if (split) {
     float mx = 0.f;
+    if (valid) {
 #pragma unroll
-    for (int j = 0; j < BN; ++j) mx = fmaxf(mx, fabsf(acc[j]));
+      for (int j = 0; j < NC; ++j) mx = fmaxf(mx, fabsf(acc[j]));
+    }
+    if (kShared) {
+      const int lane = threadIdx.x & 31;
+      float *slot = px->slot + px->parity * 64;
+      slot[px->half * 32 + lane] = mx;
+      mbar_arrive(px->bar);
+      if (!wait_or_abort(px->bar, px->parity, px->abort_flag)) return;
+      mx = fmaxf(mx, slot[(1 - px->half) * 32 + lane]);
+      if (!valid) return;
+    }
     const int s = split_scale_exponent(mx);
-    thread_split_store<BN>(p.c_split, rc, n0, acc, s);
-    p.c_split.sc[static_cast<size_t>(n0 / 128) * p.c_split.rows + rc] = static_cast<int8_t>(s);
+    thread_split_store<NC>(p.c_split, rc, n0, acc, s);
+    if (!kShared || px->half == 0)
+      p.c_split.sc[static_cast<size_t>(n0 / 128) * p.c_split.rows + rc] = static_cast<int8_t>(s);
   }
 }
 
@@ -511,13 +538,16 @@ struct F16Cfg {
   static constexpr int Stages = (192 * 1024) / StageBytes;
   static constexpr int Chunk = kSBlock / BK;          // k-tiles per TMEM pass (one A scale block)
   static constexpr int TmemBufs = 512 / BN_;
-  static constexpr int AccWarps = BN_ / 32;
+  // 8 accumulator warps, two per TMEM lane quarter, each with NC columns
+  static constexpr int AccWarps = 8;
+  static constexpr int NC = BN_ / 2;
   static constexpr int Threads = 64 + 32 * AccWarps;
   // 10 warps put 3 on some SM sub-partitions: 168 registers at most
-  static constexpr int LaunchBound = BN_ == 256 ? 384 : 192;
+  static constexpr int LaunchBound = 384;
   static constexpr uint32_t Sbo = 8 * RowBytes;      // bytes between 8-row swizzle atoms
   static constexpr uint64_t Layout = BN_ == 256 ? 4 : 2;  // SWIZZLE_64B : SWIZZLE_128B
-  static constexpr int Smem = Stages * StageBytes + 1024 + 256;
+  // stages, alignment, barriers, and the [4][2][2][32] block-max exchange
+  static constexpr int Smem = Stages * StageBytes + 1024 + 256 + 2048;
 };
 
 template <typename C>
@@ -537,11 +567,13 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t *gbase = smem_raw + (base - raw);
   const uint32_t bars = base + C::Stages * C::StageBytes;
-  // mbarriers: full[Stages], empty[Stages], accf[TmemBufs], acce[TmemBufs]
+  // mbarriers: full[Stages], empty[Stages], accf[TmemBufs], acce[TmemBufs],
+  // xchg[4] (block-max exchange of the two warps of each lane quarter)
   const uint32_t full0 = bars, empty0 = bars + 8 * C::Stages, accf0 = bars + 16 * C::Stages,
-                 acce0 = accf0 + 8 * C::TmemBufs;
+                 acce0 = accf0 + 8 * C::TmemBufs, xchg0 = acce0 + 8 * C::TmemBufs;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + C::Stages * C::StageBytes + 192);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(gbase + C::Stages * C::StageBytes + 200);
+  float *xslots = reinterpret_cast<float *>(gbase + C::Stages * C::StageBytes + 256);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nk = p.K / C::BK;
@@ -562,6 +594,7 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
       mbar_init(accf0 + 8 * b, 1);
       mbar_init(acce0 + 8 * b, 32 * C::AccWarps);
     }
+    for (int q = 0; q < 4; ++q) mbar_init(xchg0 + 8 * q, 64);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -635,18 +668,19 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
     }
     __syncwarp();
   } else {
-    // ------- accumulators + epilogue: warp -> (TMEM lane quarter, 128-column half) -------
+    // ------- accumulators + epilogue: warp -> (TMEM lane quarter, column half of NC) -------
+    constexpr int NC = C::NC;
     const int q = warp & 3;
     const int h = (warp - 2) / 4;
     const float sb = pow2f(-b_scale);
-    int chunk = 0;
+    int chunk = 0, ep = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-      const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BNt + h * 128;
+    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ep) {
+      const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BNt + h * NC;
       const int row = m0 + q * 32 + lane;
-      float acc[128];
+      float acc[NC];
 #pragma unroll
-      for (int j = 0; j < 128; ++j) acc[j] = 0.f;
+      for (int j = 0; j < NC; ++j) acc[j] = 0.f;
       for (int kt0 = 0; kt0 < nk; kt0 += C::Chunk, ++chunk) {
         const int b = chunk % C::TmemBufs;
         const float sa = row < p.M ? pow2f(-static_cast<int>(sc[static_cast<size_t>(kt0 / C::Chunk) * p.M + row])) : 0.f;
@@ -656,9 +690,9 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
         }
         tc_fence_after();
         const uint32_t taddr =
-            tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BNt + h * 128);
+            tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * BNt + h * NC);
 #pragma unroll
-        for (int c0 = 0; c0 < 128; c0 += 32) {
+        for (int c0 = 0; c0 < NC; c0 += 32) {
           float v[32];
           tmem_ld32(taddr + c0, v);
 #pragma unroll
@@ -667,7 +701,10 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
         tc_fence_before();
         mbar_arrive(acce0 + 8 * b);
       }
-      if (ok) epilogue_store<EPI, true>(p, row, n0, acc, 1.f, sb);
+      if (ok) {
+        const PairExchange px{xslots + q * 128, xchg0 + 8 * q, ep & 1, h, abort_flag};
+        epilogue_store<EPI, true, NC>(p, row, n0, acc, 1.f, sb, &px);
+      }
     }
   }
 
