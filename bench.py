@@ -308,10 +308,10 @@ def main():
                          "tensor_pipe_frac_of_bf16": div * achieved / bf16_sus,
                          # DRAM bytes per average GEMM launch: ncu dram__bytes_read.sum +
                          # dram__bytes_write.sum over all 57 GEMM launches of one step of the
-                         # 1,728-atom cell of this alloy (354 MB/launch at 65,202 tokens,
-                         # 5,429 B per token), scaled by this step's token count
-                         "traffic": (5429.0 * (shape["atoms"] + shape["edges"])
-                                     if not domains and not f16 else None),
+                         # 1,728-atom cell of this alloy (356 MB/launch at 65,202 tokens,
+                         # 5,453 B per token for the 3xFP16 build), scaled by this step's tokens
+                         "traffic": (5453.0 * (shape["atoms"] + shape["edges"])
+                                     if not domains and f16 else None),
                          "traffic_unit": "bytes per GEMM launch (scaled from the 1,728-atom capture)",
                          "gemm_share_of_step": gemm_ms / (t_dev * 1e3) if t_dev else None},
             "kernel_stats": kstats,
