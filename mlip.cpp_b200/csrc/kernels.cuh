@@ -73,6 +73,10 @@ struct AttnArgs {
   Split16View dqkv_split;
 };
 void attention_fwd(const AttnArgs &a, cudaStream_t stream);
+// Tensor-core forward (attention_tc.cu): head size 32, at most 64 tokens per
+// atom, heads a multiple of 4.  `err` (device int) is set if a wait times out.
+bool attention_tc_supported(const AttnArgs &a);
+void attention_fwd_tc(const AttnArgs &a, int *err, cudaStream_t stream);
 void attention_bwd(const AttnArgs &a, cudaStream_t stream);
 // Largest per-atom token count the attention kernels accept for head size hd.
 int attention_max_tokens(int hd);

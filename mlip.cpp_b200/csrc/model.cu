@@ -299,6 +299,10 @@ void PETModel::load(const std::string &path, float cutoff_override) {
   use_tc_ = !(g && std::string(g) == "simt");
   use_f16_ = use_tc_ && !(g && std::string(g) == "tf32");
   {
+    const char *at = std::getenv("MLIPCPP_B200_ATTN");
+    use_attn_tc_ = at && std::string(at) == "tc";
+  }
+  {
     // chain mode: every dense layer's K and N a multiple of 128 (K <= 2048),
     // 128 / head-size heads form one 128-column block, layer norms of <= 1024
     const int hd = h.d / h.heads;
@@ -498,7 +502,9 @@ void PETModel::forward_backward(bool grad) {
   auto attn = [&](bool backward, const AttnArgs &x) {
     cudaEvent_t e0 = nullptr;
     if (kprof_) mark_begin(e0);
-    if (backward) attention_bwd(x, s); else attention_fwd(x, s);
+    if (backward) attention_bwd(x, s);
+    else if (use_attn_tc_ && attention_tc_supported(x)) attention_fwd_tc(x, d_err_.as<int>(), s);
+    else attention_fwd(x, s);
     if (kprof_) mark_end(KC_ATTENTION, e0, 0.0, 4.0 * T * (backward ? 7.0 : 4.0) * d);
     (void)x;
   };

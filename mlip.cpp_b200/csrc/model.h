@@ -124,6 +124,9 @@ class PETModel {
   size_t wspan_ = 0;     // floats between the three copies
   bool use_tc_ = true;   // tensor-core GEMMs (MLIPCPP_B200_GEMM=simt disables)
   bool use_f16_ = true;  // 3xFP16 where it applies (MLIPCPP_B200_GEMM=tf32 keeps 3xTF32)
+  // tensor-core attention forward (MLIPCPP_B200_ATTN=tc): correct, but slower
+  // than the SIMT kernel at this size (see attention_tc.cu)
+  bool use_attn_tc_ = false;
   // fp16 hi / lo copies after the three fp32 copies, same element offsets;
   // one power-of-two scale per tensor: {first element, end element, scale}
   struct WScale { size_t begin, end; int scale; };

@@ -169,3 +169,16 @@ def test_gpu_tensor_core_matches_simt(mode, model_file, monkeypatch):
     if mode == "tf32":
         assert st["gemm_f16"]["launches"] == 0
     assert_close(tc, simt.energy, simt.forces, simt.stress, s.n_atoms)
+
+
+def test_gpu_tensor_core_attention_matches_simt(model_file, monkeypatch):
+    """The tcgen05 attention forward and the SIMT attention agree within the
+    fp32 parity tolerances on the same inputs (including an odd atom count,
+    whose last CTA has one atom)."""
+    path = model_file("pet-oam-l", 9)
+    s = wl.fcc_alloy(3, seed=9)  # 27 atoms
+    monkeypatch.setenv("MLIPCPP_B200_ATTN", "simt")
+    ref = mb.Predictor(path).predict(s.positions, s.numbers, s.cell, compute_stress=True)
+    monkeypatch.setenv("MLIPCPP_B200_ATTN", "tc")
+    res = mb.Predictor(path).predict(s.positions, s.numbers, s.cell, compute_stress=True)
+    assert_close(res, ref.energy, ref.forces, ref.stress, s.n_atoms)
