@@ -215,6 +215,7 @@ mlipcpp_error_t mlipcpp_model_load(mlipcpp_model_t model, const char *path) {
     }
     auto m = std::make_unique<pet::PETModel>();
     m->load(path, model->options.cutoff_override);
+    m->set_reduced_precision(model->options.precision == MLIPCPP_PRECISION_F16);
     model->model = std::move(m);
     model->loaded = true;
     clear_error();

@@ -455,7 +455,8 @@ template <int EPI, int BNt>
 __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
     k_gemm_3xf16(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
                  const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
-                 GemmArgs p, const int8_t *__restrict__ sc, int b_scale, int *err) {
+                 GemmArgs p, const int8_t *__restrict__ sc, TCWeights16 w, int *err) {
+  const int b_scale = w.b_scale;
   using C = F16Cfg<BNt>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -513,11 +514,17 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
           }
           const uint32_t st = base + s * C::StageBytes;
           const uint32_t fb = full0 + 8 * s;
-          mbar_expect_tx(fb, C::StageBytes);
-          tma_load_2d(st, &tAh, fb, kt * C::BK, m0);
-          tma_load_2d(st + C::ATile, &tAl, fb, kt * C::BK, m0);
-          tma_load_2d(st + 2 * C::ATile, &tBh, fb, kt * C::BK, n0);
-          tma_load_2d(st + 2 * C::ATile + C::BTile, &tBl, fb, kt * C::BK, n0);
+          if (w.products == 1) {  // hi tiles only
+            mbar_expect_tx(fb, C::ATile + C::BTile);
+            tma_load_2d(st, &tAh, fb, kt * C::BK, m0);
+            tma_load_2d(st + 2 * C::ATile, &tBh, fb, kt * C::BK, n0);
+          } else {
+            mbar_expect_tx(fb, C::StageBytes);
+            tma_load_2d(st, &tAh, fb, kt * C::BK, m0);
+            tma_load_2d(st + C::ATile, &tAl, fb, kt * C::BK, m0);
+            tma_load_2d(st + 2 * C::ATile, &tBh, fb, kt * C::BK, n0);
+            tma_load_2d(st + 2 * C::ATile + C::BTile, &tBl, fb, kt * C::BK, n0);
+          }
         }
       }
     }
@@ -547,13 +554,22 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
             const uint32_t st = base + s * C::StageBytes;
             const uint32_t sAhi = st, sAlo = st + C::ATile, sBhi = st + 2 * C::ATile,
                            sBlo = st + 2 * C::ATile + C::BTile;
+            if (w.products == 1) {
 #pragma unroll
-            for (int kk = 0; kk < C::BK / 16; ++kk) {
-              const uint32_t ko = kk * 32;  // 16 fp16 = 32 bytes per MMA k-step
-              mma_f16(dtm, kmajor_desc<C>(sAlo + ko), kmajor_desc<C>(sBhi + ko), idesc,
-                      (kt > kt0 || kk > 0) ? 1u : 0u);
-              mma_f16(dtm, kmajor_desc<C>(sAhi + ko), kmajor_desc<C>(sBlo + ko), idesc, 1u);
-              mma_f16(dtm, kmajor_desc<C>(sAhi + ko), kmajor_desc<C>(sBhi + ko), idesc, 1u);
+              for (int kk = 0; kk < C::BK / 16; ++kk) {
+                const uint32_t ko = kk * 32;
+                mma_f16(dtm, kmajor_desc<C>(sAhi + ko), kmajor_desc<C>(sBhi + ko), idesc,
+                        (kt > kt0 || kk > 0) ? 1u : 0u);
+              }
+            } else {
+#pragma unroll
+              for (int kk = 0; kk < C::BK / 16; ++kk) {
+                const uint32_t ko = kk * 32;  // 16 fp16 = 32 bytes per MMA k-step
+                mma_f16(dtm, kmajor_desc<C>(sAlo + ko), kmajor_desc<C>(sBhi + ko), idesc,
+                        (kt > kt0 || kk > 0) ? 1u : 0u);
+                mma_f16(dtm, kmajor_desc<C>(sAhi + ko), kmajor_desc<C>(sBlo + ko), idesc, 1u);
+                mma_f16(dtm, kmajor_desc<C>(sAhi + ko), kmajor_desc<C>(sBhi + ko), idesc, 1u);
+              }
             }
             mma_commit(empty0 + 8 * s);
           }
@@ -911,7 +927,7 @@ void launch16_bn(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t
   CUDA_CHECK(cudaFuncSetAttribute(k_gemm_3xf16<EPI, BNt>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::Smem));
   const int tiles = ceil_div(a.M, BM) * (a.N / BNt);
   const int grid = tiles < g_num_sms ? tiles : g_num_sms;
-  k_gemm_3xf16<EPI, BNt><<<grid, C::Threads, C::Smem, s>>>(ah, al, bh, bl, a, sp.sc, w.b_scale, err);
+  k_gemm_3xf16<EPI, BNt><<<grid, C::Threads, C::Smem, s>>>(ah, al, bh, bl, a, sp.sc, w, err);
   CUDA_LAUNCH_CHECK();
 }
 
@@ -955,7 +971,7 @@ void launch16(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t s)
     CUDA_LAUNCH_CHECK();
   }
   const int bn = g_f16_bn ? g_f16_bn : 128;
-  if (a.N % 256 == 0 && bn == 512) launch16_pair<EPI>(a, w, err, s);
+  if (a.N % 256 == 0 && bn == 512 && w.products == 3) launch16_pair<EPI>(a, w, err, s);
   else if (a.N % 256 == 0 && bn == 256) launch16_bn<EPI, 256>(a, w, err, s);
   else launch16_bn<EPI, 128>(a, w, err, s);
 }

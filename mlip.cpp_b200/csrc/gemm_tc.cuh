@@ -22,6 +22,9 @@ struct TCWeights16 {
   const uint16_t *hi = nullptr;
   const uint16_t *lo = nullptr;
   int b_scale = 0;
+  // 3: A_hi B_hi + A_hi B_lo + A_lo B_hi (fp32 accuracy); 1: A_hi B_hi only
+  // (the reduced-precision mode: 11 significant bits per operand)
+  int products = 3;
 };
 
 // True when the shape and alignment fit the tensor-core kernel (N multiple

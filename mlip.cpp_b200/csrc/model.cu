@@ -487,7 +487,8 @@ void PETModel::forward_backward(bool grad) {
         g.a_split_ready = false;
       }
       if (io.c) g.c_split = *io.c;
-      gemm_3xf16(g, TCWeights16{h16 + eoff, h16 + wspan_ + eoff, weight_scale(eoff)}, d_err_.as<int>(), st);
+      gemm_3xf16(g, TCWeights16{h16 + eoff, h16 + wspan_ + eoff, weight_scale(eoff), reduced_ ? 1 : 3},
+                 d_err_.as<int>(), st);
     } else if (io.c || (io.a && io.a_ready)) {
       throw Error(kErrInternal, "split-fp16 operands need the 3xFP16 GEMM");
     } else if (tc) {

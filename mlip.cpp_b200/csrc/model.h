@@ -127,6 +127,14 @@ class PETModel {
   // tensor-core attention forward (MLIPCPP_B200_ATTN=tc): correct, but slower
   // than the SIMT kernel at this size (see attention_tc.cu)
   bool use_attn_tc_ = false;
+  // MLIPCPP_PRECISION_F16: dense layers with the hi x hi product only
+  bool reduced_ = false;
+
+ public:
+  void set_reduced_precision(bool on) { reduced_ = on; }
+  bool reduced_precision() const { return reduced_; }
+
+ private:
   // fp16 hi / lo copies after the three fp32 copies, same element offsets;
   // one power-of-two scale per tensor: {first element, end element, scale}
   struct WScale { size_t begin, end; int scale; };

@@ -182,3 +182,27 @@ def test_gpu_tensor_core_attention_matches_simt(model_file, monkeypatch):
     monkeypatch.setenv("MLIPCPP_B200_ATTN", "tc")
     res = mb.Predictor(path).predict(s.positions, s.numbers, s.cell, compute_stress=True)
     assert_close(res, ref.energy, ref.forces, ref.stress, s.n_atoms)
+
+
+# Stated tolerances of the reduced-precision mode (MLIPCPP_PRECISION_F16: dense
+# layers multiply fp16 hi parts only, 11 significant bits per operand) against
+# the fp32 path (about 4x the largest differences measured on these cases:
+# 5.3e-4 eV/atom, 2.5e-3 eV/A, 1.8e-4 eV/A^3 for pet-oam-l).
+TOL_E16, TOL_F16, TOL_S16 = 2e-3, 1e-2, 1e-3
+
+
+@pytest.mark.parametrize("hname,make", [("pet-mad-s", lambda: wl.si_diamond(3, seed=13)),
+                                        ("pet-oam-l", lambda: wl.fcc_alloy(6, seed=13))])
+def test_gpu_reduced_precision_mode(hname, make, model_file):
+    path = model_file(hname, 13)
+    s = make()
+    ref = mb.Predictor(path).predict(s.positions, s.numbers, s.cell, compute_stress=True)
+    pred = mb.Predictor(path, mb.ModelOptions(precision=1))
+    pred.set_kernel_profiling(True)
+    res = pred.predict(s.positions, s.numbers, s.cell, compute_stress=True)
+    assert pred.kernel_stats()["gemm_f16"]["launches"] > 0
+    de = abs(res.energy - ref.energy) / s.n_atoms
+    df = np.abs(res.forces - ref.forces).max()
+    ds = np.abs(res.stress - ref.stress).max()
+    print(f"{hname}: |dE|/N {de:.2e}  |dF| {df:.2e}  |dS| {ds:.2e}")
+    assert de <= TOL_E16 and df <= TOL_F16 and ds <= TOL_S16
