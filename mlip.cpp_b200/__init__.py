@@ -328,10 +328,13 @@ class Predictor:
             out[k] = (8.0 * (e[1] - e[-1]) - (e[2] - e[-2])) / (12.0 * vol * delta)
         return out
 
-    def predict_batch(self, systems, compute_forces=True, compute_stress=False) -> list[Result]:
+    def predict_batch(self, systems, compute_forces=True, compute_stress=False,
+                      use_nc_forces=False) -> list[Result]:
         """Batched prediction (extension; PETModel::predict_batch in the
         reference).  `systems`: iterable of objects with positions, numbers,
-        cell and pbc attributes, or (positions, numbers[, cell[, pbc]])."""
+        cell and pbc attributes, or (positions, numbers[, cell[, pbc]]).
+        use_nc_forces: forces and stress from the model's non-conservative
+        heads instead of gradients, as in PredictOptions."""
         structs, keeps, ns = [], [], []
         for sy in systems:
             if hasattr(sy, "positions"):
@@ -345,18 +348,19 @@ class Predictor:
         n = len(structs)
         arr = (_System * max(n, 1))(*structs)
         handles = (ctypes.c_void_p * max(n, 1))()
-        po = _PredictOptions(compute_forces or compute_stress, compute_stress, False)
+        po = _PredictOptions(compute_forces or compute_stress, compute_stress, use_nc_forces)
         _check(lib().mlipcpp_predict_batch(self._h, n, arr, ctypes.byref(po), handles))
         return [_read_result(handles[k], ns[k]) for k in range(n)]
 
     def predict_device(self, d_positions: int, n_atoms: int, atomic_numbers, cell=None, pbc=None,
-                       compute_forces=True, compute_stress=False, copy_forces=True) -> Result:
+                       compute_forces=True, compute_stress=False, copy_forces=True,
+                       use_nc_forces=False) -> Result:
         """Positions already in device memory (`d_positions`: device pointer
         to [3n] float32)."""
         z = np.ascontiguousarray(atomic_numbers, dtype=np.int32)
         c = None if cell is None else np.ascontiguousarray(cell, dtype=np.float32).reshape(9)
         p = None if c is None else np.asarray([True] * 3 if pbc is None else list(pbc), np.bool_)
-        po = _PredictOptions(compute_forces or compute_stress, compute_stress, False)
+        po = _PredictOptions(compute_forces or compute_stress, compute_stress, use_nc_forces)
         h = ctypes.c_void_p()
         _check(lib().mlipcpp_b200_predict_device(
             self._h, n_atoms, ctypes.c_void_p(d_positions), z.ctypes.data,

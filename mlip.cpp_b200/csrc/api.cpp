@@ -331,7 +331,7 @@ mlipcpp_error_t mlipcpp_predict_with_options(mlipcpp_model_t model, const mlipcp
   try {
     const bool grad = (options->compute_forces || options->compute_stress) && !options->use_nc_forces;
     std::vector<pet::SystemView> v{make_view(system)};
-    auto out = model->model->predict(v, grad);
+    auto out = model->model->predict(v, grad, options->use_nc_forces);
     model->last = std::move(out[0]);
     finish_options(model->last, *options);
     auto r = std::make_unique<mlipcpp_result_impl>();
@@ -482,7 +482,7 @@ mlipcpp_error_t mlipcpp_predict_batch(mlipcpp_model_t model, int32_t n_systems,
     const bool grad = (options->compute_forces || options->compute_stress) && !options->use_nc_forces;
     std::vector<pet::SystemView> v;
     for (int k = 0; k < n_systems; ++k) v.push_back(make_view(&systems[k]));
-    auto out = model->model->predict(v, grad);
+    auto out = model->model->predict(v, grad, options->use_nc_forces);
     for (int k = 0; k < n_systems; ++k) {
       auto r = std::make_unique<mlipcpp_result_impl>();
       r->own = std::move(out[k]);
@@ -520,7 +520,7 @@ mlipcpp_error_t mlipcpp_b200_predict_device(mlipcpp_model_t model, int32_t n_ato
   try {
     const bool grad = (options->compute_forces || options->compute_stress) && !options->use_nc_forces;
     pet::SystemView v = make_view(&s);
-    model->model->predict_device(d_positions, v, grad, model->last, copy_forces);
+    model->model->predict_device(d_positions, v, grad, model->last, copy_forces, options->use_nc_forces);
     finish_options(model->last, *options);
     auto r = std::make_unique<mlipcpp_result_impl>();
     r->result = &model->last;

@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(256) k_gemm_f32(GemmArgs p) {
         } else if (EPI == EPI_SILU) {
           float y, dy;
           silu_pair(v, y, dy);
-          p.Z[static_cast<size_t>(m) * p.ldz + n] = dy;
+          if (p.Z) p.Z[static_cast<size_t>(m) * p.ldz + n] = dy;
           crow[n] = y;
         } else if (EPI == EPI_ACCUM) {
           crow[n] += v;

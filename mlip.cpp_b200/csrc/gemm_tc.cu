@@ -127,7 +127,8 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs &p, int row, int n
   if (!valid && !(split && kShared)) return;  // the block exchange needs every thread
   const int rc = valid ? (p.c_rows ? p.c_rows[row] : row) : 0;
   float *crow = (p.C && valid) ? p.C + static_cast<size_t>(rc) * p.ldc : nullptr;
-  const float *zrow = (EPI == EPI_SILU || EPI == EPI_DSILU) ? p.Z + static_cast<size_t>(row) * p.ldz : nullptr;
+  // EPI_SILU with Z == null: no derivative kept (forward-only passes)
+  const float *zrow = ((EPI == EPI_SILU || EPI == EPI_DSILU) && p.Z) ? p.Z + static_cast<size_t>(row) * p.ldz : nullptr;
   const float *rrow = EPI == EPI_RESID ? p.R + static_cast<size_t>(rc) * p.ldr : nullptr;
   // 32 columns at a time: all loads of a group (bias, Z or R, C for ACCUM)
   // are issued before its stores, so a thread waits on memory once per group
@@ -168,7 +169,7 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs &p, int row, int n
         float4 dy;
         silu_pair(x[k].x, out.x, dy.x); silu_pair(x[k].y, out.y, dy.y);
         silu_pair(x[k].z, out.z, dy.z); silu_pair(x[k].w, out.w, dy.w);
-        *reinterpret_cast<float4 *>(const_cast<float *>(zrow) + n) = dy;
+        if (zrow) *reinterpret_cast<float4 *>(const_cast<float *>(zrow) + n) = dy;
       } else if (EPI == EPI_DSILU) {
         out = make_float4(x[k].x * ld[k].x, x[k].y * ld[k].y, x[k].z * ld[k].z, x[k].w * ld[k].w);
       } else {  // EPI_RESID, EPI_ACCUM: x + R or x + C

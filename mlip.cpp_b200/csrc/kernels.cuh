@@ -13,7 +13,7 @@ namespace pet {
 
 enum Epilogue : int {
   EPI_STORE = 0,    // C = acc + bias
-  EPI_SILU = 1,     // z = acc + bias: C = silu(z), Z[m] = silu'(z) (kept for the backward)
+  EPI_SILU = 1,     // z = acc + bias: C = silu(z), Z[m] = silu'(z) (kept for the backward; Z may be null)
   EPI_ACCUM = 2,    // C += acc + bias
   EPI_DSILU = 3,    // C = acc * Z[m]  (Z = silu' from the forward)
   EPI_RESID = 4,    // C = acc + bias + R[row_c(m)]

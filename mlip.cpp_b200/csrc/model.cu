@@ -49,10 +49,17 @@ struct BlockW {
 struct HeadW {
   const float *H0, *h0, *H2, *h2, *HL, *hl, *H0T, *H2T;
 };
+// A forward-only property head (PropertyHead, pet_types.h:83-107):
+// node and edge MLPs d -> dh -> dh -> od.
+struct PropW {
+  HeadW node{}, edge{};
+  bool loaded = false;
+};
 struct LayerW {
   const float *We, *be, *node_emb, *nbr_emb, *C0, *c0, *C2, *c2, *C0T, *C2T;
   BlockW blk[2];
   HeadW node, edge;
+  PropW nc[2];  // non-conservative heads: [0] forces (od 3), [1] stress (od 9)
 };
 
 struct Acts {
@@ -63,6 +70,8 @@ struct Acts {
   float *qkv[4], *xa[4], *ra[4], *zf[4], *xm[4], *rm[4], *lse[4];
   float *zc[2], *zn1[2], *zn2[2], *ze1[2], *ze2[2];
   float *gfc, *e_atom;
+  // non-conservative outputs per atom: forces [N1, 3], stress [N1, 9]
+  float *ncF, *ncS;
   // forward scratch
   float *cat, *hc, *xin, *xmid, *xl[2], *o, *u, *x1, *hf, *u2, *yn1, *yn2, *ye1, *ye2, *node_pred,
       *edge_pred;
@@ -367,6 +376,43 @@ void PETModel::load(const std::string &path, float cutoff_override) {
       H.H0T = w(hp + "0.weight.T"); H.H2T = w(hp + "2.weight.T");
     }
   }
+  // Non-conservative property heads (pet.cpp:1263-1269, names
+  // pet_types.h:130-138).  A layer's head counts when its node_heads.*.0
+  // weight exists (PropertyHead::is_loaded); the property is used when
+  // layer 0 has one (PETWeights::has_property).
+  static const char *const kProp[2] = {"nc_forces", "nc_stress"};
+  static const char *const kLast[2] = {"nc_f", "nc_s"};
+  static const int kOut[2] = {3, 9};
+  for (int p = 0; p < 2; ++p) {
+    for (int l = 0; l < 2; ++l) {
+      PropW &P = in_->lw[l].nc[p];
+      P = PropW{};
+      const std::string ls = std::to_string(l);
+      if (!f.tensor(std::string("model.node_heads.") + kProp[p] + "." + ls + ".0.weight")) continue;
+      for (int k = 0; k < 2; ++k) {
+        const std::string kind = k == 0 ? "node" : "edge";
+        const std::string hp = "model." + kind + "_heads." + kProp[p] + "." + ls + ".";
+        const std::string lp = "model." + kind + "_last_layers." + kProp[p] + "." + ls + "." + kLast[p] + ".";
+        auto shape_is = [&](const std::string &name, int64_t in, int64_t out) {
+          const GGUFTensor *t = f.tensor(name);
+          if (!t) throw Error(kErrIO, "Required tensor '" + name + "' not found");
+          if (t->ne.size() < 2 || t->ne[0] != in || t->ne[1] != out)
+            throw Error(kErrUnsupported, "tensor '" + name + "' has an unsupported shape (expected [" +
+                                             std::to_string(out) + ", " + std::to_string(in) + "])");
+        };
+        shape_is(hp + "0.weight", h.d, h.dh);
+        shape_is(hp + "2.weight", h.dh, h.dh);
+        shape_is(lp + "weight", h.dh, kOut[p]);
+        HeadW &H = k == 0 ? P.node : P.edge;
+        H.H0 = w(hp + "0.weight"); H.h0 = w(hp + "0.bias");
+        H.H2 = w(hp + "2.weight"); H.h2 = w(hp + "2.bias");
+        H.HL = w(lp + "weight"); H.hl = w(lp + "bias");
+      }
+      P.loaded = true;
+    }
+  }
+  has_ncf_ = in_->lw[0].nc[0].loaded;
+  has_ncs_ = in_->lw[0].nc[1].loaded;
   (void)w("model.embedding.weight");
 }
 
@@ -380,7 +426,8 @@ struct Counts {
   int n_local, N0, E0, N1, E1;
 };
 
-static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, const Counts &c, bool grad, bool chain) {
+static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, const Counts &c, bool grad, bool chain,
+                        bool ncf, bool ncs) {
   const size_t d = h.d, f = h.ff, r = h.dh, H = h.hid;
   const size_t E0 = std::max(c.E0, 1), N0 = std::max(c.N0, 1), E1 = std::max(c.E1, 1),
                N1 = std::max(c.N1, 1), NL = std::max(c.n_local, 1);
@@ -406,6 +453,8 @@ static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, const Counts
   a.gfc = P.take<float>(E0);
   a.e_atom = P.take<float>(N1);
   a.F = P.take<float>(3 * NL);
+  a.ncF = ncf ? P.take<float>(3 * N1) : nullptr;
+  a.ncS = ncs ? P.take<float>(9 * N1) : nullptr;
   a.g = P.take<float>(3 * E0);
   a.g4 = P.take<float>(4 * E0);
   // forward scratch
@@ -450,6 +499,8 @@ void PETModel::forward_backward(bool grad) {
   const int *species = d_species_.as<int>();
   const float *emb0 = w("model.embedding.weight");
   const bool ch = chain_;
+  // silu' is kept for the backward only
+  auto keep = [grad](float *z) { return grad ? z : nullptr; };
 
   // Split-fp16 operands of the chain mode: each producer takes the next
   // buffer; the GEMM that consumes it runs before the buffer comes round
@@ -538,7 +589,7 @@ void PETModel::forward_backward(bool grad) {
     if (ch) sx1 = take_split(T, d);
     layer_norm_fwd(a.u, B.ga, B.ba, a.x1, a.xa[b], a.ra[b], T, d, s, ch ? &sx1 : nullptr);
     if (ch) shf = take_split(T, f);
-    gemm(a.x1, d, nullptr, B.W0, d, a.hf, f, nullptr, T, f, d, B.b0, EPI_SILU, s, a.zf[b], f, nullptr, 0,
+    gemm(a.x1, d, nullptr, B.W0, d, a.hf, f, nullptr, T, f, d, B.b0, EPI_SILU, s, keep(a.zf[b]), f, nullptr, 0,
          SplitIO{ch ? &sx1 : nullptr, true, ch ? &shf : nullptr});
     gemm(a.hf, f, nullptr, B.W3, f, a.u2, d, nullptr, T, d, f, B.b3, EPI_RESID, s, nullptr, 0, a.x1, d,
          SplitIO{ch ? &shf : nullptr});
@@ -553,13 +604,15 @@ void PETModel::forward_backward(bool grad) {
       sa = take_split(M, d);  // row-gathered copy of x
       sy = take_split(M, r);
     }
-    gemm(x, d, rows, hw.H0, d, y1, r, nullptr, M, r, d, hw.h0, EPI_SILU, s, z1, r, nullptr, 0,
+    gemm(x, d, rows, hw.H0, d, y1, r, nullptr, M, r, d, hw.h0, EPI_SILU, s, keep(z1), r, nullptr, 0,
          SplitIO{ch ? &sa : nullptr, false, ch ? &sy : nullptr});
-    gemm(y1, r, nullptr, hw.H2, r, y2, r, nullptr, M, r, r, hw.h2, EPI_SILU, s, z2, r, nullptr, 0,
+    gemm(y1, r, nullptr, hw.H2, r, y2, r, nullptr, M, r, r, hw.h2, EPI_SILU, s, keep(z2), r, nullptr, 0,
          SplitIO{ch ? &sy : nullptr});
   };
 
   if (E0 > E1) CUDA_CHECK(cudaMemsetAsync(a.gfc, 0, sizeof(float) * E0, s));
+  if (ncf_) CUDA_CHECK(cudaMemsetAsync(a.ncF, 0, sizeof(float) * 3 * N1, s));
+  if (ncs_) CUDA_CHECK(cudaMemsetAsync(a.ncS, 0, sizeof(float) * 9 * N1, s));
   for (int l = 0; l < 2; ++l) {
     const LayerW &L = g_lw[l];
     const int K = (l == 0 ? 2 : 3) * d;
@@ -582,7 +635,7 @@ void PETModel::forward_backward(bool grad) {
       }
       featurize(fa, s);
       if (ch) shc = take_split(E, H);
-      gemm(a.cat, K, nullptr, L.C0, K, a.hc, H, nullptr, E, H, K, L.c0, EPI_SILU, s, a.zc[l], H, nullptr, 0,
+      gemm(a.cat, K, nullptr, L.C0, K, a.hc, H, nullptr, E, H, K, L.c0, EPI_SILU, s, keep(a.zc[l]), H, nullptr, 0,
            SplitIO{ch ? &scat : nullptr, true, ch ? &shc : nullptr});
       if (ch) sx = take_split(T, d);
       gemm(a.hc, H, nullptr, L.C2, H, a.xin, d, a.edge_row, E, d, H, L.c2, EPI_STORE, s, nullptr, 0, nullptr, 0,
@@ -603,6 +656,16 @@ void PETModel::forward_backward(bool grad) {
       add_vec(a.edge_pred, a.gfc, E1, l > 0, s);
     }
     atom_energy(a.node_pred, a.edge_pred, a.fc, offset, a.e_atom, N1, l > 0, s);
+    // non-conservative heads of this layer (build_property_output,
+    // pet_layers.cpp:845-915), summed over the layers per atom
+    for (int p = 0; p < 2; ++p) {
+      const PropW &P = L.nc[p];
+      if (!P.loaded || !(p == 0 ? ncf_ : ncs_)) continue;
+      head_fwd(a.xl[l], a.node_row, N1, P.node, a.yn1, a.yn2, nullptr, nullptr);
+      if (E1 > 0) head_fwd(a.xl[l], a.edge_row, E1, P.edge, a.ye1, a.ye2, nullptr, nullptr);
+      nc_readout(a.yn2, E1 > 0 ? a.ye2 : nullptr, P.node.HL, P.node.hl, P.edge.HL, P.edge.hl, a.fc, offset,
+                 p == 0 ? a.ncF : a.ncS, N1, r, p == 0 ? 3 : 9, s);
+    }
   }
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[4], s));
   if (!grad) return;
@@ -709,7 +772,7 @@ void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const in
   // memory plan: size, allocate, assign
   const Counts c{n_local, N0, E0, N1, E1};
   Plan P, S;
-  plan_memory(P, S, in_->a, h_, c, grad, chain_);
+  plan_memory(P, S, in_->a, h_, c, grad, chain_, ncf_, ncs_);
   persist_.ensure(P.off);
   scratch_.ensure(S.off);
   if (use_f16_) {  // largest A operand of a 3xFP16 GEMM: [tokens, max(3d, ff, hid)]
@@ -720,7 +783,7 @@ void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const in
   }
   P = Plan{persist_.as<char>(), 0};
   S = Plan{scratch_.as<char>(), 0};
-  plan_memory(P, S, in_->a, h_, c, grad, chain_);
+  plan_memory(P, S, in_->a, h_, c, grad, chain_, ncf_, ncs_);
   const Acts &a = in_->a;
   EdgePrepArgs ep{};
   ep.n_atoms = N0; ep.n_edges = E0;
@@ -740,6 +803,7 @@ void PETModel::predict_local(const double *d_pos, int n_local, const int32_t *nu
     throw Error(kErrInvalidParameter, "local system needs 0 <= n_owned <= n_layer0 <= n_local");
   CUDA_CHECK(cudaSetDevice(device_));
   cudaStream_t s = stream_;
+  ncf_ = ncs_ = false;
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[0], s));
   int *derr = static_cast<int *>(d_err_.ensure(sizeof(int) * 4));
   CUDA_CHECK(cudaMemsetAsync(derr, 0, sizeof(int), s));
@@ -807,10 +871,13 @@ void PETModel::read_times(bool grad) {
 
 void PETModel::run_group(const float *d_pos, int n_atoms, const std::vector<const SystemView *> &systems,
                          const std::vector<int> &atom_begin, bool grad, std::vector<Result *> &results,
-                         bool copy_forces) {
+                         bool copy_forces, bool nc) {
   cudaStream_t s = stream_;
   const int n_sys = static_cast<int>(systems.size());
   n_sys_ = n_sys;
+  // pet.cpp:281-282: a property's heads run when asked for and present
+  ncf_ = nc && has_ncf_;
+  ncs_ = nc && has_ncs_;
   int *derr = static_cast<int *>(d_err_.ensure(sizeof(int) * 4));
   CUDA_CHECK(cudaMemsetAsync(derr, 0, sizeof(int), s));
   // species indices (pet_batch.cpp:146-167): unknown Z is an error
@@ -860,18 +927,24 @@ void PETModel::run_group(const float *d_pos, int n_atoms, const std::vector<cons
 
   forward_backward(grad);
 
-  // per-system energy and virial in f64 (pet.cpp:542-548, 1041-1077)
-  double *red = static_cast<double *>(d_red_.ensure(sizeof(double) * 7 * (n_sys + 1)));
+  // per-system energy and virial in f64 (pet.cpp:542-548, 1041-1077); then
+  // the per-system Voigt sums of the non-conservative stress
+  const size_t nred = static_cast<size_t>(ncs_ ? 13 : 7) * n_sys;
+  double *red = static_cast<double *>(d_red_.ensure(sizeof(double) * (nred + 7)));
   reduce_systems(nl_.vec.as<float>(), a.g, a.e_atom, nl_.offset.as<int>(), dsb, n_sys, red + n_sys, red,
                  grad && El_[0] > 0, s);
+  if (ncs_) nc_stress_reduce(a.ncS, dsb, n_sys, red + 7 * n_sys, s);
+  // pet.cpp:601-617: non-conservative forces added to the gradient forces
+  if (ncf_) add_vec(a.ncF, a.F, 3 * n_atoms, grad, s);
+  const bool have_forces = grad || ncf_;
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[6], s));
-  const size_t fbytes = (grad && copy_forces) ? sizeof(float) * 3 * n_atoms : 0;
-  char *hout = static_cast<char *>(h_out_.ensure(sizeof(double) * 7 * n_sys + fbytes + 16));
-  int *herr = reinterpret_cast<int *>(hout + sizeof(double) * 7 * n_sys + fbytes);
+  const size_t fbytes = (have_forces && copy_forces) ? sizeof(float) * 3 * n_atoms : 0;
+  char *hout = static_cast<char *>(h_out_.ensure(sizeof(double) * nred + fbytes + 16));
+  int *herr = reinterpret_cast<int *>(hout + sizeof(double) * nred + fbytes);
   CUDA_CHECK(cudaMemcpyAsync(herr, d_err_.ptr, sizeof(int), cudaMemcpyDeviceToHost, s));
-  CUDA_CHECK(cudaMemcpyAsync(hout, red, sizeof(double) * 7 * n_sys, cudaMemcpyDeviceToHost, s));
+  CUDA_CHECK(cudaMemcpyAsync(hout, red, sizeof(double) * nred, cudaMemcpyDeviceToHost, s));
   if (fbytes)
-    CUDA_CHECK(cudaMemcpyAsync(hout + sizeof(double) * 7 * n_sys, a.F, fbytes, cudaMemcpyDeviceToHost, s));
+    CUDA_CHECK(cudaMemcpyAsync(hout + sizeof(double) * nred, a.F, fbytes, cudaMemcpyDeviceToHost, s));
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[7], s));
   CUDA_CHECK(cudaStreamSynchronize(s));
   if (kprof_) collect_marks();
@@ -881,7 +954,8 @@ void PETModel::run_group(const float *d_pos, int n_atoms, const std::vector<cons
 
   const double *he = reinterpret_cast<const double *>(hout);
   const double *hv = he + n_sys;
-  const float *hF = reinterpret_cast<const float *>(hout + sizeof(double) * 7 * n_sys);
+  const double *hs = he + 7 * n_sys;
+  const float *hF = reinterpret_cast<const float *>(hout + sizeof(double) * nred);
   for (int k = 0; k < n_sys; ++k) {
     const SystemView &sv = *systems[k];
     Result &R = *results[k];
@@ -895,27 +969,41 @@ void PETModel::run_group(const float *d_pos, int n_atoms, const std::vector<cons
     R.has_stress = false;
     R.forces.clear();
     R.stress.clear();
-    if (grad) {
+    if (have_forces) {
       R.has_forces = true;
       if (copy_forces) R.forces.assign(hF + 3 * atom_begin[k], hF + 3 * atom_begin[k + 1]);
+    }
+    // pet.cpp:1079-1097: f32 determinant, stress only when |V| > 1e-10
+    const float *m = sv.cell;
+    const bool periodic = m && (sv.pbc[0] || sv.pbc[1] || sv.pbc[2]);
+    float vol = 0.f;
+    if (periodic)
+      vol = std::fabs(m[0] * (m[4] * m[8] - m[5] * m[7]) - m[1] * (m[3] * m[8] - m[5] * m[6]) +
+                      m[2] * (m[3] * m[7] - m[4] * m[6]));
+    if (grad) {
       R.stress.assign(6, 0.0f);
-      const float *m = sv.cell;
-      if (m && (sv.pbc[0] || sv.pbc[1] || sv.pbc[2])) {
-        // pet.cpp:1079-1097: f32 determinant, stress only when |V| > 1e-10
-        float vol = m[0] * (m[4] * m[8] - m[5] * m[7]) - m[1] * (m[3] * m[8] - m[5] * m[6]) +
-                    m[2] * (m[3] * m[7] - m[4] * m[6]);
-        vol = std::fabs(vol);
-        if (vol > 1e-10f) {
-          for (int c = 0; c < 6; ++c) R.stress[c] = static_cast<float>(hv[6 * k + c]) / vol;
-          R.has_stress = true;
-        }
+      if (periodic && vol > 1e-10f) {
+        for (int c = 0; c < 6; ++c) R.stress[c] = static_cast<float>(hv[6 * k + c]) / vol;
+        R.has_stress = true;
+      }
+    }
+    if (ncs_) {
+      // pet.cpp:627-686: the per-atom tensors' Voigt sum is added to the
+      // stress already there and the sum divided by the volume, as the
+      // reference does (with gradients on as well, that divides the
+      // gradient stress a second time; the mlipcpp API never asks for both)
+      if (R.stress.empty()) R.stress.assign(6, 0.0f);
+      for (int c = 0; c < 6; ++c) R.stress[c] += static_cast<float>(hs[6 * k + c]);
+      if (periodic && vol > 1e-10f) {
+        for (int c = 0; c < 6; ++c) R.stress[c] /= vol;
+        R.has_stress = true;
       }
     }
   }
   if (timing_) read_times(grad);
 }
 
-std::vector<Result> PETModel::predict(const std::vector<SystemView> &systems, bool grad) {
+std::vector<Result> PETModel::predict(const std::vector<SystemView> &systems, bool grad, bool nc) {
   std::vector<Result> out(systems.size());
   if (systems.empty()) return out;
   if (wptr_.empty()) throw Error(3, "Model weights not loaded");
@@ -936,7 +1024,7 @@ std::vector<Result> PETModel::predict(const std::vector<SystemView> &systems, bo
     float *dp = static_cast<float *>(d_pos_.ensure(sizeof(float) * 3 * (n + 1)));
     if (timing_) CUDA_CHECK(cudaEventRecord(ev_[0], stream_));
     CUDA_CHECK(cudaMemcpyAsync(dp, hp, sizeof(float) * 3 * n, cudaMemcpyHostToDevice, stream_));
-    run_group(dp, n, sv, begin, grad, rs, true);
+    run_group(dp, n, sv, begin, grad, rs, true, nc);
   };
   std::vector<int> open;
   for (size_t k = 0; k < systems.size(); ++k) {
@@ -949,13 +1037,13 @@ std::vector<Result> PETModel::predict(const std::vector<SystemView> &systems, bo
 }
 
 void PETModel::predict_device(const float *d_pos, const SystemView &sys, bool grad, Result &out,
-                              bool copy_forces) {
+                              bool copy_forces, bool nc) {
   if (wptr_.empty()) throw Error(3, "Model weights not loaded");
   std::vector<const SystemView *> sv{&sys};
   std::vector<Result *> rs{&out};
   std::vector<int> begin{0, sys.n_atoms};
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[0], stream_));
-  run_group(d_pos, sys.n_atoms, sv, begin, grad, rs, copy_forces);
+  run_group(d_pos, sys.n_atoms, sv, begin, grad, rs, copy_forces, nc);
 }
 
 }  // namespace pet

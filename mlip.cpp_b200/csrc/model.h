@@ -73,8 +73,15 @@ class PETModel {
   const Hypers &hypers() const { return h_; }
 
   // predict_batch (pet.cpp:125-694).  With compute_grad the result carries
-  // forces, and stress for periodic systems.
-  std::vector<Result> predict(const std::vector<SystemView> &systems, bool compute_grad);
+  // forces, and stress for periodic systems.  With nc the non-conservative
+  // heads the model has run in the forward pass (pet.cpp:742-784): their
+  // per-atom forces are added to the result's forces and their per-atom
+  // stress, summed per system, to its stress (pet.cpp:576-686).
+  std::vector<Result> predict(const std::vector<SystemView> &systems, bool compute_grad, bool nc = false);
+  // The model carries non-conservative force / stress heads (layer 0 present,
+  // PETWeights::has_force_heads / has_stress_heads, pet_types.h:247-254).
+  bool has_nc_forces() const { return has_ncf_; }
+  bool has_nc_stress() const { return has_ncs_; }
 
   // One spatial domain of a larger cell: n_local atoms with f64 device
   // positions (owned atoms first, then the ghost atoms within one cutoff of
@@ -90,7 +97,7 @@ class PETModel {
 
   // Device-resident entry for benchmarks: positions already on the device.
   void predict_device(const float *d_pos, const SystemView &sys, bool compute_grad, Result &out,
-                      bool copy_forces);
+                      bool copy_forces, bool nc = false);
 
   const PhaseTimes &last_times() const { return times_; }
   // Per-launch CUDA events around GEMM and attention launches, accumulated
@@ -109,7 +116,7 @@ class PETModel {
   struct Group;  // systems that share one neighbour-list launch
   void run_group(const float *d_pos, int n_atoms, const std::vector<const SystemView *> &systems,
                  const std::vector<int> &atom_begin, bool compute_grad,
-                 std::vector<Result *> &results, bool copy_forces);
+                 std::vector<Result *> &results, bool copy_forces, bool nc);
   void forward_backward(bool compute_grad);
   void setup_graph(int n_local, int N0, int E0, int N1, int E1, const int *d_species, bool grad);
   void read_times(bool grad);
@@ -129,6 +136,9 @@ class PETModel {
   bool use_attn_tc_ = false;
   // MLIPCPP_PRECISION_F16: dense layers with the hi x hi product only
   bool reduced_ = false;
+  // non-conservative heads in the file / run in the current prediction
+  bool has_ncf_ = false, has_ncs_ = false;
+  bool ncf_ = false, ncs_ = false;
 
  public:
   void set_reduced_precision(bool on) { reduced_ = on; }

@@ -351,6 +351,87 @@ __global__ void __launch_bounds__(512) k_reduce_systems(
   }
 }
 
+// ---- non-conservative heads ----------------------------------------------
+constexpr int kNcMaxOut = 9;
+
+// p[o] = y . w[o, :] for o < od, summed over the warp (every lane gets all).
+__device__ __forceinline__ void nc_row_dots(const float *__restrict__ y, const float *w, int r, int od, int lane,
+                                            float (&p)[kNcMaxOut]) {
+#pragma unroll
+  for (int o = 0; o < kNcMaxOut; ++o) p[o] = 0.f;
+  for (int c = lane; c < r; c += 32) {
+    const float yv = y[c];
+#pragma unroll
+    for (int o = 0; o < kNcMaxOut; ++o)
+      if (o < od) p[o] = fmaf(yv, w[o * r + c], p[o]);
+  }
+#pragma unroll
+  for (int o = 0; o < kNcMaxOut; ++o)
+    if (o < od) p[o] = warp_sum(p[o]);
+}
+
+// Warp per atom i: dst[i, o] += yn[i] . wn[o] + bn[o]
+//                             + sum_{e in i} fc[e] (ye[e] . we[o] + be[o]).
+// The last layers' weights sit in shared memory: [od][r] node, [od][r] edge.
+__global__ void __launch_bounds__(256) k_nc_readout(const float *__restrict__ yn, const float *__restrict__ ye,
+                                                    const float *__restrict__ wn, const float *__restrict__ bn,
+                                                    const float *__restrict__ we, const float *__restrict__ be,
+                                                    const float *__restrict__ fc, const int *__restrict__ offset,
+                                                    float *__restrict__ dst, int n, int r, int od) {
+  extern __shared__ float s_w[];
+  const int nw = od * r;
+  for (int t = threadIdx.x; t < nw; t += blockDim.x) {
+    s_w[t] = wn[t];
+    if (ye) s_w[nw + t] = we[t];
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < n; i += (gridDim.x * blockDim.x) >> 5) {
+    float out[kNcMaxOut], p[kNcMaxOut];
+    nc_row_dots(yn + static_cast<size_t>(i) * r, s_w, r, od, lane, out);
+#pragma unroll
+    for (int o = 0; o < kNcMaxOut; ++o)
+      if (o < od) out[o] += bn[o];
+    if (ye) {
+      for (int e = offset[i]; e < offset[i + 1]; ++e) {
+        nc_row_dots(ye + static_cast<size_t>(e) * r, s_w + nw, r, od, lane, p);
+        const float f = fc[e];
+#pragma unroll
+        for (int o = 0; o < kNcMaxOut; ++o)
+          if (o < od) out[o] = fmaf(f, p[o] + be[o], out[o]);
+      }
+    }
+    float v = 0.f;
+#pragma unroll
+    for (int o = 0; o < kNcMaxOut; ++o)
+      if (o == lane) v = out[o];
+    if (lane < od) dst[static_cast<size_t>(i) * od + lane] += v;
+  }
+}
+
+// Block per system: out[6k + c] = Voigt sum over its atoms of the 3x3
+// tensors S[i] (row-major xx xy xz yx yy yz zx zy zz), off-diagonals
+// symmetrised in f32 per atom as pet.cpp:644-665 does, summed in f64.
+__global__ void __launch_bounds__(256) k_nc_stress_reduce(const float *__restrict__ S,
+                                                          const int *__restrict__ sys_begin,
+                                                          double *__restrict__ out) {
+  __shared__ double sm[8 * 6];
+  const int k = blockIdx.x;
+  double v[6] = {0, 0, 0, 0, 0, 0};
+  for (int i = sys_begin[k] + threadIdx.x; i < sys_begin[k + 1]; i += blockDim.x) {
+    const float *t = S + 9 * static_cast<size_t>(i);
+    v[0] += t[0];
+    v[1] += t[4];
+    v[2] += t[8];
+    v[3] += 0.5f * (t[5] + t[7]);
+    v[4] += 0.5f * (t[2] + t[6]);
+    v[5] += 0.5f * (t[1] + t[3]);
+  }
+  block_sum<6>(v, sm);
+  if (threadIdx.x == 0)
+    for (int c = 0; c < 6; ++c) out[6 * k + c] = v[c];
+}
+
 __global__ void __launch_bounds__(1024) k_reduce_local(const float *__restrict__ vec, const float *__restrict__ g,
                                                      const float *__restrict__ e_atom, int n_energy, int n_edges,
                                                      double *__restrict__ out) {
@@ -479,6 +560,24 @@ void forces(const float *g, const int *offset, const int *nbr, const int *rev, f
     k_forces_unpaired<<<grid_for(n_edges, 256), 256, 0, s>>>(g, nbr, rev, F, n_edges);
     CUDA_LAUNCH_CHECK();
   }
+}
+
+void nc_readout(const float *yn, const float *ye, const float *wn, const float *bn, const float *we,
+                const float *be, const float *fc, const int *offset, float *dst, int n, int r, int od,
+                cudaStream_t s) {
+  if (n <= 0) return;
+  if (od < 1 || od > kNcMaxOut) throw Error(kErrInternal, "nc_readout: at most 9 outputs");
+  const size_t smem = sizeof(float) * 2 * od * r;
+  if (smem > 48 * 1024) throw Error(kErrUnsupported, "nc_readout: head width too large");
+  k_nc_readout<<<grid_for(static_cast<int64_t>(n) * 32, 256), 256, smem, s>>>(yn, ye, wn, bn, we, be, fc, offset,
+                                                                             dst, n, r, od);
+  CUDA_LAUNCH_CHECK();
+}
+
+void nc_stress_reduce(const float *S, const int *sys_atom_begin, int n_sys, double *out, cudaStream_t s) {
+  if (n_sys <= 0) return;
+  k_nc_stress_reduce<<<n_sys, 256, 0, s>>>(S, sys_atom_begin, out);
+  CUDA_LAUNCH_CHECK();
 }
 
 void reduce_systems(const float *vec, const float *g, const float *e_atom, const int *offset,

@@ -72,6 +72,19 @@ void reduce_systems(const float *vec, const float *g, const float *e_atom, const
                     const int *sys_atom_begin, int n_sys, double *virial, double *energy,
                     bool with_virial, cudaStream_t s);
 
+// Non-conservative property readout of one layer (build_property_output,
+// pet_layers.cpp:845-915), warp per atom i < n:
+//   dst[i, o] += yn[i] . wn[o] + bn[o] + sum_{e in i} fc[e] (ye[e] . we[o] + be[o])
+// yn [n, r], ye [edges, r]: the heads' second hidden layer (ye null: no
+// edges); wn, we [od, r] and bn, be [od]: the last layers; od <= 9.
+void nc_readout(const float *yn, const float *ye, const float *wn, const float *bn, const float *we,
+                const float *be, const float *fc, const int *offset, float *dst, int n, int r, int od,
+                cudaStream_t s);
+// Per system k: out[6k..6k+5] = Voigt (xx yy zz yz xz xy) sum of the per-atom
+// 3x3 tensors S [n, 9] over its atoms, off-diagonals symmetrised
+// (pet.cpp:621-666), in f64.
+void nc_stress_reduce(const float *S, const int *sys_atom_begin, int n_sys, double *out, cudaStream_t s);
+
 // out[0] = sum of e_atom[0..n_energy), out[1..6] = Voigt sum over edges
 // [0, n_edges) of sym(vec (x) g) (f64, one CTA).
 void reduce_local(const float *vec, const float *g, const float *e_atom, int n_energy, int n_edges,

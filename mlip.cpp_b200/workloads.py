@@ -96,8 +96,37 @@ def pet_tensor_shapes(h: PETHypers, n_species: int) -> dict[str, tuple[int, ...]
     return s
 
 
-def random_pet_weights(h: PETHypers, atomic_numbers, seed: int = 0) -> dict[str, np.ndarray]:
-    """Seeded random-init weights (float32) keyed by GGUF tensor name."""
+#: Non-conservative property heads of PET-MAD v1.1+ (pet_types.h:130-138):
+#: property -> (last-layer tensor suffix, outputs per atom).
+NC_HEADS = {"nc_forces": ("nc_f", 3), "nc_stress": ("nc_s", 9)}
+
+
+def nc_head_shapes(h: PETHypers, props=("nc_forces", "nc_stress"), layers=(0, 1)) -> dict[str, tuple[int, ...]]:
+    """numpy shapes of the non-conservative head tensors (node and edge MLPs
+    d -> d_head -> d_head -> od per GNN layer, pet.cpp:48-79)."""
+    d, r = h.d_pet, h.d_head
+    s = {}
+    for prop in props:
+        last, od = NC_HEADS[prop]
+        for l in layers:
+            for kind in ("node", "edge"):
+                hp = f"model.{kind}_heads.{prop}.{l}."
+                s[hp + "0.weight"] = (r, d)
+                s[hp + "0.bias"] = (r,)
+                s[hp + "2.weight"] = (r, r)
+                s[hp + "2.bias"] = (r,)
+                lp = f"model.{kind}_last_layers.{prop}.{l}.{last}."
+                s[lp + "weight"] = (od, r)
+                s[lp + "bias"] = (od,)
+    return s
+
+
+def random_pet_weights(h: PETHypers, atomic_numbers, seed: int = 0, nc_heads=False) -> dict[str, np.ndarray]:
+    """Seeded random-init weights (float32) keyed by GGUF tensor name.
+
+    nc_heads: False, True (both non-conservative properties on both layers)
+    or a dict of nc_head_shapes keyword arguments.  Their weights come from a
+    second generator, so the other tensors do not depend on this choice."""
     rng = np.random.default_rng(seed)
     z = np.asarray(atomic_numbers, dtype=np.int32)
     out: dict[str, np.ndarray] = {}
@@ -116,6 +145,13 @@ def random_pet_weights(h: PETHypers, atomic_numbers, seed: int = 0) -> dict[str,
         out[name] = np.ascontiguousarray(w, dtype=np.float32)
     out["composition.atomic_numbers"] = z
     out["composition.energies"] = (-3.0 + rng.standard_normal(len(z))).astype(np.float32)
+    if nc_heads:
+        nrng = np.random.default_rng(seed + 7919)
+        kw = nc_heads if isinstance(nc_heads, dict) else {}
+        for name, shape in nc_head_shapes(h, **kw).items():
+            fan_in = shape[1] if len(shape) == 2 else _fan_in_of_bias(name, h)
+            bound = 1.0 / math.sqrt(fan_in)
+            out[name] = np.ascontiguousarray(nrng.uniform(-bound, bound, size=shape), dtype=np.float32)
     return out
 
 
@@ -135,14 +171,15 @@ def _fan_in_of_bias(name: str, h: PETHypers) -> int:
 
 
 def write_pet_gguf(path: str, h: PETHypers, atomic_numbers=None, seed: int = 0,
-                   weights: dict[str, np.ndarray] | None = None) -> dict[str, np.ndarray]:
-    """Write a random-init ``"pet"`` GGUF and return the weights written."""
+                   weights: dict[str, np.ndarray] | None = None, nc_heads=False) -> dict[str, np.ndarray]:
+    """Write a random-init ``"pet"`` GGUF and return the weights written
+    (nc_heads: see random_pet_weights)."""
     import gguf
 
     if atomic_numbers is None:
         atomic_numbers = np.arange(1, 90, dtype=np.int32)
     if weights is None:
-        weights = random_pet_weights(h, atomic_numbers, seed)
+        weights = random_pet_weights(h, atomic_numbers, seed, nc_heads=nc_heads)
     w = gguf.GGUFWriter(path, arch="pet")
     w.add_name(f"random-init PET seed={seed}")
     w.add_float32("pet.cutoff", float(h.cutoff))

@@ -165,7 +165,16 @@ class PETOracle:
     def _lin(self, x, name):
         return x @ self.W[name + ".weight"].T + self.W[name + ".bias"]
 
-    def atomic_energies(self, b: Batch, vec: torch.Tensor) -> torch.Tensor:
+    # pet_types.h:247-254 (has_property): a property is present when its
+    # layer-0 node head is; pet_types.h:101 (is_loaded) per layer
+    NC_PROPS = {"nc_forces": ("nc_f", 3), "nc_stress": ("nc_s", 9)}
+
+    def has_property(self, prop: str, layer: int = 0) -> bool:
+        return f"model.node_heads.{prop}.{layer}.0.weight" in self.W
+
+    def atomic_energies(self, b: Batch, vec: torch.Tensor, nc: bool = False):
+        """Per-atom energies; with nc also the per-atom non-conservative
+        outputs {prop: [N, od]} of the properties the model has."""
         h, W = self.h, self.W
         N, M = b.n_atoms, b.max_nb
         d, nh = h.d_pet, h.num_heads
@@ -183,6 +192,8 @@ class PETOracle:
         m0 = W["model.embedding.weight"][nsp]                                    # [N,M,d]
         msg = m0
         energies = torch.zeros(N, dtype=self.dtype)
+        props = [p for p in self.NC_PROPS if nc and self.has_property(p)]
+        nc_out = {p: torch.zeros(N, self.NC_PROPS[p][1], dtype=self.dtype) for p in props}
         edge0 = None
         for l in range(2):
             p = f"model.gnn.{l}."
@@ -212,7 +223,20 @@ class PETOracle:
                 msg = 0.5 * (m0 + rm * edge0.reshape(N * M, d)[rev].reshape(N, M, d))
             energies = energies + self._head(node_f, "node", l) + \
                 (self._head(edge_f, "edge", l) * fc * pad).sum(-1)
-        return energies
+            # build_property_output (pet_layers.cpp:845-915): node head plus
+            # the cutoff- and padding-weighted edge head summed over neighbours
+            for p in props:
+                if self.has_property(p, l):
+                    nc_out[p] = nc_out[p] + self._prop_head(node_f, "node", p, l) + \
+                        (self._prop_head(edge_f, "edge", p, l) * (fc * pad)[..., None]).sum(1)
+        return (energies, nc_out) if nc else energies
+
+    def _prop_head(self, x, kind, prop, l):
+        """apply_mlp_head (pet_layers.cpp:811-837) of a property head."""
+        hp = f"model.{kind}_heads.{prop}.{l}."
+        y = torch.nn.functional.silu(self._lin(x, hp + "0"))
+        y = torch.nn.functional.silu(self._lin(y, hp + "2"))
+        return self._lin(y, f"model.{kind}_last_layers.{prop}.{l}.{self.NC_PROPS[prop][0]}")
 
     def _head(self, x, kind, l):
         hp = f"model.{kind}_heads.energy.{l}."
@@ -221,10 +245,16 @@ class PETOracle:
         return self._lin(y, f"model.{kind}_last_layers.energy.{l}.energy___0")[..., 0]
 
     # ----------------------------------------------------------------------
-    def predict(self, systems, compute_forces=True, key_mask=None):
+    def predict(self, systems, compute_forces=True, key_mask=None, compute_nc=False):
         """predict_batch (pet.cpp:125-694): list of dicts with energy
         (python float, f32-rounded like ModelResult), forces [n,3] and stress
         [6] (Voigt xx,yy,zz,yz,xz,xy) when available.
+
+        compute_nc runs the non-conservative heads the model has: their
+        per-atom forces are added to the forces (zero without gradients),
+        their per-atom stress tensors summed per system into Voigt form,
+        added to the stress and the sum divided by the volume for periodic
+        systems (pet.cpp:576-686).
 
         The reference's attention mask is an input built from the neighbour
         list distances, so its forces omit the mask's position dependence.
@@ -238,7 +268,10 @@ class PETOracle:
             b.key_mask = key_mask
         vec = torch.as_tensor(b.vec, dtype=self.dtype).clone().requires_grad_(compute_forces)
         with torch.set_grad_enabled(compute_forces):
-            e_at = self.atomic_energies(b, vec)
+            e_at = self.atomic_energies(b, vec, nc=compute_nc)
+            nc_out = {}
+            if compute_nc:
+                e_at, nc_out = e_at
             if compute_forces:
                 (g,) = torch.autograd.grad(e_at.sum(), vec)
         e_np = e_at.detach().to(torch.float32).numpy()
@@ -281,6 +314,31 @@ class PETOracle:
                                                m[0, 2] * (m[1, 0] * m[2, 1] - m[1, 1] * m[2, 0]))))
                     if vol > 1e-10:
                         results[k]["stress"] = (vir[k] / vol).astype(np.float32)
+        if "nc_forces" in nc_out:
+            ncf = nc_out["nc_forces"].detach().numpy()
+            off = 0
+            for k, s in enumerate(systems):
+                n = len(s.positions)
+                base = results[k].get("forces", np.zeros((n, 3), np.float32))
+                results[k]["forces"] = (base + ncf[off:off + n]).astype(np.float32)
+                off += n
+        if "nc_stress" in nc_out:
+            t = nc_out["nc_stress"].detach().numpy().astype(np.float64)
+            voigt = np.stack([t[:, 0], t[:, 4], t[:, 8], 0.5 * (t[:, 5] + t[:, 7]),
+                              0.5 * (t[:, 2] + t[:, 6]), 0.5 * (t[:, 1] + t[:, 3])], 1)
+            off = 0
+            for k, s in enumerate(systems):
+                n = len(s.positions)
+                st = results[k].get("stress", np.zeros(6, np.float32)).astype(np.float64)
+                st = st + voigt[off:off + n].sum(0)
+                off += n
+                if s.cell is not None and (s.pbc is None or any(s.pbc)):
+                    m = np.asarray(s.cell, np.float32)
+                    vol = abs(float(np.float32(m[0, 0] * (m[1, 1] * m[2, 2] - m[1, 2] * m[2, 1]) -
+                                               m[0, 1] * (m[1, 0] * m[2, 2] - m[1, 2] * m[2, 0]) +
+                                               m[0, 2] * (m[1, 0] * m[2, 1] - m[1, 1] * m[2, 0]))))
+                    if vol > 1e-10:
+                        results[k]["stress"] = (st / vol).astype(np.float32)
         return results
 
 

@@ -40,17 +40,19 @@ def gguf_dir(tmp_path_factory):
 
 @pytest.fixture(scope="session")
 def model_file(gguf_dir):
-    """model_file(name, seed) -> path of a seeded random-init "pet" GGUF."""
+    """model_file(name, seed, nc=False, **hypers) -> path of a seeded
+    random-init "pet" GGUF (nc: non-conservative heads, see
+    workloads.random_pet_weights)."""
     from mlipcpp_b200 import workloads as wl
     cache = {}
 
-    def make(name="tiny", seed=0, **over):
-        key = (name, seed, tuple(sorted(over.items())))
+    def make(name="tiny", seed=0, nc=False, **over):
+        key = (name, seed, repr(nc), tuple(sorted(over.items())))
         if key not in cache:
             import dataclasses
             h = dataclasses.replace(wl.HYPERS[name], **over)
             path = os.path.join(str(gguf_dir), f"{name}_{seed}_{len(cache)}.gguf")
-            wl.write_pet_gguf(path, h, seed=seed)
+            wl.write_pet_gguf(path, h, seed=seed, nc_heads=nc)
             cache[key] = path
         return cache[key]
     return make

@@ -7,6 +7,9 @@
 * pet_*.npz: energies, forces and stress of the PyTorch restatement
   (oracle/pet_oracle.py, float64) on seeded random-init weights; the weights
   are regenerated from the seed (a digest is stored to detect drift).
+  pet_nc_*.npz: the same for a model with non-conservative force and stress
+  heads, predicted as use_nc_forces does (no gradients; forces and stress
+  from the heads).
 
 Run from the repository root:  python tests/golden/make_golden.py
 Needs the reference tree (for oracle/_ref) only for the nl_* fixtures.
@@ -59,18 +62,21 @@ def _outside():
 
 
 def pet_cases():
-    """name -> (hypers name, seed, [Structure, ...])."""
+    """name -> (hypers name, seed, [Structure, ...], non-conservative heads)."""
     return {
-        "tiny_si8": ("tiny", 0, [wl.si_diamond(1, seed=3)]),
-        "tiny_water96": ("tiny", 0, [wl.water_box(96, seed=5)]),
-        "tiny_molecules3": ("tiny", 0, wl.molecules(3, seed=7, n_min=5, n_max=20)),
-        "mads_si216": ("pet-mad-s", 1, [wl.si_diamond(3, seed=0)]),
-        "oaml_fcc64": ("pet-oam-l", 2, [wl.fcc_alloy(4, seed=9)]),
+        "tiny_si8": ("tiny", 0, [wl.si_diamond(1, seed=3)], False),
+        "tiny_water96": ("tiny", 0, [wl.water_box(96, seed=5)], False),
+        "tiny_molecules3": ("tiny", 0, wl.molecules(3, seed=7, n_min=5, n_max=20), False),
+        "mads_si216": ("pet-mad-s", 1, [wl.si_diamond(3, seed=0)], False),
+        "oaml_fcc64": ("pet-oam-l", 2, [wl.fcc_alloy(4, seed=9)], False),
+        "nc_tiny_si8": ("tiny", 0, [wl.si_diamond(1, seed=3)], True),
+        "nc_tiny_molecules3": ("tiny", 0, wl.molecules(3, seed=7, n_min=5, n_max=20), True),
+        "nc_mads_si64": ("pet-mad-s", 1, [wl.si_diamond(2, seed=11)], True),
     }
 
 
-def weights_digest(h, seed):
-    w = wl.random_pet_weights(h, np.arange(1, 90, dtype=np.int32), seed)
+def weights_digest(h, seed, nc=False):
+    w = wl.random_pet_weights(h, np.arange(1, 90, dtype=np.int32), seed, nc_heads=nc)
     m = hashlib.sha256()
     for k in sorted(w):
         m.update(k.encode())
@@ -97,13 +103,13 @@ def main():
         print("reference tree absent: nl_* fixtures left unchanged")
 
     tmp = os.path.join(HERE, "_tmp.gguf")
-    for name, (hname, seed, systems) in pet_cases().items():
+    for name, (hname, seed, systems, nc) in pet_cases().items():
         h = wl.HYPERS[hname]
-        wl.write_pet_gguf(tmp, h, seed=seed)
+        wl.write_pet_gguf(tmp, h, seed=seed, nc_heads=nc)
         orc = pet_oracle.load_oracle(tmp, torch.float64)
-        res = orc.predict(systems, compute_forces=True)
-        payload = dict(hypers=hname, seed=seed, digest=weights_digest(h, seed),
-                       n_systems=len(systems))
+        res = orc.predict(systems, compute_forces=not nc, compute_nc=nc)
+        payload = dict(hypers=hname, seed=seed, digest=weights_digest(h, seed, nc),
+                       n_systems=len(systems), nc=nc)
         for k, (s, r) in enumerate(zip(systems, res)):
             payload[f"positions_{k}"] = s.positions
             payload[f"numbers_{k}"] = s.numbers

@@ -32,7 +32,8 @@ def assert_close(res, e_ref, f_ref, s_ref, n):
 @pytest.mark.parametrize("path", FIXTURES, ids=lambda p: os.path.basename(p)[4:-4])
 def test_gpu_matches_golden(path, model_file):
     f = np.load(path)
-    pred = mb.Predictor(model_file(str(f["hypers"]), int(f["seed"])))
+    nc = bool(f["nc"]) if "nc" in f else False
+    pred = mb.Predictor(model_file(str(f["hypers"]), int(f["seed"]), nc=nc))
     n_sys = int(f["n_systems"])
     systems = []
     for k in range(n_sys):
@@ -41,9 +42,10 @@ def test_gpu_matches_golden(path, model_file):
                                     cell if cell.size else None, (True,) * 3 if cell.size else None))
     if n_sys == 1:
         s = systems[0]
-        res = [pred.predict(s.positions, s.numbers, s.cell, s.pbc, compute_stress=s.cell is not None)]
+        res = [pred.predict_with_options(s.positions, s.numbers, s.cell, s.pbc,
+                                         mb.PredictOptions(True, s.cell is not None, nc))]
     else:
-        res = pred.predict_batch(systems)
+        res = pred.predict_batch(systems, use_nc_forces=nc)
     for k, r in enumerate(res):
         assert_close(r, float(f[f"energy_{k}"]), f[f"forces_{k}"], f[f"stress_{k}"],
                      systems[k].n_atoms)
@@ -206,3 +208,65 @@ def test_gpu_reduced_precision_mode(hname, make, model_file):
     ds = np.abs(res.stress - ref.stress).max()
     print(f"{hname}: |dE|/N {de:.2e}  |dF| {df:.2e}  |dS| {ds:.2e}")
     assert de <= TOL_E16 and df <= TOL_F16 and ds <= TOL_S16
+
+
+# ---- non-conservative heads (use_nc_forces) --------------------------------
+@pytest.mark.parametrize("hname,make", [
+    ("pet-oam-l", lambda: [wl.fcc_alloy(8, seed=61)]),
+    ("pet-mad-s", lambda: [wl.water_box(192, seed=62)]),
+    ("tiny", lambda: wl.molecules(5, seed=63, n_min=3, n_max=30)),
+], ids=["fcc512_oaml", "water192_mads", "molecules5_tiny"])
+def test_gpu_nc_heads_match_oracle(hname, make, model_file):
+    """use_nc_forces: forces and stress from the non-conservative heads of
+    both GNN layers (pet.cpp:742-784, 576-686), no gradients."""
+    path = model_file(hname, 8, nc=True)
+    systems = make()
+    ref = po.load_oracle(path, torch.float64).predict(systems, compute_forces=False, compute_nc=True)
+    pred = mb.Predictor(path)
+    if len(systems) == 1:
+        s = systems[0]
+        res = [pred.predict_with_options(s.positions, s.numbers, s.cell, s.pbc,
+                                         mb.PredictOptions(True, True, True))]
+    else:
+        res = pred.predict_batch(systems, compute_stress=True, use_nc_forces=True)
+    for s, r, q in zip(systems, res, ref):
+        assert_close(r, q["energy_f64"], q["forces"], q.get("stress"), s.n_atoms)
+        assert r.has_stress() == ("stress" in q)
+
+
+def test_gpu_nc_partial_heads(model_file):
+    """A layer without heads contributes nothing; without a layer-0 head the
+    property is absent (PETWeights::has_property, pet_types.h:247-250)."""
+    s = wl.si_diamond(1, seed=64)
+    only0 = model_file("tiny", 9, nc={"layers": (0,)})
+    ref = po.load_oracle(only0, torch.float64).predict([s], compute_forces=False, compute_nc=True)[0]
+    r = mb.Predictor(only0).predict_with_options(s.positions, s.numbers, s.cell, None,
+                                                 mb.PredictOptions(True, True, True))
+    assert_close(r, ref["energy_f64"], ref["forces"], ref["stress"], s.n_atoms)
+    # forces only, and only on layer 1: no property, so no forces and no stress
+    only1 = model_file("tiny", 9, nc={"layers": (1,), "props": ("nc_forces",)})
+    r = mb.Predictor(only1).predict_with_options(s.positions, s.numbers, s.cell, None,
+                                                 mb.PredictOptions(True, True, True))
+    assert not r.has_forces() and not r.has_stress()
+
+
+def test_gpu_nc_option_on_model_without_heads(model_file):
+    """use_nc_forces on a model without the heads: energy only
+    (pet.cpp:281-282 skips the heads, mlipcpp_api.cpp:572-577 no gradient)."""
+    s = wl.si_diamond(1, seed=65)
+    pred = mb.Predictor(model_file("tiny", 10))
+    r = pred.predict_with_options(s.positions, s.numbers, s.cell, None, mb.PredictOptions(True, True, True))
+    full = pred.predict(s.positions, s.numbers, s.cell, compute_stress=True)
+    assert not r.has_forces() and not r.has_stress()
+    assert abs(r.energy - full.energy) <= 1e-4
+
+
+def test_gpu_nc_forces_without_stress_request(model_file):
+    """compute_stress off clears the nc stress; compute_forces off clears the
+    nc forces (mlipcpp_api.cpp:586-593)."""
+    s = wl.si_diamond(1, seed=66)
+    pred = mb.Predictor(model_file("tiny", 11, nc=True))
+    r = pred.predict_with_options(s.positions, s.numbers, s.cell, None, mb.PredictOptions(True, False, True))
+    assert r.has_forces() and not r.has_stress()
+    r = pred.predict_with_options(s.positions, s.numbers, s.cell, None, mb.PredictOptions(False, True, True))
+    assert r.has_stress() and not r.has_forces()

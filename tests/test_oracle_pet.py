@@ -35,10 +35,12 @@ def _fixture_systems(f):
 def test_oracle_golden(path, model_file):
     f = np.load(path)
     h = wl.HYPERS[str(f["hypers"])]
-    if str(f["digest"]) != __import__("golden.make_golden", fromlist=["x"]).weights_digest(h, int(f["seed"])):
+    nc = bool(f["nc"]) if "nc" in f else False
+    mg = __import__("golden.make_golden", fromlist=["x"])
+    if str(f["digest"]) != mg.weights_digest(h, int(f["seed"]), nc):
         pytest.fail("seeded weight generator drifted from the committed fixture")
-    orc = po.load_oracle(model_file(str(f["hypers"]), int(f["seed"])), torch.float64)
-    res = orc.predict(_fixture_systems(f))
+    orc = po.load_oracle(model_file(str(f["hypers"]), int(f["seed"]), nc=nc), torch.float64)
+    res = orc.predict(_fixture_systems(f), compute_forces=not nc, compute_nc=nc)
     for k, r in enumerate(res):
         assert abs(r["energy_f64"] - float(f[f"energy_{k}"])) < 1e-8 * max(1, abs(float(f[f"energy_{k}"])))
         np.testing.assert_allclose(r["forces"], f[f"forces_{k}"], atol=1e-6)
@@ -144,3 +146,68 @@ def test_fp32_oracle_within_tolerance_of_fp64(model_file):
     assert abs(a["energy_f64"] - b["energy_f64"]) / s.n_atoms < 1e-5
     assert np.abs(a["forces"] - b["forces"]).max() < 1e-4
     assert np.abs(a["stress"] - b["stress"]).max() < 1e-4
+
+
+# ---- non-conservative heads ------------------------------------------------
+def _bias_only_nc_model(tmp_path, seed, layers=(0, 1)):
+    """Tiny model whose non-conservative last layers are zero weights plus a
+    random bias, so each head outputs its bias for every node and edge."""
+    h = wl.PET_TINY
+    w = wl.random_pet_weights(h, np.arange(1, 90, dtype=np.int32), seed, nc_heads={"layers": layers})
+    rng = np.random.default_rng(seed)
+    bias = {}
+    for prop, (last, od) in wl.NC_HEADS.items():
+        for l in layers:
+            for kind in ("node", "edge"):
+                lp = f"model.{kind}_last_layers.{prop}.{l}.{last}."
+                w[lp + "weight"][:] = 0.0
+                w[lp + "bias"][:] = rng.standard_normal(od).astype(np.float32)
+                bias[prop, l, kind] = w[lp + "bias"].astype(np.float64)
+    path = str(tmp_path / f"nc_bias_{seed}.gguf")
+    wl.write_pet_gguf(path, h, weights=w)
+    return path, h, bias
+
+
+@pytest.mark.parametrize("layers", [(0, 1), (0,)])
+def test_oracle_nc_bias_only_known_answer(tmp_path, layers):
+    """With bias-only last layers the heads reduce to closed forms of the
+    neighbour list alone (pet_layers.cpp:845-915, pet.cpp:576-686):
+    f_i = sum_l [b_node + b_edge sum_{j in N(i)} f_c(r_ij)], and the stress is
+    the Voigt sum of the per-atom tensors over the volume."""
+    from oracle import nl as onl
+    path, h, bias = _bias_only_nc_model(tmp_path, 21, layers)
+    orc = po.load_oracle(path, torch.float64)
+    s = wl.si_diamond(1, seed=3)
+    r = orc.predict([s], compute_forces=False, compute_nc=True)[0]
+    lst = onl.build_oracle(s.positions, s.cell, s.pbc, h.cutoff)
+    d = np.asarray(lst["distances"], np.float64)
+    x = np.clip((d - h.cutoff + h.cutoff_width) / h.cutoff_width, 0.0, 1.0)
+    fc = 0.5 * np.cos(np.pi * x) + 0.5
+    fsum = np.bincount(np.asarray(lst["centers"]), weights=fc, minlength=s.n_atoms)
+    exp = {}
+    for prop in wl.NC_HEADS:
+        exp[prop] = sum(bias[prop, l, "node"][None, :] + fsum[:, None] * bias[prop, l, "edge"][None, :]
+                        for l in layers)
+    np.testing.assert_allclose(r["forces"], exp["nc_forces"], rtol=1e-5, atol=1e-5)
+    t = exp["nc_stress"]
+    voigt = np.array([t[:, 0], t[:, 4], t[:, 8], 0.5 * (t[:, 5] + t[:, 7]),
+                      0.5 * (t[:, 2] + t[:, 6]), 0.5 * (t[:, 1] + t[:, 3])]).sum(1)
+    vol = abs(np.linalg.det(s.cell.astype(np.float64)))
+    np.testing.assert_allclose(r["stress"], voigt / vol, rtol=1e-5, atol=1e-6)
+
+
+def test_oracle_nc_energy_unchanged_and_presence(model_file):
+    """Running the heads leaves the energy alone; a model without a layer-0
+    head has no such property (pet_types.h:247-254)."""
+    s = wl.si_diamond(1, seed=5)
+    orc = po.load_oracle(model_file("tiny", 12, nc=True), torch.float64)
+    a = orc.predict([s], compute_forces=False, compute_nc=True)[0]
+    b = orc.predict([s], compute_forces=False)[0]
+    assert a["energy_f64"] == pytest.approx(b["energy_f64"], abs=1e-9)
+    assert "forces" in a and "stress" in a and "forces" not in b
+    only1 = po.load_oracle(model_file("tiny", 12, nc={"layers": (1,)}), torch.float64)
+    c = only1.predict([s], compute_forces=False, compute_nc=True)[0]
+    assert "forces" not in c and "stress" not in c
+    m = wl.molecules(1, seed=4)[0]
+    d = orc.predict([m], compute_forces=False, compute_nc=True)[0]
+    assert d["forces"].shape == (m.n_atoms, 3) and "stress" not in d   # open system: no stress
