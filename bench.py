@@ -401,7 +401,7 @@ def main():
             "phase_ms": pred.last_timings(),
             "clocks": clk.summary(),
         }
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:
             sample = wl.fcc_alloy(args.cpu_reps, seed=0)
             v, threads, dt = cpu_reference(sample, gguf, 2, 1)
             line["cpu_baseline"] = {"value": v, "unit": "atom-steps/s", "cores": threads, "kind": "port",
