@@ -102,9 +102,13 @@ __device__ __forceinline__ float dsilu_f(float z) {
   float s = 1.0f / (1.0f + expf(-z));
   return s * (1.0f + z * (1.0f - s));
 }
-// silu(z) and silu'(z) from one exponential and one reciprocal
+// silu(z) and silu'(z) from the logistic s = 1 / (1 + e^-z), computed with
+// the fast intrinsics __expf and __fdividef (a few ulp: below the 22-bit
+// precision of the split-fp16 operands these values feed).  z is clamped
+// at -80 so that e^-z stays far below the 2^126 where __fdividef returns 0
+// early; silu and silu' there are below 1e-33.
 __device__ __forceinline__ void silu_pair(float z, float &y, float &dy) {
-  const float s = __frcp_rn(1.0f + expf(-z));
+  const float s = __fdividef(1.0f, 1.0f + __expf(-fmaxf(z, -80.0f)));
   y = z * s;
   dy = s * (1.0f + z * (1.0f - s));
 }

@@ -204,6 +204,137 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs &p, int row, int n
   }
 }
 
+// ---- coalesced epilogue ------------------------------------------------------
+// In the epilogue every lane owns one row (its TMEM lane), so a plain store
+// of a 16-byte piece per lane touches 32 rows at once.  These helpers move a
+// 64-byte segment of each of the warp's 32 rows through a per-warp staging
+// block ([32][5] 16-byte chunks: an odd row pitch, so the 8 rows a
+// quarter-warp touches fall in different bank groups): a warp instruction
+// then covers 8 rows x 64 contiguous bytes.
+__device__ __forceinline__ void warp_store64(uint4 *stage, const uint4 (&v)[4], char *base, size_t pitch, int row0,
+                                             int M, int lane) {
+#pragma unroll
+  for (int m = 0; m < 4; ++m) stage[lane * 5 + m] = v[m];
+  __syncwarp();
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = 8 * k + (lane >> 2), c = lane & 3;
+    if (row0 + r < M) *reinterpret_cast<uint4 *>(base + static_cast<size_t>(row0 + r) * pitch + 16 * c) = stage[r * 5 + c];
+  }
+  __syncwarp();
+}
+__device__ __forceinline__ void warp_load64(uint4 *stage, uint4 (&v)[4], const char *base, size_t pitch, int row0,
+                                            int M, int lane) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = 8 * k + (lane >> 2), c = lane & 3;
+    stage[r * 5 + c] = row0 + r < M ? *reinterpret_cast<const uint4 *>(base + static_cast<size_t>(row0 + r) * pitch + 16 * c)
+                                    : make_uint4(0u, 0u, 0u, 0u);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int m = 0; m < 4; ++m) v[m] = stage[lane * 5 + m];
+  __syncwarp();
+}
+__device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
+__device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
+
+// epilogue_store for the 3xFP16 kernel when the output rows are not
+// scattered (p.c_rows == null): the same arithmetic, with every global load
+// and store of the epilogue (C, Z, R, the split hi / lo) made by the whole
+// warp through `stage`.  row0: the warp's first row; lanes past p.M take
+// part with zeros and store nothing.
+template <int EPI, int NC>
+__device__ __forceinline__ void epilogue_store_staged(const GemmArgs &p, int row0, int lane, int n0, float (&acc)[NC],
+                                                      float s_b, const PairExchange *px, uint4 *stage) {
+  static_assert(NC % 16 == 0, "16-column groups");
+  const int row = row0 + lane;
+  const bool valid = row < p.M;
+  const bool split = p.c_split.hi != nullptr;
+#pragma unroll
+  for (int g = 0; g < NC; g += 16) {
+    float x[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[j] = acc[g + j] * s_b;
+    if (p.bias) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 4) {
+        const float4 b = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + g + j));
+        x[j] += b.x; x[j + 1] += b.y; x[j + 2] += b.z; x[j + 3] += b.w;
+      }
+    }
+    if (EPI == EPI_DSILU || EPI == EPI_RESID || EPI == EPI_ACCUM) {
+      const float *src = EPI == EPI_DSILU ? p.Z : EPI == EPI_RESID ? p.R : p.C;
+      const int ld = EPI == EPI_DSILU ? p.ldz : EPI == EPI_RESID ? p.ldr : p.ldc;
+      uint4 lv[4];
+      warp_load64(stage, lv, reinterpret_cast<const char *>(src + n0 + g), sizeof(float) * ld, row0, p.M, lane);
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const float l4[4] = {u2f(lv[m].x), u2f(lv[m].y), u2f(lv[m].z), u2f(lv[m].w)};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) x[4 * m + k] = EPI == EPI_DSILU ? x[4 * m + k] * l4[k] : x[4 * m + k] + l4[k];
+      }
+    }
+    if (EPI == EPI_SILU) {
+      uint4 dv[4];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        float y[4], dy[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) silu_pair(x[4 * m + k], y[k], dy[k]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) x[4 * m + k] = y[k];
+        dv[m] = make_uint4(f2u(dy[0]), f2u(dy[1]), f2u(dy[2]), f2u(dy[3]));
+      }
+      if (p.Z) warp_store64(stage, dv, reinterpret_cast<char *>(p.Z + n0 + g), sizeof(float) * p.ldz, row0, p.M, lane);
+    }
+    if (p.C) {
+      uint4 cv[4];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) cv[m] = make_uint4(f2u(x[4 * m]), f2u(x[4 * m + 1]), f2u(x[4 * m + 2]), f2u(x[4 * m + 3]));
+      warp_store64(stage, cv, reinterpret_cast<char *>(p.C + n0 + g), sizeof(float) * p.ldc, row0, p.M, lane);
+    }
+    if (split) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[g + j] = x[j];
+    }
+  }
+  if (split) {
+    float mx = 0.f;
+    if (valid) {
+#pragma unroll
+      for (int j = 0; j < NC; ++j) mx = fmaxf(mx, fabsf(acc[j]));
+    }
+    if (NC < 128) {  // the partner warp holds the other half of the scale block
+      float *slot = px->slot + px->parity * 64;
+      slot[px->half * 32 + lane] = mx;
+      mbar_arrive(px->bar);
+      // warp-uniform: the stores below are warp-collective
+      if (!__all_sync(0xffffffffu, wait_or_abort(px->bar, px->parity, px->abort_flag))) return;
+      mx = fmaxf(mx, slot[(1 - px->half) * 32 + lane]);
+    }
+    const int sx = split_scale_exponent(mx);
+    const float f = pow2f(sx);
+    const size_t pitch = sizeof(uint16_t) * p.c_split.cols;
+#pragma unroll
+    for (int g = 0; g < NC; g += 32) {
+      uint4 hv[4], lv[4];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) split2(acc[g + 8 * m + 2 * k], acc[g + 8 * m + 2 * k + 1], f, h[k], l[k]);
+        hv[m] = make_uint4(h[0], h[1], h[2], h[3]);
+        lv[m] = make_uint4(l[0], l[1], l[2], l[3]);
+      }
+      warp_store64(stage, hv, reinterpret_cast<char *>(p.c_split.hi + n0 + g), pitch, row0, p.M, lane);
+      warp_store64(stage, lv, reinterpret_cast<char *>(p.c_split.lo + n0 + g), pitch, row0, p.M, lane);
+    }
+    if (valid && (NC == 128 || px->half == 0))
+      p.c_split.sc[static_cast<size_t>(n0 / 128) * p.c_split.rows + row] = static_cast<int8_t>(sx);
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kWsThreads, 1) k_gemm_3xtf32(GemmArgs p, TCWeights w, int *err) {
   extern __shared__ uint8_t smem_raw[];
@@ -442,8 +573,10 @@ struct F16Cfg {
   static constexpr int LaunchBound = 384;
   static constexpr uint32_t Sbo = 8 * RowBytes;      // bytes between 8-row swizzle atoms
   static constexpr uint64_t Layout = BN_ == 256 ? 4 : 2;  // SWIZZLE_64B : SWIZZLE_128B
-  // stages, alignment, barriers, and the [4][2][2][32] block-max exchange
-  static constexpr int Smem = Stages * StageBytes + 1024 + 256 + 2048;
+  // stages, alignment, barriers, the [4][2][2][32] block-max exchange and
+  // the epilogue warps' staging blocks ([32][5] x 16 bytes each)
+  static constexpr int StageOut = 32 * 5 * 16;
+  static constexpr int Smem = Stages * StageBytes + 1024 + 256 + 2048 + AccWarps * StageOut;
 };
 
 template <typename C>
@@ -471,6 +604,7 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + C::Stages * C::StageBytes + 192);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(gbase + C::Stages * C::StageBytes + 200);
   float *xslots = reinterpret_cast<float *>(gbase + C::Stages * C::StageBytes + 256);
+  uint4 *ostage = reinterpret_cast<uint4 *>(gbase + C::Stages * C::StageBytes + 256 + 2048);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nk = p.K / C::BK;
@@ -587,6 +721,16 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
     const float sb = pow2f(-b_scale);
     int chunk = 0, ep = 0;
     bool ok = true;
+    // A scale exponent of this thread's row for one 128-k chunk (0 beyond
+    // the matrix), loaded one chunk ahead: the first chunk of the next tile
+    // is requested before this tile's epilogue, so the load's latency
+    // overlaps it instead of stalling the promotion
+    const int nch = nk / C::Chunk;
+    auto scale_of = [&](int tile, int c) -> int {
+      const int r = (tile / tiles_n) * BM + q * 32 + lane;
+      return (tile < tiles && r < p.M) ? static_cast<int>(sc[static_cast<size_t>(c) * p.M + r]) : 0;
+    };
+    int sc_next = scale_of(blockIdx.x, 0);
     for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ep) {
       const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BNt + h * NC;
       const int row = m0 + q * 32 + lane;
@@ -595,7 +739,10 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
       for (int j = 0; j < NC; ++j) acc[j] = 0.f;
       for (int kt0 = 0; kt0 < nk; kt0 += C::Chunk, ++chunk) {
         const int b = chunk % C::TmemBufs;
-        const float sa = row < p.M ? pow2f(-static_cast<int>(sc[static_cast<size_t>(kt0 / C::Chunk) * p.M + row])) : 0.f;
+        const int c = kt0 / C::Chunk;
+        const int sc_cur = sc_next;
+        sc_next = c + 1 < nch ? scale_of(tile, c + 1) : scale_of(tile + gridDim.x, 0);
+        const float sa = row < p.M ? pow2f(-sc_cur) : 0.f;
         if (!wait_or_abort(accf0 + 8 * b, (chunk / C::TmemBufs) & 1, abort_flag)) {
           ok = false;
           break;
@@ -615,7 +762,10 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
       }
       if (ok) {
         const PairExchange px{xslots + q * 128, xchg0 + 8 * q, ep & 1, h, abort_flag};
-        epilogue_store<EPI, true, NC>(p, row, n0, acc, 1.f, sb, &px);
+        if (p.c_rows)
+          epilogue_store<EPI, true, NC>(p, row, n0, acc, 1.f, sb, &px);
+        else
+          epilogue_store_staged<EPI, NC>(p, m0 + q * 32, lane, n0, acc, sb, &px, ostage + (warp - 2) * (32 * 5));
       }
     }
   }
