@@ -204,137 +204,6 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs &p, int row, int n
   }
 }
 
-// ---- coalesced epilogue ------------------------------------------------------
-// In the epilogue every lane owns one row (its TMEM lane), so a plain store
-// of a 16-byte piece per lane touches 32 rows at once.  These helpers move a
-// 64-byte segment of each of the warp's 32 rows through a per-warp staging
-// block ([32][5] 16-byte chunks: an odd row pitch, so the 8 rows a
-// quarter-warp touches fall in different bank groups): a warp instruction
-// then covers 8 rows x 64 contiguous bytes.
-__device__ __forceinline__ void warp_store64(uint4 *stage, const uint4 (&v)[4], char *base, size_t pitch, int row0,
-                                             int M, int lane) {
-#pragma unroll
-  for (int m = 0; m < 4; ++m) stage[lane * 5 + m] = v[m];
-  __syncwarp();
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int r = 8 * k + (lane >> 2), c = lane & 3;
-    if (row0 + r < M) *reinterpret_cast<uint4 *>(base + static_cast<size_t>(row0 + r) * pitch + 16 * c) = stage[r * 5 + c];
-  }
-  __syncwarp();
-}
-__device__ __forceinline__ void warp_load64(uint4 *stage, uint4 (&v)[4], const char *base, size_t pitch, int row0,
-                                            int M, int lane) {
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int r = 8 * k + (lane >> 2), c = lane & 3;
-    stage[r * 5 + c] = row0 + r < M ? *reinterpret_cast<const uint4 *>(base + static_cast<size_t>(row0 + r) * pitch + 16 * c)
-                                    : make_uint4(0u, 0u, 0u, 0u);
-  }
-  __syncwarp();
-#pragma unroll
-  for (int m = 0; m < 4; ++m) v[m] = stage[lane * 5 + m];
-  __syncwarp();
-}
-__device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
-__device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
-
-// epilogue_store for the 3xFP16 kernel when the output rows are not
-// scattered (p.c_rows == null): the same arithmetic, with every global load
-// and store of the epilogue (C, Z, R, the split hi / lo) made by the whole
-// warp through `stage`.  row0: the warp's first row; lanes past p.M take
-// part with zeros and store nothing.
-template <int EPI, int NC>
-__device__ __forceinline__ void epilogue_store_staged(const GemmArgs &p, int row0, int lane, int n0, float (&acc)[NC],
-                                                      float s_b, const PairExchange *px, uint4 *stage) {
-  static_assert(NC % 16 == 0, "16-column groups");
-  const int row = row0 + lane;
-  const bool valid = row < p.M;
-  const bool split = p.c_split.hi != nullptr;
-#pragma unroll
-  for (int g = 0; g < NC; g += 16) {
-    float x[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = acc[g + j] * s_b;
-    if (p.bias) {
-#pragma unroll
-      for (int j = 0; j < 16; j += 4) {
-        const float4 b = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + g + j));
-        x[j] += b.x; x[j + 1] += b.y; x[j + 2] += b.z; x[j + 3] += b.w;
-      }
-    }
-    if (EPI == EPI_DSILU || EPI == EPI_RESID || EPI == EPI_ACCUM) {
-      const float *src = EPI == EPI_DSILU ? p.Z : EPI == EPI_RESID ? p.R : p.C;
-      const int ld = EPI == EPI_DSILU ? p.ldz : EPI == EPI_RESID ? p.ldr : p.ldc;
-      uint4 lv[4];
-      warp_load64(stage, lv, reinterpret_cast<const char *>(src + n0 + g), sizeof(float) * ld, row0, p.M, lane);
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const float l4[4] = {u2f(lv[m].x), u2f(lv[m].y), u2f(lv[m].z), u2f(lv[m].w)};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) x[4 * m + k] = EPI == EPI_DSILU ? x[4 * m + k] * l4[k] : x[4 * m + k] + l4[k];
-      }
-    }
-    if (EPI == EPI_SILU) {
-      uint4 dv[4];
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        float y[4], dy[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) silu_pair(x[4 * m + k], y[k], dy[k]);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) x[4 * m + k] = y[k];
-        dv[m] = make_uint4(f2u(dy[0]), f2u(dy[1]), f2u(dy[2]), f2u(dy[3]));
-      }
-      if (p.Z) warp_store64(stage, dv, reinterpret_cast<char *>(p.Z + n0 + g), sizeof(float) * p.ldz, row0, p.M, lane);
-    }
-    if (p.C) {
-      uint4 cv[4];
-#pragma unroll
-      for (int m = 0; m < 4; ++m) cv[m] = make_uint4(f2u(x[4 * m]), f2u(x[4 * m + 1]), f2u(x[4 * m + 2]), f2u(x[4 * m + 3]));
-      warp_store64(stage, cv, reinterpret_cast<char *>(p.C + n0 + g), sizeof(float) * p.ldc, row0, p.M, lane);
-    }
-    if (split) {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) acc[g + j] = x[j];
-    }
-  }
-  if (split) {
-    float mx = 0.f;
-    if (valid) {
-#pragma unroll
-      for (int j = 0; j < NC; ++j) mx = fmaxf(mx, fabsf(acc[j]));
-    }
-    if (NC < 128) {  // the partner warp holds the other half of the scale block
-      float *slot = px->slot + px->parity * 64;
-      slot[px->half * 32 + lane] = mx;
-      mbar_arrive(px->bar);
-      // warp-uniform: the stores below are warp-collective
-      if (!__all_sync(0xffffffffu, wait_or_abort(px->bar, px->parity, px->abort_flag))) return;
-      mx = fmaxf(mx, slot[(1 - px->half) * 32 + lane]);
-    }
-    const int sx = split_scale_exponent(mx);
-    const float f = pow2f(sx);
-    const size_t pitch = sizeof(uint16_t) * p.c_split.cols;
-#pragma unroll
-    for (int g = 0; g < NC; g += 32) {
-      uint4 hv[4], lv[4];
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        uint32_t h[4], l[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) split2(acc[g + 8 * m + 2 * k], acc[g + 8 * m + 2 * k + 1], f, h[k], l[k]);
-        hv[m] = make_uint4(h[0], h[1], h[2], h[3]);
-        lv[m] = make_uint4(l[0], l[1], l[2], l[3]);
-      }
-      warp_store64(stage, hv, reinterpret_cast<char *>(p.c_split.hi + n0 + g), pitch, row0, p.M, lane);
-      warp_store64(stage, lv, reinterpret_cast<char *>(p.c_split.lo + n0 + g), pitch, row0, p.M, lane);
-    }
-    if (valid && (NC == 128 || px->half == 0))
-      p.c_split.sc[static_cast<size_t>(n0 / 128) * p.c_split.rows + row] = static_cast<int8_t>(sx);
-  }
-}
-
 template <int EPI>
 __global__ void __launch_bounds__(kWsThreads, 1) k_gemm_3xtf32(GemmArgs p, TCWeights w, int *err) {
   extern __shared__ uint8_t smem_raw[];
@@ -549,6 +418,221 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
       : "memory");
 }
 
+// ---- TMA epilogue ------------------------------------------------------------
+// Tensor maps of the epilogue's global operands (only those the launch uses
+// are encoded): fp32 C, Z (silu'), R (residual) with boxes of 16 columns x
+// 32 rows, and the split output's fp16 hi / lo with boxes of 32 x 32; all
+// with 64-byte rows and the 64-byte swizzle.
+struct EpiMaps {
+  CUtensorMap c, z, r, hi, lo;
+};
+
+__device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
+__device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
+// 16-byte chunk c (0..3) of row r of a 32 x 64-byte staging box (64-byte swizzle)
+__device__ __forceinline__ uint32_t sw64(uint32_t buf, int r, int c) {
+  return buf + static_cast<uint32_t>(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(src), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most N committed bulk groups of this thread still read shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Per-warp state of the TMA epilogue: two 2 KB staging buffers and their
+// load mbarriers; `ph` holds the parity of each buffer's next load wait.
+struct EpiWarp {
+  uint32_t buf0, lbar0;
+  uint32_t ph;
+};
+
+// epilogue_store for the 3xFP16 kernel when the output rows are not
+// scattered (p.c_rows == null): the same arithmetic, with the global
+// operands of the epilogue moved by TMA.  Lane = row (row0 + lane); the
+// 64 columns [n0, n0 + NC) go in groups of 16 (32 for the split output):
+// lanes write a group into a staging buffer, one lane stores it with
+// cp.async.bulk.tensor; loads of R / Z / C come the same way, two groups
+// ahead (the first two are issued by epi_prefetch before the promotion).
+// Rows past p.M are filled with zeros on load and clipped on store.
+// Returns false if a wait timed out (the abort flag is then set).
+template <int EPI>
+__device__ __forceinline__ const CUtensorMap *epi_load_map(const EpiMaps &em) {
+  return EPI == EPI_DSILU ? &em.z : EPI == EPI_RESID ? &em.r : &em.c;
+}
+template <int EPI>
+__device__ __forceinline__ void epi_prefetch(const EpiMaps &em, const EpiWarp &ew, int row0, int n0, int lane) {
+  if (!(EPI == EPI_DSILU || EPI == EPI_RESID || EPI == EPI_ACCUM)) return;
+  if (lane == 0) {
+    bulk_wait_read<0>();  // earlier stores no longer read the buffers
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      mbar_expect_tx(ew.lbar0 + 8 * b, 2048);
+      tma_load_2d(ew.buf0 + 2048 * b, epi_load_map<EPI>(em), ew.lbar0 + 8 * b, n0 + 16 * b, row0);
+    }
+  }
+  __syncwarp();
+}
+
+template <int EPI, int NC>
+__device__ __forceinline__ bool epilogue_tma(const GemmArgs &p, const EpiMaps &em, EpiWarp &ew, int row0, int lane,
+                                             int n0, float (&acc)[NC], float s_b, const PairExchange *px,
+                                             volatile int *abort_flag) {
+  static_assert(NC % 32 == 0, "32-column split groups");
+  constexpr bool kLoad = EPI == EPI_DSILU || EPI == EPI_RESID || EPI == EPI_ACCUM;
+  const int row = row0 + lane;
+  const bool valid = row < p.M;
+  const bool split = p.c_split.hi != nullptr;
+  const bool hasC = p.C != nullptr, hasZ = EPI == EPI_SILU && p.Z != nullptr;
+  if (!kLoad) {  // stores of earlier tiles no longer read the buffers
+    if (lane == 0) bulk_wait_read<0>();
+    __syncwarp();
+  }
+#pragma unroll
+  for (int g = 0; g < NC / 16; ++g) {
+    const int b = g & 1;
+    const uint32_t buf = ew.buf0 + 2048 * b;
+    float x[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[j] = acc[16 * g + j] * s_b;
+    if (p.bias) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 4) {
+        const float4 bb = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + 16 * g + j));
+        x[j] += bb.x; x[j + 1] += bb.y; x[j + 2] += bb.z; x[j + 3] += bb.w;
+      }
+    }
+    if (kLoad) {
+      if (!__all_sync(0xffffffffu, wait_or_abort(ew.lbar0 + 8 * b, (ew.ph >> b) & 1u, abort_flag))) return false;
+      ew.ph ^= 1u << b;
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const uint4 v = lds128(sw64(buf, lane, m));
+        const float l4[4] = {u2f(v.x), u2f(v.y), u2f(v.z), u2f(v.w)};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) x[4 * m + k] = EPI == EPI_DSILU ? x[4 * m + k] * l4[k] : x[4 * m + k] + l4[k];
+      }
+      // the result goes back into the same buffer, then to C; the buffer
+      // then receives the group two ahead (the proxy fence orders this
+      // warp's reads and writes of it before those TMA operations)
+      if (hasC) {
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+          sts128(sw64(buf, lane, m), make_uint4(f2u(x[4 * m]), f2u(x[4 * m + 1]), f2u(x[4 * m + 2]), f2u(x[4 * m + 3])));
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        if (hasC) {
+          tma_store_2d(&em.c, buf, n0 + 16 * g, row0);
+          bulk_commit();
+        }
+        if (g + 2 < NC / 16) {
+          bulk_wait_read<0>();
+          mbar_expect_tx(ew.lbar0 + 8 * b, 2048);
+          tma_load_2d(buf, epi_load_map<EPI>(em), ew.lbar0 + 8 * b, n0 + 16 * (g + 2), row0);
+        }
+      }
+    } else {
+      uint4 zv[4];
+      if (EPI == EPI_SILU) {
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          float y[4], dy[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) silu_pair(x[4 * m + k], y[k], dy[k]);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) x[4 * m + k] = y[k];
+          zv[m] = make_uint4(f2u(dy[0]), f2u(dy[1]), f2u(dy[2]), f2u(dy[3]));
+        }
+      }
+      // one store per buffer and group (Z in buffer 0, C in buffer 1 for the
+      // SiLU with both; otherwise buffers alternate by group)
+      const int nst = (hasZ ? 1 : 0) + (hasC ? 1 : 0);
+      if (nst) {
+        if (lane == 0) {
+          if (nst == 2) bulk_wait_read<0>();
+          else bulk_wait_read<1>();
+        }
+        __syncwarp();
+        const uint32_t bz = nst == 2 ? ew.buf0 : buf, bc = nst == 2 ? ew.buf0 + 2048 : buf;
+        if (hasZ) {
+#pragma unroll
+          for (int m = 0; m < 4; ++m) sts128(sw64(bz, lane, m), zv[m]);
+        }
+        if (hasC) {
+#pragma unroll
+          for (int m = 0; m < 4; ++m)
+            sts128(sw64(bc, lane, m), make_uint4(f2u(x[4 * m]), f2u(x[4 * m + 1]), f2u(x[4 * m + 2]), f2u(x[4 * m + 3])));
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          if (hasZ) tma_store_2d(&em.z, bz, n0 + 16 * g, row0);
+          if (hasC) tma_store_2d(&em.c, bc, n0 + 16 * g, row0);
+          bulk_commit();
+        }
+      }
+    }
+    if (split) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[16 * g + j] = x[j];
+    }
+  }
+  if (split) {
+    float mx = 0.f;
+    if (valid) {
+#pragma unroll
+      for (int j = 0; j < NC; ++j) mx = fmaxf(mx, fabsf(acc[j]));
+    }
+    if (NC < 128) {  // the partner warp holds the other half of the scale block
+      float *slot = px->slot + px->parity * 64;
+      slot[px->half * 32 + lane] = mx;
+      mbar_arrive(px->bar);
+      if (!__all_sync(0xffffffffu, wait_or_abort(px->bar, px->parity, px->abort_flag))) return false;
+      mx = fmaxf(mx, slot[(1 - px->half) * 32 + lane]);
+    }
+    const int sx = split_scale_exponent(mx);
+    const float f = pow2f(sx);
+#pragma unroll
+    for (int g = 0; g < NC / 32; ++g) {
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) split2(acc[32 * g + 8 * m + 2 * k], acc[32 * g + 8 * m + 2 * k + 1], f, h[k], l[k]);
+        sts128(sw64(ew.buf0, lane, m), make_uint4(h[0], h[1], h[2], h[3]));
+        sts128(sw64(ew.buf0 + 2048, lane, m), make_uint4(l[0], l[1], l[2], l[3]));
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&em.hi, ew.buf0, n0 + 32 * g, row0);
+        tma_store_2d(&em.lo, ew.buf0 + 2048, n0 + 32 * g, row0);
+        bulk_commit();
+      }
+    }
+    if (valid && (NC == 128 || px->half == 0))
+      p.c_split.sc[static_cast<size_t>(n0 / 128) * p.c_split.rows + row] = static_cast<int8_t>(sx);
+  }
+  return true;
+}
+
 // Tile shapes of the 3xFP16 kernel.  BN = 128: k-tiles of 64 (128-byte rows,
 // 128-byte swizzle), 3 stages of 64 KB, 4 TMEM buffers, 4 accumulator
 // warps.  BN = 256: k-tiles of 32 (64-byte rows, 64-byte swizzle), 4 stages
@@ -573,10 +657,12 @@ struct F16Cfg {
   static constexpr int LaunchBound = 384;
   static constexpr uint32_t Sbo = 8 * RowBytes;      // bytes between 8-row swizzle atoms
   static constexpr uint64_t Layout = BN_ == 256 ? 4 : 2;  // SWIZZLE_64B : SWIZZLE_128B
-  // stages, alignment, barriers, the [4][2][2][32] block-max exchange and
-  // the epilogue warps' staging blocks ([32][5] x 16 bytes each)
-  static constexpr int StageOut = 32 * 5 * 16;
-  static constexpr int Smem = Stages * StageBytes + 1024 + 256 + 2048 + AccWarps * StageOut;
+  // stages, the epilogue warps' staging buffers (2 x 2 KB each), barriers
+  // and slots (512 B), the [4][2][2][32] block-max exchange, and up to
+  // Slack bytes lost to aligning the base to 1024 (the kernel checks)
+  static constexpr int StageOut = 2 * 2048;
+  static constexpr int Slack = 512;
+  static constexpr int Smem = Stages * StageBytes + AccWarps * StageOut + 512 + 2048 + Slack;
 };
 
 template <typename C>
@@ -589,22 +675,29 @@ template <int EPI, int BNt>
 __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
     k_gemm_3xf16(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
                  const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
-                 GemmArgs p, const int8_t *__restrict__ sc, TCWeights16 w, int *err) {
+                 const __grid_constant__ EpiMaps em, GemmArgs p, const int8_t *__restrict__ sc, TCWeights16 w,
+                 int *err) {
   const int b_scale = w.b_scale;
   using C = F16Cfg<BNt>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
+  if (base - raw > static_cast<uint32_t>(C::Slack)) {  // shared-memory plan does not fit: fail loudly
+    if (threadIdx.x == 0) atomicExch(err, 3);
+    return;
+  }
   uint8_t *gbase = smem_raw + (base - raw);
-  const uint32_t bars = base + C::Stages * C::StageBytes;
+  const uint32_t ostage = base + C::Stages * C::StageBytes;  // epilogue staging, 1024-aligned
+  const uint32_t bars = ostage + C::AccWarps * C::StageOut;
+  const int small = C::Stages * C::StageBytes + C::AccWarps * C::StageOut;  // byte offset of `bars` from gbase
   // mbarriers: full[Stages], empty[Stages], accf[TmemBufs], acce[TmemBufs],
-  // xchg[4] (block-max exchange of the two warps of each lane quarter)
+  // xchg[4] (block-max exchange of the two warps of each lane quarter),
+  // eload[2 per epilogue warp] (TMA loads of the epilogue's inputs)
   const uint32_t full0 = bars, empty0 = bars + 8 * C::Stages, accf0 = bars + 16 * C::Stages,
-                 acce0 = accf0 + 8 * C::TmemBufs, xchg0 = acce0 + 8 * C::TmemBufs;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + C::Stages * C::StageBytes + 192);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(gbase + C::Stages * C::StageBytes + 200);
-  float *xslots = reinterpret_cast<float *>(gbase + C::Stages * C::StageBytes + 256);
-  uint4 *ostage = reinterpret_cast<uint4 *>(gbase + C::Stages * C::StageBytes + 256 + 2048);
+                 acce0 = accf0 + 8 * C::TmemBufs, xchg0 = acce0 + 8 * C::TmemBufs, eload0 = xchg0 + 32;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + small + 384);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(gbase + small + 392);
+  float *xslots = reinterpret_cast<float *>(gbase + small + 512);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nk = p.K / C::BK;
@@ -626,6 +719,7 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
       mbar_init(acce0 + 8 * b, 32 * C::AccWarps);
     }
     for (int q = 0; q < 4; ++q) mbar_init(xchg0 + 8 * q, 64);
+    for (int e = 0; e < 2 * C::AccWarps; ++e) mbar_init(eload0 + 8 * e, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -731,9 +825,11 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
       return (tile < tiles && r < p.M) ? static_cast<int>(sc[static_cast<size_t>(c) * p.M + r]) : 0;
     };
     int sc_next = scale_of(blockIdx.x, 0);
+    EpiWarp ew{ostage + static_cast<uint32_t>((warp - 2) * C::StageOut), eload0 + 16u * (warp - 2), 0u};
     for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ep) {
       const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BNt + h * NC;
       const int row = m0 + q * 32 + lane;
+      if (!p.c_rows) epi_prefetch<EPI>(em, ew, m0 + q * 32, n0, lane);
       float acc[NC];
 #pragma unroll
       for (int j = 0; j < NC; ++j) acc[j] = 0.f;
@@ -765,9 +861,10 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
         if (p.c_rows)
           epilogue_store<EPI, true, NC>(p, row, n0, acc, 1.f, sb, &px);
         else
-          epilogue_store_staged<EPI, NC>(p, m0 + q * 32, lane, n0, acc, sb, &px, ostage + (warp - 2) * (32 * 5));
+          ok = epilogue_tma<EPI, NC>(p, em, ew, m0 + q * 32, lane, n0, acc, sb, &px, abort_flag);
       }
     }
+    if (lane == 0) bulk_wait_all();  // the epilogue's stores are complete before the CTA ends
   }
 
   tc_fence_before();
@@ -1046,15 +1143,18 @@ const int g_f16_bn = [] {
 
 // Row-major [rows, cols] fp16 matrix with leading dimension ld (elements):
 // boxes of box_k x box_rows, 128- or 64-byte swizzle, zero fill outside.
+void resolve_encoder() {
+  if (g_encode_tiled) return;
+  void *fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+  if (!fn || q != cudaDriverEntryPointSuccess) throw Error(kErrBackend, "cuTensorMapEncodeTiled unavailable");
+  g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+}
+
 CUtensorMap make_map_f16(const void *ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_k,
                          uint32_t box_rows) {
-  if (!g_encode_tiled) {
-    void *fn = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
-    if (!fn || q != cudaDriverEntryPointSuccess) throw Error(kErrBackend, "cuTensorMapEncodeTiled unavailable");
-    g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  }
+  resolve_encoder();
   CUtensorMap m;
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {ld * 2};
@@ -1068,6 +1168,39 @@ CUtensorMap make_map_f16(const void *ptr, uint64_t rows, uint64_t cols, uint64_t
   return m;
 }
 
+// Map of an epilogue operand: [rows][cols] of `elem`-byte elements with
+// leading dimension ld, box (32 x 64 bytes), 64-byte swizzle.
+CUtensorMap make_map_epi(const void *ptr, CUtensorMapDataType type, uint32_t elem, uint64_t rows, uint64_t cols,
+                         uint64_t ld) {
+  resolve_encoder();
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld * elem};
+  const cuuint32_t box[2] = {64 / elem, 32};
+  const cuuint32_t es[2] = {1, 1};
+  const CUresult r = g_encode_tiled(&m, type, 2, const_cast<void *>(ptr), dims, strides, box, es,
+                                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Error(kErrBackend, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return m;
+}
+
+// The epilogue maps a launch uses (unscattered output rows only).
+EpiMaps make_epi_maps(const GemmArgs &a) {
+  EpiMaps e;
+  std::memset(&e, 0, sizeof(e));
+  if (a.c_rows) return e;
+  const auto F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32, F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  if (a.C) e.c = make_map_epi(a.C, F32, 4, a.M, a.N, a.ldc);
+  if (a.Z && (a.epi == EPI_SILU || a.epi == EPI_DSILU)) e.z = make_map_epi(a.Z, F32, 4, a.M, a.N, a.ldz);
+  if (a.epi == EPI_RESID) e.r = make_map_epi(a.R, F32, 4, a.M, a.N, a.ldr);
+  if (a.c_split.hi) {
+    e.hi = make_map_epi(a.c_split.hi, F16, 2, a.M, a.N, a.c_split.cols);
+    e.lo = make_map_epi(a.c_split.lo, F16, 2, a.M, a.N, a.c_split.cols);
+  }
+  return e;
+}
+
 template <int EPI, int BNt>
 void launch16_bn(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t s) {
   const Split16View &sp = a.a_split;
@@ -1078,7 +1211,8 @@ void launch16_bn(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t
   CUDA_CHECK(cudaFuncSetAttribute(k_gemm_3xf16<EPI, BNt>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::Smem));
   const int tiles = ceil_div(a.M, BM) * (a.N / BNt);
   const int grid = tiles < g_num_sms ? tiles : g_num_sms;
-  k_gemm_3xf16<EPI, BNt><<<grid, C::Threads, C::Smem, s>>>(ah, al, bh, bl, a, sp.sc, w, err);
+  const EpiMaps em = make_epi_maps(a);
+  k_gemm_3xf16<EPI, BNt><<<grid, C::Threads, C::Smem, s>>>(ah, al, bh, bl, em, a, sp.sc, w, err);
   CUDA_LAUNCH_CHECK();
 }
 
