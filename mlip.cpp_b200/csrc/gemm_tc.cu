@@ -633,6 +633,139 @@ __device__ __forceinline__ bool epilogue_tma(const GemmArgs &p, const EpiMaps &e
   return true;
 }
 
+// ---- epilogue with scattered output rows (p.c_rows) ----------------------------
+// The rows of a warp go to arbitrary destination rows, which TMA tile stores
+// cannot express; 64-byte row segments still move through the staging
+// buffer (64-byte swizzle) so that a warp instruction covers 8 rows x 64
+// contiguous bytes.  drow: this lane's destination row, -1 for none.
+__device__ __forceinline__ void rows_store64(uint32_t buf, const uint4 (&v)[4], char *base, size_t pitch, int drow,
+                                             int lane) {
+#pragma unroll
+  for (int m = 0; m < 4; ++m) sts128(sw64(buf, lane, m), v[m]);
+  __syncwarp();
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = 8 * k + (lane >> 2), c = lane & 3;
+    const int dr = __shfl_sync(0xffffffffu, drow, r);
+    const uint4 x = lds128(sw64(buf, r, c));
+    if (dr >= 0) *reinterpret_cast<uint4 *>(base + static_cast<size_t>(dr) * pitch + 16 * c) = x;
+  }
+  __syncwarp();
+}
+__device__ __forceinline__ void rows_load64(uint32_t buf, uint4 (&v)[4], const char *base, size_t pitch, int srow,
+                                            int lane) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = 8 * k + (lane >> 2), c = lane & 3;
+    const int sr = __shfl_sync(0xffffffffu, srow, r);
+    sts128(sw64(buf, r, c), sr >= 0 ? *reinterpret_cast<const uint4 *>(base + static_cast<size_t>(sr) * pitch + 16 * c)
+                                    : make_uint4(0u, 0u, 0u, 0u));
+  }
+  __syncwarp();
+#pragma unroll
+  for (int m = 0; m < 4; ++m) v[m] = lds128(sw64(buf, lane, m));
+  __syncwarp();
+}
+
+// epilogue_store for the 3xFP16 kernel with scattered output rows: C, R and
+// the split output at rows c_rows[row], Z at rows `row`, through the
+// staging buffer with plain loads and stores.
+template <int EPI, int NC>
+__device__ __forceinline__ bool epilogue_rows(const GemmArgs &p, const EpiWarp &ew, int row0, int lane, int n0,
+                                              float (&acc)[NC], float s_b, const PairExchange *px) {
+  static_assert(NC % 32 == 0, "32-column split groups");
+  const int row = row0 + lane;
+  const bool valid = row < p.M;
+  const int rc = valid ? p.c_rows[row] : -1, rz = valid ? row : -1;
+  const bool split = p.c_split.hi != nullptr;
+  const uint32_t buf = ew.buf0;
+  if (lane == 0) bulk_wait_read<0>();  // no TMA store of this warp still reads the buffer
+  __syncwarp();
+#pragma unroll
+  for (int g = 0; g < NC / 16; ++g) {
+    const int c0 = n0 + 16 * g;
+    float x[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[j] = acc[16 * g + j] * s_b;
+    if (p.bias) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 4) {
+        const float4 bb = __ldg(reinterpret_cast<const float4 *>(p.bias + c0 + j));
+        x[j] += bb.x; x[j + 1] += bb.y; x[j + 2] += bb.z; x[j + 3] += bb.w;
+      }
+    }
+    if (EPI == EPI_DSILU || EPI == EPI_RESID || EPI == EPI_ACCUM) {
+      uint4 lv[4];
+      if (EPI == EPI_DSILU) rows_load64(buf, lv, reinterpret_cast<const char *>(p.Z + c0), sizeof(float) * p.ldz, rz, lane);
+      else if (EPI == EPI_RESID) rows_load64(buf, lv, reinterpret_cast<const char *>(p.R + c0), sizeof(float) * p.ldr, rc, lane);
+      else rows_load64(buf, lv, reinterpret_cast<const char *>(p.C + c0), sizeof(float) * p.ldc, rc, lane);
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const float l4[4] = {u2f(lv[m].x), u2f(lv[m].y), u2f(lv[m].z), u2f(lv[m].w)};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) x[4 * m + k] = EPI == EPI_DSILU ? x[4 * m + k] * l4[k] : x[4 * m + k] + l4[k];
+      }
+    }
+    if (EPI == EPI_SILU) {
+      uint4 zv[4];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        float y[4], dy[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) silu_pair(x[4 * m + k], y[k], dy[k]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) x[4 * m + k] = y[k];
+        zv[m] = make_uint4(f2u(dy[0]), f2u(dy[1]), f2u(dy[2]), f2u(dy[3]));
+      }
+      if (p.Z) rows_store64(buf, zv, reinterpret_cast<char *>(p.Z + c0), sizeof(float) * p.ldz, rz, lane);
+    }
+    if (p.C) {
+      uint4 cv[4];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) cv[m] = make_uint4(f2u(x[4 * m]), f2u(x[4 * m + 1]), f2u(x[4 * m + 2]), f2u(x[4 * m + 3]));
+      rows_store64(buf, cv, reinterpret_cast<char *>(p.C + c0), sizeof(float) * p.ldc, rc, lane);
+    }
+    if (split) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[16 * g + j] = x[j];
+    }
+  }
+  if (split) {
+    float mx = 0.f;
+    if (valid) {
+#pragma unroll
+      for (int j = 0; j < NC; ++j) mx = fmaxf(mx, fabsf(acc[j]));
+    }
+    if (NC < 128) {
+      float *slot = px->slot + px->parity * 64;
+      slot[px->half * 32 + lane] = mx;
+      mbar_arrive(px->bar);
+      if (!__all_sync(0xffffffffu, wait_or_abort(px->bar, px->parity, px->abort_flag))) return false;
+      mx = fmaxf(mx, slot[(1 - px->half) * 32 + lane]);
+    }
+    const int sx = split_scale_exponent(mx);
+    const float f = pow2f(sx);
+    const size_t pitch = sizeof(uint16_t) * p.c_split.cols;
+#pragma unroll
+    for (int g = 0; g < NC / 32; ++g) {
+      uint4 hv[4], lv[4];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) split2(acc[32 * g + 8 * m + 2 * k], acc[32 * g + 8 * m + 2 * k + 1], f, h[k], l[k]);
+        hv[m] = make_uint4(h[0], h[1], h[2], h[3]);
+        lv[m] = make_uint4(l[0], l[1], l[2], l[3]);
+      }
+      rows_store64(buf, hv, reinterpret_cast<char *>(p.c_split.hi + n0 + 32 * g), pitch, rc, lane);
+      rows_store64(buf, lv, reinterpret_cast<char *>(p.c_split.lo + n0 + 32 * g), pitch, rc, lane);
+    }
+    if (valid && (NC == 128 || px->half == 0))
+      p.c_split.sc[static_cast<size_t>(n0 / 128) * p.c_split.rows + rc] = static_cast<int8_t>(sx);
+  }
+  return true;
+}
+
 // Tile shapes of the 3xFP16 kernel.  BN = 128: k-tiles of 64 (128-byte rows,
 // 128-byte swizzle), 3 stages of 64 KB, 4 TMEM buffers, 4 accumulator
 // warps.  BN = 256: k-tiles of 32 (64-byte rows, 64-byte swizzle), 4 stages
@@ -859,7 +992,7 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
       if (ok) {
         const PairExchange px{xslots + q * 128, xchg0 + 8 * q, ep & 1, h, abort_flag};
         if (p.c_rows)
-          epilogue_store<EPI, true, NC>(p, row, n0, acc, 1.f, sb, &px);
+          ok = epilogue_rows<EPI, NC>(p, ew, m0 + q * 32, lane, n0, acc, sb, &px);
         else
           ok = epilogue_tma<EPI, NC>(p, em, ew, m0 + q * 32, lane, n0, acc, sb, &px, abort_flag);
       }
