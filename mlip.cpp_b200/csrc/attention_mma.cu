@@ -1,0 +1,579 @@
+// Per-atom multi-head attention, forward and backward, on register-resident
+// tensor-core products (mma.sync m16n8k16, fp16 inputs, fp32 accumulation)
+// in split-fp16 form: x 2^s = hi + lo and every product is the sum
+// hi.lo + lo.hi + hi.hi, which carries about 22 significant bits, as in the
+// 3xFP16 GEMM.  Head size 32, at most 64 tokens per atom.
+//
+// Reference: build_multi_head_attention, src/models/pet/pet_layers.cpp:318-492
+// (softmax(Q K^T / sqrt(hd) + mask) V per atom, the key mask shared by all
+// queries); each atom attends over its own S = n + 1 tokens only.
+//
+// Why this form: a per-atom block is at most 64 x 64.  tcgen05 works on 64-
+// or 128-row tiles whose accumulators live in tensor memory and whose
+// operands must be in shared memory, so every P and dS block would make a
+// round trip TMEM -> registers -> shared memory between products (measured:
+// 9.4 ms per forward against 6.1 ms for the SIMT kernel, attention_tc.cu).
+// Here the scores, P, dP and dS of a 16-row strip stay in the registers of
+// one warp, and the accumulator layout of one product is the operand layout
+// of the next.
+//
+// A CTA is one (atom, head), 4 warps.  Q, K, V (and dO) of the head are
+// converted once into split-fp16 shared-memory blocks [64][40] (80-byte rows,
+// conflict-free for ldmatrix), one power-of-two scale per block.
+//   forward, warp w = query rows 16w..16w+15:
+//     S = Q K^T, softmax along the row (quad shuffles), lse, O = P V;
+//   backward, pass 1, warp w = query rows:
+//     S, P (from lse), dP = dO V^T, D = rowsum(P o dP), dS = P o (dP - D),
+//     dQ = s dS K;
+//   backward, pass 2, warp w = key rows (transposed recomputation):
+//     S^T = K Q^T, P^T, dP^T = V dO^T, dS^T, dV = P^T dO, dK = s dS^T Q.
+// P enters a product at the fixed scale 2^14; dS with one scale per warp
+// strip.  Split-fp16 outputs need one scale per (row, 128-column block),
+// i.e. per 4 heads: those 4 CTAs form a cluster and exchange their row
+// maxima through distributed shared memory.
+#include <cfloat>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "split16.cuh"
+
+namespace pet {
+namespace {
+
+constexpr int kHd = 32;
+constexpr int kMaxTok = 64;
+constexpr int kPitch = 40;                  // halves per shared-memory row (80 bytes)
+constexpr int kMat = kMaxTok * kPitch;      // halves per [64][40] block
+constexpr int kThreads = 128;
+
+// ---- small helpers --------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void ldsm4(uint32_t (&r)[4], uint32_t a) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+__device__ __forceinline__ void ldsm4t(uint32_t (&r)[4], uint32_t a) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+// c += a b  (16 x 8 x 16, fp16 in, fp32 accumulate).  A register-only
+// operation: not volatile, so independent products can be interleaved.
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// c += (ah + al)(bh + bl) without the al bl term
+__device__ __forceinline__ void mma3(float (&c)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4], uint32_t bh0,
+                                     uint32_t bh1, uint32_t bl0, uint32_t bl1) {
+  mma16816(c, ah, bl0, bl1);
+  mma16816(c, al, bh0, bh1);
+  mma16816(c, ah, bh0, bh1);
+}
+
+// Address for ldmatrix.x4 of the 16 x 16 block at (r0, c0) of a [64][40]
+// fp16 block, A-operand order: matrices (r0, c0), (r0 + 8, c0), (r0, c0 + 8),
+// (r0 + 8, c0 + 8) -> a0..a3.
+__device__ __forceinline__ uint32_t a_addr(uint32_t base, int r0, int c0, int lane) {
+  const int j = lane >> 3;
+  return base + 2u * static_cast<uint32_t>((r0 + (lane & 7) + 8 * (j & 1)) * kPitch + c0 + 8 * (j >> 1));
+}
+// B operand of two n-tiles from an [n][k] block (rows = the product's
+// columns): matrices (n0, k0), (n0, k0 + 8), (n0 + 8, k0), (n0 + 8, k0 + 8)
+// -> b0, b1 of tile n0 and b0, b1 of tile n0 + 8.
+__device__ __forceinline__ uint32_t bn_addr(uint32_t base, int n0, int k0, int lane) {
+  const int j = lane >> 3;
+  return base + 2u * static_cast<uint32_t>((n0 + (lane & 7) + 8 * (j >> 1)) * kPitch + k0 + 8 * (j & 1));
+}
+// B operand of two n-tiles from a [k][n] block, with ldmatrix.trans:
+// matrices (k0, n0), (k0 + 8, n0), (k0, n0 + 8), (k0 + 8, n0 + 8).
+__device__ __forceinline__ uint32_t bk_addr(uint32_t base, int k0, int n0, int lane) {
+  const int j = lane >> 3;
+  return base + 2u * static_cast<uint32_t>((k0 + (lane & 7) + 8 * (j & 1)) * kPitch + n0 + 8 * (j >> 1));
+}
+
+// Accumulator tiles (c-layout) 2t and 2t + 1 as the A fragment of k-step t,
+// in split form at scale f.
+__device__ __forceinline__ void c_to_a(const float (&c0)[4], const float (&c1)[4], float f, uint32_t (&ah)[4],
+                                       uint32_t (&al)[4]) {
+  split2(c0[0], c0[1], f, ah[0], al[0]);
+  split2(c0[2], c0[3], f, ah[1], al[1]);
+  split2(c1[0], c1[1], f, ah[2], al[2]);
+  split2(c1[2], c1[3], f, ah[3], al[3]);
+}
+
+__device__ __forceinline__ float quad_max(float v) {
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+}
+__device__ __forceinline__ float quad_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  return v + __shfl_xor_sync(0xffffffffu, v, 2);
+}
+__device__ __forceinline__ float warp_absmax(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---- cluster helpers (split outputs) -----------------------------------------
+__device__ __forceinline__ uint32_t cta_rank_in_cluster() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ int ld_peer(const int *local, uint32_t rank) {
+  const uint32_t a = smem_addr(local);
+  uint32_t r;
+  int v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(r) : "memory");
+  return v;
+}
+// Largest of a row's maxima over the 4 CTAs (heads) of the cluster.
+__device__ __forceinline__ float cluster_row_max(const int *local) {
+  int m = 0;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) m = max(m, ld_peer(local, static_cast<uint32_t>(r)));
+  return __int_as_float(m);
+}
+
+// ---- shared memory -------------------------------------------------------------
+struct Smem {
+  uint16_t mat[8][kMat];  // Q, K, V, dO: hi then lo ([0..3] hi, [4..7] lo)
+  float lse[kMaxTok], mask[kMaxTok], D[kMaxTok];
+  int scale[4];           // block scale exponents of Q, K, V, dO
+  int rmax[3][kMaxTok];   // row maxima of the outputs (bits of non-negative floats)
+};
+
+// Q, K, V (and dO when `grad`) of (atom, head) into split-fp16 blocks; warp
+// w converts block w (rows past S are zero) with one scale from its maximum.
+__device__ __forceinline__ void load_blocks(Smem &sm, const AttnArgs &a, int t0, int S, int h, bool grad) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp < 3 || grad) {
+    float v[8][8];
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int task = lane + 32 * i, r = task >> 2, c = (task & 3) * 8;
+      if (r < S) {
+        const float *src = warp < 3 ? a.qkv + static_cast<size_t>(t0 + r) * 3 * a.d + warp * a.d + h * kHd + c
+                                    : a.d_out + static_cast<size_t>(t0 + r) * a.d + h * kHd + c;
+        const float4 x0 = *reinterpret_cast<const float4 *>(src), x1 = *reinterpret_cast<const float4 *>(src + 4);
+        v[i][0] = x0.x; v[i][1] = x0.y; v[i][2] = x0.z; v[i][3] = x0.w;
+        v[i][4] = x1.x; v[i][5] = x1.y; v[i][6] = x1.z; v[i][7] = x1.w;
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[i][k] = 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx = fmaxf(mx, fabsf(v[i][k]));
+    }
+    const int s = split_scale_exponent(warp_absmax(mx));
+    const float f = pow2f(s);
+    if (lane == 0) sm.scale[warp] = s;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int task = lane + 32 * i, r = task >> 2, c = (task & 3) * 8;
+      uint32_t hh[4], ll[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) split2(v[i][2 * k], v[i][2 * k + 1], f, hh[k], ll[k]);
+      *reinterpret_cast<uint4 *>(&sm.mat[warp][r * kPitch + c]) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
+      *reinterpret_cast<uint4 *>(&sm.mat[4 + warp][r * kPitch + c]) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+    }
+  }
+}
+
+// Row maxima of a 16-row strip's outputs (4 n-tiles of the c-layout) into
+// sm.rmax[m] (quad-reduced, one atomic per row).
+__device__ __forceinline__ void strip_rowmax(int *rm, const float (&o)[4][4], int r0, int S, int lane) {
+  float m0 = 0.f, m1 = 0.f;
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {
+    m0 = fmaxf(m0, fmaxf(fabsf(o[n][0]), fabsf(o[n][1])));
+    m1 = fmaxf(m1, fmaxf(fabsf(o[n][2]), fabsf(o[n][3])));
+  }
+  m0 = quad_max(m0);
+  m1 = quad_max(m1);
+  const int g = lane >> 2;
+  if ((lane & 3) == 0) {
+    if (r0 + g < S) atomicMax(rm + r0 + g, __float_as_int(m0));
+    if (r0 + g + 8 < S) atomicMax(rm + r0 + g + 8, __float_as_int(m1));
+  }
+}
+
+// Store a 16-row strip (4 n-tiles, columns col0 + 8n + 2 tig) as fp32 into
+// dst (row pitch ld) or, when `o` is set, in split form with the block
+// scales from the cluster's row maxima `rm`.
+__device__ __forceinline__ void strip_store(const float (&v)[4][4], int r0, int S, int t0, int lane, float *dst,
+                                            size_t ld, int col0, const Split16View *o, const int *rm, int blk,
+                                            bool write_scale) {
+  const int g = lane >> 2, tig = lane & 3;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int r = r0 + g + 8 * half;
+    if (r >= S) continue;
+    if (dst) {
+      float *p = dst + static_cast<size_t>(t0 + r) * ld + col0 + 2 * tig;
+#pragma unroll
+      for (int n = 0; n < 4; ++n) *reinterpret_cast<float2 *>(p + 8 * n) = make_float2(v[n][2 * half], v[n][2 * half + 1]);
+    }
+    if (o) {
+      const int s = split_scale_exponent(cluster_row_max(rm + r));
+      const float f = pow2f(s);
+      const size_t off = static_cast<size_t>(t0 + r) * o->cols + col0 + 2 * tig;
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        uint32_t hh, ll;
+        split2(v[n][2 * half], v[n][2 * half + 1], f, hh, ll);
+        *reinterpret_cast<uint32_t *>(o->hi + off + 8 * n) = hh;
+        *reinterpret_cast<uint32_t *>(o->lo + off + 8 * n) = ll;
+      }
+      if (write_scale && tig == 0) o->sc[static_cast<size_t>(blk) * o->rows + t0 + r] = static_cast<int8_t>(s);
+    }
+  }
+}
+
+// ---- forward ---------------------------------------------------------------------
+template <bool kSplit>
+__global__ void __launch_bounds__(kThreads) k_attn_fwd_mma(AttnArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
+  const int atom = blockIdx.x, h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+  const int e0 = a.offset[atom], S = a.offset[atom + 1] - e0 + 1, t0 = e0 + atom;
+  const int NW = (S + 15) >> 4, NK8 = 2 * NW;  // row strips, 8-key tiles
+  load_blocks(sm, a, t0, S, h, false);
+  for (int k = threadIdx.x; k < kMaxTok; k += kThreads) {
+    sm.mask[k] = k < S ? (k == 0 ? 0.f : a.key_mask[e0 + k - 1]) : 0.f;
+    if (kSplit) sm.rmax[0][k] = 0;
+  }
+  __syncthreads();
+  const uint32_t Qh = smem_addr(sm.mat[0]), Ql = smem_addr(sm.mat[4]), Kh = smem_addr(sm.mat[1]),
+                 Kl = smem_addr(sm.mat[5]), Vh = smem_addr(sm.mat[2]), Vl = smem_addr(sm.mat[6]);
+  float o[4][4];
+#pragma unroll
+  for (int n = 0; n < 4; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[n][e] = 0.f;
+  const int q0 = 16 * warp;
+  const bool act = warp < NW;
+  if (act) {
+    float s[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[n][e] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+      uint32_t ah[4], al[4];
+      ldsm4(ah, a_addr(Qh, q0, 16 * ks, lane));
+      ldsm4(al, a_addr(Ql, q0, 16 * ks, lane));
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        if (2 * p < NK8) {
+          uint32_t bh[4], bl[4];
+          ldsm4(bh, bn_addr(Kh, 16 * p, 16 * ks, lane));
+          ldsm4(bl, bn_addr(Kl, 16 * p, 16 * ks, lane));
+          mma3(s[2 * p], ah, al, bh[0], bh[1], bl[0], bl[1]);
+          mma3(s[2 * p + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+        }
+      }
+    }
+    // softmax along each row (rows g and g + 8 of the strip)
+    const float fs = pow2f(-(sm.scale[0] + sm.scale[1])) * (1.0f / sqrtf(static_cast<float>(kHd)));
+    float m[2] = {-FLT_MAX, -FLT_MAX};
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = q0 + g + 8 * (e >> 1), c = 8 * n + 2 * tig + (e & 1);
+        s[n][e] = (n < NK8 && r < S && c < S) ? fmaf(s[n][e], fs, sm.mask[c]) : -FLT_MAX;
+        m[e >> 1] = fmaxf(m[e >> 1], s[n][e]);
+      }
+    }
+    m[0] = quad_max(m[0]);
+    m[1] = quad_max(m[1]);
+    float l[2] = {0.f, 0.f};
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        s[n][e] = s[n][e] == -FLT_MAX ? 0.f : expf(s[n][e] - m[e >> 1]);
+        l[e >> 1] += s[n][e];
+      }
+    l[0] = quad_sum(l[0]);
+    l[1] = quad_sum(l[1]);
+    if (tig == 0) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int r = q0 + g + 8 * half;
+        if (r < S) a.lse[static_cast<size_t>(t0 + r) * a.heads + h] = m[half] + logf(l[half]);
+      }
+    }
+    const float inv[2] = {l[0] > 0.f ? 1.0f / l[0] : 0.f, l[1] > 0.f ? 1.0f / l[1] : 0.f};
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[n][e] *= inv[e >> 1];
+    // O = P V, P at the fixed scale 2^14
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      if (ks < NW) {
+        uint32_t ah[4], al[4];
+        c_to_a(s[2 * ks], s[2 * ks + 1], 16384.f, ah, al);
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          uint32_t bh[4], bl[4];
+          ldsm4t(bh, bk_addr(Vh, 16 * ks, 16 * p, lane));
+          ldsm4t(bl, bk_addr(Vl, 16 * ks, 16 * p, lane));
+          mma3(o[2 * p], ah, al, bh[0], bh[1], bl[0], bl[1]);
+          mma3(o[2 * p + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+        }
+      }
+    }
+    const float fo = pow2f(-(14 + sm.scale[2]));
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[n][e] *= fo;
+    if (kSplit) strip_rowmax(sm.rmax[0], o, q0, S, lane);
+    if (a.out) strip_store(o, q0, S, t0, lane, a.out, a.d, h * kHd, nullptr, nullptr, 0, false);
+  }
+  if (kSplit) {
+    cluster_barrier();
+    if (act)
+      strip_store(o, q0, S, t0, lane, nullptr, 0, h * kHd, &a.out_split, sm.rmax[0], (h * kHd) / 128,
+                  cta_rank_in_cluster() == 0);
+    cluster_barrier();  // peers may still read this CTA's row maxima
+  }
+}
+
+// ---- backward --------------------------------------------------------------------
+// Scores and dP of a 16-row strip r0.. against all rows of the other block:
+// s = A1 B1^T, dp = A2 B2^T (A from [rows][32] blocks, B likewise).
+__device__ __forceinline__ void strip_scores(float (&s)[8][4], float (&dp)[8][4], uint32_t a1h, uint32_t a1l,
+                                             uint32_t b1h, uint32_t b1l, uint32_t a2h, uint32_t a2l, uint32_t b2h,
+                                             uint32_t b2l, int r0, int NK8, int lane) {
+#pragma unroll
+  for (int n = 0; n < 8; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s[n][e] = dp[n][e] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < 2; ++ks) {
+    uint32_t ah[4], al[4], ch[4], cl[4];
+    ldsm4(ah, a_addr(a1h, r0, 16 * ks, lane));
+    ldsm4(al, a_addr(a1l, r0, 16 * ks, lane));
+    ldsm4(ch, a_addr(a2h, r0, 16 * ks, lane));
+    ldsm4(cl, a_addr(a2l, r0, 16 * ks, lane));
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      if (2 * p < NK8) {
+        uint32_t bh[4], bl[4];
+        ldsm4(bh, bn_addr(b1h, 16 * p, 16 * ks, lane));
+        ldsm4(bl, bn_addr(b1l, 16 * p, 16 * ks, lane));
+        mma3(s[2 * p], ah, al, bh[0], bh[1], bl[0], bl[1]);
+        mma3(s[2 * p + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+        ldsm4(bh, bn_addr(b2h, 16 * p, 16 * ks, lane));
+        ldsm4(bl, bn_addr(b2l, 16 * p, 16 * ks, lane));
+        mma3(dp[2 * p], ch, cl, bh[0], bh[1], bl[0], bl[1]);
+        mma3(dp[2 * p + 1], ch, cl, bh[2], bh[3], bl[2], bl[3]);
+      }
+    }
+  }
+}
+
+// acc (16 x 32) += A (16 x SP, the c-layout tiles x, scale f) times the
+// [SP][32] block B (via ldmatrix.trans).
+__device__ __forceinline__ void strip_times_block(float (&acc)[4][4], const float (&x)[8][4], float f, uint32_t bh_,
+                                                  uint32_t bl_, int NW, int lane) {
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    if (ks < NW) {
+      uint32_t ah[4], al[4];
+      c_to_a(x[2 * ks], x[2 * ks + 1], f, ah, al);
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        uint32_t bh[4], bl[4];
+        ldsm4t(bh, bk_addr(bh_, 16 * ks, 16 * p, lane));
+        ldsm4t(bl, bk_addr(bl_, 16 * ks, 16 * p, lane));
+        mma3(acc[2 * p], ah, al, bh[0], bh[1], bl[0], bl[1]);
+        mma3(acc[2 * p + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+      }
+    }
+  }
+}
+
+template <bool kSplit>
+__global__ void __launch_bounds__(kThreads) k_attn_bwd_mma(AttnArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
+  const int atom = blockIdx.x, h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+  const int e0 = a.offset[atom], S = a.offset[atom + 1] - e0 + 1, t0 = e0 + atom;
+  const int NW = (S + 15) >> 4, NK8 = 2 * NW;
+  const int d = a.d;
+  load_blocks(sm, a, t0, S, h, true);
+  for (int k = threadIdx.x; k < kMaxTok; k += kThreads) {
+    sm.mask[k] = k < S ? (k == 0 ? 0.f : a.key_mask[e0 + k - 1]) : 0.f;
+    sm.lse[k] = k < S ? a.lse[static_cast<size_t>(t0 + k) * a.heads + h] : 0.f;
+    if (kSplit) sm.rmax[0][k] = sm.rmax[1][k] = sm.rmax[2][k] = 0;
+  }
+  __syncthreads();
+  const uint32_t Qh = smem_addr(sm.mat[0]), Ql = smem_addr(sm.mat[4]), Kh = smem_addr(sm.mat[1]),
+                 Kl = smem_addr(sm.mat[5]), Vh = smem_addr(sm.mat[2]), Vl = smem_addr(sm.mat[6]),
+                 Gh = smem_addr(sm.mat[3]), Gl = smem_addr(sm.mat[7]);
+  const float rs = 1.0f / sqrtf(static_cast<float>(kHd));
+  const float fs = pow2f(-(sm.scale[0] + sm.scale[1])) * rs;
+  const float fdp = pow2f(-(sm.scale[3] + sm.scale[2]));
+  const bool act = warp < NW;
+  const int r0 = 16 * warp;
+  float dq[4][4], dk[4][4], dv[4][4];
+#pragma unroll
+  for (int n = 0; n < 4; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) dq[n][e] = dk[n][e] = dv[n][e] = 0.f;
+
+  // ---- pass 1: warp = query rows r0..r0+15 ----
+  if (act) {
+    float s[8][4], dp[8][4];
+    strip_scores(s, dp, Qh, Ql, Kh, Kl, Gh, Gl, Vh, Vl, r0, NK8, lane);
+    float Dp[2] = {0.f, 0.f};
+    const float lq[2] = {sm.lse[r0 + g], sm.lse[r0 + g + 8]};
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = r0 + g + 8 * (e >> 1), c = 8 * n + 2 * tig + (e & 1);
+        const bool v = n < NK8 && r < S && c < S;
+        s[n][e] = v ? expf(fmaf(s[n][e], fs, sm.mask[c]) - lq[e >> 1]) : 0.f;
+        dp[n][e] = v ? dp[n][e] * fdp : 0.f;
+        Dp[e >> 1] = fmaf(s[n][e], dp[n][e], Dp[e >> 1]);
+      }
+    Dp[0] = quad_sum(Dp[0]);
+    Dp[1] = quad_sum(Dp[1]);
+    if (tig == 0) {
+      sm.D[r0 + g] = Dp[0];
+      sm.D[r0 + g + 8] = Dp[1];
+    }
+    float mx = 0.f;
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        dp[n][e] = s[n][e] * (dp[n][e] - Dp[e >> 1]);  // dS
+        mx = fmaxf(mx, fabsf(dp[n][e]));
+      }
+    const int sd = split_scale_exponent(warp_absmax(mx));
+    strip_times_block(dq, dp, pow2f(sd), Kh, Kl, NW, lane);
+    const float fq = pow2f(-(sd + sm.scale[1])) * rs;
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) dq[n][e] *= fq;
+  }
+  __syncthreads();  // D of every query row
+
+  // ---- pass 2: warp = key rows r0..r0+15 (transposed) ----
+  if (act) {
+    float st[8][4], dpt[8][4];
+    strip_scores(st, dpt, Kh, Kl, Qh, Ql, Vh, Vl, Gh, Gl, r0, NK8, lane);
+    const float mk[2] = {sm.mask[r0 + g], sm.mask[r0 + g + 8]};
+    float mx = 0.f;
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = r0 + g + 8 * (e >> 1), c = 8 * n + 2 * tig + (e & 1);  // key r, query c
+        const bool v = n < NK8 && r < S && c < S;
+        const float p = v ? expf(fmaf(st[n][e], fs, mk[e >> 1]) - sm.lse[c]) : 0.f;
+        dpt[n][e] = v ? p * (dpt[n][e] * fdp - sm.D[c]) : 0.f;  // dS^T
+        st[n][e] = p;                                           // P^T
+        mx = fmaxf(mx, fabsf(dpt[n][e]));
+      }
+    strip_times_block(dv, st, 16384.f, Gh, Gl, NW, lane);
+    const int sd = split_scale_exponent(warp_absmax(mx));
+    strip_times_block(dk, dpt, pow2f(sd), Qh, Ql, NW, lane);
+    const float fv = pow2f(-(14 + sm.scale[3])), fk = pow2f(-(sd + sm.scale[0])) * rs;
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        dv[n][e] *= fv;
+        dk[n][e] *= fk;
+      }
+  }
+
+  const size_t ld = 3 * static_cast<size_t>(d);
+  if (act && a.d_qkv) {
+    strip_store(dq, r0, S, t0, lane, a.d_qkv, ld, h * kHd, nullptr, nullptr, 0, false);
+    strip_store(dk, r0, S, t0, lane, a.d_qkv, ld, d + h * kHd, nullptr, nullptr, 0, false);
+    strip_store(dv, r0, S, t0, lane, a.d_qkv, ld, 2 * d + h * kHd, nullptr, nullptr, 0, false);
+  }
+  if (kSplit) {
+    if (act) {
+      strip_rowmax(sm.rmax[0], dq, r0, S, lane);
+      strip_rowmax(sm.rmax[1], dk, r0, S, lane);
+      strip_rowmax(sm.rmax[2], dv, r0, S, lane);
+    }
+    cluster_barrier();
+    if (act) {
+      const int nb = d / 128, blk = (h * kHd) / 128;
+      const bool first = cta_rank_in_cluster() == 0;
+      strip_store(dq, r0, S, t0, lane, nullptr, 0, h * kHd, &a.dqkv_split, sm.rmax[0], blk, first);
+      strip_store(dk, r0, S, t0, lane, nullptr, 0, d + h * kHd, &a.dqkv_split, sm.rmax[1], nb + blk, first);
+      strip_store(dv, r0, S, t0, lane, nullptr, 0, 2 * d + h * kHd, &a.dqkv_split, sm.rmax[2], 2 * nb + blk, first);
+    }
+    cluster_barrier();  // peers may still read this CTA's row maxima
+  }
+}
+
+template <bool kSplit>
+void launch_mma(const AttnArgs &a, bool bwd, cudaStream_t s) {
+  const size_t smem = sizeof(Smem);
+  void (*fn)(AttnArgs) = bwd ? k_attn_bwd_mma<kSplit> : k_attn_fwd_mma<kSplit>;
+  CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.n_atoms, a.heads);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  if (kSplit) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 128 / kHd;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  CUDA_CHECK(cudaLaunchKernelEx(&cfg, fn, a));
+  CUDA_LAUNCH_CHECK();
+}
+
+}  // namespace
+
+bool attention_mma_supported(const AttnArgs &a, bool bwd) {
+  if (a.heads <= 0 || a.d != a.heads * kHd) return false;
+  if (a.max_tokens < 1 || a.max_tokens > kMaxTok) return false;
+  const bool split = bwd ? a.dqkv_split.hi != nullptr : a.out_split.hi != nullptr;
+  if (split && (a.heads % (128 / kHd) || a.d % 128)) return false;
+  return bwd ? (a.d_out && a.lse) : a.lse != nullptr;
+}
+
+void attention_mma(const AttnArgs &a, bool bwd, cudaStream_t s) {
+  if (a.n_atoms <= 0) return;
+  if (!attention_mma_supported(a, bwd)) throw Error(kErrInternal, "attention_mma: unsupported shape");
+  const bool split = bwd ? a.dqkv_split.hi != nullptr : a.out_split.hi != nullptr;
+  if (split) launch_mma<true>(a, bwd, s);
+  else launch_mma<false>(a, bwd, s);
+}
+
+}  // namespace pet

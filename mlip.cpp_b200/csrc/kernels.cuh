@@ -78,6 +78,11 @@ void attention_fwd(const AttnArgs &a, cudaStream_t stream);
 bool attention_tc_supported(const AttnArgs &a);
 void attention_fwd_tc(const AttnArgs &a, int *err, cudaStream_t stream);
 void attention_bwd(const AttnArgs &a, cudaStream_t stream);
+// Tensor-core forward / backward on register-resident split-fp16 products
+// (attention_mma.cu): head size 32, at most 64 tokens per atom; split
+// outputs need heads in groups of 4 (one cluster per 128-column block).
+bool attention_mma_supported(const AttnArgs &a, bool bwd);
+void attention_mma(const AttnArgs &a, bool bwd, cudaStream_t stream);
 // Largest per-atom token count the attention kernels accept for head size hd.
 int attention_max_tokens(int hd);
 // Largest tokens per atom for which the attention kernels can write

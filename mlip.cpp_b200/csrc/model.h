@@ -134,6 +134,9 @@ class PETModel {
   // tensor-core attention forward (MLIPCPP_B200_ATTN=tc): correct, but slower
   // than the SIMT kernel at this size (see attention_tc.cu)
   bool use_attn_tc_ = false;
+  // thread-per-row SIMT attention (MLIPCPP_B200_ATTN=rows) instead of the
+  // tensor-core kernels of attention_mma.cu where those apply
+  bool use_attn_rows_ = false;
   // MLIPCPP_PRECISION_F16: dense layers with the hi x hi product only
   bool reduced_ = false;
   // non-conservative heads in the file / run in the current prediction

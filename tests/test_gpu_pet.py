@@ -186,6 +186,36 @@ def test_gpu_tensor_core_attention_matches_simt(model_file, monkeypatch):
     assert_close(res, ref.energy, ref.forces, ref.stress, s.n_atoms)
 
 
+@pytest.mark.parametrize("hname,make,env", [
+    ("pet-oam-l", lambda: [wl.fcc_alloy(6, seed=14)], {}),                       # split outputs, clusters of 4
+    ("pet-mad-s", lambda: [wl.water_box(192, seed=14)], {}),                     # split outputs
+    ("pet-mad-s", lambda: [wl.si_diamond(2, seed=14)], {"MLIPCPP_B200_CHAIN": "0"}),  # fp32 outputs
+    ("pet-mad-s", lambda: wl.molecules(4, seed=14, n_min=2, n_max=60), {}),      # ragged, up to 60 tokens
+    ("pet-mad-s", lambda: [wl.water_box(192, seed=15)], {"_cutoff": 6.5}),       # > 64 tokens: SIMT kernels
+], ids=["oaml_fcc216", "mads_water192", "mads_si64_fp32", "mads_molecules", "mads_wide"])
+def test_gpu_mma_attention_matches_simt(hname, make, env, model_file, monkeypatch):
+    """The tensor-core attention (register-resident split-fp16 mma.sync,
+    forward and backward) and the SIMT thread-per-row kernels agree within
+    the fp32 parity tolerances: energy, forces and stress, with split and
+    fp32 outputs, ragged atoms and the fallback beyond 64 tokens."""
+    env = dict(env)
+    over = {"cutoff": env.pop("_cutoff")} if "_cutoff" in env else {}
+    path = model_file(hname, 14, **over)
+    systems = make()
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    monkeypatch.setenv("MLIPCPP_B200_ATTN", "rows")
+    ref = mb.Predictor(path).predict_batch(systems, compute_stress=True)
+    monkeypatch.delenv("MLIPCPP_B200_ATTN")
+    pred = mb.Predictor(path)
+    res = pred.predict_batch(systems, compute_stress=True)
+    for s, r, q in zip(systems, res, ref):
+        assert_close(r, q.energy, q.forces, q.stress if q.has_stress() else None, s.n_atoms)
+    e_only = pred.predict_batch(systems, compute_forces=False)
+    for s, r, q in zip(systems, e_only, ref):
+        assert abs(r.energy - q.energy) / s.n_atoms <= TOL_E
+
+
 # Stated tolerances of the reduced-precision mode (MLIPCPP_PRECISION_F16: dense
 # layers multiply fp16 hi parts only, 11 significant bits per operand) against
 # the fp32 path (about 4x the largest differences measured on these cases:
