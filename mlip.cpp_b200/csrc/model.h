@@ -134,9 +134,11 @@ class PETModel {
   // tensor-core attention forward (MLIPCPP_B200_ATTN=tc): correct, but slower
   // than the SIMT kernel at this size (see attention_tc.cu)
   bool use_attn_tc_ = false;
-  // thread-per-row SIMT attention (MLIPCPP_B200_ATTN=rows) instead of the
-  // tensor-core kernels of attention_mma.cu where those apply
-  bool use_attn_rows_ = false;
+  // attention kernels: the backward runs on the tensor-core kernel of
+  // attention_mma.cu where it applies, the forward on the SIMT kernel (the
+  // faster of the two at 16 heads of 32 and ~40 tokens);
+  // MLIPCPP_B200_ATTN=rows: SIMT for both, =mma: tensor cores for both
+  bool use_attn_rows_ = false, use_attn_mma_fwd_ = false;
   // MLIPCPP_PRECISION_F16: dense layers with the hi x hi product only
   bool reduced_ = false;
   // non-conservative heads in the file / run in the current prediction

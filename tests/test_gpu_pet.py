@@ -206,7 +206,7 @@ def test_gpu_mma_attention_matches_simt(hname, make, env, model_file, monkeypatc
         monkeypatch.setenv(k, v)
     monkeypatch.setenv("MLIPCPP_B200_ATTN", "rows")
     ref = mb.Predictor(path).predict_batch(systems, compute_stress=True)
-    monkeypatch.delenv("MLIPCPP_B200_ATTN")
+    monkeypatch.setenv("MLIPCPP_B200_ATTN", "mma")  # tensor-core forward too
     pred = mb.Predictor(path)
     res = pred.predict_batch(systems, compute_stress=True)
     for s, r, q in zip(systems, res, ref):
