@@ -535,10 +535,224 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma(AttnArgs a) {
   }
 }
 
+// ---- backward for atoms of at most 48 tokens ---------------------------------------
+// Pass 1 (warp = query rows) also leaves P and dS in shared memory in split
+// form (P at 2^14, dS at one scale for the whole item, from a block-wide
+// maximum), and pass 2 (warp = key rows) reads them transposed with
+// ldmatrix.trans as the A operands of dV = P^T dO and dK = dS^T Q instead of
+// recomputing the scores.  48-row blocks keep the footprint at 53 KB.
+constexpr int kMT = 48;
+constexpr int kPitchP = 56;  // halves per P / dS row (112 bytes: conflict-free ldmatrix)
+constexpr int kMatP = kMT * kPitchP;
+
+struct Smem48 {
+  uint16_t mat[8][kMT * kPitch];  // Q, K, V, dO: hi then lo
+  uint16_t pd[4][kMatP];          // P hi, P lo, dS hi, dS lo ([query][key])
+  float lse[kMT], mask[kMT];
+  int scale[4];
+  int dsmax;                      // bits of the item's max |dS|
+  int rmax[3][kMT];
+};
+
+// A operand (16 keys x 16 queries) of a transposed product from a stored
+// [query][key] block: matrices (q0, k0), (q0, k0 + 8), (q0 + 8, k0),
+// (q0 + 8, k0 + 8) loaded with .trans -> a0..a3.
+__device__ __forceinline__ uint32_t at_addr(uint32_t base, int k0, int q0, int lane) {
+  const int j = lane >> 3;
+  return base + 2u * static_cast<uint32_t>((q0 + (lane & 7) + 8 * (j >> 1)) * kPitchP + k0 + 8 * (j & 1));
+}
+
+// acc (16 x 32) += A^T (stored [query][key] blocks, rows k0.. as A rows)
+// times the [query][32] block B, over NW 16-query steps.
+__device__ __forceinline__ void stored_t_times_block(float (&acc)[4][4], uint32_t ah_, uint32_t al_, int k0,
+                                                     uint32_t bh_, uint32_t bl_, int NW, int lane) {
+#pragma unroll
+  for (int ks = 0; ks < 3; ++ks) {
+    if (ks < NW) {
+      uint32_t ah[4], al[4];
+      ldsm4t(ah, at_addr(ah_, k0, 16 * ks, lane));
+      ldsm4t(al, at_addr(al_, k0, 16 * ks, lane));
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        uint32_t bh[4], bl[4];
+        ldsm4t(bh, bk_addr(bh_, 16 * ks, 16 * p, lane));
+        ldsm4t(bl, bk_addr(bl_, 16 * ks, 16 * p, lane));
+        mma3(acc[2 * p], ah, al, bh[0], bh[1], bl[0], bl[1]);
+        mma3(acc[2 * p + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+      }
+    }
+  }
+}
+
+// c-layout tiles of a 16-row strip into a stored [row][col] split block
+__device__ __forceinline__ void strip_to_smem(uint16_t *hi, uint16_t *lo, const float (&x)[8][4], int NK8, int r0,
+                                              float f, int lane) {
+  const int g = lane >> 2, tig = lane & 3;
+#pragma unroll
+  for (int n = 0; n < 6; ++n) {
+    if (n < NK8) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t hh, ll;
+        split2(x[n][2 * half], x[n][2 * half + 1], f, hh, ll);
+        const int off = (r0 + g + 8 * half) * kPitchP + 8 * n + 2 * tig;
+        *reinterpret_cast<uint32_t *>(hi + off) = hh;
+        *reinterpret_cast<uint32_t *>(lo + off) = ll;
+      }
+    }
+  }
+}
+
+template <bool kSplit>
+__global__ void __launch_bounds__(kThreads) k_attn_bwd_mma48(AttnArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  Smem48 &sm = *reinterpret_cast<Smem48 *>(smem_raw);
+  const int atom = blockIdx.x, h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+  const int e0 = a.offset[atom], S = a.offset[atom + 1] - e0 + 1, t0 = e0 + atom;
+  const int NW = (S + 15) >> 4, NK8 = 2 * NW;
+  const int d = a.d;
+  {  // Q, K, V, dO into split blocks (warp w: block w, 6 row-chunks per lane)
+    float v[6][8];
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+      const int task = lane + 32 * i, r = task >> 2, c = (task & 3) * 8;
+      if (r < S) {
+        const float *src = warp < 3 ? a.qkv + static_cast<size_t>(t0 + r) * 3 * d + warp * d + h * kHd + c
+                                    : a.d_out + static_cast<size_t>(t0 + r) * d + h * kHd + c;
+        const float4 x0 = *reinterpret_cast<const float4 *>(src), x1 = *reinterpret_cast<const float4 *>(src + 4);
+        v[i][0] = x0.x; v[i][1] = x0.y; v[i][2] = x0.z; v[i][3] = x0.w;
+        v[i][4] = x1.x; v[i][5] = x1.y; v[i][6] = x1.z; v[i][7] = x1.w;
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[i][k] = 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx = fmaxf(mx, fabsf(v[i][k]));
+    }
+    const int sc = split_scale_exponent(warp_absmax(mx));
+    const float f = pow2f(sc);
+    if (lane == 0) sm.scale[warp] = sc;
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+      const int task = lane + 32 * i, r = task >> 2, c = (task & 3) * 8;
+      uint32_t hh[4], ll[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) split2(v[i][2 * k], v[i][2 * k + 1], f, hh[k], ll[k]);
+      *reinterpret_cast<uint4 *>(&sm.mat[warp][r * kPitch + c]) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
+      *reinterpret_cast<uint4 *>(&sm.mat[4 + warp][r * kPitch + c]) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+    }
+  }
+  for (int k = threadIdx.x; k < kMT; k += kThreads) {
+    sm.mask[k] = k < S ? (k == 0 ? 0.f : a.key_mask[e0 + k - 1]) : 0.f;
+    sm.lse[k] = k < S ? a.lse[static_cast<size_t>(t0 + k) * a.heads + h] : 0.f;
+    if (kSplit) sm.rmax[0][k] = sm.rmax[1][k] = sm.rmax[2][k] = 0;
+  }
+  if (threadIdx.x == 0) sm.dsmax = 0;
+  __syncthreads();
+  const uint32_t Qh = smem_addr(sm.mat[0]), Ql = smem_addr(sm.mat[4]), Kh = smem_addr(sm.mat[1]),
+                 Kl = smem_addr(sm.mat[5]), Vh = smem_addr(sm.mat[2]), Vl = smem_addr(sm.mat[6]),
+                 Gh = smem_addr(sm.mat[3]), Gl = smem_addr(sm.mat[7]);
+  const uint32_t Ph = smem_addr(sm.pd[0]), Pl = smem_addr(sm.pd[1]), Dh = smem_addr(sm.pd[2]),
+                 Dl = smem_addr(sm.pd[3]);
+  const float rs = 1.0f / sqrtf(static_cast<float>(kHd));
+  const float fs = pow2f(-(sm.scale[0] + sm.scale[1])) * rs;
+  const float fdp = pow2f(-(sm.scale[3] + sm.scale[2]));
+  const bool act = warp < NW;
+  const int r0 = 16 * warp;
+  float dq[4][4], dk[4][4], dv[4][4];
+#pragma unroll
+  for (int n = 0; n < 4; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) dq[n][e] = dk[n][e] = dv[n][e] = 0.f;
+
+  // ---- pass 1: warp = query rows; P and dS to shared memory, dQ ----
+  float s[8][4], dp[8][4];
+  if (act) {
+    strip_scores(s, dp, Qh, Ql, Kh, Kl, Gh, Gl, Vh, Vl, r0, NK8, lane);
+    float Dp[2] = {0.f, 0.f};
+    const float lq[2] = {sm.lse[r0 + g], sm.lse[r0 + g + 8]};
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = r0 + g + 8 * (e >> 1), c = 8 * n + 2 * tig + (e & 1);
+        const bool v = n < NK8 && r < S && c < S;
+        s[n][e] = v ? expf(fmaf(s[n][e], fs, sm.mask[c]) - lq[e >> 1]) : 0.f;
+        dp[n][e] = v ? dp[n][e] * fdp : 0.f;
+        Dp[e >> 1] = fmaf(s[n][e], dp[n][e], Dp[e >> 1]);
+      }
+    Dp[0] = quad_sum(Dp[0]);
+    Dp[1] = quad_sum(Dp[1]);
+    float mx = 0.f;
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        dp[n][e] = s[n][e] * (dp[n][e] - Dp[e >> 1]);  // dS
+        mx = fmaxf(mx, fabsf(dp[n][e]));
+      }
+    mx = warp_absmax(mx);
+    if (lane == 0) atomicMax(&sm.dsmax, __float_as_int(mx));
+    strip_to_smem(sm.pd[0], sm.pd[1], s, NK8, r0, 16384.f, lane);
+  }
+  __syncthreads();  // the item's max |dS|
+  const int sd = split_scale_exponent(__int_as_float(sm.dsmax));
+  if (act) {
+    strip_to_smem(sm.pd[2], sm.pd[3], dp, NK8, r0, pow2f(sd), lane);
+    strip_times_block(dq, dp, pow2f(sd), Kh, Kl, NW, lane);
+    const float fq = pow2f(-(sd + sm.scale[1])) * rs;
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) dq[n][e] *= fq;
+  }
+  __syncthreads();  // P and dS of every query row
+
+  // ---- pass 2: warp = key rows r0..r0+15: dV = P^T dO, dK = dS^T Q ----
+  if (act) {
+    stored_t_times_block(dv, Ph, Pl, r0, Gh, Gl, NW, lane);
+    stored_t_times_block(dk, Dh, Dl, r0, Qh, Ql, NW, lane);
+    const float fv = pow2f(-(14 + sm.scale[3])), fk = pow2f(-(sd + sm.scale[0])) * rs;
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        dv[n][e] *= fv;
+        dk[n][e] *= fk;
+      }
+  }
+
+  const size_t ld = 3 * static_cast<size_t>(d);
+  if (act && a.d_qkv) {
+    strip_store(dq, r0, S, t0, lane, a.d_qkv, ld, h * kHd, nullptr, nullptr, 0, false);
+    strip_store(dk, r0, S, t0, lane, a.d_qkv, ld, d + h * kHd, nullptr, nullptr, 0, false);
+    strip_store(dv, r0, S, t0, lane, a.d_qkv, ld, 2 * d + h * kHd, nullptr, nullptr, 0, false);
+  }
+  if (kSplit) {
+    if (act) {
+      strip_rowmax(sm.rmax[0], dq, r0, S, lane);
+      strip_rowmax(sm.rmax[1], dk, r0, S, lane);
+      strip_rowmax(sm.rmax[2], dv, r0, S, lane);
+    }
+    cluster_barrier();
+    if (act) {
+      const int nb = d / 128, blk = (h * kHd) / 128;
+      const bool first = cta_rank_in_cluster() == 0;
+      strip_store(dq, r0, S, t0, lane, nullptr, 0, h * kHd, &a.dqkv_split, sm.rmax[0], blk, first);
+      strip_store(dk, r0, S, t0, lane, nullptr, 0, d + h * kHd, &a.dqkv_split, sm.rmax[1], nb + blk, first);
+      strip_store(dv, r0, S, t0, lane, nullptr, 0, 2 * d + h * kHd, &a.dqkv_split, sm.rmax[2], 2 * nb + blk, first);
+    }
+    cluster_barrier();  // peers may still read this CTA's row maxima
+  }
+}
+
 template <bool kSplit>
 void launch_mma(const AttnArgs &a, bool bwd, cudaStream_t s) {
-  const size_t smem = sizeof(Smem);
-  void (*fn)(AttnArgs) = bwd ? k_attn_bwd_mma<kSplit> : k_attn_fwd_mma<kSplit>;
+  const bool small = bwd && a.max_tokens <= kMT;
+  const size_t smem = small ? sizeof(Smem48) : sizeof(Smem);
+  void (*fn)(AttnArgs) = small ? k_attn_bwd_mma48<kSplit> : bwd ? k_attn_bwd_mma<kSplit> : k_attn_fwd_mma<kSplit>;
   CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.n_atoms, a.heads);
