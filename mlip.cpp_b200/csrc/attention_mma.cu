@@ -29,8 +29,9 @@
 //     S^T = K Q^T, P^T, dP^T = V dO^T, dS^T, dV = P^T dO, dK = s dS^T Q.
 // P enters a product at the fixed scale 2^14; dS with one scale per warp
 // strip.  Split-fp16 outputs need one scale per (row, 128-column block),
-// i.e. per 4 heads: those 4 CTAs form a cluster and exchange their row
-// maxima through distributed shared memory.
+// i.e. per 4 heads: those 4 CTAs form a cluster; each pushes its row
+// maxima into every CTA's shared memory (remote atomic max) between the two
+// halves of one cluster barrier, so no CTA reads another's memory.
 #include <cfloat>
 
 #include "common.cuh"
@@ -129,20 +130,18 @@ __device__ __forceinline__ uint32_t cta_rank_in_cluster() {
 __device__ __forceinline__ void cluster_barrier() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ int ld_peer(const int *local, uint32_t rank) {
+// The two halves of a cluster barrier: arrive once this CTA's row maxima are
+// cleared, wait just before writing into the peers' (they have long arrived).
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// max into the same shared variable of cluster CTA `rank`
+__device__ __forceinline__ void red_max_peer(int *local, uint32_t rank, int v) {
   const uint32_t a = smem_addr(local);
   uint32_t r;
-  int v;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
-  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(r) : "memory");
-  return v;
-}
-// Largest of a row's maxima over the 4 CTAs (heads) of the cluster.
-__device__ __forceinline__ float cluster_row_max(const int *local) {
-  int m = 0;
-#pragma unroll
-  for (int r = 0; r < 4; ++r) m = max(m, ld_peer(local, static_cast<uint32_t>(r)));
-  return __int_as_float(m);
+  asm volatile("red.shared::cluster.max.u32 [%0], %1;" ::"r"(r), "r"(v) : "memory");
 }
 
 // ---- shared memory -------------------------------------------------------------
@@ -192,7 +191,8 @@ __device__ __forceinline__ void load_blocks(Smem &sm, const AttnArgs &a, int t0,
 }
 
 // Row maxima of a 16-row strip's outputs (4 n-tiles of the c-layout) into
-// sm.rmax[m] (quad-reduced, one atomic per row).
+// rm of every CTA of the cluster (quad-reduced, one remote max per row and
+// CTA), so that after the next cluster barrier rm holds the block maxima.
 __device__ __forceinline__ void strip_rowmax(int *rm, const float (&o)[4][4], int r0, int S, int lane) {
   float m0 = 0.f, m1 = 0.f;
 #pragma unroll
@@ -204,8 +204,11 @@ __device__ __forceinline__ void strip_rowmax(int *rm, const float (&o)[4][4], in
   m1 = quad_max(m1);
   const int g = lane >> 2;
   if ((lane & 3) == 0) {
-    if (r0 + g < S) atomicMax(rm + r0 + g, __float_as_int(m0));
-    if (r0 + g + 8 < S) atomicMax(rm + r0 + g + 8, __float_as_int(m1));
+#pragma unroll
+    for (uint32_t c = 0; c < 4; ++c) {
+      if (r0 + g < S) red_max_peer(rm + r0 + g, c, __float_as_int(m0));
+      if (r0 + g + 8 < S) red_max_peer(rm + r0 + g + 8, c, __float_as_int(m1));
+    }
   }
 }
 
@@ -226,7 +229,7 @@ __device__ __forceinline__ void strip_store(const float (&v)[4][4], int r0, int 
       for (int n = 0; n < 4; ++n) *reinterpret_cast<float2 *>(p + 8 * n) = make_float2(v[n][2 * half], v[n][2 * half + 1]);
     }
     if (o) {
-      const int s = split_scale_exponent(cluster_row_max(rm + r));
+      const int s = split_scale_exponent(__int_as_float(rm[r]));
       const float f = pow2f(s);
       const size_t off = static_cast<size_t>(t0 + r) * o->cols + col0 + 2 * tig;
 #pragma unroll
@@ -256,6 +259,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_fwd_mma(AttnArgs a) {
     if (kSplit) sm.rmax[0][k] = 0;
   }
   __syncthreads();
+  if (kSplit) cluster_arrive();
   const uint32_t Qh = smem_addr(sm.mat[0]), Ql = smem_addr(sm.mat[4]), Kh = smem_addr(sm.mat[1]),
                  Kl = smem_addr(sm.mat[5]), Vh = smem_addr(sm.mat[2]), Vl = smem_addr(sm.mat[6]);
   float o[4][4];
@@ -344,15 +348,15 @@ __global__ void __launch_bounds__(kThreads) k_attn_fwd_mma(AttnArgs a) {
     for (int n = 0; n < 4; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) o[n][e] *= fo;
-    if (kSplit) strip_rowmax(sm.rmax[0], o, q0, S, lane);
     if (a.out) strip_store(o, q0, S, t0, lane, a.out, a.d, h * kHd, nullptr, nullptr, 0, false);
   }
   if (kSplit) {
-    cluster_barrier();
+    cluster_wait();
+    if (act) strip_rowmax(sm.rmax[0], o, q0, S, lane);
+    cluster_barrier();  // every CTA's maxima have reached every CTA
     if (act)
       strip_store(o, q0, S, t0, lane, nullptr, 0, h * kHd, &a.out_split, sm.rmax[0], (h * kHd) / 128,
                   cta_rank_in_cluster() == 0);
-    cluster_barrier();  // peers may still read this CTA's row maxima
   }
 }
 
@@ -427,6 +431,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma(AttnArgs a) {
     if (kSplit) sm.rmax[0][k] = sm.rmax[1][k] = sm.rmax[2][k] = 0;
   }
   __syncthreads();
+  if (kSplit) cluster_arrive();
   const uint32_t Qh = smem_addr(sm.mat[0]), Ql = smem_addr(sm.mat[4]), Kh = smem_addr(sm.mat[1]),
                  Kl = smem_addr(sm.mat[5]), Vh = smem_addr(sm.mat[2]), Vl = smem_addr(sm.mat[6]),
                  Gh = smem_addr(sm.mat[3]), Gl = smem_addr(sm.mat[7]);
@@ -518,12 +523,13 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma(AttnArgs a) {
     strip_store(dv, r0, S, t0, lane, a.d_qkv, ld, 2 * d + h * kHd, nullptr, nullptr, 0, false);
   }
   if (kSplit) {
+    cluster_wait();
     if (act) {
       strip_rowmax(sm.rmax[0], dq, r0, S, lane);
       strip_rowmax(sm.rmax[1], dk, r0, S, lane);
       strip_rowmax(sm.rmax[2], dv, r0, S, lane);
     }
-    cluster_barrier();
+    cluster_barrier();  // every CTA's maxima have reached every CTA
     if (act) {
       const int nb = d / 128, blk = (h * kHd) / 128;
       const bool first = cta_rank_in_cluster() == 0;
@@ -531,7 +537,6 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma(AttnArgs a) {
       strip_store(dk, r0, S, t0, lane, nullptr, 0, d + h * kHd, &a.dqkv_split, sm.rmax[1], nb + blk, first);
       strip_store(dv, r0, S, t0, lane, nullptr, 0, 2 * d + h * kHd, &a.dqkv_split, sm.rmax[2], 2 * nb + blk, first);
     }
-    cluster_barrier();  // peers may still read this CTA's row maxima
   }
 }
 
@@ -651,6 +656,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma48(AttnArgs a) {
   }
   if (threadIdx.x == 0) sm.dsmax = 0;
   __syncthreads();
+  if (kSplit) cluster_arrive();
   const uint32_t Qh = smem_addr(sm.mat[0]), Ql = smem_addr(sm.mat[4]), Kh = smem_addr(sm.mat[1]),
                  Kl = smem_addr(sm.mat[5]), Vh = smem_addr(sm.mat[2]), Vl = smem_addr(sm.mat[6]),
                  Gh = smem_addr(sm.mat[3]), Gl = smem_addr(sm.mat[7]);
@@ -731,12 +737,13 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma48(AttnArgs a) {
     strip_store(dv, r0, S, t0, lane, a.d_qkv, ld, 2 * d + h * kHd, nullptr, nullptr, 0, false);
   }
   if (kSplit) {
+    cluster_wait();
     if (act) {
       strip_rowmax(sm.rmax[0], dq, r0, S, lane);
       strip_rowmax(sm.rmax[1], dk, r0, S, lane);
       strip_rowmax(sm.rmax[2], dv, r0, S, lane);
     }
-    cluster_barrier();
+    cluster_barrier();  // every CTA's maxima have reached every CTA
     if (act) {
       const int nb = d / 128, blk = (h * kHd) / 128;
       const bool first = cta_rank_in_cluster() == 0;
@@ -744,7 +751,6 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma48(AttnArgs a) {
       strip_store(dk, r0, S, t0, lane, nullptr, 0, d + h * kHd, &a.dqkv_split, sm.rmax[1], nb + blk, first);
       strip_store(dv, r0, S, t0, lane, nullptr, 0, 2 * d + h * kHd, &a.dqkv_split, sm.rmax[2], 2 * nb + blk, first);
     }
-    cluster_barrier();  // peers may still read this CTA's row maxima
   }
 }
 
