@@ -381,7 +381,7 @@ def main():
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches),
             "roofline": {"bound": "tensor",
-                         "kernel": ("k_gemm_3xf16 + k_row_scale" if f16 else "k_gemm_3xtf32")
+                         "kernel": ("k_gemm_3xf16 + k_split_a" if f16 else "k_gemm_3xtf32")
                                    + " (tcgen05, all dense layers)",
                          "achieved": achieved, "peak": bf16_sus / div, "unit": "TFLOP/s",
                          "frac": achieved / (bf16_sus / div),
@@ -391,9 +391,9 @@ def main():
                          "tensor_pipe_frac_of_bf16": div * achieved / bf16_sus,
                          # DRAM bytes per average GEMM launch: ncu dram__bytes_read.sum +
                          # dram__bytes_write.sum over all 57 GEMM launches of one step of the
-                         # 1,728-atom cell of this alloy (356 MB/launch at 65,202 tokens,
-                         # 5,453 B per token for the 3xFP16 build), scaled by this step's tokens
-                         "traffic": (5453.0 * (shape["atoms"] + shape["edges"])
+                         # 1,728-atom cell of this alloy (358 MB/launch at 65,202 tokens,
+                         # 5,493 B per token for the 3xFP16 build), scaled by this step's tokens
+                         "traffic": (5493.0 * (shape["atoms"] + shape["edges"])
                                      if not domains and f16 else None),
                          "traffic_unit": "bytes per GEMM launch (scaled from the 1,728-atom capture)",
                          "gemm_share_of_step": gemm_ms / (t_dev * 1e3) if t_dev else None},
