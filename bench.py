@@ -206,6 +206,10 @@ def main():
                     help="multi-GPU mode: one cell split into spatial domains, or a replica per rank")
     ap.add_argument("--precision", default="f32", choices=["f32", "f16"],
                     help="f16: MLIPCPP_PRECISION_F16, dense layers with one fp16 product (looser tolerances)")
+    ap.add_argument("--mode", default="forces", choices=["forces", "energy", "nc"],
+                    help="forces: E + gradient forces + stress (headline); energy: the forward pass only; "
+                         "nc: forces and stress from non-conservative heads (use_nc_forces), forward only; "
+                         "energy and nc run one replica per GPU")
     ap.add_argument("--workload", default="fcc", choices=["fcc", "si", "molecules"],
                     help="fcc: the 32k-atom alloy per GPU (headline); si: one 262,144-atom diamond-Si "
                          "cell over N >= 2 GPUs (strong scaling); molecules: 512 molecules sharded")
@@ -217,14 +221,17 @@ def main():
     mb = _package()
     from mlipcpp_b200 import workloads as wl
     h = wl.HYPERS[args.hypers]
+    what = {"forces": "E+F+stress", "energy": "E only (forward pass)",
+            "nc": "E + non-conservative F and stress heads (forward pass)"}[args.mode]
+    metric = METRIC if args.mode == "forces" else METRIC.replace("(E+F+stress)", f"({what})")
     workload = (f"fcc alloy {args.reps}^3 primitive cells ({args.reps ** 3} atoms per GPU, triclinic, a=3.6, "
                 f"20 elements, jitter 0.08), {args.hypers}-shaped random-init weights "
                 f"(d={h.d_pet}, heads={h.num_heads}, ff={h.d_feedforward}, d_head={h.d_head}, "
-                f"rc={h.cutoff}), E+F+stress")
+                f"rc={h.cutoff}{', nc heads' if args.mode == 'nc' else ''}), {what}")
 
     tmpdir = tempfile.mkdtemp(prefix="petbench")
     gguf = os.path.join(tmpdir, "w.gguf")
-    wl.write_pet_gguf(gguf, h, seed=0)
+    wl.write_pet_gguf(gguf, h, seed=0, nc_heads=args.mode == "nc")
 
     if args.impl == "reference":
         if rank != 0:
@@ -261,7 +268,8 @@ def main():
             dist.destroy_process_group()
         return
 
-    domains = world > 1 and args.parallel == "domains"
+    domains = world > 1 and args.parallel == "domains" and args.mode == "forces"
+    grad, nc = args.mode == "forces", args.mode == "nc"
     reps = (args.reps,) * 3
     if domains:
         # N x 32k atoms: double the cell along z, then y, then x
@@ -301,7 +309,8 @@ def main():
     else:
         def step_device():
             return pred.predict_device(d_pos.data_ptr(), s.n_atoms, s.numbers, s.cell, s.pbc,
-                                       compute_forces=True, compute_stress=True, copy_forces=False)
+                                       compute_forces=grad or nc, compute_stress=grad or nc, copy_forces=False,
+                                       use_nc_forces=nc)
 
     for _ in range(max(args.warmup, 3)):
         step_device()
@@ -344,8 +353,9 @@ def main():
         d2h = int(F_host.numel() * 4 + 8 * 7)
     else:
         e2e_ms = []
+        opts = mb.PredictOptions(grad or nc, grad or nc, nc)
         for _ in range(args.steps):
-            r = pred.predict(pos_host.numpy(), s.numbers, s.cell, s.pbc, compute_stress=True)
+            r = pred.predict_with_options(pos_host.numpy(), s.numbers, s.cell, s.pbc, opts)
             e2e_ms.append(pred.last_timings()["total"])
         barrier()
         t_e2e = float(np.sum(e2e_ms)) / 1e3
@@ -365,7 +375,7 @@ def main():
         div = (1.0 if f16_mode else 3.0) if f16 else 6.0
         shape = pred.last_shape()
         line = {
-            "metric": METRIC, "value": value, "unit": "atom-steps/s", "n_gpus": world,
+            "metric": metric, "value": value, "unit": "atom-steps/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": t_dev / args.steps * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f16" if f16_mode else "f32",
@@ -394,14 +404,14 @@ def main():
                          # 1,728-atom cell of this alloy (358 MB/launch at 65,202 tokens,
                          # 5,493 B per token for the 3xFP16 build), scaled by this step's tokens
                          "traffic": (5493.0 * (shape["atoms"] + shape["edges"])
-                                     if not domains and f16 else None),
+                                     if not domains and f16 and grad else None),
                          "traffic_unit": "bytes per GEMM launch (scaled from the 1,728-atom capture)",
                          "gemm_share_of_step": gemm_ms / (t_dev * 1e3) if t_dev else None},
             "kernel_stats": kstats,
             "phase_ms": pred.last_timings(),
             "clocks": clk.summary(),
         }
-        if not args.no_cpu_baseline and world == 1:
+        if not args.no_cpu_baseline and world == 1 and grad:
             sample = wl.fcc_alloy(args.cpu_reps, seed=0)
             v, threads, dt = cpu_reference(sample, gguf, 2, 1)
             line["cpu_baseline"] = {"value": v, "unit": "atom-steps/s", "cores": threads, "kind": "port",
