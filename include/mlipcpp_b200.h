@@ -36,6 +36,22 @@ mlipcpp_error_t mlipcpp_b200_predict_device(mlipcpp_model_t model, int32_t n_ato
                                             const mlipcpp_predict_options_t *options,
                                             bool copy_forces, mlipcpp_result_t *result);
 
+/* No counterpart in the reference (its Python MD loop copies positions and
+ * forces through the host each step, python/mlipcpp/ase.py:123-183).  As
+ * mlipcpp_b200_predict_device, but the forces stay on the device: they are
+ * written to d_forces (device, [3n] float, may be NULL) and the energy
+ * (eV, composition included) to *energy; stress (host [6], Voigt, may be
+ * NULL) and *has_stress (may be NULL) as in the result of
+ * mlipcpp_predict_with_options.  Forces asked for from a model that cannot
+ * give them (use_nc_forces without force heads, compute_forces off) return
+ * MLIPCPP_ERROR_INVALID_PARAMETER when d_forces is set.  For MD drivers that
+ * keep positions, velocities and forces on the GPU. */
+mlipcpp_error_t mlipcpp_b200_predict_device_forces(mlipcpp_model_t model, int32_t n_atoms,
+                                                   const float *d_positions, const int32_t *atomic_numbers,
+                                                   const float *cell, const bool *pbc,
+                                                   const mlipcpp_predict_options_t *options, float *d_forces,
+                                                   double *energy, float stress[6], bool *has_stress);
+
 /* One spatial domain of a large periodic cell (multi-GPU domain
  * decomposition).  d_positions: device pointer to [3 * n_local] double, the
  * owned atoms first, then the ghost atoms within one cutoff of the owned

@@ -96,6 +96,7 @@ def lib() -> ctypes.CDLL:
         "mlipcpp_result_free": (None, [vp]),
         "mlipcpp_predict_batch": (ctypes.c_int, [vp, i32, vp, vp, vp]),
         "mlipcpp_b200_predict_device": (ctypes.c_int, [vp, i32, vp, vp, vp, vp, vp, b, vp]),
+        "mlipcpp_b200_predict_device_forces": (ctypes.c_int, [vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
         "mlipcpp_b200_set_timing": (ctypes.c_int, [vp, b]),
         "mlipcpp_b200_predict_local": (ctypes.c_int, [vp, i32, vp, vp, i32, i32, vp, vp, b, vp, vp, vp]),
         "mlipcpp_b200_last_timings": (ctypes.c_int, [vp, vp]),
@@ -368,6 +369,24 @@ class Predictor:
             ctypes.byref(po), bool(copy_forces), ctypes.byref(h)))
         return _read_result(h, n_atoms if copy_forces else 0) if copy_forces else \
             _read_result_no_forces(h)
+
+    def predict_device_forces(self, d_positions: int, n_atoms: int, atomic_numbers, cell=None, pbc=None,
+                              d_forces: int = 0, compute_stress=False, use_nc_forces=False):
+        """Positions and forces in device memory (`d_positions`, `d_forces`:
+        device pointers to [3n] float32; d_forces may be 0).  Returns
+        (energy, stress [6] or None)."""
+        z = np.ascontiguousarray(atomic_numbers, dtype=np.int32)
+        c = None if cell is None else np.ascontiguousarray(cell, dtype=np.float32).reshape(9)
+        p = None if c is None else np.asarray([True] * 3 if pbc is None else list(pbc), np.bool_)
+        po = _PredictOptions(True, bool(compute_stress), bool(use_nc_forces))
+        e = ctypes.c_double()
+        st = np.zeros(6, np.float32)
+        hs = ctypes.c_bool(False)
+        _check(lib().mlipcpp_b200_predict_device_forces(
+            self._h, int(n_atoms), ctypes.c_void_p(d_positions), z.ctypes.data,
+            None if c is None else c.ctypes.data, None if p is None else p.ctypes.data, ctypes.byref(po),
+            ctypes.c_void_p(d_forces) if d_forces else None, ctypes.byref(e), st.ctypes.data, ctypes.byref(hs)))
+        return float(e.value), (st if hs.value else None)
 
     def predict_local(self, d_positions: int, numbers, n_layer0: int, n_owned: int, cell, pbc=None,
                       compute_forces=True, d_forces: int = 0):

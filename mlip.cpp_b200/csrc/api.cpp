@@ -533,6 +533,48 @@ mlipcpp_error_t mlipcpp_b200_predict_device(mlipcpp_model_t model, int32_t n_ato
   }
 }
 
+mlipcpp_error_t mlipcpp_b200_predict_device_forces(mlipcpp_model_t model, int32_t n_atoms, const float *d_positions,
+                                                   const int32_t *atomic_numbers, const float *cell,
+                                                   const bool *pbc, const mlipcpp_predict_options_t *options,
+                                                   float *d_forces, double *energy, float stress[6],
+                                                   bool *has_stress) {
+  if (auto e = check_model(model)) return e;
+  if (!energy) {
+    set_error("NULL energy pointer");
+    return MLIPCPP_ERROR_NULL_POINTER;
+  }
+  mlipcpp_system_t s{n_atoms, d_positions, atomic_numbers, cell, pbc};
+  if (auto e = check_system(&s)) return e;
+  mlipcpp_predict_options_t dflt;
+  if (!options) {
+    mlipcpp_predict_options_default(&dflt);
+    options = &dflt;
+  }
+  try {
+    const bool grad = (options->compute_forces || options->compute_stress) && !options->use_nc_forces;
+    pet::SystemView v = make_view(&s);
+    model->model->predict_device(d_positions, v, grad, model->last, false, options->use_nc_forces);
+    finish_options(model->last, *options);
+    *energy = model->last.energy;
+    if (d_forces) {
+      if (!model->last.has_forces) {
+        set_error("No forces: compute_forces is off or the model has no force heads");
+        return MLIPCPP_ERROR_INVALID_PARAMETER;
+      }
+      CUDA_CHECK(cudaMemcpyAsync(d_forces, model->model->device_forces(), sizeof(float) * 3 * n_atoms,
+                                 cudaMemcpyDeviceToDevice, model->model->stream()));
+      CUDA_CHECK(cudaStreamSynchronize(model->model->stream()));
+    }
+    if (has_stress) *has_stress = model->last.has_stress;
+    if (stress && model->last.has_stress)
+      for (int c = 0; c < 6; ++c) stress[c] = model->last.stress[c];
+    clear_error();
+    return MLIPCPP_OK;
+  } catch (const std::exception &e) {
+    return map_exception(e, "Prediction failed: ", MLIPCPP_ERROR_COMPUTATION);
+  }
+}
+
 mlipcpp_error_t mlipcpp_b200_predict_local(mlipcpp_model_t model, int32_t n_local, const double *d_positions,
                                            const int32_t *atomic_numbers, int32_t n_layer0, int32_t n_owned,
                                            const float cell[9], const bool *pbc, bool compute_forces,

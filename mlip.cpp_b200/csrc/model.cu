@@ -163,6 +163,8 @@ const float *PETModel::w(const std::string &name) const {
   return it->second;
 }
 
+const float *PETModel::device_forces() const { return in_->a.F; }
+
 size_t PETModel::device_bytes() const {
   return wbuf_.cap + persist_.cap + scratch_.cap + sp_[0].cap + sp_[1].cap + nl_.center.cap * 10;
 }

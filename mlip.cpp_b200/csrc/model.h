@@ -99,6 +99,9 @@ class PETModel {
   void predict_device(const float *d_pos, const SystemView &sys, bool compute_grad, Result &out,
                       bool copy_forces, bool nc = false);
 
+  // Forces [n, 3] of the last prediction in device memory (valid until the
+  // next call on this model).
+  const float *device_forces() const;
   const PhaseTimes &last_times() const { return times_; }
   // Per-launch CUDA events around GEMM and attention launches, accumulated
   // into kernel_stats() after each predict (cumulative until reset).
