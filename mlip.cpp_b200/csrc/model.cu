@@ -842,8 +842,8 @@ void PETModel::predict_local(const double *d_pos, int n_local, const int32_t *nu
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[3], s));
   forward_backward(grad);
   const Acts &a = in_->a;
-  double *red = static_cast<double *>(d_red_.ensure(sizeof(double) * 16));
-  reduce_local(nl_.vec.as<float>(), a.g, a.e_atom, n_owned, grad ? El_[0] : 0, red, s);
+  double *red = static_cast<double *>(d_red_.ensure(sizeof(double) * (16 + 7 * kReduceMaxParts)));
+  reduce_local(nl_.vec.as<float>(), a.g, a.e_atom, n_owned, grad ? El_[0] : 0, red, red + 16, s);
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[6], s));
   if (grad && d_forces)
     CUDA_CHECK(cudaMemcpyAsync(d_forces, a.F, sizeof(float) * 3 * n_local, cudaMemcpyDeviceToDevice, s));
@@ -936,9 +936,9 @@ void PETModel::run_group(const float *d_pos, int n_atoms, const std::vector<cons
   // per-system energy and virial in f64 (pet.cpp:542-548, 1041-1077); then
   // the per-system Voigt sums of the non-conservative stress
   const size_t nred = static_cast<size_t>(ncs_ ? 13 : 7) * n_sys;
-  double *red = static_cast<double *>(d_red_.ensure(sizeof(double) * (nred + 7)));
+  double *red = static_cast<double *>(d_red_.ensure(sizeof(double) * (nred + 8 + 7 * kReduceMaxParts)));
   reduce_systems(nl_.vec.as<float>(), a.g, a.e_atom, nl_.offset.as<int>(), dsb, n_sys, red + n_sys, red,
-                 grad && El_[0] > 0, s);
+                 grad && El_[0] > 0, s, n_atoms, El_[0], red + nred + 8);
   if (ncs_) nc_stress_reduce(a.ncS, dsb, n_sys, red + 7 * n_sys, s);
   // pet.cpp:601-617: non-conservative forces added to the gradient forces
   if (ncf_) add_vec(a.ncF, a.F, 3 * n_atoms, grad, s);

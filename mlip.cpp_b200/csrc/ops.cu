@@ -248,15 +248,25 @@ __global__ void k_edge_embed_bwd(const float *__restrict__ demb, int ld, const f
   }
 }
 
+// Warp per edge, 16-byte accesses along the row (d, ld multiples of 4).
 __global__ void k_message_bwd(const float *__restrict__ dmsg, int ld, const int *__restrict__ rev,
                               const int *__restrict__ edge_row, float *__restrict__ dx, int n_edges,
                               int n_msg, int d) {
-  const int64_t total = static_cast<int64_t>(n_edges) * d;
-  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
-       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int x = static_cast<int>(t / d), c = static_cast<int>(t % d);
+  const int lane = threadIdx.x & 31;
+  for (int x = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; x < n_edges; x += (gridDim.x * blockDim.x) >> 5) {
     const int rv = rev[x];
-    if (rv >= 0 && rv < n_msg) dx[static_cast<size_t>(edge_row[x]) * d + c] += 0.5f * dmsg[static_cast<size_t>(rv) * ld + c];
+    if (rv < 0 || rv >= n_msg) continue;
+    const float4 *src = reinterpret_cast<const float4 *>(dmsg + static_cast<size_t>(rv) * ld);
+    float4 *dst = reinterpret_cast<float4 *>(dx + static_cast<size_t>(edge_row[x]) * d);
+    for (int c = lane; c < d / 4; c += 32) {
+      const float4 m = src[c];
+      float4 v = dst[c];
+      v.x = fmaf(0.5f, m.x, v.x);
+      v.y = fmaf(0.5f, m.y, v.y);
+      v.z = fmaf(0.5f, m.z, v.z);
+      v.w = fmaf(0.5f, m.w, v.w);
+      dst[c] = v;
+    }
   }
 }
 
@@ -351,6 +361,47 @@ __global__ void __launch_bounds__(512) k_reduce_systems(
   }
 }
 
+// Deterministic two-stage sum of one structure's energy and virial: block b
+// sums a fixed chunk of the atoms and of the edges into partial[b][0..6]
+// (0: energy, 1..6: Voigt virial), then one block adds the partials in
+// block order.  Replaces a single-block pass over a million edges.
+__global__ void __launch_bounds__(256) k_reduce_partial(const float *__restrict__ vec, const float *__restrict__ g,
+                                                        const float *__restrict__ e_atom, int n_atoms, int n_edges,
+                                                        int with_virial, double *__restrict__ partial) {
+  __shared__ double sm[8 * 7];
+  const int B = gridDim.x, b = blockIdx.x;
+  const int ca = (n_atoms + B - 1) / B, ce = (n_edges + B - 1) / B;
+  const int a0 = b * ca, a1 = min(n_atoms, a0 + ca), e0 = b * ce, e1 = with_virial ? min(n_edges, e0 + ce) : e0;
+  double v[7] = {0, 0, 0, 0, 0, 0, 0};
+  for (int i = a0 + threadIdx.x; i < a1; i += blockDim.x) v[0] += static_cast<double>(e_atom[i]);
+  for (int e = e0 + threadIdx.x; e < e1; e += blockDim.x) {
+    const double ex = vec[3 * e], ey = vec[3 * e + 1], ez = vec[3 * e + 2];
+    const double gx = g[3 * e], gy = g[3 * e + 1], gz = g[3 * e + 2];
+    v[1] += ex * gx;
+    v[2] += ey * gy;
+    v[3] += ez * gz;
+    v[4] += 0.5 * (ey * gz + ez * gy);
+    v[5] += 0.5 * (ex * gz + ez * gx);
+    v[6] += 0.5 * (ex * gy + ey * gx);
+  }
+  block_sum<7>(v, sm);
+  if (threadIdx.x == 0)
+    for (int c = 0; c < 7; ++c) partial[7 * b + c] = v[c];
+}
+
+__global__ void __launch_bounds__(256) k_reduce_final(const double *__restrict__ partial, int n_part,
+                                                      double *__restrict__ energy, double *__restrict__ virial) {
+  __shared__ double sm[8 * 7];
+  double v[7] = {0, 0, 0, 0, 0, 0, 0};
+  for (int b = threadIdx.x; b < n_part; b += blockDim.x)
+    for (int c = 0; c < 7; ++c) v[c] += partial[7 * b + c];
+  block_sum<7>(v, sm);
+  if (threadIdx.x == 0) {
+    *energy = v[0];
+    for (int c = 0; c < 6; ++c) virial[c] = v[1 + c];
+  }
+}
+
 // ---- non-conservative heads ----------------------------------------------
 constexpr int kNcMaxOut = 9;
 
@@ -432,33 +483,22 @@ __global__ void __launch_bounds__(256) k_nc_stress_reduce(const float *__restric
     for (int c = 0; c < 6; ++c) out[6 * k + c] = v[c];
 }
 
-__global__ void __launch_bounds__(1024) k_reduce_local(const float *__restrict__ vec, const float *__restrict__ g,
-                                                     const float *__restrict__ e_atom, int n_energy, int n_edges,
-                                                     double *__restrict__ out) {
-  __shared__ double sm[32 * 7];
-  double v[7] = {0, 0, 0, 0, 0, 0, 0};
-  for (int i = threadIdx.x; i < n_energy; i += blockDim.x) v[0] += static_cast<double>(e_atom[i]);
-  for (int e = threadIdx.x; e < n_edges; e += blockDim.x) {
-    const double ex = vec[3 * e], ey = vec[3 * e + 1], ez = vec[3 * e + 2];
-    const double gx = g[3 * e], gy = g[3 * e + 1], gz = g[3 * e + 2];
-    v[1] += ex * gx;
-    v[2] += ey * gy;
-    v[3] += ez * gz;
-    v[4] += 0.5 * (ey * gz + ez * gy);
-    v[5] += 0.5 * (ex * gz + ez * gx);
-    v[6] += 0.5 * (ex * gy + ey * gx);
-  }
-  block_sum<7>(v, sm);
-  if (threadIdx.x == 0)
-    for (int c = 0; c < 7; ++c) out[c] = v[c];
-}
 
 }  // namespace
 
-void reduce_local(const float *vec, const float *g, const float *e_atom, int n_energy, int n_edges,
-                  double *out, cudaStream_t s) {
-  k_reduce_local<<<1, 1024, 0, s>>>(vec, g, e_atom, n_energy, n_edges, out);
+void reduce_one(const float *vec, const float *g, const float *e_atom, int n_atoms, int n_edges, bool with_virial,
+                double *partial, double *energy, double *virial, cudaStream_t s) {
+  const int64_t work = std::max<int64_t>(std::max(n_atoms, with_virial ? n_edges : 0), 1);
+  const int B = static_cast<int>(std::min<int64_t>(kReduceMaxParts, (work + 4095) / 4096));
+  k_reduce_partial<<<B, 256, 0, s>>>(vec, g, e_atom, n_atoms, n_edges, with_virial ? 1 : 0, partial);
   CUDA_LAUNCH_CHECK();
+  k_reduce_final<<<1, 256, 0, s>>>(partial, B, energy, virial);
+  CUDA_LAUNCH_CHECK();
+}
+
+void reduce_local(const float *vec, const float *g, const float *e_atom, int n_energy, int n_edges,
+                  double *out, double *partial, cudaStream_t s) {
+  reduce_one(vec, g, e_atom, n_energy, n_edges, n_edges > 0, partial, out, out + 1, s);
 }
 
 void edge_prep(const EdgePrepArgs &a, cudaStream_t s) {
@@ -539,8 +579,9 @@ void edge_embed_bwd(const float *demb, int ld, const float *We, float *g4, int n
 void message_bwd(const float *dmsg, int ld, const int *rev, const int *edge_row, float *dx,
                  int n_edges, int n_msg, int d, cudaStream_t s) {
   if (n_edges <= 0) return;
-  k_message_bwd<<<grid_for(static_cast<int64_t>(n_edges) * d, 256), 256, 0, s>>>(dmsg, ld, rev, edge_row, dx,
-                                                                                 n_edges, n_msg, d);
+  if (d % 4 || ld % 4) throw Error(kErrInternal, "message_bwd: rows must be multiples of 4 floats");
+  k_message_bwd<<<grid_for(static_cast<int64_t>(n_edges) * 32, 256), 256, 0, s>>>(dmsg, ld, rev, edge_row, dx,
+                                                                                  n_edges, n_msg, d);
   CUDA_LAUNCH_CHECK();
 }
 
@@ -582,8 +623,12 @@ void nc_stress_reduce(const float *S, const int *sys_atom_begin, int n_sys, doub
 
 void reduce_systems(const float *vec, const float *g, const float *e_atom, const int *offset,
                     const int *sys_atom_begin, int n_sys, double *virial, double *energy,
-                    bool with_virial, cudaStream_t s) {
+                    bool with_virial, cudaStream_t s, int n_atoms, int n_edges, double *partial) {
   if (n_sys <= 0) return;
+  if (n_sys == 1 && partial) {  // one structure: spread over the GPU
+    reduce_one(vec, g, e_atom, n_atoms, n_edges, with_virial, partial, energy, virial, s);
+    return;
+  }
   k_reduce_systems<<<n_sys, 512, 0, s>>>(vec, g, e_atom, offset, sys_atom_begin, virial, energy,
                                          with_virial ? 1 : 0);
   CUDA_LAUNCH_CHECK();

@@ -68,9 +68,14 @@ void forces(const float *g, const int *offset, const int *nbr, const int *rev, f
             int n_edges, cudaStream_t s);
 // Per system k: virial[k][6] = sum over its edges of sym(vec (x) g) (Voigt),
 // energy[k] = sum of its atomic energies (both in f64).
+// A single structure (n_sys == 1 with `partial`, scratch of
+// kReduceMaxParts x 7 doubles: n_atoms atoms and n_edges edges) is summed by
+// a deterministic two-stage reduction over the whole GPU.
+constexpr int kReduceMaxParts = 1024;
 void reduce_systems(const float *vec, const float *g, const float *e_atom, const int *offset,
                     const int *sys_atom_begin, int n_sys, double *virial, double *energy,
-                    bool with_virial, cudaStream_t s);
+                    bool with_virial, cudaStream_t s, int n_atoms = 0, int n_edges = 0,
+                    double *partial = nullptr);
 
 // Non-conservative property readout of one layer (build_property_output,
 // pet_layers.cpp:845-915), warp per atom i < n:
@@ -86,8 +91,9 @@ void nc_readout(const float *yn, const float *ye, const float *wn, const float *
 void nc_stress_reduce(const float *S, const int *sys_atom_begin, int n_sys, double *out, cudaStream_t s);
 
 // out[0] = sum of e_atom[0..n_energy), out[1..6] = Voigt sum over edges
-// [0, n_edges) of sym(vec (x) g) (f64, one CTA).
+// [0, n_edges) of sym(vec (x) g) (f64, two-stage; partial: scratch of
+// kReduceMaxParts x 7 doubles).
 void reduce_local(const float *vec, const float *g, const float *e_atom, int n_energy, int n_edges,
-                  double *out, cudaStream_t s);
+                  double *out, double *partial, cudaStream_t s);
 
 }  // namespace pet
