@@ -453,7 +453,7 @@ __global__ void k_ln_fwd4(const float *__restrict__ x, const float *__restrict__
   }
   const float var = warp_sum(q) * inv_d;
   const float sd = sqrtf(var * (1.0f + kLnEps));
-  float *yr = y + static_cast<size_t>(row) * d;
+  float *yr = y ? y + static_cast<size_t>(row) * d : nullptr;  // y null: split output only
   float *hr = xhat + static_cast<size_t>(row) * d;
 #pragma unroll
   for (int k = 0; k < NB; ++k) {
@@ -464,7 +464,7 @@ __global__ void k_ln_fwd4(const float *__restrict__ x, const float *__restrict__
                                  (v[k].w - mean) / sd);
     const float4 o = make_float4(h.x * gg.x + bb.x, h.y * gg.y + bb.y, h.z * gg.z + bb.z, h.w * gg.w + bb.w);
     *reinterpret_cast<float4 *>(hr + c) = h;
-    *reinterpret_cast<float4 *>(yr + c) = o;
+    if (yr) *reinterpret_cast<float4 *>(yr + c) = o;
     if (ys.hi) warp_split_block(ys, row, k, o, lane);
   }
   if (lane == 0) rstd[row] = 1.0f / sd;
@@ -497,13 +497,13 @@ __global__ void k_ln_bwd4(const float *__restrict__ dy, const float *__restrict_
   const float m1 = warp_sum(s1) * inv_d;
   const float m2 = warp_sum(s2) * inv_d * (1.0f + kLnEps);
   const float r = rstd[row];
-  float *dxr = dx + static_cast<size_t>(row) * d;
+  float *dxr = dx ? dx + static_cast<size_t>(row) * d : nullptr;  // dx null: split output only
 #pragma unroll
   for (int k = 0; k < NB; ++k) {
     const int c = 128 * k + 4 * lane;
     const float4 o = make_float4(r * (gh[k].x - m1 - hh[k].x * m2), r * (gh[k].y - m1 - hh[k].y * m2),
                                  r * (gh[k].z - m1 - hh[k].z * m2), r * (gh[k].w - m1 - hh[k].w * m2));
-    *reinterpret_cast<float4 *>(dxr + c) = o;
+    if (dxr) *reinterpret_cast<float4 *>(dxr + c) = o;
     if (dxs.hi) warp_split_block(dxs, row, k, o, lane);
   }
 }

@@ -425,6 +425,7 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
 // with 64-byte rows and the 64-byte swizzle.
 struct EpiMaps {
   CUtensorMap c, z, r, hi, lo;
+  CUtensorMap rhi, rlo;  // residual in split form: boxes of 16 fp16 x 32 rows, no swizzle
 };
 
 __device__ __forceinline__ uint32_t f2u(float x) { return __float_as_uint(x); }
@@ -473,16 +474,29 @@ template <int EPI>
 __device__ __forceinline__ const CUtensorMap *epi_load_map(const EpiMaps &em) {
   return EPI == EPI_DSILU ? &em.z : EPI == EPI_RESID ? &em.r : &em.c;
 }
+// Load of one 16-column group of the epilogue input into buffer b: the
+// fp32 box (64-byte swizzle), or for a split residual (rs) the hi and lo
+// boxes (1 KB each, unswizzled) side by side.
 template <int EPI>
-__device__ __forceinline__ void epi_prefetch(const EpiMaps &em, const EpiWarp &ew, int row0, int n0, int lane) {
+__device__ __forceinline__ void epi_issue_load(const EpiMaps &em, const EpiWarp &ew, int b, bool rs, int col,
+                                               int row0) {
+  const uint32_t bar = ew.lbar0 + 8 * b, buf = ew.buf0 + 2048 * b;
+  mbar_expect_tx(bar, 2048);
+  if (EPI == EPI_RESID && rs) {
+    tma_load_2d(buf, &em.rhi, bar, col, row0);
+    tma_load_2d(buf + 1024, &em.rlo, bar, col, row0);
+  } else {
+    tma_load_2d(buf, epi_load_map<EPI>(em), bar, col, row0);
+  }
+}
+template <int EPI>
+__device__ __forceinline__ void epi_prefetch(const EpiMaps &em, const EpiWarp &ew, bool rs, int row0, int n0,
+                                             int lane) {
   if (!(EPI == EPI_DSILU || EPI == EPI_RESID || EPI == EPI_ACCUM)) return;
   if (lane == 0) {
     bulk_wait_read<0>();  // earlier stores no longer read the buffers
 #pragma unroll
-    for (int b = 0; b < 2; ++b) {
-      mbar_expect_tx(ew.lbar0 + 8 * b, 2048);
-      tma_load_2d(ew.buf0 + 2048 * b, epi_load_map<EPI>(em), ew.lbar0 + 8 * b, n0 + 16 * b, row0);
-    }
+    for (int b = 0; b < 2; ++b) epi_issue_load<EPI>(em, ew, b, rs, n0 + 16 * b, row0);
   }
   __syncwarp();
 }
@@ -497,6 +511,10 @@ __device__ __forceinline__ bool epilogue_tma(const GemmArgs &p, const EpiMaps &e
   const bool valid = row < p.M;
   const bool split = p.c_split.hi != nullptr;
   const bool hasC = p.C != nullptr, hasZ = EPI == EPI_SILU && p.Z != nullptr;
+  const bool rs = EPI == EPI_RESID && p.r_split.hi != nullptr;
+  // scale of the split residual's 128-column block for this row
+  const float rsf = (rs && valid) ? pow2f(-static_cast<int>(p.r_split.sc[static_cast<size_t>(n0 / 128) * p.r_split.rows + row]))
+                                  : 0.f;
   if (!kLoad) {  // stores of earlier tiles no longer read the buffers
     if (lane == 0) bulk_wait_read<0>();
     __syncwarp();
@@ -518,12 +536,29 @@ __device__ __forceinline__ bool epilogue_tma(const GemmArgs &p, const EpiMaps &e
     if (kLoad) {
       if (!__all_sync(0xffffffffu, wait_or_abort(ew.lbar0 + 8 * b, (ew.ph >> b) & 1u, abort_flag))) return false;
       ew.ph ^= 1u << b;
+      if (rs) {  // residual = (hi + lo) 2^-s, rows of 32 bytes
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const uint4 v = lds128(sw64(buf, lane, m));
-        const float l4[4] = {u2f(v.x), u2f(v.y), u2f(v.z), u2f(v.w)};
+        for (int m = 0; m < 2; ++m) {
+          const uint4 hv = lds128(buf + static_cast<uint32_t>(lane * 32 + 16 * m));
+          const uint4 lv = lds128(buf + 1024u + static_cast<uint32_t>(lane * 32 + 16 * m));
+          const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w}, lw[4] = {lv.x, lv.y, lv.z, lv.w};
 #pragma unroll
-        for (int k = 0; k < 4; ++k) x[4 * m + k] = EPI == EPI_DSILU ? x[4 * m + k] * l4[k] : x[4 * m + k] + l4[k];
+          for (int k = 0; k < 4; ++k) {
+            const float2 h2 = __half22float2(*reinterpret_cast<const __half2 *>(&hw[k]));
+            const float2 l2 = __half22float2(*reinterpret_cast<const __half2 *>(&lw[k]));
+            x[8 * m + 2 * k] += (h2.x + l2.x) * rsf;
+            x[8 * m + 2 * k + 1] += (h2.y + l2.y) * rsf;
+          }
+        }
+        __syncwarp();  // every lane has read the buffer before it is rewritten
+      } else {
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const uint4 v = lds128(sw64(buf, lane, m));
+          const float l4[4] = {u2f(v.x), u2f(v.y), u2f(v.z), u2f(v.w)};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) x[4 * m + k] = EPI == EPI_DSILU ? x[4 * m + k] * l4[k] : x[4 * m + k] + l4[k];
+        }
       }
       // the result goes back into the same buffer, then to C; the buffer
       // then receives the group two ahead (the proxy fence orders this
@@ -542,8 +577,7 @@ __device__ __forceinline__ bool epilogue_tma(const GemmArgs &p, const EpiMaps &e
         }
         if (g + 2 < NC / 16) {
           bulk_wait_read<0>();
-          mbar_expect_tx(ew.lbar0 + 8 * b, 2048);
-          tma_load_2d(buf, epi_load_map<EPI>(em), ew.lbar0 + 8 * b, n0 + 16 * (g + 2), row0);
+          epi_issue_load<EPI>(em, ew, b, rs, n0 + 16 * (g + 2), row0);
         }
       }
     } else {
@@ -962,7 +996,7 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
     for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ep) {
       const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BNt + h * NC;
       const int row = m0 + q * 32 + lane;
-      if (!p.c_rows) epi_prefetch<EPI>(em, ew, m0 + q * 32, n0, lane);
+      if (!p.c_rows) epi_prefetch<EPI>(em, ew, p.r_split.hi != nullptr, m0 + q * 32, n0, lane);
       float acc[NC];
 #pragma unroll
       for (int j = 0; j < NC; ++j) acc[j] = 0.f;
@@ -1304,15 +1338,16 @@ CUtensorMap make_map_f16(const void *ptr, uint64_t rows, uint64_t cols, uint64_t
 // Map of an epilogue operand: [rows][cols] of `elem`-byte elements with
 // leading dimension ld, box (32 x 64 bytes), 64-byte swizzle.
 CUtensorMap make_map_epi(const void *ptr, CUtensorMapDataType type, uint32_t elem, uint64_t rows, uint64_t cols,
-                         uint64_t ld) {
+                         uint64_t ld, uint32_t box_bytes = 64) {
   resolve_encoder();
   CUtensorMap m;
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {ld * elem};
-  const cuuint32_t box[2] = {64 / elem, 32};
+  const cuuint32_t box[2] = {box_bytes / elem, 32};
   const cuuint32_t es[2] = {1, 1};
   const CUresult r = g_encode_tiled(&m, type, 2, const_cast<void *>(ptr), dims, strides, box, es,
-                                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                                    CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                    box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE,
                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw Error(kErrBackend, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
   return m;
@@ -1326,7 +1361,12 @@ EpiMaps make_epi_maps(const GemmArgs &a) {
   const auto F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32, F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   if (a.C) e.c = make_map_epi(a.C, F32, 4, a.M, a.N, a.ldc);
   if (a.Z && (a.epi == EPI_SILU || a.epi == EPI_DSILU)) e.z = make_map_epi(a.Z, F32, 4, a.M, a.N, a.ldz);
-  if (a.epi == EPI_RESID) e.r = make_map_epi(a.R, F32, 4, a.M, a.N, a.ldr);
+  if (a.epi == EPI_RESID && a.r_split.hi) {
+    e.rhi = make_map_epi(a.r_split.hi, F16, 2, a.M, a.N, a.r_split.cols, 32);
+    e.rlo = make_map_epi(a.r_split.lo, F16, 2, a.M, a.N, a.r_split.cols, 32);
+  } else if (a.epi == EPI_RESID) {
+    e.r = make_map_epi(a.R, F32, 4, a.M, a.N, a.ldr);
+  }
   if (a.c_split.hi) {
     e.hi = make_map_epi(a.c_split.hi, F16, 2, a.M, a.N, a.c_split.cols);
     e.lo = make_map_epi(a.c_split.lo, F16, 2, a.M, a.N, a.c_split.cols);
@@ -1389,7 +1429,7 @@ void launch16(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t s)
     CUDA_LAUNCH_CHECK();
   }
   const int bn = g_f16_bn ? g_f16_bn : 128;
-  if (a.N % 256 == 0 && bn == 512 && w.products == 3) launch16_pair<EPI>(a, w, err, s);
+  if (a.N % 256 == 0 && bn == 512 && w.products == 3 && !a.r_split.hi) launch16_pair<EPI>(a, w, err, s);
   else if (a.N % 256 == 0 && bn == 256) launch16_bn<EPI, 256>(a, w, err, s);
   else launch16_bn<EPI, 128>(a, w, err, s);
 }
@@ -1419,6 +1459,9 @@ void gemm_3xf16(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t 
       reinterpret_cast<uintptr_t>(sp.hi) % 16 || reinterpret_cast<uintptr_t>(sp.lo) % 16 ||
       (a.c_split.hi && (reinterpret_cast<uintptr_t>(a.c_split.hi) % 16 || reinterpret_cast<uintptr_t>(a.c_split.lo) % 16)))
     throw Error(kErrInternal, "gemm_3xf16: fp16 operands not 16-byte aligned");
+  if (a.r_split.hi && (a.epi != EPI_RESID || a.c_rows || a.r_split.rows < a.M || a.r_split.cols != a.N ||
+                       reinterpret_cast<uintptr_t>(a.r_split.hi) % 16 || reinterpret_cast<uintptr_t>(a.r_split.lo) % 16))
+    throw Error(kErrInternal, "gemm_3xf16: split residual view does not match the GEMM");
   switch (a.epi) {
     case EPI_STORE: launch16<EPI_STORE>(a, w, err, s); break;
     case EPI_SILU: launch16<EPI_SILU>(a, w, err, s); break;

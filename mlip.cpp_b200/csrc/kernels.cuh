@@ -51,6 +51,7 @@ struct GemmArgs {
   Split16View a_split;
   bool a_split_ready = false;
   Split16View c_split;
+  Split16View r_split;  // EPI_RESID: residual in split form (rows m) instead of R
 };
 
 // Dense fp32 GEMM (exact fp32 FFMA accumulation).

@@ -519,6 +519,7 @@ void PETModel::forward_backward(bool grad) {
     const Split16View *a = nullptr;  // A operand in split form
     bool a_ready = true;             // ... already written (else: write it from fp32 A first)
     const Split16View *c = nullptr;  // also write C in split form
+    const Split16View *r = nullptr;  // EPI_RESID: residual in split form (R unused)
   };
 
   auto gemm = [&](const float *A, int lda, const int *a_rows, const float *B, int ldb, float *C, int ldc,
@@ -542,9 +543,10 @@ void PETModel::forward_backward(bool grad) {
         g.a_split_ready = false;
       }
       if (io.c) g.c_split = *io.c;
+      if (io.r) g.r_split = *io.r;
       gemm_3xf16(g, TCWeights16{h16 + eoff, h16 + wspan_ + eoff, weight_scale(eoff), reduced_ ? 1 : 3},
                  d_err_.as<int>(), st);
-    } else if (io.c || (io.a && io.a_ready)) {
+    } else if (io.c || io.r || (io.a && io.a_ready)) {
       throw Error(kErrInternal, "split-fp16 operands need the 3xFP16 GEMM");
     } else if (tc) {
       gemm_3xtf32(g, TCWeights{B + wspan_, B + 2 * wspan_}, d_err_.as<int>(), st);
@@ -590,17 +592,20 @@ void PETModel::forward_backward(bool grad) {
     }
     attn(false, at);
     at.out_split = Split16View{};
-    gemm(a.o, d, nullptr, B.Wout, d, a.u, d, nullptr, T, d, d, B.bout, EPI_RESID, s, nullptr, 0, x, d,
-         SplitIO{ch ? &so : nullptr});
+    // in chain mode the residuals come from the split forms, so the fp32
+    // block input and x1 are not written at all
+    gemm(a.o, d, nullptr, B.Wout, d, a.u, d, nullptr, T, d, d, B.bout, EPI_RESID, s, nullptr, 0, ch ? nullptr : x, d,
+         SplitIO{ch ? &so : nullptr, true, nullptr, ch ? sx : nullptr});
     if (ch) sx1 = take_split(T, d);
-    layer_norm_fwd(a.u, B.ga, B.ba, a.x1, a.xa[b], a.ra[b], T, d, s, ch ? &sx1 : nullptr);
+    layer_norm_fwd(a.u, B.ga, B.ba, ch ? nullptr : a.x1, a.xa[b], a.ra[b], T, d, s, ch ? &sx1 : nullptr);
     if (ch) shf = take_split(T, f);
     gemm(a.x1, d, nullptr, B.W0, d, a.hf, f, nullptr, T, f, d, B.b0, EPI_SILU, s, keep(a.zf[b]), f, nullptr, 0,
          SplitIO{ch ? &sx1 : nullptr, true, ch ? &shf : nullptr});
-    gemm(a.hf, f, nullptr, B.W3, f, a.u2, d, nullptr, T, d, f, B.b3, EPI_RESID, s, nullptr, 0, a.x1, d,
-         SplitIO{ch ? &shf : nullptr});
+    gemm(a.hf, f, nullptr, B.W3, f, a.u2, d, nullptr, T, d, f, B.b3, EPI_RESID, s, nullptr, 0, ch ? nullptr : a.x1, d,
+         SplitIO{ch ? &shf : nullptr, true, nullptr, ch ? &sx1 : nullptr});
     if (ch && sout) *sout = take_split(T, d);
-    layer_norm_fwd(a.u2, B.gm, B.bm, out, a.xm[b], a.rm[b], T, d, s, ch ? sout : nullptr);
+    // a block output with a split form feeds only the next block: no fp32 copy
+    layer_norm_fwd(a.u2, B.gm, B.bm, (ch && sout) ? nullptr : out, a.xm[b], a.rm[b], T, d, s, ch ? sout : nullptr);
   };
   // Energy head (node or edge) on rows `rows` of the layer output.
   auto head_fwd = [&](const float *x, const int *rows, int M, const HeadW &hw, float *y1, float *y2, float *z1,
@@ -644,12 +649,12 @@ void PETModel::forward_backward(bool grad) {
       gemm(a.cat, K, nullptr, L.C0, K, a.hc, H, nullptr, E, H, K, L.c0, EPI_SILU, s, keep(a.zc[l]), H, nullptr, 0,
            SplitIO{ch ? &scat : nullptr, true, ch ? &shc : nullptr});
       if (ch) sx = take_split(T, d);
-      gemm(a.hc, H, nullptr, L.C2, H, a.xin, d, a.edge_row, E, d, H, L.c2, EPI_STORE, s, nullptr, 0, nullptr, 0,
-           SplitIO{ch ? &shc : nullptr, true, ch ? &sx : nullptr});
+      gemm(a.hc, H, nullptr, L.C2, H, ch ? nullptr : a.xin, d, a.edge_row, E, d, H, L.c2, EPI_STORE, s, nullptr, 0,
+           nullptr, 0, SplitIO{ch ? &shc : nullptr, true, ch ? &sx : nullptr});
     } else if (ch) {
       sx = take_split(T, d);
     }
-    node_tokens(L.node_emb, species, a.node_row, a.xin, N, d, s, ch ? &sx : nullptr);
+    node_tokens(L.node_emb, species, a.node_row, ch ? nullptr : a.xin, N, d, s, ch ? &sx : nullptr);
     Split16View smid;
     block_fwd(2 * l, a.xin, ch ? &sx : nullptr, a.xmid, ch ? &smid : nullptr);
     block_fwd(2 * l + 1, a.xmid, ch ? &smid : nullptr, a.xl[l], nullptr);
@@ -697,14 +702,15 @@ void PETModel::forward_backward(bool grad) {
     const BlockW &B = g_lw[b / 2].blk[b % 2];
     Split16View sdu, sdhf, sdu2, sdq;
     if (ch) sdu = take_split(T, d);
-    layer_norm_bwd(dy, a.xm[b], a.rm[b], B.gm, a.du, T, d, s, ch ? &sdu : nullptr);
+    // chain mode: du is read only in split form (GEMM operand and residual)
+    layer_norm_bwd(dy, a.xm[b], a.rm[b], B.gm, ch ? nullptr : a.du, T, d, s, ch ? &sdu : nullptr);
     if (ch) sdhf = take_split(T, f);
     gemm(a.du, d, nullptr, B.W3T, d, a.dhf, f, nullptr, T, f, d, nullptr, EPI_DSILU, s, a.zf[b], f, nullptr, 0,
          SplitIO{ch ? &sdu : nullptr, true, ch ? &sdhf : nullptr});
-    gemm(a.dhf, f, nullptr, B.W0T, f, a.dx1, d, nullptr, T, d, f, nullptr, EPI_RESID, s, nullptr, 0, a.du, d,
-         SplitIO{ch ? &sdhf : nullptr});
+    gemm(a.dhf, f, nullptr, B.W0T, f, a.dx1, d, nullptr, T, d, f, nullptr, EPI_RESID, s, nullptr, 0,
+         ch ? nullptr : a.du, d, SplitIO{ch ? &sdhf : nullptr, true, nullptr, ch ? &sdu : nullptr});
     if (ch) sdu2 = take_split(T, d);
-    layer_norm_bwd(a.dx1, a.xa[b], a.ra[b], B.ga, a.du, T, d, s, ch ? &sdu2 : nullptr);
+    layer_norm_bwd(a.dx1, a.xa[b], a.ra[b], B.ga, ch ? nullptr : a.du, T, d, s, ch ? &sdu2 : nullptr);
     gemm(a.du, d, nullptr, B.WoutT, d, a.dout, d, nullptr, T, d, d, nullptr, EPI_STORE, s, nullptr, 0, nullptr, 0,
          SplitIO{ch ? &sdu2 : nullptr});
     at.qkv = a.qkv[b];
@@ -718,7 +724,7 @@ void PETModel::forward_backward(bool grad) {
     attn(true, at);
     at.dqkv_split = Split16View{};
     gemm(a.dqkv, 3 * d, nullptr, B.WinT, 3 * d, dxin, d, nullptr, T, d, 3 * d, nullptr, EPI_RESID, s, nullptr,
-         0, a.du, d, SplitIO{ch ? &sdq : nullptr});
+         0, ch ? nullptr : a.du, d, SplitIO{ch ? &sdq : nullptr, true, nullptr, ch ? &sdu2 : nullptr});
   };
   auto compress_bwd = [&](int l, const float *dtok, bool accumulate) {
     const LayerW &L = g_lw[l];

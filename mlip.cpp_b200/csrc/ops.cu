@@ -155,7 +155,7 @@ __global__ void k_node_tokens_split(const float *__restrict__ tab, const int *__
   const int i = static_cast<int>(w / nb), blk = static_cast<int>(w % nb);
   const int c = blk * 128 + lane * 4, row = node_row[i];
   const float4 v = *reinterpret_cast<const float4 *>(tab + static_cast<size_t>(sp[i]) * d + c);
-  *reinterpret_cast<float4 *>(x + static_cast<size_t>(row) * d + c) = v;
+  if (x) *reinterpret_cast<float4 *>(x + static_cast<size_t>(row) * d + c) = v;  // x null: split only
   warp_split_block(xs, row, blk, v, lane);
 }
 
