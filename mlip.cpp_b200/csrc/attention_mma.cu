@@ -245,23 +245,65 @@ __device__ __forceinline__ void strip_store(const float (&v)[4][4], int r0, int 
 }
 
 // ---- forward ---------------------------------------------------------------------
-template <bool kSplit>
-__global__ void __launch_bounds__(kThreads) k_attn_fwd_mma(AttnArgs a) {
+// Shared memory of the forward for atoms of at most MT tokens: Q, K, V in
+// split form.  MT = 48 (3 warps, 23 KB) covers the usual neighbour counts
+// with no idle warp and more CTAs per SM; MT = 64 (4 warps) the rest.
+template <int MT>
+struct SmemF {
+  uint16_t mat[6][MT * kPitch];  // Q, K, V hi, then Q, K, V lo
+  float mask[MT];
+  int scale[3];
+  int rmax[MT];                  // row maxima of the output (bits of non-negative floats)
+};
+
+template <bool kSplit, int MT>
+__global__ void __launch_bounds__(2 * MT) k_attn_fwd_mma(AttnArgs a) {
+  constexpr int kW = MT / 16, kNT = MT / 8, kTh = 32 * kW;  // warps (row strips), 8-key tiles, threads
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
+  SmemF<MT> &sm = *reinterpret_cast<SmemF<MT> *>(smem_raw);
   const int atom = blockIdx.x, h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
   const int e0 = a.offset[atom], S = a.offset[atom + 1] - e0 + 1, t0 = e0 + atom;
   const int NW = (S + 15) >> 4, NK8 = 2 * NW;  // row strips, 8-key tiles
-  load_blocks(sm, a, t0, S, h, false);
-  for (int k = threadIdx.x; k < kMaxTok; k += kThreads) {
+  if (warp < 3) {  // warp w converts block w (Q, K, V; rows past S are zero) at one scale
+    float v[MT / 8][8];
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < MT / 8; ++i) {
+      const int task = lane + 32 * i, r = task >> 2, c = (task & 3) * 8;
+      if (r < S) {
+        const float *src = a.qkv + static_cast<size_t>(t0 + r) * 3 * a.d + warp * a.d + h * kHd + c;
+        const float4 x0 = *reinterpret_cast<const float4 *>(src), x1 = *reinterpret_cast<const float4 *>(src + 4);
+        v[i][0] = x0.x; v[i][1] = x0.y; v[i][2] = x0.z; v[i][3] = x0.w;
+        v[i][4] = x1.x; v[i][5] = x1.y; v[i][6] = x1.z; v[i][7] = x1.w;
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[i][k] = 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx = fmaxf(mx, fabsf(v[i][k]));
+    }
+    const int sc = split_scale_exponent(warp_absmax(mx));
+    const float f = pow2f(sc);
+    if (lane == 0) sm.scale[warp] = sc;
+#pragma unroll
+    for (int i = 0; i < MT / 8; ++i) {
+      const int task = lane + 32 * i, r = task >> 2, c = (task & 3) * 8;
+      uint32_t hh[4], ll[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) split2(v[i][2 * k], v[i][2 * k + 1], f, hh[k], ll[k]);
+      *reinterpret_cast<uint4 *>(&sm.mat[warp][r * kPitch + c]) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
+      *reinterpret_cast<uint4 *>(&sm.mat[3 + warp][r * kPitch + c]) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+    }
+  }
+  for (int k = threadIdx.x; k < MT; k += kTh) {
     sm.mask[k] = k < S ? (k == 0 ? 0.f : a.key_mask[e0 + k - 1]) : 0.f;
-    if (kSplit) sm.rmax[0][k] = 0;
+    if (kSplit) sm.rmax[k] = 0;
   }
   __syncthreads();
   if (kSplit) cluster_arrive();
-  const uint32_t Qh = smem_addr(sm.mat[0]), Ql = smem_addr(sm.mat[4]), Kh = smem_addr(sm.mat[1]),
-                 Kl = smem_addr(sm.mat[5]), Vh = smem_addr(sm.mat[2]), Vl = smem_addr(sm.mat[6]);
+  const uint32_t Qh = smem_addr(sm.mat[0]), Ql = smem_addr(sm.mat[3]), Kh = smem_addr(sm.mat[1]),
+                 Kl = smem_addr(sm.mat[4]), Vh = smem_addr(sm.mat[2]), Vl = smem_addr(sm.mat[5]);
   float o[4][4];
 #pragma unroll
   for (int n = 0; n < 4; ++n)
@@ -270,9 +312,9 @@ __global__ void __launch_bounds__(kThreads) k_attn_fwd_mma(AttnArgs a) {
   const int q0 = 16 * warp;
   const bool act = warp < NW;
   if (act) {
-    float s[8][4];
+    float s[kNT][4];
 #pragma unroll
-    for (int n = 0; n < 8; ++n)
+    for (int n = 0; n < kNT; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) s[n][e] = 0.f;
 #pragma unroll
@@ -281,7 +323,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_fwd_mma(AttnArgs a) {
       ldsm4(ah, a_addr(Qh, q0, 16 * ks, lane));
       ldsm4(al, a_addr(Ql, q0, 16 * ks, lane));
 #pragma unroll
-      for (int p = 0; p < 4; ++p) {
+      for (int p = 0; p < kW; ++p) {
         if (2 * p < NK8) {
           uint32_t bh[4], bl[4];
           ldsm4(bh, bn_addr(Kh, 16 * p, 16 * ks, lane));
@@ -295,7 +337,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_fwd_mma(AttnArgs a) {
     const float fs = pow2f(-(sm.scale[0] + sm.scale[1])) * (1.0f / sqrtf(static_cast<float>(kHd)));
     float m[2] = {-FLT_MAX, -FLT_MAX};
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
+    for (int n = 0; n < kNT; ++n) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int r = q0 + g + 8 * (e >> 1), c = 8 * n + 2 * tig + (e & 1);
@@ -307,7 +349,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_fwd_mma(AttnArgs a) {
     m[1] = quad_max(m[1]);
     float l[2] = {0.f, 0.f};
 #pragma unroll
-    for (int n = 0; n < 8; ++n)
+    for (int n = 0; n < kNT; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         s[n][e] = s[n][e] == -FLT_MAX ? 0.f : expf(s[n][e] - m[e >> 1]);
@@ -324,12 +366,12 @@ __global__ void __launch_bounds__(kThreads) k_attn_fwd_mma(AttnArgs a) {
     }
     const float inv[2] = {l[0] > 0.f ? 1.0f / l[0] : 0.f, l[1] > 0.f ? 1.0f / l[1] : 0.f};
 #pragma unroll
-    for (int n = 0; n < 8; ++n)
+    for (int n = 0; n < kNT; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) s[n][e] *= inv[e >> 1];
     // O = P V, P at the fixed scale 2^14
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
+    for (int ks = 0; ks < kW; ++ks) {
       if (ks < NW) {
         uint32_t ah[4], al[4];
         c_to_a(s[2 * ks], s[2 * ks + 1], 16384.f, ah, al);
@@ -352,10 +394,10 @@ __global__ void __launch_bounds__(kThreads) k_attn_fwd_mma(AttnArgs a) {
   }
   if (kSplit) {
     cluster_wait();
-    if (act) strip_rowmax(sm.rmax[0], o, q0, S, lane);
+    if (act) strip_rowmax(sm.rmax, o, q0, S, lane);
     cluster_barrier();  // every CTA's maxima have reached every CTA
     if (act)
-      strip_store(o, q0, S, t0, lane, nullptr, 0, h * kHd, &a.out_split, sm.rmax[0], (h * kHd) / 128,
+      strip_store(o, q0, S, t0, lane, nullptr, 0, h * kHd, &a.out_split, sm.rmax, (h * kHd) / 128,
                   cta_rank_in_cluster() == 0);
   }
 }
@@ -363,11 +405,12 @@ __global__ void __launch_bounds__(kThreads) k_attn_fwd_mma(AttnArgs a) {
 // ---- backward --------------------------------------------------------------------
 // Scores and dP of a 16-row strip r0.. against all rows of the other block:
 // s = A1 B1^T, dp = A2 B2^T (A from [rows][32] blocks, B likewise).
-__device__ __forceinline__ void strip_scores(float (&s)[8][4], float (&dp)[8][4], uint32_t a1h, uint32_t a1l,
+template <int NT>
+__device__ __forceinline__ void strip_scores(float (&s)[NT][4], float (&dp)[NT][4], uint32_t a1h, uint32_t a1l,
                                              uint32_t b1h, uint32_t b1l, uint32_t a2h, uint32_t a2l, uint32_t b2h,
                                              uint32_t b2l, int r0, int NK8, int lane) {
 #pragma unroll
-  for (int n = 0; n < 8; ++n)
+  for (int n = 0; n < NT; ++n)
 #pragma unroll
     for (int e = 0; e < 4; ++e) s[n][e] = dp[n][e] = 0.f;
 #pragma unroll
@@ -378,7 +421,7 @@ __device__ __forceinline__ void strip_scores(float (&s)[8][4], float (&dp)[8][4]
     ldsm4(ch, a_addr(a2h, r0, 16 * ks, lane));
     ldsm4(cl, a_addr(a2l, r0, 16 * ks, lane));
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
+    for (int p = 0; p < NT / 2; ++p) {
       if (2 * p < NK8) {
         uint32_t bh[4], bl[4];
         ldsm4(bh, bn_addr(b1h, 16 * p, 16 * ks, lane));
@@ -396,10 +439,11 @@ __device__ __forceinline__ void strip_scores(float (&s)[8][4], float (&dp)[8][4]
 
 // acc (16 x 32) += A (16 x SP, the c-layout tiles x, scale f) times the
 // [SP][32] block B (via ldmatrix.trans).
-__device__ __forceinline__ void strip_times_block(float (&acc)[4][4], const float (&x)[8][4], float f, uint32_t bh_,
+template <int NT>
+__device__ __forceinline__ void strip_times_block(float (&acc)[4][4], const float (&x)[NT][4], float f, uint32_t bh_,
                                                   uint32_t bl_, int NW, int lane) {
 #pragma unroll
-  for (int ks = 0; ks < 4; ++ks) {
+  for (int ks = 0; ks < NT / 2; ++ks) {
     if (ks < NW) {
       uint32_t ah[4], al[4];
       c_to_a(x[2 * ks], x[2 * ks + 1], f, ah, al);
@@ -541,23 +585,30 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma(AttnArgs a) {
 }
 
 // ---- backward for atoms of at most 48 tokens ---------------------------------------
-// Pass 1 (warp = query rows) also leaves P and dS in shared memory in split
-// form (P at 2^14, dS at one scale for the whole item, from a block-wide
-// maximum), and pass 2 (warp = key rows) reads them transposed with
-// ldmatrix.trans as the A operands of dV = P^T dO and dK = dS^T Q instead of
-// recomputing the scores.  48-row blocks keep the footprint at 53 KB.
+// Three warps, one per 16-row strip.  Pass 1 (warp = query rows) computes
+// S, P, dP, D and dS in registers and dQ = dS K; pass 2 (warp = key rows)
+// reads P and then dS back transposed with ldmatrix.trans as the A operands
+// of dV = P^T dO and dK = dS^T Q instead of recomputing the scores.  P and
+// dS (split form, P at 2^14, dS at one scale for the whole item from a
+// block-wide maximum) take turns in the region that held K and V, which are
+// dead once dQ is done, so a CTA needs 32 KB and six fit on an SM.
 constexpr int kMT = 48;
-constexpr int kPitchP = 56;  // halves per P / dS row (112 bytes: conflict-free ldmatrix)
+constexpr int kW48 = kMT / 16;       // warps
+constexpr int kTh48 = 32 * kW48;     // threads
+constexpr int kPitchP = 56;          // halves per P / dS row (112 bytes: conflict-free ldmatrix)
 constexpr int kMatP = kMT * kPitchP;
+constexpr int kMat48 = kMT * kPitch;
 
 struct Smem48 {
-  uint16_t mat[8][kMT * kPitch];  // Q, K, V, dO: hi then lo
-  uint16_t pd[4][kMatP];          // P hi, P lo, dS hi, dS lo ([query][key])
+  uint16_t qg[4][kMat48];         // Q hi, dO hi, Q lo, dO lo
+  uint16_t kv[4 * kMat48];        // K hi, V hi, K lo, V lo; later P or dS: hi [kMatP], lo [kMatP]
   float lse[kMT], mask[kMT];
-  int scale[4];
+  int scale[4];                   // block scale exponents of Q, K, V, dO
+  int gmax;                       // bits of max |dO|
   int dsmax;                      // bits of the item's max |dS|
   int rmax[3][kMT];
 };
+static_assert(4 * kMat48 >= 2 * kMatP, "P / dS fit in the K / V region");
 
 // A operand (16 keys x 16 queries) of a transposed product from a stored
 // [query][key] block: matrices (q0, k0), (q0, k0 + 8), (q0 + 8, k0),
@@ -590,7 +641,7 @@ __device__ __forceinline__ void stored_t_times_block(float (&acc)[4][4], uint32_
 }
 
 // c-layout tiles of a 16-row strip into a stored [row][col] split block
-__device__ __forceinline__ void strip_to_smem(uint16_t *hi, uint16_t *lo, const float (&x)[8][4], int NK8, int r0,
+__device__ __forceinline__ void strip_to_smem(uint16_t *hi, uint16_t *lo, const float (&x)[6][4], int NK8, int r0,
                                               float f, int lane) {
   const int g = lane >> 2, tig = lane & 3;
 #pragma unroll
@@ -609,7 +660,7 @@ __device__ __forceinline__ void strip_to_smem(uint16_t *hi, uint16_t *lo, const 
 }
 
 template <bool kSplit>
-__global__ void __launch_bounds__(kThreads) k_attn_bwd_mma48(AttnArgs a) {
+__global__ void __launch_bounds__(kTh48, 6) k_attn_bwd_mma48(AttnArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   Smem48 &sm = *reinterpret_cast<Smem48 *>(smem_raw);
   const int atom = blockIdx.x, h = blockIdx.y;
@@ -617,15 +668,18 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma48(AttnArgs a) {
   const int e0 = a.offset[atom], S = a.offset[atom + 1] - e0 + 1, t0 = e0 + atom;
   const int NW = (S + 15) >> 4, NK8 = 2 * NW;
   const int d = a.d;
-  {  // Q, K, V, dO into split blocks (warp w: block w, 6 row-chunks per lane)
+  // this warp's block (Q, K or V) in split form
+  uint16_t *const whi = warp == 0 ? sm.qg[0] : sm.kv + (warp - 1) * kMat48;
+  uint16_t *const wlo = warp == 0 ? sm.qg[2] : sm.kv + (warp + 1) * kMat48;
+  float gv[2][8];
+  {  // warp w: block w of Q, K, V (6 row-chunks per lane); all threads: 2 chunks of dO
     float v[6][8];
-    float mx = 0.f;
+    float mx = 0.f, gm = 0.f;
 #pragma unroll
     for (int i = 0; i < 6; ++i) {
       const int task = lane + 32 * i, r = task >> 2, c = (task & 3) * 8;
       if (r < S) {
-        const float *src = warp < 3 ? a.qkv + static_cast<size_t>(t0 + r) * 3 * d + warp * d + h * kHd + c
-                                    : a.d_out + static_cast<size_t>(t0 + r) * d + h * kHd + c;
+        const float *src = a.qkv + static_cast<size_t>(t0 + r) * 3 * d + warp * d + h * kHd + c;
         const float4 x0 = *reinterpret_cast<const float4 *>(src), x1 = *reinterpret_cast<const float4 *>(src + 4);
         v[i][0] = x0.x; v[i][1] = x0.y; v[i][2] = x0.z; v[i][3] = x0.w;
         v[i][4] = x1.x; v[i][5] = x1.y; v[i][6] = x1.z; v[i][7] = x1.w;
@@ -636,6 +690,25 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma48(AttnArgs a) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) mx = fmaxf(mx, fabsf(v[i][k]));
     }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int task = threadIdx.x + kTh48 * i, r = task >> 2, c = (task & 3) * 8;
+      if (r < S) {
+        const float *src = a.d_out + static_cast<size_t>(t0 + r) * d + h * kHd + c;
+        const float4 x0 = *reinterpret_cast<const float4 *>(src), x1 = *reinterpret_cast<const float4 *>(src + 4);
+        gv[i][0] = x0.x; gv[i][1] = x0.y; gv[i][2] = x0.z; gv[i][3] = x0.w;
+        gv[i][4] = x1.x; gv[i][5] = x1.y; gv[i][6] = x1.z; gv[i][7] = x1.w;
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) gv[i][k] = 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) gm = fmaxf(gm, fabsf(gv[i][k]));
+    }
+    if (threadIdx.x == 0) {
+      sm.gmax = 0;
+      sm.dsmax = 0;
+    }
     const int sc = split_scale_exponent(warp_absmax(mx));
     const float f = pow2f(sc);
     if (lane == 0) sm.scale[warp] = sc;
@@ -645,23 +718,37 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma48(AttnArgs a) {
       uint32_t hh[4], ll[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) split2(v[i][2 * k], v[i][2 * k + 1], f, hh[k], ll[k]);
-      *reinterpret_cast<uint4 *>(&sm.mat[warp][r * kPitch + c]) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
-      *reinterpret_cast<uint4 *>(&sm.mat[4 + warp][r * kPitch + c]) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+      *reinterpret_cast<uint4 *>(&whi[r * kPitch + c]) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
+      *reinterpret_cast<uint4 *>(&wlo[r * kPitch + c]) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+    }
+    for (int k = threadIdx.x; k < kMT; k += kTh48) {
+      sm.mask[k] = k < S ? (k == 0 ? 0.f : a.key_mask[e0 + k - 1]) : 0.f;
+      sm.lse[k] = k < S ? a.lse[static_cast<size_t>(t0 + k) * a.heads + h] : 0.f;
+      if (kSplit) sm.rmax[0][k] = sm.rmax[1][k] = sm.rmax[2][k] = 0;
+    }
+    gm = warp_absmax(gm);
+    __syncthreads();  // gmax and dsmax cleared
+    if (lane == 0) atomicMax(&sm.gmax, __float_as_int(gm));
+    __syncthreads();  // max |dO|
+    const int sg = split_scale_exponent(__int_as_float(sm.gmax));
+    const float fg = pow2f(sg);
+    if (threadIdx.x == 0) sm.scale[3] = sg;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int task = threadIdx.x + kTh48 * i, r = task >> 2, c = (task & 3) * 8;
+      uint32_t hh[4], ll[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) split2(gv[i][2 * k], gv[i][2 * k + 1], fg, hh[k], ll[k]);
+      *reinterpret_cast<uint4 *>(&sm.qg[1][r * kPitch + c]) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
+      *reinterpret_cast<uint4 *>(&sm.qg[3][r * kPitch + c]) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
     }
   }
-  for (int k = threadIdx.x; k < kMT; k += kThreads) {
-    sm.mask[k] = k < S ? (k == 0 ? 0.f : a.key_mask[e0 + k - 1]) : 0.f;
-    sm.lse[k] = k < S ? a.lse[static_cast<size_t>(t0 + k) * a.heads + h] : 0.f;
-    if (kSplit) sm.rmax[0][k] = sm.rmax[1][k] = sm.rmax[2][k] = 0;
-  }
-  if (threadIdx.x == 0) sm.dsmax = 0;
-  __syncthreads();
+  __syncthreads();  // every block and scale
   if (kSplit) cluster_arrive();
-  const uint32_t Qh = smem_addr(sm.mat[0]), Ql = smem_addr(sm.mat[4]), Kh = smem_addr(sm.mat[1]),
-                 Kl = smem_addr(sm.mat[5]), Vh = smem_addr(sm.mat[2]), Vl = smem_addr(sm.mat[6]),
-                 Gh = smem_addr(sm.mat[3]), Gl = smem_addr(sm.mat[7]);
-  const uint32_t Ph = smem_addr(sm.pd[0]), Pl = smem_addr(sm.pd[1]), Dh = smem_addr(sm.pd[2]),
-                 Dl = smem_addr(sm.pd[3]);
+  const uint32_t Qh = smem_addr(sm.qg[0]), Ql = smem_addr(sm.qg[2]), Gh = smem_addr(sm.qg[1]),
+                 Gl = smem_addr(sm.qg[3]), Kh = smem_addr(sm.kv), Vh = smem_addr(sm.kv + kMat48),
+                 Kl = smem_addr(sm.kv + 2 * kMat48), Vl = smem_addr(sm.kv + 3 * kMat48);
+  const uint32_t Xh = smem_addr(sm.kv), Xl = smem_addr(sm.kv + kMatP);  // P or dS, after K and V
   const float rs = 1.0f / sqrtf(static_cast<float>(kHd));
   const float fs = pow2f(-(sm.scale[0] + sm.scale[1])) * rs;
   const float fdp = pow2f(-(sm.scale[3] + sm.scale[2]));
@@ -673,14 +760,14 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma48(AttnArgs a) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) dq[n][e] = dk[n][e] = dv[n][e] = 0.f;
 
-  // ---- pass 1: warp = query rows; P and dS to shared memory, dQ ----
-  float s[8][4], dp[8][4];
+  // ---- pass 1: warp = query rows: P, dS and dQ in registers ----
+  float s[6][4], dp[6][4];
   if (act) {
     strip_scores(s, dp, Qh, Ql, Kh, Kl, Gh, Gl, Vh, Vl, r0, NK8, lane);
     float Dp[2] = {0.f, 0.f};
     const float lq[2] = {sm.lse[r0 + g], sm.lse[r0 + g + 8]};
 #pragma unroll
-    for (int n = 0; n < 8; ++n)
+    for (int n = 0; n < 6; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int r = r0 + g + 8 * (e >> 1), c = 8 * n + 2 * tig + (e & 1);
@@ -693,7 +780,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma48(AttnArgs a) {
     Dp[1] = quad_sum(Dp[1]);
     float mx = 0.f;
 #pragma unroll
-    for (int n = 0; n < 8; ++n)
+    for (int n = 0; n < 6; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         dp[n][e] = s[n][e] * (dp[n][e] - Dp[e >> 1]);  // dS
@@ -701,12 +788,10 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma48(AttnArgs a) {
       }
     mx = warp_absmax(mx);
     if (lane == 0) atomicMax(&sm.dsmax, __float_as_int(mx));
-    strip_to_smem(sm.pd[0], sm.pd[1], s, NK8, r0, 16384.f, lane);
   }
   __syncthreads();  // the item's max |dS|
   const int sd = split_scale_exponent(__int_as_float(sm.dsmax));
   if (act) {
-    strip_to_smem(sm.pd[2], sm.pd[3], dp, NK8, r0, pow2f(sd), lane);
     strip_times_block(dq, dp, pow2f(sd), Kh, Kl, NW, lane);
     const float fq = pow2f(-(sd + sm.scale[1])) * rs;
 #pragma unroll
@@ -714,12 +799,17 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma48(AttnArgs a) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) dq[n][e] *= fq;
   }
-  __syncthreads();  // P and dS of every query row
+  __syncthreads();  // K and V are no longer read
+  if (act) strip_to_smem(sm.kv, sm.kv + kMatP, s, NK8, r0, 16384.f, lane);
+  __syncthreads();  // P of every query row
 
-  // ---- pass 2: warp = key rows r0..r0+15: dV = P^T dO, dK = dS^T Q ----
+  // ---- pass 2: warp = key rows r0..r0+15: dV = P^T dO, then dK = dS^T Q ----
+  if (act) stored_t_times_block(dv, Xh, Xl, r0, Gh, Gl, NW, lane);
+  __syncthreads();  // P is no longer read
+  if (act) strip_to_smem(sm.kv, sm.kv + kMatP, dp, NK8, r0, pow2f(sd), lane);
+  __syncthreads();  // dS of every query row
   if (act) {
-    stored_t_times_block(dv, Ph, Pl, r0, Gh, Gl, NW, lane);
-    stored_t_times_block(dk, Dh, Dl, r0, Qh, Ql, NW, lane);
+    stored_t_times_block(dk, Xh, Xl, r0, Qh, Ql, NW, lane);
     const float fv = pow2f(-(14 + sm.scale[3])), fk = pow2f(-(sd + sm.scale[0])) * rs;
 #pragma unroll
     for (int n = 0; n < 4; ++n)
@@ -756,13 +846,23 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma48(AttnArgs a) {
 
 template <bool kSplit>
 void launch_mma(const AttnArgs &a, bool bwd, cudaStream_t s) {
-  const bool small = bwd && a.max_tokens <= kMT;
-  const size_t smem = small ? sizeof(Smem48) : sizeof(Smem);
-  void (*fn)(AttnArgs) = small ? k_attn_bwd_mma48<kSplit> : bwd ? k_attn_bwd_mma<kSplit> : k_attn_fwd_mma<kSplit>;
+  const bool small = a.max_tokens <= kMT;
+  size_t smem;
+  int threads = kThreads;
+  void (*fn)(AttnArgs);
+  if (bwd) {
+    smem = small ? sizeof(Smem48) : sizeof(Smem);
+    threads = small ? kTh48 : kThreads;
+    fn = small ? k_attn_bwd_mma48<kSplit> : k_attn_bwd_mma<kSplit>;
+  } else {
+    smem = small ? sizeof(SmemF<kMT>) : sizeof(SmemF<kMaxTok>);
+    threads = small ? 2 * kMT : 2 * kMaxTok;
+    fn = small ? k_attn_fwd_mma<kSplit, kMT> : k_attn_fwd_mma<kSplit, kMaxTok>;
+  }
   CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.n_atoms, a.heads);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];

@@ -312,8 +312,7 @@ void PETModel::load(const std::string &path, float cutoff_override) {
   {
     const char *at = std::getenv("MLIPCPP_B200_ATTN");
     use_attn_tc_ = at && std::string(at) == "tc";
-    use_attn_rows_ = at && std::string(at) == "rows";
-    use_attn_mma_fwd_ = at && std::string(at) == "mma";
+    use_attn_rows_ = at && (std::string(at) == "rows" || std::string(at) == "simt");
   }
   {
     // chain mode: every dense layer's K and N a multiple of 128 (K <= 2048),
@@ -560,7 +559,7 @@ void PETModel::forward_backward(bool grad) {
   auto attn = [&](bool backward, const AttnArgs &x) {
     cudaEvent_t e0 = nullptr;
     if (kprof_) mark_begin(e0);
-    if (!use_attn_rows_ && (backward || use_attn_mma_fwd_) && attention_mma_supported(x, backward))
+    if (!use_attn_rows_ && !(use_attn_tc_ && !backward) && attention_mma_supported(x, backward))
       attention_mma(x, backward, s);
     else if (backward) attention_bwd(x, s);
     else if (use_attn_tc_ && attention_tc_supported(x)) attention_fwd_tc(x, d_err_.as<int>(), s);

@@ -137,11 +137,10 @@ class PETModel {
   // tensor-core attention forward (MLIPCPP_B200_ATTN=tc): correct, but slower
   // than the SIMT kernel at this size (see attention_tc.cu)
   bool use_attn_tc_ = false;
-  // attention kernels: the backward runs on the tensor-core kernel of
-  // attention_mma.cu where it applies, the forward on the SIMT kernel (the
-  // faster of the two at 16 heads of 32 and ~40 tokens);
-  // MLIPCPP_B200_ATTN=rows: SIMT for both, =mma: tensor cores for both
-  bool use_attn_rows_ = false, use_attn_mma_fwd_ = false;
+  // attention kernels: forward and backward on the tensor-core kernels of
+  // attention_mma.cu where they apply (head size 32, up to 64 tokens), else
+  // on the SIMT kernels; MLIPCPP_B200_ATTN=rows (or simt): SIMT for both
+  bool use_attn_rows_ = false;
   // MLIPCPP_PRECISION_F16: dense layers with the hi x hi product only
   bool reduced_ = false;
   // non-conservative heads in the file / run in the current prediction

@@ -191,8 +191,9 @@ def test_gpu_tensor_core_attention_matches_simt(model_file, monkeypatch):
     ("pet-mad-s", lambda: [wl.water_box(192, seed=14)], {}),                     # split outputs
     ("pet-mad-s", lambda: [wl.si_diamond(2, seed=14)], {"MLIPCPP_B200_CHAIN": "0"}),  # fp32 outputs
     ("pet-mad-s", lambda: wl.molecules(4, seed=14, n_min=2, n_max=60), {}),      # ragged, up to 60 tokens
+    ("pet-mad-s", lambda: wl.molecules(6, seed=16, n_min=2, n_max=40), {}),      # ragged, 48-token kernels
     ("pet-mad-s", lambda: [wl.water_box(192, seed=15)], {"_cutoff": 6.5}),       # > 64 tokens: SIMT kernels
-], ids=["oaml_fcc216", "mads_water192", "mads_si64_fp32", "mads_molecules", "mads_wide"])
+], ids=["oaml_fcc216", "mads_water192", "mads_si64_fp32", "mads_molecules", "mads_molecules48", "mads_wide"])
 def test_gpu_mma_attention_matches_simt(hname, make, env, model_file, monkeypatch):
     """The tensor-core attention (register-resident split-fp16 mma.sync,
     forward and backward) and the SIMT thread-per-row kernels agree within
@@ -206,7 +207,7 @@ def test_gpu_mma_attention_matches_simt(hname, make, env, model_file, monkeypatc
         monkeypatch.setenv(k, v)
     monkeypatch.setenv("MLIPCPP_B200_ATTN", "rows")
     ref = mb.Predictor(path).predict_batch(systems, compute_stress=True)
-    monkeypatch.setenv("MLIPCPP_B200_ATTN", "mma")  # tensor-core forward too
+    monkeypatch.delenv("MLIPCPP_B200_ATTN")  # default: tensor-core forward and backward
     pred = mb.Predictor(path)
     res = pred.predict_batch(systems, compute_stress=True)
     for s, r, q in zip(systems, res, ref):
