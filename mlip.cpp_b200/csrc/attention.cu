@@ -375,9 +375,11 @@ namespace {
 
 constexpr float kLnEps = 1e-5f;
 
+// stats: the row's mean at stats[row], 1 / sd at stats[rows + row]; the
+// backward recomputes xhat = (x - mean) / sd from x and these.
 __global__ void k_ln_fwd(const float *__restrict__ x, const float *__restrict__ g,
                          const float *__restrict__ b, float *__restrict__ y,
-                         float *__restrict__ xhat, float *__restrict__ rstd, int rows, int d) {
+                         float *__restrict__ stats, int rows, int d) {
   const int lane = threadIdx.x & 31;
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (row >= rows) return;
@@ -392,37 +394,35 @@ __global__ void k_ln_fwd(const float *__restrict__ x, const float *__restrict__ 
     v = fmaf(t, t, v);
   }
   const float var = warp_sum(v) * inv_d;
-  const float sd = sqrtf(var * (1.0f + kLnEps));
+  const float r = 1.0f / sqrtf(var * (1.0f + kLnEps));
   float *yr = y + static_cast<size_t>(row) * d;
-  float *hr = xhat + static_cast<size_t>(row) * d;
-  for (int c = lane; c < d; c += 32) {
-    const float h = (xr[c] - mean) / sd;
-    hr[c] = h;
-    yr[c] = h * g[c] + b[c];
+  for (int c = lane; c < d; c += 32) yr[c] = (xr[c] - mean) * r * g[c] + b[c];
+  if (lane == 0) {
+    stats[row] = mean;
+    stats[rows + row] = r;
   }
-  if (lane == 0) rstd[row] = 1.0f / sd;
 }
 
-__global__ void k_ln_bwd(const float *__restrict__ dy, const float *__restrict__ xhat,
-                         const float *__restrict__ rstd, const float *__restrict__ g,
+__global__ void k_ln_bwd(const float *__restrict__ dy, const float *__restrict__ x,
+                         const float *__restrict__ stats, const float *__restrict__ g,
                          float *__restrict__ dx, int rows, int d) {
   const int lane = threadIdx.x & 31;
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (row >= rows) return;
   const float *dyr = dy + static_cast<size_t>(row) * d;
-  const float *hr = xhat + static_cast<size_t>(row) * d;
+  const float *xr = x + static_cast<size_t>(row) * d;
+  const float mean = stats[row], r = stats[rows + row];
   float s1 = 0.f, s2 = 0.f;
   for (int c = lane; c < d; c += 32) {
     const float gh = dyr[c] * g[c];
     s1 += gh;
-    s2 = fmaf(gh, hr[c], s2);
+    s2 = fmaf(gh, (xr[c] - mean) * r, s2);
   }
   const float inv_d = 1.0f / static_cast<float>(d);
   const float m1 = warp_sum(s1) * inv_d;
   const float m2 = warp_sum(s2) * inv_d * (1.0f + kLnEps);
-  const float r = rstd[row];
   float *dxr = dx + static_cast<size_t>(row) * d;
-  for (int c = lane; c < d; c += 32) dxr[c] = r * (dyr[c] * g[c] - m1 - hr[c] * m2);
+  for (int c = lane; c < d; c += 32) dxr[c] = r * (dyr[c] * g[c] - m1 - (xr[c] - mean) * r * m2);
 }
 
 // Rows of d = 128 nb columns: lane l holds float4 columns 128 b + 4 l, so
@@ -430,7 +430,7 @@ __global__ void k_ln_bwd(const float *__restrict__ dy, const float *__restrict__
 template <int NB>
 __global__ void k_ln_fwd4(const float *__restrict__ x, const float *__restrict__ g,
                           const float *__restrict__ b, float *__restrict__ y,
-                          float *__restrict__ xhat, float *__restrict__ rstd, int rows, Split16View ys) {
+                          float *__restrict__ stats, int rows, Split16View ys) {
   constexpr int d = 128 * NB;
   const int lane = threadIdx.x & 31;
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -452,34 +452,36 @@ __global__ void k_ln_fwd4(const float *__restrict__ x, const float *__restrict__
     q = fmaf(t0, t0, q); q = fmaf(t1, t1, q); q = fmaf(t2, t2, q); q = fmaf(t3, t3, q);
   }
   const float var = warp_sum(q) * inv_d;
-  const float sd = sqrtf(var * (1.0f + kLnEps));
+  const float r = 1.0f / sqrtf(var * (1.0f + kLnEps));
   float *yr = y ? y + static_cast<size_t>(row) * d : nullptr;  // y null: split output only
-  float *hr = xhat + static_cast<size_t>(row) * d;
 #pragma unroll
   for (int k = 0; k < NB; ++k) {
     const int c = 128 * k + 4 * lane;
     const float4 gg = __ldg(reinterpret_cast<const float4 *>(g + c));
     const float4 bb = __ldg(reinterpret_cast<const float4 *>(b + c));
-    const float4 h = make_float4((v[k].x - mean) / sd, (v[k].y - mean) / sd, (v[k].z - mean) / sd,
-                                 (v[k].w - mean) / sd);
+    const float4 h = make_float4((v[k].x - mean) * r, (v[k].y - mean) * r, (v[k].z - mean) * r,
+                                 (v[k].w - mean) * r);
     const float4 o = make_float4(h.x * gg.x + bb.x, h.y * gg.y + bb.y, h.z * gg.z + bb.z, h.w * gg.w + bb.w);
-    *reinterpret_cast<float4 *>(hr + c) = h;
     if (yr) *reinterpret_cast<float4 *>(yr + c) = o;
     if (ys.hi) warp_split_block(ys, row, k, o, lane);
   }
-  if (lane == 0) rstd[row] = 1.0f / sd;
+  if (lane == 0) {
+    stats[row] = mean;
+    stats[rows + row] = r;
+  }
 }
 
 template <int NB>
-__global__ void k_ln_bwd4(const float *__restrict__ dy, const float *__restrict__ xhat,
-                          const float *__restrict__ rstd, const float *__restrict__ g,
+__global__ void k_ln_bwd4(const float *__restrict__ dy, const float *__restrict__ x,
+                          const float *__restrict__ stats, const float *__restrict__ g,
                           float *__restrict__ dx, int rows, Split16View dxs) {
   constexpr int d = 128 * NB;
   const int lane = threadIdx.x & 31;
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (row >= rows) return;
   const float *dyr = dy + static_cast<size_t>(row) * d;
-  const float *hr = xhat + static_cast<size_t>(row) * d;
+  const float *xr = x + static_cast<size_t>(row) * d;
+  const float mean = stats[row], r = stats[rows + row];
   float4 gh[NB], hh[NB];
   float s1 = 0.f, s2 = 0.f;
 #pragma unroll
@@ -487,7 +489,8 @@ __global__ void k_ln_bwd4(const float *__restrict__ dy, const float *__restrict_
     const int c = 128 * k + 4 * lane;
     const float4 a = *reinterpret_cast<const float4 *>(dyr + c);
     const float4 gg = __ldg(reinterpret_cast<const float4 *>(g + c));
-    hh[k] = *reinterpret_cast<const float4 *>(hr + c);
+    const float4 xv = *reinterpret_cast<const float4 *>(xr + c);
+    hh[k] = make_float4((xv.x - mean) * r, (xv.y - mean) * r, (xv.z - mean) * r, (xv.w - mean) * r);
     gh[k] = make_float4(a.x * gg.x, a.y * gg.y, a.z * gg.z, a.w * gg.w);
     s1 += (gh[k].x + gh[k].y) + (gh[k].z + gh[k].w);
     s2 = fmaf(gh[k].x, hh[k].x, s2); s2 = fmaf(gh[k].y, hh[k].y, s2);
@@ -496,7 +499,6 @@ __global__ void k_ln_bwd4(const float *__restrict__ dy, const float *__restrict_
   const float inv_d = 1.0f / static_cast<float>(d);
   const float m1 = warp_sum(s1) * inv_d;
   const float m2 = warp_sum(s2) * inv_d * (1.0f + kLnEps);
-  const float r = rstd[row];
   float *dxr = dx ? dx + static_cast<size_t>(row) * d : nullptr;  // dx null: split output only
 #pragma unroll
   for (int k = 0; k < NB; ++k) {
@@ -510,38 +512,38 @@ __global__ void k_ln_bwd4(const float *__restrict__ dy, const float *__restrict_
 
 }  // namespace
 
-void layer_norm_fwd(const float *x, const float *g, const float *b, float *y, float *xhat,
-                    float *rstd, int rows, int d, cudaStream_t s, const Split16View *ys) {
+void layer_norm_fwd(const float *x, const float *g, const float *b, float *y, float *stats, int rows, int d,
+                    cudaStream_t s, const Split16View *ys) {
   if (rows <= 0) return;
   const int grid = ceil_div(static_cast<int64_t>(rows) * 32, 256);
   const Split16View none{};
   const Split16View &o = ys ? *ys : none;
   switch (d % 128 == 0 ? d / 128 : 0) {
-    case 1: k_ln_fwd4<1><<<grid, 256, 0, s>>>(x, g, b, y, xhat, rstd, rows, o); break;
-    case 2: k_ln_fwd4<2><<<grid, 256, 0, s>>>(x, g, b, y, xhat, rstd, rows, o); break;
-    case 4: k_ln_fwd4<4><<<grid, 256, 0, s>>>(x, g, b, y, xhat, rstd, rows, o); break;
-    case 8: k_ln_fwd4<8><<<grid, 256, 0, s>>>(x, g, b, y, xhat, rstd, rows, o); break;
+    case 1: k_ln_fwd4<1><<<grid, 256, 0, s>>>(x, g, b, y, stats, rows, o); break;
+    case 2: k_ln_fwd4<2><<<grid, 256, 0, s>>>(x, g, b, y, stats, rows, o); break;
+    case 4: k_ln_fwd4<4><<<grid, 256, 0, s>>>(x, g, b, y, stats, rows, o); break;
+    case 8: k_ln_fwd4<8><<<grid, 256, 0, s>>>(x, g, b, y, stats, rows, o); break;
     default:
       if (ys) throw Error(kErrInternal, "layer_norm_fwd: split output needs d in {128, 256, 512, 1024}");
-      k_ln_fwd<<<grid, 256, 0, s>>>(x, g, b, y, xhat, rstd, rows, d);
+      k_ln_fwd<<<grid, 256, 0, s>>>(x, g, b, y, stats, rows, d);
   }
   CUDA_LAUNCH_CHECK();
 }
 
-void layer_norm_bwd(const float *dy, const float *xhat, const float *rstd, const float *g,
-                    float *dx, int rows, int d, cudaStream_t s, const Split16View *dxs) {
+void layer_norm_bwd(const float *dy, const float *x, const float *stats, const float *g, float *dx, int rows, int d,
+                    cudaStream_t s, const Split16View *dxs) {
   if (rows <= 0) return;
   const int grid = ceil_div(static_cast<int64_t>(rows) * 32, 256);
   const Split16View none{};
   const Split16View &o = dxs ? *dxs : none;
   switch (d % 128 == 0 ? d / 128 : 0) {
-    case 1: k_ln_bwd4<1><<<grid, 256, 0, s>>>(dy, xhat, rstd, g, dx, rows, o); break;
-    case 2: k_ln_bwd4<2><<<grid, 256, 0, s>>>(dy, xhat, rstd, g, dx, rows, o); break;
-    case 4: k_ln_bwd4<4><<<grid, 256, 0, s>>>(dy, xhat, rstd, g, dx, rows, o); break;
-    case 8: k_ln_bwd4<8><<<grid, 256, 0, s>>>(dy, xhat, rstd, g, dx, rows, o); break;
+    case 1: k_ln_bwd4<1><<<grid, 256, 0, s>>>(dy, x, stats, g, dx, rows, o); break;
+    case 2: k_ln_bwd4<2><<<grid, 256, 0, s>>>(dy, x, stats, g, dx, rows, o); break;
+    case 4: k_ln_bwd4<4><<<grid, 256, 0, s>>>(dy, x, stats, g, dx, rows, o); break;
+    case 8: k_ln_bwd4<8><<<grid, 256, 0, s>>>(dy, x, stats, g, dx, rows, o); break;
     default:
       if (dxs) throw Error(kErrInternal, "layer_norm_bwd: split output needs d in {128, 256, 512, 1024}");
-      k_ln_bwd<<<grid, 256, 0, s>>>(dy, xhat, rstd, g, dx, rows, d);
+      k_ln_bwd<<<grid, 256, 0, s>>>(dy, x, stats, g, dx, rows, d);
   }
   CUDA_LAUNCH_CHECK();
 }

@@ -92,12 +92,15 @@ int attention_split_max_tokens(int hd);
 
 // ---- row-wise ops ---------------------------------------------------------
 // y = (x - mean) / sqrt(var * (1 + eps)) * g + b  (pet_layers.cpp:85-145);
-// ys: also write y in split-fp16 form (d a multiple of 128, at most 1024)
-void layer_norm_fwd(const float *x, const float *g, const float *b, float *y, float *xhat,
-                    float *rstd, int rows, int d, cudaStream_t stream, const Split16View *ys = nullptr);
-// dx = rstd (dxhat - mean(dxhat) - (1 + eps) xhat mean(dxhat xhat)), dxhat = dy g;
-// dxs: also write dx in split-fp16 form
-void layer_norm_bwd(const float *dy, const float *xhat, const float *rstd, const float *g,
-                    float *dx, int rows, int d, cudaStream_t stream, const Split16View *dxs = nullptr);
+// stats [2 rows]: each row's mean, then its 1 / sqrt(var (1 + eps)); y may be
+// null when ys is given; ys: also write y in split-fp16 form (d a multiple
+// of 128, at most 1024)
+void layer_norm_fwd(const float *x, const float *g, const float *b, float *y, float *stats, int rows, int d,
+                    cudaStream_t stream, const Split16View *ys = nullptr);
+// dx = rstd (dxhat - mean(dxhat) - (1 + eps) xhat mean(dxhat xhat)), dxhat = dy g,
+// with xhat = (x - mean) rstd recomputed from the forward's input x and its
+// stats; dxs: also write dx in split-fp16 form
+void layer_norm_bwd(const float *dy, const float *x, const float *stats, const float *g, float *dx, int rows, int d,
+                    cudaStream_t stream, const Split16View *dxs = nullptr);
 
 }  // namespace pet

@@ -73,7 +73,7 @@ struct Acts {
   // non-conservative outputs per atom: forces [N1, 3], stress [N1, 9]
   float *ncF, *ncS;
   // forward scratch
-  float *cat, *hc, *xin, *xmid, *xl[2], *o, *u, *x1, *hf, *u2, *yn1, *yn2, *ye1, *ye2, *node_pred,
+  float *cat, *hc, *xin, *xmid, *xl[2], *o, *x1, *hf, *yn1, *yn2, *ye1, *ye2, *node_pred,
       *edge_pred;
   // backward scratch
   float *dx, *dx2, *du, *dout, *dqkv, *dx1, *dhf, *dz1, *dz2, *dzc, *demb, *dmsg, *g4, *g, *F;
@@ -444,9 +444,11 @@ static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, const Counts
     const size_t T = b < 2 ? T0 : T1;
     a.qkv[b] = P.take<float>(T * 3 * d);
     a.lse[b] = P.take<float>(T * h.heads);
-    a.xa[b] = P.take<float>(T * d); a.ra[b] = P.take<float>(T);
+    // LN inputs (the residual sums) and their per-row mean and 1 / sd,
+    // from which the backward recomputes the normalised rows
+    a.xa[b] = P.take<float>(T * d); a.ra[b] = P.take<float>(2 * T);
     a.zf[b] = P.take<float>(T * f);
-    a.xm[b] = P.take<float>(T * d); a.rm[b] = P.take<float>(T);
+    a.xm[b] = P.take<float>(T * d); a.rm[b] = P.take<float>(2 * T);
   }
   for (int l = 0; l < 2; ++l) {
     a.zc[l] = P.take<float>((l == 0 ? E0 : E1) * H);
@@ -468,8 +470,8 @@ static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, const Counts
   a.cat = ftake(fs, E0 * 3 * d); a.hc = ftake(fs, E0 * H);
   a.xin = fs.take<float>(T0 * d); a.xmid = fs.take<float>(T0 * d);
   a.xl[0] = fs.take<float>(T0 * d); a.xl[1] = fs.take<float>(T1 * d);
-  a.o = ftake(fs, T0 * d); a.u = fs.take<float>(T0 * d); a.x1 = fs.take<float>(T0 * d);
-  a.hf = ftake(fs, T0 * f); a.u2 = fs.take<float>(T0 * d);
+  a.o = ftake(fs, T0 * d); a.x1 = fs.take<float>(T0 * d);
+  a.hf = ftake(fs, T0 * f);
   a.yn1 = ftake(fs, N1 * r); a.yn2 = fs.take<float>(N1 * r);
   a.ye1 = ftake(fs, E1 * r); a.ye2 = fs.take<float>(E1 * r);
   a.node_pred = fs.take<float>(N1); a.edge_pred = fs.take<float>(E1);
@@ -593,18 +595,18 @@ void PETModel::forward_backward(bool grad) {
     at.out_split = Split16View{};
     // in chain mode the residuals come from the split forms, so the fp32
     // block input and x1 are not written at all
-    gemm(a.o, d, nullptr, B.Wout, d, a.u, d, nullptr, T, d, d, B.bout, EPI_RESID, s, nullptr, 0, ch ? nullptr : x, d,
+    gemm(a.o, d, nullptr, B.Wout, d, a.xa[b], d, nullptr, T, d, d, B.bout, EPI_RESID, s, nullptr, 0, ch ? nullptr : x, d,
          SplitIO{ch ? &so : nullptr, true, nullptr, ch ? sx : nullptr});
     if (ch) sx1 = take_split(T, d);
-    layer_norm_fwd(a.u, B.ga, B.ba, ch ? nullptr : a.x1, a.xa[b], a.ra[b], T, d, s, ch ? &sx1 : nullptr);
+    layer_norm_fwd(a.xa[b], B.ga, B.ba, ch ? nullptr : a.x1, a.ra[b], T, d, s, ch ? &sx1 : nullptr);
     if (ch) shf = take_split(T, f);
     gemm(a.x1, d, nullptr, B.W0, d, a.hf, f, nullptr, T, f, d, B.b0, EPI_SILU, s, keep(a.zf[b]), f, nullptr, 0,
          SplitIO{ch ? &sx1 : nullptr, true, ch ? &shf : nullptr});
-    gemm(a.hf, f, nullptr, B.W3, f, a.u2, d, nullptr, T, d, f, B.b3, EPI_RESID, s, nullptr, 0, ch ? nullptr : a.x1, d,
+    gemm(a.hf, f, nullptr, B.W3, f, a.xm[b], d, nullptr, T, d, f, B.b3, EPI_RESID, s, nullptr, 0, ch ? nullptr : a.x1, d,
          SplitIO{ch ? &shf : nullptr, true, nullptr, ch ? &sx1 : nullptr});
     if (ch && sout) *sout = take_split(T, d);
     // a block output with a split form feeds only the next block: no fp32 copy
-    layer_norm_fwd(a.u2, B.gm, B.bm, (ch && sout) ? nullptr : out, a.xm[b], a.rm[b], T, d, s, ch ? sout : nullptr);
+    layer_norm_fwd(a.xm[b], B.gm, B.bm, (ch && sout) ? nullptr : out, a.rm[b], T, d, s, ch ? sout : nullptr);
   };
   // Energy head (node or edge) on rows `rows` of the layer output.
   auto head_fwd = [&](const float *x, const int *rows, int M, const HeadW &hw, float *y1, float *y2, float *z1,
