@@ -57,6 +57,10 @@ struct PropW {
 };
 struct LayerW {
   const float *We, *be, *node_emb, *nbr_emb, *C0, *c0, *C2, *c2, *C0T, *C2T;
+  // compress.0 with the edge and neighbour-species embeddings folded in
+  // ([hid][featurised columns], bias included) and its x, y, z, r columns
+  // as [hid][4] for the backward
+  const float *C0f, *C0xyzr;
   BlockW blk[2];
   HeadW node, edge;
   PropW nc[2];  // non-conservative heads: [0] forces (od 3), [1] stress (od 9)
@@ -76,7 +80,7 @@ struct Acts {
   float *cat, *hc, *xin, *xmid, *xl[2], *o, *x1, *hf, *yn1, *yn2, *ye1, *ye2, *node_pred,
       *edge_pred;
   // backward scratch
-  float *dx, *dx2, *du, *dout, *dqkv, *dx1, *dhf, *dz1, *dz2, *dzc, *demb, *dmsg, *g4, *g, *F;
+  float *dx, *dx2, *du, *dout, *dqkv, *dx1, *dhf, *dz1, *dz2, *dzc, *dmsg, *g4, *g, *F;
 };
 
 
@@ -266,6 +270,58 @@ void PETModel::load(const std::string &path, float cutoff_override) {
       transpose_of(hp + "2.weight");
     }
   }
+  // Fused compress.0 weights.  The reference feeds compress.0 the
+  // concatenation [W_e (x y z r) + b_e | table[nbr species] | message]
+  // (pet_layers.cpp:151-217, 685-796); the first two parts are linear in
+  // per-edge data that has 5 + (table rows) degrees of freedom, so their
+  // products with compress.0 are computed here once, in double precision:
+  //   fused[:, msg]     = C0[:, 2d:3d]                           (layer 1)
+  //   fused[:, x y z r] = C0[:, 0:d] W_e
+  //   fused[:, 1]       = C0[:, 0:d] b_e + c0
+  //   fused[:, 5 + s]   = C0[:, d:2d] table[s]
+  // and the featuriser writes rows [msg | x y z r 1 one-hot(s) 0...].
+  {
+    const GGUFTensor *e0t = f.tensor("model.embedding.weight");
+    const int64_t d = h.d, H = h.hid, n_tab = e0t->ne[1];
+    h.aux = static_cast<int>((5 + n_tab + 127) / 128 * 128);
+    auto data = [&](const std::string &name, int64_t numel) {
+      const GGUFTensor *t = f.tensor(name);
+      if (!t || t->type != 0 || static_cast<int64_t>(t->numel()) != numel)
+        throw Error(kErrIO, "Required tensor '" + name + "' not found or of an unexpected shape");
+      return reinterpret_cast<const float *>(t->data.data());
+    };
+    const float *emb0 = data("model.embedding.weight", n_tab * d);
+    for (int l = 0; l < 2; ++l) {
+      const std::string p = "model.gnn." + std::to_string(l) + ".";
+      const int64_t Kin = (l == 0 ? 2 : 3) * d, K = (l == 0 ? 0 : d) + h.aux;
+      const float *C0 = data(p + "compress.0.weight", H * Kin), *c0 = data(p + "compress.0.bias", H);
+      const float *We = data(p + "edge_embedder.weight", 4 * d), *be = data(p + "edge_embedder.bias", d);
+      const float *tab = l == 0 ? emb0 : data(p + "neighbor_embedder.weight", n_tab * d);
+      std::vector<float> fw(H * K, 0.0f), px(H * 4);
+      for (int64_t o = 0; o < H; ++o) {
+        const float *row = C0 + o * Kin;
+        float *dst = fw.data() + o * K;
+        if (l > 0)
+          for (int64_t c = 0; c < d; ++c) dst[c] = row[2 * d + c];
+        float *aux = dst + (l == 0 ? 0 : d);
+        for (int j = 0; j < 4; ++j) {
+          double acc = 0.0;
+          for (int64_t c = 0; c < d; ++c) acc += static_cast<double>(row[c]) * We[4 * c + j];
+          aux[j] = px[4 * o + j] = static_cast<float>(acc);
+        }
+        double bias = c0[o];
+        for (int64_t c = 0; c < d; ++c) bias += static_cast<double>(row[c]) * be[c];
+        aux[4] = static_cast<float>(bias);
+        for (int64_t sidx = 0; sidx < n_tab; ++sidx) {
+          double acc = 0.0;
+          for (int64_t c = 0; c < d; ++c) acc += static_cast<double>(row[d + c]) * tab[sidx * d + c];
+          aux[5 + sidx] = static_cast<float>(acc);
+        }
+      }
+      host.emplace_back(p + "compress.0.fused", std::move(fw));
+      host.emplace_back(p + "compress.0.xyzr", std::move(px));
+    }
+  }
   // One arena holding five copies with identical element layout: fp32, its
   // tf32 truncation (hi) and the remainder (lo), then fp16 hi = rn(w 2^s)
   // and lo = rn(w 2^s - hi) with one power-of-two scale s per tensor, so the
@@ -355,6 +411,8 @@ void PETModel::load(const std::string &path, float cutoff_override) {
     L.C2 = w(p + "compress.2.weight");
     L.c2 = w(p + "compress.2.bias");
     L.C0T = w(p + "compress.0.weight.T");
+    L.C0f = w(p + "compress.0.fused");
+    L.C0xyzr = w(p + "compress.0.xyzr");
     L.C2T = w(p + "compress.2.weight.T");
     for (int t = 0; t < 2; ++t) {
       const std::string q = p + "tl." + std::to_string(t) + ".";
@@ -467,7 +525,7 @@ static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, const Counts
   // chain mode keeps GEMM-only operands (cat, hc, o, hf, yn1, ye1; dqkv,
   // dhf, dzc, dz1, dz2) in the split buffers alone
   auto ftake = [&](Plan &pl, size_t n) -> float * { return chain ? nullptr : pl.take<float>(n); };
-  a.cat = ftake(fs, E0 * 3 * d); a.hc = ftake(fs, E0 * H);
+  a.cat = ftake(fs, E0 * featurize_cols(1, h.d, h.aux)); a.hc = ftake(fs, E0 * H);
   a.xin = fs.take<float>(T0 * d); a.xmid = fs.take<float>(T0 * d);
   a.xl[0] = fs.take<float>(T0 * d); a.xl[1] = fs.take<float>(T1 * d);
   a.o = ftake(fs, T0 * d); a.x1 = fs.take<float>(T0 * d);
@@ -484,7 +542,7 @@ static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, const Counts
     a.dhf = ftake(bs, T0 * f);
     const size_t rows = std::max(N1, E1);
     a.dz1 = ftake(bs, rows * r); a.dz2 = ftake(bs, rows * r);
-    a.dzc = ftake(bs, E0 * H); a.demb = bs.take<float>(E0 * d); a.dmsg = bs.take<float>(E1 * d);
+    a.dzc = ftake(bs, E0 * H); a.dmsg = bs.take<float>(E1 * d);
   }
   S.off = std::max(fwd_end, bs.off);
 }
@@ -627,7 +685,7 @@ void PETModel::forward_backward(bool grad) {
   if (ncs_) CUDA_CHECK(cudaMemsetAsync(a.ncS, 0, sizeof(float) * 9 * N1, s));
   for (int l = 0; l < 2; ++l) {
     const LayerW &L = g_lw[l];
-    const int K = (l == 0 ? 2 : 3) * d;
+    const int K = featurize_cols(l, d, h.aux);
     N = Nl_[l];
     E = El_[l];
     T = Tl_[l];
@@ -635,10 +693,10 @@ void PETModel::forward_backward(bool grad) {
     Split16View sx;
     if (E > 0) {
       FeaturizeArgs fa{};
-      fa.n_edges = E; fa.d = d; fa.layer = l;
+      fa.n_edges = E; fa.d = d; fa.layer = l; fa.aux = h.aux;
       fa.vec = nl_.vec.as<float>(); fa.r = a.r;
       fa.nbr_species = a.nbr_species; fa.rev = a.rev; fa.edge_row = a.edge_row;
-      fa.We = L.We; fa.be = L.be; fa.emb0 = emb0; fa.nbr_emb = L.nbr_emb; fa.x_prev = a.xl[0];
+      fa.emb0 = emb0; fa.x_prev = a.xl[0];
       fa.cat = a.cat;
       Split16View scat, shc;
       if (ch) {
@@ -647,7 +705,7 @@ void PETModel::forward_backward(bool grad) {
       }
       featurize(fa, s);
       if (ch) shc = take_split(E, H);
-      gemm(a.cat, K, nullptr, L.C0, K, a.hc, H, nullptr, E, H, K, L.c0, EPI_SILU, s, keep(a.zc[l]), H, nullptr, 0,
+      gemm(a.cat, K, nullptr, L.C0f, K, a.hc, H, nullptr, E, H, K, nullptr, EPI_SILU, s, keep(a.zc[l]), H, nullptr, 0,
            SplitIO{ch ? &scat : nullptr, true, ch ? &shc : nullptr});
       if (ch) sx = take_split(T, d);
       gemm(a.hc, H, nullptr, L.C2, H, ch ? nullptr : a.xin, d, a.edge_row, E, d, H, L.c2, EPI_STORE, s, nullptr, 0,
@@ -736,12 +794,11 @@ void PETModel::forward_backward(bool grad) {
     }
     gemm(dtok, d, a.edge_row, L.C2T, d, a.dzc, H, nullptr, E, H, d, nullptr, EPI_DSILU, s, a.zc[l], H, nullptr, 0,
          SplitIO{ch ? &sa : nullptr, false, ch ? &sz : nullptr});
-    gemm(a.dzc, H, nullptr, L.C0T, H, a.demb, d, nullptr, E, d, H, nullptr, EPI_STORE, s, nullptr, 0, nullptr, 0,
-         SplitIO{ch ? &sz : nullptr});
     if (l == 1)
       gemm(a.dzc, H, nullptr, L.C0T + static_cast<size_t>(2) * d * H, H, a.dmsg, d, nullptr, E, d, H, nullptr,
            EPI_STORE, s, nullptr, 0, nullptr, 0, SplitIO{ch ? &sz : nullptr});
-    edge_embed_bwd(a.demb, d, L.We, a.g4, E, d, accumulate, s);
+    // d/d[x y z r] through the fused weight's edge-embedding columns
+    edge_xyzr_bwd(a.dzc, ch ? &sz : nullptr, L.C0xyzr, a.g4, E, H, accumulate, s);
   };
 
   // layer 1 (its N1 atoms), then layer 0 (N0 atoms); layer-0 tokens of
@@ -789,7 +846,7 @@ void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const in
   persist_.ensure(P.off);
   scratch_.ensure(S.off);
   if (use_f16_) {  // largest A operand of a 3xFP16 GEMM: [tokens, max(3d, ff, hid)]
-    const size_t kmax = static_cast<size_t>(std::max({3 * h_.d, h_.ff, h_.hid}));
+    const size_t kmax = static_cast<size_t>(std::max({3 * h_.d, h_.ff, h_.hid, featurize_cols(1, h_.d, h_.aux)}));
     const size_t mk = static_cast<size_t>(std::max(Tl_[0], Tl_[1])) * kmax;
     sp_[0].ensure(mk * 4 + mk / 128 + 256);
     if (chain_) sp_[1].ensure(mk * 4 + mk / 128 + 256);

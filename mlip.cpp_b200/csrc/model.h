@@ -19,6 +19,9 @@ namespace pet {
 struct Hypers {
   int d = 256, heads = 8, ff = 512, dh = 128, hid = 256;  // hid: compress hidden width
   int gnn_layers = 2, attn_layers = 2, n_species = 0;
+  // columns of the featurised rows' auxiliary block (x, y, z, r, 1 and one
+  // per embedding row, rounded up to 128): see FeaturizeArgs
+  int aux = 128;
   float cutoff = 4.5f, width = 0.5f;
 };
 

@@ -66,26 +66,28 @@ __global__ void k_edge_prep(EdgePrepArgs a) {
   }
 }
 
+// Column j of the auxiliary block: x, y, z, r, 1, one-hot(species), zeros.
+__device__ __forceinline__ float aux_value(int j, float x, float y, float z, float r, int sp) {
+  return j == 0 ? x : j == 1 ? y : j == 2 ? z : j == 3 ? r : j == 4 ? 1.0f : (j - 5 == sp ? 1.0f : 0.0f);
+}
+
 __device__ __forceinline__ float feat_value(const FeaturizeArgs &a, int e, int c) {
   const int d = a.d;
-  if (c < d) {
-    const float *w = a.We + 4 * c;
-    const float x = a.vec[3 * e], y = a.vec[3 * e + 1], z = a.vec[3 * e + 2];
-    return fmaf(w[2], z, fmaf(w[1], y, w[0] * x)) + w[3] * a.r[e] + a.be[c];
+  const int sp = a.nbr_species[e];
+  if (a.layer > 0) {
+    if (c < d) {
+      const int rv = a.rev[e];
+      const float m0 = a.emb0[static_cast<size_t>(sp) * d + c];
+      const float mr = rv >= 0 ? a.x_prev[static_cast<size_t>(a.edge_row[rv]) * d + c] : 0.0f;
+      return 0.5f * (m0 + mr);
+    }
+    c -= d;
   }
-  if (c < 2 * d) {
-    const float *tab = a.layer == 0 ? a.emb0 : a.nbr_emb;
-    return tab[static_cast<size_t>(a.nbr_species[e]) * d + (c - d)];
-  }
-  const int cc = c - 2 * d;
-  const int rv = a.rev[e];
-  const float m0 = a.emb0[static_cast<size_t>(a.nbr_species[e]) * d + cc];
-  const float mr = rv >= 0 ? a.x_prev[static_cast<size_t>(a.edge_row[rv]) * d + cc] : 0.0f;
-  return 0.5f * (m0 + mr);
+  return aux_value(c, a.vec[3 * e], a.vec[3 * e + 1], a.vec[3 * e + 2], a.r[e], sp);
 }
 
 __global__ void k_featurize(FeaturizeArgs a) {
-  const int K = (a.layer == 0 ? 2 : 3) * a.d;
+  const int K = featurize_cols(a.layer, a.d, a.aux);
   const int64_t total = static_cast<int64_t>(a.n_edges) * K;
   for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
        t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -95,42 +97,33 @@ __global__ void k_featurize(FeaturizeArgs a) {
 }
 
 // Split-fp16 output: warp per edge, lane l holds columns 4l..4l+3 of each
-// 128-column block (d a multiple of 128, so a block lies in one section).
+// 128-column block (d and aux multiples of 128, so a block lies in one part).
 __global__ void k_featurize_split(FeaturizeArgs a) {
-  const int d = a.d, nbd = d / 128;
+  const int d = a.d, nbd = a.layer > 0 ? d / 128 : 0;
   const int e = static_cast<int>((blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
   if (e >= a.n_edges) return;
-  const float x = a.vec[3 * e], y = a.vec[3 * e + 1], z = a.vec[3 * e + 2], r = a.r[e];
   const int sp = a.nbr_species[e];
-  // edge embedding W [x y z r] + b  (W rows of 4)
-  for (int k = 0; k < nbd; ++k) {
-    const int c = k * 128 + lane * 4;
-    float o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float4 w = __ldg(reinterpret_cast<const float4 *>(a.We + 4 * (c + j)));
-      o[j] = fmaf(w.z, z, fmaf(w.y, y, w.x * x)) + w.w * r + __ldg(a.be + c + j);
+  if (a.layer > 0) {  // message: 0.5 (embedding[nbr species] + X0[row(reverse edge)])
+    const int rv = a.rev[e];
+    const float *m0 = a.emb0 + static_cast<size_t>(sp) * d;
+    const float *mr = rv >= 0 ? a.x_prev + static_cast<size_t>(a.edge_row[rv]) * d : nullptr;
+    for (int k = 0; k < nbd; ++k) {
+      const int c = k * 128 + lane * 4;
+      const float4 p = __ldg(reinterpret_cast<const float4 *>(m0 + c));
+      const float4 q = mr ? *reinterpret_cast<const float4 *>(mr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      warp_split_block(a.cat_split, e, k,
+                       make_float4(0.5f * (p.x + q.x), 0.5f * (p.y + q.y), 0.5f * (p.z + q.z), 0.5f * (p.w + q.w)),
+                       lane);
     }
-    warp_split_block(a.cat_split, e, k, make_float4(o[0], o[1], o[2], o[3]), lane);
   }
-  // neighbour-species embedding
-  const float *tab = (a.layer == 0 ? a.emb0 : a.nbr_emb) + static_cast<size_t>(sp) * d;
-  for (int k = 0; k < nbd; ++k) {
-    const float4 v = __ldg(reinterpret_cast<const float4 *>(tab + k * 128 + lane * 4));
-    warp_split_block(a.cat_split, e, nbd + k, v, lane);
-  }
-  if (a.layer == 0) return;
-  // message: 0.5 (embedding[nbr species] + X0[row(reverse edge)])
-  const int rv = a.rev[e];
-  const float *m0 = a.emb0 + static_cast<size_t>(sp) * d;
-  const float *mr = rv >= 0 ? a.x_prev + static_cast<size_t>(a.edge_row[rv]) * d : nullptr;
-  for (int k = 0; k < nbd; ++k) {
+  const float x = a.vec[3 * e], y = a.vec[3 * e + 1], z = a.vec[3 * e + 2], r = a.r[e];
+  for (int k = 0; k < a.aux / 128; ++k) {
     const int c = k * 128 + lane * 4;
-    const float4 p = __ldg(reinterpret_cast<const float4 *>(m0 + c));
-    const float4 q = mr ? *reinterpret_cast<const float4 *>(mr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-    warp_split_block(a.cat_split, e, 2 * nbd + k,
-                     make_float4(0.5f * (p.x + q.x), 0.5f * (p.y + q.y), 0.5f * (p.z + q.z), 0.5f * (p.w + q.w)), lane);
+    warp_split_block(a.cat_split, e, nbd + k,
+                     make_float4(aux_value(c, x, y, z, r, sp), aux_value(c + 1, x, y, z, r, sp),
+                                 aux_value(c + 2, x, y, z, r, sp), aux_value(c + 3, x, y, z, r, sp)),
+                     lane);
   }
 }
 
@@ -217,20 +210,44 @@ __global__ void k_add_vec(const float *__restrict__ x, float *__restrict__ y, in
     y[t] = accumulate ? y[t] + x[t] : x[t];
 }
 
-__global__ void k_edge_embed_bwd(const float *__restrict__ demb, int ld, const float *__restrict__ We,
-                                 float *__restrict__ g4, int n_edges, int d, int accumulate) {
+template <bool kSplit>
+__global__ void k_edge_xyzr_bwd(const float *__restrict__ dz, Split16View dzs, const float *__restrict__ P,
+                                float *__restrict__ g4, int n_edges, int H, int accumulate) {
   const int lane = threadIdx.x & 31;
   for (int e = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; e < n_edges;
        e += (gridDim.x * blockDim.x) >> 5) {
-    const float *gr = demb + static_cast<size_t>(e) * ld;
     float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-    for (int o = lane; o < d; o += 32) {
-      const float g = gr[o];
-      const float4 w = *reinterpret_cast<const float4 *>(We + 4 * o);
-      s0 = fmaf(g, w.x, s0);
-      s1 = fmaf(g, w.y, s1);
-      s2 = fmaf(g, w.z, s2);
-      s3 = fmaf(g, w.w, s3);
+    if (kSplit) {  // lane: columns 4 lane .. 4 lane + 3 of each 128-column block
+      for (int k = 0; k < H / 128; ++k) {
+        const int c = 128 * k + 4 * lane;
+        const size_t off = static_cast<size_t>(e) * H + c;
+        const uint2 hv = *reinterpret_cast<const uint2 *>(dzs.hi + off);
+        const uint2 lv = *reinterpret_cast<const uint2 *>(dzs.lo + off);
+        const float f = pow2f(-static_cast<int>(dzs.sc[static_cast<size_t>(k) * dzs.rows + e]));
+        const float2 h0 = __half22float2(*reinterpret_cast<const __half2 *>(&hv.x));
+        const float2 h1 = __half22float2(*reinterpret_cast<const __half2 *>(&hv.y));
+        const float2 l0 = __half22float2(*reinterpret_cast<const __half2 *>(&lv.x));
+        const float2 l1 = __half22float2(*reinterpret_cast<const __half2 *>(&lv.y));
+        const float g[4] = {(h0.x + l0.x) * f, (h0.y + l0.y) * f, (h1.x + l1.x) * f, (h1.y + l1.y) * f};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 w = __ldg(reinterpret_cast<const float4 *>(P + 4 * (c + q)));
+          s0 = fmaf(g[q], w.x, s0);
+          s1 = fmaf(g[q], w.y, s1);
+          s2 = fmaf(g[q], w.z, s2);
+          s3 = fmaf(g[q], w.w, s3);
+        }
+      }
+    } else {
+      const float *gr = dz + static_cast<size_t>(e) * H;
+      for (int o = lane; o < H; o += 32) {
+        const float g = gr[o];
+        const float4 w = __ldg(reinterpret_cast<const float4 *>(P + 4 * o));
+        s0 = fmaf(g, w.x, s0);
+        s1 = fmaf(g, w.y, s1);
+        s2 = fmaf(g, w.z, s2);
+        s3 = fmaf(g, w.w, s3);
+      }
     }
     s0 = warp_sum(s0);
     s1 = warp_sum(s1);
@@ -509,11 +526,13 @@ void edge_prep(const EdgePrepArgs &a, cudaStream_t s) {
 }
 
 void featurize(const FeaturizeArgs &a, cudaStream_t s) {
-  const int K = (a.layer == 0 ? 2 : 3) * a.d;
+  const int K = featurize_cols(a.layer, a.d, a.aux);
   const int64_t total = static_cast<int64_t>(a.n_edges) * K;
   if (total <= 0) return;
+  if (a.aux < 5) throw Error(kErrInternal, "featurize: the auxiliary block needs at least 5 columns");
   if (a.cat_split.hi) {
-    if (a.d % 128) throw Error(kErrInternal, "featurize: split output needs d a multiple of 128");
+    if (a.d % 128 || a.aux % 128)
+      throw Error(kErrInternal, "featurize: split output needs d and the auxiliary block multiples of 128");
     k_featurize_split<<<ceil_div(static_cast<int64_t>(a.n_edges) * 32, 256), 256, 0, s>>>(a);
   } else {
     k_featurize<<<grid_for(total, 256), 256, 0, s>>>(a);
@@ -568,11 +587,16 @@ void add_vec(const float *x, float *y, int n, bool accumulate, cudaStream_t s) {
   CUDA_LAUNCH_CHECK();
 }
 
-void edge_embed_bwd(const float *demb, int ld, const float *We, float *g4, int n_edges, int d,
-                    bool accumulate, cudaStream_t s) {
+void edge_xyzr_bwd(const float *dz, const Split16View *dzs, const float *P, float *g4, int n_edges, int H,
+                   bool accumulate, cudaStream_t s) {
   if (n_edges <= 0) return;
-  k_edge_embed_bwd<<<grid_for(static_cast<int64_t>(n_edges) * 32, 256), 256, 0, s>>>(demb, ld, We, g4, n_edges,
-                                                                                     d, accumulate);
+  const int grid = grid_for(static_cast<int64_t>(n_edges) * 32, 256);
+  if (dzs) {
+    if (H % 128) throw Error(kErrInternal, "edge_xyzr_bwd: split input needs H a multiple of 128");
+    k_edge_xyzr_bwd<true><<<grid, 256, 0, s>>>(nullptr, *dzs, P, g4, n_edges, H, accumulate);
+  } else {
+    k_edge_xyzr_bwd<false><<<grid, 256, 0, s>>>(dz, Split16View{}, P, g4, n_edges, H, accumulate);
+  }
   CUDA_LAUNCH_CHECK();
 }
 

@@ -22,19 +22,28 @@ struct EdgePrepArgs {
 // rows; neighbour species; reverse edge (pet_batch.cpp:399-495).
 void edge_prep(const EdgePrepArgs &a, cudaStream_t s);
 
-// cat[e, 0:d] = W_e [x y z r] + b_e  (pet_layers.cpp:151-217)
-// layer 0: cat[e, d:2d] = embedding[nbr species]               (pet.cpp:789-832)
-// layer 1: cat[e, d:2d] = neighbor_embedder[nbr species],
-//          cat[e, 2d:3d] = 0.5 (embedding[nbr species] + X0[row(rev e)])  (pet_layers.cpp:608-679)
+// Input rows of the compression's first linear (build_tokens,
+// pet_layers.cpp:685-796).  The reference concatenates the edge embedding
+// W_e [x y z r] + b_e (pet_layers.cpp:151-217), the neighbour-species
+// embedding (embedding[nbr species] in layer 0, pet.cpp:789-832;
+// neighbor_embedder[nbr species] in layer 1) and, in layer 1, the message
+// 0.5 (embedding[nbr species] + X0[row(rev e)]) (pet_layers.cpp:608-679).
+// The first two enter compress.0 linearly, so the model folds their
+// products with its weight into a fused weight at load, and the rows here
+// carry only what those products multiply:
+//   layer 1: cat[e, 0:d] = the message;
+//   then `aux` columns: x, y, z, r, 1, one-hot(nbr species), zeros.
 struct FeaturizeArgs {
-  int n_edges, d, layer;
+  int n_edges, d, layer, aux;
   const float *vec, *r;
   const int *nbr_species, *rev, *edge_row;
-  const float *We, *be, *emb0, *nbr_emb, *x_prev;
+  const float *emb0, *x_prev;
   float *cat;
   Split16View cat_split;  // if set, cat is written in split-fp16 form only
 };
 void featurize(const FeaturizeArgs &a, cudaStream_t s);
+// Columns of a featurised row: the message (layer 1) plus the auxiliary block.
+__host__ __device__ inline int featurize_cols(int layer, int d, int aux) { return (layer > 0 ? d : 0) + aux; }
 
 // X[node_row[i], :] = table[species[i], :]  (xs: the same rows in split form too)
 void node_tokens(const float *table, const int *species, const int *node_row, float *x, int n,
@@ -54,9 +63,12 @@ void atom_energy(const float *node_pred, const float *edge_pred, const float *fc
 // gfc[e] (+)= edge_pred[e]
 void add_vec(const float *x, float *y, int n, bool accumulate, cudaStream_t s);
 
-// g4[e, 0:3] (+)= W_e[:, 0:3]^T demb[e],  g4[e, 3] (+)= W_e[:, 3]^T demb[e]
-void edge_embed_bwd(const float *demb, int ld, const float *We, float *g4, int n_edges, int d,
-                    bool accumulate, cudaStream_t s);
+// g4[e, 0:4] (+)= P^T dz[e]: the gradient of the compression pre-activation
+// with respect to [x y z r] of each edge, P [H][4] being the fused weight's
+// x, y, z, r columns (i.e. compress.0's edge-embedding block times W_e).
+// dz is [n_edges][H] fp32, or in split form when dzs is given.
+void edge_xyzr_bwd(const float *dz, const Split16View *dzs, const float *P, float *g4, int n_edges, int H,
+                   bool accumulate, cudaStream_t s);
 // dX[edge_row[x], :] += 0.5 dmsg[rev[x], :]   for 0 <= rev[x] < n_msg
 void message_bwd(const float *dmsg, int ld, const int *rev, const int *edge_row, float *dx,
                  int n_edges, int n_msg, int d, cudaStream_t s);
