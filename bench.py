@@ -400,10 +400,10 @@ def main():
                                          if f16 else f"{src} bf16 sustained / 6 (3 tf32 MMAs at half bf16 rate)"),
                          "tensor_pipe_frac_of_bf16": div * achieved / bf16_sus,
                          # DRAM bytes per average GEMM launch: ncu dram__bytes_read.sum +
-                         # dram__bytes_write.sum over all 57 GEMM launches of one step of the
-                         # 1,728-atom cell of this alloy (358 MB/launch at 65,202 tokens,
-                         # 5,493 B per token for the 3xFP16 build), scaled by this step's tokens
-                         "traffic": (5493.0 * (shape["atoms"] + shape["edges"])
+                         # dram__bytes_write.sum over all 55 GEMM launches of one step of the
+                         # 1,728-atom cell of this alloy (350 MB/launch at 65,202 tokens,
+                         # 5,371 B per token for the 3xFP16 build), scaled by this step's tokens
+                         "traffic": (5371.0 * (shape["atoms"] + shape["edges"])
                                      if not domains and f16 and grad else None),
                          "traffic_unit": "bytes per GEMM launch (scaled from the 1,728-atom capture)",
                          "gemm_share_of_step": gemm_ms / (t_dev * 1e3) if t_dev else None},

@@ -210,44 +210,68 @@ __global__ void k_add_vec(const float *__restrict__ x, float *__restrict__ y, in
     y[t] = accumulate ? y[t] + x[t] : x[t];
 }
 
-template <bool kSplit>
-__global__ void k_edge_xyzr_bwd(const float *__restrict__ dz, Split16View dzs, const float *__restrict__ P,
-                                float *__restrict__ g4, int n_edges, int H, int accumulate) {
+// Split input: lane l owns columns 4l..4l+3 of every 128-column block for
+// all the edges it visits, so its H/32 rows of P stay in registers.
+template <int NB>
+__global__ void k_edge_xyzr_bwd_split(Split16View dzs, const float *__restrict__ P, float *__restrict__ g4,
+                                      int n_edges, int accumulate) {
+  constexpr int H = 128 * NB;
   const int lane = threadIdx.x & 31;
-  for (int e = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; e < n_edges;
-       e += (gridDim.x * blockDim.x) >> 5) {
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-    if (kSplit) {  // lane: columns 4 lane .. 4 lane + 3 of each 128-column block
-      for (int k = 0; k < H / 128; ++k) {
-        const int c = 128 * k + 4 * lane;
-        const size_t off = static_cast<size_t>(e) * H + c;
-        const uint2 hv = *reinterpret_cast<const uint2 *>(dzs.hi + off);
-        const uint2 lv = *reinterpret_cast<const uint2 *>(dzs.lo + off);
-        const float f = pow2f(-static_cast<int>(dzs.sc[static_cast<size_t>(k) * dzs.rows + e]));
-        const float2 h0 = __half22float2(*reinterpret_cast<const __half2 *>(&hv.x));
-        const float2 h1 = __half22float2(*reinterpret_cast<const __half2 *>(&hv.y));
-        const float2 l0 = __half22float2(*reinterpret_cast<const __half2 *>(&lv.x));
-        const float2 l1 = __half22float2(*reinterpret_cast<const __half2 *>(&lv.y));
-        const float g[4] = {(h0.x + l0.x) * f, (h0.y + l0.y) * f, (h1.x + l1.x) * f, (h1.y + l1.y) * f};
+  float4 w[NB][4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 w = __ldg(reinterpret_cast<const float4 *>(P + 4 * (c + q)));
-          s0 = fmaf(g[q], w.x, s0);
-          s1 = fmaf(g[q], w.y, s1);
-          s2 = fmaf(g[q], w.z, s2);
-          s3 = fmaf(g[q], w.w, s3);
-        }
+  for (int k = 0; k < NB; ++k)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) w[k][q] = __ldg(reinterpret_cast<const float4 *>(P + 4 * (128 * k + 4 * lane + q)));
+  for (int e = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; e < n_edges; e += (gridDim.x * blockDim.x) >> 5) {
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+      const size_t off = static_cast<size_t>(e) * H + 128 * k + 4 * lane;
+      const uint2 hv = *reinterpret_cast<const uint2 *>(dzs.hi + off);
+      const uint2 lv = *reinterpret_cast<const uint2 *>(dzs.lo + off);
+      const float f = pow2f(-static_cast<int>(dzs.sc[static_cast<size_t>(k) * dzs.rows + e]));
+      const float2 h0 = __half22float2(*reinterpret_cast<const __half2 *>(&hv.x));
+      const float2 h1 = __half22float2(*reinterpret_cast<const __half2 *>(&hv.y));
+      const float2 l0 = __half22float2(*reinterpret_cast<const __half2 *>(&lv.x));
+      const float2 l1 = __half22float2(*reinterpret_cast<const __half2 *>(&lv.y));
+      const float g[4] = {(h0.x + l0.x) * f, (h0.y + l0.y) * f, (h1.x + l1.x) * f, (h1.y + l1.y) * f};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        s0 = fmaf(g[q], w[k][q].x, s0);
+        s1 = fmaf(g[q], w[k][q].y, s1);
+        s2 = fmaf(g[q], w[k][q].z, s2);
+        s3 = fmaf(g[q], w[k][q].w, s3);
       }
-    } else {
-      const float *gr = dz + static_cast<size_t>(e) * H;
-      for (int o = lane; o < H; o += 32) {
-        const float g = gr[o];
-        const float4 w = __ldg(reinterpret_cast<const float4 *>(P + 4 * o));
-        s0 = fmaf(g, w.x, s0);
-        s1 = fmaf(g, w.y, s1);
-        s2 = fmaf(g, w.z, s2);
-        s3 = fmaf(g, w.w, s3);
+    }
+    s0 = warp_sum(s0);
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    s3 = warp_sum(s3);
+    if (lane == 0) {
+      float4 *o = reinterpret_cast<float4 *>(g4) + e;
+      float4 v = make_float4(s0, s1, s2, s3);
+      if (accumulate) {
+        const float4 p = *o;
+        v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
       }
+      *o = v;
+    }
+  }
+}
+
+__global__ void k_edge_xyzr_bwd(const float *__restrict__ dz, const float *__restrict__ P, float *__restrict__ g4,
+                                int n_edges, int H, int accumulate) {
+  const int lane = threadIdx.x & 31;
+  for (int e = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; e < n_edges; e += (gridDim.x * blockDim.x) >> 5) {
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    const float *gr = dz + static_cast<size_t>(e) * H;
+    for (int o = lane; o < H; o += 32) {
+      const float g = gr[o];
+      const float4 w = __ldg(reinterpret_cast<const float4 *>(P + 4 * o));
+      s0 = fmaf(g, w.x, s0);
+      s1 = fmaf(g, w.y, s1);
+      s2 = fmaf(g, w.z, s2);
+      s3 = fmaf(g, w.w, s3);
     }
     s0 = warp_sum(s0);
     s1 = warp_sum(s1);
@@ -592,10 +616,15 @@ void edge_xyzr_bwd(const float *dz, const Split16View *dzs, const float *P, floa
   if (n_edges <= 0) return;
   const int grid = grid_for(static_cast<int64_t>(n_edges) * 32, 256);
   if (dzs) {
-    if (H % 128) throw Error(kErrInternal, "edge_xyzr_bwd: split input needs H a multiple of 128");
-    k_edge_xyzr_bwd<true><<<grid, 256, 0, s>>>(nullptr, *dzs, P, g4, n_edges, H, accumulate);
+    switch (H % 128 == 0 ? H / 128 : 0) {
+      case 1: k_edge_xyzr_bwd_split<1><<<grid, 256, 0, s>>>(*dzs, P, g4, n_edges, accumulate); break;
+      case 2: k_edge_xyzr_bwd_split<2><<<grid, 256, 0, s>>>(*dzs, P, g4, n_edges, accumulate); break;
+      case 4: k_edge_xyzr_bwd_split<4><<<grid, 256, 0, s>>>(*dzs, P, g4, n_edges, accumulate); break;
+      case 8: k_edge_xyzr_bwd_split<8><<<grid, 256, 0, s>>>(*dzs, P, g4, n_edges, accumulate); break;
+      default: throw Error(kErrInternal, "edge_xyzr_bwd: split input needs H in {128, 256, 512, 1024}");
+    }
   } else {
-    k_edge_xyzr_bwd<false><<<grid, 256, 0, s>>>(dz, Split16View{}, P, g4, n_edges, H, accumulate);
+    k_edge_xyzr_bwd<<<grid, 256, 0, s>>>(dz, P, g4, n_edges, H, accumulate);
   }
   CUDA_LAUNCH_CHECK();
 }
