@@ -1300,8 +1300,9 @@ void launch(const GemmArgs &a, const TCWeights &w, int *err, cudaStream_t s) {
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
 // Tile of the 3xFP16 GEMM.  By default 128 x 128 (3 stages, 4 TMEM
-// buffers: the MMA runs furthest ahead of the epilogue; fastest on the PET
-// layer shapes).  MLIPCPP_B200_F16_TILE selects 256 (one-SM 128 x 256) or
+// buffers: the MMA runs furthest ahead of the epilogue; fastest on most PET
+// layer shapes), and 128 x 256 for wide plain-store layers (see launch16).
+// MLIPCPP_B200_F16_TILE forces 128 (128 x 128), 256 (one-SM 128 x 256) or
 // 512 (the SM-pair 256 x 256) where N allows.
 const int g_f16_bn = [] {
   const char *e = std::getenv("MLIPCPP_B200_F16_TILE");
@@ -1428,7 +1429,13 @@ void launch16(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t s)
     k_split_a<<<ceil_div(a.M, 8), 256, 0, s>>>(a.A, a.lda, a.a_rows, a.M, a.K, a.a_split);
     CUDA_LAUNCH_CHECK();
   }
-  const int bn = g_f16_bn ? g_f16_bn : 128;
+  // default tile: 128 x 128; wide plain-store layers (QKV, N = 1536: 4.31 ->
+  // 3.92 ms on the 32k cell) run faster on 128 x 256, whose B-tile reuse
+  // halves the A traffic per product, while the layers with split outputs,
+  // SiLU or residual epilogues ran slower there (their epilogue, 128
+  // columns per warp, sets the pace)
+  const bool wide = EPI == EPI_STORE && !a.c_split.hi && !a.c_rows && a.N % 256 == 0 && a.N >= 1024;
+  const int bn = g_f16_bn ? g_f16_bn : (wide ? 256 : 128);
   if (a.N % 256 == 0 && bn == 512 && w.products == 3 && !a.r_split.hi) launch16_pair<EPI>(a, w, err, s);
   else if (a.N % 256 == 0 && bn == 256) launch16_bn<EPI, 256>(a, w, err, s);
   else launch16_bn<EPI, 128>(a, w, err, s);
