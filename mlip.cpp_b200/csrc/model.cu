@@ -56,11 +56,12 @@ struct PropW {
   bool loaded = false;
 };
 struct LayerW {
-  const float *We, *be, *node_emb, *nbr_emb, *C0, *c0, *C2, *c2, *C0T, *C2T;
+  const float *node_emb, *C2, *c2, *C2T;
   // compress.0 with the edge and neighbour-species embeddings folded in
-  // ([hid][featurised columns], bias included) and its x, y, z, r columns
-  // as [hid][4] for the backward
-  const float *C0f, *C0xyzr;
+  // ([hid][featurised columns], bias included), its x, y, z, r columns as
+  // [hid][4] for the backward, and (layer 1) the transpose of compress.0,
+  // whose message rows give the message gradient
+  const float *C0f, *C0xyzr, *C0T;
   BlockW blk[2];
   HeadW node, edge;
   PropW nc[2];  // non-conservative heads: [0] forces (od 3), [1] stress (od 9)
@@ -255,7 +256,7 @@ void PETModel::load(const std::string &path, float cutoff_override) {
   };
   for (int l = 0; l < 2; ++l) {
     const std::string p = "model.gnn." + std::to_string(l) + ".";
-    transpose_of(p + "compress.0.weight");
+    if (l > 0) transpose_of(p + "compress.0.weight");
     transpose_of(p + "compress.2.weight");
     for (int t = 0; t < 2; ++t) {
       const std::string q = p + "tl." + std::to_string(t) + ".";
@@ -402,15 +403,10 @@ void PETModel::load(const std::string &path, float cutoff_override) {
   for (int l = 0; l < 2; ++l) {
     const std::string p = "model.gnn." + std::to_string(l) + ".";
     LayerW &L = in_->lw[l];
-    L.We = w(p + "edge_embedder.weight");
-    L.be = w(p + "edge_embedder.bias");
     L.node_emb = w(p + "node_embedder.weight");
-    L.nbr_emb = l > 0 ? w(p + "neighbor_embedder.weight") : nullptr;
-    L.C0 = w(p + "compress.0.weight");
-    L.c0 = w(p + "compress.0.bias");
     L.C2 = w(p + "compress.2.weight");
     L.c2 = w(p + "compress.2.bias");
-    L.C0T = w(p + "compress.0.weight.T");
+    L.C0T = l > 0 ? w(p + "compress.0.weight.T") : nullptr;
     L.C0f = w(p + "compress.0.fused");
     L.C0xyzr = w(p + "compress.0.xyzr");
     L.C2T = w(p + "compress.2.weight.T");

@@ -67,6 +67,23 @@ def test_gpu_matches_oracle(case, model_file):
     assert_close(res, ref["energy_f64"], ref["forces"], ref.get("stress"), s.n_atoms)
 
 
+def test_gpu_many_species_matches_oracle(tmp_path):
+    """A model with 130 species: the featurised rows' one-hot block spans two
+    128-column blocks (x, y, z, r, 1 and 131 table rows), and the fused
+    compress.0 weight has as many species columns; atoms use species on
+    both sides of the block boundary."""
+    path = str(tmp_path / "species130.gguf")
+    wl.write_pet_gguf(path, wl.HYPERS["pet-mad-s"], atomic_numbers=np.arange(1, 131, dtype=np.int32), seed=41)
+    s = wl.si_diamond(2, seed=41)
+    rng = np.random.default_rng(41)
+    numbers = rng.choice(np.array([1, 6, 8, 60, 118, 119, 122, 123, 124, 125, 129, 130], np.int32), s.n_atoms)
+    s = wl.Structure(s.positions, numbers, s.cell, s.pbc)
+    orc = po.load_oracle(path, torch.float64)
+    ref = orc.predict([s])[0]
+    res = mb.Predictor(path).predict(s.positions, s.numbers, s.cell, s.pbc, compute_stress=True)
+    assert_close(res, ref["energy_f64"], ref["forces"], ref.get("stress"), s.n_atoms)
+
+
 def test_gpu_molecule_batch_matches_single(model_file):
     """Batch == individual within 1e-5 (tests/test_pet.cpp:147-184)."""
     pred = mb.Predictor(model_file("tiny", 4))
