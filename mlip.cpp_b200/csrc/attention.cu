@@ -57,7 +57,7 @@ __device__ __forceinline__ void group_split_store(const Split16View &o, int row,
   for (int k = 0; k < hg; ++k) m = fmaxf(m, mx[k * S + r]);
   const int s = split_scale_exponent(m);
   thread_split_store<HD>(o, row, col, v, s);
-  if (hh == 0) o.sc[static_cast<size_t>(blk) * o.rows + row] = static_cast<int8_t>(s);
+  if (hh == 0) o.sc[static_cast<size_t>(blk) * split_ld(o) + row] = static_cast<int8_t>(s);
 }
 
 template <int HD>
@@ -99,14 +99,14 @@ __device__ __forceinline__ void axpy_row(float (&o)[HD], float p, const float *_
 // array into smem laid out [HG][S][HD]; every copy of the block is in flight
 // at once.  The caller commits and waits (cp_async_wait_all) before use.
 template <int HD>
-__device__ __forceinline__ void load_block(float *dst, const float *src, int ld, int col, int t0, int S,
+__device__ __forceinline__ void load_block(float *dst, const float *src, int ld, int col, AtomRows tr, int S,
                                            int hg) {
   const int per_row = HD / 4, per_head = S * per_row, n = hg * per_head, hs = head_stride(S, HD);
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int hh = i / per_head, rem = i - hh * per_head, k = rem / per_row, c = (rem - k * per_row) * 4;
     const uint32_t d32 = static_cast<uint32_t>(__cvta_generic_to_shared(dst + hh * hs + k * HD + c));
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d32),
-                 "l"(src + static_cast<size_t>(t0 + k) * ld + col + hh * HD + c)
+                 "l"(src + static_cast<size_t>(tr(k)) * ld + col + hh * HD + c)
                  : "memory");
   }
 }
@@ -120,12 +120,12 @@ __global__ void k_attn_fwd(AttnArgs a, int hg) {
   const int atom = blockIdx.x, h0 = blockIdx.y * hg;
   const int e0 = a.offset[atom];
   const int S = a.offset[atom + 1] - e0 + 1;
-  const int t0 = e0 + atom;
+  const AtomRows tr = atom_rows(atom, e0, a.edge_base);
   const int d = a.d, ld = 3 * d;
   const int hs = head_stride(S, HD);
   float *sK = sm, *sV = sK + hg * hs, *sM = sV + hg * hs, *sX = sM + S;
-  load_block<HD>(sK, a.qkv, ld, d + h0 * HD, t0, S, hg);
-  load_block<HD>(sV, a.qkv, ld, 2 * d + h0 * HD, t0, S, hg);
+  load_block<HD>(sK, a.qkv, ld, d + h0 * HD, tr, S, hg);
+  load_block<HD>(sV, a.qkv, ld, 2 * d + h0 * HD, tr, S, hg);
   for (int k = threadIdx.x; k < S; k += blockDim.x) sM[k] = k == 0 ? 0.f : a.key_mask[e0 + k - 1];
   cp_async_wait_all();
   __syncthreads();
@@ -135,7 +135,7 @@ __global__ void k_attn_fwd(AttnArgs a, int hg) {
   float o[HD];
   if (live) {
     float qr[HD];
-    const float *qsrc = a.qkv + static_cast<size_t>(t0 + q) * ld + h * HD;
+    const float *qsrc = a.qkv + static_cast<size_t>(tr(q)) * ld + h * HD;
 #pragma unroll
     for (int c = 0; c < HD; c += 4) {
       const float4 v = *reinterpret_cast<const float4 *>(qsrc + c);
@@ -161,9 +161,9 @@ __global__ void k_attn_fwd(AttnArgs a, int hg) {
     const float inv = 1.0f / l;
 #pragma unroll
     for (int c = 0; c < HD; ++c) o[c] *= inv;
-    a.lse[static_cast<size_t>(t0 + q) * a.heads + h] = m + logf(l);
+    a.lse[static_cast<size_t>(tr(q)) * a.heads + h] = m + logf(l);
     if (a.out) {
-      float *dst = a.out + static_cast<size_t>(t0 + q) * d + h * HD;
+      float *dst = a.out + static_cast<size_t>(tr(q)) * d + h * HD;
 #pragma unroll
       for (int c = 0; c < HD; c += 4) *reinterpret_cast<float4 *>(dst + c) = make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]);
     }
@@ -171,7 +171,7 @@ __global__ void k_attn_fwd(AttnArgs a, int hg) {
   }
   if (a.out_split.hi) {
     __syncthreads();
-    if (live) group_split_store<HD>(a.out_split, t0 + q, h * HD, blockIdx.y, sX, hg, S, q, hh, o);
+    if (live) group_split_store<HD>(a.out_split, tr(q), h * HD, blockIdx.y, sX, hg, S, q, hh, o);
   }
 }
 
@@ -187,18 +187,18 @@ __global__ void k_attn_bwd(AttnArgs a, int hg) {
   const int atom = blockIdx.x, h0 = blockIdx.y * hg;
   const int e0 = a.offset[atom];
   const int S = a.offset[atom + 1] - e0 + 1;
-  const int t0 = e0 + atom;
+  const AtomRows tr = atom_rows(atom, e0, a.edge_base);
   const int d = a.d, ld = 3 * d;
   const int PS = S | 1;
   const int hs = head_stride(S, HD), ms = mat_stride(S);
   float *sA = sm, *sB = sA + hg * hs;  // K, V (phase A) then Q, dO (phase B)
   float *sP = sB + hg * hs, *sD = sP + hg * ms, *sM = sD + hg * ms, *sL = sM + S, *sX = sL + hg * S;
-  load_block<HD>(sA, a.qkv, ld, d + h0 * HD, t0, S, hg);
-  load_block<HD>(sB, a.qkv, ld, 2 * d + h0 * HD, t0, S, hg);
+  load_block<HD>(sA, a.qkv, ld, d + h0 * HD, tr, S, hg);
+  load_block<HD>(sB, a.qkv, ld, 2 * d + h0 * HD, tr, S, hg);
   for (int k = threadIdx.x; k < S; k += blockDim.x) sM[k] = k == 0 ? 0.f : a.key_mask[e0 + k - 1];
   for (int i = threadIdx.x; i < hg * S; i += blockDim.x) {
     const int hh = i / S, q = i - hh * S;
-    sL[i] = a.lse[static_cast<size_t>(t0 + q) * a.heads + h0 + hh];
+    sL[i] = a.lse[static_cast<size_t>(tr(q)) * a.heads + h0 + hh];
   }
   const int t = threadIdx.x;
   const bool live = t < hg * S;
@@ -206,8 +206,8 @@ __global__ void k_attn_bwd(AttnArgs a, int hg) {
   const float scale = 1.0f / sqrtf(static_cast<float>(HD));
   float qr[HD], g[HD];
   if (live) {
-    const float *qs = a.qkv + static_cast<size_t>(t0 + r) * ld + h * HD;
-    const float *gs = a.d_out + static_cast<size_t>(t0 + r) * d + h * HD;
+    const float *qs = a.qkv + static_cast<size_t>(tr(r)) * ld + h * HD;
+    const float *gs = a.d_out + static_cast<size_t>(tr(r)) * d + h * HD;
 #pragma unroll
     for (int c = 0; c < HD; c += 4) {
       const float4 v = *reinterpret_cast<const float4 *>(qs + c);
@@ -245,7 +245,7 @@ __global__ void k_attn_bwd(AttnArgs a, int hg) {
 #pragma unroll
     for (int c = 0; c < HD; ++c) acc[c] *= scale;
     if (a.d_qkv) {
-      float *dq = a.d_qkv + static_cast<size_t>(t0 + r) * ld + h * HD;
+      float *dq = a.d_qkv + static_cast<size_t>(tr(r)) * ld + h * HD;
 #pragma unroll
       for (int c = 0; c < HD; c += 4)
         *reinterpret_cast<float4 *>(dq + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
@@ -253,9 +253,9 @@ __global__ void k_attn_bwd(AttnArgs a, int hg) {
     if (split) sX[hh * S + r] = absmax<HD>(acc);
   }
   __syncthreads();  // K and V no longer read: bring in Q and dO
-  if (split && live) group_split_store<HD>(a.dqkv_split, t0 + r, h * HD, blockIdx.y, sX, hg, S, r, hh, acc);
-  load_block<HD>(sA, a.qkv, ld, h0 * HD, t0, S, hg);
-  load_block<HD>(sB, a.d_out, d, h0 * HD, t0, S, hg);
+  if (split && live) group_split_store<HD>(a.dqkv_split, tr(r), h * HD, blockIdx.y, sX, hg, S, r, hh, acc);
+  load_block<HD>(sA, a.qkv, ld, h0 * HD, tr, S, hg);
+  load_block<HD>(sB, a.d_out, d, h0 * HD, tr, S, hg);
   cp_async_wait_all();
   __syncthreads();
   float dk[HD], dv[HD];
@@ -272,7 +272,7 @@ __global__ void k_attn_bwd(AttnArgs a, int hg) {
 #pragma unroll
     for (int c = 0; c < HD; ++c) dk[c] *= scale;
     if (a.d_qkv) {
-      float *dst = a.d_qkv + static_cast<size_t>(t0 + r) * ld + h * HD;
+      float *dst = a.d_qkv + static_cast<size_t>(tr(r)) * ld + h * HD;
 #pragma unroll
       for (int c = 0; c < HD; c += 4) {
         *reinterpret_cast<float4 *>(dst + d + c) = make_float4(dk[c], dk[c + 1], dk[c + 2], dk[c + 3]);
@@ -288,8 +288,8 @@ __global__ void k_attn_bwd(AttnArgs a, int hg) {
     __syncthreads();
     if (live) {
       const int nbq = d / 128;
-      group_split_store<HD>(a.dqkv_split, t0 + r, d + h * HD, nbq + blockIdx.y, sX + hg * S, hg, S, r, hh, dk);
-      group_split_store<HD>(a.dqkv_split, t0 + r, 2 * d + h * HD, 2 * nbq + blockIdx.y, sX + 2 * hg * S, hg, S, r,
+      group_split_store<HD>(a.dqkv_split, tr(r), d + h * HD, nbq + blockIdx.y, sX + hg * S, hg, S, r, hh, dk);
+      group_split_store<HD>(a.dqkv_split, tr(r), 2 * d + h * HD, 2 * nbq + blockIdx.y, sX + 2 * hg * S, hg, S, r,
                             hh, dv);
     }
   }

@@ -154,7 +154,7 @@ struct Smem {
 
 // Q, K, V (and dO when `grad`) of (atom, head) into split-fp16 blocks; warp
 // w converts block w (rows past S are zero) with one scale from its maximum.
-__device__ __forceinline__ void load_blocks(Smem &sm, const AttnArgs &a, int t0, int S, int h, bool grad) {
+__device__ __forceinline__ void load_blocks(Smem &sm, const AttnArgs &a, AtomRows tr, int S, int h, bool grad) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp < 3 || grad) {
     float v[8][8];
@@ -163,8 +163,8 @@ __device__ __forceinline__ void load_blocks(Smem &sm, const AttnArgs &a, int t0,
     for (int i = 0; i < 8; ++i) {
       const int task = lane + 32 * i, r = task >> 2, c = (task & 3) * 8;
       if (r < S) {
-        const float *src = warp < 3 ? a.qkv + static_cast<size_t>(t0 + r) * 3 * a.d + warp * a.d + h * kHd + c
-                                    : a.d_out + static_cast<size_t>(t0 + r) * a.d + h * kHd + c;
+        const float *src = warp < 3 ? a.qkv + static_cast<size_t>(tr(r)) * 3 * a.d + warp * a.d + h * kHd + c
+                                    : a.d_out + static_cast<size_t>(tr(r)) * a.d + h * kHd + c;
         const float4 x0 = *reinterpret_cast<const float4 *>(src), x1 = *reinterpret_cast<const float4 *>(src + 4);
         v[i][0] = x0.x; v[i][1] = x0.y; v[i][2] = x0.z; v[i][3] = x0.w;
         v[i][4] = x1.x; v[i][5] = x1.y; v[i][6] = x1.z; v[i][7] = x1.w;
@@ -215,7 +215,7 @@ __device__ __forceinline__ void strip_rowmax(int *rm, const float (&o)[4][4], in
 // Store a 16-row strip (4 n-tiles, columns col0 + 8n + 2 tig) as fp32 into
 // dst (row pitch ld) or, when `o` is set, in split form with the block
 // scales from the cluster's row maxima `rm`.
-__device__ __forceinline__ void strip_store(const float (&v)[4][4], int r0, int S, int t0, int lane, float *dst,
+__device__ __forceinline__ void strip_store(const float (&v)[4][4], int r0, int S, AtomRows tr, int lane, float *dst,
                                             size_t ld, int col0, const Split16View *o, const int *rm, int blk,
                                             bool write_scale) {
   const int g = lane >> 2, tig = lane & 3;
@@ -224,14 +224,14 @@ __device__ __forceinline__ void strip_store(const float (&v)[4][4], int r0, int 
     const int r = r0 + g + 8 * half;
     if (r >= S) continue;
     if (dst) {
-      float *p = dst + static_cast<size_t>(t0 + r) * ld + col0 + 2 * tig;
+      float *p = dst + static_cast<size_t>(tr(r)) * ld + col0 + 2 * tig;
 #pragma unroll
       for (int n = 0; n < 4; ++n) *reinterpret_cast<float2 *>(p + 8 * n) = make_float2(v[n][2 * half], v[n][2 * half + 1]);
     }
     if (o) {
       const int s = split_scale_exponent(__int_as_float(rm[r]));
       const float f = pow2f(s);
-      const size_t off = static_cast<size_t>(t0 + r) * o->cols + col0 + 2 * tig;
+      const size_t off = static_cast<size_t>(tr(r)) * o->cols + col0 + 2 * tig;
 #pragma unroll
       for (int n = 0; n < 4; ++n) {
         uint32_t hh, ll;
@@ -239,7 +239,7 @@ __device__ __forceinline__ void strip_store(const float (&v)[4][4], int r0, int 
         *reinterpret_cast<uint32_t *>(o->hi + off + 8 * n) = hh;
         *reinterpret_cast<uint32_t *>(o->lo + off + 8 * n) = ll;
       }
-      if (write_scale && tig == 0) o->sc[static_cast<size_t>(blk) * o->rows + t0 + r] = static_cast<int8_t>(s);
+      if (write_scale && tig == 0) o->sc[static_cast<size_t>(blk) * split_ld(*o) + tr(r)] = static_cast<int8_t>(s);
     }
   }
 }
@@ -263,7 +263,8 @@ __global__ void __launch_bounds__(2 * MT) k_attn_fwd_mma(AttnArgs a) {
   SmemF<MT> &sm = *reinterpret_cast<SmemF<MT> *>(smem_raw);
   const int atom = blockIdx.x, h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
-  const int e0 = a.offset[atom], S = a.offset[atom + 1] - e0 + 1, t0 = e0 + atom;
+  const int e0 = a.offset[atom], S = a.offset[atom + 1] - e0 + 1;
+  const AtomRows tr = atom_rows(atom, e0, a.edge_base);
   const int NW = (S + 15) >> 4, NK8 = 2 * NW;  // row strips, 8-key tiles
   if (warp < 3) {  // warp w converts block w (Q, K, V; rows past S are zero) at one scale
     float v[MT / 8][8];
@@ -272,7 +273,7 @@ __global__ void __launch_bounds__(2 * MT) k_attn_fwd_mma(AttnArgs a) {
     for (int i = 0; i < MT / 8; ++i) {
       const int task = lane + 32 * i, r = task >> 2, c = (task & 3) * 8;
       if (r < S) {
-        const float *src = a.qkv + static_cast<size_t>(t0 + r) * 3 * a.d + warp * a.d + h * kHd + c;
+        const float *src = a.qkv + static_cast<size_t>(tr(r)) * 3 * a.d + warp * a.d + h * kHd + c;
         const float4 x0 = *reinterpret_cast<const float4 *>(src), x1 = *reinterpret_cast<const float4 *>(src + 4);
         v[i][0] = x0.x; v[i][1] = x0.y; v[i][2] = x0.z; v[i][3] = x0.w;
         v[i][4] = x1.x; v[i][5] = x1.y; v[i][6] = x1.z; v[i][7] = x1.w;
@@ -361,7 +362,7 @@ __global__ void __launch_bounds__(2 * MT) k_attn_fwd_mma(AttnArgs a) {
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int r = q0 + g + 8 * half;
-        if (r < S) a.lse[static_cast<size_t>(t0 + r) * a.heads + h] = m[half] + logf(l[half]);
+        if (r < S) a.lse[static_cast<size_t>(tr(r)) * a.heads + h] = m[half] + logf(l[half]);
       }
     }
     const float inv[2] = {l[0] > 0.f ? 1.0f / l[0] : 0.f, l[1] > 0.f ? 1.0f / l[1] : 0.f};
@@ -390,14 +391,14 @@ __global__ void __launch_bounds__(2 * MT) k_attn_fwd_mma(AttnArgs a) {
     for (int n = 0; n < 4; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) o[n][e] *= fo;
-    if (a.out) strip_store(o, q0, S, t0, lane, a.out, a.d, h * kHd, nullptr, nullptr, 0, false);
+    if (a.out) strip_store(o, q0, S, tr, lane, a.out, a.d, h * kHd, nullptr, nullptr, 0, false);
   }
   if (kSplit) {
     cluster_wait();
     if (act) strip_rowmax(sm.rmax, o, q0, S, lane);
     cluster_barrier();  // every CTA's maxima have reached every CTA
     if (act)
-      strip_store(o, q0, S, t0, lane, nullptr, 0, h * kHd, &a.out_split, sm.rmax, (h * kHd) / 128,
+      strip_store(o, q0, S, tr, lane, nullptr, 0, h * kHd, &a.out_split, sm.rmax, (h * kHd) / 128,
                   cta_rank_in_cluster() == 0);
   }
 }
@@ -465,13 +466,14 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma(AttnArgs a) {
   Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
   const int atom = blockIdx.x, h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
-  const int e0 = a.offset[atom], S = a.offset[atom + 1] - e0 + 1, t0 = e0 + atom;
+  const int e0 = a.offset[atom], S = a.offset[atom + 1] - e0 + 1;
+  const AtomRows tr = atom_rows(atom, e0, a.edge_base);
   const int NW = (S + 15) >> 4, NK8 = 2 * NW;
   const int d = a.d;
-  load_blocks(sm, a, t0, S, h, true);
+  load_blocks(sm, a, tr, S, h, true);
   for (int k = threadIdx.x; k < kMaxTok; k += kThreads) {
     sm.mask[k] = k < S ? (k == 0 ? 0.f : a.key_mask[e0 + k - 1]) : 0.f;
-    sm.lse[k] = k < S ? a.lse[static_cast<size_t>(t0 + k) * a.heads + h] : 0.f;
+    sm.lse[k] = k < S ? a.lse[static_cast<size_t>(tr(k)) * a.heads + h] : 0.f;
     if (kSplit) sm.rmax[0][k] = sm.rmax[1][k] = sm.rmax[2][k] = 0;
   }
   __syncthreads();
@@ -562,9 +564,9 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma(AttnArgs a) {
 
   const size_t ld = 3 * static_cast<size_t>(d);
   if (act && a.d_qkv) {
-    strip_store(dq, r0, S, t0, lane, a.d_qkv, ld, h * kHd, nullptr, nullptr, 0, false);
-    strip_store(dk, r0, S, t0, lane, a.d_qkv, ld, d + h * kHd, nullptr, nullptr, 0, false);
-    strip_store(dv, r0, S, t0, lane, a.d_qkv, ld, 2 * d + h * kHd, nullptr, nullptr, 0, false);
+    strip_store(dq, r0, S, tr, lane, a.d_qkv, ld, h * kHd, nullptr, nullptr, 0, false);
+    strip_store(dk, r0, S, tr, lane, a.d_qkv, ld, d + h * kHd, nullptr, nullptr, 0, false);
+    strip_store(dv, r0, S, tr, lane, a.d_qkv, ld, 2 * d + h * kHd, nullptr, nullptr, 0, false);
   }
   if (kSplit) {
     cluster_wait();
@@ -577,9 +579,9 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma(AttnArgs a) {
     if (act) {
       const int nb = d / 128, blk = (h * kHd) / 128;
       const bool first = cta_rank_in_cluster() == 0;
-      strip_store(dq, r0, S, t0, lane, nullptr, 0, h * kHd, &a.dqkv_split, sm.rmax[0], blk, first);
-      strip_store(dk, r0, S, t0, lane, nullptr, 0, d + h * kHd, &a.dqkv_split, sm.rmax[1], nb + blk, first);
-      strip_store(dv, r0, S, t0, lane, nullptr, 0, 2 * d + h * kHd, &a.dqkv_split, sm.rmax[2], 2 * nb + blk, first);
+      strip_store(dq, r0, S, tr, lane, nullptr, 0, h * kHd, &a.dqkv_split, sm.rmax[0], blk, first);
+      strip_store(dk, r0, S, tr, lane, nullptr, 0, d + h * kHd, &a.dqkv_split, sm.rmax[1], nb + blk, first);
+      strip_store(dv, r0, S, tr, lane, nullptr, 0, 2 * d + h * kHd, &a.dqkv_split, sm.rmax[2], 2 * nb + blk, first);
     }
   }
 }
@@ -665,7 +667,8 @@ __global__ void __launch_bounds__(kTh48, 6) k_attn_bwd_mma48(AttnArgs a) {
   Smem48 &sm = *reinterpret_cast<Smem48 *>(smem_raw);
   const int atom = blockIdx.x, h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
-  const int e0 = a.offset[atom], S = a.offset[atom + 1] - e0 + 1, t0 = e0 + atom;
+  const int e0 = a.offset[atom], S = a.offset[atom + 1] - e0 + 1;
+  const AtomRows tr = atom_rows(atom, e0, a.edge_base);
   const int NW = (S + 15) >> 4, NK8 = 2 * NW;
   const int d = a.d;
   // this warp's block (Q, K or V) in split form
@@ -679,7 +682,7 @@ __global__ void __launch_bounds__(kTh48, 6) k_attn_bwd_mma48(AttnArgs a) {
     for (int i = 0; i < 6; ++i) {
       const int task = lane + 32 * i, r = task >> 2, c = (task & 3) * 8;
       if (r < S) {
-        const float *src = a.qkv + static_cast<size_t>(t0 + r) * 3 * d + warp * d + h * kHd + c;
+        const float *src = a.qkv + static_cast<size_t>(tr(r)) * 3 * d + warp * d + h * kHd + c;
         const float4 x0 = *reinterpret_cast<const float4 *>(src), x1 = *reinterpret_cast<const float4 *>(src + 4);
         v[i][0] = x0.x; v[i][1] = x0.y; v[i][2] = x0.z; v[i][3] = x0.w;
         v[i][4] = x1.x; v[i][5] = x1.y; v[i][6] = x1.z; v[i][7] = x1.w;
@@ -694,7 +697,7 @@ __global__ void __launch_bounds__(kTh48, 6) k_attn_bwd_mma48(AttnArgs a) {
     for (int i = 0; i < 2; ++i) {
       const int task = threadIdx.x + kTh48 * i, r = task >> 2, c = (task & 3) * 8;
       if (r < S) {
-        const float *src = a.d_out + static_cast<size_t>(t0 + r) * d + h * kHd + c;
+        const float *src = a.d_out + static_cast<size_t>(tr(r)) * d + h * kHd + c;
         const float4 x0 = *reinterpret_cast<const float4 *>(src), x1 = *reinterpret_cast<const float4 *>(src + 4);
         gv[i][0] = x0.x; gv[i][1] = x0.y; gv[i][2] = x0.z; gv[i][3] = x0.w;
         gv[i][4] = x1.x; gv[i][5] = x1.y; gv[i][6] = x1.z; gv[i][7] = x1.w;
@@ -723,7 +726,7 @@ __global__ void __launch_bounds__(kTh48, 6) k_attn_bwd_mma48(AttnArgs a) {
     }
     for (int k = threadIdx.x; k < kMT; k += kTh48) {
       sm.mask[k] = k < S ? (k == 0 ? 0.f : a.key_mask[e0 + k - 1]) : 0.f;
-      sm.lse[k] = k < S ? a.lse[static_cast<size_t>(t0 + k) * a.heads + h] : 0.f;
+      sm.lse[k] = k < S ? a.lse[static_cast<size_t>(tr(k)) * a.heads + h] : 0.f;
       if (kSplit) sm.rmax[0][k] = sm.rmax[1][k] = sm.rmax[2][k] = 0;
     }
     gm = warp_absmax(gm);
@@ -822,9 +825,9 @@ __global__ void __launch_bounds__(kTh48, 6) k_attn_bwd_mma48(AttnArgs a) {
 
   const size_t ld = 3 * static_cast<size_t>(d);
   if (act && a.d_qkv) {
-    strip_store(dq, r0, S, t0, lane, a.d_qkv, ld, h * kHd, nullptr, nullptr, 0, false);
-    strip_store(dk, r0, S, t0, lane, a.d_qkv, ld, d + h * kHd, nullptr, nullptr, 0, false);
-    strip_store(dv, r0, S, t0, lane, a.d_qkv, ld, 2 * d + h * kHd, nullptr, nullptr, 0, false);
+    strip_store(dq, r0, S, tr, lane, a.d_qkv, ld, h * kHd, nullptr, nullptr, 0, false);
+    strip_store(dk, r0, S, tr, lane, a.d_qkv, ld, d + h * kHd, nullptr, nullptr, 0, false);
+    strip_store(dv, r0, S, tr, lane, a.d_qkv, ld, 2 * d + h * kHd, nullptr, nullptr, 0, false);
   }
   if (kSplit) {
     cluster_wait();
@@ -837,9 +840,9 @@ __global__ void __launch_bounds__(kTh48, 6) k_attn_bwd_mma48(AttnArgs a) {
     if (act) {
       const int nb = d / 128, blk = (h * kHd) / 128;
       const bool first = cta_rank_in_cluster() == 0;
-      strip_store(dq, r0, S, t0, lane, nullptr, 0, h * kHd, &a.dqkv_split, sm.rmax[0], blk, first);
-      strip_store(dk, r0, S, t0, lane, nullptr, 0, d + h * kHd, &a.dqkv_split, sm.rmax[1], nb + blk, first);
-      strip_store(dv, r0, S, t0, lane, nullptr, 0, 2 * d + h * kHd, &a.dqkv_split, sm.rmax[2], 2 * nb + blk, first);
+      strip_store(dq, r0, S, tr, lane, nullptr, 0, h * kHd, &a.dqkv_split, sm.rmax[0], blk, first);
+      strip_store(dk, r0, S, tr, lane, nullptr, 0, d + h * kHd, &a.dqkv_split, sm.rmax[1], nb + blk, first);
+      strip_store(dv, r0, S, tr, lane, nullptr, 0, 2 * d + h * kHd, &a.dqkv_split, sm.rmax[2], 2 * nb + blk, first);
     }
   }
 }

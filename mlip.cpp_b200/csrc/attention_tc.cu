@@ -99,7 +99,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_attn_fwd_tc(AttnArgs a, int *er
   const int e0 = has_atom ? a.offset[atom] : 0;
   const int S = has_atom ? a.offset[atom + 1] - e0 + 1 : 0;
   const bool valid = r < S;
-  const int tr = e0 + atom + r;  // token row
+  const int tr = atom_rows(atom, e0, a.edge_base)(r);  // token row
   const int d = a.d, ld = 3 * d;
 
   if (warp == 0) {
@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_attn_fwd_tc(AttnArgs a, int *er
       }
       const int s = split_scale_exponent(row_absmax<128>(ob));
       thread_split_store<128>(a.out_split, tr, hg * 128, ob, s);
-      a.out_split.sc[static_cast<size_t>(hg) * a.out_split.rows + tr] = static_cast<int8_t>(s);
+      a.out_split.sc[static_cast<size_t>(hg) * split_ld(a.out_split) + tr] = static_cast<int8_t>(s);
     }
     if (*abort_flag) break;  // read after a barrier: the same for every thread
   }

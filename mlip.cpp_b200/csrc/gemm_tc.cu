@@ -200,7 +200,7 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs &p, int row, int n
     const int s = split_scale_exponent(mx);
     thread_split_store<NC>(p.c_split, rc, n0, acc, s);
     if (!kShared || px->half == 0)
-      p.c_split.sc[static_cast<size_t>(n0 / 128) * p.c_split.rows + rc] = static_cast<int8_t>(s);
+      p.c_split.sc[static_cast<size_t>(n0 / 128) * split_ld(p.c_split) + rc] = static_cast<int8_t>(s);
   }
 }
 
@@ -513,7 +513,7 @@ __device__ __forceinline__ bool epilogue_tma(const GemmArgs &p, const EpiMaps &e
   const bool hasC = p.C != nullptr, hasZ = EPI == EPI_SILU && p.Z != nullptr;
   const bool rs = EPI == EPI_RESID && p.r_split.hi != nullptr;
   // scale of the split residual's 128-column block for this row
-  const float rsf = (rs && valid) ? pow2f(-static_cast<int>(p.r_split.sc[static_cast<size_t>(n0 / 128) * p.r_split.rows + row]))
+  const float rsf = (rs && valid) ? pow2f(-static_cast<int>(p.r_split.sc[static_cast<size_t>(n0 / 128) * split_ld(p.r_split) + row]))
                                   : 0.f;
   if (!kLoad) {  // stores of earlier tiles no longer read the buffers
     if (lane == 0) bulk_wait_read<0>();
@@ -662,7 +662,7 @@ __device__ __forceinline__ bool epilogue_tma(const GemmArgs &p, const EpiMaps &e
       }
     }
     if (valid && (NC == 128 || px->half == 0))
-      p.c_split.sc[static_cast<size_t>(n0 / 128) * p.c_split.rows + row] = static_cast<int8_t>(sx);
+      p.c_split.sc[static_cast<size_t>(n0 / 128) * split_ld(p.c_split) + row] = static_cast<int8_t>(sx);
   }
   return true;
 }
@@ -795,7 +795,7 @@ __device__ __forceinline__ bool epilogue_rows(const GemmArgs &p, const EpiWarp &
       rows_store64(buf, lv, reinterpret_cast<char *>(p.c_split.lo + n0 + 32 * g), pitch, rc, lane);
     }
     if (valid && (NC == 128 || px->half == 0))
-      p.c_split.sc[static_cast<size_t>(n0 / 128) * p.c_split.rows + rc] = static_cast<int8_t>(sx);
+      p.c_split.sc[static_cast<size_t>(n0 / 128) * split_ld(p.c_split) + rc] = static_cast<int8_t>(sx);
   }
   return true;
 }
@@ -989,7 +989,7 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
     const int nch = nk / C::Chunk;
     auto scale_of = [&](int tile, int c) -> int {
       const int r = (tile / tiles_n) * BM + q * 32 + lane;
-      return (tile < tiles && r < p.M) ? static_cast<int>(sc[static_cast<size_t>(c) * p.M + r]) : 0;
+      return (tile < tiles && r < p.M) ? static_cast<int>(sc[static_cast<size_t>(c) * split_ld(p.a_split) + r]) : 0;
     };
     int sc_next = scale_of(blockIdx.x, 0);
     EpiWarp ew{ostage + static_cast<uint32_t>((warp - 2) * C::StageOut), eload0 + 16u * (warp - 2), 0u};
@@ -1252,7 +1252,7 @@ __global__ void __launch_bounds__(384, 1)
       for (int j = 0; j < 128; ++j) acc[j] = 0.f;
       for (int kt0 = 0; kt0 < nk; kt0 += C::Chunk, ++chunk) {
         const int b = chunk % C::TmemBufs;
-        const float sa = row < p.M ? pow2f(-static_cast<int>(sc[static_cast<size_t>(kt0 / C::Chunk) * p.M + row])) : 0.f;
+        const float sa = row < p.M ? pow2f(-static_cast<int>(sc[static_cast<size_t>(kt0 / C::Chunk) * split_ld(p.a_split) + row])) : 0.f;
         if (!wait_or_abort(accf0 + 8 * b, (chunk / C::TmemBufs) & 1, abort_flag)) {
           ok = false;
           break;

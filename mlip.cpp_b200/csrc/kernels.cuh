@@ -26,7 +26,20 @@ struct Split16View {
   uint16_t *lo = nullptr;
   int8_t *sc = nullptr;
   int rows = 0, cols = 0;
+  int ld = 0;  // scale entries between consecutive 128-column blocks (0: rows)
 };
+// Scale of (row, block): sc[block * split_ld(v) + row].
+__host__ __device__ inline int split_ld(const Split16View &v) { return v.ld ? v.ld : v.rows; }
+// Rows [r0, r0 + n) of v as a view of its own.
+inline Split16View split_rows(const Split16View &v, int r0, int n) {
+  Split16View o = v;
+  o.hi = v.hi + static_cast<size_t>(r0) * v.cols;
+  o.lo = v.lo + static_cast<size_t>(r0) * v.cols;
+  o.sc = v.sc + r0;
+  o.rows = n;
+  o.ld = split_ld(v);
+  return o;
+}
 
 struct GemmArgs {
   const float *A = nullptr;
@@ -58,6 +71,9 @@ struct GemmArgs {
 void gemm_f32(const GemmArgs &a, cudaStream_t stream);
 
 // ---- attention over each atom's token block -------------------------------
+// Token rows of a GNN layer: node token of atom i at row i, the token of
+// edge e (CSR order) at row edge_base + e; atom i's sequence is its node
+// token, then its edges.
 struct AttnArgs {
   const float *qkv;       // [T, 3d]  (q | k | v, heads contiguous)
   float *out;             // [T, d]   forward output
@@ -67,12 +83,21 @@ struct AttnArgs {
   const float *key_mask;  // [E] additive mask of each edge key (node key: 0)
   const int *offset;      // [N+1] edge offsets (CSR)
   int n_atoms, d, heads, max_tokens;
+  int edge_base;          // token row of edge 0
   // Optional split-fp16 outputs (then out / d_qkv may be null): the forward
   // output [T, d] and the backward result [T, 3d].  Needs 128 / head size
   // heads per CTA, one 128-column block.
   Split16View out_split;
   Split16View dqkv_split;
 };
+// Row of token k (0: the node) of one atom's sequence.
+struct AtomRows {
+  int node, ebase;  // ebase + k is the row of token k >= 1
+  __host__ __device__ int operator()(int k) const { return k == 0 ? node : ebase + k; }
+};
+__host__ __device__ inline AtomRows atom_rows(int atom, int e0, int edge_base) {
+  return AtomRows{atom, edge_base + e0 - 1};
+}
 void attention_fwd(const AttnArgs &a, cudaStream_t stream);
 // Tensor-core forward (attention_tc.cu): head size 32, at most 64 tokens per
 // atom, heads a multiple of 4.  `err` (device int) is set if a wait times out.

@@ -70,7 +70,7 @@ struct LayerW {
 struct Acts {
   // graph
   float *r, *fc, *dfc_dr, *key_mask;
-  int *edge_row, *node_row, *nbr_species, *rev;
+  int *nbr_species, *rev;
   // kept for backward
   float *qkv[4], *xa[4], *ra[4], *zf[4], *xm[4], *rm[4], *lse[4];
   float *zc[2], *zn1[2], *zn2[2], *ze1[2], *ze2[2];
@@ -492,7 +492,7 @@ static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, const Counts
   // persistent (graph + activations kept for backward)
   a.r = P.take<float>(E0); a.fc = P.take<float>(E0); a.dfc_dr = P.take<float>(E0);
   a.key_mask = P.take<float>(E0);
-  a.edge_row = P.take<int>(E0); a.node_row = P.take<int>(N0); a.nbr_species = P.take<int>(E0);
+  a.nbr_species = P.take<int>(E0);
   a.rev = P.take<int>(E0);
   for (int b = 0; b < 4; ++b) {
     const size_t T = b < 2 ? T0 : T1;
@@ -564,9 +564,10 @@ void PETModel::forward_backward(bool grad) {
   // Split-fp16 operands of the chain mode: each producer takes the next
   // buffer; the GEMM that consumes it runs before the buffer comes round
   // again, and a GEMM that writes a split result writes the other buffer.
-  int next_sp = 0;
+  int next_sp = 0, last_sp = 0;
   auto take_split = [&](int rows, int cols) {
     const Split16View v = split_view(next_sp, rows, cols);
+    last_sp = next_sp;
     next_sp ^= 1;
     return v;
   };
@@ -630,9 +631,11 @@ void PETModel::forward_backward(bool grad) {
   at.d = d;
   at.heads = h.heads;
   at.max_tokens = max_tok_;
+  at.edge_base = N;
 
   // Transformer block b on input x (its split form sx in chain mode); the
-  // output goes to `out`, and in chain mode also to *sout when non-null.
+  // output goes to `out` when non-null, and in chain mode also to *sout when
+  // non-null.
   auto block_fwd = [&](int b, const float *x, const Split16View *sx, float *out, Split16View *sout) {
     const BlockW &B = g_lw[b / 2].blk[b % 2];
     gemm(x, d, nullptr, B.Win, d, a.qkv[b], 3 * d, nullptr, T, 3 * d, d, B.bin, EPI_STORE, s, nullptr, 0, nullptr,
@@ -659,19 +662,22 @@ void PETModel::forward_backward(bool grad) {
     gemm(a.hf, f, nullptr, B.W3, f, a.xm[b], d, nullptr, T, d, f, B.b3, EPI_RESID, s, nullptr, 0, ch ? nullptr : a.x1, d,
          SplitIO{ch ? &shf : nullptr, true, nullptr, ch ? &sx1 : nullptr});
     if (ch && sout) *sout = take_split(T, d);
-    // a block output with a split form feeds only the next block: no fp32 copy
-    layer_norm_fwd(a.xm[b], B.gm, B.bm, (ch && sout) ? nullptr : out, a.rm[b], T, d, s, ch ? sout : nullptr);
+    layer_norm_fwd(a.xm[b], B.gm, B.bm, out, a.rm[b], T, d, s, ch ? sout : nullptr);
   };
-  // Energy head (node or edge) on rows `rows` of the layer output.
-  auto head_fwd = [&](const float *x, const int *rows, int M, const HeadW &hw, float *y1, float *y2, float *z1,
+  // Energy head (node or edge) on rows [row0, row0 + M) of the layer output:
+  // x in fp32, or in chain mode its split form sxl (in split buffer fin_sp;
+  // the head's hidden layer takes the other buffer).
+  Split16View sxl;
+  int fin_sp = 0;
+  auto head_fwd = [&](const float *x, int row0, int M, const HeadW &hw, float *y1, float *y2, float *z1,
                       float *z2) {
     Split16View sa, sy;
     if (ch) {
-      sa = take_split(M, d);  // row-gathered copy of x
-      sy = take_split(M, r);
+      sa = split_rows(sxl, row0, M);
+      sy = split_view(fin_sp ^ 1, M, r);
     }
-    gemm(x, d, rows, hw.H0, d, y1, r, nullptr, M, r, d, hw.h0, EPI_SILU, s, keep(z1), r, nullptr, 0,
-         SplitIO{ch ? &sa : nullptr, false, ch ? &sy : nullptr});
+    gemm(x ? x + static_cast<size_t>(row0) * d : nullptr, d, nullptr, hw.H0, d, y1, r, nullptr, M, r, d, hw.h0,
+         EPI_SILU, s, keep(z1), r, nullptr, 0, SplitIO{ch ? &sa : nullptr, true, ch ? &sy : nullptr});
     gemm(y1, r, nullptr, hw.H2, r, y2, r, nullptr, M, r, r, hw.h2, EPI_SILU, s, keep(z2), r, nullptr, 0,
          SplitIO{ch ? &sy : nullptr});
   };
@@ -686,13 +692,14 @@ void PETModel::forward_backward(bool grad) {
     E = El_[l];
     T = Tl_[l];
     at.n_atoms = N;
+    at.edge_base = N;
     Split16View sx;
     if (E > 0) {
       FeaturizeArgs fa{};
       fa.n_edges = E; fa.d = d; fa.layer = l; fa.aux = h.aux;
       fa.vec = nl_.vec.as<float>(); fa.r = a.r;
-      fa.nbr_species = a.nbr_species; fa.rev = a.rev; fa.edge_row = a.edge_row;
-      fa.emb0 = emb0; fa.x_prev = a.xl[0];
+      fa.nbr_species = a.nbr_species; fa.rev = a.rev;
+      fa.emb0 = emb0; fa.x_prev = a.xl[0]; fa.prev_base = Nl_[0];
       fa.cat = a.cat;
       Split16View scat, shc;
       if (ch) {
@@ -703,21 +710,31 @@ void PETModel::forward_backward(bool grad) {
       if (ch) shc = take_split(E, H);
       gemm(a.cat, K, nullptr, L.C0f, K, a.hc, H, nullptr, E, H, K, nullptr, EPI_SILU, s, keep(a.zc[l]), H, nullptr, 0,
            SplitIO{ch ? &scat : nullptr, true, ch ? &shc : nullptr});
-      if (ch) sx = take_split(T, d);
-      gemm(a.hc, H, nullptr, L.C2, H, ch ? nullptr : a.xin, d, a.edge_row, E, d, H, L.c2, EPI_STORE, s, nullptr, 0,
-           nullptr, 0, SplitIO{ch ? &shc : nullptr, true, ch ? &sx : nullptr});
+      // edge tokens: rows [N, N + E) of the layer's tokens
+      Split16View sxe;
+      if (ch) {
+        sx = take_split(T, d);
+        sxe = split_rows(sx, N, E);
+      }
+      gemm(a.hc, H, nullptr, L.C2, H, ch ? nullptr : a.xin + static_cast<size_t>(N) * d, d, nullptr, E, d, H, L.c2,
+           EPI_STORE, s, nullptr, 0, nullptr, 0, SplitIO{ch ? &shc : nullptr, true, ch ? &sxe : nullptr});
     } else if (ch) {
       sx = take_split(T, d);
     }
-    node_tokens(L.node_emb, species, a.node_row, ch ? nullptr : a.xin, N, d, s, ch ? &sx : nullptr);
+    node_tokens(L.node_emb, species, ch ? nullptr : a.xin, N, d, s, ch ? &sx : nullptr);
     Split16View smid;
-    block_fwd(2 * l, a.xin, ch ? &sx : nullptr, a.xmid, ch ? &smid : nullptr);
-    block_fwd(2 * l + 1, a.xmid, ch ? &smid : nullptr, a.xl[l], nullptr);
-    // readout (pet_layers.cpp:920-1015) of the N1 atoms whose energy counts
-    head_fwd(a.xl[l], a.node_row, N1, L.node, a.yn1, a.yn2, a.zn1[l], a.zn2[l]);
+    block_fwd(2 * l, a.xin, ch ? &sx : nullptr, ch ? nullptr : a.xmid, ch ? &smid : nullptr);
+    // layer output: fp32 for the next layer's messages (layer 0) and the
+    // fp32 path; in chain mode the readout reads its split form
+    block_fwd(2 * l + 1, a.xmid, ch ? &smid : nullptr, (ch && l > 0) ? nullptr : a.xl[l], ch ? &sxl : nullptr);
+    fin_sp = last_sp;
+    const float *xo = ch ? nullptr : a.xl[l];
+    // readout (pet_layers.cpp:920-1015) of the N1 atoms whose energy counts:
+    // node rows [0, N1), edge rows [N, N + E1)
+    head_fwd(xo, 0, N1, L.node, a.yn1, a.yn2, a.zn1[l], a.zn2[l]);
     head_last(a.yn2, L.node.HL, L.node.hl, a.node_pred, N1, r, s);
     if (E1 > 0) {
-      head_fwd(a.xl[l], a.edge_row, E1, L.edge, a.ye1, a.ye2, a.ze1[l], a.ze2[l]);
+      head_fwd(xo, N, E1, L.edge, a.ye1, a.ye2, a.ze1[l], a.ze2[l]);
       head_last(a.ye2, L.edge.HL, L.edge.hl, a.edge_pred, E1, r, s);
       add_vec(a.edge_pred, a.gfc, E1, l > 0, s);
     }
@@ -727,8 +744,8 @@ void PETModel::forward_backward(bool grad) {
     for (int p = 0; p < 2; ++p) {
       const PropW &P = L.nc[p];
       if (!P.loaded || !(p == 0 ? ncf_ : ncs_)) continue;
-      head_fwd(a.xl[l], a.node_row, N1, P.node, a.yn1, a.yn2, nullptr, nullptr);
-      if (E1 > 0) head_fwd(a.xl[l], a.edge_row, E1, P.edge, a.ye1, a.ye2, nullptr, nullptr);
+      head_fwd(xo, 0, N1, P.node, a.yn1, a.yn2, nullptr, nullptr);
+      if (E1 > 0) head_fwd(xo, N, E1, P.edge, a.ye1, a.ye2, nullptr, nullptr);
       nc_readout(a.yn2, E1 > 0 ? a.ye2 : nullptr, P.node.HL, P.node.hl, P.edge.HL, P.edge.hl, a.fc, offset,
                  p == 0 ? a.ncF : a.ncS, N1, r, p == 0 ? 3 : 9, s);
     }
@@ -737,7 +754,8 @@ void PETModel::forward_backward(bool grad) {
   if (!grad) return;
 
   // ---- backward ----------------------------------------------------------
-  auto head_bwd = [&](const HeadW &hw, const float *z1, const float *z2, const float *scale, const int *rows, int M,
+  // gradient of the head's input into rows [row0, row0 + M) of dst
+  auto head_bwd = [&](const HeadW &hw, const float *z1, const float *z2, const float *scale, int row0, int M,
                       float *dst) {
     Split16View s2, s1;
     if (ch) s2 = take_split(M, r);
@@ -745,13 +763,13 @@ void PETModel::forward_backward(bool grad) {
     if (ch) s1 = take_split(M, r);
     gemm(a.dz2, r, nullptr, hw.H2T, r, a.dz1, r, nullptr, M, r, r, nullptr, EPI_DSILU, s, const_cast<float *>(z1), r,
          nullptr, 0, SplitIO{ch ? &s2 : nullptr, true, ch ? &s1 : nullptr});
-    gemm(a.dz1, r, nullptr, hw.H0T, r, dst, d, rows, M, d, r, nullptr, EPI_STORE, s, nullptr, 0, nullptr, 0,
-         SplitIO{ch ? &s1 : nullptr});
+    gemm(a.dz1, r, nullptr, hw.H0T, r, dst + static_cast<size_t>(row0) * d, d, nullptr, M, d, r, nullptr, EPI_STORE,
+         s, nullptr, 0, nullptr, 0, SplitIO{ch ? &s1 : nullptr});
   };
   auto readout_bwd = [&](int l, float *dst) {
     const LayerW &L = g_lw[l];
-    head_bwd(L.node, a.zn1[l], a.zn2[l], nullptr, a.node_row, N1, dst);
-    if (E1 > 0) head_bwd(L.edge, a.ze1[l], a.ze2[l], a.fc, a.edge_row, E1, dst);
+    head_bwd(L.node, a.zn1[l], a.zn2[l], nullptr, 0, N1, dst);
+    if (E1 > 0) head_bwd(L.edge, a.ze1[l], a.ze2[l], a.fc, Nl_[l], E1, dst);
   };
   auto block_bwd = [&](int b, const float *dy, float *dxin) {
     const BlockW &B = g_lw[b / 2].blk[b % 2];
@@ -785,10 +803,11 @@ void PETModel::forward_backward(bool grad) {
     const LayerW &L = g_lw[l];
     Split16View sa, sz;
     if (ch) {
-      sa = take_split(E, d);  // row-gathered copy of dtok
+      sa = take_split(E, d);  // split copy of the edge rows of dtok
       sz = take_split(E, H);
     }
-    gemm(dtok, d, a.edge_row, L.C2T, d, a.dzc, H, nullptr, E, H, d, nullptr, EPI_DSILU, s, a.zc[l], H, nullptr, 0,
+    gemm(dtok + static_cast<size_t>(Nl_[l]) * d, d, nullptr, L.C2T, d, a.dzc, H, nullptr, E, H, d, nullptr, EPI_DSILU,
+         s, a.zc[l], H, nullptr, 0,
          SplitIO{ch ? &sa : nullptr, false, ch ? &sz : nullptr});
     if (l == 1)
       gemm(a.dzc, H, nullptr, L.C0T + static_cast<size_t>(2) * d * H, H, a.dmsg, d, nullptr, E, d, H, nullptr,
@@ -801,6 +820,7 @@ void PETModel::forward_backward(bool grad) {
   // atoms beyond N1 receive gradient only through the reversed messages.
   N = N1; E = E1; T = Tl_[1];
   at.n_atoms = N;
+  at.edge_base = N;
   if (E0 > 0) CUDA_CHECK(cudaMemsetAsync(a.g4, 0, sizeof(float) * 4 * E0, s));
   readout_bwd(1, a.dx);
   block_bwd(3, a.dx, a.dx2);
@@ -808,9 +828,10 @@ void PETModel::forward_backward(bool grad) {
   if (E > 0) compress_bwd(1, a.dx, true);
   N = Nl_[0]; E = E0; T = T0;
   at.n_atoms = N;
+  at.edge_base = N;
   if (T0 > Tl_[1]) CUDA_CHECK(cudaMemsetAsync(a.dx, 0, sizeof(float) * static_cast<size_t>(T0) * d, s));
   readout_bwd(0, a.dx);
-  if (E1 > 0) message_bwd(a.dmsg, d, a.rev, a.edge_row, a.dx, E0, E1, d, s);
+  if (E1 > 0) message_bwd(a.dmsg, d, a.rev, Nl_[0], a.dx, E0, E1, d, s);
   block_bwd(1, a.dx, a.dx2);
   block_bwd(0, a.dx2, a.dx);
   if (E0 > 0) {
@@ -858,7 +879,7 @@ void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const in
   ep.vec = nl_.vec.as<float>(); ep.dist_nl = nl_.dist.as<float>();
   ep.cutoff = h_.cutoff; ep.width = h_.width;
   ep.r = a.r; ep.fc = a.fc; ep.dfc_dr = a.dfc_dr; ep.key_mask = a.key_mask;
-  ep.edge_row = a.edge_row; ep.node_row = a.node_row; ep.nbr_species = a.nbr_species; ep.rev = a.rev;
+  ep.nbr_species = a.nbr_species; ep.rev = a.rev;
   edge_prep(ep, stream_);
 }
 

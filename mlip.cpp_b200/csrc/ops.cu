@@ -26,7 +26,6 @@ __global__ void k_edge_prep(EdgePrepArgs a) {
   const float off = (a.width - a.cutoff) * inv_delta;
   const int total = a.n_edges > a.n_atoms ? a.n_edges : a.n_atoms;
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
-    if (e < a.n_atoms) a.node_row[e] = a.offset[e] + e;
     if (e >= a.n_edges) continue;
     const int i = a.center[e], j = a.nbr[e];
     const float x = a.vec[3 * e], y = a.vec[3 * e + 1], z = a.vec[3 * e + 2];
@@ -50,7 +49,6 @@ __global__ void k_edge_prep(EdgePrepArgs a) {
     a.key_mask[e] = fcm > 0.0f
         ? __half2float(__float2half_rn(static_cast<float>(log(static_cast<double>(fcm)))))
         : -INFINITY;
-    a.edge_row[e] = e + i + 1;
     a.nbr_species[e] = a.species[j];
     // reverse edge (j -> i, -S); the reference's hash map keeps the last edge
     // inserted under a key, so the last match wins (pet_batch.cpp:416-436)
@@ -78,7 +76,7 @@ __device__ __forceinline__ float feat_value(const FeaturizeArgs &a, int e, int c
     if (c < d) {
       const int rv = a.rev[e];
       const float m0 = a.emb0[static_cast<size_t>(sp) * d + c];
-      const float mr = rv >= 0 ? a.x_prev[static_cast<size_t>(a.edge_row[rv]) * d + c] : 0.0f;
+      const float mr = rv >= 0 ? a.x_prev[static_cast<size_t>(a.prev_base + rv) * d + c] : 0.0f;
       return 0.5f * (m0 + mr);
     }
     c -= d;
@@ -107,7 +105,7 @@ __global__ void k_featurize_split(FeaturizeArgs a) {
   if (a.layer > 0) {  // message: 0.5 (embedding[nbr species] + X0[row(reverse edge)])
     const int rv = a.rev[e];
     const float *m0 = a.emb0 + static_cast<size_t>(sp) * d;
-    const float *mr = rv >= 0 ? a.x_prev + static_cast<size_t>(a.edge_row[rv]) * d : nullptr;
+    const float *mr = rv >= 0 ? a.x_prev + static_cast<size_t>(a.prev_base + rv) * d : nullptr;
     for (int k = 0; k < nbd; ++k) {
       const int c = k * 128 + lane * 4;
       const float4 p = __ldg(reinterpret_cast<const float4 *>(m0 + c));
@@ -127,26 +125,25 @@ __global__ void k_featurize_split(FeaturizeArgs a) {
   }
 }
 
-__global__ void k_node_tokens(const float *__restrict__ tab, const int *__restrict__ sp,
-                              const int *__restrict__ node_row, float *__restrict__ x, int n, int d) {
+__global__ void k_node_tokens(const float *__restrict__ tab, const int *__restrict__ sp, float *__restrict__ x,
+                              int n, int d) {
   const int64_t total = static_cast<int64_t>(n) * d;
   for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
        t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int i = static_cast<int>(t / d), c = static_cast<int>(t % d);
-    x[static_cast<size_t>(node_row[i]) * d + c] = tab[static_cast<size_t>(sp[i]) * d + c];
+    x[static_cast<size_t>(i) * d + c] = tab[static_cast<size_t>(sp[i]) * d + c];
   }
 }
 
 // Node tokens with the split-fp16 form of the same rows: warp per (atom, block).
 __global__ void k_node_tokens_split(const float *__restrict__ tab, const int *__restrict__ sp,
-                                    const int *__restrict__ node_row, float *__restrict__ x, int n, int d,
-                                    Split16View xs) {
+                                    float *__restrict__ x, int n, int d, Split16View xs) {
   const int nb = d / 128;
   const int64_t w = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= static_cast<int64_t>(n) * nb) return;
   const int i = static_cast<int>(w / nb), blk = static_cast<int>(w % nb);
-  const int c = blk * 128 + lane * 4, row = node_row[i];
+  const int c = blk * 128 + lane * 4, row = i;
   const float4 v = *reinterpret_cast<const float4 *>(tab + static_cast<size_t>(sp[i]) * d + c);
   if (x) *reinterpret_cast<float4 *>(x + static_cast<size_t>(row) * d + c) = v;  // x null: split only
   warp_split_block(xs, row, blk, v, lane);
@@ -229,7 +226,7 @@ __global__ void k_edge_xyzr_bwd_split(Split16View dzs, const float *__restrict__
       const size_t off = static_cast<size_t>(e) * H + 128 * k + 4 * lane;
       const uint2 hv = *reinterpret_cast<const uint2 *>(dzs.hi + off);
       const uint2 lv = *reinterpret_cast<const uint2 *>(dzs.lo + off);
-      const float f = pow2f(-static_cast<int>(dzs.sc[static_cast<size_t>(k) * dzs.rows + e]));
+      const float f = pow2f(-static_cast<int>(dzs.sc[static_cast<size_t>(k) * split_ld(dzs) + e]));
       const float2 h0 = __half22float2(*reinterpret_cast<const __half2 *>(&hv.x));
       const float2 h1 = __half22float2(*reinterpret_cast<const __half2 *>(&hv.y));
       const float2 l0 = __half22float2(*reinterpret_cast<const __half2 *>(&lv.x));
@@ -290,15 +287,15 @@ __global__ void k_edge_xyzr_bwd(const float *__restrict__ dz, const float *__res
 }
 
 // Warp per edge, 16-byte accesses along the row (d, ld multiples of 4).
-__global__ void k_message_bwd(const float *__restrict__ dmsg, int ld, const int *__restrict__ rev,
-                              const int *__restrict__ edge_row, float *__restrict__ dx, int n_edges,
+__global__ void k_message_bwd(const float *__restrict__ dmsg, int ld, const int *__restrict__ rev, int base,
+                              float *__restrict__ dx, int n_edges,
                               int n_msg, int d) {
   const int lane = threadIdx.x & 31;
   for (int x = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; x < n_edges; x += (gridDim.x * blockDim.x) >> 5) {
     const int rv = rev[x];
     if (rv < 0 || rv >= n_msg) continue;
     const float4 *src = reinterpret_cast<const float4 *>(dmsg + static_cast<size_t>(rv) * ld);
-    float4 *dst = reinterpret_cast<float4 *>(dx + static_cast<size_t>(edge_row[x]) * d);
+    float4 *dst = reinterpret_cast<float4 *>(dx + static_cast<size_t>(base + x) * d);
     for (int c = lane; c < d / 4; c += 32) {
       const float4 m = src[c];
       float4 v = dst[c];
@@ -564,15 +561,15 @@ void featurize(const FeaturizeArgs &a, cudaStream_t s) {
   CUDA_LAUNCH_CHECK();
 }
 
-void node_tokens(const float *table, const int *species, const int *node_row, float *x, int n,
-                 int d, cudaStream_t s, const Split16View *xs) {
+void node_tokens(const float *table, const int *species, float *x, int n, int d, cudaStream_t s,
+                 const Split16View *xs) {
   if (n <= 0) return;
   if (xs) {
     if (d % 128) throw Error(kErrInternal, "node_tokens: split output needs a multiple of 128 columns");
     k_node_tokens_split<<<ceil_div(static_cast<int64_t>(n) * (d / 128) * 32, 256), 256, 0, s>>>(
-        table, species, node_row, x, n, d, *xs);
+        table, species, x, n, d, *xs);
   } else {
-    k_node_tokens<<<grid_for(static_cast<int64_t>(n) * d, 256), 256, 0, s>>>(table, species, node_row, x, n, d);
+    k_node_tokens<<<grid_for(static_cast<int64_t>(n) * d, 256), 256, 0, s>>>(table, species, x, n, d);
   }
   CUDA_LAUNCH_CHECK();
 }
@@ -629,11 +626,11 @@ void edge_xyzr_bwd(const float *dz, const Split16View *dzs, const float *P, floa
   CUDA_LAUNCH_CHECK();
 }
 
-void message_bwd(const float *dmsg, int ld, const int *rev, const int *edge_row, float *dx,
+void message_bwd(const float *dmsg, int ld, const int *rev, int base, float *dx,
                  int n_edges, int n_msg, int d, cudaStream_t s) {
   if (n_edges <= 0) return;
   if (d % 4 || ld % 4) throw Error(kErrInternal, "message_bwd: rows must be multiples of 4 floats");
-  k_message_bwd<<<grid_for(static_cast<int64_t>(n_edges) * 32, 256), 256, 0, s>>>(dmsg, ld, rev, edge_row, dx,
+  k_message_bwd<<<grid_for(static_cast<int64_t>(n_edges) * 32, 256), 256, 0, s>>>(dmsg, ld, rev, base, dx,
                                                                                   n_edges, n_msg, d);
   CUDA_LAUNCH_CHECK();
 }

@@ -15,11 +15,11 @@ struct EdgePrepArgs {
   float cutoff, width;
   // outputs
   float *r, *fc, *dfc_dr, *key_mask;
-  int *edge_row, *node_row, *nbr_species, *rev;
+  int *nbr_species, *rev;
 };
 // r, f_c and df_c/dr in-graph (pet.cpp:208-256); the fp16 log-cutoff key
 // mask from the neighbour-list distance (pet_batch.cpp:37-47,603-653); token
-// rows; neighbour species; reverse edge (pet_batch.cpp:399-495).
+// neighbour species; reverse edge (pet_batch.cpp:399-495).
 void edge_prep(const EdgePrepArgs &a, cudaStream_t s);
 
 // Input rows of the compression's first linear (build_tokens,
@@ -36,8 +36,9 @@ void edge_prep(const EdgePrepArgs &a, cudaStream_t s);
 struct FeaturizeArgs {
   int n_edges, d, layer, aux;
   const float *vec, *r;
-  const int *nbr_species, *rev, *edge_row;
-  const float *emb0, *x_prev;
+  const int *nbr_species, *rev;
+  const float *emb0, *x_prev;  // x_prev: layer-0 output tokens, edge e at row prev_base + e
+  int prev_base;
   float *cat;
   Split16View cat_split;  // if set, cat is written in split-fp16 form only
 };
@@ -45,8 +46,9 @@ void featurize(const FeaturizeArgs &a, cudaStream_t s);
 // Columns of a featurised row: the message (layer 1) plus the auxiliary block.
 __host__ __device__ inline int featurize_cols(int layer, int d, int aux) { return (layer > 0 ? d : 0) + aux; }
 
-// X[node_row[i], :] = table[species[i], :]  (xs: the same rows in split form too)
-void node_tokens(const float *table, const int *species, const int *node_row, float *x, int n,
+// X[i, :] = table[species[i], :] for the n node-token rows (xs: the same
+// rows in split form too)
+void node_tokens(const float *table, const int *species, float *x, int n,
                  int d, cudaStream_t s, const Split16View *xs = nullptr);
 
 // pred[m] = dot(y[m, :], w) + b
@@ -69,8 +71,8 @@ void add_vec(const float *x, float *y, int n, bool accumulate, cudaStream_t s);
 // dz is [n_edges][H] fp32, or in split form when dzs is given.
 void edge_xyzr_bwd(const float *dz, const Split16View *dzs, const float *P, float *g4, int n_edges, int H,
                    bool accumulate, cudaStream_t s);
-// dX[edge_row[x], :] += 0.5 dmsg[rev[x], :]   for 0 <= rev[x] < n_msg
-void message_bwd(const float *dmsg, int ld, const int *rev, const int *edge_row, float *dx,
+// dX[base + x, :] += 0.5 dmsg[rev[x], :]   for 0 <= rev[x] < n_msg
+void message_bwd(const float *dmsg, int ld, const int *rev, int base, float *dx,
                  int n_edges, int n_msg, int d, cudaStream_t s);
 // g[e] = g4[e, 0:3] + (g4[e, 3] + gfc[e] dfc_dr[e]) vec[e] / r[e]
 void edge_grad(const float *g4, const float *gfc, const float *dfc_dr, const float *vec,

@@ -51,7 +51,7 @@ __device__ __forceinline__ void warp_split_block(const Split16View &o, int row, 
   const size_t off = static_cast<size_t>(row) * o.cols + blk * 128 + lane * 4;
   *reinterpret_cast<uint2 *>(o.hi + off) = make_uint2(h0, h1);
   *reinterpret_cast<uint2 *>(o.lo + off) = make_uint2(l0, l1);
-  if (lane == 0) o.sc[static_cast<size_t>(blk) * o.rows + row] = static_cast<int8_t>(s);
+  if (lane == 0) o.sc[static_cast<size_t>(blk) * split_ld(o) + row] = static_cast<int8_t>(s);
 }
 
 // One thread: n consecutive values (n a multiple of 8) of one row segment
