@@ -171,7 +171,7 @@ const float *PETModel::w(const std::string &name) const {
 const float *PETModel::device_forces() const { return in_->a.F; }
 
 size_t PETModel::device_bytes() const {
-  return wbuf_.cap + persist_.cap + scratch_.cap + sp_[0].cap + sp_[1].cap + nl_.center.cap * 10;
+  return wbuf_.cap + persist_.cap + scratch_.cap + sp_[0].cap + sp_[1].cap + sp_[2].cap + nl_.center.cap * 10;
 }
 
 // ---------------------------------------------------------------------------
@@ -771,7 +771,9 @@ void PETModel::forward_backward(bool grad) {
     head_bwd(L.node, a.zn1[l], a.zn2[l], nullptr, 0, N1, dst);
     if (E1 > 0) head_bwd(L.edge, a.ze1[l], a.ze2[l], a.fc, Nl_[l], E1, dst);
   };
-  auto block_bwd = [&](int b, const float *dy, float *dxin) {
+  // dxin: the block input's gradient in fp32; in chain mode it goes instead
+  // to *sdxin in split form when that is given
+  auto block_bwd = [&](int b, const float *dy, float *dxin, const Split16View *sdxin = nullptr) {
     const BlockW &B = g_lw[b / 2].blk[b % 2];
     Split16View sdu, sdhf, sdu2, sdq;
     if (ch) sdu = take_split(T, d);
@@ -796,19 +798,21 @@ void PETModel::forward_backward(bool grad) {
     }
     attn(true, at);
     at.dqkv_split = Split16View{};
-    gemm(a.dqkv, 3 * d, nullptr, B.WinT, 3 * d, dxin, d, nullptr, T, d, 3 * d, nullptr, EPI_RESID, s, nullptr,
-         0, ch ? nullptr : a.du, d, SplitIO{ch ? &sdq : nullptr, true, nullptr, ch ? &sdu2 : nullptr});
+    const bool sout = ch && sdxin;
+    gemm(a.dqkv, 3 * d, nullptr, B.WinT, 3 * d, sout ? nullptr : dxin, d, nullptr, T, d, 3 * d, nullptr, EPI_RESID, s,
+         nullptr, 0, ch ? nullptr : a.du, d,
+         SplitIO{ch ? &sdq : nullptr, true, sout ? sdxin : nullptr, ch ? &sdu2 : nullptr});
   };
-  auto compress_bwd = [&](int l, const float *dtok, bool accumulate) {
+  // dtok: the token gradient (fp32; in chain mode its split form sdtok)
+  auto compress_bwd = [&](int l, const float *dtok, const Split16View *sdtok, bool accumulate) {
     const LayerW &L = g_lw[l];
     Split16View sa, sz;
     if (ch) {
-      sa = take_split(E, d);  // split copy of the edge rows of dtok
+      sa = split_rows(*sdtok, Nl_[l], E);  // the edge rows
       sz = take_split(E, H);
     }
-    gemm(dtok + static_cast<size_t>(Nl_[l]) * d, d, nullptr, L.C2T, d, a.dzc, H, nullptr, E, H, d, nullptr, EPI_DSILU,
-         s, a.zc[l], H, nullptr, 0,
-         SplitIO{ch ? &sa : nullptr, false, ch ? &sz : nullptr});
+    gemm(ch ? nullptr : dtok + static_cast<size_t>(Nl_[l]) * d, d, nullptr, L.C2T, d, a.dzc, H, nullptr, E, H, d,
+         nullptr, EPI_DSILU, s, a.zc[l], H, nullptr, 0, SplitIO{ch ? &sa : nullptr, true, ch ? &sz : nullptr});
     if (l == 1)
       gemm(a.dzc, H, nullptr, L.C0T + static_cast<size_t>(2) * d * H, H, a.dmsg, d, nullptr, E, d, H, nullptr,
            EPI_STORE, s, nullptr, 0, nullptr, 0, SplitIO{ch ? &sz : nullptr});
@@ -824,8 +828,11 @@ void PETModel::forward_backward(bool grad) {
   if (E0 > 0) CUDA_CHECK(cudaMemsetAsync(a.g4, 0, sizeof(float) * 4 * E0, s));
   readout_bwd(1, a.dx);
   block_bwd(3, a.dx, a.dx2);
-  block_bwd(2, a.dx2, a.dx);
-  if (E > 0) compress_bwd(1, a.dx, true);
+  // the first block's input gradient feeds only the compression backward
+  Split16View sdx;
+  if (ch) sdx = split_view(2, T, d);
+  block_bwd(2, a.dx2, a.dx, ch ? &sdx : nullptr);
+  if (E > 0) compress_bwd(1, a.dx, ch ? &sdx : nullptr, true);
   N = Nl_[0]; E = E0; T = T0;
   at.n_atoms = N;
   at.edge_base = N;
@@ -833,9 +840,10 @@ void PETModel::forward_backward(bool grad) {
   readout_bwd(0, a.dx);
   if (E1 > 0) message_bwd(a.dmsg, d, a.rev, Nl_[0], a.dx, E0, E1, d, s);
   block_bwd(1, a.dx, a.dx2);
-  block_bwd(0, a.dx2, a.dx);
+  if (ch) sdx = split_view(2, T, d);
+  block_bwd(0, a.dx2, a.dx, ch ? &sdx : nullptr);
   if (E0 > 0) {
-    compress_bwd(0, a.dx, true);
+    compress_bwd(0, a.dx, ch ? &sdx : nullptr, true);
     edge_grad(a.g4, a.gfc, a.dfc_dr, nl_.vec.as<float>(), a.r, a.g, E0, s);
   }
   if (n_local_ > Nl_[0]) CUDA_CHECK(cudaMemsetAsync(a.F, 0, sizeof(float) * 3 * n_local_, s));
@@ -867,6 +875,8 @@ void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const in
     const size_t mk = static_cast<size_t>(std::max(Tl_[0], Tl_[1])) * kmax;
     sp_[0].ensure(mk * 4 + mk / 128 + 256);
     if (chain_) sp_[1].ensure(mk * 4 + mk / 128 + 256);
+    const size_t md = static_cast<size_t>(std::max(Tl_[0], Tl_[1])) * h_.d;
+    if (chain_ && grad) sp_[2].ensure(md * 4 + md / 128 + 256);
   }
   P = Plan{persist_.as<char>(), 0};
   S = Plan{scratch_.as<char>(), 0};

@@ -163,7 +163,9 @@ class PETModel {
   // fp32.  In chain mode (every dense layer on 3xFP16) the kernels that
   // produce a GEMM's A operand write it in split form, alternating between
   // sp_[0] and sp_[1]; each is consumed by the next GEMM.
-  DevBuf sp_[2];
+  // sp_[2] (chain mode): the split gradient of a layer's first block input,
+  // whose edge rows the compression backward reads
+  DevBuf sp_[3];
   bool chain_ok_ = false;  // the model's shapes allow chain mode (set at load)
   bool chain_ = false;     // chain mode for the current prediction
   Split16View split_view(int i, int rows, int cols);
