@@ -1429,12 +1429,13 @@ void launch16(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t s)
     k_split_a<<<ceil_div(a.M, 8), 256, 0, s>>>(a.A, a.lda, a.a_rows, a.M, a.K, a.a_split);
     CUDA_LAUNCH_CHECK();
   }
-  // default tile: 128 x 128; wide plain-store layers (QKV, N = 1536: 4.31 ->
-  // 3.92 ms on the 32k cell) run faster on 128 x 256, whose B-tile reuse
-  // halves the A traffic per product, while the layers with split outputs,
-  // SiLU or residual epilogues ran slower there (their epilogue, 128
-  // columns per warp, sets the pace)
-  const bool wide = EPI == EPI_STORE && !a.c_split.hi && !a.c_rows && a.N % 256 == 0 && a.N >= 1024;
+  // default tile: 128 x 128; plain fp32-store layers run faster on 128 x 256,
+  // whose B-tile reuse halves the A traffic per product (32k cell, ms per
+  // launch: QKV N = 1536 4.29 -> 3.92, N = 512 K = 512 1.48 -> 1.33,
+  // N = 512 K = 256 0.87 -> 0.84), while the layers with split outputs,
+  // SiLU or residual epilogues ran slower there (their epilogue, 128 columns
+  // per warp, sets the pace)
+  const bool wide = EPI == EPI_STORE && !a.c_split.hi && !a.c_rows && a.N % 256 == 0;
   const int bn = g_f16_bn ? g_f16_bn : (wide ? 256 : 128);
   if (a.N % 256 == 0 && bn == 512 && w.products == 3 && !a.r_split.hi) launch16_pair<EPI>(a, w, err, s);
   else if (a.N % 256 == 0 && bn == 256) launch16_bn<EPI, 256>(a, w, err, s);
