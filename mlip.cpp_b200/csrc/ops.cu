@@ -208,50 +208,72 @@ __global__ void k_add_vec(const float *__restrict__ x, float *__restrict__ y, in
 }
 
 // Split input: lane l owns columns 4l..4l+3 of every 128-column block for
-// all the edges it visits, so its H/32 rows of P stay in registers.
+// all the edges it visits, so its H/32 rows of P stay in registers; a warp
+// takes U edges per iteration and issues all their loads before the
+// arithmetic, so U edges' memory latency overlaps.
 template <int NB>
 __global__ void k_edge_xyzr_bwd_split(Split16View dzs, const float *__restrict__ P, float *__restrict__ g4,
                                       int n_edges, int accumulate) {
-  constexpr int H = 128 * NB;
+  constexpr int H = 128 * NB, U = NB <= 4 ? 2 : 1;
   const int lane = threadIdx.x & 31;
   float4 w[NB][4];
 #pragma unroll
   for (int k = 0; k < NB; ++k)
 #pragma unroll
     for (int q = 0; q < 4; ++q) w[k][q] = __ldg(reinterpret_cast<const float4 *>(P + 4 * (128 * k + 4 * lane + q)));
-  for (int e = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; e < n_edges; e += (gridDim.x * blockDim.x) >> 5) {
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int e0 = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; e0 < n_edges; e0 += U * warps) {
+    uint2 hv[U][NB], lv[U][NB];
+    int8_t sv[U][NB];
 #pragma unroll
-    for (int k = 0; k < NB; ++k) {
-      const size_t off = static_cast<size_t>(e) * H + 128 * k + 4 * lane;
-      const uint2 hv = *reinterpret_cast<const uint2 *>(dzs.hi + off);
-      const uint2 lv = *reinterpret_cast<const uint2 *>(dzs.lo + off);
-      const float f = pow2f(-static_cast<int>(dzs.sc[static_cast<size_t>(k) * split_ld(dzs) + e]));
-      const float2 h0 = __half22float2(*reinterpret_cast<const __half2 *>(&hv.x));
-      const float2 h1 = __half22float2(*reinterpret_cast<const __half2 *>(&hv.y));
-      const float2 l0 = __half22float2(*reinterpret_cast<const __half2 *>(&lv.x));
-      const float2 l1 = __half22float2(*reinterpret_cast<const __half2 *>(&lv.y));
-      const float g[4] = {(h0.x + l0.x) * f, (h0.y + l0.y) * f, (h1.x + l1.x) * f, (h1.y + l1.y) * f};
+    for (int u = 0; u < U; ++u) {
+      const int e = e0 + u * warps;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        s0 = fmaf(g[q], w[k][q].x, s0);
-        s1 = fmaf(g[q], w[k][q].y, s1);
-        s2 = fmaf(g[q], w[k][q].z, s2);
-        s3 = fmaf(g[q], w[k][q].w, s3);
+      for (int k = 0; k < NB; ++k) {
+        if (e < n_edges) {
+          const size_t off = static_cast<size_t>(e) * H + 128 * k + 4 * lane;
+          hv[u][k] = *reinterpret_cast<const uint2 *>(dzs.hi + off);
+          lv[u][k] = *reinterpret_cast<const uint2 *>(dzs.lo + off);
+          sv[u][k] = dzs.sc[static_cast<size_t>(k) * split_ld(dzs) + e];
+        } else {
+          hv[u][k] = lv[u][k] = make_uint2(0u, 0u);
+          sv[u][k] = 0;
+        }
       }
     }
-    s0 = warp_sum(s0);
-    s1 = warp_sum(s1);
-    s2 = warp_sum(s2);
-    s3 = warp_sum(s3);
-    if (lane == 0) {
-      float4 *o = reinterpret_cast<float4 *>(g4) + e;
-      float4 v = make_float4(s0, s1, s2, s3);
-      if (accumulate) {
-        const float4 p = *o;
-        v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int e = e0 + u * warps;
+      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+      for (int k = 0; k < NB; ++k) {
+        const float f = pow2f(-static_cast<int>(sv[u][k]));
+        const float2 h0 = __half22float2(*reinterpret_cast<const __half2 *>(&hv[u][k].x));
+        const float2 h1 = __half22float2(*reinterpret_cast<const __half2 *>(&hv[u][k].y));
+        const float2 l0 = __half22float2(*reinterpret_cast<const __half2 *>(&lv[u][k].x));
+        const float2 l1 = __half22float2(*reinterpret_cast<const __half2 *>(&lv[u][k].y));
+        const float g[4] = {(h0.x + l0.x) * f, (h0.y + l0.y) * f, (h1.x + l1.x) * f, (h1.y + l1.y) * f};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          s0 = fmaf(g[q], w[k][q].x, s0);
+          s1 = fmaf(g[q], w[k][q].y, s1);
+          s2 = fmaf(g[q], w[k][q].z, s2);
+          s3 = fmaf(g[q], w[k][q].w, s3);
+        }
       }
-      *o = v;
+      s0 = warp_sum(s0);
+      s1 = warp_sum(s1);
+      s2 = warp_sum(s2);
+      s3 = warp_sum(s3);
+      if (lane == 0 && e < n_edges) {
+        float4 *o = reinterpret_cast<float4 *>(g4) + e;
+        float4 v = make_float4(s0, s1, s2, s3);
+        if (accumulate) {
+          const float4 p = *o;
+          v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
+        }
+        *o = v;
+      }
     }
   }
 }
