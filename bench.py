@@ -391,7 +391,7 @@ def main():
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches),
             "roofline": {"bound": "tensor",
-                         "kernel": ("k_gemm_3xf16 + k_split_a" if f16 else "k_gemm_3xtf32")
+                         "kernel": ("k_gemm_3xf16 (+ k_split_a where an input is fp32)" if f16 else "k_gemm_3xtf32")
                                    + " (tcgen05, all dense layers)",
                          "achieved": achieved, "peak": bf16_sus / div, "unit": "TFLOP/s",
                          "frac": achieved / (bf16_sus / div),
