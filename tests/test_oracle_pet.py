@@ -48,6 +48,54 @@ def test_oracle_golden(path, model_file):
             np.testing.assert_allclose(r["stress"], f[f"stress_{k}"], atol=1e-7)
 
 
+def test_fused_compression_weight_matches_concatenation(tiny64):
+    """The GPU path feeds compress.0 a folded weight: the reference's input
+    [W_e (x y z r) + b_e | table[nbr species] | message] is linear in
+    [x y z r 1 one-hot(species)] apart from the message, so the library
+    multiplies compress.0 into the edge embedding and the species tables at
+    load and the featuriser writes [message | x y z r 1 one-hot 0...] rows.
+    This restates that fold in float64 and checks it reproduces the
+    reference's pre-activation on random edges of both layers."""
+    W = {k: v.numpy() for k, v in tiny64.W.items()}
+    d = W["model.embedding.weight"].shape[1]
+    n_tab = W["model.embedding.weight"].shape[0]
+    aux = (5 + n_tab + 127) // 128 * 128
+    rng = np.random.default_rng(7)
+    E = 257
+    vec = rng.normal(size=(E, 3))
+    r = np.linalg.norm(vec, axis=1)
+    sp = rng.integers(0, n_tab, E)
+    msg = rng.normal(size=(E, d))
+    for l in range(2):
+        p = f"model.gnn.{l}."
+        C0, c0 = W[p + "compress.0.weight"], W[p + "compress.0.bias"]
+        We, be = W[p + "edge_embedder.weight"], W[p + "edge_embedder.bias"]
+        tab = W["model.embedding.weight"] if l == 0 else W[p + "neighbor_embedder.weight"]
+        # reference: concatenation then linear (pet_layers.cpp:151-217, 685-796)
+        emb = vec @ We[:, :3].T + r[:, None] * We[:, 3] + be
+        parts = [emb, tab[sp]] + ([msg] if l == 1 else [])
+        z_ref = np.concatenate(parts, 1) @ C0.T + c0
+        # fold: [msg | x y z r 1 one-hot] against [C0_msg | C0_emb W_e | C0_emb b_e + c0 | C0_tab table^T]
+        C_emb, C_tab = C0[:, :d], C0[:, d:2 * d]
+        fused = np.zeros((C0.shape[0], (d if l else 0) + aux))
+        o = 0
+        if l == 1:
+            fused[:, :d] = C0[:, 2 * d:]
+            o = d
+        fused[:, o:o + 4] = C_emb @ We
+        fused[:, o + 4] = C_emb @ be + c0
+        fused[:, o + 5:o + 5 + n_tab] = C_tab @ tab.T
+        rows = np.zeros((E, fused.shape[1]))
+        if l == 1:
+            rows[:, :d] = msg
+        rows[:, o:o + 3] = vec
+        rows[:, o + 3] = r
+        rows[:, o + 4] = 1.0
+        rows[np.arange(E), o + 5 + sp] = 1.0
+        z = rows @ fused.T
+        assert np.abs(z - z_ref).max() <= 1e-10 * max(1.0, np.abs(z_ref).max())
+
+
 def test_fd_forces_frozen_mask(tiny64):
     """Autograd forces equal -dE/dx with the attention mask held fixed (the
     reference treats the mask as a constant input, pet.cpp:274-275)."""
