@@ -109,14 +109,18 @@ int64_t mlipcpp_b200_neighbor_list(int32_t n_atoms, const float *positions, cons
  * fixed static device array of 2.6 MB inside this library, which limits a
  * call to at most 65536 atoms and 65536 cutoff-sized bins; larger requests
  * return -MLIPCPP_ERROR_INVALID_PARAMETER with a message naming the limit,
- * before any device work.  The first call on each device looks up that
+ * before any device work; so do a cutoff that is not finite and positive,
+ * one that spans more than 511 cell widths along an axis, and a list that
+ * could exceed 2^31 - 1 pairs.  The first call on each device looks up that
  * array's address (cudaGetSymbolAddress), so make it before any stream
- * capture.  All calls on one device share the array: calls that overlap in
- * time (from several host threads) race, so serialise them.
- * Work runs on `stream` (NULL: the legacy default stream); the call returns
- * after that work has finished.  Returns the total pair count; the arrays
- * are written only when it is at most `cap` (else call again with larger
- * arrays), or -(error code) on failure. */
+ * capture.  All calls on one device share the array, and each call clears
+ * the parts that must start at zero: calls that overlap in time (from
+ * several host threads or streams) race, so serialise them.
+ * Work runs on `stream` (NULL: the legacy default stream).  Every call
+ * copies the pair count to the host and synchronises `stream` before it
+ * returns, so its work there has finished by then.  Returns the total pair
+ * count; the arrays are written only when it is at most `cap` (else call
+ * again with larger arrays), or -(error code) on failure. */
 int64_t mlipcpp_b200_neighbor_list_noalloc(int32_t n_atoms, const float *d_positions, const float *cell,
                                            const bool *pbc, float cutoff, int64_t cap, int32_t *d_centers,
                                            int32_t *d_neighbors, int32_t *d_shifts, float *d_vectors,
@@ -124,6 +128,10 @@ int64_t mlipcpp_b200_neighbor_list_noalloc(int32_t n_atoms, const float *d_posit
 
 /* Number of CUDA kernels this library has launched in this process. */
 int64_t mlipcpp_b200_kernel_launches(void);
+
+/* Number of device allocations (cudaMalloc calls) this library has made in
+ * this process. */
+int64_t mlipcpp_b200_device_allocations(void);
 
 /* CUDA device ordinal used by models created afterwards (default: the
  * calling thread's current device). */

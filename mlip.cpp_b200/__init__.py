@@ -103,6 +103,7 @@ def lib() -> ctypes.CDLL:
         "mlipcpp_b200_last_shape": (ctypes.c_int, [vp, vp]),
         "mlipcpp_b200_neighbor_list": (i64, [i32, vp, vp, vp, f32, i64, vp, vp, vp, vp, vp]),
         "mlipcpp_b200_kernel_launches": (i64, []),
+        "mlipcpp_b200_device_allocations": (i64, []),
         "mlipcpp_b200_set_device": (ctypes.c_int, [i32]),
         "mlipcpp_b200_set_kernel_profiling": (ctypes.c_int, [vp, b]),
         "mlipcpp_b200_kernel_stats": (ctypes.c_int, [vp, vp]),

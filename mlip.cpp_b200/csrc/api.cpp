@@ -4,6 +4,7 @@
 // ABI, and a result handle that refers to the model's last result.
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -17,6 +18,7 @@
 
 namespace pet {
 std::atomic<long long> g_kernel_launches{0};
+std::atomic<long long> g_device_allocations{0};
 extern int g_default_device;
 }
 
@@ -645,6 +647,10 @@ int64_t mlipcpp_b200_neighbor_list(int32_t n_atoms, const float *positions, cons
     set_error("NULL positions");
     return -MLIPCPP_ERROR_NULL_POINTER;
   }
+  if (!std::isfinite(cutoff) || cutoff <= 0.0f) {
+    set_error("The cutoff must be finite and positive");
+    return -MLIPCPP_ERROR_INVALID_PARAMETER;
+  }
   if (!have_cuda_device()) {
     set_error("No CUDA device available (this backend has no CPU fallback)");
     return -MLIPCPP_ERROR_BACKEND;
@@ -709,11 +715,20 @@ int64_t mlipcpp_b200_neighbor_list_noalloc(int32_t n_atoms, const float *d_posit
     set_error("The no-allocation neighbour list needs a cell (open boundaries: mlipcpp_b200_neighbor_list)");
     return -MLIPCPP_ERROR_INVALID_PARAMETER;
   }
+  if (!std::isfinite(cutoff) || cutoff <= 0.0f) {
+    set_error("The cutoff must be finite and positive");
+    return -MLIPCPP_ERROR_INVALID_PARAMETER;
+  }
   bool p[3] = {true, true, true};
   if (pbc) { p[0] = pbc[0]; p[1] = pbc[1]; p[2] = pbc[2]; }
   pet::GridParams g;
   pet::make_grid_params(cell, p, cutoff, &g);
   // size limits before any device work, so an oversized call touches nothing
+  if (g.ns[0] > pet::kMaxSearchBins || g.ns[1] > pet::kMaxSearchBins || g.ns[2] > pet::kMaxSearchBins) {
+    set_error("The cutoff spans more than " + std::to_string(pet::kMaxSearchBins) +
+              " cell widths along one axis");
+    return -MLIPCPP_ERROR_INVALID_PARAMETER;
+  }
   const int64_t nbins = static_cast<int64_t>(g.nb[0]) * g.nb[1] * g.nb[2];
   if (n_atoms > pet::kNoAllocMaxAtoms || nbins > pet::kNoAllocMaxBins) {
     set_error("The no-allocation neighbour list takes at most " + std::to_string(pet::kNoAllocMaxAtoms) +
@@ -746,6 +761,8 @@ int64_t mlipcpp_b200_neighbor_list_noalloc(int32_t n_atoms, const float *d_posit
 }
 
 int64_t mlipcpp_b200_kernel_launches(void) { return pet::g_kernel_launches.load(); }
+
+int64_t mlipcpp_b200_device_allocations(void) { return pet::g_device_allocations.load(); }
 
 mlipcpp_error_t mlipcpp_b200_set_device(int32_t device) {
   int n = 0;

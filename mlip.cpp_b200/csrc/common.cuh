@@ -37,6 +37,8 @@ inline void cuda_check(cudaError_t e, const char *what, const char *file, int li
 }
 // Kernels launched by this library (reported through the C API).
 extern std::atomic<long long> g_kernel_launches;
+// Device allocations (cudaMalloc calls) this library has made in this process.
+extern std::atomic<long long> g_device_allocations;
 
 #define CUDA_CHECK(x) ::pet::cuda_check((x), #x, __FILE__, __LINE__)
 #define CUDA_LAUNCH_CHECK()                                                  \
@@ -66,6 +68,7 @@ struct DevBuf {
     if (bytes <= cap && ptr) return ptr;
     release();
     size_t want = bytes < 256 ? 256 : bytes;
+    g_device_allocations.fetch_add(1, std::memory_order_relaxed);
     CUDA_CHECK(cudaMalloc(&ptr, want));
     cap = want;
     return ptr;

@@ -224,6 +224,8 @@ void PETModel::load(const std::string &path, float cutoff_override) {
   h.dh = f.get_i32("pet.d_head", 128);
   h.width = f.get_f32("pet.cutoff_width", 0.5f);
   h.d = static_cast<int>(emb->ne[0]);
+  if (!std::isfinite(h.cutoff) || h.cutoff <= 0.0f || !std::isfinite(h.width) || h.width <= 0.0f)
+    throw Error(kErrIO, "pet.cutoff and pet.cutoff_width must be finite and positive");
   if (h.gnn_layers != 2) throw Error(kErrUnsupported, "pet layout supports exactly 2 GNN layers");
   if (h.d % h.heads != 0) throw Error(kErrIO, "d_pet not divisible by num_heads");
   const auto *c0 = f.tensor("model.gnn.0.compress.0.weight");

@@ -383,12 +383,32 @@ void scan_counts(const int *in, int *out, int *max_out, int n, cudaStream_t stre
   CUDA_LAUNCH_CHECK();
 }
 
+// The pair offsets are int32 scans; the largest per-centre count times the
+// number of centres bounds the total, so below 2^31 nothing wrapped.
+void check_pair_total(int max_count, int n_centers) {
+  if (static_cast<int64_t>(max_count) * n_centers > INT32_MAX)
+    throw Error(kErrInvalidParameter, "the neighbour list could exceed 2^31 - 1 pairs (" +
+                                          std::to_string(n_centers) + " centres with up to " +
+                                          std::to_string(max_count) + " neighbours each)");
+}
+
+// k_periodic packs each search-bin offset into 10 bits, so at most 511 bins
+// are searched on either side along any axis.
+void check_search_extent(const GridParams &g) {
+  for (int a = 0; a < 3; ++a)
+    if (g.ns[a] > kMaxSearchBins)
+      throw Error(kErrInvalidParameter, "the cutoff spans " + std::to_string(g.ns[a]) +
+                                            " cell widths along one axis (at most " +
+                                            std::to_string(kMaxSearchBins) + ")");
+}
+
 namespace {
 void size_edges(EdgeList &out, int n, cudaStream_t stream) {
   int host[2];
   CUDA_CHECK(cudaMemcpyAsync(&host[0], out.offset.as<int>() + n, sizeof(int), cudaMemcpyDeviceToHost, stream));
   CUDA_CHECK(cudaMemcpyAsync(&host[1], out.offset.as<int>() + n + 1, sizeof(int), cudaMemcpyDeviceToHost, stream));
   CUDA_CHECK(cudaStreamSynchronize(stream));
+  check_pair_total(host[1], n);
   out.n_edges = host[0];
   out.max_count = host[1];
   size_t e = static_cast<size_t>(out.n_edges > 0 ? out.n_edges : 1);
@@ -403,6 +423,7 @@ void size_edges(EdgeList &out, int n, cudaStream_t stream) {
 template <typename P>
 void build_grid_nl(const P *pos, int n, int n_centers, const GridParams &g, EdgeList &out, NLScratch &s,
                    cudaStream_t stream) {
+  check_search_extent(g);
   out.n_atoms = n_centers;
   const int nbins = g.nb[0] * g.nb[1] * g.nb[2];
   int *braw = static_cast<int *>(s.braw.ensure(sizeof(int) * 3 * (n + 1)));
@@ -534,6 +555,7 @@ int64_t build_periodic_nl_noalloc(const float *pos, int n, const GridParams &g, 
     throw Error(kErrInvalidParameter, "the no-allocation neighbour list takes at most " +
                                           std::to_string(kNoAllocMaxBins) + " cutoff-sized bins (this cell needs " +
                                           std::to_string(nbins) + ")");
+  check_search_extent(g);
   if (n == 0) return 0;
   int *braw = noalloc_scratch();
   int *bin_of = braw + kNAOffBinOf;
@@ -557,9 +579,11 @@ int64_t build_periodic_nl_noalloc(const float *pos, int n, const GridParams &g, 
       pos, n, g, braw, bin_start, bin_atoms, count, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr);
   CUDA_LAUNCH_CHECK();
   scan_counts(count, offset, offset + n + 1, n, stream);
-  int total = 0;
-  CUDA_CHECK(cudaMemcpyAsync(&total, offset + n, sizeof(int), cudaMemcpyDeviceToHost, stream));
+  int total_max[2] = {0, 0};  // the scan's total and largest count
+  CUDA_CHECK(cudaMemcpyAsync(total_max, offset + n, 2 * sizeof(int), cudaMemcpyDeviceToHost, stream));
   CUDA_CHECK(cudaStreamSynchronize(stream));
+  check_pair_total(total_max[1], n);
+  const int total = total_max[0];
   if (total > 0 && total <= cap) {
     k_periodic<true, float><<<ceil_div(n, kNLWarps), 32 * kNLWarps, 0, stream>>>(
         pos, n, g, braw, bin_start, bin_atoms, nullptr, offset, e_center, e_nbr, e_shift, e_vec, e_dist);

@@ -20,7 +20,17 @@ struct GridParams {
   double cutoff_sq;  // (double)cutoff squared in f64 (periodic path)
 };
 
+// `cutoff` must be finite and positive (the callers check it).
 void make_grid_params(const float cell[9], const bool pbc[3], float cutoff, GridParams *g);
+
+// Largest search half-width per axis (bin offsets are packed in 10 bits).
+constexpr int kMaxSearchBins = 511;
+// Throws Error(kErrInvalidParameter) when a cutoff spans more than
+// kMaxSearchBins bins along an axis.
+void check_search_extent(const GridParams &g);
+// Throws Error(kErrInvalidParameter) when n_centers x max_count may exceed
+// the int32 pair offsets.
+void check_pair_total(int max_count, int n_centers);
 void cell_inverse_f32(const float m[9], float inv[9]);
 
 // Edges of a neighbour list in centre-major order (the reference's slot

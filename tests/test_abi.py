@@ -92,3 +92,18 @@ def test_python_api_surface():
     for name in ("predict", "predict_with_options", "predict_batch", "predict_device", "cutoff",
                  "model_type", "set_timing", "last_timings", "last_shape"):
         assert hasattr(mb.Predictor, name)
+
+
+def test_neighbor_list_rejects_bad_cutoff_before_device_work():
+    L = mb.lib()
+    fn = L.mlipcpp_b200_neighbor_list
+    pos = (ctypes.c_float * 3)(0.0, 0.0, 0.0)
+    cell = (ctypes.c_float * 9)(10, 0, 0, 0, 10, 0, 0, 0, 10)
+    for bad in (0.0, -2.0, float("nan"), float("inf")):
+        rc = fn(1, pos, cell, None, ctypes.c_float(bad), 0, None, None, None, None, None)
+        assert rc == -mb.INVALID_PARAMETER, bad
+        assert b"cutoff" in L.mlipcpp_get_last_error()
+
+
+def test_device_allocation_counter_exported():
+    assert mb.lib().mlipcpp_b200_device_allocations() >= 0
