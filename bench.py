@@ -1,23 +1,32 @@
 """Throughput benchmark: atom-steps/s for PET energy + forces + stress.
 
-Workload (the configuration the headline metric is quoted on): the periodic
-random fcc alloy of 32^3 primitive cells (32,768 atoms, triclinic cell,
-a = 3.6 A, 20 random elements among Z = 1..89, jitter N(0, 0.08 A)) with
-random-init pet-oam-l-shaped weights (d_pet 512, 16 heads, d_ff 1024,
+Default workload (the configuration the headline metric is quoted on): the
+periodic random fcc alloy of 32^3 primitive cells (32,768 atoms, triclinic
+cell, a = 3.6 A, 20 random elements among Z = 1..89, jitter N(0, 0.08 A))
+with random-init pet-oam-l-shaped weights (d_pet 512, 16 heads, d_ff 1024,
 d_head 256, cutoff 4.5 A); seeded synthetic data.  One step = one
 prediction of energy, forces and stress: neighbour list, featuriser, both
 GNN layers, readout and the full backward pass.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload fcc|si216|water|molecules|si] [--precision f32|f16]
+                  [--mode forces|energy|nc]
 
-Multi-GPU (launched with torch.distributed.run), weak scaling at 32,768 atoms
-per GPU: N ranks evaluate one cell of N x 32,768 atoms (32x32x64 primitive
-cells for 2 GPUs, 32x64x64 for 4, 64^3 = 262,144 for 8) split into N spatial
-domains (owned atoms plus two ghost shells of one cutoff each); the only
-exchange is an NCCL all-reduce of the forces and of (energy, virial) per
-step.  `--parallel replicas` instead runs an independent copy of the 32k cell
-per rank.  The timed region is bracketed by barriers and the reported time is
-the max over ranks.
+Other workloads (one JSON line each; pet-mad-s-shaped weights):
+  si216      diamond Si 3x3x3 (216 atoms), E+F+stress
+  water      liquid water, 4,096 atoms, E+F+stress
+  molecules  512 non-periodic molecules of 10-60 atoms, E+F, one batched
+             call (structures sharded over the ranks for N > 1)
+  si         diamond Si 32^3 (262,144 atoms), E+F+stress, spatial domains
+             over N >= 2 GPUs (strong scaling)
+
+Timing.  `value` keeps the positions resident on the device and sums the
+library's own CUDA events (recorded on its stream) around each whole step;
+`e2e` is the host clock around each public predict call, host arrays in
+and numpy forces and stress out.  Multi-GPU (launched with
+torch.distributed.run): barriers around the timed region, the max over
+ranks.  With --gpus N > 1 the fcc workload is weak scaling at 32,768 atoms
+per GPU (one cell of N x 32,768 atoms split into spatial domains).
 
 `--impl reference` times the CPU implementation of the path on the host
 cores: the reference's model cannot be built here (its ggml dependency is
@@ -26,6 +35,7 @@ absent), so this is the PyTorch restatement in oracle/ at float32.
 import argparse
 import importlib.util
 import json
+import math
 import os
 import subprocess
 import sys
@@ -37,6 +47,7 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "atom-steps/s (E+F+stress), 32k-atom PET cell, 1/2/4/8 B200; % of roofline"
+L2_BYTES = 126 << 20
 
 
 def _package():
@@ -105,9 +116,12 @@ class ClockSampler:
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(self.rows)}
 
 
-def cpu_reference(structure, gguf_path, steps, warmup):
+def cpu_reference(structures, gguf_path, steps, warmup, repeats=1, forces=True, nc=False):
     """Time the CPU implementation of the path (float32, all host threads)
-    on `structure`; returns (atom-steps/s, threads, per-step seconds)."""
+    on `structures` (one batched predict per step): `warmup` untimed steps,
+    then `repeats` runs of `steps` steps each, timed with the host clock.
+    Returns (median atom-steps/s, threads, median per-step seconds,
+    [atom-steps/s of every run])."""
     import torch
     if ROOT not in sys.path:
         sys.path.insert(0, ROOT)
@@ -115,81 +129,118 @@ def cpu_reference(structure, gguf_path, steps, warmup):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     orc = pet_oracle.load_oracle(gguf_path, torch.float32)
+    n_atoms = sum(s.n_atoms for s in structures)
     for _ in range(warmup):
-        orc.predict([structure])
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        orc.predict([structure])
-    dt = (time.perf_counter() - t0) / max(steps, 1)
-    return structure.n_atoms / dt, threads, dt
+        orc.predict(list(structures), compute_forces=forces, compute_nc=nc)
+    runs = []
+    for _ in range(max(repeats, 1)):
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            orc.predict(list(structures), compute_forces=forces, compute_nc=nc)
+        runs.append((time.perf_counter() - t0) / max(steps, 1))
+    dt = float(np.median(runs))
+    return n_atoms / dt, threads, dt, [n_atoms / r for r in runs]
 
 
-def run_other_workload(args, world, rank, local, mb, wl, torch, dist):
-    """The 262,144-atom Si cell over N GPUs (domain decomposition, strong
-    scaling) or a batch of 512 molecules sharded over N GPUs; pet-mad-s-shaped
-    weights; one JSON line from rank 0."""
-    from mlipcpp_b200 import domain as dd
-    from mlipcpp_b200 import sharding as sh
-    h = wl.PET_MAD_S
-    gguf = os.path.join(tempfile.mkdtemp(prefix="petbench"), "w.gguf")
-    wl.write_pet_gguf(gguf, h, seed=0)
-    pred = mb.Predictor(gguf)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+def spread(values):
+    """Relative half-range of repeated measurements."""
+    v = np.asarray(values, np.float64)
+    return float((v.max() - v.min()) / (2.0 * np.median(v))) if len(v) > 1 else 0.0
 
-    def max_over_ranks(x):
-        if dist:
-            t = torch.tensor([x], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            x = float(t.item())
-        return x
 
-    def barrier():
-        torch.cuda.synchronize()
-        if dist:
-            dist.barrier()
-        torch.cuda.synchronize()
+class Workload:
+    """One benchmark configuration: its structures, weights and CPU sample."""
 
-    if args.workload == "si":
-        s = wl.si_diamond(32, seed=0)
-        desc = (f"diamond Si 32^3 conventional cells ({s.n_atoms} atoms, a=5.431, jitter 0.05), "
-                f"pet-mad-s-shaped random-init weights, E+F+stress")
-        if world < 2:
-            if rank == 0:
-                print(json.dumps({"workload": desc, "unavailable": "262,144 atoms need at least 2 GPUs (about "
-                                                                   "280 GB of activations on one)"}), flush=True)
-            return
-        runner = dd.DomainRunner(dd.predictor_eval(pred), s.numbers, s.cell, h.cutoff, world=world, rank=rank)
-        d_pos = torch.from_numpy(s.positions).cuda()
-        step = lambda: runner.step(d_pos)  # noqa: E731
-        n_atoms, metric = s.n_atoms, "atom-steps/s (E+F+stress), 262k-atom Si cell, domain decomposition"
-        par = f"spatial domains {'x'.join(map(str, dd.grid_for(world)))}"
-    else:
-        mols = wl.molecules(512, seed=0)
-        runner = sh.BatchRunner(sh.predictor_batch_eval(pred), world=world, rank=rank)
-        step = lambda: runner.run(mols)  # noqa: E731
-        n_atoms = sum(m.n_atoms for m in mols)
-        desc = f"512 molecules of 10-60 atoms ({n_atoms} atoms), pet-mad-s-shaped random-init weights, E+F"
-        metric = "atom-steps/s (E+F), 512-molecule batch, structures sharded over GPUs"
-        par = f"batch shards x{world} (LPT on n^3), final all-gather"
-    for _ in range(max(args.warmup, 3)):
-        step()
-    barrier()
-    ev0.record()
-    for _ in range(args.steps):
-        step()
-    ev1.record()
-    barrier()
-    t = max_over_ranks(ev0.elapsed_time(ev1) / 1e3)
-    if rank == 0:
-        v = n_atoms * args.steps / t
-        print(json.dumps({"metric": metric, "value": v, "unit": "atom-steps/s", "n_gpus": world,
-                          "steps": args.steps, "warmup": max(args.warmup, 3),
-                          "ms_per_step": t / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
-                          "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                          "config": {"workload": desc, "atoms_total": n_atoms, "parallelism": par},
-                          "e2e": {"value": v, "unit": "atom-steps/s",
-                                  "note": "positions enter from the device (si) or the host (molecules)"}}),
-              flush=True)
+    def __init__(self, name, args, wl):
+        self.name = name
+        self.periodic = name != "molecules"
+        if name == "fcc":
+            self.hname = args.hypers
+            reps = args.reps
+            self.structures = None  # built per world size (weak scaling)
+            self.reps = reps
+            self.cpu_sample = [wl.fcc_alloy(args.cpu_reps, seed=0)]
+            self.cpu_desc = f"{args.cpu_reps ** 3}-atom cell of the same alloy"
+            self.desc = (f"fcc alloy {reps}^3 primitive cells ({reps ** 3} atoms per GPU, triclinic, a=3.6, "
+                         f"20 elements, jitter 0.08)")
+        elif name == "si216":
+            self.hname = "pet-mad-s"
+            self.structures = [wl.si_diamond(3, seed=0)]
+            self.cpu_sample = self.structures
+            self.cpu_desc = "the same 216-atom cell"
+            self.desc = "diamond Si 3x3x3 conventional cells (216 atoms, a=5.431, jitter 0.05)"
+        elif name == "water":
+            self.hname = "pet-mad-s"
+            self.structures = [wl.water_box(4096, seed=0)]
+            self.cpu_sample = [wl.water_box(384, seed=0)]
+            self.cpu_desc = "384-atom box of the same liquid water (density, geometry, generator)"
+            self.desc = ("liquid water, 4,096 atoms (1,365 H2O + 1 H), 1.0 g/cm^3, O-H 0.96, H-O-H 104.5, "
+                         "2.0 A min O-O")
+        elif name == "molecules":
+            self.hname = "pet-mad-s"
+            self.structures = wl.molecules(512, seed=0)
+            self.cpu_sample = self.structures[:8]
+            self.cpu_desc = (f"the first 8 molecules of the batch "
+                             f"({sum(s.n_atoms for s in self.cpu_sample)} atoms)")
+            n = sum(s.n_atoms for s in self.structures)
+            self.desc = (f"512 non-periodic molecules of 10-60 atoms ({n} atoms), Z from H/C/N/O "
+                         f"(.5/.3/.1/.1), 0.9 A min pair distance")
+        elif name == "si":
+            self.hname = "pet-mad-s"
+            self.structures = [wl.si_diamond(32, seed=0)]
+            self.cpu_sample = [wl.si_diamond(3, seed=0)]
+            self.cpu_desc = "216-atom cell of the same diamond Si (3x3x3)"
+            self.desc = "diamond Si 32^3 conventional cells (262,144 atoms, a=5.431, jitter 0.05)"
+        else:
+            raise ValueError(name)
+        self.h = wl.HYPERS[self.hname]
+
+    def metric(self, mode):
+        what = {"forces": "E+F+stress" if self.periodic else "E+F", "energy": "E only (forward pass)",
+                "nc": "E + non-conservative F and stress heads (forward pass)"}[mode]
+        if self.name == "fcc":
+            return METRIC if mode == "forces" else METRIC.replace("(E+F+stress)", f"({what})")
+        label = {"si216": "216-atom Si cell", "water": "4,096-atom water box",
+                 "molecules": "512-molecule batch", "si": "262k-atom Si cell, spatial domains"}[self.name]
+        return f"atom-steps/s ({what}), {label}, PET, B200"
+
+    def weights_desc(self, mode):
+        h = self.h
+        return (f"{self.hname}-shaped random-init weights (d={h.d_pet}, heads={h.num_heads}, "
+                f"ff={h.d_feedforward}, d_head={h.d_head}, rc={h.cutoff}{', nc heads' if mode == 'nc' else ''})")
+
+
+def roofline(kstats, t_dev_s, f16_mode, traffic, peaks):
+    hbm, bf16, bf16_sus, src = peaks
+    f16 = kstats["gemm_f16"]["launches"] > 0
+    g = kstats["gemm_f16" if f16 else "gemm_tc"]
+    gemm_ms = kstats["gemm_f16"]["ms"] + kstats["gemm_tc"]["ms"] + kstats["gemm_simt"]["ms"]
+    achieved = g["flops"] / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else 0.0
+    # achieved counts 2MNK.  3xFP16 runs three fp16 MMAs per fp32 product at
+    # the bf16 rate (ceiling: measured bf16 peak / 3); 3xTF32 three tf32
+    # MMAs at half that rate (ceiling / 6).
+    div = (1.0 if f16_mode else 3.0) if f16 else 6.0
+    att = kstats["attention"]
+    return {"bound": "tensor",
+            "kernel": ("k_gemm_3xf16" if f16 else "k_gemm_3xtf32") + " (tcgen05, all dense layers)",
+            "achieved": achieved, "peak": bf16_sus / div, "unit": "TFLOP/s",
+            "frac": achieved / (bf16_sus / div),
+            "peak_source": ((f"{src} bf16 sustained (1 fp16 MMA per product)" if f16_mode else
+                             f"{src} bf16 sustained / 3 (3 fp16 MMAs per product at the bf16 rate)")
+                            if f16 else f"{src} bf16 sustained / 6 (3 tf32 MMAs at half bf16 rate)"),
+            "tensor_pipe_frac_of_bf16": div * achieved / bf16_sus,
+            # DRAM bytes per average GEMM launch: ncu dram__bytes_read.sum +
+            # dram__bytes_write.sum over all GEMM launches of one step of the
+            # 1,728-atom cell of this alloy (5,371 B per token for the 3xFP16
+            # build), scaled by this step's tokens; null where not captured
+            "traffic": traffic,
+            "traffic_unit": "bytes per GEMM launch (scaled from the 1,728-atom capture)",
+            "gemm_share_of_step": gemm_ms / (t_dev_s * 1e3) if t_dev_s else None,
+            "attention": {"ms_per_launch": att["ms"] / att["launches"] if att["launches"] else None,
+                          "achieved_gbs": (att["bytes"] / (att["ms"] / 1e3) / 1e9) if att["ms"] > 0 else None,
+                          "peak_gbs": hbm, "frac": ((att["bytes"] / (att["ms"] / 1e3) / 1e9) / hbm)
+                          if att["ms"] > 0 else None,
+                          "bound": "hbm", "peak_source": f"{src} copy bandwidth"}}
 
 
 def main():
@@ -198,21 +249,20 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--hypers", default="pet-oam-l")
-    ap.add_argument("--reps", type=int, default=32, help="primitive fcc cells per axis")
-    ap.add_argument("--cpu-reps", type=int, default=6, help="CPU-baseline sample cells per axis")
+    ap.add_argument("--workload", default="fcc", choices=["fcc", "si216", "water", "molecules", "si"])
+    ap.add_argument("--hypers", default="pet-oam-l", help="weights shape of the fcc workload")
+    ap.add_argument("--reps", type=int, default=32, help="primitive fcc cells per axis and GPU")
+    ap.add_argument("--cpu-reps", type=int, default=6, help="fcc CPU-baseline sample cells per axis")
+    ap.add_argument("--cpu-steps", type=int, default=10, help="timed CPU-baseline steps per repeat")
+    ap.add_argument("--cpu-repeats", type=int, default=3, help="CPU-baseline repeats (median reported)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--parallel", default="domains", choices=["domains", "replicas"],
-                    help="multi-GPU mode: one cell split into spatial domains, or a replica per rank")
+                    help="fcc on N > 1 GPUs: one cell split into spatial domains, or a replica per rank")
     ap.add_argument("--precision", default="f32", choices=["f32", "f16"],
                     help="f16: MLIPCPP_PRECISION_F16, dense layers with one fp16 product (looser tolerances)")
     ap.add_argument("--mode", default="forces", choices=["forces", "energy", "nc"],
-                    help="forces: E + gradient forces + stress (headline); energy: the forward pass only; "
-                         "nc: forces and stress from non-conservative heads (use_nc_forces), forward only; "
-                         "energy and nc run one replica per GPU")
-    ap.add_argument("--workload", default="fcc", choices=["fcc", "si", "molecules"],
-                    help="fcc: the 32k-atom alloy per GPU (headline); si: one 262,144-atom diamond-Si "
-                         "cell over N >= 2 GPUs (strong scaling); molecules: 512 molecules sharded")
+                    help="forces: E + gradient forces (+ stress when periodic; headline); energy: the forward "
+                         "pass only; nc: forces and stress from non-conservative heads, forward only")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -220,32 +270,30 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     mb = _package()
     from mlipcpp_b200 import workloads as wl
-    h = wl.HYPERS[args.hypers]
-    what = {"forces": "E+F+stress", "energy": "E only (forward pass)",
-            "nc": "E + non-conservative F and stress heads (forward pass)"}[args.mode]
-    metric = METRIC if args.mode == "forces" else METRIC.replace("(E+F+stress)", f"({what})")
-    workload = (f"fcc alloy {args.reps}^3 primitive cells ({args.reps ** 3} atoms per GPU, triclinic, a=3.6, "
-                f"20 elements, jitter 0.08), {args.hypers}-shaped random-init weights "
-                f"(d={h.d_pet}, heads={h.num_heads}, ff={h.d_feedforward}, d_head={h.d_head}, "
-                f"rc={h.cutoff}{', nc heads' if args.mode == 'nc' else ''}), {what}")
-
+    W = Workload(args.workload, args, wl)
+    grad, nc = args.mode == "forces", args.mode == "nc"
     tmpdir = tempfile.mkdtemp(prefix="petbench")
     gguf = os.path.join(tmpdir, "w.gguf")
-    wl.write_pet_gguf(gguf, h, seed=0, nc_heads=args.mode == "nc")
+    wl.write_pet_gguf(gguf, W.h, seed=0, nc_heads=nc)
+    metric = W.metric(args.mode)
 
     if args.impl == "reference":
         if rank != 0:
             return
-        sample = wl.fcc_alloy(args.cpu_reps, seed=0)
-        v, threads, dt = cpu_reference(sample, gguf, args.steps, args.warmup)
-        line = {"metric": METRIC, "value": v, "unit": "atom-steps/s", "n_gpus": args.gpus,
+        v, threads, dt, runs = cpu_reference(W.cpu_sample, gguf, 1, args.warmup, repeats=args.steps,
+                                             forces=grad, nc=nc)
+        n_s = sum(s.n_atoms for s in W.cpu_sample)
+        line = {"metric": metric, "value": v, "unit": "atom-steps/s", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic", "impl": "reference",
-                "config": {"workload": workload, "sample": f"{sample.n_atoms}-atom cell of the same alloy"},
+                "config": {"workload": W.desc + ", " + W.weights_desc(args.mode),
+                           "sample": W.cpu_desc},
                 "cpu_baseline": {"value": v, "unit": "atom-steps/s", "cores": threads, "kind": "port",
-                                 "sample": f"{sample.n_atoms}-atom fcc alloy cell, {args.steps} steps "
-                                           "(PyTorch-CPU restatement of the reference; ggml absent)"},
+                                 "sample": f"{W.cpu_desc}, {n_s} atoms per step, median of {args.steps} "
+                                           "timed steps (PyTorch-CPU restatement of the reference, float32; "
+                                           "ggml absent)",
+                                 "spread": spread(runs)},
                 "e2e": {"value": v, "unit": "atom-steps/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
@@ -261,32 +309,6 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
 
-    if args.workload != "fcc":
-        run_other_workload(args, world, rank, local, mb, wl, torch, dist)
-        if dist:
-            dist.barrier()
-            dist.destroy_process_group()
-        return
-
-    domains = world > 1 and args.parallel == "domains" and args.mode == "forces"
-    grad, nc = args.mode == "forces", args.mode == "nc"
-    reps = (args.reps,) * 3
-    if domains:
-        # N x 32k atoms: double the cell along z, then y, then x
-        r = list(reps)
-        k, w = 2, world
-        while w > 1:
-            r[k] *= 2
-            w //= 2
-            k = (k - 1) % 3
-        reps = tuple(r)
-    s = wl.fcc_alloy(reps, seed=0)
-    f16_mode = args.precision == "f16"
-    pred = mb.Predictor(gguf, mb.ModelOptions(precision=1 if f16_mode else 0))
-    pred.set_timing(True)
-    d_pos = torch.from_numpy(s.positions).cuda()
-    torch.cuda.synchronize()
-
     def barrier():
         torch.cuda.synchronize()
         if dist:
@@ -295,128 +317,185 @@ def main():
 
     def max_over_ranks(x):
         if dist:
-            t = torch.tensor([x], device="cuda")
+            t = torch.tensor([float(x)], device="cuda", dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             x = float(t.item())
         return x
 
-    from mlipcpp_b200 import domain as dd
-    if domains:
-        runner = dd.DomainRunner(dd.predictor_eval(pred), s.numbers, s.cell, h.cutoff, world=world, rank=rank)
+    f16_mode = args.precision == "f16"
+    pred = mb.Predictor(gguf, mb.ModelOptions(precision=1 if f16_mode else 0))
+    pred.set_timing(True)
+    peaks = _peaks()
+    flush_buf = None
 
-        def step_device():
-            return runner.step(d_pos)
+    # ---- choose the step functions ----------------------------------------
+    from mlipcpp_b200 import domain as dd
+    from mlipcpp_b200 import sharding as sh
+    domains = world > 1 and ((W.name == "fcc" and args.parallel == "domains" and grad) or W.name == "si")
+    par = f"replicas x{world}"
+    scaling = "weak"
+    if W.name == "si" and world < 2:
+        if rank == 0:
+            print(json.dumps({"metric": metric, "workload": W.desc,
+                              "unavailable": "262,144 atoms need at least 2 GPUs (about 280 GB of "
+                                             "activations on one)"}), flush=True)
+        return
+    if W.name == "si" and not grad:
+        raise SystemExit("the si workload runs E+F+stress only")
+    if W.name == "fcc":
+        reps = (W.reps,) * 3
+        if domains:
+            # N x 32k atoms: double the cell along z, then y, then x
+            r = list(reps)
+            k, w = 2, world
+            while w > 1:
+                r[k] *= 2
+                w //= 2
+                k = (k - 1) % 3
+            reps = tuple(r)
+        s = wl.fcc_alloy(reps, seed=0)
+        structs = [s]
     else:
-        def step_device():
-            return pred.predict_device(d_pos.data_ptr(), s.n_atoms, s.numbers, s.cell, s.pbc,
-                                       compute_forces=grad or nc, compute_stress=grad or nc, copy_forces=False,
-                                       use_nc_forces=nc)
+        structs = W.structures
+        s = structs[0]
+    n_atoms_job = sum(x.n_atoms for x in structs) * (1 if domains else world)
+    if W.name == "molecules" and world > 1:
+        n_atoms_job = sum(x.n_atoms for x in structs)
+    if W.name == "si":
+        scaling = "strong"
+    if W.name == "molecules":
+        scaling = "strong" if world > 1 else "weak"
+
+    if domains:
+        runner = dd.DomainRunner(dd.predictor_eval(pred), s.numbers, s.cell, W.h.cutoff, world=world, rank=rank)
+        d_pos = torch.from_numpy(s.positions).cuda()
+        pos_host = torch.from_numpy(s.positions).pin_memory()
+        par = (f"spatial domains {'x'.join(map(str, dd.grid_for(world)))} (owned + 2 ghost shells), "
+               "NCCL all-reduce of F and (E, virial)")
+
+        def step_value():
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record()
+            runner.step(d_pos)
+            ev1.record()
+            ev1.synchronize()
+            return ev0.elapsed_time(ev1)
+
+        def step_e2e():
+            t0 = time.perf_counter()
+            e, F, vir = runner.step(pos_host.to("cuda", non_blocking=True))
+            F_host = F.cpu()
+            return (time.perf_counter() - t0) * 1e3, F_host
+        h2d_bytes = int(s.positions.nbytes)
+        d2h_bytes = int(s.positions.nbytes + 8 * 7)
+    elif W.name == "molecules":
+        mine = sh.shard([sh.structure_cost(x.n_atoms) for x in structs], world)[rank]
+        my_structs = [structs[i] for i in mine]
+        runner = sh.BatchRunner(sh.predictor_batch_eval(pred, compute_forces=grad or nc), world=world, rank=rank)
+        if world > 1:
+            par = f"batch shards x{world} (LPT on n^3), final all-gather"
+
+        def step_value():
+            pred.predict_batch(my_structs, compute_forces=grad or nc, use_nc_forces=nc)
+            return pred.last_timings()["total"]
+
+        def step_e2e():
+            t0 = time.perf_counter()
+            out = runner.run(structs)
+            return (time.perf_counter() - t0) * 1e3, out
+        h2d_bytes = int(sum(x.positions.nbytes + x.numbers.nbytes for x in my_structs))
+        d2h_bytes = int(sum(x.positions.nbytes + 8 for x in my_structs))
+    else:
+        d_pos = torch.from_numpy(s.positions).cuda()
+        opts = mb.PredictOptions(grad or nc, grad or nc, nc)
+
+        def step_value():
+            pred.predict_device(d_pos.data_ptr(), s.n_atoms, s.numbers, s.cell, s.pbc,
+                                compute_forces=grad or nc, compute_stress=grad or nc, copy_forces=False,
+                                use_nc_forces=nc)
+            return pred.last_timings()["total"]
+
+        def step_e2e():
+            t0 = time.perf_counter()
+            r = pred.predict_with_options(s.positions, s.numbers, s.cell, s.pbc, opts)
+            return (time.perf_counter() - t0) * 1e3, r
+        h2d_bytes = int(s.positions.nbytes + s.numbers.nbytes)
+        d2h_bytes = int(s.positions.nbytes + 6 * 4 + 8 * 7) if (grad or nc) else 8 * 7
+
+    # small working sets: flush L2 between steps (outside the timed calls)
+    small = W.name == "si216"
+    if small:
+        flush_buf = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+
+    def flush():
+        if flush_buf is not None:
+            flush_buf.zero_()
+            torch.cuda.synchronize()
 
     for _ in range(max(args.warmup, 3)):
-        step_device()
+        step_value()
     # ---- device-resident timed region (value) -----------------------------
     pred.set_kernel_profiling(True)
     launches0 = mb.kernel_launches()
     barrier()
+    dev_ms = []
     with ClockSampler(local) as clk:
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        dev_ms = []
-        ev0.record()
         for _ in range(args.steps):
-            step_device()
-            if not domains:
-                dev_ms.append(pred.last_timings()["total"])
-        ev1.record()
+            flush()
+            dev_ms.append(step_value())
         barrier()
     launches = mb.kernel_launches() - launches0
     kstats = pred.kernel_stats()
+    phase = pred.last_timings()
     pred.set_kernel_profiling(False)
-    # single cell: the library's own events on its stream; domains: torch
-    # events around whole steps (the library synchronises its stream before
-    # returning, so they span its work, the partition and the all-reduces)
-    t_dev = float(np.sum(dev_ms)) / 1e3 if not domains else ev0.elapsed_time(ev1) / 1e3
-    t_dev = max_over_ranks(t_dev)
-    n_job = s.n_atoms if domains else world * s.n_atoms
-    value = n_job * args.steps / t_dev
+    t_dev = max_over_ranks(float(np.sum(dev_ms)) / 1e3)
+    value = n_atoms_job * args.steps / t_dev
 
     # ---- end-to-end through the public API with host buffers --------------
-    pos_host = torch.from_numpy(s.positions).pin_memory()
+    for _ in range(2):
+        step_e2e()
     barrier()
-    if domains:
-        ev0.record()
-        for _ in range(args.steps):
-            e, F, vir = runner.step(pos_host.to("cuda", non_blocking=True))
-            F_host = F.cpu()
-        ev1.record()
-        barrier()
-        t_e2e = ev0.elapsed_time(ev1) / 1e3
-        d2h = int(F_host.numel() * 4 + 8 * 7)
-    else:
-        e2e_ms = []
-        opts = mb.PredictOptions(grad or nc, grad or nc, nc)
-        for _ in range(args.steps):
-            r = pred.predict_with_options(pos_host.numpy(), s.numbers, s.cell, s.pbc, opts)
-            e2e_ms.append(pred.last_timings()["total"])
-        barrier()
-        t_e2e = float(np.sum(e2e_ms)) / 1e3
-        d2h = int(r.forces.nbytes + r.stress.nbytes + 4)
-    t_e2e = max_over_ranks(t_e2e)
-    e2e = n_job * args.steps / t_e2e
+    wall_ms = []
+    for _ in range(args.steps):
+        flush()
+        wall_ms.append(step_e2e()[0])
+    barrier()
+    t_e2e = max_over_ranks(float(np.sum(wall_ms)) / 1e3)
+    e2e = n_atoms_job * args.steps / t_e2e
 
     if rank == 0:
-        hbm, bf16, bf16_sus, src = _peaks()
-        f16 = kstats["gemm_f16"]["launches"] > 0
-        g = kstats["gemm_f16" if f16 else "gemm_tc"]
-        gemm_ms = kstats["gemm_f16"]["ms"] + kstats["gemm_tc"]["ms"] + kstats["gemm_simt"]["ms"]
-        achieved = g["flops"] / (g["ms"] / 1e3) / 1e12 if g["ms"] > 0 else 0.0
-        # achieved counts 2MNK.  3xFP16 runs three fp16 MMAs per fp32 product at
-        # the bf16 rate (ceiling: measured bf16 peak / 3); 3xTF32 three tf32
-        # MMAs at half that rate (ceiling / 6).
-        div = (1.0 if f16_mode else 3.0) if f16 else 6.0
         shape = pred.last_shape()
+        fcc_traffic = (W.name == "fcc" and not domains and not f16_mode and grad)
         line = {
             "metric": metric, "value": value, "unit": "atom-steps/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": t_dev / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f16" if f16_mode else "f32",
-            "data": "synthetic",
-            "config": {"workload": workload, "atoms_per_gpu": n_job // world, "atoms_total": n_job,
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+            "dtype": "f16" if f16_mode else "f32", "data": "synthetic",
+            "config": {"workload": W.desc + ", " + W.weights_desc(args.mode),
+                       "atoms_per_gpu": n_atoms_job // world, "atoms_total": n_atoms_job,
                        "edges_rank0": shape["edges"], "max_neighbors": shape["max_neighbors"],
-                       "parallelism": (f"spatial domains {'x'.join(map(str, dd.grid_for(world)))} "
-                                       "(owned + 2 ghost shells), NCCL all-reduce of F and (E, virial)"
-                                       if domains else f"replicas x{world}"),
-                       "l2": "inputs larger than L2 (multi-GB working set per step)"},
-            "e2e": {"value": e2e, "unit": "atom-steps/s",
-                    "h2d_bytes_per_step": int(s.positions.nbytes + (0 if domains else s.numbers.nbytes)),
-                    "d2h_bytes_per_step": d2h},
+                       "parallelism": par,
+                       "l2": ("L2 flushed between steps (a 252 MB write outside the timed calls)" if small
+                              else "inputs larger than L2 (hundreds of MB to GB working set per step)")},
+            "e2e": {"value": e2e, "unit": "atom-steps/s", "h2d_bytes_per_step": h2d_bytes,
+                    "d2h_bytes_per_step": d2h_bytes,
+                    "timing": "host clock around each public predict call (host arrays in, numpy out)"},
             "gpu_launches": int(launches),
-            "roofline": {"bound": "tensor",
-                         "kernel": ("k_gemm_3xf16 (+ k_split_a where an input is fp32)" if f16 else "k_gemm_3xtf32")
-                                   + " (tcgen05, all dense layers)",
-                         "achieved": achieved, "peak": bf16_sus / div, "unit": "TFLOP/s",
-                         "frac": achieved / (bf16_sus / div),
-                         "peak_source": ((f"{src} bf16 sustained (1 fp16 MMA per product)" if f16_mode else
-                                          f"{src} bf16 sustained / 3 (3 fp16 MMAs per product at the bf16 rate)")
-                                         if f16 else f"{src} bf16 sustained / 6 (3 tf32 MMAs at half bf16 rate)"),
-                         "tensor_pipe_frac_of_bf16": div * achieved / bf16_sus,
-                         # DRAM bytes per average GEMM launch: ncu dram__bytes_read.sum +
-                         # dram__bytes_write.sum over all 55 GEMM launches of one step of the
-                         # 1,728-atom cell of this alloy (350 MB/launch at 65,202 tokens,
-                         # 5,371 B per token for the 3xFP16 build), scaled by this step's tokens
-                         "traffic": (5371.0 * (shape["atoms"] + shape["edges"])
-                                     if not domains and f16 and grad else None),
-                         "traffic_unit": "bytes per GEMM launch (scaled from the 1,728-atom capture)",
-                         "gemm_share_of_step": gemm_ms / (t_dev * 1e3) if t_dev else None},
+            "roofline": roofline(kstats, t_dev, f16_mode,
+                                 5371.0 * (shape["atoms"] + shape["edges"]) if fcc_traffic else None, peaks),
             "kernel_stats": kstats,
-            "phase_ms": pred.last_timings(),
+            "phase_ms": phase,
             "clocks": clk.summary(),
         }
-        if not args.no_cpu_baseline and world == 1 and grad:
-            sample = wl.fcc_alloy(args.cpu_reps, seed=0)
-            v, threads, dt = cpu_reference(sample, gguf, 2, 1)
-            line["cpu_baseline"] = {"value": v, "unit": "atom-steps/s", "cores": threads, "kind": "port",
-                                    "sample": f"{sample.n_atoms}-atom cell of the same alloy, 2 steps "
-                                              "(PyTorch-CPU restatement, float32)"}
+        if not args.no_cpu_baseline and world == 1:
+            v, threads, dt, runs = cpu_reference(W.cpu_sample, gguf, args.cpu_steps, 2,
+                                                 repeats=args.cpu_repeats, forces=grad, nc=nc)
+            n_s = sum(x.n_atoms for x in W.cpu_sample)
+            line["cpu_baseline"] = {
+                "value": v, "unit": "atom-steps/s", "cores": threads, "kind": "port",
+                "sample": (f"{W.cpu_desc}, {n_s} atoms per step; 2 warm-up steps, then the median of "
+                           f"{args.cpu_repeats} runs of {args.cpu_steps} steps (PyTorch-CPU restatement, float32)"),
+                "spread": spread(runs), "runs": runs}
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
