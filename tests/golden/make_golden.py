@@ -72,7 +72,18 @@ def pet_cases():
         "nc_tiny_si8": ("tiny", 0, [wl.si_diamond(1, seed=3)], True),
         "nc_tiny_molecules3": ("tiny", 0, wl.molecules(3, seed=7, n_min=5, n_max=20), True),
         "nc_mads_si64": ("pet-mad-s", 1, [wl.si_diamond(2, seed=11)], True),
+        # the benchmark configurations at their stated sizes (the fcc alloy
+        # at the largest cell the float64 oracle holds here, 12^3 primitive)
+        "mads_water4096": ("pet-mad-s", 1, [wl.water_box(4096, seed=0)], False),
+        "mads_molecules512": ("pet-mad-s", 1, wl.molecules(512, seed=0), False),
+        "oaml_fcc1728": ("pet-oam-l", 2, [wl.fcc_alloy(12, seed=0)], False),
     }
+
+
+# Structures per oracle call: the oracle pads every atom to the batch's
+# largest neighbour count, so large batches of independent molecules are
+# evaluated in chunks (batch == single, test_oracle_pet.py)
+CHUNK = 16
 
 
 def weights_digest(h, seed, nc=False):
@@ -84,13 +95,14 @@ def weights_digest(h, seed, nc=False):
     return m.hexdigest()
 
 
-def main():
+def main(only=None):
     from oracle import nl
     import torch
 
     from oracle import pet_oracle
 
-    if nl.reference_available():
+    torch.set_num_threads(os.cpu_count() or 1)
+    if only is None and nl.reference_available():
         for name, (s, rc) in nl_cases().items():
             ref = nl.build_reference(s.positions, s.cell, s.pbc, rc)
             np.savez_compressed(
@@ -99,15 +111,21 @@ def main():
                 pbc=np.asarray(s.pbc if s.pbc is not None else (False,) * 3),
                 cutoff=np.float32(rc), **{k: v for k, v in ref.items() if k != "n_atoms"})
             print("nl", name, len(ref["centers"]))
-    else:
+    elif only is None:
         print("reference tree absent: nl_* fixtures left unchanged")
 
     tmp = os.path.join(HERE, "_tmp.gguf")
     for name, (hname, seed, systems, nc) in pet_cases().items():
+        if only is not None and name not in only:
+            continue
         h = wl.HYPERS[hname]
         wl.write_pet_gguf(tmp, h, seed=seed, nc_heads=nc)
         orc = pet_oracle.load_oracle(tmp, torch.float64)
-        res = orc.predict(systems, compute_forces=not nc, compute_nc=nc)
+        periodic = systems[0].cell is not None
+        step = 1 if periodic else CHUNK
+        res = []
+        for k in range(0, len(systems), step):
+            res += orc.predict(systems[k:k + step], compute_forces=not nc, compute_nc=nc)
         payload = dict(hypers=hname, seed=seed, digest=weights_digest(h, seed, nc),
                        n_systems=len(systems), nc=nc)
         for k, (s, r) in enumerate(zip(systems, res)):
@@ -123,4 +141,5 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    # optional arguments: names of the pet_* fixtures to regenerate (default: all)
+    main(set(sys.argv[1:]) or None)

@@ -22,6 +22,10 @@ def tiny64(model_file):
     return po.load_oracle(model_file("tiny", 0), torch.float64)
 
 
+# fixtures above this many atoms are re-run on the CPU only in part
+CPU_RERUN_ATOMS = 1000
+
+
 def _fixture_systems(f):
     out = []
     for k in range(int(f["n_systems"])):
@@ -39,8 +43,23 @@ def test_oracle_golden(path, model_file):
     mg = __import__("golden.make_golden", fromlist=["x"])
     if str(f["digest"]) != mg.weights_digest(h, int(f["seed"]), nc):
         pytest.fail("seeded weight generator drifted from the committed fixture")
+    systems = _fixture_systems(f)
+    if sum(s.n_atoms for s in systems) > CPU_RERUN_ATOMS:
+        # the benchmark-size fixtures: their inputs are the seeded workload
+        # generators' output, and the oracle is re-run here on a bounded part
+        # (a batch's first structures; periodic cells only on the GPU box's
+        # side, through the GPU comparison)
+        name = os.path.basename(path)[4:-4]
+        _, _, gen, _ = mg.pet_cases()[name]
+        assert len(gen) == len(systems)
+        for a, b in zip(gen, systems):
+            np.testing.assert_array_equal(a.positions, b.positions)
+            np.testing.assert_array_equal(a.numbers, b.numbers)
+        if systems[0].cell is not None:
+            return
+        systems = systems[:mg.CHUNK]
     orc = po.load_oracle(model_file(str(f["hypers"]), int(f["seed"]), nc=nc), torch.float64)
-    res = orc.predict(_fixture_systems(f), compute_forces=not nc, compute_nc=nc)
+    res = orc.predict(systems, compute_forces=not nc, compute_nc=nc)
     for k, r in enumerate(res):
         assert abs(r["energy_f64"] - float(f[f"energy_{k}"])) < 1e-8 * max(1, abs(float(f[f"energy_{k}"])))
         np.testing.assert_allclose(r["forces"], f[f"forces_{k}"], atol=1e-6)
