@@ -368,28 +368,32 @@ def main():
     if W.name == "molecules":
         scaling = "strong" if world > 1 else "weak"
 
+    dom = None
     if domains:
-        runner = dd.DomainRunner(dd.predictor_eval(pred), s.numbers, s.cell, W.h.cutoff, world=world, rank=rank)
-        d_pos = torch.from_numpy(s.positions).cuda()
-        pos_host = torch.from_numpy(s.positions).pin_memory()
-        par = (f"spatial domains {'x'.join(map(str, dd.grid_for(world)))} (owned + 2 ghost shells), "
-               "NCCL all-reduce of F and (E, virial)")
+        grid = dd.grid_for(world)
+        mine = np.nonzero(dd.owners(s.positions, s.cell, grid) == rank)[0]
+        comm = dd.NcclComm()
+        dom = dd.Domain(pred, s.cell, grid, rank, comm.c)
+        dom.set_atoms(s.numbers[mine])
+        own_pos = np.ascontiguousarray(s.positions[mine], np.float32)
+        d_pos = torch.from_numpy(own_pos).cuda()
+        d_F = torch.zeros_like(d_pos)
+        pos_host = torch.from_numpy(own_pos).pin_memory()
+        par = (f"spatial domains {'x'.join(map(str, grid))}: layer 0 and 1 on owned atoms, NCCL alltoallv of "
+               "halo positions, reverse-edge layer-0 tokens and their gradients, ghost forces; all-reduce of "
+               "(E, virial)")
 
         def step_value():
-            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            ev0.record()
-            runner.step(d_pos)
-            ev1.record()
-            ev1.synchronize()
-            return ev0.elapsed_time(ev1)
+            dom.step(d_pos, d_F)
+            return dom.stats()["step_ms"]
 
         def step_e2e():
             t0 = time.perf_counter()
-            e, F, vir = runner.step(pos_host.to("cuda", non_blocking=True))
-            F_host = F.cpu()
+            dom.step(pos_host.to("cuda", non_blocking=True), d_F)
+            F_host = d_F.cpu()
             return (time.perf_counter() - t0) * 1e3, F_host
-        h2d_bytes = int(s.positions.nbytes)
-        d2h_bytes = int(s.positions.nbytes + 8 * 7)
+        h2d_bytes = int(own_pos.nbytes)
+        d2h_bytes = int(own_pos.nbytes + 8 * 7)
     elif W.name == "molecules":
         mine = sh.shard([sh.structure_cost(x.n_atoms) for x in structs], world)[rank]
         my_structs = [structs[i] for i in mine]
@@ -474,6 +478,12 @@ def main():
     t_e2e = max_over_ranks(float(np.sum(wall_ms)) / 1e3)
     e2e = n_atoms_job * args.steps / t_e2e
 
+    domain_stats = None
+    if dom is not None:
+        # per-phase device times of the last step: the max over ranks, with
+        # rank 0's counts
+        st = dom.stats()
+        domain_stats = {k: (max_over_ranks(v) if k.endswith("_ms") else v) for k, v in st.items()}
     if rank == 0:
         shape = pred.last_shape()
         fcc_traffic = (W.name == "fcc" and not domains and not f16_mode and grad)
@@ -496,6 +506,7 @@ def main():
                                  5371.0 * (shape["atoms"] + shape["edges"]) if fcc_traffic else None, peaks),
             "kernel_stats": kstats,
             "phase_ms": phase,
+            "domain": domain_stats,
             "clocks": clk.summary(),
         }
         if not args.no_cpu_baseline and world == 1:

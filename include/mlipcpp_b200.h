@@ -52,28 +52,6 @@ mlipcpp_error_t mlipcpp_b200_predict_device_forces(mlipcpp_model_t model, int32_
                                                    const mlipcpp_predict_options_t *options, float *d_forces,
                                                    double *energy, float stress[6], bool *has_stress);
 
-/* One spatial domain of a large periodic cell (multi-GPU domain
- * decomposition).  d_positions: device pointer to [3 * n_local] double, the
- * owned atoms first, then the ghost atoms within one cutoff of the owned
- * region, then the other ghosts (periodic images already placed);
- * atomic_numbers is a host array.  Layer 0 runs on the first n_layer0
- * atoms, layer 1 and the readout on the first n_owned.  cell: row-major
- * cell of the search grid; pbc: per axis, whether the local system is
- * periodic along it (an axis the decomposition does not split) or open
- * (NULL: open along all three).  Along open axes the local positions should
- * lie inside the cell, for an even spread over the bins.
- * Outputs: energy of the owned atoms (host, eV, f64, composition included),
- * gradient forces on every local atom (d_forces: device [3 * n_local] float,
- * may be NULL), and the local virial sum_e e (x) dE/de in Voigt order (host,
- * f64, not divided by a volume).  Summing energies, virials and the forces
- * of each atom over all domains gives the whole cell's results. */
-mlipcpp_error_t mlipcpp_b200_predict_local(mlipcpp_model_t model, int32_t n_local,
-                                           const double *d_positions,
-                                           const int32_t *atomic_numbers, int32_t n_layer0,
-                                           int32_t n_owned, const float cell[9],
-                                           const bool *pbc, bool compute_forces, float *d_forces, double *energy,
-                                           double virial[6]);
-
 /* Enable per-phase CUDA-event timing of later predictions. */
 mlipcpp_error_t mlipcpp_b200_set_timing(mlipcpp_model_t model, bool enable);
 
@@ -126,12 +104,77 @@ int64_t mlipcpp_b200_neighbor_list_noalloc(int32_t n_atoms, const float *d_posit
                                            int32_t *d_neighbors, int32_t *d_shifts, float *d_vectors,
                                            float *d_distances, void *stream);
 
+/* ---- Spatial domain decomposition of one periodic cell (no counterpart in
+ * the reference, which evaluates a structure on one device:
+ * PETModel::predict_batch, src/models/pet/pet.cpp:125-694) ----------------
+ * One rank per GPU, each with its own model.  The cell is split into
+ * grid[0] x grid[1] x grid[2] fractional slabs; rank r owns slab
+ * (r % g0, r / g0 % g1, r / (g0 g1)) and the atoms assigned to it.  Every
+ * step: owned atoms within cutoff + skin of another slab are sent there as
+ * ghosts (periodic images included); each rank runs both GNN layers and the
+ * readout on its owned atoms only; a layer-1 message that needs the layer-0
+ * token of an edge held by another rank gets it from that rank, and the
+ * token's gradient goes back; forces on ghosts return to their owners; the
+ * energy and virial are summed over the ranks.  The exchanges are the
+ * caller's collectives (mlipcpp_b200_comm_t), e.g. torch.distributed over
+ * NCCL: alltoallv sends rank r the send_counts[r] elements of elem_bytes
+ * bytes of d_send's r-th segment and receives recv_counts[r] elements from
+ * rank r into d_recv's r-th segment (segments in rank order);
+ * allreduce_sum_f64 sums n doubles in place.  Buffers are device memory of
+ * the model's device; both calls must be ordered on `stream` (a cudaStream_t)
+ * and return 0 on success.  Every call of domain_step is collective. */
+typedef struct {
+  void *user;
+  int32_t (*alltoallv)(void *user, const void *d_send, const int64_t *send_counts, void *d_recv,
+                       const int64_t *recv_counts, int64_t elem_bytes, void *stream);
+  int32_t (*allreduce_sum_f64)(void *user, double *d_buf, int64_t n, void *stream);
+} mlipcpp_b200_comm_t;
+
+typedef struct mlipcpp_b200_domain_impl *mlipcpp_b200_domain_t;
+
+/* This rank's domain.  cell: row-major lattice of the whole cell (periodic);
+ * skin: halo width beyond the cutoff (A) for atoms that moved since
+ * ownership was assigned.  Returns NULL on failure (message in
+ * mlipcpp_get_last_error), e.g. when a slab is not wider than twice the
+ * cutoff plus skin. */
+mlipcpp_b200_domain_t mlipcpp_b200_domain_create(mlipcpp_model_t model, const float cell[9],
+                                                 const int32_t grid[3], int32_t rank, float skin,
+                                                 const mlipcpp_b200_comm_t *comm);
+void mlipcpp_b200_domain_free(mlipcpp_b200_domain_t domain);
+/* The owned atoms' atomic numbers (host), in the order of the positions of
+ * every step.  An unknown Z returns MLIPCPP_ERROR_COMPUTATION. */
+mlipcpp_error_t mlipcpp_b200_domain_set_atoms(mlipcpp_b200_domain_t domain, int32_t n_owned,
+                                              const int32_t *atomic_numbers);
+/* One evaluation: d_positions [3 n_owned] f32 device; d_forces [3 n_owned]
+ * f32 device (may be NULL); energy (eV, composition included) and virial
+ * (Voigt xx yy zz yz xz xy, sum_e e (x) dE/de, not divided by the volume)
+ * over the whole cell, on every rank. */
+mlipcpp_error_t mlipcpp_b200_domain_step(mlipcpp_b200_domain_t domain, const float *d_positions,
+                                         float *d_forces, bool compute_forces, double *energy,
+                                         double virial[6]);
+/* Last step: device ms of halo, neighbour list + requests, model (with the
+ * token exchanges), reverse force halo, sum over ranks, whole step; host ms
+ * of the call; then owned atoms, ghosts, edges, token rows received, token
+ * rows sent, halo copies sent -> stats[0..12]. */
+mlipcpp_error_t mlipcpp_b200_domain_stats(mlipcpp_b200_domain_t domain, double stats[13]);
+
 /* Number of CUDA kernels this library has launched in this process. */
 int64_t mlipcpp_b200_kernel_launches(void);
 
 /* Number of device allocations (cudaMalloc calls) this library has made in
  * this process. */
 int64_t mlipcpp_b200_device_allocations(void);
+
+/* Failure-detection test hooks (no counterpart in the reference).  Every
+ * wait of the tensor-core GEMM pipelines is bounded; on expiry the CTA
+ * stops, lets its own copies and MMAs complete, frees its tensor memory and
+ * records a device error that the call returns as MLIPCPP_ERROR_COMPUTATION;
+ * the model stays usable.  set_wait_bound_ns sets that bound on the current
+ * device (0: the default of 1 s).  inject_gemm_stall makes the next GEMM
+ * launch with a plain store epilogue withhold the operand loads of its
+ * first CTA, so that CTA's waits run out. */
+mlipcpp_error_t mlipcpp_b200_set_wait_bound_ns(uint64_t ns);
+mlipcpp_error_t mlipcpp_b200_inject_gemm_stall(void);
 
 /* CUDA device ordinal used by models created afterwards (default: the
  * calling thread's current device). */

@@ -98,13 +98,19 @@ def lib() -> ctypes.CDLL:
         "mlipcpp_b200_predict_device": (ctypes.c_int, [vp, i32, vp, vp, vp, vp, vp, b, vp]),
         "mlipcpp_b200_predict_device_forces": (ctypes.c_int, [vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
         "mlipcpp_b200_set_timing": (ctypes.c_int, [vp, b]),
-        "mlipcpp_b200_predict_local": (ctypes.c_int, [vp, i32, vp, vp, i32, i32, vp, vp, b, vp, vp, vp]),
         "mlipcpp_b200_last_timings": (ctypes.c_int, [vp, vp]),
         "mlipcpp_b200_last_shape": (ctypes.c_int, [vp, vp]),
         "mlipcpp_b200_neighbor_list": (i64, [i32, vp, vp, vp, f32, i64, vp, vp, vp, vp, vp]),
         "mlipcpp_b200_kernel_launches": (i64, []),
         "mlipcpp_b200_device_allocations": (i64, []),
+        "mlipcpp_b200_set_wait_bound_ns": (ctypes.c_int, [ctypes.c_uint64]),
+        "mlipcpp_b200_inject_gemm_stall": (ctypes.c_int, []),
         "mlipcpp_b200_set_device": (ctypes.c_int, [i32]),
+        "mlipcpp_b200_domain_create": (vp, [vp, vp, vp, i32, f32, vp]),
+        "mlipcpp_b200_domain_free": (None, [vp]),
+        "mlipcpp_b200_domain_set_atoms": (ctypes.c_int, [vp, i32, vp]),
+        "mlipcpp_b200_domain_step": (ctypes.c_int, [vp, vp, vp, b, vp, vp]),
+        "mlipcpp_b200_domain_stats": (ctypes.c_int, [vp, vp]),
         "mlipcpp_b200_set_kernel_profiling": (ctypes.c_int, [vp, b]),
         "mlipcpp_b200_kernel_stats": (ctypes.c_int, [vp, vp]),
     }
@@ -388,22 +394,6 @@ class Predictor:
             None if c is None else c.ctypes.data, None if p is None else p.ctypes.data, ctypes.byref(po),
             ctypes.c_void_p(d_forces) if d_forces else None, ctypes.byref(e), st.ctypes.data, ctypes.byref(hs)))
         return float(e.value), (st if hs.value else None)
-
-    def predict_local(self, d_positions: int, numbers, n_layer0: int, n_owned: int, cell, pbc=None,
-                      compute_forces=True, d_forces: int = 0):
-        """One spatial domain (see include/mlipcpp_b200.h): `d_positions` is a
-        device pointer to [3 n_local] float64, `d_forces` a device pointer to
-        [3 n_local] float32 (or 0).  Returns (energy_owned, virial[6])."""
-        z = np.ascontiguousarray(numbers, dtype=np.int32)
-        bb = np.ascontiguousarray(cell, dtype=np.float32).reshape(9)
-        pb = None if pbc is None else np.asarray([bool(x) for x in pbc], np.bool_)
-        e = ctypes.c_double()
-        v = np.zeros(6, np.float64)
-        _check(lib().mlipcpp_b200_predict_local(
-            self._h, int(z.shape[0]), ctypes.c_void_p(d_positions), z.ctypes.data, int(n_layer0), int(n_owned),
-            bb.ctypes.data, None if pb is None else pb.ctypes.data, bool(compute_forces), ctypes.c_void_p(d_forces) if d_forces else None,
-            ctypes.byref(e), v.ctypes.data))
-        return float(e.value), v
 
     def set_timing(self, on: bool = True):
         _check(lib().mlipcpp_b200_set_timing(self._h, bool(on)))

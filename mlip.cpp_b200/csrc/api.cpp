@@ -13,6 +13,8 @@
 
 #include "mlipcpp.h"
 #include "mlipcpp_b200.h"
+#include "domain.h"
+#include "gemm_tc.cuh"
 #include "gguf.h"
 #include "model.h"
 
@@ -27,6 +29,10 @@ struct mlipcpp_model_impl {
   mlipcpp_model_options_t options{};
   pet::Result last;
   bool loaded = false;
+};
+
+struct mlipcpp_b200_domain_impl {
+  std::unique_ptr<pet::DomainEngine> engine;
 };
 
 struct mlipcpp_result_impl {
@@ -577,28 +583,95 @@ mlipcpp_error_t mlipcpp_b200_predict_device_forces(mlipcpp_model_t model, int32_
   }
 }
 
-mlipcpp_error_t mlipcpp_b200_predict_local(mlipcpp_model_t model, int32_t n_local, const double *d_positions,
-                                           const int32_t *atomic_numbers, int32_t n_layer0, int32_t n_owned,
-                                           const float cell[9], const bool *pbc, bool compute_forces,
-                                           float *d_forces, double *energy, double virial[6]) {
-  if (auto e = check_model(model)) return e;
-  if (!d_positions || !atomic_numbers || !cell || !energy || !virial) {
+static_assert(sizeof(mlipcpp_b200_comm_t) == sizeof(pet::DomainComm), "comm layout");
+
+mlipcpp_b200_domain_t mlipcpp_b200_domain_create(mlipcpp_model_t model, const float cell[9], const int32_t grid[3],
+                                                 int32_t rank, float skin, const mlipcpp_b200_comm_t *comm) {
+  if (check_model(model)) return nullptr;
+  if (!cell || !grid || !comm) {
     set_error("NULL pointer argument");
-    return MLIPCPP_ERROR_NULL_POINTER;
+    return nullptr;
   }
-  if (n_local <= 0 || n_owned < 0 || n_layer0 < n_owned || n_local < n_layer0) {
-    set_error("local system needs 0 <= n_owned <= n_layer0 <= n_local, n_local > 0");
+  try {
+    pet::DomainComm c;
+    c.user = comm->user;
+    c.alltoallv = comm->alltoallv;
+    c.allreduce_sum_f64 = comm->allreduce_sum_f64;
+    const int g[3] = {grid[0], grid[1], grid[2]};
+    auto *d = new mlipcpp_b200_domain_impl();
+    try {
+      d->engine.reset(new pet::DomainEngine(*model->model, cell, g, rank, skin, c));
+    } catch (...) {
+      delete d;
+      throw;
+    }
+    clear_error();
+    return d;
+  } catch (const std::exception &e) {
+    map_exception(e, "Domain set-up failed: ", MLIPCPP_ERROR_INVALID_PARAMETER);
+    return nullptr;
+  }
+}
+
+void mlipcpp_b200_domain_free(mlipcpp_b200_domain_t domain) { delete domain; }
+
+mlipcpp_error_t mlipcpp_b200_domain_set_atoms(mlipcpp_b200_domain_t domain, int32_t n_owned,
+                                              const int32_t *atomic_numbers) {
+  if (!domain) {
+    set_error("Invalid domain handle");
+    return MLIPCPP_ERROR_INVALID_HANDLE;
+  }
+  if (n_owned < 0 || (n_owned > 0 && !atomic_numbers)) {
+    set_error("owned atoms: negative count or NULL atomic numbers");
     return MLIPCPP_ERROR_INVALID_PARAMETER;
   }
   try {
-    const bool open3[3] = {false, false, false};
-    model->model->predict_local(d_positions, n_local, atomic_numbers, n_layer0, n_owned, cell,
-                                pbc ? pbc : open3, compute_forces, d_forces, energy, virial);
+    domain->engine->set_atoms(n_owned, atomic_numbers);
+    clear_error();
+    return MLIPCPP_OK;
+  } catch (const std::exception &e) {
+    return map_exception(e, "Domain set-up failed: ", MLIPCPP_ERROR_COMPUTATION);
+  }
+}
+
+mlipcpp_error_t mlipcpp_b200_domain_step(mlipcpp_b200_domain_t domain, const float *d_positions, float *d_forces,
+                                         bool compute_forces, double *energy, double virial[6]) {
+  if (!domain) {
+    set_error("Invalid domain handle");
+    return MLIPCPP_ERROR_INVALID_HANDLE;
+  }
+  if (!energy || !virial) {
+    set_error("NULL energy or virial pointer");
+    return MLIPCPP_ERROR_NULL_POINTER;
+  }
+  try {
+    domain->engine->step(d_positions, d_forces, compute_forces, energy, virial);
     clear_error();
     return MLIPCPP_OK;
   } catch (const std::exception &e) {
     return map_exception(e, "Prediction failed: ", MLIPCPP_ERROR_COMPUTATION);
   }
+}
+
+mlipcpp_error_t mlipcpp_b200_domain_stats(mlipcpp_b200_domain_t domain, double stats[13]) {
+  if (!domain) {
+    set_error("Invalid domain handle");
+    return MLIPCPP_ERROR_INVALID_HANDLE;
+  }
+  if (!stats) {
+    set_error("NULL stats pointer");
+    return MLIPCPP_ERROR_NULL_POINTER;
+  }
+  const pet::DomainStats &st = domain->engine->stats();
+  for (int k = 0; k < 7; ++k) stats[k] = st.ms[k];
+  stats[7] = static_cast<double>(st.n_own);
+  stats[8] = static_cast<double>(st.n_ghost);
+  stats[9] = static_cast<double>(st.n_edges);
+  stats[10] = static_cast<double>(st.n_req_out);
+  stats[11] = static_cast<double>(st.n_req_in);
+  stats[12] = static_cast<double>(st.n_sent);
+  clear_error();
+  return MLIPCPP_OK;
 }
 
 mlipcpp_error_t mlipcpp_b200_set_timing(mlipcpp_model_t model, bool enable) {
@@ -763,6 +836,27 @@ int64_t mlipcpp_b200_neighbor_list_noalloc(int32_t n_atoms, const float *d_posit
 int64_t mlipcpp_b200_kernel_launches(void) { return pet::g_kernel_launches.load(); }
 
 int64_t mlipcpp_b200_device_allocations(void) { return pet::g_device_allocations.load(); }
+
+mlipcpp_error_t mlipcpp_b200_set_wait_bound_ns(uint64_t ns) {
+  if (!have_cuda_device()) {
+    set_error("No CUDA device available (this backend has no CPU fallback)");
+    return MLIPCPP_ERROR_BACKEND;
+  }
+  try {
+    pet::set_gemm_wait_bound_ns(ns);
+  } catch (const pet::Error &e) {
+    set_error(e.what());
+    return static_cast<mlipcpp_error_t>(e.code);
+  }
+  clear_error();
+  return MLIPCPP_OK;
+}
+
+mlipcpp_error_t mlipcpp_b200_inject_gemm_stall(void) {
+  pet::inject_gemm_stall();
+  clear_error();
+  return MLIPCPP_OK;
+}
 
 mlipcpp_error_t mlipcpp_b200_set_device(int32_t device) {
   int n = 0;

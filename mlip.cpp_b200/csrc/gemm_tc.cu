@@ -38,6 +38,7 @@
 
 #include <cstdint>
 #include <cstdlib>
+#include <atomic>
 #include <cstring>
 
 #include "common.cuh"
@@ -455,10 +456,13 @@ __device__ __forceinline__ void bulk_wait_read() {
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Per-warp state of the TMA epilogue: two 2 KB staging buffers and their
-// load mbarriers; `ph` holds the parity of each buffer's next load wait.
+// load mbarriers; `ph` holds the parity of each buffer's next load wait,
+// `pend` (lane 0's copy) the buffers with a load issued and not yet waited
+// for, which an aborting warp lets land before the CTA ends.
 struct EpiWarp {
   uint32_t buf0, lbar0;
   uint32_t ph;
+  uint32_t pend;
 };
 
 // epilogue_store for the 3xFP16 kernel when the output rows are not
@@ -478,9 +482,10 @@ __device__ __forceinline__ const CUtensorMap *epi_load_map(const EpiMaps &em) {
 // fp32 box (64-byte swizzle), or for a split residual (rs) the hi and lo
 // boxes (1 KB each, unswizzled) side by side.
 template <int EPI>
-__device__ __forceinline__ void epi_issue_load(const EpiMaps &em, const EpiWarp &ew, int b, bool rs, int col,
+__device__ __forceinline__ void epi_issue_load(const EpiMaps &em, EpiWarp &ew, int b, bool rs, int col,
                                                int row0) {
   const uint32_t bar = ew.lbar0 + 8 * b, buf = ew.buf0 + 2048 * b;
+  ew.pend |= 1u << b;
   mbar_expect_tx(bar, 2048);
   if (EPI == EPI_RESID && rs) {
     tma_load_2d(buf, &em.rhi, bar, col, row0);
@@ -490,7 +495,7 @@ __device__ __forceinline__ void epi_issue_load(const EpiMaps &em, const EpiWarp 
   }
 }
 template <int EPI>
-__device__ __forceinline__ void epi_prefetch(const EpiMaps &em, const EpiWarp &ew, bool rs, int row0, int n0,
+__device__ __forceinline__ void epi_prefetch(const EpiMaps &em, EpiWarp &ew, bool rs, int row0, int n0,
                                              int lane) {
   if (!(EPI == EPI_DSILU || EPI == EPI_RESID || EPI == EPI_ACCUM)) return;
   if (lane == 0) {
@@ -536,6 +541,7 @@ __device__ __forceinline__ bool epilogue_tma(const GemmArgs &p, const EpiMaps &e
     if (kLoad) {
       if (!__all_sync(0xffffffffu, wait_or_abort(ew.lbar0 + 8 * b, (ew.ph >> b) & 1u, abort_flag))) return false;
       ew.ph ^= 1u << b;
+      ew.pend &= ~(1u << b);
       if (rs) {  // residual = (hi + lo) 2^-s, rows of 32 bytes
 #pragma unroll
         for (int m = 0; m < 2; ++m) {
@@ -862,6 +868,10 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
   // eload[2 per epilogue warp] (TMA loads of the epilogue's inputs)
   const uint32_t full0 = bars, empty0 = bars + 8 * C::Stages, accf0 = bars + 16 * C::Stages,
                  acce0 = accf0 + 8 * C::TmemBufs, xchg0 = acce0 + 8 * C::TmemBufs, eload0 = xchg0 + 32;
+  // drain: the MMA thread's commit after an abort (its MMAs complete before
+  // the TMEM is freed); after eload's 16 x AccWarps bytes, below tmem_slot
+  const uint32_t drain = bars + 376;
+  static_assert(16 * C::Stages + 16 * C::TmemBufs + 32 + 16 * C::AccWarps <= 376, "mbarrier area");
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gbase + small + 384);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(gbase + small + 392);
   float *xslots = reinterpret_cast<float *>(gbase + small + 512);
@@ -887,6 +897,7 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
     }
     for (int q = 0; q < 4; ++q) mbar_init(xchg0 + 8 * q, 64);
     for (int e = 0; e < 2 * C::AccWarps; ++e) mbar_init(eload0 + 8 * e, 1);
+    mbar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -894,12 +905,14 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  int issued = 0;  // producer: k-stages whose loads it issued
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       int it = 0;
-      bool ok = true;
+      // the failure-detection hook: this CTA's producer issues nothing
+      bool ok = p.stall_cta != static_cast<int>(blockIdx.x);
       for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
         const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BNt;
         for (int kt = 0; kt < nk; ++kt, ++it) {
@@ -923,6 +936,7 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
           }
         }
       }
+      issued = it;
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -992,7 +1006,7 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
       return (tile < tiles && r < p.M) ? static_cast<int>(sc[static_cast<size_t>(c) * split_ld(p.a_split) + r]) : 0;
     };
     int sc_next = scale_of(blockIdx.x, 0);
-    EpiWarp ew{ostage + static_cast<uint32_t>((warp - 2) * C::StageOut), eload0 + 16u * (warp - 2), 0u};
+    EpiWarp ew{ostage + static_cast<uint32_t>((warp - 2) * C::StageOut), eload0 + 16u * (warp - 2), 0u, 0u};
     for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++ep) {
       const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BNt + h * NC;
       const int row = m0 + q * 32 + lane;
@@ -1006,7 +1020,7 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
         const int sc_cur = sc_next;
         sc_next = c + 1 < nch ? scale_of(tile, c + 1) : scale_of(tile + gridDim.x, 0);
         const float sa = row < p.M ? pow2f(-sc_cur) : 0.f;
-        if (!wait_or_abort(accf0 + 8 * b, (chunk / C::TmemBufs) & 1, abort_flag)) {
+        if (!__all_sync(0xffffffffu, wait_or_abort(accf0 + 8 * b, (chunk / C::TmemBufs) & 1, abort_flag))) {
           ok = false;
           break;
         }
@@ -1031,11 +1045,29 @@ __global__ void __launch_bounds__(F16Cfg<BNt>::LaunchBound, 1)
           ok = epilogue_tma<EPI, NC>(p, em, ew, m0 + q * 32, lane, n0, acc, sb, &px, abort_flag);
       }
     }
-    if (lane == 0) bulk_wait_all();  // the epilogue's stores are complete before the CTA ends
+    if (lane == 0) {
+      // after an abort: loads of epilogue inputs still in flight land first
+      for (int b = 0; b < 2; ++b)
+        if ((ew.pend >> b) & 1u) wait_bounded(ew.lbar0 + 8 * b, (ew.ph >> b) & 1u);
+      bulk_wait_all();  // the epilogue's stores are complete before the CTA ends
+    }
   }
 
   tc_fence_before();
   __syncthreads();
+  if (*abort_flag) {
+    // after an abort, this CTA's own asynchronous work completes before it
+    // ends: the loads issued for the last stages (earlier ones were
+    // consumed) and every MMA issued (before its TMEM is freed)
+    if (warp == 0 && lane == 0)
+      for (int j = issued > C::Stages ? issued - C::Stages : 0; j < issued; ++j)
+        wait_bounded(full0 + 8 * (j % C::Stages), (j / C::Stages) & 1);
+    if (warp == 1 && lane == 0) {
+      mma_commit(drain);
+      wait_bounded(drain, 0);
+    }
+    __syncwarp();
+  }
   if (tid == 0 && *abort_flag) atomicExch(err, 1);
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
 }
@@ -1354,6 +1386,8 @@ CUtensorMap make_map_epi(const void *ptr, CUtensorMapDataType type, uint32_t ele
   return m;
 }
 
+std::atomic<bool> g_gemm_stall{false};
+
 // The epilogue maps a launch uses (unscattered output rows only).
 EpiMaps make_epi_maps(const GemmArgs &a) {
   EpiMaps e;
@@ -1386,7 +1420,11 @@ void launch16_bn(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t
   const int tiles = ceil_div(a.M, BM) * (a.N / BNt);
   const int grid = tiles < g_num_sms ? tiles : g_num_sms;
   const EpiMaps em = make_epi_maps(a);
-  k_gemm_3xf16<EPI, BNt><<<grid, C::Threads, C::Smem, s>>>(ah, al, bh, bl, em, a, sp.sc, w, err);
+  GemmArgs args = a;
+  // failure-detection hook: a store epilogue with unscattered rows reads no
+  // global inputs, so the stalled CTA only has its mainloop to drain
+  if (EPI == EPI_STORE && !a.c_rows && g_gemm_stall.exchange(false)) args.stall_cta = 0;
+  k_gemm_3xf16<EPI, BNt><<<grid, C::Threads, C::Smem, s>>>(ah, al, bh, bl, em, args, sp.sc, w, err);
   CUDA_LAUNCH_CHECK();
 }
 
@@ -1455,6 +1493,13 @@ int f16_scale_exponent(float mx) {
 
 bool gemm_f16_supported(const GemmArgs &a) {
   return gemm_tc_supported(a) && a.K % kSBlock == 0 && a.K <= kSBlock * kMaxSBlocks && a.ldb % 8 == 0;
+}
+
+void inject_gemm_stall() { g_gemm_stall.store(true); }
+
+void set_gemm_wait_bound_ns(uint64_t ns) {
+  const uint64_t v = ns ? ns : tc::kWaitNs;
+  CUDA_CHECK(cudaMemcpyToSymbol(tc::g_wait_ns, &v, sizeof(v)));
 }
 
 void gemm_3xf16(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t s) {

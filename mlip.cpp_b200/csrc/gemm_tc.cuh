@@ -47,6 +47,14 @@ void gemm_3xtf32(const GemmArgs &a, const TCWeights &w, int *err, cudaStream_t s
 // a.c_split the epilogue also writes the result in split form.
 void gemm_3xf16(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t s);
 
+// Failure-detection test hooks.  inject_gemm_stall: the next 3xFP16 launch
+// with a plain store epilogue withholds the operand loads of its first CTA,
+// whose bounded waits then run out (the launch sets *err = 1; the CTA
+// drains its own copies and MMAs and frees its TMEM).  set_gemm_wait_bound_ns:
+// the bound of the GEMM kernels' waits on the current device (0: 1 s).
+void inject_gemm_stall();
+void set_gemm_wait_bound_ns(uint64_t ns);
+
 // Power-of-two scale exponent s with max|x| 2^s in [2^14, 2^15) (0 for an
 // all-zero tensor, clamped to [-120, 120]).
 int f16_scale_exponent(float max_abs);

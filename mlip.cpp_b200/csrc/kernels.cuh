@@ -65,6 +65,9 @@ struct GemmArgs {
   bool a_split_ready = false;
   Split16View c_split;
   Split16View r_split;  // EPI_RESID: residual in split form (rows m) instead of R
+  // Failure-detection test hook (3xFP16 kernel): the producer of this CTA
+  // issues no loads, so its MMA warp's bounded wait runs out; -1: none.
+  int stall_cta = -1;
 };
 
 // Dense fp32 GEMM (exact fp32 FFMA accumulation).

@@ -483,6 +483,7 @@ void PETModel::load(const std::string &path, float cutoff_override) {
 // (E1, T1).  A whole structure has n_local = N0 = N1.
 struct Counts {
   int n_local, N0, E0, N1, E1;
+  int n_in;  // layer-0 token rows received from other domains (after the T0 rows)
 };
 
 static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, const Counts &c, bool grad, bool chain,
@@ -525,7 +526,7 @@ static void plan_memory(Plan &P, Plan &S, Acts &a, const Hypers &h, const Counts
   auto ftake = [&](Plan &pl, size_t n) -> float * { return chain ? nullptr : pl.take<float>(n); };
   a.cat = ftake(fs, E0 * featurize_cols(1, h.d, h.aux)); a.hc = ftake(fs, E0 * H);
   a.xin = fs.take<float>(T0 * d); a.xmid = fs.take<float>(T0 * d);
-  a.xl[0] = fs.take<float>(T0 * d); a.xl[1] = fs.take<float>(T1 * d);
+  a.xl[0] = fs.take<float>((T0 + c.n_in) * d); a.xl[1] = fs.take<float>(T1 * d);
   a.o = ftake(fs, T0 * d); a.x1 = fs.take<float>(T0 * d);
   a.hf = ftake(fs, T0 * f);
   a.yn1 = ftake(fs, N1 * r); a.yn2 = fs.take<float>(N1 * r);
@@ -696,12 +697,15 @@ void PETModel::forward_backward(bool grad) {
     at.n_atoms = N;
     at.edge_base = N;
     Split16View sx;
+    // layer-0 tokens of reverse edges held by other domains (collective)
+    if (l == 1 && rm_) rm_->exchange_tokens(a.xl[0], Nl_[0], Tl_[0], d, s);
     if (E > 0) {
       FeaturizeArgs fa{};
       fa.n_edges = E; fa.d = d; fa.layer = l; fa.aux = h.aux;
       fa.vec = nl_.vec.as<float>(); fa.r = a.r;
       fa.nbr_species = a.nbr_species; fa.rev = a.rev;
       fa.emb0 = emb0; fa.x_prev = a.xl[0]; fa.prev_base = Nl_[0];
+      fa.msg_row = (l == 1 && rm_) ? rm_->msg_row : nullptr;
       fa.cat = a.cat;
       Split16View scat, shc;
       if (ch) {
@@ -841,6 +845,9 @@ void PETModel::forward_backward(bool grad) {
   if (T0 > Tl_[1]) CUDA_CHECK(cudaMemsetAsync(a.dx, 0, sizeof(float) * static_cast<size_t>(T0) * d, s));
   readout_bwd(0, a.dx);
   if (E1 > 0) message_bwd(a.dmsg, d, a.rev, Nl_[0], a.dx, E0, E1, d, s);
+  // gradients of the messages whose tokens came from other domains go back
+  // to them, and theirs for this domain's tokens come in (collective)
+  if (rm_) rm_->exchange_token_grads(a.dmsg, a.dx, Nl_[0], d, s);
   block_bwd(1, a.dx, a.dx2);
   if (ch) sdx = split_view(2, T, d);
   block_bwd(0, a.dx2, a.dx, ch ? &sdx : nullptr);
@@ -856,7 +863,7 @@ void PETModel::forward_backward(bool grad) {
 // ---------------------------------------------------------------------------
 // Prediction
 // ---------------------------------------------------------------------------
-void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const int *d_species, bool grad) {
+void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const int *d_species, bool grad, int n_in) {
   n_local_ = n_local;
   Nl_[0] = N0; El_[0] = E0; Tl_[0] = N0 + E0;
   Nl_[1] = N1; El_[1] = E1; Tl_[1] = N1 + E1;
@@ -867,7 +874,7 @@ void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const in
                                      std::to_string(attention_max_tokens(h_.d / h_.heads) - 1));
   chain_ = chain_ok_ && max_tok_ <= attention_split_max_tokens(h_.d / h_.heads);
   // memory plan: size, allocate, assign
-  const Counts c{n_local, N0, E0, N1, E1};
+  const Counts c{n_local, N0, E0, N1, E1, n_in};
   Plan P, S;
   plan_memory(P, S, in_->a, h_, c, grad, chain_, ncf_, ncs_);
   persist_.ensure(P.off);
@@ -895,63 +902,59 @@ void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const in
   edge_prep(ep, stream_);
 }
 
-void PETModel::predict_local(const double *d_pos, int n_local, const int32_t *numbers, int n_layer0, int n_owned,
-                             const float cell[9], const bool pbc[3], bool grad, float *d_forces, double *energy, double virial[6]) {
+const int *PETModel::device_species_map() {
+  if (!d_zmap_.ptr) {
+    int h[128];
+    for (int z = 0; z < 128; ++z) {
+      auto it = species_index_.find(z);
+      h[z] = it == species_index_.end() ? -1 : it->second;
+    }
+    CUDA_CHECK(cudaMemcpy(d_zmap_.ensure(sizeof(h)), h, sizeof(h), cudaMemcpyHostToDevice));
+  }
+  return d_zmap_.as<int>();
+}
+
+const EdgeList &PETModel::domain_neighbors(const double *d_pos, int n_local, int n_own, const GridParams &g) {
   if (wptr_.empty()) throw Error(3, "Model weights not loaded");
-  if (n_owned < 0 || n_layer0 < n_owned || n_local < n_layer0)
-    throw Error(kErrInvalidParameter, "local system needs 0 <= n_owned <= n_layer0 <= n_local");
   CUDA_CHECK(cudaSetDevice(device_));
+  int *derr = static_cast<int *>(d_err_.ensure(sizeof(int) * 4));
+  CUDA_CHECK(cudaMemsetAsync(derr, 0, sizeof(int), stream_));
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[0], stream_));
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[1], stream_));
+  build_local_nl(d_pos, n_local, n_own, g, nl_, nls_, stream_);
+  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[2], stream_));
+  return nl_;
+}
+
+void PETModel::domain_predict(const int *d_species, int n_local, int n_own, RemoteMessages *rm, bool grad,
+                              double *d_red) {
   cudaStream_t s = stream_;
   ncf_ = ncs_ = false;
-  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[0], s));
-  int *derr = static_cast<int *>(d_err_.ensure(sizeof(int) * 4));
-  CUDA_CHECK(cudaMemsetAsync(derr, 0, sizeof(int), s));
-  int *hsp = static_cast<int *>(h_species_.ensure(sizeof(int) * (n_local + 1)));
-  double comp = 0.0;
-  for (int i = 0; i < n_local; ++i) {
-    auto it = species_index_.find(numbers[i]);
-    if (it == species_index_.end())
-      throw Error(kErrComputation, "Unknown atomic number " + std::to_string(numbers[i]) +
-                                       " not found in species_to_index mapping");
-    hsp[i] = it->second;
-    if (i < n_owned) {
-      auto ct = composition_.find(numbers[i]);
-      if (ct != composition_.end()) comp += ct->second;
-    }
+  rm_ = rm;
+  try {
+    setup_graph(n_local, n_own, nl_.n_edges, n_own, nl_.n_edges, d_species, grad, rm ? rm->n_in : 0);
+    if (timing_) CUDA_CHECK(cudaEventRecord(ev_[3], s));
+    forward_backward(grad);
+  } catch (...) {
+    rm_ = nullptr;
+    throw;
   }
-  int *dsp = static_cast<int *>(d_species_.ensure(sizeof(int) * (n_local + 1)));
-  CUDA_CHECK(cudaMemcpyAsync(dsp, hsp, sizeof(int) * n_local, cudaMemcpyHostToDevice, s));
-  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[1], s));
-  // grid over the cell, periodic only along unsplit axes; only the first
-  // n_layer0 atoms are centres, every local atom is a candidate neighbour
-  GridParams g;
-  make_grid_params(cell, pbc, h_.cutoff, &g);
-  build_local_nl(d_pos, n_local, n_layer0, g, nl_, nls_, s);
-  int e1 = 0;
-  CUDA_CHECK(cudaMemcpyAsync(&e1, nl_.offset.as<int>() + n_owned, sizeof(int), cudaMemcpyDeviceToHost, s));
-  CUDA_CHECK(cudaStreamSynchronize(s));
-  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[2], s));
-  setup_graph(n_local, n_layer0, nl_.n_edges, n_owned, e1, dsp, grad);
-  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[3], s));
-  forward_backward(grad);
-  const Acts &a = in_->a;
+  rm_ = nullptr;
   double *red = static_cast<double *>(d_red_.ensure(sizeof(double) * (16 + 7 * kReduceMaxParts)));
-  reduce_local(nl_.vec.as<float>(), a.g, a.e_atom, n_owned, grad ? El_[0] : 0, red, red + 16, s);
-  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[6], s));
-  if (grad && d_forces)
-    CUDA_CHECK(cudaMemcpyAsync(d_forces, a.F, sizeof(float) * 3 * n_local, cudaMemcpyDeviceToDevice, s));
-  double *hout = static_cast<double *>(h_out_.ensure(sizeof(double) * 16));
-  int *herr = reinterpret_cast<int *>(hout + 8);
-  CUDA_CHECK(cudaMemcpyAsync(hout, red, sizeof(double) * 7, cudaMemcpyDeviceToHost, s));
-  CUDA_CHECK(cudaMemcpyAsync(herr, d_err_.ptr, sizeof(int), cudaMemcpyDeviceToHost, s));
-  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[7], s));
-  CUDA_CHECK(cudaStreamSynchronize(s));
+  reduce_local(nl_.vec.as<float>(), in_->a.g, in_->a.e_atom, n_own, grad ? El_[0] : 0, red, red + 16, s);
+  CUDA_CHECK(cudaMemcpyAsync(d_red, red, sizeof(double) * 7, cudaMemcpyDeviceToDevice, s));
+  if (timing_) {
+    CUDA_CHECK(cudaEventRecord(ev_[6], s));
+    CUDA_CHECK(cudaEventRecord(ev_[7], s));
+  }
+}
+
+void PETModel::check_device_error(bool grad) {
+  int herr = 0;
+  CUDA_CHECK(cudaMemcpy(&herr, d_err_.ptr, sizeof(int), cudaMemcpyDeviceToHost));
   if (kprof_) collect_marks();
-  if (*herr != 0)
-    throw Error(kErrComputation, "a tensor-core pipeline wait timed out (device error " +
-                                     std::to_string(*herr) + ")");
-  *energy = hout[0] + comp;
-  for (int c = 0; c < 6; ++c) virial[c] = grad ? hout[1 + c] : 0.0;
+  if (herr != 0)
+    throw Error(kErrComputation, "a tensor-core pipeline wait timed out (device error " + std::to_string(herr) + ")");
   if (timing_) read_times(grad);
 }
 

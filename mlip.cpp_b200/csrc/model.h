@@ -63,6 +63,24 @@ struct PhaseTimes {
   float h2d = 0, nl = 0, prep = 0, forward = 0, backward = 0, reduce = 0, d2h = 0, total = 0;
 };
 
+// Layer-1 messages of a spatial domain whose reverse edges live on other
+// ranks (implemented by DomainEngine, domain.cu).  The message of a layer-1
+// edge i -> j reads the layer-0 token of j -> i (pet_layers.cpp:608-679);
+// when j is a ghost that token is computed by j's owner.  Both calls are
+// collective over the ranks and made exactly once per prediction.
+struct RemoteMessages {
+  virtual ~RemoteMessages() = default;
+  int n_in = 0;                  // remote tokens received after the T0 layer-0 rows
+  const int *msg_row = nullptr;  // [E1]: x_prev row of each edge's message, -1: its local reverse
+  // After the layer-0 forward: x0 = the T0 layer-0 token rows (d floats
+  // each, node rows then edge rows from N0); fill x0 rows [T0, T0 + n_in).
+  virtual void exchange_tokens(float *x0, int N0, int T0, int d, cudaStream_t s) = 0;
+  // After the layer-1 compression backward: dmsg [E1][d] holds the message
+  // gradients; add the gradients other ranks' messages send back into the
+  // layer-0 token gradient rows dx (edge rows from N0).
+  virtual void exchange_token_grads(const float *dmsg, float *dx, int N0, int d, cudaStream_t s) = 0;
+};
+
 class PETModel {
  public:
   PETModel();
@@ -86,17 +104,26 @@ class PETModel {
   bool has_nc_forces() const { return has_ncf_; }
   bool has_nc_stress() const { return has_ncs_; }
 
-  // One spatial domain of a larger cell: n_local atoms with f64 device
-  // positions (owned atoms first, then the ghost atoms within one cutoff of
-  // the owned region, then the remaining ghosts, periodic images already
-  // placed).  Layer 0 runs on the first n_layer0 atoms, layer 1 and the
-  // readout on the first n_owned.  Returns the owned atoms' energy (with
-  // composition), the gradient forces on all n_local atoms (device, may be
-  // null) and the virial sum_e e (x) dE/de over the local edges (not divided
-  // by a volume).  `cell` and `pbc` define the search grid: periodic along
-  // the axes the decomposition leaves whole, open along the split ones.
-  void predict_local(const double *d_pos, int n_local, const int32_t *numbers, int n_layer0, int n_owned,
-                     const float cell[9], const bool pbc[3], bool grad, float *d_forces, double *energy, double virial[6]);
+  // A spatial domain whose layer-0 messages cross to other ranks
+  // (DomainEngine).  domain_neighbors: the neighbour list of the local
+  // system (n_own owned atoms, then ghosts; f64 device positions; only the
+  // owned atoms are centres).  domain_predict: both layers and the readout
+  // on the owned atoms with `rm` supplying the remote messages; gradient
+  // forces on all n_local atoms (device_forces), and the owned energy and
+  // the local virial into d_red[0..6] (device f64).  Synchronises nothing:
+  // the caller reads d_red after a stream synchronisation and then calls
+  // check_device_error.
+  const EdgeList &domain_neighbors(const double *d_pos, int n_local, int n_own, const GridParams &g);
+  void domain_predict(const int *d_species, int n_local, int n_own, RemoteMessages *rm, bool grad, double *d_red);
+  void check_device_error(bool grad);
+  int device() const { return device_; }
+  // species index of every atomic number 0..127 (-1: not in the model), device
+  const int *device_species_map();
+  double composition_energy(int z) const {
+    auto it = composition_.find(z);
+    return it == composition_.end() ? 0.0 : it->second;
+  }
+  bool knows_species(int z) const { return species_index_.count(z) != 0; }
 
   // Device-resident entry for benchmarks: positions already on the device.
   void predict_device(const float *d_pos, const SystemView &sys, bool compute_grad, Result &out,
@@ -124,7 +151,7 @@ class PETModel {
                  const std::vector<int> &atom_begin, bool compute_grad,
                  std::vector<Result *> &results, bool copy_forces, bool nc);
   void forward_backward(bool compute_grad);
-  void setup_graph(int n_local, int N0, int E0, int N1, int E1, const int *d_species, bool grad);
+  void setup_graph(int n_local, int N0, int E0, int N1, int E1, const int *d_species, bool grad, int n_in = 0);
   void read_times(bool grad);
   const float *w(const std::string &name) const;
 
@@ -176,7 +203,8 @@ class PETModel {
   std::map<int, float> composition_;
 
   // per-call device state
-  DevBuf d_pos_, d_species_, d_sys_begin_, d_sys_end_, d_sys_atoms_;
+  DevBuf d_pos_, d_species_, d_sys_begin_, d_sys_end_, d_sys_atoms_, d_zmap_;
+  RemoteMessages *rm_ = nullptr;  // set during domain_predict
   EdgeList nl_;
   NLScratch nls_;
   DevBuf persist_, scratch_;

@@ -69,14 +69,22 @@ __device__ __forceinline__ float aux_value(int j, float x, float y, float z, flo
   return j == 0 ? x : j == 1 ? y : j == 2 ? z : j == 3 ? r : j == 4 ? 1.0f : (j - 5 == sp ? 1.0f : 0.0f);
 }
 
+// Row of x_prev whose token enters edge e's layer-1 message, or -1.
+__device__ __forceinline__ int message_row(const FeaturizeArgs &a, int e) {
+  const int m = a.msg_row ? a.msg_row[e] : -1;
+  if (m >= 0) return m;
+  const int rv = a.rev[e];
+  return rv >= 0 ? a.prev_base + rv : -1;
+}
+
 __device__ __forceinline__ float feat_value(const FeaturizeArgs &a, int e, int c) {
   const int d = a.d;
   const int sp = a.nbr_species[e];
   if (a.layer > 0) {
     if (c < d) {
-      const int rv = a.rev[e];
+      const int row = message_row(a, e);
       const float m0 = a.emb0[static_cast<size_t>(sp) * d + c];
-      const float mr = rv >= 0 ? a.x_prev[static_cast<size_t>(a.prev_base + rv) * d + c] : 0.0f;
+      const float mr = row >= 0 ? a.x_prev[static_cast<size_t>(row) * d + c] : 0.0f;
       return 0.5f * (m0 + mr);
     }
     c -= d;
@@ -103,9 +111,9 @@ __global__ void k_featurize_split(FeaturizeArgs a) {
   if (e >= a.n_edges) return;
   const int sp = a.nbr_species[e];
   if (a.layer > 0) {  // message: 0.5 (embedding[nbr species] + X0[row(reverse edge)])
-    const int rv = a.rev[e];
+    const int row = message_row(a, e);
     const float *m0 = a.emb0 + static_cast<size_t>(sp) * d;
-    const float *mr = rv >= 0 ? a.x_prev + static_cast<size_t>(a.prev_base + rv) * d : nullptr;
+    const float *mr = row >= 0 ? a.x_prev + static_cast<size_t>(row) * d : nullptr;
     for (int k = 0; k < nbd; ++k) {
       const int c = k * 128 + lane * 4;
       const float4 p = __ldg(reinterpret_cast<const float4 *>(m0 + c));

@@ -39,6 +39,10 @@ struct FeaturizeArgs {
   const int *nbr_species, *rev;
   const float *emb0, *x_prev;  // x_prev: layer-0 output tokens, edge e at row prev_base + e
   int prev_base;
+  // optional [n_edges]: the x_prev row of edge e's message where it is not
+  // prev_base + rev[e] (a reverse edge held by another spatial domain, its
+  // token received after the layer-0 rows); -1 where rev[e] applies
+  const int *msg_row = nullptr;
   float *cat;
   Split16View cat_split;  // if set, cat is written in split-fp16 form only
 };

@@ -1,6 +1,6 @@
 // Device helpers shared by the tcgen05 kernels (GEMM, attention): shared
 // memory addresses, bounded mbarrier waits, proxy fences, tcgen05.mma of
-// kind::f16, commits and TMEM loads.  Every wait is bounded (kWaitNs of
+// kind::f16, commits and TMEM loads.  Every wait is bounded (g_wait_ns of
 // %globaltimer); on expiry it raises the CTA's abort flag and returns false.
 #pragma once
 
@@ -9,7 +9,10 @@
 namespace pet {
 namespace tc {
 
-constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s bound on every wait
+constexpr uint64_t kWaitNs = 1000000000ull;  // default bound on every wait: 1 s
+// The bound in force, per device and per translation unit (the host may
+// lower it to test the abort path; see set_gemm_wait_bound_ns).
+static __device__ uint64_t g_wait_ns = kWaitNs;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -97,14 +100,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 // Bounded wait that also gives up when another role has aborted.
 __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, volatile int *abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  const uint64_t t0 = globaltimer(), bound = g_wait_ns;
   while (!mbar_try_wait(bar, parity)) {
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > kWaitNs) {
+    if (globaltimer() - t0 > bound) {
       *abort_flag = 1;
       return false;
     }
   }
+  return true;
+}
+
+// Bounded wait that ignores the abort flag: after an abort, a role lets the
+// asynchronous operations it issued itself (TMA loads, MMAs) complete before
+// the CTA ends.  The default bound applies (these always complete).
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer() - t0 > kWaitNs) return false;
   return true;
 }
 

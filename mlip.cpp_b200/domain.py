@@ -1,54 +1,44 @@
 """Spatial domain decomposition of one large periodic cell over several GPUs.
 
 The reference evaluates one structure on one device (PETModel::predict_batch,
-src/models/pet/pet.cpp:125-694). For cells too large or too slow for one
-GPU, the cell is split into px x py x pz fractional-coordinate slabs, one per
-rank (one process per GPU).
+src/models/pet/pet.cpp:125-694).  Here the cell is split into px x py x pz
+fractional-coordinate slabs, one per rank (one process per GPU); rank r owns
+slab (r % px, r // px % py, r // (px py)) and the atoms whose wrapped
+fractional coordinates fall in it.  The library's domain engine
+(csrc/domain.cu, C ABI mlipcpp_b200_domain_*) does the work of a step on the
+GPU:
 
-Atom i's energy depends on every atom within num_gnn_layers x cutoff of i:
-* layer-1 tokens of i use messages from i's neighbours' layer-0 outputs;
-* those outputs depend on the neighbours' own neighbours;
-* attention is per atom.
+* halo: owned atoms within cutoff (+ skin) of another slab go there as
+  ghosts (periodic images included);
+* both GNN layers and the readout run on the owned atoms only.  A layer-1
+  message of edge i -> j reads the layer-0 token of the reverse edge j -> i
+  (pet_layers.cpp:608-679); for a ghost j that token comes from j's owner,
+  and its gradient goes back after the layer-1 backward;
+* forces on ghosts go back to their owners; energy and virial are summed.
 
-So each rank builds a local system of three groups (ghosts only across the
-faces the grid splits; along an unsplit axis the local system stays
-periodic):
-
-    owned atoms                           layer 0, layer 1 and the readout
-    ghosts within 1 cutoff of the slab    layer 0 only (their outputs feed
-                                          the owned atoms' messages)
-    ghosts within 2 cutoffs of the slab   neighbour candidates only
-
-The local energy is the owned atoms' energy. The local forces are its gradient
-on every local atom, owned and ghost, and the local virial is over the local
-edges. Summing the three over ranks gives the whole cell's energy, forces and
-virial. That sum is the only exchange step: one NCCL all-reduce of the force
-array and one of (energy, virial). Every rank holds the whole position array;
-each step it partitions on the device (fractional coordinates, 27 image
-shifts, two host synchronisations for the counts) and gathers its local
-system with exact f64 image shifts.
+The exchanges are collectives this module supplies to the engine: over NCCL
+with torch.distributed (``NcclComm``), or between threads of one process for
+tests that emulate several ranks on one GPU (``LocalComm``).  Each exchange is
+issued on the library's CUDA stream, so it is ordered with the kernels around
+it without host synchronisation.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass
+import ctypes
+import sys
+import threading
+import traceback
 
 import numpy as np
 
+ALLTOALLV = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64),
+                             ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64), ctypes.c_int64, ctypes.c_void_p)
+ALLREDUCE = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p)
 
-@dataclass
-class LocalDomain:
-    index: np.ndarray       # [n_local] global atom of each local atom
-    shift: np.ndarray       # [n_local, 3] integer image shift (in cell vectors)
-    n_layer0: int           # owned + first ghost shell
-    n_owned: int
-    cell: np.ndarray        # (3, 3) float32 search-grid cell (the global cell)
-    pbc: tuple              # periodic along the axes the grid does not split
-    grid: tuple
-    rank: int
 
-    @property
-    def n_local(self) -> int:
-        return int(self.index.shape[0])
+class _CComm(ctypes.Structure):
+    """mlipcpp_b200_comm_t (include/mlipcpp_b200.h)."""
+    _fields_ = [("user", ctypes.c_void_p), ("alltoallv", ALLTOALLV), ("allreduce_sum_f64", ALLREDUCE)]
 
 
 def face_distances(cell) -> np.ndarray:
@@ -74,136 +64,277 @@ def grid_for(world: int) -> tuple:
     return tuple(g)
 
 
-def partition(positions, cell, cutoff: float, grid: tuple, rank: int, layers: int = 2) -> LocalDomain:
-    """Local system of `rank` on the fractional grid `grid` (px, py, pz),
-    computed on the host in float64.  Atom order: owned atoms (ascending
-    global index), then the first ghost shell, then the second, each shell
-    ordered by image shift (x slowest, -1..1) and then global index."""
-    import torch
-    d = partition_device(torch.from_numpy(np.asarray(positions, np.float64).reshape(-1, 3)),
-                         torch.from_numpy(np.asarray(cell, np.float64).reshape(3, 3)), cutoff, grid, rank, layers)
-    return LocalDomain(d["index"].numpy(), d["shift"].numpy(), d["n_layer0"], d["n_owned"], d["cell"],
-                       d["pbc"], tuple(int(x) for x in grid), rank)
+def slab_of_rank(rank: int, grid) -> tuple:
+    px, py, _ = grid
+    return rank % px, (rank // px) % py, rank // (px * py)
 
 
-_SHIFTS = np.array(np.meshgrid(*([(-1, 0, 1)] * 3), indexing="ij")).reshape(3, -1).T  # [27, 3]
+def owners(positions, cell, grid) -> np.ndarray:
+    """Owning rank of every atom: the slab of its wrapped fractional
+    coordinates (float64)."""
+    pos = np.asarray(positions, np.float64).reshape(-1, 3)
+    frac = pos @ np.linalg.inv(np.asarray(cell, np.float64).reshape(3, 3))
+    fw = frac - np.floor(frac)
+    p = np.asarray(grid, np.int64)
+    c = np.minimum((fw * p).astype(np.int64), p - 1)
+    return (c[:, 0] + p[0] * (c[:, 1] + p[1] * c[:, 2])).astype(np.int32)
 
 
-def partition_device(positions, cell, cutoff: float, grid: tuple, rank: int, layers: int = 2) -> dict:
-    """partition() with torch tensors on any device (positions [N, 3],
-    cell [3, 3]).  An axis the grid does not split stays periodic and gets
-    no ghosts.  Returns index and shift tensors on that device, the local
-    positions (f64; translated along split axes so that their fractional
-    coordinates start at 0), the counts, the search cell and its pbc flags.
-    Two host synchronisations (the counts)."""
-    import torch
-
-    dev = positions.device
-    pos = positions.to(torch.float64)
-    c = cell.to(device=dev, dtype=torch.float64)
-    p = torch.tensor(grid, dtype=torch.float64, device=dev)
-    pi = torch.tensor(grid, dtype=torch.int64, device=dev)
-    face = torch.from_numpy(face_distances(c.cpu().numpy())).to(dev)
-    split = p > 1
-    d1 = torch.where(split, cutoff / face, torch.zeros_like(face))
-    dn = torch.where(split, layers * cutoff / face, torch.zeros_like(face))
-    if bool(torch.any(dn >= 1.0 / p)):
-        # one image (+-1) per axis suffices only if a ghost shell is thinner than a slab
-        raise ValueError("cell too small for this many domains (ghost shell thicker than a slab)")
-    frac = pos @ torch.linalg.inv(c)
-    base = -torch.floor(frac)                 # shift into the primary cell
-    fw = frac + base                          # in [0, 1)
-    coord = torch.minimum((fw * p).to(torch.int64), pi - 1)
-    rc = torch.tensor(np.unravel_index(rank, tuple(grid), order="F"), dtype=torch.int64, device=dev)
-    lo, hi = rc / p, (rc + 1) / p
-    own_mask = torch.all(coord == rc, dim=1)
-    S = torch.from_numpy(_SHIFTS).to(dev)
-    f = fw.unsqueeze(0) + S.unsqueeze(1).to(torch.float64)       # [27, N, 3]
-    in2 = torch.all((f >= lo - dn) & (f < hi + dn), dim=2)
-    in1 = torch.all((f >= lo - d1) & (f < hi + d1), dim=2)
-    centre = 13                                                  # shift (0, 0, 0)
-    in1[centre] &= ~own_mask
-    in2[centre] &= ~own_mask
-    in2 &= ~in1
-    owned = torch.nonzero(own_mask).squeeze(1)
-    k1, i1 = torch.nonzero(in1, as_tuple=True)
-    k2, i2 = torch.nonzero(in2, as_tuple=True)
-    index = torch.cat([owned, i1, i2])
-    shift = torch.cat([torch.zeros((owned.shape[0], 3), dtype=torch.int64, device=dev), S[k1], S[k2]])
-    shift = shift + base[index].to(torch.int64)
-    n_owned = int(owned.shape[0])
-    n_layer0 = n_owned + int(i1.shape[0])
-    origin = torch.where(split, lo - dn, torch.zeros_like(lo))
-    local = pos[index] + (shift.to(torch.float64) - origin) @ c
-    pbc = tuple(bool(x) for x in (np.asarray(grid) == 1))
-    return {"index": index, "shift": shift, "local": local, "n_owned": n_owned, "n_layer0": n_layer0,
-            "cell": c.cpu().numpy().astype(np.float32), "pbc": pbc}
+def halo_copies(positions, cell, grid, rank: int, dest: int, width: float) -> list:
+    """(atom, image shift) pairs that rank `rank`'s owned atoms send to rank
+    `dest`: the images (shifted only along split axes) inside dest's slab
+    widened by `width` (A) along each split axis; no unshifted copy to
+    itself.  A float64 restatement of the engine's halo test, for the
+    geometry checks."""
+    pos = np.asarray(positions, np.float64).reshape(-1, 3)
+    c = np.asarray(cell, np.float64).reshape(3, 3)
+    frac = pos @ np.linalg.inv(c)
+    fw = frac - np.floor(frac)
+    face = face_distances(c)
+    own = owners(pos, c, grid) == rank
+    cd = slab_of_rank(dest, grid)
+    out = []
+    rng = [(-1, 0, 1) if grid[a] > 1 else (0,) for a in range(3)]
+    for i in np.nonzero(own)[0]:
+        for sx in rng[0]:
+            for sy in rng[1]:
+                for sz in rng[2]:
+                    s = (sx, sy, sz)
+                    if dest == rank and s == (0, 0, 0):
+                        continue
+                    ok = True
+                    for a in range(3):
+                        if grid[a] == 1:
+                            continue
+                        d1 = width / face[a]
+                        v = fw[i, a] + s[a]
+                        ok &= (cd[a] / grid[a] - d1) <= v < ((cd[a] + 1) / grid[a] + d1)
+                    if ok:
+                        out.append((int(i), s))
+    return out
 
 
-def predictor_eval(predictor):
-    """Per-domain evaluator backed by the GPU library (C ABI
-    mlipcpp_b200_predict_local).  Returns (owned energy, local virial)."""
-    import torch
+# ---------------------------------------------------------------------------
+# Collectives
+# ---------------------------------------------------------------------------
+class _DevBytes:
+    """A device byte range as a zero-copy torch tensor (CUDA array interface)."""
 
-    def run(d: LocalDomain, local_pos, numbers, forces_out):
-        torch.cuda.synchronize()  # the library runs on its own stream
-        return predictor.predict_local(local_pos.data_ptr(), numbers, d.n_layer0, d.n_owned, d.cell, d.pbc,
-                                       True, forces_out.data_ptr())
-    return run
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (int(nbytes),), "typestr": "|u1", "data": (int(ptr), False),
+                                         "version": 2, "strides": None}
 
 
-class DomainRunner:
-    """Evaluates one cell split over the ranks of a torch.distributed group,
-    or over `emulate` domains one after another in a single process.
+def _bytes(torch, ptr: int, nbytes: int):
+    if nbytes == 0:
+        return torch.empty(0, dtype=torch.uint8, device="cuda")
+    return torch.as_tensor(_DevBytes(ptr, nbytes), device="cuda")
 
-    `local_eval(domain, local_pos f64 [n,3], numbers, forces_out f32 [n,3])`
-    evaluates one local system and returns (owned energy, virial[6])."""
 
-    def __init__(self, local_eval, numbers, cell, cutoff: float, world: int = 1, rank: int = 0,
-                 group=None, emulate: int | None = None, device: str = "cuda"):
+class NcclComm:
+    """The engine's collectives over a torch.distributed process group (NCCL):
+    all_to_all_single and all_reduce, issued on the library's stream."""
+
+    def __init__(self, group=None):
         import torch
+        import torch.distributed as dist
+        self.torch, self.dist, self.group = torch, dist, group
+        self.world = dist.get_world_size(group)
+        self._a2a = ALLTOALLV(self._alltoallv)
+        self._ar = ALLREDUCE(self._allreduce)
+        self.c = _CComm(None, self._a2a, self._ar)
 
+    def _alltoallv(self, user, send, sc, recv, rc, eb, stream):
+        try:
+            torch = self.torch
+            s = [int(sc[r]) * eb for r in range(self.world)]
+            r_ = [int(rc[r]) * eb for r in range(self.world)]
+            st = torch.cuda.ExternalStream(int(stream))
+            with torch.cuda.stream(st):
+                self.dist.all_to_all_single(_bytes(torch, recv, sum(r_)), _bytes(torch, send, sum(s)), r_, s,
+                                            group=self.group)
+            return 0
+        except Exception:  # noqa: BLE001 - the engine raises the error
+            traceback.print_exc(file=sys.stderr)
+            return 1
+
+    def _allreduce(self, user, buf, n, stream):
+        try:
+            torch = self.torch
+            st = torch.cuda.ExternalStream(int(stream))
+            with torch.cuda.stream(st):
+                t = _bytes(torch, buf, 8 * n).view(torch.float64)
+                self.dist.all_reduce(t, group=self.group)
+            return 0
+        except Exception:  # noqa: BLE001
+            traceback.print_exc(file=sys.stderr)
+            return 1
+
+
+class LocalComm:
+    """The engine's collectives between `world` threads of one process, each
+    driving one rank's engine on the same GPU (tests that emulate several
+    ranks).  Each exchange synchronises the caller's stream, meets the other
+    threads at a barrier (with a timeout, so a failing rank cannot hang the
+    others) and copies its incoming segments from the senders' buffers."""
+
+    def __init__(self, world: int, timeout: float = 300.0):
+        import torch
         self.torch = torch
-        self.local_eval = local_eval
-        self.device = device
-        self.numbers = np.asarray(numbers, np.int32)
-        self.cell = np.asarray(cell, np.float64).reshape(3, 3)
-        self.cutoff = float(cutoff)
-        self.world, self.rank, self.group = world, rank, group
-        self.n_domains = emulate if emulate else world
-        self.my_domains = list(range(self.n_domains)) if emulate else [rank]
-        self.grid = grid_for(self.n_domains)
-        self.cell_t = torch.from_numpy(self.cell).to(device)
+        self.world = world
+        self.barrier = threading.Barrier(world, timeout=timeout)
+        self.posts = [None] * world
+        self._keep = []
 
-    def step(self, positions):
-        """One E + F + virial evaluation from positions [N, 3] (f32 or f64)
-        on the runner's device: partition, gather of the local systems,
-        per-domain evaluation, scatter of the local forces and the sums over
-        ranks.  Returns (energy, forces [N, 3] f32, virial [6] f64)."""
+    def for_rank(self, rank: int) -> _CComm:
+        a2a = ALLTOALLV(lambda u, s, sc, r, rc, eb, st: self._alltoallv(rank, s, sc, r, rc, eb, st))
+        ar = ALLREDUCE(lambda u, b, n, st: self._allreduce(rank, b, n, st))
+        self._keep += [a2a, ar]
+        return _CComm(None, a2a, ar)
+
+    def _alltoallv(self, rank, send, sc, recv, rc, eb, stream):
         torch = self.torch
-        n = positions.shape[0]
-        F = torch.zeros((n, 3), dtype=torch.float32, device=self.device)
-        acc = torch.zeros(7, dtype=torch.float64)
-        for r in self.my_domains:
-            d = partition_device(positions, self.cell_t, self.cutoff, self.grid, r)
-            idx = d["index"]
-            dom = LocalDomain(idx, d["shift"], d["n_layer0"], d["n_owned"], d["cell"], d["pbc"], self.grid, r)
-            z = self.numbers[idx.cpu().numpy()]
-            local = d["local"].contiguous()
-            forces = torch.empty((idx.shape[0], 3), dtype=torch.float32, device=self.device)
-            e, vir = self.local_eval(dom, local, z, forces)
-            F.index_add_(0, idx, forces)
-            acc[0] += e
-            acc[1:] += torch.from_numpy(np.asarray(vir, np.float64))
-        if self.world > 1:
-            import torch.distributed as dist
-            dist.all_reduce(F, group=self.group)
-            accd = acc.to(self.device)
-            dist.all_reduce(accd, group=self.group)
-            acc = accd.cpu()
-        return float(acc[0]), F, acc[1:].numpy()
+        try:
+            torch.cuda.ExternalStream(int(stream)).synchronize()
+            self.posts[rank] = (int(send or 0), [int(sc[r]) for r in range(self.world)])
+            self.barrier.wait()
+            off = 0
+            for r in range(self.world):
+                sp, scr = self.posts[r]
+                n = scr[rank] * eb
+                if n != int(rc[r]) * eb:
+                    raise RuntimeError("alltoallv counts disagree")
+                if n:
+                    src_off = sum(scr[:rank]) * eb
+                    _bytes(torch, recv + off, n).copy_(_bytes(torch, sp + src_off, n))
+                off += n
+            torch.cuda.synchronize()
+            self.barrier.wait()
+            return 0
+        except Exception:  # noqa: BLE001
+            traceback.print_exc(file=sys.stderr)
+            self.barrier.abort()
+            return 1
+
+    def _allreduce(self, rank, buf, n, stream):
+        torch = self.torch
+        try:
+            torch.cuda.ExternalStream(int(stream)).synchronize()
+            self.posts[rank] = _bytes(torch, buf, 8 * n).view(torch.float64).clone()
+            self.barrier.wait()
+            total = sum(p.to(torch.float64) for p in self.posts)
+            self.barrier.wait()
+            _bytes(torch, buf, 8 * n).view(torch.float64).copy_(total)
+            torch.cuda.synchronize()
+            self.barrier.wait()
+            return 0
+        except Exception:  # noqa: BLE001
+            traceback.print_exc(file=sys.stderr)
+            self.barrier.abort()
+            return 1
+
+
+# ---------------------------------------------------------------------------
+# One rank's domain
+# ---------------------------------------------------------------------------
+class Domain:
+    """This rank's part of one periodic cell (mlipcpp_b200_domain_*).
+
+    `numbers` are the owned atoms' atomic numbers; each step takes their
+    positions as a device float32 tensor [n_owned, 3] and returns the energy
+    and virial of the whole cell (and writes the owned atoms' forces into
+    `forces`, a device float32 tensor of the same shape, when given)."""
+
+    def __init__(self, predictor, cell, grid, rank: int, comm: _CComm, skin: float = 0.0):
+        from . import lib, _check
+        self._lib, self._check = lib(), _check
+        self._comm = comm
+        c = np.ascontiguousarray(cell, np.float32).reshape(9)
+        g = np.ascontiguousarray(grid, np.int32).reshape(3)
+        self._h = self._lib.mlipcpp_b200_domain_create(predictor._h, c.ctypes.data, g.ctypes.data, int(rank),
+                                                       float(skin), ctypes.byref(comm))
+        if not self._h:
+            from . import MLIPError, INVALID_PARAMETER
+            msg = self._lib.mlipcpp_get_last_error()
+            raise MLIPError(INVALID_PARAMETER, (msg or b"domain set-up failed").decode())
+        self.predictor = predictor  # keeps the model alive
+        self.grid, self.rank = tuple(int(x) for x in grid), int(rank)
+        self.cell = np.asarray(cell, np.float64).reshape(3, 3)
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h:
+            try:
+                self._lib.mlipcpp_b200_domain_free(h)
+            except Exception:  # noqa: BLE001
+                pass
+            self._h = None
+
+    def set_atoms(self, numbers):
+        z = np.ascontiguousarray(numbers, np.int32)
+        self._check(self._lib.mlipcpp_b200_domain_set_atoms(self._h, int(z.shape[0]), z.ctypes.data))
+        self.n_owned = int(z.shape[0])
+
+    def step(self, positions, forces=None, compute_forces: bool = True):
+        e = ctypes.c_double()
+        v = np.zeros(6, np.float64)
+        self._check(self._lib.mlipcpp_b200_domain_step(
+            self._h, ctypes.c_void_p(positions.data_ptr() if self.n_owned else 0),
+            ctypes.c_void_p(forces.data_ptr()) if forces is not None else None, bool(compute_forces),
+            ctypes.byref(e), v.ctypes.data))
+        return float(e.value), v
+
+    def stats(self) -> dict:
+        a = np.zeros(13, np.float64)
+        self._check(self._lib.mlipcpp_b200_domain_stats(self._h, a.ctypes.data))
+        keys = ["halo_ms", "neighbors_requests_ms", "model_ms", "force_halo_ms", "sum_ms", "step_ms",
+                "host_ms", "owned", "ghosts", "edges", "token_rows_in", "token_rows_out", "halo_copies_out"]
+        return {k: (float(x) if k.endswith("ms") else int(x)) for k, x in zip(keys, a)}
 
     def stress(self, virial) -> np.ndarray:
         """Voigt stress = virial / |det cell| (pet.cpp:1079-1097)."""
         vol = abs(float(np.linalg.det(self.cell)))
         return (np.asarray(virial) / vol).astype(np.float32)
+
+
+def run_emulated(make_predictor, structure, grid, skin: float = 0.0, steps: int = 1, compute_forces=True):
+    """Evaluates `structure` (periodic) split over prod(grid) emulated ranks on
+    the current GPU: one thread, one model (make_predictor()) and one engine
+    per rank, exchanging through LocalComm.  Returns (energy, forces [N, 3],
+    virial, per-rank stats) of the last step."""
+    import torch
+    world = int(np.prod(grid))
+    own = owners(structure.positions, structure.cell, grid)
+    comm = LocalComm(world)
+    doms, idx = [], []
+    for r in range(world):
+        d = Domain(make_predictor(), structure.cell, grid, r, comm.for_rank(r), skin)
+        ix = np.nonzero(own == r)[0]
+        d.set_atoms(structure.numbers[ix])
+        doms.append(d)
+        idx.append(ix)
+    out = [None] * world
+    errors = []
+
+    def run(r):
+        try:
+            pos = torch.from_numpy(np.ascontiguousarray(structure.positions[idx[r]], np.float32)).cuda()
+            F = torch.zeros_like(pos)
+            for _ in range(steps):
+                e, v = doms[r].step(pos, F, compute_forces)
+            out[r] = (e, F.cpu().numpy(), v, doms[r].stats())
+        except Exception as ex:  # noqa: BLE001
+            errors.append(ex)
+            comm.barrier.abort()
+
+    th = [threading.Thread(target=run, args=(r,)) for r in range(world)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    if errors:
+        raise errors[0]
+    forces = np.zeros((structure.n_atoms, 3), np.float32)
+    for r in range(world):
+        forces[idx[r]] = out[r][1]
+    return out[0][0], forces, out[0][2], [o[3] for o in out]

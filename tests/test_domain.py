@@ -1,17 +1,14 @@
-"""Spatial domain decomposition (mlip.cpp_b200/domain.py) on CPU: the
-partition, the ghost shells, and the cross-rank sums over a 2-rank gloo
-group.  The per-domain evaluation here is the float64 oracle restricted to
-the owned atoms' energy; the GPU evaluator is tested in test_gpu_domain.py."""
-import os
-
+"""Spatial domain decomposition (mlip.cpp_b200/domain.py, csrc/domain.cu) on
+CPU: the grid, the ownership of atoms, and the halo geometry.  The halo test
+is a float64 restatement of the engine's (every atom within the cutoff of an
+owned atom must reach the local system exactly once, images included); the
+engine itself runs in test_gpu_domain.py."""
 import numpy as np
 import pytest
-import torch
 
-import conftest  # noqa: F401  (registers mlipcpp_b200, also in spawned ranks)
+import conftest  # noqa: F401  (registers mlipcpp_b200)
 from mlipcpp_b200 import domain as dd
 from mlipcpp_b200 import workloads as wl
-from oracle import pet_oracle as po
 
 
 def test_grid_for():
@@ -21,113 +18,55 @@ def test_grid_for():
     assert dd.grid_for(8) == (2, 2, 2)
 
 
+@pytest.mark.parametrize("grid", [(1, 1, 2), (1, 2, 2), (2, 2, 2), (1, 1, 3)])
+def test_every_atom_owned_once(grid):
+    s = wl.fcc_alloy(10, seed=2)
+    # some atoms outside the cell (unwrapped coordinates)
+    shift = np.random.default_rng(3).integers(-2, 3, size=(s.n_atoms, 3)) @ s.cell.astype(np.float64)
+    pos = s.positions.astype(np.float64) + shift
+    own = dd.owners(pos, s.cell, grid)
+    assert own.min() >= 0 and own.max() < np.prod(grid)
+    assert np.array_equal(own, dd.owners(s.positions, s.cell, grid))
+    assert len(np.unique(own)) == np.prod(grid)
+
+
+def _local_system(pos, cell, grid, rank, width):
+    """Owned atoms (wrapped) and received copies of rank `rank`: global
+    atom, image shift (cell vectors), position."""
+    cell = np.asarray(cell, np.float64)
+    frac = pos @ np.linalg.inv(cell)
+    W = -np.floor(frac)
+    own = np.nonzero(dd.owners(pos, cell, grid) == rank)[0]
+    atoms = [(int(i), tuple(W[i].astype(int))) for i in own]
+    for src in range(int(np.prod(grid))):
+        for i, s in dd.halo_copies(pos, cell, grid, src, rank, width):
+            atoms.append((i, tuple((W[i] + np.array(s)).astype(int))))
+    return atoms, len(own)
+
+
 @pytest.mark.parametrize("grid", [(1, 1, 2), (1, 2, 2), (2, 2, 2)])
-def test_partition_owns_once_and_ghosts_complete(grid):
-    s = wl.si_diamond(3, seed=1)
-    rc = 3.0
-    n_dom = int(np.prod(grid))
-    owners = np.zeros(s.n_atoms, int)
+def test_halo_reaches_every_neighbour_once(grid):
+    s = wl.si_diamond(4, seed=1)
+    rc = 4.5
     cell = s.cell.astype(np.float64)
-    for r in range(n_dom):
-        d = dd.partition(s.positions, cell, rc, grid, r)
-        owners[d.index[:d.n_owned]] += 1
-        assert d.pbc == tuple(g == 1 for g in grid)
-        split = np.array([g > 1 for g in grid])
-        local = s.positions[d.index].astype(np.float64) + d.shift @ cell
+    pos = s.positions.astype(np.float64)
+    split = np.array([g > 1 for g in grid])
+    for r in range(int(np.prod(grid))):
+        atoms, n_own = _local_system(pos, cell, grid, r, rc)
         # images are told apart only along split axes (the local system is
         # periodic along the others)
-        key = lambda i, sh: (int(i), *(int(x) if sp else 0 for x, sp in zip(sh, split)))  # noqa: E731
-        keys = {key(i, sh) for i, sh in zip(d.index, d.shift)}
-        assert len(keys) == d.n_local  # no duplicate images
-        own = local[:d.n_owned]
-        # every image of every atom within 2 rc of an owned atom is local, and
-        # within rc of an owned atom it is in the layer-0 set
-        shifts = np.array(np.meshgrid(*([(-2, -1, 0, 1, 2)] * 3), indexing="ij")).reshape(3, -1).T
-        frac = s.positions.astype(np.float64) @ np.linalg.inv(cell)
+        key = lambda i, sh: (i, *(int(x) if sp else 0 for x, sp in zip(sh, split)))  # noqa: E731
+        keys = [key(i, sh) for i, sh in atoms]
+        assert len(set(keys)) == len(keys)  # no atom image twice
+        present = set(keys)
+        owned = atoms[:n_own]
+        opos = np.array([pos[i] + np.array(sh) @ cell for i, sh in owned])
+        frac = pos @ np.linalg.inv(cell)
         base = -np.floor(frac)
-        lay0 = {key(i, sh) for i, sh in zip(d.index[:d.n_layer0], d.shift[:d.n_layer0])}
+        shifts = np.array(np.meshgrid(*([(-1, 0, 1)] * 3), indexing="ij")).reshape(3, -1).T
         for sh in shifts:
-            img_shift = base + sh
-            pos_img = s.positions.astype(np.float64) + img_shift @ cell
-            dmin = np.min(np.linalg.norm(pos_img[:, None, :] - own[None, :, :], axis=2), axis=1)
-            for i in np.nonzero(dmin < 2 * rc)[0]:
-                assert key(i, img_shift[i]) in keys
+            img = base + sh
+            pimg = pos + img @ cell
+            dmin = np.min(np.linalg.norm(pimg[:, None, :] - opos[None, :, :], axis=2), axis=1)
             for i in np.nonzero(dmin < rc)[0]:
-                assert key(i, img_shift[i]) in lay0
-    assert np.all(owners == 1)
-
-
-def oracle_local_eval(orc):
-    """Owned-atom energy, its forces on every local atom, and the local
-    virial, from the float64 oracle on the open local system."""
-    h = orc.h
-
-    def run(d, local_pos, numbers, forces_out):
-        st = wl.Structure(local_pos.numpy().astype(np.float32), np.asarray(numbers, np.int32), d.cell, d.pbc)
-        b = po.prepare_batch([st], h.cutoff, h.cutoff_width, orc.species_to_index)
-        vec = torch.tensor(b.vec, dtype=torch.float64, requires_grad=True)
-        e = orc.atomic_energies(b, vec)[:d.n_owned].sum()
-        (g,) = torch.autograd.grad(e, vec)
-        g = g.numpy()
-        valid = b.pad > 0.5
-        ci = np.repeat(np.arange(b.n_atoms), b.max_nb).reshape(b.n_atoms, b.max_nb)
-        F = np.zeros((b.n_atoms, 3))
-        np.add.at(F, ci[valid], g[valid])
-        np.add.at(F, b.nbr[valid], -g[valid])
-        ev, gv = b.vec[valid].astype(np.float64), g[valid]
-        vir = np.array([np.sum(ev[:, 0] * gv[:, 0]), np.sum(ev[:, 1] * gv[:, 1]), np.sum(ev[:, 2] * gv[:, 2]),
-                        0.5 * np.sum(ev[:, 1] * gv[:, 2] + ev[:, 2] * gv[:, 1]),
-                        0.5 * np.sum(ev[:, 0] * gv[:, 2] + ev[:, 2] * gv[:, 0]),
-                        0.5 * np.sum(ev[:, 0] * gv[:, 1] + ev[:, 1] * gv[:, 0])])
-        comp = sum(orc.composition.get(int(z), 0.0) for z in numbers[:d.n_owned])
-        forces_out.copy_(torch.from_numpy(F.astype(np.float32)))
-        return float(e.detach()) + comp, vir
-    return run
-
-
-def _system(model_file):
-    orc = po.load_oracle(model_file("tiny", 3, cutoff=3.0, cutoff_width=0.5), torch.float64)
-    return orc, wl.si_diamond(3, seed=2)
-
-
-def test_emulated_domains_match_full_oracle(model_file):
-    orc, s = _system(model_file)
-    full = orc.predict([s])[0]
-    for n_dom in (2, 8):
-        run = dd.DomainRunner(oracle_local_eval(orc), s.numbers, s.cell, orc.h.cutoff, emulate=n_dom, device="cpu")
-        e, F, vir = run.step(torch.from_numpy(s.positions))
-        assert abs(e - full["energy_f64"]) / s.n_atoms < 1e-6
-        np.testing.assert_allclose(F.numpy(), full["forces"], atol=2e-5)
-        np.testing.assert_allclose(run.stress(vir), full["stress"], atol=2e-6)
-
-
-def _rank(rank, world, port, path, out):
-    import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
-    orc = po.load_oracle(path, torch.float64)
-    s = wl.si_diamond(3, seed=2)
-    run = dd.DomainRunner(oracle_local_eval(orc), s.numbers, s.cell, orc.h.cutoff, world=world, rank=rank,
-                           device="cpu")
-    e, F, vir = run.step(torch.from_numpy(s.positions))
-    if rank == 0:
-        np.savez(out, e=e, F=F.numpy(), S=run.stress(vir))
-    dist.barrier()
-    dist.destroy_process_group()
-
-
-def test_two_gloo_ranks_match_full_oracle(model_file, tmp_path):
-    import socket
-    import torch.multiprocessing as mp
-    orc, s = _system(model_file)
-    full = orc.predict([s])[0]
-    with socket.socket() as sock:
-        sock.bind(("127.0.0.1", 0))
-        port = sock.getsockname()[1]
-    out = str(tmp_path / "r.npz")
-    mp.start_processes(_rank, args=(2, port, model_file("tiny", 3, cutoff=3.0, cutoff_width=0.5), out),
-                       nprocs=2, start_method="spawn")
-    r = np.load(out)
-    assert abs(float(r["e"]) - full["energy_f64"]) / s.n_atoms < 1e-6
-    np.testing.assert_allclose(r["F"], full["forces"], atol=2e-5)
-    np.testing.assert_allclose(r["S"], full["stress"], atol=2e-6)
+                assert key(int(i), img[i].astype(int)) in present, (r, i, img[i])

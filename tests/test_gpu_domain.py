@@ -1,7 +1,9 @@
-"""Spatial domain decomposition with the GPU evaluator (C ABI
-mlipcpp_b200_predict_local): 2 and 8 domains run one after another on one
-GPU and summed must equal the whole-cell evaluation.  Tolerances are the
-fp32 parity bar (|dE|/N <= 1e-5 eV, |dF| <= 1e-4 eV/A, |dsigma| <= 1e-4 eV/A^3)."""
+"""Spatial domain decomposition on the GPU (csrc/domain.cu through the C ABI
+mlipcpp_b200_domain_*): several ranks emulated on one GPU, one thread, model
+and engine each, exchanging through in-process collectives.  Their summed
+energy, gathered forces and stress must equal the whole-cell evaluation and
+the float64 oracle.  Tolerances are the fp32 parity bar (|dE|/N <= 1e-5 eV,
+|dF| <= 1e-4 eV/A, |dsigma| <= 1e-4 eV/A^3)."""
 import numpy as np
 import pytest
 import torch
@@ -15,28 +17,58 @@ pytestmark = pytest.mark.gpu
 TOL_E, TOL_F, TOL_S = 1e-5, 1e-4, 1e-4
 
 
-def run_domains(pred, s, cutoff, n_dom):
-    run = dd.DomainRunner(dd.predictor_eval(pred), s.numbers, s.cell, cutoff, emulate=n_dom)
-    e, F, vir = run.step(torch.from_numpy(s.positions).cuda())
-    return e, F.cpu().numpy(), run.stress(vir)
+def check(e, F, S, ref_e, ref_F, ref_S, n):
+    assert abs(e - ref_e) / n <= TOL_E, (e, ref_e)
+    assert np.abs(F - ref_F).max() <= TOL_F, np.abs(F - ref_F).max()
+    assert np.abs(S - ref_S).max() <= TOL_S, np.abs(S - ref_S).max()
 
 
-@pytest.mark.parametrize("n_dom", [2, 8])
-def test_domains_match_whole_cell(n_dom, model_file):
-    s = wl.si_diamond(6, seed=41)
-    pred = mb.Predictor(model_file("pet-mad-s", 5))
-    full = pred.predict(s.positions, s.numbers, s.cell, s.pbc, compute_stress=True)
-    e, F, S = run_domains(pred, s, 4.5, n_dom)
-    assert abs(e - full.energy) / s.n_atoms <= TOL_E
-    assert np.abs(F - full.forces).max() <= TOL_F
-    assert np.abs(S - full.stress).max() <= TOL_S
+def stress(virial, cell):
+    return np.asarray(virial) / abs(np.linalg.det(np.asarray(cell, np.float64)))
 
 
-def test_domains_match_oracle(model_file):
-    path = model_file("tiny", 6, cutoff=3.0, cutoff_width=0.5)
-    s = wl.si_diamond(4, seed=42)
+@pytest.mark.parametrize("grid", [(1, 1, 1), (1, 1, 2), (1, 2, 2), (2, 2, 2)])
+def test_domains_match_whole_cell(grid, model_file):
+    path = model_file("pet-mad-s", 5)
+    s = wl.si_diamond(4, seed=61)
+    full = mb.Predictor(path).predict(s.positions, s.numbers, s.cell, s.pbc, compute_stress=True)
+    e, F, vir, st = dd.run_emulated(lambda: mb.Predictor(path), s, grid)
+    check(e, F, stress(vir, s.cell), full.energy, full.forces, full.stress, s.n_atoms)
+    if grid != (1, 1, 1):
+        assert all(x["ghosts"] > 0 and x["token_rows_in"] > 0 for x in st)
+        # every requested token was found by its owner: rows sent == rows
+        # requested, summed over the ranks
+        assert sum(x["token_rows_in"] for x in st) == sum(x["token_rows_out"] for x in st)
+
+
+def test_domains_match_oracle_triclinic(model_file):
+    path = model_file("pet-oam-l", 7)
+    s = wl.fcc_alloy(10, seed=62)
     ref = po.load_oracle(path, torch.float64).predict([s])[0]
-    e, F, S = run_domains(mb.Predictor(path), s, 3.0, 8)
-    assert abs(e - ref["energy_f64"]) / s.n_atoms <= TOL_E
-    assert np.abs(F - ref["forces"]).max() <= TOL_F
-    assert np.abs(S - ref["stress"]).max() <= TOL_S
+    e, F, vir, _ = dd.run_emulated(lambda: mb.Predictor(path), s, (2, 2, 2))
+    check(e, F, stress(vir, s.cell), ref["energy_f64"], ref["forces"], ref["stress"], s.n_atoms)
+
+
+def test_domains_unwrapped_positions_skin_and_repeat(model_file):
+    # positions moved by whole cell vectors, a skin, and two steps in a row:
+    # the same cell, the same answer, bit for bit from step to step
+    path = model_file("pet-mad-s", 8)
+    s = wl.si_diamond(4, seed=63)
+    rng = np.random.default_rng(5)
+    moved = wl.Structure((s.positions + rng.integers(-3, 4, size=(s.n_atoms, 3)) @ s.cell).astype(np.float32),
+                         s.numbers, s.cell, s.pbc)
+    full = mb.Predictor(path).predict(s.positions, s.numbers, s.cell, s.pbc, compute_stress=True)
+    e1, F1, v1, _ = dd.run_emulated(lambda: mb.Predictor(path), moved, (1, 2, 2), skin=0.4, steps=1)
+    e2, F2, v2, _ = dd.run_emulated(lambda: mb.Predictor(path), moved, (1, 2, 2), skin=0.4, steps=2)
+    check(e1, F1, stress(v1, s.cell), full.energy, full.forces, full.stress, s.n_atoms)
+    assert e1 == e2 and np.array_equal(F1, F2) and np.array_equal(v1, v2)
+
+
+def test_domain_rejects_too_small_cell(model_file):
+    pred = mb.Predictor(model_file("pet-mad-s", 5))
+    s = wl.si_diamond(2, seed=64)  # 10.9 A: a slab of 5.4 A is thinner than 2 cutoffs
+    comm = dd.LocalComm(2)
+    with pytest.raises(mb.MLIPError) as ei:
+        dd.Domain(pred, s.cell, (1, 1, 2), 0, comm.for_rank(0))
+    assert ei.value.code == mb.INVALID_PARAMETER
+    assert "slab" in str(ei.value)
