@@ -558,7 +558,7 @@ void PETModel::forward_backward(bool grad) {
   int N = Nl_[0], E = El_[0], T = Tl_[0];  // the layer being processed
   cudaStream_t s = stream_;
   const int *offset = nl_.offset.as<int>();
-  const int *species = d_species_.as<int>();
+  const int *species = species_;
   const float *emb0 = w("model.embedding.weight");
   const bool ch = chain_;
   // silu' is kept for the backward only
@@ -868,6 +868,7 @@ void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const in
   Nl_[0] = N0; El_[0] = E0; Tl_[0] = N0 + E0;
   Nl_[1] = N1; El_[1] = E1; Tl_[1] = N1 + E1;
   max_tok_ = nl_.max_count + 1;
+  species_ = d_species;
   if (max_tok_ > attention_max_tokens(h_.d / h_.heads))
     throw Error(kErrUnsupported, "an atom has " + std::to_string(nl_.max_count) +
                                      " neighbours, above the supported maximum of " +

@@ -205,6 +205,7 @@ class PETModel {
   // per-call device state
   DevBuf d_pos_, d_species_, d_sys_begin_, d_sys_end_, d_sys_atoms_, d_zmap_;
   RemoteMessages *rm_ = nullptr;  // set during domain_predict
+  const int *species_ = nullptr;  // species index of every local atom (device), set by setup_graph
   EdgeList nl_;
   NLScratch nls_;
   DevBuf persist_, scratch_;

@@ -51,17 +51,23 @@ def test_domains_match_oracle_triclinic(model_file):
 
 def test_domains_unwrapped_positions_skin_and_repeat(model_file):
     # positions moved by whole cell vectors, a skin, and two steps in a row:
-    # the same cell, the same answer, bit for bit from step to step
+    # the same cell, the same answer from step to step
     path = model_file("pet-mad-s", 8)
     s = wl.si_diamond(4, seed=63)
     rng = np.random.default_rng(5)
     moved = wl.Structure((s.positions + rng.integers(-3, 4, size=(s.n_atoms, 3)) @ s.cell).astype(np.float32),
                          s.numbers, s.cell, s.pbc)
-    full = mb.Predictor(path).predict(s.positions, s.numbers, s.cell, s.pbc, compute_stress=True)
+    # the reference sees the same float32 positions (moving by cell vectors
+    # rounds them by ~1e-5 A at |x| ~ 65 A, which moves forces by ~1e-4)
+    full = mb.Predictor(path).predict(moved.positions, s.numbers, s.cell, s.pbc, compute_stress=True)
     e1, F1, v1, _ = dd.run_emulated(lambda: mb.Predictor(path), moved, (1, 2, 2), skin=0.4, steps=1)
     e2, F2, v2, _ = dd.run_emulated(lambda: mb.Predictor(path), moved, (1, 2, 2), skin=0.4, steps=2)
     check(e1, F1, stress(v1, s.cell), full.energy, full.forces, full.stress, s.n_atoms)
-    assert e1 == e2 and np.array_equal(F1, F2) and np.array_equal(v1, v2)
+    # energy and virial are deterministic sums; forces on ghosts are
+    # accumulated with atomic adds (edges whose reverse is on another rank),
+    # so repeated steps agree to rounding
+    assert e1 == e2 and np.array_equal(v1, v2)
+    assert np.abs(F1 - F2).max() <= 2e-6
 
 
 def test_domain_rejects_too_small_cell(model_file):
