@@ -440,19 +440,28 @@ def main():
 
     for _ in range(max(args.warmup, 3)):
         step_value()
-    # ---- device-resident timed region (value) -----------------------------
-    launches0 = mb.kernel_launches()
+    for _ in range(2):
+        step_e2e()
+    # ---- timed region: K device-resident steps (value) interleaved with K
+    # end-to-end steps through the public API (e2e), so that both see the
+    # same clocks -------------------------------------------------------------
+    launches = 0
     barrier()
-    dev_ms = []
+    dev_ms, wall_ms = [], []
     with ClockSampler(local) as clk:
         for _ in range(args.steps):
             flush()
+            l0 = mb.kernel_launches()
             dev_ms.append(step_value())
+            launches += mb.kernel_launches() - l0
+            flush()
+            wall_ms.append(step_e2e()[0])
         barrier()
-    launches = mb.kernel_launches() - launches0
     phase = pred.last_timings()
     t_dev = max_over_ranks(float(np.sum(dev_ms)) / 1e3)
     value = n_atoms_job * args.steps / t_dev
+    t_e2e = max_over_ranks(float(np.sum(wall_ms)) / 1e3)
+    e2e = n_atoms_job * args.steps / t_e2e
 
     # ---- per-launch kernel times for the roofline: the same K steps again,
     # with CUDA events around every GEMM and attention launch on the
@@ -465,18 +474,6 @@ def main():
     barrier()
     kstats = pred.kernel_stats()
     pred.set_kernel_profiling(False)
-
-    # ---- end-to-end through the public API with host buffers --------------
-    for _ in range(2):
-        step_e2e()
-    barrier()
-    wall_ms = []
-    for _ in range(args.steps):
-        flush()
-        wall_ms.append(step_e2e()[0])
-    barrier()
-    t_e2e = max_over_ranks(float(np.sum(wall_ms)) / 1e3)
-    e2e = n_atoms_job * args.steps / t_e2e
 
     domain_stats = None
     if dom is not None:
