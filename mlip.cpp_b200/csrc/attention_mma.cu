@@ -403,6 +403,168 @@ __global__ void __launch_bounds__(2 * MT) k_attn_fwd_mma(AttnArgs a) {
   }
 }
 
+// ---- forward with split output, one CTA per 128-column block ---------------------
+// For atoms of at most 48 tokens: the 128 / 32 = 4 heads of one 128-column
+// block of the output share a CTA of 12 warps (head = warp / 3, row strip or
+// converted block = warp % 3), so the row maxima that fix the block's split
+// scale meet in shared memory instead of crossing a thread-block cluster.
+constexpr int kBlkHeads = 128 / kHd;
+struct SmemFB {
+  uint16_t mat[kBlkHeads][6][48 * kPitch];  // per head: Q, K, V hi, then Q, K, V lo
+  float mask[48];
+  int scale[kBlkHeads][3];
+  int rmax[48];  // row maxima of the block's output (bits of non-negative floats)
+};
+
+__global__ void __launch_bounds__(32 * 3 * kBlkHeads) k_attn_fwd_mma_blk(AttnArgs a) {
+  constexpr int MT = 48, kNT = MT / 8;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  SmemFB &sm = *reinterpret_cast<SmemFB *>(smem_raw);
+  const int atom = blockIdx.x, blk = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+  const int hl = warp / 3, sw = warp % 3, h = blk * kBlkHeads + hl;
+  const int e0 = a.offset[atom], S = a.offset[atom + 1] - e0 + 1;
+  const AtomRows tr = atom_rows(atom, e0, a.edge_base);
+  const int NW = (S + 15) >> 4, NK8 = 2 * NW;
+  uint16_t(*mat)[48 * kPitch] = sm.mat[hl];
+  {  // warp (hl, sw): block sw (Q, K or V) of head hl, rows past S zero, one scale
+    float v[MT / 8][8];
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < MT / 8; ++i) {
+      const int task = lane + 32 * i, r = task >> 2, c = (task & 3) * 8;
+      if (r < S) {
+        const float *src = a.qkv + static_cast<size_t>(tr(r)) * 3 * a.d + sw * a.d + h * kHd + c;
+        const float4 x0 = *reinterpret_cast<const float4 *>(src), x1 = *reinterpret_cast<const float4 *>(src + 4);
+        v[i][0] = x0.x; v[i][1] = x0.y; v[i][2] = x0.z; v[i][3] = x0.w;
+        v[i][4] = x1.x; v[i][5] = x1.y; v[i][6] = x1.z; v[i][7] = x1.w;
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[i][k] = 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx = fmaxf(mx, fabsf(v[i][k]));
+    }
+    const int sc = split_scale_exponent(warp_absmax(mx));
+    const float f = pow2f(sc);
+    if (lane == 0) sm.scale[hl][sw] = sc;
+#pragma unroll
+    for (int i = 0; i < MT / 8; ++i) {
+      const int task = lane + 32 * i, r = task >> 2, c = (task & 3) * 8;
+      uint32_t hh[4], ll[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) split2(v[i][2 * k], v[i][2 * k + 1], f, hh[k], ll[k]);
+      *reinterpret_cast<uint4 *>(&mat[sw][r * kPitch + c]) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
+      *reinterpret_cast<uint4 *>(&mat[3 + sw][r * kPitch + c]) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+    }
+  }
+  for (int k = threadIdx.x; k < MT; k += blockDim.x) {
+    sm.mask[k] = k < S ? (k == 0 ? 0.f : a.key_mask[e0 + k - 1]) : 0.f;
+    sm.rmax[k] = 0;
+  }
+  __syncthreads();
+  const uint32_t Qh = smem_addr(mat[0]), Ql = smem_addr(mat[3]), Kh = smem_addr(mat[1]), Kl = smem_addr(mat[4]),
+                 Vh = smem_addr(mat[2]), Vl = smem_addr(mat[5]);
+  float o[4][4];
+#pragma unroll
+  for (int n = 0; n < 4; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[n][e] = 0.f;
+  const int q0 = 16 * sw;
+  const bool act = sw < NW;
+  if (act) {
+    float s[kNT][4];
+#pragma unroll
+    for (int n = 0; n < kNT; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[n][e] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+      uint32_t ah[4], al[4];
+      ldsm4(ah, a_addr(Qh, q0, 16 * ks, lane));
+      ldsm4(al, a_addr(Ql, q0, 16 * ks, lane));
+#pragma unroll
+      for (int p = 0; p < 3; ++p) {
+        if (2 * p < NK8) {
+          uint32_t bh[4], bl[4];
+          ldsm4(bh, bn_addr(Kh, 16 * p, 16 * ks, lane));
+          ldsm4(bl, bn_addr(Kl, 16 * p, 16 * ks, lane));
+          mma3(s[2 * p], ah, al, bh[0], bh[1], bl[0], bl[1]);
+          mma3(s[2 * p + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+        }
+      }
+    }
+    const float fs = pow2f(-(sm.scale[hl][0] + sm.scale[hl][1])) * (1.0f / sqrtf(static_cast<float>(kHd)));
+    float m[2] = {-FLT_MAX, -FLT_MAX};
+#pragma unroll
+    for (int n = 0; n < kNT; ++n) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = q0 + g + 8 * (e >> 1), c = 8 * n + 2 * tig + (e & 1);
+        s[n][e] = (n < NK8 && r < S && c < S) ? fmaf(s[n][e], fs, sm.mask[c]) : -FLT_MAX;
+        m[e >> 1] = fmaxf(m[e >> 1], s[n][e]);
+      }
+    }
+    m[0] = quad_max(m[0]);
+    m[1] = quad_max(m[1]);
+    float l[2] = {0.f, 0.f};
+#pragma unroll
+    for (int n = 0; n < kNT; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        s[n][e] = s[n][e] == -FLT_MAX ? 0.f : expf(s[n][e] - m[e >> 1]);
+        l[e >> 1] += s[n][e];
+      }
+    l[0] = quad_sum(l[0]);
+    l[1] = quad_sum(l[1]);
+    if (tig == 0) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int r = q0 + g + 8 * half;
+        if (r < S) a.lse[static_cast<size_t>(tr(r)) * a.heads + h] = m[half] + logf(l[half]);
+      }
+    }
+    const float inv[2] = {l[0] > 0.f ? 1.0f / l[0] : 0.f, l[1] > 0.f ? 1.0f / l[1] : 0.f};
+#pragma unroll
+    for (int n = 0; n < kNT; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[n][e] *= inv[e >> 1];
+#pragma unroll
+    for (int ks = 0; ks < 3; ++ks) {
+      if (ks < NW) {
+        uint32_t ah[4], al[4];
+        c_to_a(s[2 * ks], s[2 * ks + 1], 16384.f, ah, al);
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          uint32_t bh[4], bl[4];
+          ldsm4t(bh, bk_addr(Vh, 16 * ks, 16 * p, lane));
+          ldsm4t(bl, bk_addr(Vl, 16 * ks, 16 * p, lane));
+          mma3(o[2 * p], ah, al, bh[0], bh[1], bl[0], bl[1]);
+          mma3(o[2 * p + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+        }
+      }
+    }
+    const float fo = pow2f(-(14 + sm.scale[hl][2]));
+    float m0 = 0.f, m1 = 0.f;
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[n][e] *= fo;
+      m0 = fmaxf(m0, fmaxf(fabsf(o[n][0]), fabsf(o[n][1])));
+      m1 = fmaxf(m1, fmaxf(fabsf(o[n][2]), fabsf(o[n][3])));
+    }
+    // this head's row maxima into the block's (quad-reduced, one atomic per row)
+    m0 = quad_max(m0);
+    m1 = quad_max(m1);
+    if (tig == 0) {
+      if (q0 + g < S) atomicMax(&sm.rmax[q0 + g], __float_as_int(m0));
+      if (q0 + g + 8 < S) atomicMax(&sm.rmax[q0 + g + 8], __float_as_int(m1));
+    }
+  }
+  __syncthreads();  // the block's row maxima
+  if (act) strip_store(o, q0, S, tr, lane, nullptr, 0, h * kHd, &a.out_split, sm.rmax, blk, hl == 0);
+}
+
 // ---- backward --------------------------------------------------------------------
 // Scores and dP of a 16-row strip r0.. against all rows of the other block:
 // s = A1 B1^T, dp = A2 B2^T (A from [rows][32] blocks, B likewise).
@@ -857,6 +1019,14 @@ void launch_mma(const AttnArgs &a, bool bwd, cudaStream_t s) {
     smem = small ? sizeof(Smem48) : sizeof(Smem);
     threads = small ? kTh48 : kThreads;
     fn = small ? k_attn_bwd_mma48<kSplit> : k_attn_bwd_mma<kSplit>;
+  } else if (kSplit && small) {
+    // one CTA per (atom, 128-column block): no cluster
+    smem = sizeof(SmemFB);
+    CUDA_CHECK(cudaFuncSetAttribute(k_attn_fwd_mma_blk, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem)));
+    k_attn_fwd_mma_blk<<<dim3(a.n_atoms, a.heads / kBlkHeads), 32 * 3 * kBlkHeads, smem, s>>>(a);
+    CUDA_LAUNCH_CHECK();
+    return;
   } else {
     smem = small ? sizeof(SmemF<kMT>) : sizeof(SmemF<kMaxTok>);
     threads = small ? 2 * kMT : 2 * kMaxTok;
