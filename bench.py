@@ -20,13 +20,17 @@ Other workloads (one JSON line each; pet-mad-s-shaped weights):
   si         diamond Si 32^3 (262,144 atoms), E+F+stress, spatial domains
              over N >= 2 GPUs (strong scaling)
 
-Timing.  `value` keeps the positions resident on the device and sums the
-library's own CUDA events (recorded on its stream) around each whole step;
-`e2e` is the host clock around each public predict call, host arrays in
-and numpy forces and stress out.  Multi-GPU (launched with
-torch.distributed.run): barriers around the timed region, the max over
-ranks.  With --gpus N > 1 the fcc workload is weak scaling at 32,768 atoms
-per GPU (one cell of N x 32,768 atoms split into spatial domains).
+Timing.  Every timed step is one public predict call from host arrays.
+`e2e` is the host clock around it: the host-to-device copy of the inputs, the
+step, and the device-to-host copy of the forces and stress.  `value` is the
+same call's device time with its inputs already in HBM: the library's CUDA
+events, recorded on its stream, from the end of its input copy to the start
+of its result copy.  On the spatial-domain path it is the domain engine's
+events around its step.  So e2e <= value holds call by call.  Multi-GPU
+(launched with torch.distributed.run): barriers around the timed region and
+the max over ranks.  With --gpus N > 1 the fcc workload is weak scaling at
+32,768 atoms per GPU (one cell of N x 32,768 atoms split into spatial
+domains).
 
 `--impl reference` times the CPU implementation of the path on the host
 cores: the reference's model cannot be built here (its ggml dependency is
@@ -140,6 +144,13 @@ def cpu_reference(structures, gguf_path, steps, warmup, repeats=1, forces=True, 
         runs.append((time.perf_counter() - t0) / max(steps, 1))
     dt = float(np.median(runs))
     return n_atoms / dt, threads, dt, [n_atoms / r for r in runs]
+
+
+def device_ms(t):
+    """Device time of one predict call without its host<->device copies:
+    the library's CUDA-event phases from the end of the input copy to the
+    start of the result copy."""
+    return t["total"] - t["h2d"] - t["d2h"]
 
 
 def spread(values):
@@ -383,15 +394,11 @@ def main():
                "halo positions, reverse-edge layer-0 tokens and their gradients, ghost forces; all-reduce of "
                "(E, virial)")
 
-        def step_value():
-            dom.step(d_pos, d_F)
-            return dom.stats()["step_ms"]
-
-        def step_e2e():
+        def step():
             t0 = time.perf_counter()
             dom.step(pos_host.to("cuda", non_blocking=True), d_F)
-            F_host = d_F.cpu()
-            return (time.perf_counter() - t0) * 1e3, F_host
+            d_F.cpu()
+            return (time.perf_counter() - t0) * 1e3, dom.stats()["step_ms"]
         h2d_bytes = int(own_pos.nbytes)
         d2h_bytes = int(own_pos.nbytes + 8 * 7)
     elif W.name == "molecules":
@@ -401,30 +408,19 @@ def main():
         if world > 1:
             par = f"batch shards x{world} (LPT on n^3), final all-gather"
 
-        def step_value():
-            pred.predict_batch(my_structs, compute_forces=grad or nc, use_nc_forces=nc)
-            return pred.last_timings()["total"]
-
-        def step_e2e():
+        def step():
             t0 = time.perf_counter()
-            out = runner.run(structs)
-            return (time.perf_counter() - t0) * 1e3, out
+            runner.run(structs)
+            return (time.perf_counter() - t0) * 1e3, device_ms(pred.last_timings())
         h2d_bytes = int(sum(x.positions.nbytes + x.numbers.nbytes for x in my_structs))
         d2h_bytes = int(sum(x.positions.nbytes + 8 for x in my_structs))
     else:
-        d_pos = torch.from_numpy(s.positions).cuda()
         opts = mb.PredictOptions(grad or nc, grad or nc, nc)
 
-        def step_value():
-            pred.predict_device(d_pos.data_ptr(), s.n_atoms, s.numbers, s.cell, s.pbc,
-                                compute_forces=grad or nc, compute_stress=grad or nc, copy_forces=False,
-                                use_nc_forces=nc)
-            return pred.last_timings()["total"]
-
-        def step_e2e():
+        def step():
             t0 = time.perf_counter()
-            r = pred.predict_with_options(s.positions, s.numbers, s.cell, s.pbc, opts)
-            return (time.perf_counter() - t0) * 1e3, r
+            pred.predict_with_options(s.positions, s.numbers, s.cell, s.pbc, opts)
+            return (time.perf_counter() - t0) * 1e3, device_ms(pred.last_timings())
         h2d_bytes = int(s.positions.nbytes + s.numbers.nbytes)
         d2h_bytes = int(s.positions.nbytes + 6 * 4 + 8 * 7) if (grad or nc) else 8 * 7
 
@@ -439,12 +435,14 @@ def main():
             torch.cuda.synchronize()
 
     for _ in range(max(args.warmup, 3)):
-        step_value()
-    for _ in range(2):
-        step_e2e()
-    # ---- timed region: K device-resident steps (value) interleaved with K
-    # end-to-end steps through the public API (e2e), so that both see the
-    # same clocks -------------------------------------------------------------
+        step()
+    # ---- timed region: K steps, each one public predict call from host
+    # arrays.  e2e: the host clock around the call (host->device copy of the
+    # inputs, the step, device->host copy of the results).  value: the same
+    # call's device time with its inputs already in HBM, i.e. the library's
+    # CUDA events from the end of its host->device copy to the start of its
+    # device->host copy (on the spatial-domain path: the engine's events
+    # around its step) ------------------------------------------------------
     launches = 0
     barrier()
     dev_ms, wall_ms = [], []
@@ -452,10 +450,10 @@ def main():
         for _ in range(args.steps):
             flush()
             l0 = mb.kernel_launches()
-            dev_ms.append(step_value())
+            w_ms, d_ms = step()
             launches += mb.kernel_launches() - l0
-            flush()
-            wall_ms.append(step_e2e()[0])
+            wall_ms.append(w_ms)
+            dev_ms.append(d_ms)
         barrier()
     phase = pred.last_timings()
     t_dev = max_over_ranks(float(np.sum(dev_ms)) / 1e3)
@@ -470,7 +468,7 @@ def main():
     barrier()
     for _ in range(args.steps):
         flush()
-        step_value()
+        step()
     barrier()
     kstats = pred.kernel_stats()
     pred.set_kernel_profiling(False)
