@@ -12,7 +12,8 @@
 // or 128-row tiles whose accumulators live in tensor memory and whose
 // operands must be in shared memory, so every P and dS block would make a
 // round trip TMEM -> registers -> shared memory between products (measured:
-// 9.4 ms per forward against 6.1 ms for the SIMT kernel, attention_tc.cu).
+// 9.4 ms per forward against 6.1 ms for the SIMT kernel, in an earlier
+// tcgen05 forward kept in this repository's history).
 // Here the scores, P, dP and dS of a 16-row strip stay in the registers of
 // one warp, and the accumulator layout of one product is the operand layout
 // of the next.

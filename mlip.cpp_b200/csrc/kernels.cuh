@@ -102,10 +102,6 @@ __host__ __device__ inline AtomRows atom_rows(int atom, int e0, int edge_base) {
   return AtomRows{atom, edge_base + e0 - 1};
 }
 void attention_fwd(const AttnArgs &a, cudaStream_t stream);
-// Tensor-core forward (attention_tc.cu): head size 32, at most 64 tokens per
-// atom, heads a multiple of 4.  `err` (device int) is set if a wait times out.
-bool attention_tc_supported(const AttnArgs &a);
-void attention_fwd_tc(const AttnArgs &a, int *err, cudaStream_t stream);
 void attention_bwd(const AttnArgs &a, cudaStream_t stream);
 // Tensor-core forward / backward on register-resident split-fp16 products
 // (attention_mma.cu): head size 32, at most 64 tokens per atom; split

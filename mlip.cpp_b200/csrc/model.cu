@@ -370,7 +370,6 @@ void PETModel::load(const std::string &path, float cutoff_override) {
   use_f16_ = use_tc_ && !(g && std::string(g) == "tf32");
   {
     const char *at = std::getenv("MLIPCPP_B200_ATTN");
-    use_attn_tc_ = at && std::string(at) == "tc";
     use_attn_rows_ = at && (std::string(at) == "rows" || std::string(at) == "simt");
   }
   {
@@ -619,10 +618,8 @@ void PETModel::forward_backward(bool grad) {
   auto attn = [&](bool backward, const AttnArgs &x) {
     cudaEvent_t e0 = nullptr;
     if (kprof_) mark_begin(e0);
-    if (!use_attn_rows_ && !(use_attn_tc_ && !backward) && attention_mma_supported(x, backward))
-      attention_mma(x, backward, s);
+    if (!use_attn_rows_ && attention_mma_supported(x, backward)) attention_mma(x, backward, s);
     else if (backward) attention_bwd(x, s);
-    else if (use_attn_tc_ && attention_tc_supported(x)) attention_fwd_tc(x, d_err_.as<int>(), s);
     else attention_fwd(x, s);
     if (kprof_) mark_end(KC_ATTENTION, e0, 0.0, 4.0 * T * (backward ? 7.0 : 4.0) * d);
     (void)x;

@@ -164,9 +164,6 @@ class PETModel {
   size_t wspan_ = 0;     // floats between the three copies
   bool use_tc_ = true;   // tensor-core GEMMs (MLIPCPP_B200_GEMM=simt disables)
   bool use_f16_ = true;  // 3xFP16 where it applies (MLIPCPP_B200_GEMM=tf32 keeps 3xTF32)
-  // tensor-core attention forward (MLIPCPP_B200_ATTN=tc): correct, but slower
-  // than the SIMT kernel at this size (see attention_tc.cu)
-  bool use_attn_tc_ = false;
   // attention kernels: forward and backward on the tensor-core kernels of
   // attention_mma.cu where they apply (head size 32, up to 64 tokens), else
   // on the SIMT kernels; MLIPCPP_B200_ATTN=rows (or simt): SIMT for both

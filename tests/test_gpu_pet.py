@@ -190,19 +190,6 @@ def test_gpu_tensor_core_matches_simt(mode, model_file, monkeypatch):
     assert_close(tc, simt.energy, simt.forces, simt.stress, s.n_atoms)
 
 
-def test_gpu_tensor_core_attention_matches_simt(model_file, monkeypatch):
-    """The tcgen05 attention forward and the SIMT attention agree within the
-    fp32 parity tolerances on the same inputs (including an odd atom count,
-    whose last CTA has one atom)."""
-    path = model_file("pet-oam-l", 9)
-    s = wl.fcc_alloy(3, seed=9)  # 27 atoms
-    monkeypatch.setenv("MLIPCPP_B200_ATTN", "simt")
-    ref = mb.Predictor(path).predict(s.positions, s.numbers, s.cell, compute_stress=True)
-    monkeypatch.setenv("MLIPCPP_B200_ATTN", "tc")
-    res = mb.Predictor(path).predict(s.positions, s.numbers, s.cell, compute_stress=True)
-    assert_close(res, ref.energy, ref.forces, ref.stress, s.n_atoms)
-
-
 @pytest.mark.parametrize("hname,make,env", [
     ("pet-oam-l", lambda: [wl.fcc_alloy(6, seed=14)], {}),                       # split outputs, clusters of 4
     ("pet-mad-s", lambda: [wl.water_box(192, seed=14)], {}),                     # split outputs
