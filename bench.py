@@ -16,7 +16,8 @@ Other workloads (one JSON line each; pet-mad-s-shaped weights):
   si216      diamond Si 3x3x3 (216 atoms), E+F+stress
   water      liquid water, 4,096 atoms, E+F+stress
   molecules  512 non-periodic molecules of 10-60 atoms, E+F, one batched
-             call (structures sharded over the ranks for N > 1)
+             call on the packed batch (predict_packed; structures sharded
+             over the ranks for N > 1)
   si         diamond Si 32^3 (262,144 atoms), E+F+stress, spatial domains
              over N >= 2 GPUs (strong scaling)
 
@@ -404,13 +405,16 @@ def main():
     elif W.name == "molecules":
         mine = sh.shard([sh.structure_cost(x.n_atoms) for x in structs], world)[rank]
         my_structs = [structs[i] for i in mine]
-        runner = sh.BatchRunner(sh.predictor_batch_eval(pred, compute_forces=grad or nc), world=world, rank=rank)
+        # the batch as a data loader holds it: one packed block of host arrays
+        batch = sh.PackedBatch.pack(structs)
+        runner = sh.PackedBatchRunner(sh.predictor_packed_eval(pred, compute_forces=grad or nc), world=world,
+                                      rank=rank)
         if world > 1:
             par = f"batch shards x{world} (LPT on n^3), final all-gather"
 
         def step():
             t0 = time.perf_counter()
-            runner.run(structs)
+            runner.run(batch)
             return (time.perf_counter() - t0) * 1e3, device_ms(pred.last_timings())
         h2d_bytes = int(sum(x.positions.nbytes + x.numbers.nbytes for x in my_structs))
         d2h_bytes = int(sum(x.positions.nbytes + 8 for x in my_structs))

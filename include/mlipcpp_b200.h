@@ -25,6 +25,22 @@ mlipcpp_error_t mlipcpp_predict_batch(mlipcpp_model_t model, int32_t n_systems,
                                       const mlipcpp_predict_options_t *options,
                                       mlipcpp_result_t *results);
 
+/* The same batch from packed arrays, with the results written straight into
+ * the caller's arrays (no result handles), for callers that hold many
+ * structures as one block (data loaders, screening loops).  Structure k has
+ * n_atoms[k] > 0 atoms; its positions ([3 n_atoms[k]] float) and atomic
+ * numbers follow those of structure k - 1 in `positions` and `numbers`.
+ * cells: [9 n_systems] row-major lattices, or NULL when every structure is
+ * non-periodic; pbc: [3 n_systems], or NULL for periodic along all axes when
+ * cells are given.  Out: energies [n_systems]; forces [3 sum n_atoms] (NULL:
+ * not copied out); stress [6 n_systems], Voigt (NULL: not copied out).
+ * Outputs the options do not ask for, and stress of a non-periodic
+ * structure, are written as zeros. */
+mlipcpp_error_t mlipcpp_b200_predict_packed(mlipcpp_model_t model, int32_t n_systems, const int32_t *n_atoms,
+                                            const float *positions, const int32_t *numbers, const float *cells,
+                                            const bool *pbc, const mlipcpp_predict_options_t *options,
+                                            float *energies, float *forces, float *stress);
+
 /* Predict one structure whose positions are already in device memory
  * (d_positions: device pointer to [3n] float).  atomic_numbers, cell and pbc
  * are host pointers.  Forces are copied back only when copy_forces is true.

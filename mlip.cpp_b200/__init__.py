@@ -95,6 +95,7 @@ def lib() -> ctypes.CDLL:
         "mlipcpp_result_has_stress": (ctypes.c_int, [vp, vp]),
         "mlipcpp_result_free": (None, [vp]),
         "mlipcpp_predict_batch": (ctypes.c_int, [vp, i32, vp, vp, vp]),
+        "mlipcpp_b200_predict_packed": (ctypes.c_int, [vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
         "mlipcpp_b200_predict_device": (ctypes.c_int, [vp, i32, vp, vp, vp, vp, vp, b, vp]),
         "mlipcpp_b200_predict_device_forces": (ctypes.c_int, [vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
         "mlipcpp_b200_set_timing": (ctypes.c_int, [vp, b]),
@@ -206,6 +207,15 @@ class Result:
 
     def has_stress(self) -> bool:
         return self._has_stress
+
+
+@dataclass
+class PackedResult:
+    """Results of Predictor.predict_packed: energies [n_systems], forces
+    [sum n, 3] in the input's packed order, stress [n_systems, 6] (Voigt)."""
+    energies: np.ndarray
+    forces: np.ndarray | None = None
+    stress: np.ndarray | None = None
 
 
 def _read_result(handle, n_atoms: int, free: bool = True) -> Result:
@@ -359,6 +369,32 @@ class Predictor:
         po = _PredictOptions(compute_forces or compute_stress, compute_stress, use_nc_forces)
         _check(lib().mlipcpp_predict_batch(self._h, n, arr, ctypes.byref(po), handles))
         return [_read_result(handles[k], ns[k]) for k in range(n)]
+
+    def predict_packed(self, positions, numbers, n_atoms, cells=None, pbc=None, compute_forces=True,
+                       compute_stress=False, use_nc_forces=False) -> "PackedResult":
+        """Batched prediction from packed arrays (mlipcpp_b200_predict_packed):
+        structure k is the next n_atoms[k] rows of `positions` [sum n, 3] and
+        entries of `numbers`; `cells` [n_systems, 3, 3] (None: all
+        non-periodic) and `pbc` [n_systems, 3].  Returns energies
+        [n_systems], forces [sum n, 3] (None unless compute_forces) and
+        stress [n_systems, 6] (None unless compute_stress) in one call,
+        without a result object per structure."""
+        counts = np.ascontiguousarray(n_atoms, np.int32).reshape(-1)
+        pos = np.ascontiguousarray(positions, np.float32).reshape(-1, 3)
+        z = np.ascontiguousarray(numbers, np.int32).reshape(-1)
+        ns = counts.shape[0]
+        if z.shape[0] != pos.shape[0] or int(counts.sum(dtype=np.int64)) != pos.shape[0]:
+            raise RuntimeError("positions, numbers and n_atoms do not describe the same atoms")
+        c = None if cells is None else np.ascontiguousarray(cells, np.float32).reshape(ns, 9)
+        p = None if pbc is None else np.ascontiguousarray(pbc, np.bool_).reshape(ns, 3)
+        e = np.empty(ns, np.float32)
+        f = np.empty((pos.shape[0], 3), np.float32) if compute_forces else None
+        st = np.empty((ns, 6), np.float32) if compute_stress else None
+        po = _PredictOptions(compute_forces, compute_stress, use_nc_forces)
+        ptr = lambda a: None if a is None else a.ctypes.data  # noqa: E731
+        _check(lib().mlipcpp_b200_predict_packed(self._h, ns, counts.ctypes.data, pos.ctypes.data, z.ctypes.data,
+                                                 ptr(c), ptr(p), ctypes.byref(po), e.ctypes.data, ptr(f), ptr(st)))
+        return PackedResult(e, f, st)
 
     def predict_device(self, d_positions: int, n_atoms: int, atomic_numbers, cell=None, pbc=None,
                        compute_forces=True, compute_stress=False, copy_forces=True,

@@ -509,6 +509,71 @@ mlipcpp_error_t mlipcpp_predict_batch(mlipcpp_model_t model, int32_t n_systems,
   }
 }
 
+mlipcpp_error_t mlipcpp_b200_predict_packed(mlipcpp_model_t model, int32_t n_systems, const int32_t *n_atoms,
+                                            const float *positions, const int32_t *numbers, const float *cells,
+                                            const bool *pbc, const mlipcpp_predict_options_t *options,
+                                            float *energies, float *forces, float *stress) {
+  if (auto e = check_model(model)) return e;
+  if (n_systems < 0) {
+    set_error("Invalid number of systems");
+    return MLIPCPP_ERROR_INVALID_PARAMETER;
+  }
+  if (n_systems > 0 && (!n_atoms || !positions || !numbers || !energies)) {
+    set_error("NULL n_atoms, positions, atomic_numbers or energies pointer");
+    return MLIPCPP_ERROR_NULL_POINTER;
+  }
+  mlipcpp_predict_options_t dflt;
+  if (!options) {
+    mlipcpp_predict_options_default(&dflt);
+    options = &dflt;
+  }
+  std::vector<pet::SystemView> v(static_cast<size_t>(n_systems));
+  std::vector<int64_t> first(static_cast<size_t>(n_systems) + 1, 0);
+  for (int k = 0; k < n_systems; ++k) {
+    if (n_atoms[k] <= 0) {
+      set_error("Invalid number of atoms");
+      return MLIPCPP_ERROR_INVALID_PARAMETER;
+    }
+    pet::SystemView &s = v[k];
+    s.n_atoms = n_atoms[k];
+    s.positions = positions + 3 * first[k];
+    s.numbers = numbers + first[k];
+    if (cells) {
+      s.cell = cells + 9 * static_cast<size_t>(k);
+      if (pbc)
+        for (int c = 0; c < 3; ++c) s.pbc[c] = pbc[3 * static_cast<size_t>(k) + c];
+    }
+    first[k + 1] = first[k] + n_atoms[k];
+  }
+  try {
+    const bool grad = (options->compute_forces || options->compute_stress) && !options->use_nc_forces;
+    auto out = model->model->predict(v, grad, options->use_nc_forces);
+    for (int k = 0; k < n_systems; ++k) {
+      pet::Result &r = out[k];
+      finish_options(r, *options);
+      energies[k] = r.energy;
+      if (forces) {
+        float *f = forces + 3 * first[k];
+        const size_t n3 = 3 * static_cast<size_t>(n_atoms[k]);
+        if (r.has_forces && r.forces.size() == n3) std::memcpy(f, r.forces.data(), sizeof(float) * n3);
+        else std::memset(f, 0, sizeof(float) * n3);
+      }
+      if (stress) {
+        float *st = stress + 6 * static_cast<size_t>(k);
+        if (r.has_stress && r.stress.size() == 6) std::memcpy(st, r.stress.data(), sizeof(float) * 6);
+        else std::memset(st, 0, sizeof(float) * 6);
+      }
+    }
+    clear_error();
+    return MLIPCPP_OK;
+  } catch (const std::exception &e) {
+    return map_exception(e, "Prediction failed: ", MLIPCPP_ERROR_COMPUTATION);
+  } catch (...) {
+    set_error("Prediction failed: unknown error");
+    return MLIPCPP_ERROR_INTERNAL;
+  }
+}
+
 mlipcpp_error_t mlipcpp_b200_predict_device(mlipcpp_model_t model, int32_t n_atoms, const float *d_positions,
                                             const int32_t *atomic_numbers, const float *cell, const bool *pbc,
                                             const mlipcpp_predict_options_t *options, bool copy_forces,

@@ -1497,6 +1497,8 @@ bool gemm_f16_supported(const GemmArgs &a) {
 
 void inject_gemm_stall() { g_gemm_stall.store(true); }
 
+bool gemm_stall_armed() { return g_gemm_stall.load(); }
+
 void set_gemm_wait_bound_ns(uint64_t ns) {
   const uint64_t v = ns ? ns : tc::kWaitNs;
   CUDA_CHECK(cudaMemcpyToSymbol(tc::g_wait_ns, &v, sizeof(v)));

@@ -53,6 +53,7 @@ void gemm_3xf16(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t 
 // drains its own copies and MMAs and frees its TMEM).  set_gemm_wait_bound_ns:
 // the bound of the GEMM kernels' waits on the current device (0: 1 s).
 void inject_gemm_stall();
+bool gemm_stall_armed();
 void set_gemm_wait_bound_ns(uint64_t ns);
 
 // Power-of-two scale exponent s with max|x| 2^s in [2^14, 2^15) (0 for an

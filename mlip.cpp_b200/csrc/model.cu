@@ -124,6 +124,7 @@ PETModel::PETModel() : in_(new Internals()) {
 }
 
 PETModel::~PETModel() {
+  if (gexec_) cudaGraphExecDestroy(gexec_);
   for (auto &e : ev_)
     if (e) cudaEventDestroy(e);
   for (auto &e : ev_pool_) cudaEventDestroy(e);
@@ -365,6 +366,10 @@ void PETModel::load(const std::string &path, float cutoff_override) {
     off += (kv.second.size() * 4 + 255) / 256 * 256;
   }
   CUDA_CHECK(cudaMemcpy(wbuf_.ptr, staging.data(), 4 * total, cudaMemcpyHostToDevice));
+  {
+    const char *gr = std::getenv("MLIPCPP_B200_GRAPH");
+    use_graph_ = !(gr && std::string(gr) == "0");
+  }
   const char *g = std::getenv("MLIPCPP_B200_GEMM");
   use_tc_ = !(g && std::string(g) == "simt");
   use_f16_ = use_tc_ && !(g && std::string(g) == "tf32");
@@ -753,7 +758,7 @@ void PETModel::forward_backward(bool grad) {
                  p == 0 ? a.ncF : a.ncS, N1, r, p == 0 ? 3 : 9, s);
     }
   }
-  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[4], s));
+  if (timing_) record_phase(4);
   if (!grad) return;
 
   // ---- backward ----------------------------------------------------------
@@ -854,12 +859,97 @@ void PETModel::forward_backward(bool grad) {
   }
   if (n_local_ > Nl_[0]) CUDA_CHECK(cudaMemsetAsync(a.F, 0, sizeof(float) * 3 * n_local_, s));
   forces(a.g, offset, nl_.nbr.as<int>(), a.rev, a.F, Nl_[0], E0, s);
-  if (timing_) CUDA_CHECK(cudaEventRecord(ev_[5], s));
+  if (timing_) record_phase(5);
 }
 
 // ---------------------------------------------------------------------------
 // Prediction
 // ---------------------------------------------------------------------------
+// Everything the launches of forward_backward depend on: shapes, modes and
+// the addresses of every buffer they touch.  Equal keys launch identical
+// work, so a graph captured under one key replays for the next.
+std::vector<uintptr_t> PETModel::graph_key(bool grad) const {
+  auto p = [](const void *x) { return reinterpret_cast<uintptr_t>(x); };
+  return {static_cast<uintptr_t>(n_local_), static_cast<uintptr_t>(Nl_[0]), static_cast<uintptr_t>(Nl_[1]),
+          static_cast<uintptr_t>(El_[0]), static_cast<uintptr_t>(El_[1]), static_cast<uintptr_t>(max_tok_),
+          (grad ? 1u : 0u) | (ncf_ ? 2u : 0u) | (ncs_ ? 4u : 0u) | (chain_ ? 8u : 0u) | (reduced_ ? 16u : 0u) |
+              (timing_ ? 32u : 0u),
+          p(persist_.ptr), p(scratch_.ptr), p(sp_[0].ptr), p(sp_[1].ptr), p(sp_[2].ptr), p(wbuf_.ptr),
+          p(nl_.offset.ptr), p(nl_.center.ptr), p(nl_.nbr.ptr), p(nl_.shift.ptr), p(nl_.vec.ptr), p(nl_.dist.ptr),
+          p(species_), p(d_err_.ptr)};
+}
+
+// Phase boundary i of the step's timing.  Inside a capture the record
+// becomes a node of the graph, so that each replay records the event.
+void PETModel::record_phase(int i) {
+  if (capturing_) CUDA_CHECK(cudaEventRecordWithFlags(ev_[i], stream_, cudaEventRecordExternal));
+  else CUDA_CHECK(cudaEventRecord(ev_[i], stream_));
+}
+
+// forward_backward is about 110 launches.  For small structures their
+// launch latency is a large part of a step, so when a prediction has the
+// same key as the one before it (the same shapes in the same buffers, as
+// when a structure is evaluated again or strained in place), the launches
+// are captured once into a CUDA graph and replayed from then on.  A first
+// or changed key runs eagerly, so one-off shapes pay no capture.  Kernel
+// profiling, the domain path's exchanges and an armed failure-test stall
+// always run eagerly.  If the capture fails, graphs are switched off for
+// this model and the step runs eagerly.
+void PETModel::run_forward_backward(bool grad) {
+  if (!use_graph_ || kprof_ || rm_ || gemm_stall_armed()) {
+    forward_backward(grad);
+    return;
+  }
+  std::vector<uintptr_t> key = graph_key(grad);
+  if (gexec_ && key == gkey_) {
+    CUDA_CHECK(cudaGraphLaunch(gexec_, stream_));
+    g_kernel_launches.fetch_add(graph_kernels_, std::memory_order_relaxed);
+    return;
+  }
+  if (key != last_key_) {
+    last_key_ = std::move(key);
+    forward_backward(grad);
+    return;
+  }
+  const long long k0 = g_kernel_launches.load();
+  cudaGraph_t graph = nullptr;
+  CUDA_CHECK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+  capturing_ = true;
+  try {
+    forward_backward(grad);
+    capturing_ = false;
+  } catch (...) {
+    capturing_ = false;
+    cudaStreamEndCapture(stream_, &graph);
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    use_graph_ = false;
+    forward_backward(grad);
+    return;
+  }
+  if (cudaStreamEndCapture(stream_, &graph) != cudaSuccess || !graph) {
+    cudaGetLastError();
+    use_graph_ = false;
+    forward_backward(grad);
+    return;
+  }
+  graph_kernels_ = g_kernel_launches.load() - k0;
+  bool updated = false;
+  if (gexec_) {
+    cudaGraphExecUpdateResultInfo info;
+    updated = cudaGraphExecUpdate(gexec_, graph, &info) == cudaSuccess;
+    if (!updated) {
+      cudaGetLastError();
+      cudaGraphExecDestroy(gexec_);
+      gexec_ = nullptr;
+    }
+  }
+  if (!updated) CUDA_CHECK(cudaGraphInstantiate(&gexec_, graph, 0));
+  cudaGraphDestroy(graph);
+  gkey_ = last_key_;
+  CUDA_CHECK(cudaGraphLaunch(gexec_, stream_));
+}
+
 void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const int *d_species, bool grad, int n_in) {
   n_local_ = n_local;
   Nl_[0] = N0; El_[0] = E0; Tl_[0] = N0 + E0;
@@ -1025,7 +1115,7 @@ void PETModel::run_group(const float *d_pos, int n_atoms, const std::vector<cons
   const Acts &a = in_->a;
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[3], s));
 
-  forward_backward(grad);
+  run_forward_backward(grad);
 
   // per-system energy and virial in f64 (pet.cpp:542-548, 1041-1077); then
   // the per-system Voigt sums of the non-conservative stress

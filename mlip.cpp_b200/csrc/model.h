@@ -151,6 +151,11 @@ class PETModel {
                  const std::vector<int> &atom_begin, bool compute_grad,
                  std::vector<Result *> &results, bool copy_forces, bool nc);
   void forward_backward(bool compute_grad);
+  // forward_backward through a CUDA graph when the same shapes and buffers
+  // come back (see model.cu)
+  void run_forward_backward(bool compute_grad);
+  std::vector<uintptr_t> graph_key(bool compute_grad) const;
+  void record_phase(int i);
   void setup_graph(int n_local, int N0, int E0, int N1, int E1, const int *d_species, bool grad, int n_in = 0);
   void read_times(bool grad);
   const float *w(const std::string &name) const;
@@ -202,6 +207,14 @@ class PETModel {
   // per-call device state
   DevBuf d_pos_, d_species_, d_sys_begin_, d_sys_end_, d_sys_atoms_, d_zmap_;
   RemoteMessages *rm_ = nullptr;  // set during domain_predict
+  // CUDA graph of forward_backward (MLIPCPP_B200_GRAPH=0 disables): the key
+  // of the last prediction, the key and executable of the captured graph,
+  // and the kernels it launches (added to the launch counter on replay)
+  bool use_graph_ = true;
+  std::vector<uintptr_t> last_key_, gkey_;
+  cudaGraphExec_t gexec_ = nullptr;
+  long long graph_kernels_ = 0;
+  bool capturing_ = false;
   const int *species_ = nullptr;  // species index of every local atom (device), set by setup_graph
   EdgeList nl_;
   NLScratch nls_;

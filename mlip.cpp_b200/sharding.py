@@ -76,3 +76,132 @@ def predictor_batch_eval(predictor, compute_forces: bool = True, compute_stress:
         return [(r.energy, r.forces if r.has_forces() else np.zeros((0, 3), np.float32),
                  r.stress if r.has_stress() else None) for r in res]
     return run
+
+
+class PackedBatch:
+    """A batch of structures held as one block: the positions [sum n, 3] and
+    atomic numbers [sum n] of structure k follow those of structure k - 1;
+    n_atoms [n_systems]; cells [n_systems, 9] and pbc [n_systems, 3], or
+    None for non-periodic structures.  The layout of
+    Predictor.predict_packed."""
+
+    def __init__(self, positions, numbers, n_atoms, cells=None, pbc=None):
+        self.positions = np.ascontiguousarray(positions, np.float32).reshape(-1, 3)
+        self.numbers = np.ascontiguousarray(numbers, np.int32).reshape(-1)
+        self.n_atoms = np.ascontiguousarray(n_atoms, np.int32).reshape(-1)
+        ns = self.n_atoms.shape[0]
+        self.cells = None if cells is None else np.ascontiguousarray(cells, np.float32).reshape(ns, 9)
+        self.pbc = None if pbc is None else np.ascontiguousarray(pbc, np.bool_).reshape(ns, 3)
+        self.first = np.zeros(ns + 1, np.int64)
+        np.cumsum(self.n_atoms, out=self.first[1:])
+        if self.first[-1] != self.positions.shape[0] or self.numbers.shape[0] != self.positions.shape[0]:
+            raise ValueError("positions, numbers and n_atoms do not describe the same atoms")
+
+    @classmethod
+    def pack(cls, structs) -> "PackedBatch":
+        """From objects with positions, numbers and (optional) cell / pbc."""
+        structs = list(structs)
+        cells = [getattr(s, "cell", None) for s in structs]
+        periodic = any(c is not None for c in cells)
+        if periodic and any(c is None for c in cells):
+            raise ValueError("a packed batch is either all periodic or all non-periodic")
+        pbc = None
+        if periodic:
+            pbc = [getattr(s, "pbc", None) for s in structs]
+            pbc = [[True] * 3 if p is None else list(p) for p in pbc]
+        return cls(np.concatenate([np.asarray(s.positions, np.float32).reshape(-1, 3) for s in structs]),
+                   np.concatenate([np.asarray(s.numbers, np.int32).reshape(-1) for s in structs]),
+                   [len(s.numbers) for s in structs],
+                   None if not periodic else np.stack([np.asarray(c, np.float32).reshape(9) for c in cells]),
+                   pbc)
+
+    def __len__(self) -> int:
+        return int(self.n_atoms.shape[0])
+
+    def structures(self) -> list:
+        """The structures one by one (views with positions, numbers, n_atoms,
+        cell and pbc)."""
+        from types import SimpleNamespace
+        out = []
+        for k in range(len(self)):
+            a, b = int(self.first[k]), int(self.first[k + 1])
+            out.append(SimpleNamespace(positions=self.positions[a:b], numbers=self.numbers[a:b], n_atoms=b - a,
+                                       cell=None if self.cells is None else self.cells[k].reshape(3, 3),
+                                       pbc=None if self.pbc is None else self.pbc[k]))
+        return out
+
+    def atom_index(self, idx) -> np.ndarray:
+        """Rows of the atoms of structures `idx`, in that order."""
+        idx = np.asarray(idx, np.int64)
+        n = self.n_atoms[idx].astype(np.int64)
+        starts = np.repeat(self.first[idx] - np.concatenate([[0], np.cumsum(n)[:-1]]), n)
+        return starts + np.arange(int(n.sum()), dtype=np.int64)
+
+    def take(self, idx) -> "PackedBatch":
+        """The structures `idx`, in that order, as a batch of their own."""
+        idx = np.asarray(idx, np.int64)
+        if idx.shape[0] == len(self) and np.array_equal(idx, np.arange(len(self))):
+            return self
+        rows = self.atom_index(idx)
+        return PackedBatch(self.positions[rows], self.numbers[rows], self.n_atoms[idx],
+                           None if self.cells is None else self.cells[idx],
+                           None if self.pbc is None else self.pbc[idx])
+
+
+class PackedBatchRunner:
+    """BatchRunner for packed batches: each rank evaluates its share with
+    one call and the ranks exchange one set of arrays each, so nothing in the
+    step is done per structure in Python.
+
+    `evaluate(PackedBatch) -> (energies [n], forces [sum n, 3] or None,
+    stress [n, 6] or None)` (for the GPU library:
+    ``predictor_packed_eval(predictor)``).  `run` returns the same triple for
+    the whole batch, in input order, on every rank."""
+
+    def __init__(self, evaluate, world: int = 1, rank: int = 0, group=None):
+        self.evaluate = evaluate
+        self.world, self.rank, self.group = world, rank, group
+        self._parts = None
+
+    def run(self, batch: PackedBatch, costs=None):
+        if self.world == 1:
+            return self.evaluate(batch)
+        if costs is None:  # the split depends only on the sizes: kept while they repeat
+            key = batch.n_atoms.tobytes()
+            if self._parts is None or self._parts[0] != key:
+                self._parts = (key, shard([structure_cost(int(n)) for n in batch.n_atoms], self.world))
+            parts = self._parts[1]
+        else:
+            parts = shard(costs, self.world)
+        mine = parts[self.rank]
+        local = self.evaluate(batch.take(mine)) if mine else (np.zeros(0, np.float32), None, None)
+        import torch.distributed as dist
+        gathered = [None] * self.world
+        dist.all_gather_object(gathered, (mine,) + tuple(local), group=self.group)
+        e = f = st = None
+        for idx, pe, pf, ps in gathered:
+            if not idx:
+                continue
+            if e is None:
+                e = np.zeros(len(batch), np.asarray(pe).dtype)
+            e[idx] = pe
+            if pf is not None:
+                if f is None:
+                    f = np.zeros_like(batch.positions)
+                f[batch.atom_index(idx)] = pf
+            if ps is not None:
+                if st is None:
+                    st = np.zeros((len(batch), 6), np.float32)
+                st[idx] = ps
+        return e, f, st
+
+
+def predictor_packed_eval(predictor, compute_forces: bool = True, compute_stress: bool = False):
+    """Rank-local packed evaluator backed by the GPU library's
+    Predictor.predict_packed."""
+
+    def run(batch: PackedBatch):
+        r = predictor.predict_packed(batch.positions, batch.numbers, batch.n_atoms, batch.cells, batch.pbc,
+                                     compute_forces=compute_forces, compute_stress=compute_stress)
+        return r.energies, r.forces, r.stress
+    return run

@@ -61,6 +61,97 @@ def test_two_gloo_ranks_match_one_process(model_file, tmp_path):
         np.testing.assert_allclose(r[f"f{i}"], x["forces"], rtol=0, atol=1e-9)
 
 
+def test_packed_batch_layout():
+    mols = wl.molecules(9, n_min=4, n_max=14, seed=3)
+    b = sh.PackedBatch.pack(mols)
+    assert len(b) == 9 and b.first[-1] == sum(m.n_atoms for m in mols)
+    for k, m in enumerate(b.structures()):
+        np.testing.assert_array_equal(m.positions, mols[k].positions)
+        np.testing.assert_array_equal(m.numbers, mols[k].numbers)
+    idx = [7, 2, 5]
+    sub = b.take(idx)
+    np.testing.assert_array_equal(sub.n_atoms, [mols[i].n_atoms for i in idx])
+    np.testing.assert_array_equal(sub.positions, np.concatenate([mols[i].positions for i in idx]))
+    np.testing.assert_array_equal(b.positions[b.atom_index(idx)], sub.positions)
+    assert b.take(range(9)) is b
+    cells = [wl.si_diamond(1, seed=s) for s in (1, 2)]
+    pc = sh.PackedBatch.pack(cells)
+    assert pc.cells.shape == (2, 9) and pc.pbc.all()
+    with pytest.raises(ValueError):
+        sh.PackedBatch.pack([mols[0], cells[0]])
+
+
+def oracle_packed_eval(orc):
+    def run(batch):
+        res = orc.predict(batch.structures())
+        return (np.array([r["energy_f64"] for r in res]),
+                np.concatenate([np.asarray(r["forces"]) for r in res]), None)
+    return run
+
+
+def _rank_packed(rank, world, port, path, out):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    orc = po.load_oracle(path, torch.float64)
+    b = sh.PackedBatch.pack(wl.molecules(12, n_min=4, n_max=14, seed=5))
+    e, f, st = sh.PackedBatchRunner(oracle_packed_eval(orc), world=world, rank=rank).run(b)
+    assert st is None
+    if rank == 0:
+        np.savez(out, e=e, f=f)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_packed_match_one_process(model_file, tmp_path):
+    import torch.multiprocessing as mp
+    path = model_file("tiny", 11, cutoff=3.0, cutoff_width=0.5)
+    mols = wl.molecules(12, n_min=4, n_max=14, seed=5)
+    ref = po.load_oracle(path, torch.float64).predict(mols)
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        port = sock.getsockname()[1]
+    out = str(tmp_path / "p.npz")
+    mp.start_processes(_rank_packed, args=(2, port, path, out), nprocs=2, start_method="spawn")
+    r = np.load(out)
+    np.testing.assert_allclose(r["e"], [x["energy_f64"] for x in ref], rtol=0, atol=1e-9)
+    np.testing.assert_allclose(r["f"], np.concatenate([x["forces"] for x in ref]), rtol=0, atol=1e-9)
+
+
+@pytest.mark.gpu
+def test_gpu_packed_batch_matches_batch(model_file):
+    """predict_packed equals predict_batch (same kernels, same grouping),
+    for molecules and for periodic cells, and the packed runner's one-rank
+    path is the same call."""
+    import mlipcpp_b200 as mb
+    pred = mb.Predictor(model_file("pet-mad-s", 12))
+    mols = wl.molecules(40, seed=13)
+    whole = pred.predict_batch(mols)
+    b = sh.PackedBatch.pack(mols)
+    r = pred.predict_packed(b.positions, b.numbers, b.n_atoms)
+    assert r.stress is None
+    for k, w in enumerate(whole):
+        assert r.energies[k] == np.float32(w.energy)
+        np.testing.assert_array_equal(r.forces[b.first[k]:b.first[k + 1]], w.forces)
+    e, f, _ = sh.PackedBatchRunner(sh.predictor_packed_eval(pred)).run(b)
+    np.testing.assert_array_equal(e, r.energies)
+    np.testing.assert_array_equal(f, r.forces)
+    cells = [wl.si_diamond(2, seed=s) for s in (1, 2)]
+    pc = sh.PackedBatch.pack(cells)
+    rp = pred.predict_packed(pc.positions, pc.numbers, pc.n_atoms, pc.cells, pc.pbc, compute_stress=True)
+    for k, c in enumerate(cells):
+        one = pred.predict(c.positions, c.numbers, c.cell, compute_stress=True)
+        assert rp.energies[k] == np.float32(one.energy)
+        np.testing.assert_array_equal(rp.forces[pc.first[k]:pc.first[k + 1]], one.forces)
+        np.testing.assert_array_equal(rp.stress[k], one.stress)
+    # energy only: forces not asked for, not returned
+    eo = pred.predict_packed(b.positions, b.numbers, b.n_atoms, compute_forces=False)
+    assert eo.forces is None and eo.energies.shape == (40,)
+    with pytest.raises(mb.MLIPError) as ei:
+        pred.predict_packed(b.positions[:3], b.numbers[:3], [3, 0])
+    assert ei.value.code == mb.INVALID_PARAMETER
+
+
 @pytest.mark.gpu
 def test_gpu_sharded_batch_matches_one_batch(model_file):
     """Two shards evaluated one after the other with the GPU library give
