@@ -156,7 +156,10 @@ class PackedBatchRunner:
     `evaluate(PackedBatch) -> (energies [n], forces [sum n, 3] or None,
     stress [n, 6] or None)` (for the GPU library:
     ``predictor_packed_eval(predictor)``).  `run` returns the same triple for
-    the whole batch, in input order, on every rank."""
+    the whole batch, in input order, on every rank; over several ranks the
+    energies come back as float64 and forces and stress in the evaluator's
+    dtype.  The results cross the process group in one all-gather (device
+    tensors over NCCL, host tensors over gloo)."""
 
     def __init__(self, evaluate, world: int = 1, rank: int = 0, group=None):
         self.evaluate = evaluate
@@ -174,26 +177,47 @@ class PackedBatchRunner:
         else:
             parts = shard(costs, self.world)
         mine = parts[self.rank]
-        local = self.evaluate(batch.take(mine)) if mine else (np.zeros(0, np.float32), None, None)
+        e, f, st = self.evaluate(batch.take(mine)) if mine else (None, None, None)
+        # Every rank knows every share, so each sends one float64 row of a
+        # fixed width: [forces itemsize, stress itemsize | energies | stress
+        # | forces], padded to the largest share; one all-gather moves them.
+        n_s = [len(p) for p in parts]
+        n_a = [int(batch.n_atoms[p].sum()) if p else 0 for p in parts]
+        width = max(2 + 7 * ns + 3 * na for ns, na in zip(n_s, n_a))
+        row = np.zeros(width, np.float64)
+        k, na = len(mine), n_a[self.rank]
+        if mine:
+            row[0] = 0 if f is None else np.asarray(f).dtype.itemsize
+            row[1] = 0 if st is None else np.asarray(st).dtype.itemsize
+            row[2:2 + k] = e
+            if st is not None:
+                row[2 + k:2 + 7 * k] = np.asarray(st).reshape(-1)
+            if f is not None:
+                row[2 + 7 * k:2 + 7 * k + 3 * na] = np.asarray(f).reshape(-1)
+        import torch
         import torch.distributed as dist
-        gathered = [None] * self.world
-        dist.all_gather_object(gathered, (mine,) + tuple(local), group=self.group)
-        e = f = st = None
-        for idx, pe, pf, ps in gathered:
-            if not idx:
+        dev = (torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(self.group) == "nccl"
+               else torch.device("cpu"))
+        send = torch.from_numpy(row).to(dev)
+        recv = [torch.empty_like(send) for _ in range(self.world)]
+        dist.all_gather(recv, send, group=self.group)
+        rows = torch.stack(recv).cpu().numpy()
+        e_all = np.zeros(len(batch), np.float64)
+        f_all = st_all = None
+        for r, p in enumerate(parts):
+            if not p:
                 continue
-            if e is None:
-                e = np.zeros(len(batch), np.asarray(pe).dtype)
-            e[idx] = pe
-            if pf is not None:
-                if f is None:
-                    f = np.zeros_like(batch.positions)
-                f[batch.atom_index(idx)] = pf
-            if ps is not None:
-                if st is None:
-                    st = np.zeros((len(batch), 6), np.float32)
-                st[idx] = ps
-        return e, f, st
+            x, k, na = rows[r], n_s[r], n_a[r]
+            e_all[p] = x[2:2 + k]
+            if x[1] and st_all is None:
+                st_all = np.zeros((len(batch), 6), np.float32 if x[1] == 4 else np.float64)
+            if x[1]:
+                st_all[p] = x[2 + k:2 + 7 * k].reshape(k, 6)
+            if x[0] and f_all is None:
+                f_all = np.zeros(batch.positions.shape, np.float32 if x[0] == 4 else np.float64)
+            if x[0]:
+                f_all[batch.atom_index(p)] = x[2 + 7 * k:2 + 7 * k + 3 * na].reshape(na, 3)
+        return e_all, f_all, st_all
 
 
 def predictor_packed_eval(predictor, compute_forces: bool = True, compute_stress: bool = False):

@@ -169,3 +169,35 @@ def test_gpu_sharded_batch_matches_one_batch(model_file):
     for i, w in enumerate(whole):
         assert abs(got[i][0] - w.energy) / mols[i].n_atoms <= 1e-5
         assert np.abs(got[i][1] - w.forces).max() <= 1e-4
+
+
+def _rank_packed_small(rank, world, port, out):
+    """More ranks than structures: some shares are empty."""
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    b = sh.PackedBatch.pack(wl.molecules(2, n_min=3, n_max=6, seed=8))
+
+    def ev(sub):  # energy = sum of Z, force = the positions, stress = 1..6 per structure
+        e = np.array([float(s.numbers.sum()) for s in sub.structures()])
+        return e, sub.positions.astype(np.float64), np.tile(np.arange(1, 7, dtype=np.float32), (len(sub), 1))
+    e, f, st = sh.PackedBatchRunner(ev, world=world, rank=rank).run(b)
+    if rank == 0:
+        np.savez(out, e=e, f=f, st=st)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_three_gloo_ranks_with_empty_shares(tmp_path):
+    import torch.multiprocessing as mp
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        port = sock.getsockname()[1]
+    out = str(tmp_path / "s.npz")
+    mp.start_processes(_rank_packed_small, args=(3, port, out), nprocs=3, start_method="spawn")
+    r = np.load(out)
+    b = sh.PackedBatch.pack(wl.molecules(2, n_min=3, n_max=6, seed=8))
+    np.testing.assert_array_equal(r["e"], [float(s.numbers.sum()) for s in b.structures()])
+    assert r["f"].dtype == np.float64 and r["st"].dtype == np.float32
+    np.testing.assert_array_equal(r["f"], b.positions)
+    np.testing.assert_array_equal(r["st"], np.tile(np.arange(1, 7), (2, 1)))
