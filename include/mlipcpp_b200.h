@@ -68,6 +68,26 @@ mlipcpp_error_t mlipcpp_b200_predict_device_forces(mlipcpp_model_t model, int32_
                                                    const mlipcpp_predict_options_t *options, float *d_forces,
                                                    double *energy, float stress[6], bool *has_stress);
 
+/* Verlet neighbour list for repeated single-structure predictions (MD):
+ * the reference builds a new list every call (PETModel::predict_batch,
+ * src/models/pet/pet.cpp:125-694).  With skin > 0 (Angstrom) the list is
+ * built with cutoff + skin and kept across calls, its vectors and distances
+ * recomputed from the new positions, until an atom has moved more than
+ * skin / 2 since the build (a move by a lattice vector along a periodic
+ * axis, as when an integrator wraps positions into the cell, does not
+ * count), the atom count, cell or pbc change, or a batch or another call
+ * rebuilds the list.  The extra pairs lie beyond the cutoff, where the
+ * smooth cutoff is 0 and the key mask -inf, like the reference's padding,
+ * so results agree with fresh lists to rounding.  A kept list also keeps
+ * the shapes, so the model's kernels replay from a CUDA graph.  0 (the
+ * default) rebuilds every call.  A skin that is negative or not finite is
+ * MLIPCPP_ERROR_INVALID_PARAMETER. */
+mlipcpp_error_t mlipcpp_b200_set_neighbor_skin(mlipcpp_model_t model, float skin);
+
+/* Neighbour lists this model has built so far (kept lists count once);
+ * -1 for an invalid or unloaded model. */
+int64_t mlipcpp_b200_neighbor_builds(mlipcpp_model_t model);
+
 /* Enable per-phase CUDA-event timing of later predictions. */
 mlipcpp_error_t mlipcpp_b200_set_timing(mlipcpp_model_t model, bool enable);
 

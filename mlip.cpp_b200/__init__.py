@@ -98,6 +98,8 @@ def lib() -> ctypes.CDLL:
         "mlipcpp_b200_predict_packed": (ctypes.c_int, [vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
         "mlipcpp_b200_predict_device": (ctypes.c_int, [vp, i32, vp, vp, vp, vp, vp, b, vp]),
         "mlipcpp_b200_predict_device_forces": (ctypes.c_int, [vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+        "mlipcpp_b200_set_neighbor_skin": (ctypes.c_int, [vp, f32]),
+        "mlipcpp_b200_neighbor_builds": (i64, [vp]),
         "mlipcpp_b200_set_timing": (ctypes.c_int, [vp, b]),
         "mlipcpp_b200_last_timings": (ctypes.c_int, [vp, vp]),
         "mlipcpp_b200_last_shape": (ctypes.c_int, [vp, vp]),
@@ -430,6 +432,15 @@ class Predictor:
             None if c is None else c.ctypes.data, None if p is None else p.ctypes.data, ctypes.byref(po),
             ctypes.c_void_p(d_forces) if d_forces else None, ctypes.byref(e), st.ctypes.data, ctypes.byref(hs)))
         return float(e.value), (st if hs.value else None)
+
+    def set_neighbor_skin(self, skin: float):
+        """Keep a Verlet list of cutoff + skin across single-structure calls
+        (mlipcpp_b200_set_neighbor_skin); 0 rebuilds every call."""
+        _check(lib().mlipcpp_b200_set_neighbor_skin(self._h, float(skin)))
+
+    def neighbor_builds(self) -> int:
+        """Neighbour lists built by this model so far."""
+        return int(lib().mlipcpp_b200_neighbor_builds(self._h))
 
     def set_timing(self, on: bool = True):
         _check(lib().mlipcpp_b200_set_timing(self._h, bool(on)))

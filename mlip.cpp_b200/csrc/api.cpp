@@ -739,6 +739,22 @@ mlipcpp_error_t mlipcpp_b200_domain_stats(mlipcpp_b200_domain_t domain, double s
   return MLIPCPP_OK;
 }
 
+mlipcpp_error_t mlipcpp_b200_set_neighbor_skin(mlipcpp_model_t model, float skin) {
+  if (auto e = check_model(model)) return e;
+  if (!(skin >= 0.f) || !std::isfinite(skin)) {
+    set_error("Invalid neighbour-list skin");
+    return MLIPCPP_ERROR_INVALID_PARAMETER;
+  }
+  model->model->set_neighbor_skin(skin);
+  clear_error();
+  return MLIPCPP_OK;
+}
+
+int64_t mlipcpp_b200_neighbor_builds(mlipcpp_model_t model) {
+  if (check_model(model)) return -1;
+  return model->model->neighbor_builds();
+}
+
 mlipcpp_error_t mlipcpp_b200_set_timing(mlipcpp_model_t model, bool enable) {
   if (auto e = check_model(model)) return e;
   model->model->set_timing(enable);

@@ -958,7 +958,9 @@ void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const in
   species_ = d_species;
   if (max_tok_ > attention_max_tokens(h_.d / h_.heads))
     throw Error(kErrUnsupported, "an atom has " + std::to_string(nl_.max_count) +
-                                     " neighbours, above the supported maximum of " +
+                                     (skin_ > 0.f ? " neighbours within the cutoff plus the neighbour-list skin"
+                                                  : " neighbours") +
+                                     ", above the supported maximum of " +
                                      std::to_string(attention_max_tokens(h_.d / h_.heads) - 1));
   chain_ = chain_ok_ && max_tok_ <= attention_split_max_tokens(h_.d / h_.heads);
   // memory plan: size, allocate, assign
@@ -1002,9 +1004,72 @@ const int *PETModel::device_species_map() {
   return d_zmap_.as<int>();
 }
 
+bool PETModel::skin_list(const float *d_pos, int n, const SystemView &sys, cudaStream_t s) {
+  const bool periodic = sys.cell != nullptr;
+  SkinGeom sg{};
+  if (periodic) {
+    for (int k = 0; k < 9; ++k) sg.cell[k] = sys.cell[k];
+    const double *m = sg.cell;
+    const double det = m[0] * (m[4] * m[8] - m[5] * m[7]) - m[1] * (m[3] * m[8] - m[5] * m[6]) +
+                       m[2] * (m[3] * m[7] - m[4] * m[6]);
+    const double c[9] = {m[4] * m[8] - m[5] * m[7], m[2] * m[7] - m[1] * m[8], m[1] * m[5] - m[2] * m[4],
+                         m[5] * m[6] - m[3] * m[8], m[0] * m[8] - m[2] * m[6], m[2] * m[3] - m[0] * m[5],
+                         m[3] * m[7] - m[4] * m[6], m[1] * m[6] - m[0] * m[7], m[0] * m[4] - m[1] * m[3]};
+    for (int k = 0; k < 9; ++k) sg.inv[k] = det != 0.0 ? c[k] / det : 0.0;
+    for (int a = 0; a < 3; ++a) sg.pbc[a] = sys.pbc[a] && det != 0.0 ? 1 : 0;
+  }
+  bool keep = vl_valid_ && vl_n_ == n && vl_periodic_ == periodic &&
+              (!periodic || (std::memcmp(vl_cell_, sys.cell, sizeof(vl_cell_)) == 0 &&
+                             vl_pbc_[0] == sys.pbc[0] && vl_pbc_[1] == sys.pbc[1] && vl_pbc_[2] == sys.pbc[2]));
+  if (keep) {
+    unsigned *dmax = static_cast<unsigned *>(vl_max_.ensure(sizeof(unsigned)));
+    CUDA_CHECK(cudaMemsetAsync(dmax, 0, sizeof(unsigned), s));
+    skin_displacement(d_pos, vl_ref_.as<float>(), n, sg, vl_img_.as<int>(), dmax, s);
+    unsigned bits = 0;
+    CUDA_CHECK(cudaMemcpyAsync(&bits, dmax, sizeof(bits), cudaMemcpyDeviceToHost, s));
+    CUDA_CHECK(cudaStreamSynchronize(s));
+    float m2;
+    std::memcpy(&m2, &bits, sizeof(m2));
+    const float half = 0.5f * skin_;
+    keep = m2 <= half * half;
+  }
+  if (keep) {
+    refresh_edges(d_pos, nl_.n_edges, nl_.center.as<int>(), nl_.nbr.as<int>(), nl_.shift.as<int>(),
+                  vl_img_.as<int>(), sg, nl_.vec.as<float>(), nl_.dist.as<float>(), s);
+    return true;
+  }
+  const float rc = h_.cutoff + skin_;
+  if (periodic) {
+    GridParams g;
+    make_grid_params(sys.cell, sys.pbc, rc, &g);
+    build_periodic_nl(d_pos, n, g, nl_, nls_, s);
+  } else {
+    std::vector<int> b(n, 0), e(n, n);
+    int *db = static_cast<int *>(d_sys_begin_.ensure(sizeof(int) * (n + 1)));
+    int *de = static_cast<int *>(d_sys_end_.ensure(sizeof(int) * (n + 1)));
+    CUDA_CHECK(cudaMemcpyAsync(db, b.data(), sizeof(int) * n, cudaMemcpyHostToDevice, s));
+    CUDA_CHECK(cudaMemcpyAsync(de, e.data(), sizeof(int) * n, cudaMemcpyHostToDevice, s));
+    build_open_nl(d_pos, db, de, n, rc, nl_, nls_, s);
+  }
+  CUDA_CHECK(cudaMemcpyAsync(vl_ref_.ensure(sizeof(float) * 3 * n), d_pos, sizeof(float) * 3 * n,
+                             cudaMemcpyDeviceToDevice, s));
+  vl_img_.ensure(sizeof(int) * 3 * n);
+  vl_valid_ = true;
+  vl_n_ = n;
+  vl_periodic_ = periodic;
+  if (periodic) {
+    std::memcpy(vl_cell_, sys.cell, sizeof(vl_cell_));
+    for (int a = 0; a < 3; ++a) vl_pbc_[a] = sys.pbc[a];
+  }
+  ++nl_builds_;
+  return false;
+}
+
 const EdgeList &PETModel::domain_neighbors(const double *d_pos, int n_local, int n_own, const GridParams &g) {
   if (wptr_.empty()) throw Error(3, "Model weights not loaded");
   CUDA_CHECK(cudaSetDevice(device_));
+  vl_valid_ = false;
+  ++nl_builds_;
   int *derr = static_cast<int *>(d_err_.ensure(sizeof(int) * 4));
   CUDA_CHECK(cudaMemsetAsync(derr, 0, sizeof(int), stream_));
   if (timing_) CUDA_CHECK(cudaEventRecord(ev_[0], stream_));
@@ -1092,12 +1157,18 @@ void PETModel::run_group(const float *d_pos, int n_atoms, const std::vector<cons
 
   // neighbour list
   const bool periodic = systems[0]->cell != nullptr;
-  if (periodic) {
+  if (n_sys == 1 && skin_ > 0.f) {
+    skin_list(d_pos, n_atoms, *systems[0], s);
+  } else if (periodic) {
     if (n_sys != 1) throw Error(kErrInternal, "periodic systems run one per group");
+    vl_valid_ = false;
+    ++nl_builds_;
     GridParams g;
     make_grid_params(systems[0]->cell, systems[0]->pbc, h_.cutoff, &g);
     build_periodic_nl(d_pos, n_atoms, g, nl_, nls_, s);
   } else {
+    vl_valid_ = false;
+    ++nl_builds_;
     std::vector<int> b(n_atoms), e(n_atoms);
     for (int k = 0; k < n_sys; ++k)
       for (int i = atom_begin[k]; i < atom_begin[k + 1]; ++i) {

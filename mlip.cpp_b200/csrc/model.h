@@ -142,6 +142,20 @@ class PETModel {
   int last_edges() const { return El_[0]; }
   int last_max_neighbors() const { return max_tok_ - 1; }
   void set_timing(bool on) { timing_ = on; }
+  // Verlet list for single-structure predictions: with skin > 0 the list is
+  // built with cutoff + skin and kept across calls (vectors and distances
+  // refreshed from the new positions) until an atom has moved more than
+  // skin / 2 since the build, the atom count, cell or pbc change, or another
+  // call rebuilds the list.  Pairs beyond the cutoff get f_c = 0 and a -inf
+  // key mask, the reference's padding, so results are unchanged.  0: a new
+  // list every call (the default).
+  void set_neighbor_skin(float skin) {
+    skin_ = skin;
+    vl_valid_ = false;
+  }
+  float neighbor_skin() const { return skin_; }
+  // neighbour lists built by this model so far (kept lists not counted again)
+  long long neighbor_builds() const { return nl_builds_; }
   cudaStream_t stream() const { return stream_; }
   size_t device_bytes() const;
 
@@ -159,6 +173,9 @@ class PETModel {
   void setup_graph(int n_local, int N0, int E0, int N1, int E1, const int *d_species, bool grad, int n_in = 0);
   void read_times(bool grad);
   const float *w(const std::string &name) const;
+  // neighbour list of a single structure through the kept Verlet list
+  // (builds it when it cannot be kept); true when the list was kept
+  bool skin_list(const float *d_pos, int n_atoms, const SystemView &sys, cudaStream_t s);
 
   struct Internals;  // device pointers of weights and activations (model.cu)
   std::unique_ptr<Internals> in_;
@@ -215,6 +232,17 @@ class PETModel {
   cudaGraphExec_t gexec_ = nullptr;
   long long graph_kernels_ = 0;
   bool capturing_ = false;
+  // Verlet list state (set_neighbor_skin): positions at the build, per-atom
+  // image offsets, the device maximum of the displacements, and the
+  // geometry the list was built for
+  float skin_ = 0.f;
+  bool vl_valid_ = false;
+  int vl_n_ = 0;
+  bool vl_periodic_ = false;
+  float vl_cell_[9] = {};
+  bool vl_pbc_[3] = {};
+  DevBuf vl_ref_, vl_img_, vl_max_;
+  long long nl_builds_ = 0;
   const int *species_ = nullptr;  // species index of every local atom (device), set by setup_graph
   EdgeList nl_;
   NLScratch nls_;

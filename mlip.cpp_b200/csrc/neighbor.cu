@@ -473,6 +473,69 @@ void build_local_nl(const double *pos, int n, int n_centers, const GridParams &g
   build_grid_nl<double>(pos, n, n_centers, g, out, s, stream);
 }
 
+__global__ void k_skin_displacement(const float *__restrict__ pos, const float *__restrict__ ref, int n, SkinGeom g,
+                                    int *__restrict__ img, unsigned *__restrict__ d_max2) {
+  const int a = blockIdx.x * blockDim.x + threadIdx.x;
+  float d2 = 0.f;
+  if (a < n) {
+    double d[3], k[3];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) d[c] = static_cast<double>(ref[3 * a + c]) - static_cast<double>(pos[3 * a + c]);
+    // k = round((ref - pos) inv) along periodic axes
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const double f = d[0] * g.inv[0 * 3 + c] + d[1] * g.inv[1 * 3 + c] + d[2] * g.inv[2 * 3 + c];
+      k[c] = g.pbc[c] ? rint(f) : 0.0;
+      img[3 * a + c] = static_cast<int>(k[c]);
+    }
+    double m = 0.0;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const double u = k[0] * g.cell[0 * 3 + c] + k[1] * g.cell[1 * 3 + c] + k[2] * g.cell[2 * 3 + c] - d[c];
+      m += u * u;
+    }
+    d2 = static_cast<float>(m);
+  }
+  d2 = warp_max(d2);
+  if ((threadIdx.x & 31) == 0 && d2 > 0.f) atomicMax(d_max2, __float_as_uint(d2));
+}
+
+__global__ void k_refresh_edges(const float *__restrict__ pos, int n_edges, const int *__restrict__ center,
+                                const int *__restrict__ nbr, const int *__restrict__ shift,
+                                const int *__restrict__ img, SkinGeom g, float *__restrict__ vec,
+                                float *__restrict__ dist) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= n_edges) return;
+  const int i = center[e], j = nbr[e];
+  double s[3], v[3];
+#pragma unroll
+  for (int c = 0; c < 3; ++c)
+    s[c] = static_cast<double>(shift[3 * e + c] + img[3 * j + c] - img[3 * i + c]);
+  double d2 = 0.0;
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    v[c] = (static_cast<double>(pos[3 * j + c]) - static_cast<double>(pos[3 * i + c])) +
+           (s[0] * g.cell[0 * 3 + c] + s[1] * g.cell[1 * 3 + c] + s[2] * g.cell[2 * 3 + c]);
+    vec[3 * e + c] = __double2float_rn(v[c]);
+    d2 += v[c] * v[c];
+  }
+  dist[e] = __double2float_rn(sqrt(d2));
+}
+
+void skin_displacement(const float *pos, const float *ref, int n, const SkinGeom &g, int *img, unsigned *d_max2,
+                       cudaStream_t stream) {
+  if (n <= 0) return;
+  k_skin_displacement<<<ceil_div(n, 256), 256, 0, stream>>>(pos, ref, n, g, img, d_max2);
+  CUDA_LAUNCH_CHECK();
+}
+
+void refresh_edges(const float *pos, int n_edges, const int *center, const int *nbr, const int *shift,
+                   const int *img, const SkinGeom &g, float *vec, float *dist, cudaStream_t stream) {
+  if (n_edges <= 0) return;
+  k_refresh_edges<<<ceil_div(n_edges, 256), 256, 0, stream>>>(pos, n_edges, center, nbr, shift, img, g, vec, dist);
+  CUDA_LAUNCH_CHECK();
+}
+
 void build_open_nl(const float *pos, const int *sys_begin, const int *sys_end, int n, float cutoff,
                    EdgeList &out, NLScratch &s, cudaStream_t stream) {
   (void)s;

@@ -67,6 +67,28 @@ void build_local_nl(const double *pos, int n, int n_centers, const GridParams &g
 void build_open_nl(const float *pos, const int *sys_begin, const int *sys_end, int n,
                    float cutoff, EdgeList &out, NLScratch &s, cudaStream_t stream);
 
+// ---- Verlet lists: a list built with cutoff + skin, kept across calls -------
+// Cell geometry of a kept list: the lattice (rows) and its inverse in f64
+// and the periodic axes (a non-periodic system has pbc all 0).
+struct SkinGeom {
+  double cell[9], inv[9];
+  int pbc[3];
+};
+// Displacement of every atom since the list was built, modulo the cell:
+// img[a] (3 ints) = the lattice translation k that brings pos[a] + k cell
+// nearest to ref[a] along periodic axes, so that wrapping an atom back
+// into the cell is not a move.  *d_max2 (device, bits of a non-negative
+// float) receives the largest |pos + k cell - ref|^2; the caller zeroes it
+// first.
+void skin_displacement(const float *pos, const float *ref, int n, const SkinGeom &g, int *img,
+                       unsigned *d_max2, cudaStream_t stream);
+// Vectors and distances of the kept pairs at the current positions:
+// vec = pos[j] - pos[i] + (shift + img[j] - img[i]) cell in f64, rounded to
+// f32 (vec) and f32(sqrt) (dist), the arithmetic of a fresh build up to the
+// order of its additions.
+void refresh_edges(const float *pos, int n_edges, const int *center, const int *nbr, const int *shift,
+                   const int *img, const SkinGeom &g, float *vec, float *dist, cudaStream_t stream);
+
 // Periodic (or partially periodic) search that allocates nothing, for
 // callers that own all device memory.  Positions and the five pair arrays
 // are the caller's device buffers on the current device; the working memory

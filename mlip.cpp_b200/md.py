@@ -5,8 +5,15 @@ step copies positions to the host, calls predict, and copies forces back.
 Here positions, velocities and forces stay in device memory between steps
 (torch tensors); a step is two half kicks and a drift around one
 `Predictor.predict_device_forces` call, and only the potential energy (a
-scalar) comes back to the host.  The neighbour list is rebuilt every step
-on the GPU (well under 1% of a step), so no Verlet skin is kept.
+scalar) comes back to the host.  By default the neighbour list is rebuilt
+every step on the GPU, as the reference does (well under 1% of a step on
+large cells).  `Predictor.set_neighbor_skin(s)` keeps a cutoff + s list
+across steps until an atom has moved s / 2 (wrapping into the cell does not
+count); the steps then keep their shapes and replay the model from a CUDA
+graph, which pays on small, launch-bound cells.  The extra pairs raise the
+tokens per atom, so on dense systems whose atoms have more than 47 pairs
+within cutoff + s the model leaves its fastest attention kernels, and a
+kept list costs more than it saves.
 
 Units: Angstrom, eV, amu, fs.  1 amu A^2 / fs^2 = 103.6427 eV.
 """
