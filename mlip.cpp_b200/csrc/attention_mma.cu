@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(2 * MT) k_attn_fwd_mma(AttnArgs a) {
   constexpr int kW = MT / 16, kNT = MT / 8, kTh = 32 * kW;  // warps (row strips), 8-key tiles, threads
   extern __shared__ __align__(16) uint8_t smem_raw[];
   SmemF<MT> &sm = *reinterpret_cast<SmemF<MT> *>(smem_raw);
-  const int atom = blockIdx.x, h = blockIdx.y;
+  const int atom = a.atoms ? a.atoms[blockIdx.x] : static_cast<int>(blockIdx.x), h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
   const int e0 = a.offset[atom], S = a.offset[atom + 1] - e0 + 1;
   const AtomRows tr = atom_rows(atom, e0, a.edge_base);
@@ -421,7 +421,7 @@ __global__ void __launch_bounds__(32 * 3 * kBlkHeads) k_attn_fwd_mma_blk(AttnArg
   constexpr int MT = 48, kNT = MT / 8;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   SmemFB &sm = *reinterpret_cast<SmemFB *>(smem_raw);
-  const int atom = blockIdx.x, blk = blockIdx.y;
+  const int atom = a.atoms ? a.atoms[blockIdx.x] : static_cast<int>(blockIdx.x), blk = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
   const int hl = warp / 3, sw = warp % 3, h = blk * kBlkHeads + hl;
   const int e0 = a.offset[atom], S = a.offset[atom + 1] - e0 + 1;
@@ -627,7 +627,7 @@ template <bool kSplit>
 __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma(AttnArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
-  const int atom = blockIdx.x, h = blockIdx.y;
+  const int atom = a.atoms ? a.atoms[blockIdx.x] : static_cast<int>(blockIdx.x), h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
   const int e0 = a.offset[atom], S = a.offset[atom + 1] - e0 + 1;
   const AtomRows tr = atom_rows(atom, e0, a.edge_base);
@@ -828,7 +828,7 @@ template <bool kSplit>
 __global__ void __launch_bounds__(kTh48, 6) k_attn_bwd_mma48(AttnArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   Smem48 &sm = *reinterpret_cast<Smem48 *>(smem_raw);
-  const int atom = blockIdx.x, h = blockIdx.y;
+  const int atom = a.atoms ? a.atoms[blockIdx.x] : static_cast<int>(blockIdx.x), h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
   const int e0 = a.offset[atom], S = a.offset[atom + 1] - e0 + 1;
   const AtomRows tr = atom_rows(atom, e0, a.edge_base);
@@ -1010,9 +1010,12 @@ __global__ void __launch_bounds__(kTh48, 6) k_attn_bwd_mma48(AttnArgs a) {
   }
 }
 
+// One class of atoms: n CTA rows (a.atoms maps them to atoms; null for
+// atoms 0..n-1) on the kernels for short sequences (at most kMT tokens) or
+// for any length up to kMaxTok.
 template <bool kSplit>
-void launch_mma(const AttnArgs &a, bool bwd, cudaStream_t s) {
-  const bool small = a.max_tokens <= kMT;
+void launch_class(const AttnArgs &a, bool bwd, bool small, int n, cudaStream_t s) {
+  if (n <= 0) return;
   size_t smem;
   int threads = kThreads;
   void (*fn)(AttnArgs);
@@ -1025,7 +1028,7 @@ void launch_mma(const AttnArgs &a, bool bwd, cudaStream_t s) {
     smem = sizeof(SmemFB);
     CUDA_CHECK(cudaFuncSetAttribute(k_attn_fwd_mma_blk, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(smem)));
-    k_attn_fwd_mma_blk<<<dim3(a.n_atoms, a.heads / kBlkHeads), 32 * 3 * kBlkHeads, smem, s>>>(a);
+    k_attn_fwd_mma_blk<<<dim3(n, a.heads / kBlkHeads), 32 * 3 * kBlkHeads, smem, s>>>(a);
     CUDA_LAUNCH_CHECK();
     return;
   } else {
@@ -1035,7 +1038,7 @@ void launch_mma(const AttnArgs &a, bool bwd, cudaStream_t s) {
   }
   CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.n_atoms, a.heads);
+  cfg.gridDim = dim3(n, a.heads);
   cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -1052,6 +1055,44 @@ void launch_mma(const AttnArgs &a, bool bwd, cudaStream_t s) {
   CUDA_LAUNCH_CHECK();
 }
 
+// With atoms longer than kMT tokens and the class lists given, the short
+// atoms keep the faster short-sequence kernels and only the long ones take
+// the general kernels; otherwise one launch over atoms 0..n_atoms-1.
+template <bool kSplit>
+void launch_mma(const AttnArgs &a0, bool bwd, cudaStream_t s) {
+  AttnArgs a = a0;
+  a.atoms = nullptr;
+  if (a0.max_tokens <= kMT || !a0.short_atoms || !a0.long_atoms) {
+    launch_class<kSplit>(a, bwd, a0.max_tokens <= kMT, a0.n_atoms, s);
+    return;
+  }
+  a.atoms = a0.short_atoms;
+  a.max_tokens = kMT;
+  launch_class<kSplit>(a, bwd, true, a0.n_short, s);
+  a.atoms = a0.long_atoms;
+  a.max_tokens = a0.max_tokens;
+  launch_class<kSplit>(a, bwd, false, a0.n_long, s);
+}
+
+__global__ void k_attention_classes(const int *__restrict__ offset, int n, int short_tokens,
+                                    int *__restrict__ short_atoms, int *__restrict__ long_atoms,
+                                    int *__restrict__ counts) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x, lane = threadIdx.x & 31;
+  const bool valid = i < n;
+  const bool is_short = valid && offset[i + 1] - offset[i] + 1 <= short_tokens;
+  const unsigned ms = __ballot_sync(0xffffffffu, is_short), ml = __ballot_sync(0xffffffffu, valid && !is_short);
+  int bs = 0, bl = 0;
+  if (lane == 0) {
+    if (ms) bs = atomicAdd(&counts[0], __popc(ms));
+    if (ml) bl = atomicAdd(&counts[1], __popc(ml));
+  }
+  bs = __shfl_sync(0xffffffffu, bs, 0);
+  bl = __shfl_sync(0xffffffffu, bl, 0);
+  const unsigned below = (1u << lane) - 1u;
+  if (is_short) short_atoms[bs + __popc(ms & below)] = i;
+  else if (valid) long_atoms[bl + __popc(ml & below)] = i;
+}
+
 }  // namespace
 
 bool attention_mma_supported(const AttnArgs &a, bool bwd) {
@@ -1060,6 +1101,15 @@ bool attention_mma_supported(const AttnArgs &a, bool bwd) {
   const bool split = bwd ? a.dqkv_split.hi != nullptr : a.out_split.hi != nullptr;
   if (split && (a.heads % (128 / kHd) || a.d % 128)) return false;
   return bwd ? (a.d_out && a.lse) : a.lse != nullptr;
+}
+
+int attention_short_tokens() { return kMT; }
+
+void attention_classes(const int *offset, int n, int short_tokens, int *short_atoms, int *long_atoms, int *counts,
+                       cudaStream_t s) {
+  if (n <= 0) return;
+  k_attention_classes<<<(n + 255) / 256, 256, 0, s>>>(offset, n, short_tokens, short_atoms, long_atoms, counts);
+  CUDA_LAUNCH_CHECK();
 }
 
 void attention_mma(const AttnArgs &a, bool bwd, cudaStream_t s) {

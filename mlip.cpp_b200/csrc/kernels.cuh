@@ -92,6 +92,15 @@ struct AttnArgs {
   // heads per CTA, one 128-column block.
   Split16View out_split;
   Split16View dqkv_split;
+  // Optional split of the atoms by sequence length (tensor-core kernels
+  // only): the n_short atoms in short_atoms have at most
+  // attention_short_tokens() tokens and run on the kernels for short
+  // sequences, the n_long in long_atoms on the others.  Null: one class
+  // chosen by max_tokens.  `atoms` (set per launch): the atom of each CTA
+  // row of the grid, null for the identity.
+  const int *short_atoms = nullptr, *long_atoms = nullptr;
+  int n_short = 0, n_long = 0;
+  const int *atoms = nullptr;
 };
 // Row of token k (0: the node) of one atom's sequence.
 struct AtomRows {
@@ -108,6 +117,14 @@ void attention_bwd(const AttnArgs &a, cudaStream_t stream);
 // outputs need heads in groups of 4 (one cluster per 128-column block).
 bool attention_mma_supported(const AttnArgs &a, bool bwd);
 void attention_mma(const AttnArgs &a, bool bwd, cudaStream_t stream);
+// Longest sequence the short-sequence tensor-core kernels take.
+int attention_short_tokens();
+// Atoms [0, n) split by sequence length (edges + 1 from the CSR offsets):
+// at most `short_tokens` into short_atoms, the rest into long_atoms, in
+// ascending order within each warp of 32 atoms; counts[0..1] (device,
+// zeroed by the caller) receive the two class sizes.
+void attention_classes(const int *offset, int n, int short_tokens, int *short_atoms, int *long_atoms,
+                       int *counts, cudaStream_t stream);
 // Largest per-atom token count the attention kernels accept for head size hd.
 int attention_max_tokens(int hd);
 // Largest tokens per atom for which the attention kernels can write

@@ -637,6 +637,12 @@ void PETModel::forward_backward(bool grad) {
   at.heads = h.heads;
   at.max_tokens = max_tok_;
   at.edge_base = N;
+  if (n_short_ + n_long_ > 0) {
+    at.short_atoms = attn_cls_.as<int>();
+    at.long_atoms = attn_cls_.as<int>() + Nl_[0];
+    at.n_short = n_short_;
+    at.n_long = n_long_;
+  }
 
   // Transformer block b on input x (its split form sx in chain mode); the
   // output goes to `out` when non-null, and in chain mode also to *sout when
@@ -876,7 +882,7 @@ std::vector<uintptr_t> PETModel::graph_key(bool grad) const {
               (timing_ ? 32u : 0u),
           p(persist_.ptr), p(scratch_.ptr), p(sp_[0].ptr), p(sp_[1].ptr), p(sp_[2].ptr), p(wbuf_.ptr),
           p(nl_.offset.ptr), p(nl_.center.ptr), p(nl_.nbr.ptr), p(nl_.shift.ptr), p(nl_.vec.ptr), p(nl_.dist.ptr),
-          p(species_), p(d_err_.ptr)};
+          p(species_), p(d_err_.ptr), static_cast<uintptr_t>(n_short_), p(attn_cls_.ptr)};
 }
 
 // Phase boundary i of the step's timing.  Inside a capture the record
@@ -963,6 +969,21 @@ void PETModel::setup_graph(int n_local, int N0, int E0, int N1, int E1, const in
                                      ", above the supported maximum of " +
                                      std::to_string(attention_max_tokens(h_.d / h_.heads) - 1));
   chain_ = chain_ok_ && max_tok_ <= attention_split_max_tokens(h_.d / h_.heads);
+  // atoms with more tokens than the short-sequence attention kernels take:
+  // split the atoms into two classes so that only those run on the general
+  // kernels (one host read of the class sizes)
+  n_short_ = n_long_ = 0;
+  if (!use_attn_rows_ && max_tok_ > attention_short_tokens() && N0 == N1 && N0 > 0) {
+    int *cls = static_cast<int *>(attn_cls_.ensure(sizeof(int) * (2 * static_cast<size_t>(N0) + 2)));
+    int *counts = cls + 2 * static_cast<size_t>(N0);
+    CUDA_CHECK(cudaMemsetAsync(counts, 0, 2 * sizeof(int), stream_));
+    attention_classes(nl_.offset.as<int>(), N0, attention_short_tokens(), cls, cls + N0, counts, stream_);
+    int hc[2] = {0, 0};
+    CUDA_CHECK(cudaMemcpyAsync(hc, counts, sizeof(hc), cudaMemcpyDeviceToHost, stream_));
+    CUDA_CHECK(cudaStreamSynchronize(stream_));
+    n_short_ = hc[0];
+    n_long_ = hc[1];
+  }
   // memory plan: size, allocate, assign
   const Counts c{n_local, N0, E0, N1, E1, n_in};
   Plan P, S;

@@ -243,6 +243,10 @@ class PETModel {
   bool vl_pbc_[3] = {};
   DevBuf vl_ref_, vl_img_, vl_max_;
   long long nl_builds_ = 0;
+  // attention atom classes of the current prediction (short_atoms, then
+  // long_atoms, then two counts); both sizes 0 when one class holds all
+  DevBuf attn_cls_;
+  int n_short_ = 0, n_long_ = 0;
   const int *species_ = nullptr;  // species index of every local atom (device), set by setup_graph
   EdgeList nl_;
   NLScratch nls_;
