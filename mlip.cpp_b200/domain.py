@@ -297,15 +297,17 @@ class Domain:
         return (np.asarray(virial) / vol).astype(np.float32)
 
 
-def run_emulated(make_predictor, structure, grid, skin: float = 0.0, steps: int = 1, compute_forces=True):
+def run_emulated(make_predictor, structure, grid, skin: float = 0.0, steps: int = 1, compute_forces=True,
+                 comm=None):
     """Evaluates `structure` (periodic) split over prod(grid) emulated ranks on
     the current GPU: one thread, one model (make_predictor()) and one engine
-    per rank, exchanging through LocalComm.  Returns (energy, forces [N, 3],
-    virial, per-rank stats) of the last step."""
+    per rank, exchanging through `comm` (default: a new LocalComm).  Returns
+    (energy, forces [N, 3], virial, per-rank stats) of the last step; raises
+    the first rank's error if any rank's step fails."""
     import torch
     world = int(np.prod(grid))
     own = owners(structure.positions, structure.cell, grid)
-    comm = LocalComm(world)
+    comm = comm or LocalComm(world)
     doms, idx = [], []
     for r in range(world):
         d = Domain(make_predictor(), structure.cell, grid, r, comm.for_rank(r), skin)

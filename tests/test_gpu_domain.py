@@ -78,3 +78,53 @@ def test_domain_rejects_too_small_cell(model_file):
         dd.Domain(pred, s.cell, (1, 1, 2), 0, comm.for_rank(0))
     assert ei.value.code == mb.INVALID_PARAMETER
     assert "slab" in str(ei.value)
+
+
+class AbandoningComm(dd.LocalComm):
+    """Rank `bad` abandons one exchange of the step (the `at`-th alltoallv,
+    or the final all-reduce for at = 0): it reports an error without
+    joining the others, as a rank that dies or never posts its halo would.
+    The failure is made on the host; no kernel is made to fault or wait."""
+
+    def __init__(self, world, bad, at):
+        super().__init__(world, timeout=30.0)
+        self.bad, self.at, self.calls = bad, at, 0
+
+    def _alltoallv(self, rank, *args):
+        if rank == self.bad:
+            self.calls += 1
+            if self.calls == self.at:
+                return 1
+        return super()._alltoallv(rank, *args)
+
+    def _allreduce(self, rank, *args):
+        if rank == self.bad and self.at == 0:
+            return 1
+        return super()._allreduce(rank, *args)
+
+
+@pytest.mark.parametrize("at", [1, 4, 5, 6, 7, 0])
+def test_domain_exchange_failure_is_reported_and_ranks_recover(at, model_file):
+    """A failed exchange at any point of the step (halo counts, requests,
+    the layer-0 tokens inside the forward pass, their gradients inside the
+    backward, the force halo, the final sum) ends every rank's step with
+    MLIPCPP_ERROR_COMPUTATION instead of a hang; the same models then give
+    the result of a clean step again."""
+    path = model_file("pet-mad-s", 9)
+    s = wl.si_diamond(4, seed=64)
+    preds = [mb.Predictor(path), mb.Predictor(path)]
+    grid = (1, 1, 2)
+
+    def run(comm=None):
+        it = iter(preds)
+        return dd.run_emulated(lambda: next(it), s, grid, comm=comm)
+
+    e0, F0, v0, _ = run()
+    with pytest.raises(mb.MLIPError) as ei:
+        run(AbandoningComm(2, bad=1, at=at))
+    assert ei.value.code == mb.COMPUTATION
+    assert "domain exchange" in str(ei.value)
+    e1, F1, v1, _ = run()
+    assert e1 == e0
+    np.testing.assert_allclose(F1, F0, rtol=0, atol=2e-6)
+    np.testing.assert_allclose(np.asarray(v1), np.asarray(v0), rtol=0, atol=1e-9 * max(1.0, np.abs(v0).max()))
