@@ -81,6 +81,7 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.rows = []
+        self.first = 0
         self.proc = None
 
     def __enter__(self):
@@ -93,6 +94,12 @@ class ClockSampler:
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # the sampler is live before the timed region starts: its first
+            # sample (taken at start-up, before the region) is set aside
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.01)
+            self.first = len(self.rows)
         except OSError:
             self.proc = None
         return self
@@ -110,15 +117,24 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        if not self.rows:
+        # samples from inside the timed region; a region shorter than the
+        # 200 ms period may hold none, and then the sample taken just before
+        # it is reported and flagged
+        rows, before = self.rows[self.first:], False
+        if not rows and self.rows:
+            rows, before = self.rows[-1:], True
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+        sm = [float(r[1]) for r in rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[k] for r in self.rows if len(r) > 8
+        reasons = sorted({names[k] for r in rows if len(r) > 8
                           for k in range(4) if r[5 + k].lower() == "active"})
-        return {"sm_mhz": float(np.median(sm)) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(self.rows)}
+        out = {"sm_mhz": float(np.median(sm)) if sm else None,
+               "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+        if before:
+            out["sampled_before_region"] = True
+        return out
 
 
 def cpu_reference(structures, gguf_path, steps, warmup, repeats=1, forces=True, nc=False):
@@ -448,9 +464,9 @@ def main():
     # device->host copy (on the spatial-domain path: the engine's events
     # around its step) ------------------------------------------------------
     launches = 0
-    barrier()
     dev_ms, wall_ms = [], []
     with ClockSampler(local) as clk:
+        barrier()
         for _ in range(args.steps):
             flush()
             l0 = mb.kernel_launches()
