@@ -403,6 +403,12 @@ void PETModel::load(const std::string &path, float cutoff_override) {
     }
     h.n_species = ns;
   }
+  for (int z = 0; z < kZTable; ++z) {
+    auto si = species_index_.find(z);
+    auto ci = composition_.find(z);
+    zidx_[z] = si == species_index_.end() ? -1 : si->second;
+    zcomp_[z] = ci == composition_.end() ? 0.0f : ci->second;
+  }
   h_ = h;
 
   // resolve pointers once
@@ -1017,8 +1023,7 @@ const int *PETModel::device_species_map() {
   if (!d_zmap_.ptr) {
     int h[128];
     for (int z = 0; z < 128; ++z) {
-      auto it = species_index_.find(z);
-      h[z] = it == species_index_.end() ? -1 : it->second;
+      h[z] = species_of(z);
     }
     CUDA_CHECK(cudaMemcpy(d_zmap_.ensure(sizeof(h)), h, sizeof(h), cudaMemcpyHostToDevice));
   }
@@ -1161,11 +1166,11 @@ void PETModel::run_group(const float *d_pos, int n_atoms, const std::vector<cons
   for (int k = 0; k < n_sys; ++k) {
     const SystemView &sv = *systems[k];
     for (int i = 0; i < sv.n_atoms; ++i) {
-      auto it = species_index_.find(sv.numbers[i]);
-      if (it == species_index_.end())
+      const int si = species_of(sv.numbers[i]);
+      if (si < 0)
         throw Error(kErrComputation, "Unknown atomic number " + std::to_string(sv.numbers[i]) +
                                          " not found in species_to_index mapping");
-      hsp[atom_begin[k] + i] = it->second;
+      hsp[atom_begin[k] + i] = si;
     }
   }
   int *hsb = hsp + n_atoms + 1;
@@ -1242,10 +1247,7 @@ void PETModel::run_group(const float *d_pos, int n_atoms, const std::vector<cons
     const SystemView &sv = *systems[k];
     Result &R = *results[k];
     double tot = he[k];
-    for (int i = 0; i < sv.n_atoms; ++i) {
-      auto it = composition_.find(sv.numbers[i]);
-      if (it != composition_.end()) tot += it->second;
-    }
+    for (int i = 0; i < sv.n_atoms; ++i) tot += composition_energy(sv.numbers[i]);
     R.energy = static_cast<float>(tot);
     R.has_forces = false;
     R.has_stress = false;

@@ -120,10 +120,17 @@ class PETModel {
   // species index of every atomic number 0..127 (-1: not in the model), device
   const int *device_species_map();
   double composition_energy(int z) const {
+    if (z >= 0 && z < kZTable) return zcomp_[z];
     auto it = composition_.find(z);
     return it == composition_.end() ? 0.0 : it->second;
   }
-  bool knows_species(int z) const { return species_index_.count(z) != 0; }
+  // species index of atomic number z, -1 when the model does not know it
+  int species_of(int z) const {
+    if (z >= 0 && z < kZTable) return zidx_[z];
+    auto it = species_index_.find(z);
+    return it == species_index_.end() ? -1 : it->second;
+  }
+  bool knows_species(int z) const { return species_of(z) >= 0; }
 
   // Device-resident entry for benchmarks: positions already on the device.
   void predict_device(const float *d_pos, const SystemView &sys, bool compute_grad, Result &out,
@@ -220,6 +227,10 @@ class PETModel {
   std::map<std::string, const float *> wptr_;
   std::map<int, int> species_index_;
   std::map<int, float> composition_;
+  // the same for Z < kZTable as flat tables (per-atom lookups on the host)
+  static constexpr int kZTable = 128;
+  int zidx_[kZTable];
+  float zcomp_[kZTable];
 
   // per-call device state
   DevBuf d_pos_, d_species_, d_sys_begin_, d_sys_end_, d_sys_atoms_, d_zmap_;
