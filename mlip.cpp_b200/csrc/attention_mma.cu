@@ -29,7 +29,8 @@
 //   backward, pass 2, warp w = key rows (transposed recomputation):
 //     S^T = K Q^T, P^T, dP^T = V dO^T, dS^T, dV = P^T dO, dK = s dS^T Q.
 // P enters a product at the fixed scale 2^14; dS with one scale per warp
-// strip.  Split-fp16 outputs need one scale per (row, 128-column block),
+// strip.  The exponentials of P use the __expf intrinsic: its few-ulp
+// error is at the level of the ~22 significant bits P keeps in split form.  Split-fp16 outputs need one scale per (row, 128-column block),
 // i.e. per 4 heads: those 4 CTAs form a cluster; each pushes its row
 // maxima into every CTA's shared memory (remote atomic max) between the two
 // halves of one cluster barrier, so no CTA reads another's memory.
@@ -354,7 +355,7 @@ __global__ void __launch_bounds__(2 * MT) k_attn_fwd_mma(AttnArgs a) {
     for (int n = 0; n < kNT; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        s[n][e] = s[n][e] == -FLT_MAX ? 0.f : expf(s[n][e] - m[e >> 1]);
+        s[n][e] = s[n][e] == -FLT_MAX ? 0.f : __expf(s[n][e] - m[e >> 1]);
         l[e >> 1] += s[n][e];
       }
     l[0] = quad_sum(l[0]);
@@ -513,7 +514,7 @@ __global__ void __launch_bounds__(32 * 3 * kBlkHeads) k_attn_fwd_mma_blk(AttnArg
     for (int n = 0; n < kNT; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        s[n][e] = s[n][e] == -FLT_MAX ? 0.f : expf(s[n][e] - m[e >> 1]);
+        s[n][e] = s[n][e] == -FLT_MAX ? 0.f : __expf(s[n][e] - m[e >> 1]);
         l[e >> 1] += s[n][e];
       }
     l[0] = quad_sum(l[0]);
@@ -667,7 +668,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma(AttnArgs a) {
       for (int e = 0; e < 4; ++e) {
         const int r = r0 + g + 8 * (e >> 1), c = 8 * n + 2 * tig + (e & 1);
         const bool v = n < NK8 && r < S && c < S;
-        s[n][e] = v ? expf(fmaf(s[n][e], fs, sm.mask[c]) - lq[e >> 1]) : 0.f;
+        s[n][e] = v ? __expf(fmaf(s[n][e], fs, sm.mask[c]) - lq[e >> 1]) : 0.f;
         dp[n][e] = v ? dp[n][e] * fdp : 0.f;
         Dp[e >> 1] = fmaf(s[n][e], dp[n][e], Dp[e >> 1]);
       }
@@ -707,7 +708,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_bwd_mma(AttnArgs a) {
       for (int e = 0; e < 4; ++e) {
         const int r = r0 + g + 8 * (e >> 1), c = 8 * n + 2 * tig + (e & 1);  // key r, query c
         const bool v = n < NK8 && r < S && c < S;
-        const float p = v ? expf(fmaf(st[n][e], fs, mk[e >> 1]) - sm.lse[c]) : 0.f;
+        const float p = v ? __expf(fmaf(st[n][e], fs, mk[e >> 1]) - sm.lse[c]) : 0.f;
         dpt[n][e] = v ? p * (dpt[n][e] * fdp - sm.D[c]) : 0.f;  // dS^T
         st[n][e] = p;                                           // P^T
         mx = fmaxf(mx, fabsf(dpt[n][e]));
@@ -938,7 +939,7 @@ __global__ void __launch_bounds__(kTh48, 6) k_attn_bwd_mma48(AttnArgs a) {
       for (int e = 0; e < 4; ++e) {
         const int r = r0 + g + 8 * (e >> 1), c = 8 * n + 2 * tig + (e & 1);
         const bool v = n < NK8 && r < S && c < S;
-        s[n][e] = v ? expf(fmaf(s[n][e], fs, sm.mask[c]) - lq[e >> 1]) : 0.f;
+        s[n][e] = v ? __expf(fmaf(s[n][e], fs, sm.mask[c]) - lq[e >> 1]) : 0.f;
         dp[n][e] = v ? dp[n][e] * fdp : 0.f;
         Dp[e >> 1] = fmaf(s[n][e], dp[n][e], Dp[e >> 1]);
       }
