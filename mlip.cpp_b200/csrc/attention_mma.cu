@@ -239,7 +239,7 @@ __device__ __forceinline__ void strip_store(const float (&v)[4][4], int r0, int 
         uint32_t hh, ll;
         split2(v[n][2 * half], v[n][2 * half + 1], f, hh, ll);
         *reinterpret_cast<uint32_t *>(o->hi + off + 8 * n) = hh;
-        *reinterpret_cast<uint32_t *>(o->lo + off + 8 * n) = ll;
+        if (o->lo) *reinterpret_cast<uint32_t *>(o->lo + off + 8 * n) = ll;
       }
       if (write_scale && tig == 0) o->sc[static_cast<size_t>(blk) * split_ld(*o) + tr(r)] = static_cast<int8_t>(s);
     }

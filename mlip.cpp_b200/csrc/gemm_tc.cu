@@ -647,23 +647,38 @@ __device__ __forceinline__ bool epilogue_tma(const GemmArgs &p, const EpiMaps &e
     }
     const int sx = split_scale_exponent(mx);
     const float f = pow2f(sx);
+    const bool has_lo = p.c_split.lo != nullptr;
 #pragma unroll
     for (int g = 0; g < NC / 32; ++g) {
       if (lane == 0) bulk_wait_read<0>();
       __syncwarp();
+      if (has_lo) {
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        uint32_t h[4], l[4];
+        for (int m = 0; m < 4; ++m) {
+          uint32_t h[4], l[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) split2(acc[32 * g + 8 * m + 2 * k], acc[32 * g + 8 * m + 2 * k + 1], f, h[k], l[k]);
-        sts128(sw64(ew.buf0, lane, m), make_uint4(h[0], h[1], h[2], h[3]));
-        sts128(sw64(ew.buf0 + 2048, lane, m), make_uint4(l[0], l[1], l[2], l[3]));
+          for (int k = 0; k < 4; ++k)
+            split2(acc[32 * g + 8 * m + 2 * k], acc[32 * g + 8 * m + 2 * k + 1], f, h[k], l[k]);
+          sts128(sw64(ew.buf0, lane, m), make_uint4(h[0], h[1], h[2], h[3]));
+          sts128(sw64(ew.buf0 + 2048, lane, m), make_uint4(l[0], l[1], l[2], l[3]));
+        }
+      } else {  // hi parts only: one rounding per element, no lo store
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          uint32_t h[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const __half2 hh = __floats2half2_rn(acc[32 * g + 8 * m + 2 * k] * f, acc[32 * g + 8 * m + 2 * k + 1] * f);
+            h[k] = *reinterpret_cast<const uint32_t *>(&hh);
+          }
+          sts128(sw64(ew.buf0, lane, m), make_uint4(h[0], h[1], h[2], h[3]));
+        }
       }
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) {
         tma_store_2d(&em.hi, ew.buf0, n0 + 32 * g, row0);
-        tma_store_2d(&em.lo, ew.buf0 + 2048, n0 + 32 * g, row0);
+        if (has_lo) tma_store_2d(&em.lo, ew.buf0 + 2048, n0 + 32 * g, row0);
         bulk_commit();
       }
     }
@@ -798,7 +813,7 @@ __device__ __forceinline__ bool epilogue_rows(const GemmArgs &p, const EpiWarp &
         lv[m] = make_uint4(l[0], l[1], l[2], l[3]);
       }
       rows_store64(buf, hv, reinterpret_cast<char *>(p.c_split.hi + n0 + 32 * g), pitch, rc, lane);
-      rows_store64(buf, lv, reinterpret_cast<char *>(p.c_split.lo + n0 + 32 * g), pitch, rc, lane);
+      if (p.c_split.lo) rows_store64(buf, lv, reinterpret_cast<char *>(p.c_split.lo + n0 + 32 * g), pitch, rc, lane);
     }
     if (valid && (NC == 128 || px->half == 0))
       p.c_split.sc[static_cast<size_t>(n0 / 128) * split_ld(p.c_split) + rc] = static_cast<int8_t>(sx);
@@ -1404,7 +1419,7 @@ EpiMaps make_epi_maps(const GemmArgs &a) {
   }
   if (a.c_split.hi) {
     e.hi = make_map_epi(a.c_split.hi, F16, 2, a.M, a.N, a.c_split.cols);
-    e.lo = make_map_epi(a.c_split.lo, F16, 2, a.M, a.N, a.c_split.cols);
+    if (a.c_split.lo) e.lo = make_map_epi(a.c_split.lo, F16, 2, a.M, a.N, a.c_split.cols);
   }
   return e;
 }
@@ -1413,7 +1428,10 @@ template <int EPI, int BNt>
 void launch16_bn(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t s) {
   const Split16View &sp = a.a_split;
   using C = F16Cfg<BNt>;
-  const CUtensorMap ah = make_map_f16(sp.hi, a.M, a.K, a.K, C::BK, BM), al = make_map_f16(sp.lo, a.M, a.K, a.K, C::BK, BM);
+  // a hi-only A (sp.lo null) is read by one-product launches only, which
+  // never load the lo map
+  const CUtensorMap ah = make_map_f16(sp.hi, a.M, a.K, a.K, C::BK, BM),
+                    al = make_map_f16(sp.lo ? sp.lo : sp.hi, a.M, a.K, a.K, C::BK, BM);
   const CUtensorMap bh = make_map_f16(w.hi, a.N, a.K, a.ldb, C::BK, BNt),
                     bl = make_map_f16(w.lo, a.N, a.K, a.ldb, C::BK, BNt);
   CUDA_CHECK(cudaFuncSetAttribute(k_gemm_3xf16<EPI, BNt>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::Smem));
@@ -1432,7 +1450,10 @@ template <int EPI>
 void launch16_pair(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t s) {
   const Split16View &sp = a.a_split;
   using C = PairCfg;
-  const CUtensorMap ah = make_map_f16(sp.hi, a.M, a.K, a.K, C::BK, BM), al = make_map_f16(sp.lo, a.M, a.K, a.K, C::BK, BM);
+  // a hi-only A (sp.lo null) is read by one-product launches only, which
+  // never load the lo map
+  const CUtensorMap ah = make_map_f16(sp.hi, a.M, a.K, a.K, C::BK, BM),
+                    al = make_map_f16(sp.lo ? sp.lo : sp.hi, a.M, a.K, a.K, C::BK, BM);
   const CUtensorMap bh = make_map_f16(w.hi, a.N, a.K, a.ldb, C::BK, 128),
                     bl = make_map_f16(w.lo, a.N, a.K, a.ldb, C::BK, 128);
   CUDA_CHECK(cudaFuncSetAttribute(k_gemm_3xf16_pair<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::Smem));
@@ -1514,6 +1535,9 @@ void gemm_3xf16(const GemmArgs &a, const TCWeights16 &w, int *err, cudaStream_t 
       reinterpret_cast<uintptr_t>(sp.hi) % 16 || reinterpret_cast<uintptr_t>(sp.lo) % 16 ||
       (a.c_split.hi && (reinterpret_cast<uintptr_t>(a.c_split.hi) % 16 || reinterpret_cast<uintptr_t>(a.c_split.lo) % 16)))
     throw Error(kErrInternal, "gemm_3xf16: fp16 operands not 16-byte aligned");
+  if (!sp.lo && w.products != 1)
+    throw Error(kErrInternal, "gemm_3xf16: an A operand without lo parts needs the one-product mode");
+  if (a.r_split.hi && !a.r_split.lo) throw Error(kErrInternal, "gemm_3xf16: a split residual needs its lo parts");
   if (a.r_split.hi && (a.epi != EPI_RESID || a.c_rows || a.r_split.rows < a.M || a.r_split.cols != a.N ||
                        reinterpret_cast<uintptr_t>(a.r_split.hi) % 16 || reinterpret_cast<uintptr_t>(a.r_split.lo) % 16))
     throw Error(kErrInternal, "gemm_3xf16: split residual view does not match the GEMM");

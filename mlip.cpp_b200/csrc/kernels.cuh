@@ -20,7 +20,9 @@ enum Epilogue : int {
 };
 
 // A matrix in split-fp16 form (split16.cuh): hi, lo [rows][cols] fp16 and
-// scale exponents sc [cols / 128][rows].  hi == nullptr: none.
+// scale exponents sc [cols / 128][rows].  hi == nullptr: none.  lo ==
+// nullptr with hi set: the hi parts only, for a matrix whose only reader is
+// a one-product (reduced-precision) GEMM; writers then skip the lo parts.
 struct Split16View {
   uint16_t *hi = nullptr;
   uint16_t *lo = nullptr;
@@ -34,7 +36,7 @@ __host__ __device__ inline int split_ld(const Split16View &v) { return v.ld ? v.
 inline Split16View split_rows(const Split16View &v, int r0, int n) {
   Split16View o = v;
   o.hi = v.hi + static_cast<size_t>(r0) * v.cols;
-  o.lo = v.lo + static_cast<size_t>(r0) * v.cols;
+  o.lo = v.lo ? v.lo + static_cast<size_t>(r0) * v.cols : nullptr;
   o.sc = v.sc + r0;
   o.rows = n;
   o.ld = split_ld(v);

@@ -584,6 +584,13 @@ void PETModel::forward_backward(bool grad) {
     next_sp ^= 1;
     return v;
   };
+  // A split buffer whose only reader is the next GEMM's A operand: in the
+  // reduced-precision mode that GEMM multiplies the hi parts alone, so the
+  // lo parts are neither computed nor stored.
+  auto operand = [this](Split16View v) {
+    if (reduced_) v.lo = nullptr;
+    return v;
+  };
   struct SplitIO {
     const Split16View *a = nullptr;  // A operand in split form
     bool a_ready = true;             // ... already written (else: write it from fp32 A first)
@@ -608,7 +615,7 @@ void PETModel::forward_backward(bool grad) {
         g.a_split = *io.a;
         g.a_split_ready = io.a_ready;
       } else {
-        g.a_split = split_view(0, M, K);
+        g.a_split = operand(split_view(0, M, K));
         g.a_split_ready = false;
       }
       if (io.c) g.c_split = *io.c;
@@ -662,7 +669,7 @@ void PETModel::forward_backward(bool grad) {
     at.out = a.o;
     Split16View so, sx1, shf;
     if (ch) {
-      so = take_split(T, d);
+      so = operand(take_split(T, d));
       at.out_split = so;
     }
     attn(false, at);
@@ -673,7 +680,7 @@ void PETModel::forward_backward(bool grad) {
          SplitIO{ch ? &so : nullptr, true, nullptr, ch ? sx : nullptr});
     if (ch) sx1 = take_split(T, d);
     layer_norm_fwd(a.xa[b], B.ga, B.ba, ch ? nullptr : a.x1, a.ra[b], T, d, s, ch ? &sx1 : nullptr);
-    if (ch) shf = take_split(T, f);
+    if (ch) shf = operand(take_split(T, f));
     gemm(a.x1, d, nullptr, B.W0, d, a.hf, f, nullptr, T, f, d, B.b0, EPI_SILU, s, keep(a.zf[b]), f, nullptr, 0,
          SplitIO{ch ? &sx1 : nullptr, true, ch ? &shf : nullptr});
     gemm(a.hf, f, nullptr, B.W3, f, a.xm[b], d, nullptr, T, d, f, B.b3, EPI_RESID, s, nullptr, 0, ch ? nullptr : a.x1, d,
@@ -691,7 +698,7 @@ void PETModel::forward_backward(bool grad) {
     Split16View sa, sy;
     if (ch) {
       sa = split_rows(sxl, row0, M);
-      sy = split_view(fin_sp ^ 1, M, r);
+      sy = operand(split_view(fin_sp ^ 1, M, r));
     }
     gemm(x ? x + static_cast<size_t>(row0) * d : nullptr, d, nullptr, hw.H0, d, y1, r, nullptr, M, r, d, hw.h0,
          EPI_SILU, s, keep(z1), r, nullptr, 0, SplitIO{ch ? &sa : nullptr, true, ch ? &sy : nullptr});
@@ -723,11 +730,11 @@ void PETModel::forward_backward(bool grad) {
       fa.cat = a.cat;
       Split16View scat, shc;
       if (ch) {
-        scat = take_split(E, K);
+        scat = operand(take_split(E, K));
         fa.cat_split = scat;
       }
       featurize(fa, s);
-      if (ch) shc = take_split(E, H);
+      if (ch) shc = operand(take_split(E, H));
       gemm(a.cat, K, nullptr, L.C0f, K, a.hc, H, nullptr, E, H, K, nullptr, EPI_SILU, s, keep(a.zc[l]), H, nullptr, 0,
            SplitIO{ch ? &scat : nullptr, true, ch ? &shc : nullptr});
       // edge tokens: rows [N, N + E) of the layer's tokens
@@ -778,9 +785,9 @@ void PETModel::forward_backward(bool grad) {
   auto head_bwd = [&](const HeadW &hw, const float *z1, const float *z2, const float *scale, int row0, int M,
                       float *dst) {
     Split16View s2, s1;
-    if (ch) s2 = take_split(M, r);
+    if (ch) s2 = operand(take_split(M, r));
     head_last_bwd(z2, hw.HL, scale, a.dz2, M, r, s, ch ? &s2 : nullptr);
-    if (ch) s1 = take_split(M, r);
+    if (ch) s1 = operand(take_split(M, r));
     gemm(a.dz2, r, nullptr, hw.H2T, r, a.dz1, r, nullptr, M, r, r, nullptr, EPI_DSILU, s, const_cast<float *>(z1), r,
          nullptr, 0, SplitIO{ch ? &s2 : nullptr, true, ch ? &s1 : nullptr});
     gemm(a.dz1, r, nullptr, hw.H0T, r, dst + static_cast<size_t>(row0) * d, d, nullptr, M, d, r, nullptr, EPI_STORE,
@@ -799,7 +806,7 @@ void PETModel::forward_backward(bool grad) {
     if (ch) sdu = take_split(T, d);
     // chain mode: du is read only in split form (GEMM operand and residual)
     layer_norm_bwd(dy, a.xm[b], a.rm[b], B.gm, ch ? nullptr : a.du, T, d, s, ch ? &sdu : nullptr);
-    if (ch) sdhf = take_split(T, f);
+    if (ch) sdhf = operand(take_split(T, f));
     gemm(a.du, d, nullptr, B.W3T, d, a.dhf, f, nullptr, T, f, d, nullptr, EPI_DSILU, s, a.zf[b], f, nullptr, 0,
          SplitIO{ch ? &sdu : nullptr, true, ch ? &sdhf : nullptr});
     gemm(a.dhf, f, nullptr, B.W0T, f, a.dx1, d, nullptr, T, d, f, nullptr, EPI_RESID, s, nullptr, 0,
@@ -813,7 +820,7 @@ void PETModel::forward_backward(bool grad) {
     at.d_out = a.dout;
     at.d_qkv = a.dqkv;
     if (ch) {
-      sdq = take_split(T, 3 * d);
+      sdq = operand(take_split(T, 3 * d));
       at.dqkv_split = sdq;
     }
     attn(true, at);
@@ -850,7 +857,7 @@ void PETModel::forward_backward(bool grad) {
   block_bwd(3, a.dx, a.dx2);
   // the first block's input gradient feeds only the compression backward
   Split16View sdx;
-  if (ch) sdx = split_view(2, T, d);
+  if (ch) sdx = operand(split_view(2, T, d));
   block_bwd(2, a.dx2, a.dx, ch ? &sdx : nullptr);
   if (E > 0) compress_bwd(1, a.dx, ch ? &sdx : nullptr, true);
   N = Nl_[0]; E = E0; T = T0;
@@ -863,7 +870,7 @@ void PETModel::forward_backward(bool grad) {
   // to them, and theirs for this domain's tokens come in (collective)
   if (rm_) rm_->exchange_token_grads(a.dmsg, a.dx, Nl_[0], d, s);
   block_bwd(1, a.dx, a.dx2);
-  if (ch) sdx = split_view(2, T, d);
+  if (ch) sdx = operand(split_view(2, T, d));
   block_bwd(0, a.dx2, a.dx, ch ? &sdx : nullptr);
   if (E0 > 0) {
     compress_bwd(0, a.dx, ch ? &sdx : nullptr, true);

@@ -50,7 +50,7 @@ __device__ __forceinline__ void warp_split_block(const Split16View &o, int row, 
   split2(v.z, v.w, f, h1, l1);
   const size_t off = static_cast<size_t>(row) * o.cols + blk * 128 + lane * 4;
   *reinterpret_cast<uint2 *>(o.hi + off) = make_uint2(h0, h1);
-  *reinterpret_cast<uint2 *>(o.lo + off) = make_uint2(l0, l1);
+  if (o.lo) *reinterpret_cast<uint2 *>(o.lo + off) = make_uint2(l0, l1);
   if (lane == 0) o.sc[static_cast<size_t>(blk) * split_ld(o) + row] = static_cast<int8_t>(s);
 }
 
@@ -60,14 +60,14 @@ template <int n>
 __device__ __forceinline__ void thread_split_store(const Split16View &o, int row, int c0, const float *v, int s) {
   const float f = pow2f(s);
   uint16_t *hp = o.hi + static_cast<size_t>(row) * o.cols + c0;
-  uint16_t *lp = o.lo + static_cast<size_t>(row) * o.cols + c0;
+  uint16_t *lp = o.lo ? o.lo + static_cast<size_t>(row) * o.cols + c0 : nullptr;
 #pragma unroll
   for (int i = 0; i < n; i += 8) {
     uint32_t h[4], l[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) split2(v[i + 2 * k], v[i + 2 * k + 1], f, h[k], l[k]);
     *reinterpret_cast<uint4 *>(hp + i) = make_uint4(h[0], h[1], h[2], h[3]);
-    *reinterpret_cast<uint4 *>(lp + i) = make_uint4(l[0], l[1], l[2], l[3]);
+    if (lp) *reinterpret_cast<uint4 *>(lp + i) = make_uint4(l[0], l[1], l[2], l[3]);
   }
 }
 
