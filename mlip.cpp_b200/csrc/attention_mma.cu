@@ -246,6 +246,48 @@ __device__ __forceinline__ void strip_store(const float (&v)[4][4], int r0, int 
   }
 }
 
+// Split-fp16 stores of a warp's 16-row strip through shared memory: the
+// 16 x 32 block of one output (hi and lo parts, 1 KB each) is staged with
+// the 16-byte chunks of each row XOR-swizzled by (row & 3), then written
+// out in 16-byte stores, four lanes per row covering its 64 contiguous
+// bytes, instead of 4-byte stores spread over eight rows.  lo == nullptr:
+// the hi parts only.  Row scales and their bytes as in strip_store.
+__device__ __forceinline__ void strip_stage(const float (&v)[4][4], int r0, int S, AtomRows tr, int lane,
+                                            uint16_t *hi, uint16_t *lo, const int *rm, const Split16View &o,
+                                            int blk, bool write_scale) {
+  const int g = lane >> 2, tig = lane & 3;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int lr = g + 8 * half, r = r0 + lr;
+    const int s = r < S ? split_scale_exponent(__int_as_float(rm[r])) : 0;
+    const float f = pow2f(s);
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      uint32_t hh, ll;
+      split2(v[n][2 * half], v[n][2 * half + 1], f, hh, ll);
+      const int off = lr * 32 + ((n ^ (lr & 3)) << 3) + 2 * tig;
+      *reinterpret_cast<uint32_t *>(hi + off) = hh;
+      if (lo) *reinterpret_cast<uint32_t *>(lo + off) = ll;
+    }
+    if (write_scale && tig == 0 && r < S) o.sc[static_cast<size_t>(blk) * split_ld(o) + tr(r)] = static_cast<int8_t>(s);
+  }
+}
+// The strip staged by strip_stage into columns col0 .. col0 + 31 of rows
+// r0 .. r0 + 15 (those below S) of o.
+__device__ __forceinline__ void stage_store(const uint16_t *hi, const uint16_t *lo, int r0, int S, AtomRows tr,
+                                            int lane, const Split16View &o, int col0) {
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    const int c = 32 * it + lane, lr = c >> 2, ch = c & 3, r = r0 + lr;
+    const int off = lr * 32 + ((ch ^ (lr & 3)) << 3);
+    if (r < S) {
+      const size_t go = static_cast<size_t>(tr(r)) * o.cols + col0 + 8 * ch;
+      *reinterpret_cast<uint4 *>(o.hi + go) = *reinterpret_cast<const uint4 *>(hi + off);
+      if (o.lo) *reinterpret_cast<uint4 *>(o.lo + go) = *reinterpret_cast<const uint4 *>(lo + off);
+    }
+  }
+}
+
 // ---- forward ---------------------------------------------------------------------
 // Shared memory of the forward for atoms of at most MT tokens: Q, K, V in
 // split form.  MT = 48 (3 warps, 23 KB) covers the usual neighbour counts
@@ -775,6 +817,7 @@ struct Smem48 {
   int rmax[3][kMT];
 };
 static_assert(4 * kMat48 >= 2 * kMatP, "P / dS fit in the K / V region");
+static_assert(kW48 * 3072 * 2 <= 8 * kMat48 * 2, "split-output staging fits in the Q / dO / K / V blocks");
 
 // A operand (16 keys x 16 queries) of a transposed product from a stored
 // [query][key] block: matrices (q0, k0), (q0, k0 + 8), (q0 + 8, k0),
@@ -1004,9 +1047,18 @@ __global__ void __launch_bounds__(kTh48, 6) k_attn_bwd_mma48(AttnArgs a) {
     if (act) {
       const int nb = d / 128, blk = (h * kHd) / 128;
       const bool first = cta_rank_in_cluster() == 0;
-      strip_store(dq, r0, S, tr, lane, nullptr, 0, h * kHd, &a.dqkv_split, sm.rmax[0], blk, first);
-      strip_store(dk, r0, S, tr, lane, nullptr, 0, d + h * kHd, &a.dqkv_split, sm.rmax[1], nb + blk, first);
-      strip_store(dv, r0, S, tr, lane, nullptr, 0, 2 * d + h * kHd, &a.dqkv_split, sm.rmax[2], 2 * nb + blk, first);
+      // staging: 6 KB per warp in the Q / dO / K / V blocks, dead once every
+      // warp of the cluster has passed the barrier
+      uint16_t *st = reinterpret_cast<uint16_t *>(smem_raw) + warp * 3072;
+      const bool lo = a.dqkv_split.lo != nullptr;
+      strip_stage(dq, r0, S, tr, lane, st, lo ? st + 512 : nullptr, sm.rmax[0], a.dqkv_split, blk, first);
+      strip_stage(dk, r0, S, tr, lane, st + 1024, lo ? st + 1536 : nullptr, sm.rmax[1], a.dqkv_split, nb + blk, first);
+      strip_stage(dv, r0, S, tr, lane, st + 2048, lo ? st + 2560 : nullptr, sm.rmax[2], a.dqkv_split, 2 * nb + blk,
+                  first);
+      __syncwarp();
+      stage_store(st, st + 512, r0, S, tr, lane, a.dqkv_split, h * kHd);
+      stage_store(st + 1024, st + 1536, r0, S, tr, lane, a.dqkv_split, d + h * kHd);
+      stage_store(st + 2048, st + 2560, r0, S, tr, lane, a.dqkv_split, 2 * d + h * kHd);
     }
   }
 }
