@@ -459,6 +459,7 @@ struct SmemFB {
   int scale[kBlkHeads][3];
   int rmax[48];  // row maxima of the block's output (bits of non-negative floats)
 };
+static_assert(3 * kBlkHeads * 1024 <= kBlkHeads * 6 * 48 * kPitch, "output staging fits in the Q / K / V blocks");
 
 __global__ void __launch_bounds__(32 * 3 * kBlkHeads) k_attn_fwd_mma_blk(AttnArgs a) {
   constexpr int MT = 48, kNT = MT / 8;
@@ -605,8 +606,14 @@ __global__ void __launch_bounds__(32 * 3 * kBlkHeads) k_attn_fwd_mma_blk(AttnArg
       if (q0 + g + 8 < S) atomicMax(&sm.rmax[q0 + g + 8], __float_as_int(m1));
     }
   }
-  __syncthreads();  // the block's row maxima
-  if (act) strip_store(o, q0, S, tr, lane, nullptr, 0, h * kHd, &a.out_split, sm.rmax, blk, hl == 0);
+  __syncthreads();  // the block's row maxima; every warp is past its products
+  if (act) {
+    // staging: 2 KB per warp in the Q / K / V blocks, dead after the barrier
+    uint16_t *st = reinterpret_cast<uint16_t *>(smem_raw) + (threadIdx.x >> 5) * 1024;
+    strip_stage(o, q0, S, tr, lane, st, a.out_split.lo ? st + 512 : nullptr, sm.rmax, a.out_split, blk, hl == 0);
+    __syncwarp();
+    stage_store(st, st + 512, q0, S, tr, lane, a.out_split, h * kHd);
+  }
 }
 
 // ---- backward --------------------------------------------------------------------
