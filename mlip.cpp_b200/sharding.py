@@ -137,12 +137,13 @@ class PackedBatch:
         starts = np.repeat(self.first[idx] - np.concatenate([[0], np.cumsum(n)[:-1]]), n)
         return starts + np.arange(int(n.sum()), dtype=np.int64)
 
-    def take(self, idx) -> "PackedBatch":
-        """The structures `idx`, in that order, as a batch of their own."""
+    def take(self, idx, rows=None) -> "PackedBatch":
+        """The structures `idx`, in that order, as a batch of their own
+        (`rows`: their atom_index, when the caller has it already)."""
         idx = np.asarray(idx, np.int64)
         if idx.shape[0] == len(self) and np.array_equal(idx, np.arange(len(self))):
             return self
-        rows = self.atom_index(idx)
+        rows = self.atom_index(idx) if rows is None else rows
         return PackedBatch(self.positions[rows], self.numbers[rows], self.n_atoms[idx],
                            None if self.cells is None else self.cells[idx],
                            None if self.pbc is None else self.pbc[idx])
@@ -164,27 +165,46 @@ class PackedBatchRunner:
     def __init__(self, evaluate, world: int = 1, rank: int = 0, group=None):
         self.evaluate = evaluate
         self.world, self.rank, self.group = world, rank, group
-        self._parts = None
+        self._plan_cache = None
+
+    def _plan(self, batch: PackedBatch, costs):
+        """The split and every index array the exchange needs.  They depend
+        only on the sizes of the structures, so they are kept while the
+        sizes repeat (costs given: made anew)."""
+        key = batch.n_atoms.tobytes() if costs is None else None
+        if key is not None and self._plan_cache is not None and self._plan_cache[0] == key:
+            return self._plan_cache[1]
+        if costs is None:
+            costs = [structure_cost(int(n)) for n in batch.n_atoms]
+        parts = shard(costs, self.world)
+        n_s = [len(p) for p in parts]
+        n_a = [int(batch.n_atoms[p].sum()) if p else 0 for p in parts]
+        rows = [batch.atom_index(p) if p else np.zeros(0, np.int64) for p in parts]
+        # the gathered shares hold structures (atoms) in rank order; the
+        # inverse permutations put them back in input order with one gather
+        s_order = np.concatenate([np.asarray(p, np.int64) for p in parts])
+        a_order = np.concatenate(rows)
+        s_inv = np.empty_like(s_order)
+        s_inv[s_order] = np.arange(s_order.shape[0])
+        a_inv = np.empty_like(a_order)
+        a_inv[a_order] = np.arange(a_order.shape[0])
+        plan = {"parts": parts, "n_s": n_s, "n_a": n_a, "rows": rows, "s_inv": s_inv, "a_inv": a_inv,
+                "width": max(2 + 7 * ns + 3 * na for ns, na in zip(n_s, n_a))}
+        if key is not None:
+            self._plan_cache = (key, plan)
+        return plan
 
     def run(self, batch: PackedBatch, costs=None):
         if self.world == 1:
             return self.evaluate(batch)
-        if costs is None:  # the split depends only on the sizes: kept while they repeat
-            key = batch.n_atoms.tobytes()
-            if self._parts is None or self._parts[0] != key:
-                self._parts = (key, shard([structure_cost(int(n)) for n in batch.n_atoms], self.world))
-            parts = self._parts[1]
-        else:
-            parts = shard(costs, self.world)
+        P = self._plan(batch, costs)
+        parts, n_s, n_a = P["parts"], P["n_s"], P["n_a"]
         mine = parts[self.rank]
-        e, f, st = self.evaluate(batch.take(mine)) if mine else (None, None, None)
+        e, f, st = self.evaluate(batch.take(mine, P["rows"][self.rank])) if mine else (None, None, None)
         # Every rank knows every share, so each sends one float64 row of a
         # fixed width: [forces itemsize, stress itemsize | energies | stress
         # | forces], padded to the largest share; one all-gather moves them.
-        n_s = [len(p) for p in parts]
-        n_a = [int(batch.n_atoms[p].sum()) if p else 0 for p in parts]
-        width = max(2 + 7 * ns + 3 * na for ns, na in zip(n_s, n_a))
-        row = np.zeros(width, np.float64)
+        row = np.zeros(P["width"], np.float64)
         k, na = len(mine), n_a[self.rank]
         if mine:
             row[0] = 0 if f is None else np.asarray(f).dtype.itemsize
@@ -202,21 +222,18 @@ class PackedBatchRunner:
         recv = [torch.empty_like(send) for _ in range(self.world)]
         dist.all_gather(recv, send, group=self.group)
         rows = torch.stack(recv).cpu().numpy()
-        e_all = np.zeros(len(batch), np.float64)
-        f_all = st_all = None
-        for r, p in enumerate(parts):
-            if not p:
-                continue
-            x, k, na = rows[r], n_s[r], n_a[r]
-            e_all[p] = x[2:2 + k]
-            if x[1] and st_all is None:
-                st_all = np.zeros((len(batch), 6), np.float32 if x[1] == 4 else np.float64)
-            if x[1]:
-                st_all[p] = x[2 + k:2 + 7 * k].reshape(k, 6)
-            if x[0] and f_all is None:
-                f_all = np.zeros(batch.positions.shape, np.float32 if x[0] == 4 else np.float64)
-            if x[0]:
-                f_all[batch.atom_index(p)] = x[2 + 7 * k:2 + 7 * k + 3 * na].reshape(na, 3)
+        live = [r for r in range(self.world) if n_s[r]]
+        if not live:
+            return np.zeros(0, np.float64), None, None
+        fsize, ssize = rows[live[0], 0], rows[live[0], 1]
+        e_all = np.concatenate([rows[r, 2:2 + n_s[r]] for r in live])[P["s_inv"]]
+        st_all = f_all = None
+        if ssize:
+            st_cat = np.concatenate([rows[r, 2 + n_s[r]:2 + 7 * n_s[r]] for r in live]).reshape(-1, 6)
+            st_all = st_cat[P["s_inv"]].astype(np.float32 if ssize == 4 else np.float64)
+        if fsize:
+            f_cat = np.concatenate([rows[r, 2 + 7 * n_s[r]:2 + 7 * n_s[r] + 3 * n_a[r]] for r in live]).reshape(-1, 3)
+            f_all = f_cat[P["a_inv"]].astype(np.float32 if fsize == 4 else np.float64)
         return e_all, f_all, st_all
 
 
