@@ -201,3 +201,21 @@ def test_three_gloo_ranks_with_empty_shares(tmp_path):
     assert r["f"].dtype == np.float64 and r["st"].dtype == np.float32
     np.testing.assert_array_equal(r["f"], b.positions)
     np.testing.assert_array_equal(r["st"], np.tile(np.arange(1, 7), (2, 1)))
+
+
+def test_packed_runner_plan_inverts_the_rank_order_and_is_kept():
+    """The exchange plan of a 3-rank runner: the gathered shares, in rank
+    order, go back to input order through its inverse permutations; the plan
+    is reused while the sizes repeat and remade when they change."""
+    mols = wl.molecules(10, n_min=3, n_max=9, seed=11)
+    b = sh.PackedBatch.pack(mols)
+    r = sh.PackedBatchRunner(None, world=3, rank=1)
+    P = r._plan(b, None)
+    assert sorted(i for p in P["parts"] for i in p) == list(range(10))
+    s_cat = np.concatenate([np.asarray(p) for p in P["parts"]])
+    np.testing.assert_array_equal(s_cat[P["s_inv"]], np.arange(10))
+    a_cat = np.concatenate(P["rows"])
+    np.testing.assert_array_equal(a_cat[P["a_inv"]], np.arange(b.positions.shape[0]))
+    assert r._plan(sh.PackedBatch.pack(mols), None) is P
+    other = sh.PackedBatch.pack(wl.molecules(10, n_min=3, n_max=9, seed=12))
+    assert r._plan(other, None) is not P
